@@ -1,0 +1,168 @@
+/* xencb -- C ABI of the B200-native xenc Library read.
+ *
+ * One shared library (libxencb.so) with plain pointers and sizes: no torch, no C++ types. Every compute
+ * entry point enqueues work on the CUDA stream `stream` (a cudaStream_t passed as void*; NULL = legacy
+ * default stream), performs no host synchronisation and allocates no device memory: callers own every
+ * buffer, including the scratch `workspace` whose size the matching *_workspace() query returns.
+ *
+ * Layouts (row-major, C order):
+ *   rows        n_rows query tokens (the reference's [B, T] flattened), each reading one Library;
+ *               row r reads Library  r / rows_per_lib.
+ *   slots       a pool of n_pages pages; page p holds up to `page_rows` slot rows of d_s elements at
+ *               slots + p * page_stride (elements). A Library is a table page_of[lib, c] -> page index
+ *               with n_valid[lib, c] valid rows (the reference's mask, xenc/library.py:51-55).
+ *   S           summary keys, float32 [n_lib, C, d_s] (xenc/library.py:69-74).
+ *   weights     nn.Linear layout: out_features x in_features, float32.
+ *
+ * Return value: XENCB_OK or an error code; xencb_last_error() gives the message of the last failing call on
+ * the calling thread. XENCB_EINVAL is the reference's ValueError (bad shape / argument), the others are
+ * runtime failures. Kernels never trap: a bounded wait that runs out sets a bit in the per-device status
+ * word that xencb_device_status() returns.
+ */
+#ifndef XENCB_H_
+#define XENCB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define XENCB_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define XENCB_API __attribute__((visibility("default")))
+#else
+#define XENCB_API
+#endif
+
+/* status codes */
+#define XENCB_OK 0
+#define XENCB_EINVAL 1   /* invalid argument: maps to ValueError                         */
+#define XENCB_ECUDA 2    /* CUDA runtime error (launch, attribute): RuntimeError         */
+#define XENCB_ENOTSUP 3  /* valid but unsupported configuration: NotImplementedError    */
+
+/* device status bits (xencb_device_status) */
+#define XENCB_DEV_TIMEOUT 1u /* an mbarrier wait gave up after its time limit                  */
+#define XENCB_DEV_CLAMPED 2u /* an n_valid entry exceeded page_rows and was clamped            */
+#define XENCB_DEV_BADPAGE 4u /* a page_of entry was outside [0, n_pages); that chunk was skipped */
+
+/* element type codes */
+#define XENCB_F32 0
+#define XENCB_F16 1
+#define XENCB_BF16 2
+
+XENCB_API int xencb_abi_version(void);
+XENCB_API const char* xencb_last_error(void);
+
+/* Synchronises `stream`, returns the device status bits of the current device and clears them if `clear`. */
+XENCB_API int xencb_device_status(void* stream, int clear, unsigned int* status_out);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Input projection: hn = rms_norm(h); q = L2(hn @ W_in^T + b_in); gate = sigmoid(hn . gate_w + gate_b).
+ * Replaces xenc/injector.py:235-236 (rms_norm + itf_query, :54-58) and :266 (itf_gate, :61-65).
+ *   flags    XENCB_PIN_RMS: multiply the input rows by 1/rms (rms_norm, no weight);
+ *            XENCB_PIN_L2:  L2-normalise the output rows (x / (||x|| + 1e-6)).
+ *            A full-rank A is one call with both flags; a low-rank A = Sequential(A1, A2) is a call with
+ *            XENCB_PIN_RMS into a float32 [n_rows, rank] buffer, then one with XENCB_PIN_L2 over it.
+ *   h        [n_rows, d_m] of h_dtype (the reference upcasts h to float32 first; so does this)
+ *   w_in     [d_s, d_m] float32; b_in [d_s] or NULL
+ *   gate_w   [d_m] or NULL (then gate_out is not written); gate_b the scalar gate_b[pos[li]]
+ *   sel_w    [n_cand, d_m] or NULL: LayerSelector logits z = hn @ sel_w^T + sel_b (xenc/selector.py:69-74)
+ *   q_out    [n_rows, d_s] float32; gate_out [n_rows] or NULL; rstd_out [n_rows] or NULL (1/rms)
+ *   z_out    [n_rows, n_cand] or NULL
+ *   workspace at least xencb_project_in_workspace(n_rows, d_m, d_s) bytes, 256-byte aligned */
+#define XENCB_PIN_RMS 1
+#define XENCB_PIN_L2 2
+XENCB_API size_t xencb_project_in_workspace(int64_t n_rows, int d_m, int d_s);
+XENCB_API int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const float* w_in,
+                               const float* b_in, int d_s, int flags, const float* gate_w, float gate_b,
+                               const float* sel_w, const float* sel_b, int n_cand, float rms_eps, float* q_out,
+                               float* gate_out, float* rstd_out, float* z_out, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* rms_norm alone (deltaskill.derive.rms_norm as called at xenc/injector.py:235): out = h * rsqrt(mean(h^2) + eps),
+ * float32 out [n_rows, d_m]; for interfaces that are duck-typed objects (xenc/injector.py:55-56). */
+XENCB_API int xencb_rms_norm(const void* h, int h_dtype, int64_t n_rows, int d_m, float eps, float* out,
+                             void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Chunk routing. Replaces LibraryInjector.route (xenc/injector.py:220-229):
+ *   logit[r, c] = (q[r] . S[lib(r), c]) * route_temp for c < n_chunks_of[lib] (else excluded);
+ *   if 0 < top_k < n_chunks_of[lib]: keep the top_k logits, ties to the LOWER chunk index;
+ *   softmax over the kept chunks.
+ * Outputs: idx [n_rows, k_out] chunk ids sorted by (logit desc, index asc), -1 padded; wk [n_rows, k_out]
+ * their weights (0 padded); w_dense [n_rows, C] the reference's w (zeros off the kept set) or NULL;
+ * logit_out [n_rows, C] raw logits or NULL. k_out = xencb_route_k(top_k, C).
+ * n_chunks_of may be NULL (every Library has C chunks). */
+XENCB_API int xencb_route_k(int top_k, int n_chunks);
+XENCB_API int xencb_route(const float* q, int64_t n_rows, int d_s, const float* S, int n_chunks, const int32_t* n_chunks_of,
+                int64_t rows_per_lib, int64_t n_lib, float route_temp, int top_k, int32_t* idx, float* wk,
+                float* w_dense, float* logit_out, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Masked decode read over the routed chunks. Replaces the read of LibraryInjector._branch
+ * (xenc/injector.py:239-245 and :263-265) for query rows that each read their own routed chunks:
+ *   r[row] = sum_j wk[row, j] * read_c(q[row]),  c = idx[row, j] (skipped when c < 0 or wk == 0),
+ *   read_c(q) = softmax_n(read_temp * q . k_cn) @ K_c   over the n_valid[lib, c] rows   (read_softmax != 0)
+ *             = (sum_n (q . k_cn) k_cn) / sqrt(max(n_valid, 1))                         (read_softmax == 0)
+ * K = V (tied). slots_dtype XENCB_F16 / XENCB_BF16 / XENCB_F32; accumulation is float32.
+ * page_rows bounds n_valid (checked on the device: larger values are clamped and flagged). Slot pages and q
+ * must be 16-byte aligned and d_s * sizeof(slot) a multiple of 16. The chunk read is split into row
+ * ranges processed by a persistent, TMA-bulk-pipelined kernel and merged by log-sum-exp into r. */
+XENCB_API size_t xencb_read_decode_workspace(int64_t n_rows, int k, int d_s, int page_rows, int slots_dtype);
+XENCB_API int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots, int slots_dtype,
+                      int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of, const int32_t* n_valid,
+                      int n_chunks, int64_t rows_per_lib, int64_t n_lib, const int32_t* idx, const float* wk, int k,
+                      float read_temp, int read_softmax, float* r_out, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Output projection and injection epilogue. Replaces xenc/injector.py:266-267 (gain_scale * gain * gate *
+ * itf_write(r), :74-77), LayerSelector.apply (xenc/selector.py:95-110) and the hook arithmetic
+ * (xenc/injector.py:185-197: delta.to(h.dtype), position mask, mag term, h + delta):
+ *   d        = scale * gate[row] * (r @ W_out^T + b_out)                 (gate NULL -> 1)
+ *   if sel_w: d = sel_w[row] * exp(log_alpha) * d / (||d|| / (||h|| + 1e-6) + 1e-6)
+ *   d       *= pos_mask[row]                                              (pos_mask NULL -> 1)
+ *   delta_out = d in h_dtype (or NULL); h_out = h + delta_out in h_dtype (or NULL; may alias h);
+ *   rel_out[row] = ||delta_out|| / (||h|| + 1e-6)                         (or NULL)
+ *   h        [n_rows, d_m] of h_dtype; r [n_rows, d_s] float32; w_out [d_m, d_s]; b_out [d_m] or NULL. */
+XENCB_API size_t xencb_project_out_workspace(int64_t n_rows, int d_s, int d_m);
+XENCB_API int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_out, const float* b_out, int d_m,
+                      float scale, const float* gate, const float* sel_w, float log_alpha, const float* pos_mask,
+                      const void* h, int h_dtype, void* delta_out, void* h_out, float* rel_out, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * LayerSelector weights from logits. Replaces LayerSelector._weights_from_logits (xenc/selector.py:59-67),
+ * forward value: top-k of z (ties to the lower index), softmax over the kept (or 1/k when
+ * straight_through), zeros elsewhere. z, w_out: [n_rows, n_cand] float32, n_cand <= 32. */
+XENCB_API int xencb_selector_weights(const float* z, int64_t n_rows, int n_cand, int k, int straight_through, float* w_out,
+                           void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * LayerSelector logits. Replaces LayerSelector.compute (xenc/selector.py:69-74): z = x @ u_w^T + u_b, with
+ * x = rms_norm(h) when `rms` != 0 (the recompute at the first candidate layer, :98-101) or x = h as given
+ * (an explicit compute(hn0)). h [n_rows, d_m] of h_dtype; u_w [n_cand, d_m]; u_b [n_cand] or NULL. */
+XENCB_API int xencb_selector_logits(const void* h, int h_dtype, int64_t n_rows, int d_m, const float* u_w,
+                                    const float* u_b, int n_cand, int rms, float rms_eps, float* z_out, void* stream);
+
+/* LayerSelector.apply once the weights exist (xenc/selector.py:106-110), for a delta computed elsewhere:
+ *   out = w[row, pos] * exp(log_alpha) * d / (||d|| / (||h|| + 1e-6) + 1e-6),  d = float32(delta)
+ * delta [n_rows, d] of delta_dtype; h [n_rows, d] of h_dtype; w [n_rows, n_cand] float32; out like delta. */
+XENCB_API int xencb_selector_apply(const void* delta, int delta_dtype, const void* h, int h_dtype, int64_t n_rows,
+                                   int d, const float* w, int n_cand, int pos, float log_alpha, void* out,
+                                   void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Summary keys on the device. Replaces Library._summaries (xenc/library.py:69-74):
+ *   S[lib, c] = L2(mean of the n_valid[lib, c] rows of page page_of[lib, c]) (zero rows give S = 0). */
+XENCB_API int xencb_summaries(const void* slots, int slots_dtype, int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of,
+                    const int32_t* n_valid, int64_t n_lib, int n_chunks, int d_s, float* S_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XENCB_H_ */

@@ -1,0 +1,217 @@
+// Chunk routing (xenc/injector.py:220-229), LayerSelector weights (xenc/selector.py:59-67) and the
+// Library's summary keys (xenc/library.py:69-74).
+//
+// Routing is two kernels: route_logits (one warp per (row, chunk) dot product, q . S * route_temp, the
+// reference's order: dot first, then the temperature) and route_topk (one warp per row: k rounds of a warp
+// arg-max with ties to the lower chunk index, then the softmax over the kept logits).
+#pragma once
+
+#include <math_constants.h>
+
+#include "common.cuh"
+
+namespace xencb {
+
+__global__ void __launch_bounds__(256) route_logits_kernel(const float* __restrict__ q, int64_t n_rows, int d_s,
+                                                          const float* __restrict__ S, int C,
+                                                          const int32_t* __restrict__ n_chunks_of,
+                                                          int64_t rows_per_lib, float temp,
+                                                          float* __restrict__ logit) {
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= n_rows * C) return;
+  const int64_t row = gw / C;
+  const int c = (int)(gw % C);
+  const int64_t lib = row / rows_per_lib;
+  const int nc = n_chunks_of ? n_chunks_of[lib] : C;
+  if (c >= nc) {
+    if (lane == 0) logit[row * C + c] = -CUDART_INF_F;
+    return;
+  }
+  const float* qr = q + row * d_s;
+  const float* sr = S + (lib * C + c) * (int64_t)d_s;
+  float d = 0.f;
+  if ((d_s & 3) == 0) {
+    const float4* q4 = reinterpret_cast<const float4*>(qr);
+    const float4* s4 = reinterpret_cast<const float4*>(sr);
+    for (int i = lane; i < (d_s >> 2); i += 32) {
+      const float4 a = __ldg(q4 + i), b = __ldg(s4 + i);
+      d = fmaf(a.x, b.x, d); d = fmaf(a.y, b.y, d); d = fmaf(a.z, b.z, d); d = fmaf(a.w, b.w, d);
+    }
+  } else {
+    for (int i = lane; i < d_s; i += 32) d = fmaf(__ldg(qr + i), __ldg(sr + i), d);
+  }
+  d = warp_sum(d);
+  if (lane == 0) logit[row * C + c] = d * temp;
+}
+
+// Warp arg-max over (value desc, index asc); returns the winner in every lane.
+__device__ __forceinline__ void warp_argmax(float& v, int& i) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
+  }
+}
+
+constexpr int TOPK_WARPS = 4;
+
+// One warp per row; dynamic smem: TOPK_WARPS * C floats.
+__global__ void __launch_bounds__(TOPK_WARPS * 32) route_topk_kernel(
+    const float* __restrict__ logit, int64_t n_rows, int C, const int32_t* __restrict__ n_chunks_of,
+    int64_t rows_per_lib, int top_k, int k_out, int32_t* __restrict__ idx, float* __restrict__ wk,
+    float* __restrict__ w_dense) {
+  extern __shared__ float sv_all[];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * TOPK_WARPS + w;
+  if (row >= n_rows) return;
+  float* v = sv_all + (int64_t)w * C;
+  const int64_t lib = row / rows_per_lib;
+  const int nc = n_chunks_of ? min(n_chunks_of[lib], C) : C;
+  const float* lr = logit + row * C;
+  for (int c = lane; c < C; c += 32) v[c] = (c < nc) ? lr[c] : -CUDART_INF_F;
+  __syncwarp();
+  int32_t* ir = idx + row * k_out;
+  float* wr = wk + row * k_out;
+  const bool sparse = top_k > 0 && top_k < nc;
+  if (!sparse) {
+    float mx = -CUDART_INF_F;
+    for (int c = lane; c < nc; c += 32) mx = fmaxf(mx, v[c]);
+    mx = warp_max(mx);
+    float sum = 0.f;
+    for (int c = lane; c < nc; c += 32) sum += expf(v[c] - mx);
+    sum = warp_sum(sum);
+    for (int j = lane; j < k_out; j += 32) {
+      ir[j] = j < nc ? j : -1;
+      wr[j] = j < nc ? expf(v[j] - mx) / sum : 0.f;
+    }
+    if (w_dense)
+      for (int c = lane; c < C; c += 32) w_dense[row * C + c] = c < nc ? expf(v[c] - mx) / sum : 0.f;
+    return;
+  }
+  // sparse: top_k rounds of arg-max, the winner's slot is then retired to -inf
+  for (int t = 0; t < top_k; ++t) {
+    float bv = -CUDART_INF_F;
+    int bi = 0x7fffffff;
+    for (int c = lane; c < nc; c += 32) {
+      const float x = v[c];
+      if (x > bv || (x == bv && c < bi)) { bv = x; bi = c; }
+    }
+    warp_argmax(bv, bi);
+    if (lane == 0) {
+      if (bi < nc) {
+        ir[t] = bi;
+        v[bi] = -CUDART_INF_F;
+      } else {
+        ir[t] = -1;  // only reachable with non-finite logits
+      }
+    }
+    __syncwarp();
+  }
+  for (int j = top_k + lane; j < k_out; j += 32) { ir[j] = -1; wr[j] = 0.f; }
+  __syncwarp();
+  // softmax over the kept logits (the first one is the maximum)
+  float mx = -CUDART_INF_F;
+  for (int j = lane; j < top_k; j += 32) { const int c = ir[j]; if (c >= 0) mx = fmaxf(mx, lr[c]); }
+  mx = warp_max(mx);
+  float sum = 0.f;
+  for (int j = lane; j < top_k; j += 32) { const int c = ir[j]; if (c >= 0) sum += expf(lr[c] - mx); }
+  sum = warp_sum(sum);
+  for (int j = lane; j < top_k; j += 32) {
+    const int c = ir[j];
+    wr[j] = c >= 0 ? expf(lr[c] - mx) / sum : 0.f;
+  }
+  if (w_dense) {
+    for (int c = lane; c < C; c += 32) w_dense[row * C + c] = 0.f;
+    __syncwarp();
+    for (int j = lane; j < top_k; j += 32) {
+      const int c = ir[j];
+      if (c >= 0) w_dense[row * C + c] = expf(lr[c] - mx) / sum;
+    }
+  }
+}
+
+// LayerSelector weights: one warp per row, lane = candidate (n_cand <= 32).
+__global__ void __launch_bounds__(128) selector_weights_kernel(const float* __restrict__ z, int64_t n_rows,
+                                                              int n_cand, int k, int straight_through,
+                                                              float* __restrict__ w_out) {
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= n_rows) return;
+  const float x = lane < n_cand ? z[row * n_cand + lane] : -CUDART_INF_F;
+  float cur = lane < n_cand ? x : -CUDART_INF_F;
+  bool kept = false;
+  float vmax = -CUDART_INF_F;
+  for (int t = 0; t < k; ++t) {
+    float bv = cur;
+    int bi = lane < n_cand ? lane : 0x7fffffff;
+    warp_argmax(bv, bi);
+    if (t == 0) vmax = bv;
+    if (lane == bi) { kept = true; cur = -CUDART_INF_F; }
+  }
+  float e = 0.f;
+  if (kept) e = straight_through ? 1.f : expf(x - vmax);
+  const float sum = warp_sum(e);
+  if (lane < n_cand) w_out[row * n_cand + lane] = kept ? (straight_through ? 1.f / (float)k : e / sum) : 0.f;
+}
+
+// Selector logits: one CTA per row; x = rms_norm(h) (rms != 0) or h; one warp per candidate dot product.
+template <typename TH>
+__global__ void __launch_bounds__(256) selector_logits_kernel(const TH* __restrict__ h, int d_m,
+                                                             const float* __restrict__ u_w,
+                                                             const float* __restrict__ u_b, int n_cand, int rms,
+                                                             float eps, float* __restrict__ z_out) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const TH* hr = h + row * d_m;
+  float scale = 1.f;
+  if (rms) {
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < d_m; i += blockDim.x) { const float x = to_f32(hr[i]); ss = fmaf(x, x, ss); }
+    ss = block_sum(ss, red);
+    scale = rsqrtf(ss / (float)d_m + eps);
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int c = wid; c < n_cand; c += nw) {
+    const float* u = u_w + (int64_t)c * d_m;
+    float d = 0.f;
+    for (int i = lane; i < d_m; i += 32) d = fmaf(to_f32(hr[i]), u[i], d);
+    d = warp_sum(d);
+    if (lane == 0) z_out[row * n_cand + c] = d * scale + (u_b ? u_b[c] : 0.f);
+  }
+}
+
+// S[lib, c] = L2(mean of the valid rows); one CTA per (lib, chunk), columns strided over threads.
+template <typename T>
+__global__ void __launch_bounds__(256) summaries_kernel(const T* __restrict__ slots, int64_t n_pages,
+                                                       int64_t page_stride,
+                                                       int page_rows, const int32_t* __restrict__ page_of,
+                                                       const int32_t* __restrict__ n_valid, int C, int d_s,
+                                                       float* __restrict__ S) {
+  __shared__ float red[32];
+  const int64_t lc = blockIdx.x;  // lib * C + c
+  const int64_t page = page_of[lc];
+  int nv = n_valid[lc];
+  if (page < 0 || page >= n_pages) {  // never read outside the pool
+    if (threadIdx.x == 0) flag_error(XENCB_DEV_BADPAGE);
+    nv = 0;
+  }
+  nv = nv < 0 ? 0 : (nv > page_rows ? page_rows : nv);
+  const T* base = slots + (nv > 0 ? page : 0) * page_stride;
+  float* out = S + lc * (int64_t)d_s;
+  const float cnt = (float)(nv > 0 ? nv : 1);
+  float ss = 0.f;
+  for (int j = threadIdx.x; j < d_s; j += blockDim.x) {
+    float s = 0.f;
+    for (int n = 0; n < nv; ++n) s += to_f32(base[(int64_t)n * d_s + j]);
+    const float m = s / cnt;
+    out[j] = m;
+    ss = fmaf(m, m, ss);
+  }
+  ss = block_sum(ss, red);
+  const float den = sqrtf(ss) + 1e-6f;
+  for (int j = threadIdx.x; j < d_s; j += blockDim.x) out[j] = out[j] / den;
+}
+
+}  // namespace xencb

@@ -1,0 +1,557 @@
+// libxencb: the C ABI (include/xencb.h) over the sm_100a kernels of the Library read.
+//
+// Host side of every entry point: validate arguments (XENCB_EINVAL with a message, the reference's
+// ValueError), plan the launch from the device's SM count, check the caller's workspace, launch on the
+// caller's stream. No entry point allocates device memory or synchronises, except xencb_device_status.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <type_traits>
+
+#include "common.cuh"
+#include "project.cuh"
+#include "read_decode.cuh"
+#include "route.cuh"
+
+namespace xencb {
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(XENCB_ECUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+#define XENCB_CHECK_LAUNCH(what)                         \
+  do {                                                   \
+    cudaError_t e__ = cudaGetLastError();                \
+    if (e__ != cudaSuccess) return cuda_fail(e__, what); \
+  } while (0)
+
+constexpr int kMaxDev = 64;
+
+struct DevInfo {
+  int sms = 0;
+  int max_smem_optin = 0;
+};
+
+DevInfo g_dev[kMaxDev];
+std::mutex g_mu;
+
+int device_info(DevInfo* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDev) return fail(XENCB_ENOTSUP, "device ordinal %d out of range", dev);
+  if (g_dev[dev].sms == 0) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_dev[dev].sms == 0) {
+      int sms = 0, smem = 0;
+      e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+      e = cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(smem opt-in)");
+      g_dev[dev].max_smem_optin = smem;
+      g_dev[dev].sms = sms;
+    }
+  }
+  *out = g_dev[dev];
+  return XENCB_OK;
+}
+
+int elem_size(int dtype) {
+  switch (dtype) {
+    case XENCB_F32: return 4;
+    case XENCB_F16: return 2;
+    case XENCB_BF16: return 2;
+    default: return 0;
+  }
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Opt a kernel into `smem` bytes of dynamic shared memory once per (device, kernel).
+template <typename K>
+int ensure_smem(K kernel, int smem, int* done_flags) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDev) return fail(XENCB_ENOTSUP, "device ordinal %d out of range", dev);
+  if (done_flags[dev] >= smem) return XENCB_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+  done_flags[dev] = smem;
+  return XENCB_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ GEMM plan
+struct GemmPlan {
+  int splits, kps;
+  size_t part_bytes;
+};
+
+GemmPlan plan_gemm(int64_t M, int N, int K, int sms) {
+  GemmPlan p;
+  p.splits = gemm_splits(M, N, K, sms);
+  p.kps = gemm_kps(K, p.splits);
+  p.splits = (K + p.kps - 1) / p.kps;
+  p.part_bytes = align_up((size_t)p.splits * (size_t)M * (size_t)N * sizeof(float), 256);
+  return p;
+}
+
+template <typename TX>
+void launch_gemm(const void* X, int64_t M, int K, const float* W, int N, const GemmPlan& p, float* part,
+                 cudaStream_t st) {
+  dim3 grid((N + GEMM_BN - 1) / GEMM_BN, (unsigned)((M + GEMM_BM - 1) / GEMM_BM), p.splits);
+  gemm_tn_splitk_kernel<TX><<<grid, GEMM_THREADS, 0, st>>>(static_cast<const TX*>(X), M, K, W, N, p.kps, part);
+}
+
+// ------------------------------------------------------------------------------------------------ read plan
+struct ReadPlan {
+  int vpt, ncw, rps, n_stage, n_split, split_rows, row_bytes, nvec, threads, grid;
+  size_t smem, acc_bytes, ml_bytes;
+  int64_t n_items;
+};
+
+int plan_read(int64_t n_rows, int k, int d_s, int page_rows, int dtype, ReadPlan* p) {
+  DevInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  const int es = elem_size(dtype);
+  if (!es) return fail(XENCB_EINVAL, "slots_dtype %d is not one of XENCB_F32/F16/BF16", dtype);
+  if (d_s <= 0 || (int64_t)d_s * es % 16 != 0)
+    return fail(XENCB_EINVAL, "d_s=%d: a slot row must be a multiple of 16 bytes (d_s %% %d == 0)", d_s, 16 / es);
+  p->row_bytes = d_s * es;
+  p->nvec = p->row_bytes / 16;
+  // at most 15 consumer warps (512 threads per CTA with the producer warp)
+  if (p->nvec <= 15 * 32) p->vpt = 1;
+  else if (p->nvec <= 15 * 64) p->vpt = 2;
+  else return fail(XENCB_ENOTSUP, "d_s=%d: slot rows above 15 KiB are not supported", d_s);
+  p->ncw = (p->nvec + 32 * p->vpt - 1) / (32 * p->vpt);
+  p->threads = 32 * (p->ncw + 1);
+  // rows per stage: a power of two <= 64 with a stage of about 32 KiB
+  int rps = 64;
+  while (rps > 1 && rps * p->row_bytes > 32768) rps >>= 1;
+  p->rps = rps;
+  const size_t stage_bytes = align_up((size_t)rps * p->row_bytes, 128);
+  const size_t tail = align_up(2 * (size_t)p->ncw * RD_G * sizeof(float), 8) + 2 * 8 * 8 + 16;
+  const size_t budget = (size_t)(di.max_smem_optin > 0 ? di.max_smem_optin : 232448) - 1024;
+  int n_stage = (int)((budget - tail) / stage_bytes);
+  if (n_stage > 8) n_stage = 8;
+  if (n_stage < 2) return fail(XENCB_ENOTSUP, "d_s=%d: two pipeline stages do not fit in shared memory", d_s);
+  p->n_stage = n_stage;
+  p->smem = (size_t)n_stage * stage_bytes + align_up(2 * (size_t)p->ncw * RD_G * sizeof(float), 8) +
+            2 * (size_t)n_stage * 8 + 16;
+  // row splits: pick the count with the smallest modelled makespan on one CTA per SM
+  const int64_t pairs = n_rows * k;
+  const int grid_max = di.sms;
+  const int max_split = page_rows > 64 ? (page_rows + 63) / 64 : 1;
+  double best = 1e300;
+  int best_n = 1, best_rows = page_rows;
+  for (int n = 1; n <= max_split; ++n) {
+    int rows = page_rows;
+    if (n > 1) rows = ((page_rows + n - 1) / n + 63) / 64 * 64;
+    const int n_eff = (page_rows + rows - 1) / rows;
+    if (n_eff != n) continue;
+    const int64_t items = pairs * n_eff;
+    const int64_t rounds = (items + grid_max - 1) / grid_max;
+    const double cost = (double)rounds * ((double)rows * p->row_bytes + 8.0 * d_s * 4 + 16384.0);
+    if (cost < best * 0.999) { best = cost; best_n = n_eff; best_rows = rows; }
+  }
+  p->n_split = best_n;
+  p->split_rows = best_rows < 1 ? 1 : best_rows;
+  p->n_items = pairs * p->n_split;
+  p->grid = (int)(p->n_items < grid_max ? p->n_items : grid_max);
+  if (p->grid < 1) p->grid = 1;
+  p->acc_bytes = align_up((size_t)p->n_items * d_s * sizeof(float), 256);
+  p->ml_bytes = align_up((size_t)p->n_items * 2 * sizeof(float), 256);
+  return XENCB_OK;
+}
+
+int g_read_smem_done[3][2][2][kMaxDev];
+
+template <typename TD>
+void launch_sel_apply(const void* delta, const void* h, int h_dtype, int64_t n_rows, int d, const float* w,
+                             int n_cand, int pos, float alpha, void* out, cudaStream_t st) {
+  const TD* dp = static_cast<const TD*>(delta);
+  TD* op = static_cast<TD*>(out);
+  switch (h_dtype) {
+    case XENCB_F32:
+      selector_apply_kernel<TD, float><<<(unsigned)n_rows, 256, 0, st>>>(dp, static_cast<const float*>(h), d, w,
+                                                                         n_cand, pos, alpha, op);
+      break;
+    case XENCB_F16:
+      selector_apply_kernel<TD, __half><<<(unsigned)n_rows, 256, 0, st>>>(dp, static_cast<const __half*>(h), d, w,
+                                                                          n_cand, pos, alpha, op);
+      break;
+    default:
+      selector_apply_kernel<TD, __nv_bfloat16><<<(unsigned)n_rows, 256, 0, st>>>(
+          dp, static_cast<const __nv_bfloat16*>(h), d, w, n_cand, pos, alpha, op);
+      break;
+  }
+}
+
+}  // namespace
+}  // namespace xencb
+
+using namespace xencb;
+
+extern "C" {
+
+int xencb_abi_version(void) { return XENCB_ABI_VERSION; }
+
+const char* xencb_last_error(void) { return g_err.c_str(); }
+
+int xencb_device_status(void* stream, int clear, unsigned int* status_out) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  unsigned int v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_dev_status, sizeof(v));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyFromSymbol(status)");
+  if (clear && v) {
+    const unsigned int z = 0;
+    e = cudaMemcpyToSymbol(g_dev_status, &z, sizeof(z));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyToSymbol(status)");
+  }
+  if (status_out) *status_out = v;
+  return XENCB_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ project_in
+size_t xencb_project_in_workspace(int64_t n_rows, int d_m, int d_s) {
+  DevInfo di;
+  if (device_info(&di)) return 0;
+  if (n_rows <= 0 || d_m <= 0 || d_s <= 0) return 0;
+  return plan_gemm(n_rows, d_s, d_m, di.sms).part_bytes;
+}
+
+int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const float* w_in, const float* b_in,
+                     int d_s, int flags, const float* gate_w, float gate_b, const float* sel_w, const float* sel_b,
+                     int n_cand, float rms_eps, float* q_out, float* gate_out, float* rstd_out, float* z_out,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  if (flags & ~(XENCB_PIN_RMS | XENCB_PIN_L2)) return fail(XENCB_EINVAL, "project_in: unknown flags 0x%x", flags);
+  if (!h || !w_in || !q_out) return fail(XENCB_EINVAL, "project_in: h, w_in and q_out are required");
+  if (n_rows <= 0 || d_m <= 0 || d_s <= 0)
+    return fail(XENCB_EINVAL, "project_in: n_rows=%lld d_m=%d d_s=%d must be positive", (long long)n_rows, d_m, d_s);
+  if (!elem_size(h_dtype)) return fail(XENCB_EINVAL, "project_in: h_dtype %d unknown", h_dtype);
+  if (gate_w && !gate_out) return fail(XENCB_EINVAL, "project_in: gate_w given without gate_out");
+  if (sel_w && (!z_out || n_cand <= 0 || n_cand > 32))
+    return fail(XENCB_EINVAL, "project_in: selector needs z_out and 1 <= n_cand <= 32 (got %d)", n_cand);
+  DevInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  const GemmPlan gp = plan_gemm(n_rows, d_s, d_m, di.sms);
+  if (!workspace || workspace_bytes < gp.part_bytes || !aligned(workspace, 256))
+    return fail(XENCB_EINVAL, "project_in: workspace needs %zu bytes, 256-byte aligned (got %zu)", gp.part_bytes,
+                workspace_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float* part = static_cast<float*>(workspace);
+  switch (h_dtype) {
+    case XENCB_F32: launch_gemm<float>(h, n_rows, d_m, w_in, d_s, gp, part, st); break;
+    case XENCB_F16: launch_gemm<__half>(h, n_rows, d_m, w_in, d_s, gp, part, st); break;
+    default: launch_gemm<__nv_bfloat16>(h, n_rows, d_m, w_in, d_s, gp, part, st); break;
+  }
+  XENCB_CHECK_LAUNCH("project_in gemm launch");
+#define XENCB_PIN(T)                                                                                         \
+  project_in_finish_kernel<T><<<(unsigned)n_rows, 256, 0, st>>>(                                            \
+      static_cast<const T*>(h), d_m, part, gp.splits, n_rows, d_s, flags, b_in, gate_w, gate_b, sel_w, sel_b,    \
+      n_cand, \
+      rms_eps, q_out, gate_out, rstd_out, z_out)
+  switch (h_dtype) {
+    case XENCB_F32: XENCB_PIN(float); break;
+    case XENCB_F16: XENCB_PIN(__half); break;
+    default: XENCB_PIN(__nv_bfloat16); break;
+  }
+#undef XENCB_PIN
+  XENCB_CHECK_LAUNCH("project_in finish launch");
+  return XENCB_OK;
+}
+
+int xencb_rms_norm(const void* h, int h_dtype, int64_t n_rows, int d_m, float eps, float* out, void* stream) {
+  if (!h || !out) return fail(XENCB_EINVAL, "rms_norm: h and out are required");
+  if (n_rows <= 0 || d_m <= 0) return fail(XENCB_EINVAL, "rms_norm: sizes must be positive");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (h_dtype) {
+    case XENCB_F32: rms_norm_kernel<float><<<(unsigned)n_rows, 256, 0, st>>>(static_cast<const float*>(h), d_m, eps, out); break;
+    case XENCB_F16: rms_norm_kernel<__half><<<(unsigned)n_rows, 256, 0, st>>>(static_cast<const __half*>(h), d_m, eps, out); break;
+    case XENCB_BF16:
+      rms_norm_kernel<__nv_bfloat16><<<(unsigned)n_rows, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(h), d_m, eps, out);
+      break;
+    default: return fail(XENCB_EINVAL, "rms_norm: h_dtype %d unknown", h_dtype);
+  }
+  XENCB_CHECK_LAUNCH("rms_norm launch");
+  return XENCB_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ route
+int xencb_route_k(int top_k, int n_chunks) { return (top_k > 0 && top_k < n_chunks) ? top_k : n_chunks; }
+
+int xencb_route(const float* q, int64_t n_rows, int d_s, const float* S, int n_chunks, const int32_t* n_chunks_of,
+                int64_t rows_per_lib, int64_t n_lib, float route_temp, int top_k, int32_t* idx, float* wk,
+                float* w_dense, float* logit_out, void* stream) {
+  if (!q || !S || !idx || !wk) return fail(XENCB_EINVAL, "route: q, S, idx and wk are required");
+  if (n_rows <= 0 || d_s <= 0 || n_chunks <= 0 || rows_per_lib <= 0 || n_lib <= 0)
+    return fail(XENCB_EINVAL, "route: sizes must be positive (n_rows=%lld d_s=%d C=%d rows_per_lib=%lld n_lib=%lld)",
+                (long long)n_rows, d_s, n_chunks, (long long)rows_per_lib, (long long)n_lib);
+  if ((n_rows + rows_per_lib - 1) / rows_per_lib > n_lib)
+    return fail(XENCB_EINVAL, "route: %lld rows at %lld rows per Library need more than %lld Libraries",
+                (long long)n_rows, (long long)rows_per_lib, (long long)n_lib);
+  if (top_k < 0) return fail(XENCB_EINVAL, "route: top_k=%d must be >= 0", top_k);
+  if ((size_t)n_chunks * 4 * TOPK_WARPS > 200 * 1024)
+    return fail(XENCB_ENOTSUP, "route: C=%d chunks exceed the router's shared-memory row buffer", n_chunks);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // logits go to logit_out when given, else to w_dense, which the top-k pass then overwrites row by row
+  float* lg = logit_out ? logit_out : w_dense;
+  if (!lg) return fail(XENCB_EINVAL, "route: one of w_dense / logit_out must be given (logit buffer)");
+  const int64_t warps = n_rows * n_chunks;
+  const int64_t blocks = (warps + 7) / 8;
+  route_logits_kernel<<<(unsigned)blocks, 256, 0, st>>>(q, n_rows, d_s, S, n_chunks, n_chunks_of, rows_per_lib,
+                                                        route_temp, lg);
+  XENCB_CHECK_LAUNCH("route_logits launch");
+  static int done[kMaxDev];
+  const int smem = n_chunks * 4 * TOPK_WARPS;
+  int rc = ensure_smem(route_topk_kernel, smem > 48 * 1024 ? smem : 48 * 1024, done);
+  if (rc) return rc;
+  const int k_out = xencb_route_k(top_k, n_chunks);
+  route_topk_kernel<<<(unsigned)((n_rows + TOPK_WARPS - 1) / TOPK_WARPS), TOPK_WARPS * 32, smem, st>>>(
+      lg, n_rows, n_chunks, n_chunks_of, rows_per_lib, top_k, k_out, idx, wk, w_dense);
+  XENCB_CHECK_LAUNCH("route_topk launch");
+  return XENCB_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ read
+size_t xencb_read_decode_workspace(int64_t n_rows, int k, int d_s, int page_rows, int slots_dtype) {
+  if (n_rows <= 0 || k <= 0 || d_s <= 0 || page_rows <= 0) return 0;
+  ReadPlan p;
+  if (plan_read(n_rows, k, d_s, page_rows, slots_dtype, &p)) return 0;
+  return p.acc_bytes + p.ml_bytes;
+}
+
+int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots, int slots_dtype,
+                      int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of, const int32_t* n_valid,
+                      int n_chunks, int64_t rows_per_lib, int64_t n_lib, const int32_t* idx, const float* wk, int k,
+                      float read_temp, int read_softmax, float* r_out, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  if (!q || !slots || !page_of || !n_valid || !idx || !wk || !r_out)
+    return fail(XENCB_EINVAL, "read_decode: q, slots, page_of, n_valid, idx, wk and r_out are required");
+  if (n_rows <= 0 || d_s <= 0 || page_rows <= 0 || n_chunks <= 0 || rows_per_lib <= 0 || n_lib <= 0 || k <= 0)
+    return fail(XENCB_EINVAL, "read_decode: sizes must be positive");
+  if ((n_rows + rows_per_lib - 1) / rows_per_lib > n_lib)
+    return fail(XENCB_EINVAL, "read_decode: %lld rows need more than %lld Libraries", (long long)n_rows,
+                (long long)n_lib);
+  const int es = elem_size(slots_dtype);
+  if (!es) return fail(XENCB_EINVAL, "read_decode: slots_dtype %d unknown", slots_dtype);
+  if (n_pages <= 0) return fail(XENCB_EINVAL, "read_decode: n_pages=%lld must be positive", (long long)n_pages);
+  if (page_stride < (int64_t)page_rows * d_s)
+    return fail(XENCB_EINVAL, "read_decode: page_stride %lld < page_rows*d_s %lld", (long long)page_stride,
+                (long long)page_rows * d_s);
+  if (!aligned(slots, 16) || (page_stride * es) % 16 != 0 || !aligned(q, 16) || !aligned(r_out, 16))
+    return fail(XENCB_EINVAL, "read_decode: slots, q, r_out and page_stride*elem must be 16-byte aligned");
+  ReadPlan p;
+  int rc = plan_read(n_rows, k, d_s, page_rows, slots_dtype, &p);
+  if (rc) return rc;
+  if (!workspace || !aligned(workspace, 256) || workspace_bytes < p.acc_bytes + p.ml_bytes)
+    return fail(XENCB_EINVAL, "read_decode: workspace needs %zu bytes, 256-byte aligned (got %zu)",
+                p.acc_bytes + p.ml_bytes, workspace_bytes);
+  ReadArgs a;
+  a.q = q; a.n_rows = n_rows; a.d_s = d_s;
+  a.slots = static_cast<const char*>(slots);
+  a.n_pages = n_pages;
+  a.page_stride_bytes = page_stride * es;
+  a.page_rows = page_rows;
+  a.page_of = page_of; a.n_valid = n_valid; a.n_chunks = n_chunks; a.rows_per_lib = rows_per_lib;
+  a.idx = idx; a.wk = wk; a.k = k;
+  a.qscale = read_softmax ? read_temp * 1.4426950408889634f : 1.f;
+  a.n_split = p.n_split; a.split_rows = p.split_rows; a.rps = p.rps; a.n_stage = p.n_stage;
+  a.row_bytes = p.row_bytes; a.nvec = p.nvec; a.n_items = p.n_items;
+  a.part_acc = static_cast<float*>(workspace);
+  a.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + p.acc_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int di = slots_dtype, vi = p.vpt == 1 ? 0 : 1, si = read_softmax ? 1 : 0;
+  int* done = g_read_smem_done[di][vi][si];
+  rc = XENCB_OK;
+  {
+    auto run = [&](auto tag_t, auto tag_v, auto tag_s) -> int {
+      using T = typename decltype(tag_t)::type;
+      constexpr int V = decltype(tag_v)::value;
+      constexpr bool S = decltype(tag_s)::value;
+      auto k1 = read_decode_kernel<T, V, S>;
+      int r2 = ensure_smem(k1, (int)p.smem, done);
+      if (r2) return r2;
+      k1<<<p.grid, p.threads, p.smem, st>>>(a);
+      XENCB_CHECK_LAUNCH("read_decode_kernel launch");
+      dim3 mg((unsigned)n_rows, (d_s + 511) / 512);
+      read_merge_kernel<S><<<mg, 128, 0, st>>>(a, r_out);
+      XENCB_CHECK_LAUNCH("read_merge_kernel launch");
+      return XENCB_OK;
+    };
+    struct F32T { using type = float; };
+    struct F16T { using type = __half; };
+    struct BF16T { using type = __nv_bfloat16; };
+    using V1 = std::integral_constant<int, 1>;
+    using V2 = std::integral_constant<int, 2>;
+    using ST = std::true_type;
+    using SF = std::false_type;
+    if (slots_dtype == XENCB_F16) {
+      if (p.vpt == 1) rc = read_softmax ? run(F16T{}, V1{}, ST{}) : run(F16T{}, V1{}, SF{});
+      else rc = read_softmax ? run(F16T{}, V2{}, ST{}) : run(F16T{}, V2{}, SF{});
+    } else if (slots_dtype == XENCB_BF16) {
+      if (p.vpt == 1) rc = read_softmax ? run(BF16T{}, V1{}, ST{}) : run(BF16T{}, V1{}, SF{});
+      else rc = read_softmax ? run(BF16T{}, V2{}, ST{}) : run(BF16T{}, V2{}, SF{});
+    } else {
+      if (p.vpt == 1) rc = read_softmax ? run(F32T{}, V1{}, ST{}) : run(F32T{}, V1{}, SF{});
+      else rc = read_softmax ? run(F32T{}, V2{}, ST{}) : run(F32T{}, V2{}, SF{});
+    }
+  }
+  return rc;
+}
+
+// ------------------------------------------------------------------------------------------------ project_out
+size_t xencb_project_out_workspace(int64_t n_rows, int d_s, int d_m) {
+  DevInfo di;
+  if (device_info(&di)) return 0;
+  if (n_rows <= 0 || d_m <= 0 || d_s <= 0) return 0;
+  return plan_gemm(n_rows, d_m, d_s, di.sms).part_bytes;
+}
+
+int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_out, const float* b_out, int d_m,
+                      float scale, const float* gate, const float* sel_w, float log_alpha, const float* pos_mask,
+                      const void* h, int h_dtype, void* delta_out, void* h_out, float* rel_out, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  if (!r || !w_out || !h) return fail(XENCB_EINVAL, "project_out: r, w_out and h are required");
+  if (n_rows <= 0 || d_m <= 0 || d_s <= 0) return fail(XENCB_EINVAL, "project_out: sizes must be positive");
+  if (!elem_size(h_dtype)) return fail(XENCB_EINVAL, "project_out: h_dtype %d unknown", h_dtype);
+  if ((size_t)d_m * 4 > 200 * 1024) return fail(XENCB_ENOTSUP, "project_out: d_m=%d too large", d_m);
+  DevInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  const GemmPlan gp = plan_gemm(n_rows, d_m, d_s, di.sms);
+  if (!workspace || workspace_bytes < gp.part_bytes || !aligned(workspace, 256))
+    return fail(XENCB_EINVAL, "project_out: workspace needs %zu bytes, 256-byte aligned (got %zu)", gp.part_bytes,
+                workspace_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float* part = static_cast<float*>(workspace);
+  launch_gemm<float>(r, n_rows, d_s, w_out, d_m, gp, part, st);
+  XENCB_CHECK_LAUNCH("project_out gemm launch");
+  const float alpha = expf(log_alpha);
+  const int smem = d_m * 4;
+#define XENCB_POUT(T)                                                                                          \
+  do {                                                                                                         \
+    static int done[kMaxDev];                                                                                  \
+    int rc2 = ensure_smem(project_out_finish_kernel<T>, smem > 48 * 1024 ? smem : 48 * 1024, done);          \
+    if (rc2) return rc2;                                                                                       \
+    project_out_finish_kernel<T><<<(unsigned)n_rows, 256, smem, st>>>(                                        \
+        part, gp.splits, n_rows, d_m, b_out, scale, gate, sel_w, alpha, pos_mask, static_cast<const T*>(h),   \
+        static_cast<T*>(delta_out), static_cast<T*>(h_out), rel_out);                                          \
+  } while (0)
+  switch (h_dtype) {
+    case XENCB_F32: XENCB_POUT(float); break;
+    case XENCB_F16: XENCB_POUT(__half); break;
+    default: XENCB_POUT(__nv_bfloat16); break;
+  }
+#undef XENCB_POUT
+  XENCB_CHECK_LAUNCH("project_out finish launch");
+  return XENCB_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ selector
+int xencb_selector_weights(const float* z, int64_t n_rows, int n_cand, int k, int straight_through, float* w_out,
+                           void* stream) {
+  if (!z || !w_out) return fail(XENCB_EINVAL, "selector_weights: z and w_out are required");
+  if (n_rows <= 0 || n_cand <= 0 || n_cand > 32)
+    return fail(XENCB_EINVAL, "selector_weights: need n_rows > 0 and 1 <= n_cand <= 32 (got %d)", n_cand);
+  if (k < 1 || k > n_cand) return fail(XENCB_EINVAL, "k=%d must be in [1, %d]", k, n_cand);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  selector_weights_kernel<<<(unsigned)((n_rows + 3) / 4), 128, 0, st>>>(z, n_rows, n_cand, k, straight_through,
+                                                                          w_out);
+  XENCB_CHECK_LAUNCH("selector_weights launch");
+  return XENCB_OK;
+}
+
+int xencb_selector_logits(const void* h, int h_dtype, int64_t n_rows, int d_m, const float* u_w, const float* u_b,
+                          int n_cand, int rms, float rms_eps, float* z_out, void* stream) {
+  if (!h || !u_w || !z_out) return fail(XENCB_EINVAL, "selector_logits: h, u_w and z_out are required");
+  if (n_rows <= 0 || d_m <= 0 || n_cand <= 0 || n_cand > 32)
+    return fail(XENCB_EINVAL, "selector_logits: need positive sizes and n_cand <= 32 (got %d)", n_cand);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (h_dtype) {
+    case XENCB_F32:
+      selector_logits_kernel<float><<<(unsigned)n_rows, 256, 0, st>>>(static_cast<const float*>(h), d_m, u_w, u_b,
+                                                                       n_cand, rms, rms_eps, z_out);
+      break;
+    case XENCB_F16:
+      selector_logits_kernel<__half><<<(unsigned)n_rows, 256, 0, st>>>(static_cast<const __half*>(h), d_m, u_w, u_b,
+                                                                        n_cand, rms, rms_eps, z_out);
+      break;
+    case XENCB_BF16:
+      selector_logits_kernel<__nv_bfloat16><<<(unsigned)n_rows, 256, 0, st>>>(
+          static_cast<const __nv_bfloat16*>(h), d_m, u_w, u_b, n_cand, rms, rms_eps, z_out);
+      break;
+    default: return fail(XENCB_EINVAL, "selector_logits: h_dtype %d unknown", h_dtype);
+  }
+  XENCB_CHECK_LAUNCH("selector_logits launch");
+  return XENCB_OK;
+}
+
+int xencb_selector_apply(const void* delta, int delta_dtype, const void* h, int h_dtype, int64_t n_rows, int d,
+                         const float* w, int n_cand, int pos, float log_alpha, void* out, void* stream) {
+  if (!delta || !h || !w || !out) return fail(XENCB_EINVAL, "selector_apply: null pointer argument");
+  if (n_rows <= 0 || d <= 0 || n_cand <= 0 || pos < 0 || pos >= n_cand)
+    return fail(XENCB_EINVAL, "selector_apply: bad sizes (n_rows=%lld d=%d n_cand=%d pos=%d)", (long long)n_rows, d,
+                n_cand, pos);
+  if (!elem_size(delta_dtype) || !elem_size(h_dtype)) return fail(XENCB_EINVAL, "selector_apply: unknown dtype");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float alpha = expf(log_alpha);
+  switch (delta_dtype) {
+    case XENCB_F32: launch_sel_apply<float>(delta, h, h_dtype, n_rows, d, w, n_cand, pos, alpha, out, st); break;
+    case XENCB_F16: launch_sel_apply<__half>(delta, h, h_dtype, n_rows, d, w, n_cand, pos, alpha, out, st); break;
+    default: launch_sel_apply<__nv_bfloat16>(delta, h, h_dtype, n_rows, d, w, n_cand, pos, alpha, out, st); break;
+  }
+  XENCB_CHECK_LAUNCH("selector_apply launch");
+  return XENCB_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ summaries
+int xencb_summaries(const void* slots, int slots_dtype, int64_t n_pages, int64_t page_stride, int page_rows,
+                    const int32_t* page_of,
+                    const int32_t* n_valid, int64_t n_lib, int n_chunks, int d_s, float* S_out, void* stream) {
+  if (!slots || !page_of || !n_valid || !S_out) return fail(XENCB_EINVAL, "summaries: null pointer argument");
+  if (n_lib <= 0 || n_chunks <= 0 || d_s <= 0 || page_rows <= 0 || n_pages <= 0)
+    return fail(XENCB_EINVAL, "summaries: sizes must be positive");
+  if (page_stride < (int64_t)page_rows * d_s) return fail(XENCB_EINVAL, "summaries: page_stride too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned blocks = (unsigned)(n_lib * n_chunks);
+  switch (slots_dtype) {
+    case XENCB_F32:
+      summaries_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(slots), n_pages, page_stride, page_rows,
+                                                      page_of, n_valid, n_chunks, d_s, S_out);
+      break;
+    case XENCB_F16:
+      summaries_kernel<__half><<<blocks, 256, 0, st>>>(static_cast<const __half*>(slots), n_pages, page_stride, page_rows,
+                                                       page_of, n_valid, n_chunks, d_s, S_out);
+      break;
+    case XENCB_BF16:
+      summaries_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(slots), n_pages, page_stride,
+                                                              page_rows, page_of, n_valid, n_chunks, d_s, S_out);
+      break;
+    default: return fail(XENCB_EINVAL, "summaries: slots_dtype %d unknown", slots_dtype);
+  }
+  XENCB_CHECK_LAUNCH("summaries launch");
+  return XENCB_OK;
+}
+
+}  // extern "C"

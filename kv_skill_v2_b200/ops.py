@@ -1,0 +1,308 @@
+"""Tensor-level entry points of the Library read, one per C-ABI call (include/xencb.h).
+
+Each function checks its tensors (CUDA device, dtype, contiguity), allocates outputs and the scratch
+workspace through torch's caching allocator, and launches on the current torch stream of the tensors'
+device. There is no CPU path: a CPU tensor raises RuntimeError.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _native as N
+
+_DT = {torch.float32: N.F32, torch.float16: N.F16, torch.bfloat16: N.BF16}
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(dev: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _cuda(what: str, *ts) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(f"{what}: xencb kernels run on CUDA tensors only (got a {t.device} tensor); "
+                               "the Library read has no CPU path")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"{what}: tensors on {dev} and {t.device}")
+    return dev
+
+
+def _f32(t: Optional[torch.Tensor], what: str) -> Optional[torch.Tensor]:
+    if t is None:
+        return None
+    if t.dtype != torch.float32:
+        raise ValueError(f"{what} must be float32, got {t.dtype}")
+    return t.contiguous()
+
+
+def _hdt(t: torch.Tensor, what: str) -> int:
+    if t.dtype not in _DT:
+        raise ValueError(f"{what}: dtype {t.dtype} not supported (float32 / float16 / bfloat16)")
+    return _DT[t.dtype]
+
+
+class _on_device:
+    """Make `dev` the current CUDA device for the duration (the C side queries it)."""
+
+    def __init__(self, dev: torch.device):
+        self.dev = dev.index if dev.index is not None else torch.cuda.current_device()
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.dev:
+            self.prev = cur
+            torch.cuda.set_device(self.dev)
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+
+
+def _workspace(nbytes: int, dev: torch.device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=dev)
+
+
+# ------------------------------------------------------------------------------------------------ rms / project
+def rms_norm(h: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """float32 rms_norm of the last dim (deltaskill.derive.rms_norm as used at xenc/injector.py:235)."""
+    dev = _cuda("rms_norm", h)
+    h2 = h.reshape(-1, h.shape[-1]).contiguous()
+    out = torch.empty(h2.shape, dtype=torch.float32, device=dev)
+    with _on_device(dev):
+        N.call("xencb_rms_norm", _ptr(h2), _hdt(h2, "h"), h2.shape[0], h2.shape[1], eps, _ptr(out), _stream(dev))
+    return out.view(*h.shape[:-1], h.shape[-1])
+
+
+def project_in(h2: torch.Tensor, w_in: torch.Tensor, b_in=None, *, rms: bool = True, l2: bool = True,
+               gate_w=None, gate_b: float = 0.0, sel_w=None, sel_b=None, eps: float = 1e-6):
+    """(q [R, d_s], gate [R] | None, rstd [R], z [R, n_cand] | None) for rows h2 [R, d_m].
+
+    q = L2((rms_norm(h2) if rms else h2) @ w_in^T + b_in) (L2 only if l2); w_in is [d_s, d_m]."""
+    dev = _cuda("project_in", h2, w_in, b_in, gate_w, sel_w, sel_b)
+    h2 = h2.contiguous()
+    w_in = _f32(w_in, "w_in")
+    R, d_m = h2.shape
+    d_s = w_in.shape[0]
+    if w_in.shape[1] != d_m:
+        raise ValueError(f"w_in is {tuple(w_in.shape)}, expected [d_s, {d_m}]")
+    q = torch.empty(R, d_s, dtype=torch.float32, device=dev)
+    gate = torch.empty(R, dtype=torch.float32, device=dev) if gate_w is not None else None
+    rstd = torch.empty(R, dtype=torch.float32, device=dev)
+    n_cand = 0 if sel_w is None else int(sel_w.shape[0])
+    z = torch.empty(R, n_cand, dtype=torch.float32, device=dev) if sel_w is not None else None
+    flags = (N.PIN_RMS if rms else 0) | (N.PIN_L2 if l2 else 0)
+    # converted inputs are bound to locals so they outlive the launch
+    b_in, gate_w = _f32(b_in, "b_in"), _f32(gate_w, "gate_w")
+    sel_w, sel_b = _f32(sel_w, "sel_w"), _f32(sel_b, "sel_b")
+    with _on_device(dev):
+        ws_bytes = N.lib().xencb_project_in_workspace(R, d_m, d_s)
+        ws = _workspace(ws_bytes, dev)
+        N.call("xencb_project_in", _ptr(h2), _hdt(h2, "h"), R, d_m, _ptr(w_in), _ptr(b_in), d_s, flags,
+               _ptr(gate_w), float(gate_b), _ptr(sel_w), _ptr(sel_b), n_cand, eps, _ptr(q), _ptr(gate),
+               _ptr(rstd), _ptr(z), _ptr(ws), ws.numel(), _stream(dev))
+    return q, gate, rstd, z
+
+
+def project_out(r: torch.Tensor, w_out: torch.Tensor, h2: torch.Tensor, *, b_out=None, scale: float = 1.0,
+                gate=None, sel_w=None, log_alpha: float = 0.0, pos_mask=None, want_delta: bool = True,
+                h_out: Optional[torch.Tensor] = None, want_rel: bool = False):
+    """(delta | None, h_out | None, rel | None).
+
+    d = scale * gate * (r @ w_out^T + b_out); optional LayerSelector matched norm with per-row weight sel_w;
+    d *= pos_mask; delta = d in h2's dtype; h_out = h2 + delta; rel = ||delta|| / (||h2|| + 1e-6)."""
+    dev = _cuda("project_out", r, w_out, h2, b_out, gate, sel_w, pos_mask, h_out)
+    r = _f32(r, "r")
+    w_out = _f32(w_out, "w_out")
+    h2 = h2.contiguous()
+    R, d_s = r.shape
+    d_m = w_out.shape[0]
+    if w_out.shape[1] != d_s or h2.shape != (R, d_m):
+        raise ValueError(f"project_out: r {tuple(r.shape)}, w_out {tuple(w_out.shape)}, h {tuple(h2.shape)}")
+    delta = torch.empty_like(h2) if want_delta else None
+    if h_out is not None and (h_out.shape != h2.shape or h_out.dtype != h2.dtype or not h_out.is_contiguous()):
+        raise ValueError("project_out: h_out must match h (shape, dtype, contiguous)")
+    rel = torch.empty(R, dtype=torch.float32, device=dev) if want_rel else None
+    b_out, gate = _f32(b_out, "b_out"), _f32(gate, "gate")
+    sel_w, pos_mask = _f32(sel_w, "sel_w"), _f32(pos_mask, "pos_mask")
+    with _on_device(dev):
+        ws_bytes = N.lib().xencb_project_out_workspace(R, d_s, d_m)
+        ws = _workspace(ws_bytes, dev)
+        N.call("xencb_project_out", _ptr(r), R, d_s, _ptr(w_out), _ptr(b_out), d_m, float(scale), _ptr(gate),
+               _ptr(sel_w), float(log_alpha), _ptr(pos_mask), _ptr(h2), _hdt(h2, "h"), _ptr(delta), _ptr(h_out),
+               _ptr(rel), _ptr(ws), ws.numel(), _stream(dev))
+    return delta, h_out, rel
+
+
+# ------------------------------------------------------------------------------------------------ routing
+def route_k(top_k: int, n_chunks: int) -> int:
+    return int(top_k) if 0 < int(top_k) < int(n_chunks) else int(n_chunks)
+
+
+def route(q: torch.Tensor, S: torch.Tensor, *, rows_per_lib: int, top_k: int, route_temp: float,
+          n_chunks_of: Optional[torch.Tensor] = None, want_logits: bool = False):
+    """(idx [R, k] int32, wk [R, k], w_dense [R, C], logits [R, C] | None); S is [n_lib, C, d_s] float32."""
+    dev = _cuda("route", q, S, n_chunks_of)
+    q = _f32(q, "q")
+    S = _f32(S, "S")
+    R, d_s = q.shape
+    n_lib, C, d2 = S.shape
+    if d2 != d_s:
+        raise ValueError(f"route: q has d_s={d_s}, S has {d2}")
+    k = route_k(top_k, C)
+    idx = torch.empty(R, k, dtype=torch.int32, device=dev)
+    wk = torch.empty(R, k, dtype=torch.float32, device=dev)
+    w = torch.empty(R, C, dtype=torch.float32, device=dev)
+    lg = torch.empty(R, C, dtype=torch.float32, device=dev) if want_logits else None
+    if n_chunks_of is not None:
+        n_chunks_of = n_chunks_of.to(torch.int32).contiguous()
+    with _on_device(dev):
+        N.call("xencb_route", _ptr(q), R, d_s, _ptr(S), C, _ptr(n_chunks_of), int(rows_per_lib), n_lib,
+               float(route_temp), int(top_k), _ptr(idx), _ptr(wk), _ptr(w), _ptr(lg), _stream(dev))
+    return idx, wk, w, lg
+
+
+# ------------------------------------------------------------------------------------------------ read
+@dataclass
+class Pages:
+    """Device view of one depth of one or more Libraries, in the layout the read kernels take.
+
+    slots    [P, page_rows, d_s] pool (float16 / bfloat16 / float32); page p = slots[p]
+    page_of  [n_lib, C] int32 page of chunk c of Library l
+    n_valid  [n_lib, C] int32 valid rows (the reference's mask, as a length)
+    S        [n_lib, C, d_s] float32 summary keys
+    n_chunks_of [n_lib] int32 chunks per Library (None: all have C)"""
+
+    slots: torch.Tensor
+    page_of: torch.Tensor
+    n_valid: torch.Tensor
+    S: torch.Tensor
+    n_chunks_of: Optional[torch.Tensor] = None
+
+    @property
+    def n_lib(self) -> int:
+        return int(self.page_of.shape[0])
+
+    @property
+    def n_chunks(self) -> int:
+        return int(self.page_of.shape[1])
+
+    @property
+    def d_s(self) -> int:
+        return int(self.slots.shape[-1])
+
+    @property
+    def page_rows(self) -> int:
+        return int(self.slots.shape[1])
+
+    @property
+    def device(self) -> torch.device:
+        return self.slots.device
+
+
+def read_decode(q: torch.Tensor, pages: Pages, idx: torch.Tensor, wk: torch.Tensor, *, rows_per_lib: int,
+                read_temp: float = 12.0, read_softmax: bool = True) -> torch.Tensor:
+    """r [R, d_s] float32: the masked two-level read over each row's routed chunks."""
+    dev = _cuda("read_decode", q, pages.slots, pages.page_of, pages.n_valid, idx, wk)
+    q = _f32(q, "q")
+    wk = _f32(wk, "wk")
+    R, d_s = q.shape
+    slots = pages.slots
+    if not slots.is_contiguous():
+        raise ValueError("read_decode: the slot pool must be contiguous")
+    if slots.shape[-1] != d_s:
+        raise ValueError(f"read_decode: q has d_s={d_s}, slots have {slots.shape[-1]}")
+    if idx.dtype != torch.int32 or idx.shape != wk.shape or idx.shape[0] != R:
+        raise ValueError("read_decode: idx must be int32 [R, k] matching wk")
+    k = int(idx.shape[1])
+    idx = idx.contiguous()
+    r = torch.empty(R, d_s, dtype=torch.float32, device=dev)
+    dt = _hdt(slots, "slots")
+    page_rows = pages.page_rows
+    with _on_device(dev):
+        ws_bytes = N.lib().xencb_read_decode_workspace(R, k, d_s, page_rows, dt)
+        if ws_bytes == 0:
+            N.check(N.EINVAL, "read_decode_workspace")
+        ws = _workspace(ws_bytes, dev)
+        N.call("xencb_read_decode", _ptr(q), R, d_s, _ptr(slots), dt, slots.shape[0], page_rows * d_s, page_rows,
+               _ptr(pages.page_of), _ptr(pages.n_valid), pages.n_chunks, int(rows_per_lib), pages.n_lib,
+               _ptr(idx), _ptr(wk), k, float(read_temp), int(bool(read_softmax)), _ptr(r), _ptr(ws),
+               ws.numel(), _stream(dev))
+    return r
+
+
+# ------------------------------------------------------------------------------------------------ selector
+def selector_logits(h2: torch.Tensor, u_w: torch.Tensor, u_b=None, *, rms: bool, eps: float = 1e-6) -> torch.Tensor:
+    dev = _cuda("selector_logits", h2, u_w, u_b)
+    h2 = h2.contiguous()
+    u_w, u_b = _f32(u_w, "u.weight"), _f32(u_b, "u.bias")
+    z = torch.empty(h2.shape[0], u_w.shape[0], dtype=torch.float32, device=dev)
+    with _on_device(dev):
+        N.call("xencb_selector_logits", _ptr(h2), _hdt(h2, "h"), h2.shape[0], h2.shape[1], _ptr(u_w), _ptr(u_b),
+               u_w.shape[0], int(bool(rms)), eps, _ptr(z), _stream(dev))
+    return z
+
+
+def selector_weights(z: torch.Tensor, k: int, straight_through: bool = False) -> torch.Tensor:
+    dev = _cuda("selector_weights", z)
+    z2 = _f32(z.reshape(-1, z.shape[-1]), "z")
+    w = torch.empty_like(z2)
+    with _on_device(dev):
+        N.call("xencb_selector_weights", _ptr(z2), z2.shape[0], z2.shape[1], int(k), int(bool(straight_through)),
+               _ptr(w), _stream(dev))
+    return w.view(z.shape)
+
+
+def selector_apply(delta: torch.Tensor, h: torch.Tensor, w: torch.Tensor, pos: int, log_alpha: float) -> torch.Tensor:
+    """LayerSelector.apply's matched-norm rescale (xenc/selector.py:106-110); returns delta's dtype."""
+    dev = _cuda("selector_apply", delta, h, w)
+    d2 = delta.reshape(-1, delta.shape[-1]).contiguous()
+    h2 = h.reshape(-1, h.shape[-1]).contiguous()
+    w2 = _f32(w.reshape(-1, w.shape[-1]), "w")
+    if h2.shape != d2.shape or w2.shape[0] != d2.shape[0]:
+        raise ValueError(f"selector_apply: delta {tuple(delta.shape)}, h {tuple(h.shape)}, w {tuple(w.shape)}")
+    out = torch.empty_like(d2)
+    with _on_device(dev):
+        N.call("xencb_selector_apply", _ptr(d2), _hdt(d2, "delta"), _ptr(h2), _hdt(h2, "h"), d2.shape[0],
+               d2.shape[1], _ptr(w2), w2.shape[1], int(pos), float(log_alpha), _ptr(out), _stream(dev))
+    return out.view(delta.shape)
+
+
+# ------------------------------------------------------------------------------------------------ summaries
+def summaries(slots: torch.Tensor, page_of: torch.Tensor, n_valid: torch.Tensor) -> torch.Tensor:
+    """S [n_lib, C, d_s] float32 = L2(mean of the valid rows of each chunk's page)."""
+    dev = _cuda("summaries", slots, page_of, n_valid)
+    if not slots.is_contiguous():
+        raise ValueError("summaries: the slot pool must be contiguous")
+    n_lib, C = page_of.shape
+    d_s = slots.shape[-1]
+    S = torch.empty(n_lib, C, d_s, dtype=torch.float32, device=dev)
+    page_of = page_of.to(torch.int32).contiguous()
+    n_valid = n_valid.to(torch.int32).contiguous()
+    with _on_device(dev):
+        N.call("xencb_summaries", _ptr(slots), _hdt(slots, "slots"), slots.shape[0], slots.shape[1] * d_s,
+               slots.shape[1],
+               _ptr(page_of), _ptr(n_valid), n_lib, C, d_s, _ptr(S), _stream(dev))
+    return S
+
+
+def device_status(dev: torch.device, clear: bool = True) -> int:
+    """Synchronise the current stream of `dev` and return the device status bits (XENCB_DEV_*)."""
+    v = ctypes.c_uint(0)
+    with _on_device(dev):
+        N.call("xencb_device_status", _stream(dev), int(clear), ctypes.byref(v))
+    return int(v.value)

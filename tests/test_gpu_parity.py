@@ -1,0 +1,384 @@
+"""Parity of the CUDA path (through the C ABI) with the reference's outputs and the oracle.
+
+Bar: routing index sets identical per token; outputs within max|out - ref| <= 2e-3 * max|ref|.
+Golden cases come from the reference's own code (tests/golden/make_golden.py); larger cases use seeded
+synthetic inputs checked against the numpy oracle; BASELINE config-2 shapes are checked on a sample of
+documents plus size-independent properties."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import xenc_oracle as X
+from tests._fixtures import TOL, TinyReader, load_case, rel_err, topk_sets
+
+pytestmark = pytest.mark.gpu
+
+READ_CASES = ["cfg1_softmax_top2", "cfg1_dense", "cfg1_linear_top2", "cfg1_topk_eq_C", "cfg1_linear_dense",
+              "small_ragged_top2", "small_ragged_linear", "small_ragged_dense_t3", "one_chunk", "odd_dims_top3"]
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    return torch.device("cuda:0")
+
+
+def _status_clean(dev):
+    from kv_skill_v2_b200 import ops
+    assert ops.device_status(dev) == 0, "a kernel flagged a device status bit"
+
+
+def _pages_from_case(c, dev, slot_dtype=torch.float16):
+    from kv_skill_v2_b200 import ops
+    K = torch.from_numpy(c["K"]).to(dev)
+    C = K.shape[0]
+    nv = torch.from_numpy(c["n_valid"].astype(np.int32)).to(dev).view(1, C)
+    page_of = torch.arange(C, dtype=torch.int32, device=dev).view(1, C)
+    slots = K.to(slot_dtype).contiguous()
+    S = ops.summaries(slots, page_of, nv)
+    return ops.Pages(slots=slots, page_of=page_of, n_valid=nv, S=S)
+
+
+# ------------------------------------------------------------------------------------------------ ops level
+@pytest.mark.parametrize("name", READ_CASES)
+@pytest.mark.parametrize("slot_dtype", [torch.float16, torch.float32])
+def test_read_path_matches_reference(dev, name, slot_dtype):
+    from kv_skill_v2_b200 import ops
+    c = load_case(name)
+    pages = _pages_from_case(c, dev, slot_dtype)
+    assert rel_err(pages.S[0], c["S"]) < 1e-5
+    h = torch.from_numpy(c["h"]).to(dev)
+    h2 = h.reshape(-1, h.shape[-1])
+    W_in_t = torch.from_numpy(c["W_in"]).t().contiguous().to(dev)
+    W_out_t = torch.from_numpy(c["W_out"]).t().contiguous().to(dev)
+    q, _, _, _ = ops.project_in(h2, W_in_t)
+    assert rel_err(q, c["q"].reshape(q.shape)) < 1e-4
+    R = q.shape[0]
+    idx, wk, w, _ = ops.route(q, pages.S, rows_per_lib=R, top_k=int(c["top_k"]), route_temp=float(c["route_temp"]))
+    w_ref = c["w"].reshape(w.shape)
+    assert topk_sets(w) == topk_sets(w_ref), "routing index sets differ from the reference"
+    assert rel_err(w, w_ref) < 1e-4
+    r = ops.read_decode(q, pages, idx, wk, rows_per_lib=R, read_temp=float(c["read_temp"]),
+                        read_softmax=bool(c["read_softmax"]))
+    assert rel_err(r, c["r"].reshape(r.shape)) < TOL
+    delta, _, _ = ops.project_out(r, W_out_t, h2)
+    assert rel_err(delta, c["delta"].reshape(delta.shape)) < TOL
+    _status_clean(dev)
+
+
+def test_route_ties_go_to_lower_index(dev):
+    from kv_skill_v2_b200 import ops
+    S = torch.zeros(1, 6, 8, device=dev)
+    S[0, :, 0] = torch.tensor([0.5, 0.9, 0.9, 0.1, 0.9, 0.2])
+    q = torch.zeros(3, 8, device=dev)
+    q[:, 0] = 1.0
+    idx, wk, w, _ = ops.route(q, S, rows_per_lib=3, top_k=2, route_temp=10.0)
+    assert idx.tolist() == [[1, 2]] * 3
+    assert torch.allclose(wk, torch.full_like(wk, 0.5))
+    assert (w > 0).sum(-1).tolist() == [2, 2, 2]
+
+
+def test_route_chunks_per_library(dev):
+    from kv_skill_v2_b200 import ops
+    g = torch.Generator().manual_seed(3)
+    S = torch.nn.functional.normalize(torch.randn(2, 5, 16, generator=g), dim=-1).to(dev)
+    q = torch.nn.functional.normalize(torch.randn(4, 16, generator=g), dim=-1).to(dev)
+    n_of = torch.tensor([3, 5], dtype=torch.int32, device=dev)
+    for top_k in (0, 2, 4):
+        idx, wk, w, _ = ops.route(q, S, rows_per_lib=2, top_k=top_k, route_temp=10.0, n_chunks_of=n_of)
+        assert (w[:2, 3:] == 0).all(), "chunks beyond a Library's count must get no weight"
+        assert torch.allclose(w.sum(-1), torch.ones(4, device=dev), atol=1e-6)
+        for row in range(4):
+            lib = row // 2
+            wo, _, _ = X.route(q[row:row + 1].cpu().numpy(), S[lib, : int(n_of[lib])].cpu().numpy(), 10.0, top_k)
+            assert topk_sets(w[row:row + 1, : int(n_of[lib])]) == topk_sets(wo)
+
+
+def test_batched_documents_match_reference(dev):
+    """Each row reads its own Library (a paged pool of 4 documents) -- checked per document against
+    reference runs of the single-Library read."""
+    from kv_skill_v2_b200 import ops
+    c = load_case("batch_docs_top2")
+    K = torch.from_numpy(c["K"]).to(dev)  # [B, C, N, d]
+    B, C, N, d = K.shape
+    slots = K.reshape(B * C, N, d).half().contiguous()
+    page_of = torch.arange(B * C, dtype=torch.int32, device=dev).view(B, C)
+    nv = torch.from_numpy(c["n_valid"].astype(np.int32)).to(dev)
+    pages = ops.Pages(slots=slots, page_of=page_of, n_valid=nv, S=ops.summaries(slots, page_of, nv))
+    h = torch.from_numpy(c["h"]).to(dev).reshape(B, -1)
+    q, _, _, _ = ops.project_in(h, torch.from_numpy(c["W_in"]).t().contiguous().to(dev))
+    idx, wk, w, _ = ops.route(q, pages.S, rows_per_lib=1, top_k=2, route_temp=10.0)
+    assert topk_sets(w) == topk_sets(c["w"].reshape(B, C))
+    r = ops.read_decode(q, pages, idx, wk, rows_per_lib=1)
+    assert rel_err(r, c["r"].reshape(B, d)) < TOL
+    _status_clean(dev)
+
+
+def test_selector_kernels_match_reference(dev):
+    from kv_skill_v2_b200 import ops
+    c = dict(np.load(__import__("tests._fixtures", fromlist=["GOLDEN"]).GOLDEN / "selector.npz"))
+    for st in (0, 1):
+        for k in (1, 2, 3):
+            key = f"st{st}_k{k}"
+            hs = torch.from_numpy(c[f"{key}_h"]).to(dev)
+            z = ops.selector_logits(hs[0].reshape(-1, hs.shape[-1]), torch.from_numpy(c[f"{key}_u_w"]).to(dev),
+                                    torch.from_numpy(c[f"{key}_u_b"]).to(dev), rms=True)
+            assert rel_err(z, c[f"{key}_z"].reshape(z.shape)) < 1e-4
+            w = ops.selector_weights(z, k, bool(st))
+            assert topk_sets(w) == topk_sets(c[f"{key}_w"])
+            assert rel_err(w, c[f"{key}_w"].reshape(w.shape)) < 1e-4
+            for i in range(len(c["cand"])):
+                delta = torch.from_numpy(c[f"{key}_delta"][i]).to(dev)
+                out = ops.selector_apply(delta, hs[i], w, i, float(c[f"{key}_log_alpha"]))
+                assert rel_err(out, c[f"{key}_out"][i]) < 1e-4
+    _status_clean(dev)
+
+
+@pytest.mark.parametrize("hdt", [torch.float32, torch.bfloat16, torch.float16])
+def test_projections_with_gate_selector_mask(dev, hdt):
+    """project_in / project_out against the oracle with bias, gate, selector rescale, position mask and a
+    low-precision hidden state (cast, residual add and mag term in h's dtype)."""
+    from kv_skill_v2_b200 import ops
+    g = torch.Generator().manual_seed(7)
+    R, d_m, d_s = 37, 264, 136
+    h = (torch.randn(R, d_m, generator=g) * 2).to(hdt)
+    W_in = torch.randn(d_s, d_m, generator=g) * 0.05
+    b_in = torch.randn(d_s, generator=g) * 0.1
+    gate_w = torch.randn(d_m, generator=g) * 0.1
+    W_out = torch.randn(d_m, d_s, generator=g) * 0.05
+    b_out = torch.randn(d_m, generator=g) * 0.1
+    sel_col = torch.rand(R, generator=g)
+    pm = (torch.rand(R, generator=g) > 0.3).float()
+    r = torch.randn(R, d_s, generator=g)
+    hf = h.float().numpy()
+    hn = X.rms_norm(hf)
+    q_ref = X.query(hn, W_in.t().numpy(), b_in.numpy())
+    g_ref = X.gate(hn, gate_w.numpy(), 0.25)[:, 0]
+    q, gate, rstd, _ = ops.project_in(h.to(dev), W_in.to(dev), b_in.to(dev), gate_w=gate_w.to(dev), gate_b=0.25)
+    assert rel_err(q, q_ref) < 1e-4 and rel_err(gate, g_ref) < 1e-5
+    d = 0.7 * g_ref[:, None] * (r.numpy() @ W_out.t().numpy() + b_out.numpy())
+    d = X.selector_apply(d, hf, sel_col.numpy(), -2.0) * pm.numpy()[:, None]
+    d_h = torch.from_numpy(d.astype(np.float32)).to(hdt)
+    delta, h_new, rel = ops.project_out(r.to(dev), W_out.to(dev), h.to(dev), b_out=b_out.to(dev), scale=0.7,
+                                        gate=gate, sel_w=sel_col.to(dev), log_alpha=-2.0, pos_mask=pm.to(dev),
+                                        want_delta=True, h_out=torch.empty_like(h.to(dev)), want_rel=True)
+    assert delta.dtype == hdt and h_new.dtype == hdt
+    tol = TOL if hdt == torch.float32 else 1e-2
+    assert rel_err(delta.float(), d_h.float()) < tol
+    assert rel_err(h_new.float(), (h.float() + d_h.float()).to(hdt).float()) < tol
+    assert rel_err(rel, X.rel_norm(d_h.float().numpy(), hf)) < tol
+    _status_clean(dev)
+
+
+def test_low_rank_query_two_calls(dev):
+    from kv_skill_v2_b200 import ops
+    g = torch.Generator().manual_seed(8)
+    h = torch.randn(9, 96, generator=g)
+    A1, A2 = torch.randn(16, 96, generator=g) * 0.1, torch.randn(48, 16, generator=g) * 0.1
+    t, _, _, _ = ops.project_in(h.to(dev), A1.to(dev), rms=True, l2=False)
+    q, _, _, _ = ops.project_in(t, A2.to(dev), rms=False, l2=True)
+    ref = X.l2(X.rms_norm(h.numpy()) @ A1.t().numpy() @ A2.t().numpy())
+    assert rel_err(q, ref) < 1e-4
+
+
+# ------------------------------------------------------------------------------------------------ API level
+def test_injector_branch_cfg1(dev):
+    from kv_skill_v2_b200 import Library, LibraryInjector, LinearInterface
+    c = load_case("cfg1_softmax_top2")
+    reader = TinyReader(8, 8).to(dev)
+    li = 4
+    rows = [torch.from_numpy(c["K"][i, :n]).float() for i, n in enumerate(c["n_valid"])]
+    lib = Library([{"K": {0.5: r}} for r in rows], [li], [0.5])
+    itf = LinearInterface(torch.from_numpy(c["W_in"]), torch.from_numpy(c["W_out"]), [li]).to(dev)
+    for top_k, name in ((2, "cfg1_softmax_top2"), (0, "cfg1_dense")):
+        ref = load_case(name)
+        inj = LibraryInjector(reader, itf, top_k=top_k)
+        inj.load_library(lib)
+        with torch.no_grad():
+            delta = inj._branch(torch.from_numpy(c["h"]).to(dev), li)
+        assert topk_sets(inj.last_route) == topk_sets(ref["w"])
+        assert rel_err(delta, ref["delta"]) < TOL
+        inj.detach()
+
+
+def test_hooked_model_with_interface_and_selector(dev):
+    """Full hook path: ModelInterface (gate, gain, B), LayerSelector over 8 candidate depths, top-4 routing;
+    the model output and mag terms match the reference's hooked forward."""
+    from kv_skill_v2_b200 import CAND, LayerSelector, Library, LibraryInjector, ModelInterface
+    c = load_case("hooked")
+    d_m = c["x"].shape[-1]
+    L = 10
+    reader = TinyReader(d_m, L)
+    with torch.no_grad():
+        for i, blk in enumerate(reader.model.layers):
+            blk.weight.copy_(torch.from_numpy(c[f"blk{i}_w"]))
+            blk.bias.copy_(torch.from_numpy(c[f"blk{i}_b"]))
+    reader = reader.to(dev).eval().requires_grad_(False)
+    layers = [int(x) for x in c["layers"]]
+    d_s = c[f"K_{layers[0]}"].shape[-1]
+    chunks = [{"K": {float(r): torch.from_numpy(c[f"K_{li}"][i, :n]) for r, li in zip(CAND, layers)}}
+              for i, n in enumerate(c["n"])]
+    lib = Library(chunks, layers, CAND)
+    itf = ModelInterface(d_m, d_s, layers)
+    with torch.no_grad():
+        itf.A.weight.copy_(torch.from_numpy(c["A_w"]))
+        itf.B.weight.copy_(torch.from_numpy(c["B_w"]))
+        itf.gate_w.copy_(torch.from_numpy(c["gate_w"]))
+        itf.gate_b.copy_(torch.from_numpy(c["gate_b"]))
+        itf.log_gain.copy_(torch.from_numpy(c["log_gain"]))
+    itf = itf.to(dev).requires_grad_(False)
+    sel = LayerSelector(d_m, layers, k=2, alpha_init=0.05)
+    with torch.no_grad():
+        sel.u.weight.copy_(torch.from_numpy(c["u_w"]))
+        sel.u.bias.copy_(torch.from_numpy(c["u_b"]))
+        sel.log_alpha.fill_(float(c["log_alpha"]))
+    sel = sel.to(dev).requires_grad_(False)
+    x = torch.from_numpy(c["x"]).to(dev)
+    with torch.no_grad():
+        assert rel_err(reader(x), c["bare"]) < 1e-5
+    for use_sel in (0, 1):
+        inj = LibraryInjector(reader, itf, top_k=4, selector=sel if use_sel else None)
+        inj.load_library(lib)
+        with torch.no_grad():
+            y = reader(x)
+        assert rel_err(y, c[f"out_sel{use_sel}"]) < TOL
+        mags = np.array([float(m) for m in inj.mag_terms], np.float32)
+        assert mags.shape == c[f"mag_sel{use_sel}"].shape
+        assert np.abs(mags - c[f"mag_sel{use_sel}"]).max() <= TOL * np.abs(c[f"mag_sel{use_sel}"]).max()
+        if use_sel:
+            assert topk_sets(sel.weights()) == topk_sets(c["sel_w"])
+        inj.detach()
+    _status_clean(dev)
+
+
+def test_noop_at_init_and_unload(dev):
+    from kv_skill_v2_b200 import DEPTHS, Library, LibraryInjector, injection_layers, make_interface, rho_layer_map
+    reader = TinyReader(40, 8).to(dev).requires_grad_(False)
+    layers = injection_layers(reader, DEPTHS)
+    itf = make_interface(40, 24, layers).to(dev).requires_grad_(False)
+    g = torch.Generator().manual_seed(9)
+    rmap = rho_layer_map(reader, DEPTHS)
+    lib = Library([{"K": {r: torch.nn.functional.normalize(torch.randn(n, 24, generator=g), dim=-1)
+                          for r in DEPTHS}} for n in (5, 9, 3)], [rmap[r] for r in DEPTHS], DEPTHS)
+    x = torch.randn(2, 7, 40, generator=g).to(dev)
+    with torch.no_grad():
+        bare = reader(x)
+    inj = LibraryInjector(reader, itf, top_k=2)
+    inj.load_library(lib)
+    with torch.no_grad():
+        assert torch.equal(reader(x), bare), "zero-init B must be a no-op"
+    assert len(inj.mag_terms) == len(layers) and all(float(m) == 0 for m in inj.mag_terms)
+    inj.unload()
+    assert inj.mag_terms == [] and inj.last_route is None
+    inj.detach()
+
+
+def test_duck_selector_and_forward_only_guard(dev):
+    from kv_skill_v2_b200 import DEPTHS, Library, LibraryInjector, LinearInterface, injection_layers, rho_layer_map
+
+    class Halver:
+        def __init__(self):
+            self.resets, self.applied = 0, []
+
+        def reset(self):
+            self.resets += 1
+
+        def apply(self, delta, h, li):
+            self.applied.append(li)
+            return 0.5 * delta
+
+    reader = TinyReader(32, 8).to(dev).requires_grad_(False)
+    layers = injection_layers(reader, DEPTHS)
+    g = torch.Generator().manual_seed(10)
+    itf = LinearInterface(torch.randn(32, 32, generator=g) * 0.3, torch.randn(32, 32, generator=g) * 0.3,
+                          layers).to(dev).requires_grad_(False)
+    rmap = rho_layer_map(reader, DEPTHS)
+    lib = Library([{"K": {r: torch.nn.functional.normalize(torch.randn(6, 32, generator=g), dim=-1)
+                          for r in DEPTHS}} for _ in range(3)], [rmap[r] for r in DEPTHS], DEPTHS)
+    x = torch.randn(2, 7, 32, generator=g).to(dev)
+    base = LibraryInjector(reader, itf)
+    base.load_library(lib)
+    with torch.no_grad():
+        full = reader(x)
+    base.detach()
+    sel = Halver()
+    inj = LibraryInjector(reader, itf, selector=sel)
+    inj.load_library(lib)
+    with torch.no_grad():
+        reader(x)
+        reader(x)
+        halved = reader(x)
+    assert sel.resets == 3 and sel.applied == layers * 3
+    assert (halved - full).abs().max() > 1e-4
+    inj.detach()
+    itf.requires_grad_(True)
+    inj = LibraryInjector(reader, itf)
+    inj.load_library(lib)
+    with pytest.raises(RuntimeError, match="forward-only"):
+        reader(x)
+    inj.detach()
+
+
+# ------------------------------------------------------------------------------------------------ full size
+def _cfg2_sample(dev, n_docs=8, seed=0):
+    """BASELINE config-2 shapes (C=64 x 512 slots, d_s=2048, d_m=4096, top-4, T=1) for n_docs documents."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    C, N, d_s, d_m = 64, 512, 2048, 4096
+    slots = torch.randn(n_docs * C, N, d_s, generator=g, device=dev)
+    slots = (slots / slots.norm(dim=-1, keepdim=True)).half()
+    nv = torch.full((n_docs, C), N, dtype=torch.int32, device=dev)
+    nv[:, -1] = torch.randint(1, N + 1, (n_docs,), generator=g, device=dev, dtype=torch.int32)
+    page_of = torch.arange(n_docs * C, dtype=torch.int32, device=dev).view(n_docs, C)
+    h = torch.randn(n_docs, d_m, generator=g, device=dev)
+    W_in = torch.randn(d_s, d_m, generator=g, device=dev) * 0.02
+    W_out = torch.randn(d_m, d_s, generator=g, device=dev) * 0.02
+    return slots, nv, page_of, h, W_in, W_out
+
+
+def test_config2_sample_matches_oracle(dev):
+    from kv_skill_v2_b200 import ops
+    slots, nv, page_of, h, W_in, W_out = _cfg2_sample(dev, n_docs=6)
+    S = ops.summaries(slots, page_of, nv)
+    pages = ops.Pages(slots=slots, page_of=page_of, n_valid=nv, S=S)
+    q, _, _, _ = ops.project_in(h, W_in)
+    idx, wk, w, _ = ops.route(q, S, rows_per_lib=1, top_k=4, route_temp=10.0)
+    r = ops.read_decode(q, pages, idx, wk, rows_per_lib=1)
+    delta, _, _ = ops.project_out(r, W_out, h)
+    for b in range(h.shape[0]):
+        K = slots[b * 64:(b + 1) * 64].float().cpu().numpy()
+        M = np.arange(K.shape[1])[None, :] < nv[b].cpu().numpy()[:, None]
+        S_ref = X.summaries(K, M)
+        assert rel_err(S[b], S_ref) < 1e-5
+        out = X.branch(h[b:b + 1].cpu().numpy(), W_in.t().cpu().numpy(), W_out.t().cpu().numpy(), K, M, S_ref,
+                       top_k=4)
+        assert topk_sets(w[b:b + 1]) == topk_sets(out["w"])
+        assert rel_err(r[b], out["r"][0]) < TOL
+        assert rel_err(delta[b], out["delta"][0]) < TOL
+    _status_clean(dev)
+
+
+def test_config2_properties(dev):
+    """Size-independent properties at full config-2 scale: weights sum to 1 with exactly k nonzeros, a
+    one-hot routing reproduces the single-chunk read, and reading with weights (a, 1-a) is linear."""
+    from kv_skill_v2_b200 import ops
+    slots, nv, page_of, h, W_in, _ = _cfg2_sample(dev, n_docs=64, seed=1)
+    S = ops.summaries(slots, page_of, nv)
+    pages = ops.Pages(slots=slots, page_of=page_of, n_valid=nv, S=S)
+    q, _, _, _ = ops.project_in(h, W_in)
+    idx, wk, w, _ = ops.route(q, S, rows_per_lib=1, top_k=4, route_temp=10.0)
+    assert ((w > 0).sum(-1) == 4).all() and torch.allclose(w.sum(-1), torch.ones(64, device=dev), atol=1e-5)
+    r = ops.read_decode(q, pages, idx, wk, rows_per_lib=1)
+    parts = []
+    for j in range(4):
+        one = torch.zeros_like(wk)
+        one[:, j] = 1.0
+        parts.append(ops.read_decode(q, pages, idx, one, rows_per_lib=1))
+    lin = sum(wk[:, j:j + 1] * parts[j] for j in range(4))
+    assert rel_err(r, lin) < 1e-5
+    # a chunk read is a convex combination of unit rows: norm <= 1
+    assert (parts[0].norm(dim=-1) <= 1.0 + 1e-4).all()
+    _status_clean(dev)

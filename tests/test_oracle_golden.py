@@ -1,0 +1,116 @@
+"""Pin the numpy oracle to the golden fixtures produced by the reference's own code.
+
+The fixtures under tests/golden/ were written by tests/golden/make_golden.py, which ran the reference's
+unchanged xenc.library / xenc.injector / xenc.selector. Every oracle function used as a checker for the
+CUDA path is compared here first. CPU only."""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import xenc_oracle as X
+
+G = Path(__file__).resolve().parent / "golden"
+READ_CASES = ["cfg1_softmax_top2", "cfg1_dense", "cfg1_linear_top2", "cfg1_topk_eq_C", "cfg1_linear_dense",
+              "small_ragged_top2", "small_ragged_linear", "small_ragged_dense_t3", "one_chunk", "odd_dims_top3"]
+
+
+def load_case(name: str) -> dict:
+    """Golden case with its inputs (cases that share inputs name the case that holds them)."""
+    rec = dict(np.load(G / f"{name}.npz"))
+    if "inputs" in rec:
+        base = dict(np.load(G / f"{str(rec.pop('inputs'))}.npz"))
+        for k in ("K", "n_valid", "h", "W_in", "W_out"):
+            rec[k] = base[k]
+    return rec
+
+
+def rel_err(a, b) -> float:
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def topk_sets(w: np.ndarray) -> list:
+    return [frozenset(np.flatnonzero(row > 0).tolist()) for row in w.reshape(-1, w.shape[-1])]
+
+
+@pytest.mark.parametrize("name", READ_CASES)
+def test_oracle_branch_matches_reference(name):
+    c = load_case(name)
+    K = c["K"].astype(np.float32)
+    M = np.arange(K.shape[1])[None, :] < c["n_valid"][:, None]
+    S = X.summaries(K, M)
+    assert rel_err(S, c["S"]) < 1e-6
+    assert np.array_equal(M, c["mask"])
+    h = c["h"].reshape(-1, c["h"].shape[-1])
+    out = X.branch(h, c["W_in"], c["W_out"], K, M, S, read_temp=float(c["read_temp"]),
+                   route_temp=float(c["route_temp"]), top_k=int(c["top_k"]), read_softmax=bool(c["read_softmax"]))
+    assert rel_err(out["q"], c["q"].reshape(out["q"].shape)) < 1e-5
+    w_ref = c["w"].reshape(out["w"].shape)
+    assert topk_sets(out["w"]) == topk_sets(w_ref), "routing index sets must be identical"
+    assert rel_err(out["w"], w_ref) < 1e-5
+    assert rel_err(out["r"], c["r"].reshape(out["r"].shape)) < 1e-5
+    assert rel_err(out["delta"], c["delta"].reshape(out["delta"].shape)) < 1e-5
+
+
+def test_oracle_batch_docs_matches_reference():
+    c = load_case("batch_docs_top2")
+    for b in range(c["K"].shape[0]):
+        K = c["K"][b].astype(np.float32)
+        M = np.arange(K.shape[1])[None, :] < c["n_valid"][b][:, None]
+        out = X.branch(c["h"][b], c["W_in"], c["W_out"], K, M, X.summaries(K, M), top_k=2)
+        assert topk_sets(out["w"]) == topk_sets(c["w"][b])
+        assert rel_err(out["r"], c["r"][b]) < 1e-5
+        assert rel_err(out["delta"], c["delta"][b]) < 1e-5
+
+
+def test_oracle_topk_every_row_has_k_nonzeros():
+    c = load_case("cfg1_softmax_top2")
+    nz = (c["w"] > 0).sum(-1)
+    assert (nz == 2).all()
+    assert np.allclose(c["w"].sum(-1), 1.0, atol=1e-6)
+
+
+def test_oracle_selector_matches_reference():
+    c = dict(np.load(G / "selector.npz"))
+    for st in (0, 1):
+        for k in (1, 2, 3):
+            key = f"st{st}_k{k}"
+            h0 = c[f"{key}_h"][0]
+            z = X.selector_logits(X.rms_norm(h0), c[f"{key}_u_w"], c[f"{key}_u_b"])
+            assert rel_err(z, c[f"{key}_z"]) < 1e-5
+            w = X.selector_weights(z, k, straight_through=bool(st))
+            assert np.array_equal(w > 0, c[f"{key}_w"] > 0)
+            assert rel_err(w, c[f"{key}_w"]) < 1e-5
+            for i in range(len(c["cand"])):
+                out = X.selector_apply(c[f"{key}_delta"][i], c[f"{key}_h"][i], w[..., i], float(c[f"{key}_log_alpha"]))
+                assert rel_err(out, c[f"{key}_out"][i]) < 1e-5
+
+
+def test_oracle_library_matches_reference():
+    c = dict(np.load(G / "library.npz"))
+    for li in c["layers"]:
+        rows = c[f"rows_{li}"].astype(np.float32)
+        chunk_rows = [rows[i, :n] for i, n in enumerate(c["n"])]
+        K, M, S = X.build_library(chunk_rows)
+        assert np.array_equal(K, c[f"K_{li}"]) and np.array_equal(M, c[f"mask_{li}"])
+        assert rel_err(S, c[f"S_{li}"]) < 1e-6
+        Kc, Mc, Sc = X.build_library(chunk_rows, center_mu=c[f"mu_{li}"])
+        assert rel_err(Kc, c[f"Kc_{li}"]) < 1e-6 and rel_err(Sc, c[f"Sc_{li}"]) < 1e-6
+        Ks, Ms, Ss = X.subset(K, M, [1, 3])
+        assert np.array_equal(Ks, c[f"Ksub_{li}"]) and np.array_equal(Ms, c[f"masksub_{li}"])
+        assert rel_err(Ss, c[f"Ssub_{li}"]) < 1e-6
+
+
+def test_oracle_shard_merge_equals_dense_read():
+    c = load_case("cfg1_dense")
+    K = c["K"].astype(np.float32)
+    M = np.arange(K.shape[1])[None, :] < c["n_valid"][:, None]
+    S = X.summaries(K, M)
+    q = c["q"].reshape(-1, c["q"].shape[-1])
+    parts = [X.shard_partials(q, K[a:b], M[a:b], S[a:b], 10.0, 12.0) for a, b in ((0, 3), (3, 5), (5, 8))]
+    r = X.merge_shards(parts)
+    assert rel_err(r, c["r"].reshape(r.shape)) < 1e-5
