@@ -123,11 +123,14 @@ __global__ void __launch_bounds__(TOPK_WARPS * 32) route_topk_kernel(
     wr[j] = c >= 0 ? expf(lr[c] - mx) / sum : 0.f;
   }
   if (w_dense) {
+    // w_dense may alias the logit buffer: every lane is done reading lr before it is overwritten, and the
+    // scatter takes the weights from wk
+    __syncwarp();
     for (int c = lane; c < C; c += 32) w_dense[row * C + c] = 0.f;
     __syncwarp();
     for (int j = lane; j < top_k; j += 32) {
       const int c = ir[j];
-      if (c >= 0) w_dense[row * C + c] = expf(lr[c] - mx) / sum;
+      if (c >= 0) w_dense[row * C + c] = wr[j];
     }
   }
 }
