@@ -118,6 +118,24 @@ XENCB_API int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const v
                       float read_temp, int read_softmax, float* r_out, void* workspace, size_t workspace_bytes,
                       void* stream);
 
+/* Same read as xencb_read_decode, for callers that cannot allocate device memory at all: a host runtime that
+ * owns every device byte through its own allocator and offers no way to request scratch, or a serving loop
+ * that must not allocate (an allocation may synchronise the device). There is no counterpart of this entry
+ * point in the reference; it exists for such callers of this library.
+ * The scratch lives in a fixed device array inside libxencb.so, XENCB_NOALLOC_SCRATCH_BYTES bytes, which every
+ * GPU that loads the library keeps until the process exits. A call whose scratch need
+ * (xencb_read_decode_workspace) exceeds it returns XENCB_EINVAL and launches nothing. The first call on each
+ * device looks up that array's device address (cudaGetSymbolAddress) with the device current; make that first
+ * call before any stream capture. All calls share the one array: calls on one device that overlap on the GPU
+ * (issued to different streams) race and corrupt each other's results, so serialise them. Nothing in the
+ * array needs to start at zero: every word the merge reads is written earlier in the same call. */
+#define XENCB_NOALLOC_SCRATCH_BYTES (16u << 20)
+XENCB_API int xencb_read_decode_noalloc(const float* q, int64_t n_rows, int d_s, const void* slots, int slots_dtype,
+                                        int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of,
+                                        const int32_t* n_valid, int n_chunks, int64_t rows_per_lib, int64_t n_lib,
+                                        const int32_t* idx, const float* wk, int k, float read_temp,
+                                        int read_softmax, float* r_out, void* stream);
+
 /* ---------------------------------------------------------------------------------------------------------
  * Output projection and injection epilogue. Replaces xenc/injector.py:266-267 (gain_scale * gain * gate *
  * itf_write(r), :74-77), LayerSelector.apply (xenc/selector.py:95-110) and the hook arithmetic

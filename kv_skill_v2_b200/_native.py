@@ -18,6 +18,7 @@ F32, F16, BF16 = 0, 1, 2
 OK, EINVAL, ECUDA, ENOTSUP = 0, 1, 2, 3
 DEV_TIMEOUT, DEV_CLAMPED, DEV_BADPAGE = 1, 2, 4
 PIN_RMS, PIN_L2 = 1, 2
+NOALLOC_SCRATCH_BYTES = 16 << 20
 ABI_VERSION = 1
 
 _p, _i, _i64, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
@@ -36,6 +37,8 @@ SIGNATURES: dict = {
     "xencb_read_decode_workspace": (_sz, [_i64, _i, _i, _i, _i]),
     "xencb_read_decode": (_i, [_p, _i64, _i, _p, _i, _i64, _i64, _i, _p, _p, _i, _i64, _i64, _p, _p, _i, _f, _i,
                                _p, _p, _sz, _p]),
+    "xencb_read_decode_noalloc": (_i, [_p, _i64, _i, _p, _i, _i64, _i64, _i, _p, _p, _i, _i64, _i64, _p, _p, _i,
+                                       _f, _i, _p, _p]),
     "xencb_project_out_workspace": (_sz, [_i64, _i, _i]),
     "xencb_project_out": (_i, [_p, _i64, _i, _p, _p, _i, _f, _p, _p, _f, _p, _p, _i, _p, _p, _p, _p, _sz, _p]),
     "xencb_selector_weights": (_i, [_p, _i64, _i, _i, _i, _p, _p]),

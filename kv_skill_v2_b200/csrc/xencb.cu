@@ -15,6 +15,9 @@
 #include "read_decode.cuh"
 #include "route.cuh"
 
+// Scratch of xencb_read_decode_noalloc: a fixed device array, so that entry point never allocates.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[XENCB_NOALLOC_SCRATCH_BYTES];
+
 namespace xencb {
 namespace {
 
@@ -202,6 +205,28 @@ void launch_sel_apply(const void* delta, const void* h, int h_dtype, int64_t n_r
           dp, static_cast<const __nv_bfloat16*>(h), d, w, n_cand, pos, alpha, op);
       break;
   }
+}
+
+// Device address of g_noalloc_scratch on the current device, looked up once per device. Host code cannot use
+// the array's name as a device pointer (it names a host-side shadow), so the address comes from the runtime.
+void* g_noalloc_ptr[kMaxDev];
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDev) return fail(XENCB_ENOTSUP, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    if (p == nullptr) return fail(XENCB_ECUDA, "cudaGetSymbolAddress returned a null scratch address");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return XENCB_OK;
 }
 
 }  // namespace
@@ -552,6 +577,30 @@ int xencb_summaries(const void* slots, int slots_dtype, int64_t n_pages, int64_t
   }
   XENCB_CHECK_LAUNCH("summaries launch");
   return XENCB_OK;
+}
+
+int xencb_read_decode_noalloc(const float* q, int64_t n_rows, int d_s, const void* slots, int slots_dtype,
+                              int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of,
+                              const int32_t* n_valid, int n_chunks, int64_t rows_per_lib, int64_t n_lib,
+                              const int32_t* idx, const float* wk, int k, float read_temp, int read_softmax,
+                              float* r_out, void* stream) {
+  const size_t need = (n_rows > 0 && k > 0 && d_s > 0 && page_rows > 0)
+                          ? xencb_read_decode_workspace(n_rows, k, d_s, page_rows, slots_dtype)
+                          : 0;
+  if (need > (size_t)XENCB_NOALLOC_SCRATCH_BYTES)
+    return fail(XENCB_EINVAL,
+                "read_decode_noalloc: this call needs %zu bytes of scratch, more than the library's fixed "
+                "%zu-byte device array; use xencb_read_decode with a caller workspace, or fewer rows per call",
+                need, (size_t)XENCB_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  if (need > 0) {
+    const int rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+  }
+  // need == 0 means invalid arguments: xencb_read_decode reports which one (it checks them before the workspace)
+  return xencb_read_decode(q, n_rows, d_s, slots, slots_dtype, n_pages, page_stride, page_rows, page_of, n_valid,
+                           n_chunks, rows_per_lib, n_lib, idx, wk, k, read_temp, read_softmax, r_out, scratch,
+                           need > 0 ? (size_t)XENCB_NOALLOC_SCRATCH_BYTES : 0, stream);
 }
 
 }  // extern "C"
