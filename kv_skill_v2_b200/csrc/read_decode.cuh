@@ -46,6 +46,7 @@ struct ReadArgs {
   int k;
   float qscale;  // read_temp * log2(e) for the softmax read, 1 for the linear read
   int n_split, split_rows, rps, n_stage, row_bytes, nvec;
+  int row_stride;  // shared-memory bytes between staged rows (the tensor-core kernel pads rows by 16 B)
   int64_t n_items;
   float* part_acc;  // [n_items, d_s]
   float* part_ml;   // [n_items, 2]
@@ -310,52 +311,87 @@ __global__ void __launch_bounds__(512, 1) read_decode_kernel(const ReadArgs a) {
 }
 
 // r[row] = sum_j w_j * read_j; grid (n_rows, ceil(d_s / 512)), 128 threads x 4 columns.
+// Per batch of routed chunks, one thread per chunk turns its splits' (m, l) into merge coefficients in shared
+// memory (log-sum-exp within the chunk, routing weight, 1/l or 1/sqrt(n)); then every thread issues the
+// partial loads of its 4 columns independently of each other.
+constexpr int MERGE_THREADS = 128, MERGE_ENTRIES = 256;
+
 template <bool SOFTMAX>
-__global__ void __launch_bounds__(128) read_merge_kernel(const ReadArgs a, float* __restrict__ r_out) {
+__global__ void __launch_bounds__(MERGE_THREADS) read_merge_kernel(const ReadArgs a, float* __restrict__ r_out) {
+  __shared__ float coef[MERGE_ENTRIES];
+  __shared__ long long item_of[MERGE_ENTRIES];
+  __shared__ int n_entries, nan_flag;
   const int64_t row = blockIdx.x;
   const int col = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
   const bool colok = col < a.d_s;
+  const int jb_step = max(1, MERGE_ENTRIES / a.n_split);  // chunks per batch
   float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int j = 0; j < a.k; ++j) {
-    const int64_t pair = row * a.k + j;
-    const int32_t c = a.idx[pair];
-    const float w = a.wk[pair];
-    if (c < 0 || c >= a.n_chunks || w == 0.f) continue;
-    {
-      const int64_t page = a.page_of[(row / a.rows_per_lib) * a.n_chunks + c];
+  if (threadIdx.x == 0) nan_flag = 0;
+  for (int jb = 0; jb < a.k; jb += jb_step) {
+    if (threadIdx.x == 0) n_entries = 0;
+    __syncthreads();
+    for (int jj = threadIdx.x; jj < jb_step && jb + jj < a.k; jj += blockDim.x) {
+      const int j = jb + jj;
+      const int64_t pair = row * a.k + j;
+      const int32_t c = a.idx[pair];
+      const float w = a.wk[pair];
+      if (c < 0 || c >= a.n_chunks || w == 0.f) continue;
+      const int64_t lc = (row / a.rows_per_lib) * a.n_chunks + c;
+      const int64_t page = a.page_of[lc];
       if (page < 0 || page >= a.n_pages) continue;  // skipped by the read (flagged there)
-    }
-    const int64_t item0 = pair * a.n_split;
-    float M = -CUDART_INF_F, L = 0.f;
-    if (SOFTMAX) {
-      for (int s = 0; s < a.n_split; ++s) {
+      int nv = a.n_valid[lc];
+      nv = nv > a.page_rows ? a.page_rows : (nv < 0 ? 0 : nv);
+      const int n_live = min(a.n_split, (nv + a.split_rows - 1) / a.split_rows);  // splits holding rows
+      const int64_t item0 = pair * a.n_split;
+      float M = -CUDART_INF_F, L = 0.f;
+      if (SOFTMAX) {
+        for (int s = 0; s < n_live; ++s)
+          if (a.part_ml[(item0 + s) * 2 + 1] > 0.f) M = fmaxf(M, a.part_ml[(item0 + s) * 2]);
+        for (int s = 0; s < n_live; ++s) {
+          const float ls = a.part_ml[(item0 + s) * 2 + 1];
+          if (ls > 0.f) L += ls * exp2f(a.part_ml[(item0 + s) * 2] - M);
+        }
+        if (!(L > 0.f)) {  // a routed chunk without a valid slot: the reference's softmax gives NaN
+          atomicOr(&nan_flag, 1);
+          continue;
+        }
+      } else {
+        L = sqrtf((float)(nv > 1 ? nv : 1));
+      }
+      for (int s = 0; s < n_live; ++s) {
         const float ls = a.part_ml[(item0 + s) * 2 + 1];
-        if (ls > 0.f) M = fmaxf(M, a.part_ml[(item0 + s) * 2]);
-      }
-      for (int s = 0; s < a.n_split; ++s) {
-        const float ls = a.part_ml[(item0 + s) * 2 + 1];
-        if (ls > 0.f) L += ls * exp2f(a.part_ml[(item0 + s) * 2] - M);
-      }
-    } else {
-      const int64_t lib = row / a.rows_per_lib;
-      int nv = a.n_valid[lib * a.n_chunks + c];
-      nv = nv > a.page_rows ? a.page_rows : nv;
-      L = sqrtf((float)(nv > 1 ? nv : 1));
-    }
-    for (int s = 0; s < a.n_split; ++s) {
-      const float ls = a.part_ml[(item0 + s) * 2 + 1];
-      if (!(ls > 0.f)) continue;
-      const float coef = SOFTMAX ? w * exp2f(a.part_ml[(item0 + s) * 2] - M) / L : w / L;
-      if (colok) {
-        const float4 v = *reinterpret_cast<const float4*>(a.part_acc + (item0 + s) * (int64_t)a.d_s + col);
-        r.x = fmaf(coef, v.x, r.x); r.y = fmaf(coef, v.y, r.y);
-        r.z = fmaf(coef, v.z, r.z); r.w = fmaf(coef, v.w, r.w);
+        if (!(ls > 0.f)) continue;
+        const int e = atomicAdd(&n_entries, 1);
+        coef[e] = SOFTMAX ? w * exp2f(a.part_ml[(item0 + s) * 2] - M) / L : w / L;
+        item_of[e] = item0 + s;
       }
     }
-    if (SOFTMAX && !(L > 0.f)) {  // a routed chunk with no valid slot: the reference's softmax gives NaN
-      r = make_float4(CUDART_NAN_F, CUDART_NAN_F, CUDART_NAN_F, CUDART_NAN_F);
+    __syncthreads();
+    const int ne = n_entries;
+    if (colok) {
+      int e = 0;
+      for (; e + 4 <= ne; e += 4) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          v[u] = *reinterpret_cast<const float4*>(a.part_acc + item_of[e + u] * (int64_t)a.d_s + col);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float cf = coef[e + u];
+          r.x = fmaf(cf, v[u].x, r.x); r.y = fmaf(cf, v[u].y, r.y);
+          r.z = fmaf(cf, v[u].z, r.z); r.w = fmaf(cf, v[u].w, r.w);
+        }
+      }
+      for (; e < ne; ++e) {
+        const float4 v = *reinterpret_cast<const float4*>(a.part_acc + item_of[e] * (int64_t)a.d_s + col);
+        const float cf = coef[e];
+        r.x = fmaf(cf, v.x, r.x); r.y = fmaf(cf, v.y, r.y);
+        r.z = fmaf(cf, v.z, r.z); r.w = fmaf(cf, v.w, r.w);
+      }
     }
+    __syncthreads();
   }
+  if (nan_flag) r = make_float4(CUDART_NAN_F, CUDART_NAN_F, CUDART_NAN_F, CUDART_NAN_F);
   if (colok) *reinterpret_cast<float4*>(r_out + row * (int64_t)a.d_s + col) = r;
 }
 

@@ -1,0 +1,315 @@
+// Tensor-core decode read (f16 / bf16 slots): the same work items and partial format as read_decode_kernel,
+// with the per-row arithmetic on mma.sync.m16n8k16.
+//
+// Producer (warp 0, lane 0): decodes each work item once (page, valid rows), then per stage of `rps` rows
+// writes a small descriptor (item, rows, first/last flags) into a shared ring and bulk-copies (TMA, no
+// multicast) the rows one per copy into the stage, rows padded by 16 bytes so the eight row addresses of an
+// ldmatrix fall in distinct banks. A final descriptor marks the end of the CTA's work.
+// Consumers (warps 1..ncw): warp w owns the (16*TPW)-column slice [16*TPW*w, 16*TPW*(w+1)) of d_s. Per
+// 16-row group:
+//   scores  S[16 x 8]  += K[rows, 16 cols] (ldmatrix)        x q[16 cols, query in column 0]   (TPW MMAs, 4 chains)
+//   cross-warp sum of the 16 partial scores through a double-buffered shared array guarded by an mbarrier,
+//   online softmax in fp32 (exp2 domain)
+//   accum   A[16d x 8] += K^T[16d, rows] (ldmatrix.trans)    x p[rows, column 0]              (TPW MMAs)
+// The same shared-memory tile feeds both products (K = V). q and p are rounded to the slot type (bf16 adds a
+// residual term to both, so its products carry about 16 mantissa bits); accumulation is fp32.
+// Rows past a group's valid count get p = 0; the ring is zeroed at start so those rows hold finite values.
+// Every wait is an mbarrier wait with a time limit; a warp that gives up raises the abort flag and leaves,
+// and every other wait then ends by itself, so no thread can be left waiting forever.
+#pragma once
+
+#include "read_decode.cuh"
+
+namespace xencb {
+
+constexpr int RM_TILES = 16;      // upper bound of the 16-column k-tiles per consumer warp (TPW <= RM_TILES)
+constexpr int RM_MAX_WARPS = 16;  // consumer warps per CTA
+
+struct __align__(16) StageMeta {
+  long long item;
+  int nr;     // rows in this stage
+  int flags;  // RM_FIRST | RM_LAST | RM_DONE
+};
+constexpr int RM_FIRST = 1, RM_LAST = 2, RM_DONE = 4;
+
+// Shared-memory bytes of the tensor-core read for a plan (the host and the kernel use the same layout).
+__host__ __device__ inline size_t rm_smem_bytes(int n_stage, int stage_bytes, int ncw, int tpw) {
+  return (size_t)n_stage * stage_bytes           // stages
+         + (size_t)ncw * 2 * tpw * 4 * 2 * 4       // q fragments
+         + 2 * (size_t)ncw * 16 * 4                 // cross-warp partial scores
+         + (size_t)n_stage * sizeof(StageMeta)      // stage descriptors
+         + (2 * (size_t)n_stage + 2) * 8            // full / empty / two score barriers
+         + 16;                                      // abort flag
+}
+
+template <typename T, bool SPLIT, bool SOFTMAX, int TPW>
+__global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 1) read_decode_mma_kernel(const ReadArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ncw = (blockDim.x >> 5) - 1;
+  const int row_stride = a.row_stride;
+  const int stage_bytes = ((a.rps * row_stride + 127) / 128) * 128;
+  unsigned char* stages = smem;
+  uint32_t* qfrag = reinterpret_cast<uint32_t*>(smem + (size_t)a.n_stage * stage_bytes);  // [ncw][2][TPW][4][2]
+  float* red = reinterpret_cast<float*>(qfrag + ncw * 2 * TPW * 4 * 2);                   // [2][ncw][16]
+  StageMeta* meta = reinterpret_cast<StageMeta*>(red + 2 * ncw * 16);
+  uint64_t* full = reinterpret_cast<uint64_t*>(meta + a.n_stage);
+  uint64_t* empty = full + a.n_stage;
+  uint64_t* sbar = empty + a.n_stage;  // [2] partial scores of a group are complete
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sbar + 2);
+
+  {
+    uint4* z = reinterpret_cast<uint4*>(stages);
+    const int n16 = a.n_stage * stage_bytes / 16;
+    for (int i = threadIdx.x; i < n16; i += blockDim.x) z[i] = make_uint4(0u, 0u, 0u, 0u);
+    fence_proxy_async_smem();  // the zeros precede the bulk copies into the same bytes
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < a.n_stage; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], ncw);
+    }
+    mbar_init(&sbar[0], ncw);
+    mbar_init(&sbar[1], ncw);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // ------------------------------------------------------------------------------------------- producer
+  if (warp == 0) {
+    if (lane != 0) return;
+    const uint64_t pol = policy_evict_first();
+    uint32_t it_count = 0;
+    bool ok = true;
+    // the next item's page and row range are looked up while the current item's stages stream in
+    ItemRange nxt;
+    bool have_nxt = blockIdx.x < a.n_items;
+    if (have_nxt) nxt = decode_item(a, blockIdx.x);
+    for (int64_t item = blockIdx.x; item < a.n_items && ok; item += gridDim.x) {
+      const ItemRange it = nxt;
+      const int64_t item_next = item + gridDim.x;
+      have_nxt = false;
+      if (!it.active || it.r1 <= it.r0) {
+        if (item_next < a.n_items) { nxt = decode_item(a, item_next); have_nxt = true; }
+        continue;
+      }
+      for (int rs = it.r0; rs < it.r1; rs += a.rps) {
+        const int nr = min(a.rps, it.r1 - rs);
+        const uint32_t slot = it_count % a.n_stage, use = it_count / a.n_stage;
+        if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) { ok = false; break; }
+        meta[slot].item = item;
+        meta[slot].nr = nr;
+        meta[slot].flags = (rs == it.r0 ? RM_FIRST : 0) | (rs + nr >= it.r1 ? RM_LAST : 0);
+        mbar_arrive_expect_tx(&full[slot], (uint32_t)nr * a.row_bytes);
+        unsigned char* dst = stages + (size_t)slot * stage_bytes;
+        const char* src = it.base + (int64_t)rs * a.row_bytes;
+        for (int r = 0; r < nr; ++r)
+          bulk_g2s(dst + (size_t)r * row_stride, src + (int64_t)r * a.row_bytes, (uint32_t)a.row_bytes, &full[slot], pol);
+        ++it_count;
+        if (!have_nxt && item_next < a.n_items) { nxt = decode_item(a, item_next); have_nxt = true; }
+      }
+      if (!have_nxt && item_next < a.n_items) { nxt = decode_item(a, item_next); have_nxt = true; }
+    }
+    if (ok) {  // end-of-work descriptor
+      const uint32_t slot = it_count % a.n_stage, use = it_count / a.n_stage;
+      if (use == 0 || mbar_wait_bounded(&empty[slot], (use - 1) & 1)) {
+        meta[slot].item = -1;
+        meta[slot].nr = 0;
+        meta[slot].flags = RM_DONE;
+        mbar_arrive(&full[slot]);
+        ++it_count;
+      }
+    }
+    const uint32_t n_slots = it_count < (uint32_t)a.n_stage ? it_count : (uint32_t)a.n_stage;
+    for (uint32_t i = 0; i < n_slots; ++i) {
+      const uint32_t last = it_count - 1 - i;
+      mbar_wait_bounded(&full[last % a.n_stage], (last / a.n_stage) & 1);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------------------------------- consumers
+  const int cw = warp - 1;
+  const int d0 = cw * (16 * TPW);
+  const int nt = min(TPW, (a.d_s - d0) / 16);  // >= 1 (host: d_s % 16 == 0, ncw = ceil(d_s / (16 * TPW)))
+  uint32_t* qf = qfrag + cw * 2 * TPW * 4 * 2;
+  const uint32_t stages_u32 = smem_u32(stages);
+  const int mtx = lane >> 3, r8 = lane & 7;
+  const uint32_t off_s = (uint32_t)((r8 + (mtx & 1) * 8) * row_stride + (mtx >> 1) * 16 + d0 * 2);
+  const uint32_t off_a = (uint32_t)((r8 + (mtx >> 1) * 8) * row_stride + (mtx & 1) * 16 + d0 * 2);
+  const int prow = lane & 15;  // the group row this lane finishes
+  const int ka = (lane & 3) * 2;
+
+  float acc[TPW][4];
+  float m = -CUDART_INF_F, l = 0.f;
+  uint32_t it_count = 0, grp = 0;
+
+  while (true) {
+    const uint32_t slot = it_count % a.n_stage, use = it_count / a.n_stage;
+    ++it_count;
+    if (!mbar_wait_bounded(&full[slot], use & 1) || *abort_flag) { *abort_flag = 1; break; }
+    const StageMeta md = meta[slot];
+    if (md.flags & RM_DONE) break;
+
+    if (md.flags & RM_FIRST) {
+      // q fragments (B operand, query in column 0 = lanes 0..3), hi and residual, into this warp's slot
+      if (lane < 4) {
+        const int64_t row = (md.item / a.n_split) / a.k;
+        const float* qr = a.q + row * a.d_s;
+        for (int t = 0; t < nt; ++t) {
+          const int k = d0 + t * 16 + lane * 2;
+          const float x0 = __ldg(qr + k) * a.qscale, x1 = __ldg(qr + k + 1) * a.qscale;
+          const float x2 = __ldg(qr + k + 8) * a.qscale, x3 = __ldg(qr + k + 9) * a.qscale;
+          float h0, h1, h2, h3, l0, l1, l2, l3;
+          qf[t * 8 + lane * 2] = pack2<T>(x0, x1, h0, h1);
+          qf[t * 8 + lane * 2 + 1] = pack2<T>(x2, x3, h2, h3);
+          qf[(TPW + t) * 8 + lane * 2] = SPLIT ? pack2<T>(x0 - h0, x1 - h1, l0, l1) : 0u;
+          qf[(TPW + t) * 8 + lane * 2 + 1] = SPLIT ? pack2<T>(x2 - h2, x3 - h3, l2, l3) : 0u;
+        }
+      }
+      __syncwarp();
+#pragma unroll
+      for (int t = 0; t < TPW; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+      m = -CUDART_INF_F;
+      l = 0.f;
+    }
+    const uint32_t sbase = stages_u32 + slot * (uint32_t)stage_bytes;
+    bool aborted = false;
+
+    for (int g0 = 0; g0 < md.nr; g0 += 16) {
+      const int gv = min(16, md.nr - g0);
+      const uint32_t gbase = sbase + (uint32_t)(g0 * row_stride);
+      // ---- scores: four accumulator chains
+      float sa[4][4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) sa[c][0] = sa[c][1] = sa[c][2] = sa[c][3] = 0.f;
+#pragma unroll
+      for (int t = 0; t < TPW; ++t) {
+        if (t < nt) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(gbase + off_s + t * 32, a0, a1, a2, a3);
+          uint32_t b0 = 0u, b1 = 0u;
+          if (lane < 4) {
+            b0 = qf[t * 8 + lane * 2];
+            b1 = qf[t * 8 + lane * 2 + 1];
+          }
+          mma16816<T>(sa[t & 3], a0, a1, a2, a3, b0, b1);
+          if (SPLIT) {
+            uint32_t c0 = 0u, c1 = 0u;
+            if (lane < 4) {
+              c0 = qf[(TPW + t) * 8 + lane * 2];
+              c1 = qf[(TPW + t) * 8 + lane * 2 + 1];
+            }
+            mma16816<T>(sa[(t + 2) & 3], a0, a1, a2, a3, c0, c1);
+          }
+        }
+      }
+      const float sc_lo = (sa[0][0] + sa[1][0]) + (sa[2][0] + sa[3][0]);  // row lane/4 (lanes with lane%4 == 0)
+      const float sc_hi = (sa[0][2] + sa[1][2]) + (sa[2][2] + sa[3][2]);  // row lane/4 + 8
+      float srow;
+      if (ncw > 1) {
+        const int b = grp & 1;
+        float* rb = red + b * ncw * 16;
+        if ((lane & 3) == 0) {
+          rb[cw * 16 + (lane >> 2)] = sc_lo;
+          rb[cw * 16 + (lane >> 2) + 8] = sc_hi;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sbar[b]);
+        if (!mbar_wait_bounded(&sbar[b], (grp >> 1) & 1) || *abort_flag) {
+          *abort_flag = 1;
+          aborted = true;
+          break;
+        }
+        srow = 0.f;
+        for (int w = 0; w < ncw; ++w) srow += rb[w * 16 + prow];
+      } else {
+        const float v_lo = __shfl_sync(0xffffffffu, sc_lo, (prow & 7) * 4);
+        const float v_hi = __shfl_sync(0xffffffffu, sc_hi, (prow & 7) * 4);
+        srow = prow < 8 ? v_lo : v_hi;
+      }
+      ++grp;
+      const bool valid = prow < gv;
+      float p;
+      if (SOFTMAX) {
+        float mx = valid ? srow : -CUDART_INF_F;
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        const float m_new = fmaxf(m, mx);
+        if (m_new != m) {
+          const float sc = exp2f(m - m_new);
+          l *= sc;
+#pragma unroll
+          for (int t = 0; t < TPW; ++t) {
+            acc[t][0] *= sc;
+            acc[t][2] *= sc;
+          }
+          m = m_new;
+        }
+        p = valid ? exp2f(srow - m) : 0.f;
+      } else {
+        p = valid ? srow : 0.f;
+      }
+      // round p to the slot type (+ residual for bf16); l sums the values the MMA uses
+      const T ph = from_f32<T>(p);
+      const float phf = to_f32(ph);
+      const T pl = from_f32<T>(SPLIT ? p - phf : 0.f);
+      if (SOFTMAX) {
+        float ps = phf + (SPLIT ? to_f32(pl) : 0.f);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+        l += ps;
+      }
+      uint16_t uh, ul;
+      memcpy(&uh, &ph, 2);
+      memcpy(&ul, &pl, 2);
+      const uint32_t ubits = (uint32_t)uh | ((uint32_t)ul << 16);
+      const uint32_t e0 = __shfl_sync(0xffffffffu, ubits, ka);
+      const uint32_t e1 = __shfl_sync(0xffffffffu, ubits, ka + 1);
+      const uint32_t e8 = __shfl_sync(0xffffffffu, ubits, ka + 8);
+      const uint32_t e9 = __shfl_sync(0xffffffffu, ubits, ka + 9);
+      const uint32_t pb0 = lane < 4 ? ((e0 & 0xffffu) | (e1 << 16)) : 0u;
+      const uint32_t pb1 = lane < 4 ? ((e8 & 0xffffu) | (e9 << 16)) : 0u;
+      const uint32_t pc0 = lane < 4 ? ((e0 >> 16) | (e1 & 0xffff0000u)) : 0u;
+      const uint32_t pc1 = lane < 4 ? ((e8 >> 16) | (e9 & 0xffff0000u)) : 0u;
+      // ---- accumulate: acc[d, 0] += sum_rows K[row, d] p[row]
+#pragma unroll
+      for (int t = 0; t < TPW; ++t) {
+        if (t < nt) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4_t(gbase + off_a + t * 32, a0, a1, a2, a3);
+          mma16816<T>(acc[t], a0, a1, a2, a3, pb0, pb1);
+          if (SPLIT) mma16816<T>(acc[t], a0, a1, a2, a3, pc0, pc1);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+    if (aborted) break;
+
+    if (md.flags & RM_LAST) {
+      float* pa = a.part_acc + md.item * (int64_t)a.d_s;
+      if ((lane & 3) == 0) {
+#pragma unroll
+        for (int t = 0; t < TPW; ++t) {
+          if (t < nt) {
+            const int d = d0 + t * 16 + (lane >> 2);
+            pa[d] = acc[t][0];
+            pa[d + 8] = acc[t][2];
+          }
+        }
+      }
+      if (cw == 0 && lane == 0) {
+        a.part_ml[md.item * 2] = SOFTMAX ? m : 0.f;
+        a.part_ml[md.item * 2 + 1] = SOFTMAX ? l : 1.f;
+      }
+    }
+  }
+}
+
+}  // namespace xencb

@@ -5,7 +5,9 @@
 // caller's stream. No entry point allocates device memory or synchronises, except xencb_device_status.
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
+#include <unordered_map>
 #include <mutex>
 #include <string>
 #include <type_traits>
@@ -13,6 +15,7 @@
 #include "common.cuh"
 #include "project.cuh"
 #include "read_decode.cuh"
+#include "read_decode_mma.cuh"
 #include "route.cuh"
 
 // Scratch of xencb_read_decode_noalloc: a fixed device array, so that entry point never allocates.
@@ -88,15 +91,21 @@ bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // Opt a kernel into `smem` bytes of dynamic shared memory once per (device, kernel).
+std::unordered_map<const void*, int> g_smem_set[kMaxDev];
+std::mutex g_smem_mu;
+
 template <typename K>
-int ensure_smem(K kernel, int smem, int* done_flags) {
+int ensure_smem(K kernel, int smem) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= kMaxDev) return fail(XENCB_ENOTSUP, "device ordinal %d out of range", dev);
-  if (done_flags[dev] >= smem) return XENCB_OK;
+  const void* key = reinterpret_cast<const void*>(kernel);
+  std::lock_guard<std::mutex> lk(g_smem_mu);
+  auto itr = g_smem_set[dev].find(key);
+  if (itr != g_smem_set[dev].end() && itr->second >= smem) return XENCB_OK;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
-  done_flags[dev] = smem;
+  g_smem_set[dev][key] = smem;
   return XENCB_OK;
 }
 
@@ -124,7 +133,9 @@ void launch_gemm(const void* X, int64_t M, int K, const float* W, int N, const G
 
 // ------------------------------------------------------------------------------------------------ read plan
 struct ReadPlan {
-  int vpt, ncw, rps, n_stage, n_split, split_rows, row_bytes, nvec, threads, grid;
+  bool mma;  // tensor-core kernel (f16 / bf16 slots, d_s % 16 == 0, d_s <= 2560)
+  int tpw;   // its 16-column tiles per consumer warp (8 or 16)
+  int vpt, ncw, rps, n_stage, n_split, split_rows, row_bytes, row_stride, nvec, threads, grid;
   size_t smem, acc_bytes, ml_bytes;
   int64_t n_items;
 };
@@ -139,25 +150,54 @@ int plan_read(int64_t n_rows, int k, int d_s, int page_rows, int dtype, ReadPlan
     return fail(XENCB_EINVAL, "d_s=%d: a slot row must be a multiple of 16 bytes (d_s %% %d == 0)", d_s, 16 / es);
   p->row_bytes = d_s * es;
   p->nvec = p->row_bytes / 16;
-  // at most 15 consumer warps (512 threads per CTA with the producer warp)
-  if (p->nvec <= 15 * 32) p->vpt = 1;
-  else if (p->nvec <= 15 * 64) p->vpt = 2;
-  else return fail(XENCB_ENOTSUP, "d_s=%d: slot rows above 15 KiB are not supported", d_s);
-  p->ncw = (p->nvec + 32 * p->vpt - 1) / (32 * p->vpt);
-  p->threads = 32 * (p->ncw + 1);
-  // rows per stage: a power of two <= 64 with a stage of about 32 KiB
-  int rps = 64;
-  while (rps > 1 && rps * p->row_bytes > 32768) rps >>= 1;
-  p->rps = rps;
-  const size_t stage_bytes = align_up((size_t)rps * p->row_bytes, 128);
-  const size_t tail = align_up(2 * (size_t)p->ncw * RD_G * sizeof(float), 8) + 2 * 8 * 8 + 16;
   const size_t budget = (size_t)(di.max_smem_optin > 0 ? di.max_smem_optin : 232448) - 1024;
-  int n_stage = (int)((budget - tail) / stage_bytes);
-  if (n_stage > 8) n_stage = 8;
-  if (n_stage < 2) return fail(XENCB_ENOTSUP, "d_s=%d: two pipeline stages do not fit in shared memory", d_s);
-  p->n_stage = n_stage;
-  p->smem = (size_t)n_stage * stage_bytes + align_up(2 * (size_t)p->ncw * RD_G * sizeof(float), 8) +
-            2 * (size_t)n_stage * 8 + 16;
+  p->mma = false;
+  const char* force_simt = getenv("XENCB_READ_SIMT");
+  // tensor-core read: 128-column slices (up to 16 warps) for d_s <= 2048, 256-column slices (up to 10) above
+  const int tpw = d_s <= 2048 ? 8 : 16;
+  const int mma_ncw = (d_s + 16 * tpw - 1) / (16 * tpw);
+  const int max_ncw = tpw == 8 ? RM_MAX_WARPS : 10;
+  if ((dtype == XENCB_F16 || dtype == XENCB_BF16) && d_s % 16 == 0 && mma_ncw <= max_ncw &&
+      !(force_simt && force_simt[0] == '1')) {
+    const int stride = p->row_bytes + 16;
+    int rps = 64;
+    while (rps > 16 && rps * stride > 69632) rps >>= 1;
+    const int stage_bytes = (int)align_up((size_t)rps * stride, 128);
+    int n_stage = 8;
+    while (n_stage >= 2 && rm_smem_bytes(n_stage, stage_bytes, mma_ncw, tpw) > budget) --n_stage;
+    if (n_stage >= 2) {
+      p->mma = true;
+      p->tpw = tpw;
+      p->vpt = 0;
+      p->ncw = mma_ncw;
+      p->threads = 32 * (mma_ncw + 1);
+      p->rps = rps;
+      p->row_stride = stride;
+      p->n_stage = n_stage;
+      p->smem = rm_smem_bytes(n_stage, stage_bytes, mma_ncw, tpw);
+    }
+  }
+  if (!p->mma) {
+    // at most 15 consumer warps (512 threads per CTA with the producer warp)
+    if (p->nvec <= 15 * 32) p->vpt = 1;
+    else if (p->nvec <= 15 * 64) p->vpt = 2;
+    else return fail(XENCB_ENOTSUP, "d_s=%d: slot rows above 15 KiB are not supported", d_s);
+    p->ncw = (p->nvec + 32 * p->vpt - 1) / (32 * p->vpt);
+    p->threads = 32 * (p->ncw + 1);
+    // rows per stage: a power of two <= 64 with a stage of about 32 KiB
+    int rps = 64;
+    while (rps > 1 && rps * p->row_bytes > 32768) rps >>= 1;
+    p->rps = rps;
+    p->row_stride = p->row_bytes;
+    const size_t stage_bytes = align_up((size_t)rps * p->row_bytes, 128);
+    const size_t tail = align_up(2 * (size_t)p->ncw * RD_G * sizeof(float), 8) + 2 * 8 * 8 + 16;
+    int n_stage = (int)((budget - tail) / stage_bytes);
+    if (n_stage > 8) n_stage = 8;
+    if (n_stage < 2) return fail(XENCB_ENOTSUP, "d_s=%d: two pipeline stages do not fit in shared memory", d_s);
+    p->n_stage = n_stage;
+    p->smem = (size_t)n_stage * stage_bytes + align_up(2 * (size_t)p->ncw * RD_G * sizeof(float), 8) +
+              2 * (size_t)n_stage * 8 + 16;
+  }
   // row splits: pick the count with the smallest modelled makespan on one CTA per SM
   const int64_t pairs = n_rows * k;
   const int grid_max = di.sms;
@@ -183,8 +223,6 @@ int plan_read(int64_t n_rows, int k, int d_s, int page_rows, int dtype, ReadPlan
   p->ml_bytes = align_up((size_t)p->n_items * 2 * sizeof(float), 256);
   return XENCB_OK;
 }
-
-int g_read_smem_done[3][2][2][kMaxDev];
 
 template <typename TD>
 void launch_sel_apply(const void* delta, const void* h, int h_dtype, int64_t n_rows, int d, const float* w,
@@ -347,9 +385,8 @@ int xencb_route(const float* q, int64_t n_rows, int d_s, const float* S, int n_c
   route_logits_kernel<<<(unsigned)blocks, 256, 0, st>>>(q, n_rows, d_s, S, n_chunks, n_chunks_of, rows_per_lib,
                                                         route_temp, lg);
   XENCB_CHECK_LAUNCH("route_logits launch");
-  static int done[kMaxDev];
   const int smem = n_chunks * 4 * TOPK_WARPS;
-  int rc = ensure_smem(route_topk_kernel, smem > 48 * 1024 ? smem : 48 * 1024, done);
+  int rc = ensure_smem(route_topk_kernel, smem > 48 * 1024 ? smem : 48 * 1024);
   if (rc) return rc;
   const int k_out = xencb_route_k(top_k, n_chunks);
   route_topk_kernel<<<(unsigned)((n_rows + TOPK_WARPS - 1) / TOPK_WARPS), TOPK_WARPS * 32, smem, st>>>(
@@ -402,12 +439,10 @@ int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots
   a.idx = idx; a.wk = wk; a.k = k;
   a.qscale = read_softmax ? read_temp * 1.4426950408889634f : 1.f;
   a.n_split = p.n_split; a.split_rows = p.split_rows; a.rps = p.rps; a.n_stage = p.n_stage;
-  a.row_bytes = p.row_bytes; a.nvec = p.nvec; a.n_items = p.n_items;
+  a.row_bytes = p.row_bytes; a.nvec = p.nvec; a.n_items = p.n_items; a.row_stride = p.row_stride;
   a.part_acc = static_cast<float*>(workspace);
   a.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + p.acc_bytes);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int di = slots_dtype, vi = p.vpt == 1 ? 0 : 1, si = read_softmax ? 1 : 0;
-  int* done = g_read_smem_done[di][vi][si];
   rc = XENCB_OK;
   {
     auto run = [&](auto tag_t, auto tag_v, auto tag_s) -> int {
@@ -415,12 +450,12 @@ int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots
       constexpr int V = decltype(tag_v)::value;
       constexpr bool S = decltype(tag_s)::value;
       auto k1 = read_decode_kernel<T, V, S>;
-      int r2 = ensure_smem(k1, (int)p.smem, done);
+      int r2 = ensure_smem(k1, (int)p.smem);
       if (r2) return r2;
       k1<<<p.grid, p.threads, p.smem, st>>>(a);
       XENCB_CHECK_LAUNCH("read_decode_kernel launch");
       dim3 mg((unsigned)n_rows, (d_s + 511) / 512);
-      read_merge_kernel<S><<<mg, 128, 0, st>>>(a, r_out);
+      read_merge_kernel<S><<<mg, MERGE_THREADS, 0, st>>>(a, r_out);
       XENCB_CHECK_LAUNCH("read_merge_kernel launch");
       return XENCB_OK;
     };
@@ -431,7 +466,30 @@ int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots
     using V2 = std::integral_constant<int, 2>;
     using ST = std::true_type;
     using SF = std::false_type;
-    if (slots_dtype == XENCB_F16) {
+    auto run_mma = [&](auto tag_t, auto tag_s, auto tag_w) -> int {
+      using T = typename decltype(tag_t)::type;
+      constexpr bool S = decltype(tag_s)::value;
+      constexpr int W = decltype(tag_w)::value;
+      constexpr bool SPLIT = std::is_same<T, __nv_bfloat16>::value;
+      auto k1 = read_decode_mma_kernel<T, SPLIT, S, W>;
+      int r2 = ensure_smem(k1, (int)p.smem);
+      if (r2) return r2;
+      k1<<<p.grid, p.threads, p.smem, st>>>(a);
+      XENCB_CHECK_LAUNCH("read_decode_mma_kernel launch");
+      dim3 mg((unsigned)n_rows, (d_s + 511) / 512);
+      read_merge_kernel<S><<<mg, MERGE_THREADS, 0, st>>>(a, r_out);
+      XENCB_CHECK_LAUNCH("read_merge_kernel launch");
+      return XENCB_OK;
+    };
+    using W8 = std::integral_constant<int, 8>;
+    using W16 = std::integral_constant<int, 16>;
+    if (p.mma && p.tpw == 8) {
+      if (slots_dtype == XENCB_F16) rc = read_softmax ? run_mma(F16T{}, ST{}, W8{}) : run_mma(F16T{}, SF{}, W8{});
+      else rc = read_softmax ? run_mma(BF16T{}, ST{}, W8{}) : run_mma(BF16T{}, SF{}, W8{});
+    } else if (p.mma) {
+      if (slots_dtype == XENCB_F16) rc = read_softmax ? run_mma(F16T{}, ST{}, W16{}) : run_mma(F16T{}, SF{}, W16{});
+      else rc = read_softmax ? run_mma(BF16T{}, ST{}, W16{}) : run_mma(BF16T{}, SF{}, W16{});
+    } else if (slots_dtype == XENCB_F16) {
       if (p.vpt == 1) rc = read_softmax ? run(F16T{}, V1{}, ST{}) : run(F16T{}, V1{}, SF{});
       else rc = read_softmax ? run(F16T{}, V2{}, ST{}) : run(F16T{}, V2{}, SF{});
     } else if (slots_dtype == XENCB_BF16) {
@@ -476,8 +534,7 @@ int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_ou
   const int smem = d_m * 4;
 #define XENCB_POUT(T)                                                                                          \
   do {                                                                                                         \
-    static int done[kMaxDev];                                                                                  \
-    int rc2 = ensure_smem(project_out_finish_kernel<T>, smem > 48 * 1024 ? smem : 48 * 1024, done);          \
+    int rc2 = ensure_smem(project_out_finish_kernel<T>, smem > 48 * 1024 ? smem : 48 * 1024);                \
     if (rc2) return rc2;                                                                                       \
     project_out_finish_kernel<T><<<(unsigned)n_rows, 256, smem, st>>>(                                        \
         part, gp.splits, n_rows, d_m, b_out, scale, gate, sel_w, alpha, pos_mask, static_cast<const T*>(h),   \

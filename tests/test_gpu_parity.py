@@ -70,6 +70,36 @@ def test_read_path_matches_reference(dev, name, slot_dtype):
     _status_clean(dev)
 
 
+@pytest.mark.parametrize("kernel", ["auto", "simt"])
+@pytest.mark.parametrize("slot_dtype", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("softmax", [True, False])
+def test_read_ragged_rows_both_kernels(dev, monkeypatch, kernel, slot_dtype, softmax):
+    """Valid-row counts around the 16-row group and 64-row stage edges, every slot type, both read kernels
+    (tensor-core for f16/bf16 when d_s % 16 == 0, SIMT otherwise or when forced), against the oracle."""
+    from kv_skill_v2_b200 import ops
+    if kernel == "simt":
+        monkeypatch.setenv("XENCB_READ_SIMT", "1")
+    g = torch.Generator().manual_seed(21)
+    ns = [1, 15, 16, 17, 63, 64, 65, 200, 511]
+    C, N, d_s, R = len(ns), 512, 512, 12
+    K = torch.randn(C, N, d_s, generator=g)
+    K = (K / K.norm(dim=-1, keepdim=True)).to(slot_dtype)
+    for c, n in enumerate(ns):
+        K[c, n:] = 0
+    Kf = K.float().numpy()
+    M = np.arange(N)[None, :] < np.array(ns)[:, None]
+    q = torch.nn.functional.normalize(torch.randn(R, d_s, generator=g), dim=-1)
+    S = torch.from_numpy(X.summaries(Kf, M)).to(dev).view(1, C, d_s)
+    pages = ops.Pages(slots=K.to(dev).contiguous(), page_of=torch.arange(C, dtype=torch.int32, device=dev).view(1, C),
+                      n_valid=torch.tensor(ns, dtype=torch.int32, device=dev).view(1, C), S=S)
+    for top_k in (0, 3):
+        idx, wk, w, _ = ops.route(q.to(dev), pages.S, rows_per_lib=R, top_k=top_k, route_temp=10.0)
+        r = ops.read_decode(q.to(dev), pages, idx, wk, rows_per_lib=R, read_temp=12.0, read_softmax=softmax)
+        ref = X.read(q.numpy(), Kf, M, w.cpu().numpy(), 12.0, softmax)
+        assert rel_err(r, ref) < TOL, (kernel, slot_dtype, softmax, top_k)
+    _status_clean(dev)
+
+
 def test_route_ties_go_to_lower_index(dev):
     from kv_skill_v2_b200 import ops
     S = torch.zeros(1, 6, 8, device=dev)
