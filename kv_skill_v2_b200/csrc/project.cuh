@@ -14,91 +14,119 @@
 
 namespace xencb {
 
-constexpr int GEMM_BM = 64, GEMM_BN = 128, GEMM_BK = 16, GEMM_THREADS = 128;
-constexpr int GEMM_APAD = GEMM_BM + 4, GEMM_BPAD = GEMM_BN + 4;
+constexpr int GEMM_BM = 64, GEMM_BN = 128, GEMM_BK = 32, GEMM_THREADS = 128, GEMM_BSTAGES = 3;
+constexpr int GEMM_APAD = GEMM_BM + 4;
+constexpr size_t GEMM_SMEM = (size_t)(2 * GEMM_BK * GEMM_APAD + GEMM_BSTAGES * GEMM_BK * GEMM_BN) * sizeof(float);
 
-// part[z][m][n] = sum_{k in [z*kps, min(K,(z+1)*kps))} X[m][k] * W[n][k]
-// grid: (ceil(N/BN), ceil(M/BM), splits); block 128 threads, each an 8x8 register tile.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src, bool valid) {
+  const uint32_t d = smem_u32(smem_dst);
+  const int n = valid ? 16 : 0;  // 0 source bytes: the 16 destination bytes are zero-filled
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(gmem_src), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// part[z][m][n] = sum_{k in [z*kps, min(K,(z+1)*kps))} X[m][k] * Wt[k][n]   (Wt input-major: [K, N])
+// grid: (ceil(N/128), ceil(M/64), splits); 128 threads, each an 8x8 register tile (rows 8*ty.., columns
+// 4*tx.. and 64+4*tx..), packed f32x2 FMAs. The weight tile streams through a 3-stage cp.async ring (16-byte
+// chunks, N % 4 == 0); the activation tile (any float type) is loaded through registers, converted and stored
+// transposed (As[k][m]) one slice ahead.
 template <typename TX>
-__global__ void __launch_bounds__(GEMM_THREADS) gemm_tn_splitk_kernel(const TX* __restrict__ X, int64_t M, int K,
-                                                                       const float* __restrict__ W, int N, int kps,
-                                                                       float* __restrict__ part) {
-  __shared__ __align__(16) float As[2][GEMM_BK][GEMM_APAD];
-  __shared__ __align__(16) float Bs[2][GEMM_BK][GEMM_BPAD];
+__global__ void __launch_bounds__(GEMM_THREADS) gemm_xw_splitk_kernel(const TX* __restrict__ X, int64_t M, int K,
+                                                                       const float* __restrict__ Wt, int N, int kps,
+                                                                       float* __restrict__ part,
+                                                                       int* __restrict__ row_done) {
+  // zero the per-row completion counters the following reduce kernel counts on (stream order)
+  if (row_done && blockIdx.x == 0 && blockIdx.z == 0)
+    for (int64_t i = (int64_t)blockIdx.y * GEMM_BM + threadIdx.x; i < min(M, (int64_t)(blockIdx.y + 1) * GEMM_BM);
+         i += blockDim.x)
+      row_done[i] = 0;
+  extern __shared__ __align__(16) float gsm[];
+  float (*As)[GEMM_BK][GEMM_APAD] = reinterpret_cast<float (*)[GEMM_BK][GEMM_APAD]>(gsm);
+  float (*Bs)[GEMM_BK][GEMM_BN] = reinterpret_cast<float (*)[GEMM_BK][GEMM_BN]>(gsm + 2 * GEMM_BK * GEMM_APAD);
 
   const int tid = threadIdx.x;
-  const int ty = tid >> 4, tx = tid & 15;  // 8 x 16 thread grid
+  const int ty = tid >> 4, tx = tid & 15;
   const int64_t m0 = (int64_t)blockIdx.y * GEMM_BM;
   const int n0 = blockIdx.x * GEMM_BN;
   const int kbeg = blockIdx.z * kps;
   const int kend = min(K, kbeg + kps);
+  const int nslices = kend > kbeg ? (kend - kbeg + GEMM_BK - 1) / GEMM_BK : 0;
 
-  float acc[8][8];
+  float2 acc[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.f, 0.f);
 
-  // staging registers: A tile 64x16 = 1024 elems -> 8 per thread; B tile 128x16 = 2048 -> 16 per thread
-  float ra[8], rb[16];
-  auto load_tile = [&](int k0) {
+  auto load_b = [&](int s) {
+    const int k0 = kbeg + s * GEMM_BK;
+    float* dst = &Bs[s % GEMM_BSTAGES][0][0];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const int f = tid + i * GEMM_THREADS;  // 0..1023
-      const int mm = f >> 4, kk = f & 15;
+      const int c = tid + i * GEMM_THREADS;  // 0..1023 16-byte chunks
+      const int kk = c >> 5, nn = (c & 31) * 4;
+      const int gk = k0 + kk, gn = n0 + nn;
+      const bool ok = gk < kend && gn < N;  // N % 4 == 0: a chunk is all in or all out
+      cp_async16(dst + kk * GEMM_BN + nn, ok ? (const void*)(Wt + (int64_t)gk * N + gn) : (const void*)Wt, ok);
+    }
+  };
+  float ra[16];
+  auto load_a = [&](int s) {
+    const int k0 = kbeg + s * GEMM_BK;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int e = tid + i * GEMM_THREADS;  // 0..2047
+      const int mm = e >> 5, kk = e & 31;
       const int64_t gm = m0 + mm;
       const int gk = k0 + kk;
       ra[i] = (gm < M && gk < kend) ? to_f32(X[gm * K + gk]) : 0.f;
     }
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int f = tid + i * GEMM_THREADS;  // 0..2047
-      const int nn = f >> 4, kk = f & 15;
-      const int gn = n0 + nn;
-      const int gk = k0 + kk;
-      rb[i] = (gn < N && gk < kend) ? __ldg(W + (int64_t)gn * K + gk) : 0.f;
-    }
   };
-  auto store_tile = [&](int buf) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int f = tid + i * GEMM_THREADS;
-      As[buf][f & 15][f >> 4] = ra[i];
-    }
+  auto store_a = [&](int buf) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const int f = tid + i * GEMM_THREADS;
-      Bs[buf][f & 15][f >> 4] = rb[i];
+      const int e = tid + i * GEMM_THREADS;
+      As[buf][e & 31][e >> 5] = ra[i];
     }
   };
 
-  if (kbeg < kend) {
-    load_tile(kbeg);
-    store_tile(0);
-    __syncthreads();
-    int buf = 0;
-    for (int k0 = kbeg; k0 < kend; k0 += GEMM_BK) {
-      const bool more = k0 + GEMM_BK < kend;
-      if (more) load_tile(k0 + GEMM_BK);
-#pragma unroll
+  if (nslices > 0) {
+    load_b(0);
+    cp_async_commit();
+    if (nslices > 1) load_b(1);
+    cp_async_commit();
+    load_a(0);
+    store_a(0);
+    for (int s = 0; s < nslices; ++s) {
+      cp_async_wait<1>();
+      __syncthreads();
+      if (s + 2 < nslices) load_b(s + 2);
+      cp_async_commit();
+      const bool more = s + 1 < nslices;
+      if (more) load_a(s + 1);
+      const float* as = &As[s & 1][0][0];
+      const float* bs = &Bs[s % GEMM_BSTAGES][0][0];
+#pragma unroll 8
       for (int kk = 0; kk < GEMM_BK; ++kk) {
-        const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 8]);
-        const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 8 + 4]);
-        const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
-        const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][64 + tx * 4]);
+        const float4 a0 = *reinterpret_cast<const float4*>(as + kk * GEMM_APAD + ty * 8);
+        const float4 a1 = *reinterpret_cast<const float4*>(as + kk * GEMM_APAD + ty * 8 + 4);
+        const float4 b0 = *reinterpret_cast<const float4*>(bs + kk * GEMM_BN + tx * 4);
+        const float4 b1 = *reinterpret_cast<const float4*>(bs + kk * GEMM_BN + 64 + tx * 4);
         const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        const float2 b[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
+                             make_float2(b1.z, b1.w)};
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < 8; ++i) {
+          const float2 ai = make_float2(a[i], a[i]);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+          for (int j = 0; j < 4; ++j) acc[i][j] = __ffma2_rn(ai, b[j], acc[i][j]);
+        }
       }
-      if (more) {
-        store_tile(buf ^ 1);
-        __syncthreads();
-        buf ^= 1;
-      }
+      if (more) store_a((s + 1) & 1);
     }
+    cp_async_wait<0>();
   }
 
   float* out = part + (int64_t)blockIdx.z * M * N;
@@ -106,22 +134,21 @@ __global__ void __launch_bounds__(GEMM_THREADS) gemm_tn_splitk_kernel(const TX* 
   for (int i = 0; i < 8; ++i) {
     const int64_t gm = m0 + ty * 8 + i;
     if (gm >= M) continue;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int gn = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
-      if (gn < N) out[gm * N + gn] = acc[i][j];
-    }
+    const int c0 = n0 + tx * 4, c1 = n0 + 64 + tx * 4;
+    if (c0 < N)
+      *reinterpret_cast<float4*>(out + gm * N + c0) = make_float4(acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y);
+    if (c1 < N)
+      *reinterpret_cast<float4*>(out + gm * N + c1) = make_float4(acc[i][2].x, acc[i][2].y, acc[i][3].x, acc[i][3].y);
   }
 }
 
-// Split count so that the GEMM grid covers the SMs about twice; each split is a multiple of BK.
+// Split count: at least ~256 columns of K per split, enough CTAs to fill the SMs about twice.
 inline int gemm_splits(int64_t M, int N, int K, int sms) {
   const int64_t tiles = ((N + GEMM_BN - 1) / GEMM_BN) * ((M + GEMM_BM - 1) / GEMM_BM);
-  const int kblocks = (K + GEMM_BK - 1) / GEMM_BK;
+  const int max_s = (K + 255) / 256;
   int64_t s = (2 * (int64_t)sms + tiles - 1) / tiles;
   if (s < 1) s = 1;
-  if (s > kblocks) s = kblocks;
-  if (s > 32) s = 32;
+  if (s > max_s) s = max_s;
   return (int)s;
 }
 
@@ -130,66 +157,139 @@ inline int gemm_kps(int K, int splits) {
   return ((kblocks + splits - 1) / splits) * GEMM_BK;
 }
 
-// ------------------------------------------------------------------------------------------------ project_in
-// One CTA per row: 1/rms of h, reduce the GEMM splits, bias, L2, gate, selector logits.
+// Sum of the split partials of 4 consecutive columns (col % 4 == 0, N % 4 == 0), loads kept independent.
+__device__ __forceinline__ float4 sum_splits4(const float* __restrict__ part, int splits, int64_t M, int N,
+                                              int64_t row, int col) {
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float* p = part + row * N + col;
+  const int64_t zs = M * N;
+  int z = 0;
+  for (; z + 4 <= splits; z += 4) {
+    float4 t[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) t[u] = *reinterpret_cast<const float4*>(p + (int64_t)(z + u) * zs);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) { v.x += t[u].x; v.y += t[u].y; v.z += t[u].z; v.w += t[u].w; }
+  }
+  for (; z < splits; ++z) {
+    const float4 t = *reinterpret_cast<const float4*>(p + (int64_t)z * zs);
+    v.x += t.x; v.y += t.y; v.z += t.z; v.w += t.w;
+  }
+  return v;
+}
+
+// Row passes with 16-byte loads, four in flight per thread: sum of x^2, and sum of x*w for up to two vectors.
 template <typename TH>
-__global__ void __launch_bounds__(256) project_in_finish_kernel(
+__device__ __forceinline__ void row_dots(const TH* __restrict__ hr, int d, const float* __restrict__ w1,
+                                         const float* __restrict__ w2, float& ss, float& s1, float& s2) {
+  constexpr int EPV = 16 / sizeof(TH);
+  ss = s1 = s2 = 0.f;
+  const bool vec = (d % EPV == 0) && ((reinterpret_cast<uintptr_t>(hr) & 15) == 0) &&
+                   (!w1 || (reinterpret_cast<uintptr_t>(w1) & 15) == 0) &&
+                   (!w2 || (reinterpret_cast<uintptr_t>(w2) & 15) == 0);
+  if (vec) {
+    const uint4* h4 = reinterpret_cast<const uint4*>(hr);
+    const int nv = d / EPV;
+#pragma unroll 4
+    for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+      float x[EPV];
+      unpack16<TH>(__ldg(h4 + v), x);
+#pragma unroll
+      for (int e = 0; e < EPV; ++e) {
+        ss = fmaf(x[e], x[e], ss);
+        if (w1) s1 = fmaf(x[e], __ldg(w1 + v * EPV + e), s1);
+        if (w2) s2 = fmaf(x[e], __ldg(w2 + v * EPV + e), s2);
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+      const float x = to_f32(hr[i]);
+      ss = fmaf(x, x, ss);
+      if (w1) s1 = fmaf(x, w1[i], s1);
+      if (w2) s2 = fmaf(x, w2[i], s2);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ project_in
+// Two launches after the GEMM. project_in_reduce: one CTA per (row, 1024-column chunk) sums the split
+// partials (independent 16-byte loads), applies 1/rms and the bias, writes the unnormalised row and the
+// chunk's sum of squares; the chunk-0 CTA also writes 1/rms, the gate and the selector logits.
+// project_in_normalize: one CTA per row divides by ||q|| + 1e-6 (the reference's L2, xenc/injector.py:58).
+constexpr int PIN_CHUNK = 1024;  // columns per reduce CTA (256 threads x 4)
+
+template <typename TH>
+__global__ void __launch_bounds__(256) project_in_reduce_kernel(
     const TH* __restrict__ h, int d_m, const float* __restrict__ part, int splits, int64_t M, int d_s, int flags,
     const float* __restrict__ b_in, const float* __restrict__ gate_w, float gate_b,
     const float* __restrict__ sel_w, const float* __restrict__ sel_b, int n_cand, float eps,
-    float* __restrict__ q_out, float* __restrict__ gate_out, float* __restrict__ rstd_out,
-    float* __restrict__ z_out) {
+    float* __restrict__ q_out, float* __restrict__ nq_part, int* __restrict__ row_done, float* __restrict__ gate_out,
+    float* __restrict__ rstd_out, float* __restrict__ z_out) {
   __shared__ float red[32];
   __shared__ float zsh[32];
   const int64_t row = blockIdx.x;
+  const int chunk = blockIdx.y;
   const TH* hr = h + row * d_m;
 
-  // rms_norm scale
-  float ss = 0.f, gd = 0.f;
-  for (int i = threadIdx.x; i < d_m; i += blockDim.x) {
-    const float x = to_f32(hr[i]);
-    ss = fmaf(x, x, ss);
-    if (gate_w) gd = fmaf(x, gate_w[i], gd);
+  float ss, gd, unused;
+  row_dots<TH>(hr, d_m, chunk == 0 ? gate_w : nullptr, nullptr, ss, gd, unused);
+  float rstd = 1.f;
+  if (flags & XENCB_PIN_RMS) {  // every chunk CTA needs 1/rms; the row is 4-16 KB and L2-resident
+    ss = block_sum(ss, red);
+    rstd = rsqrtf(ss / (float)d_m + eps);
   }
-  ss = block_sum(ss, red);
-  const float rstd = (flags & XENCB_PIN_RMS) ? rsqrtf(ss / (float)d_m + eps) : 1.f;
-  if (gate_w) {
-    gd = block_sum(gd, red);
-    if (threadIdx.x == 0) {
-      const float zg = gd * rstd + gate_b;
-      gate_out[row] = 1.f / (1.f + expf(-zg));
+  if (chunk == 0) {
+    if (rstd_out && threadIdx.x == 0) rstd_out[row] = (flags & XENCB_PIN_RMS) ? rstd : 1.f;
+    if (gate_w) {
+      gd = block_sum(gd, red);
+      if (threadIdx.x == 0) gate_out[row] = 1.f / (1.f + expf(-(gd * rstd + gate_b)));
+    }
+    if (sel_w) {
+      const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+      for (int c = wid; c < n_cand; c += nw) {
+        const float* u = sel_w + (int64_t)c * d_m;
+        float d = 0.f;
+        for (int i = lane; i < d_m; i += 32) d = fmaf(to_f32(hr[i]), u[i], d);
+        d = warp_sum(d);
+        if (lane == 0) zsh[c] = d * rstd + (sel_b ? sel_b[c] : 0.f);
+      }
+      __syncthreads();
+      if (threadIdx.x < n_cand) z_out[row * n_cand + threadIdx.x] = zsh[threadIdx.x];
     }
   }
-  if (rstd_out && threadIdx.x == 0) rstd_out[row] = rstd;
-
-  // selector logits: one warp per candidate
-  if (sel_w) {
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (int c = wid; c < n_cand; c += nw) {
-      const float* u = sel_w + (int64_t)c * d_m;
-      float d = 0.f;
-      for (int i = lane; i < d_m; i += 32) d = fmaf(to_f32(hr[i]), u[i], d);
-      d = warp_sum(d);
-      if (lane == 0) zsh[c] = d * rstd + (sel_b ? sel_b[c] : 0.f);
-    }
-    __syncthreads();
-    if (threadIdx.x < n_cand) z_out[row * n_cand + threadIdx.x] = zsh[threadIdx.x];
-  }
-
-  // q = rstd * sum_z part + b, then L2
-  float* qr = q_out + row * d_s;
   float nq = 0.f;
-  for (int n = threadIdx.x; n < d_s; n += blockDim.x) {
-    float v = 0.f;
-    for (int z = 0; z < splits; ++z) v += part[((int64_t)z * M + row) * d_s + n];
-    v = v * rstd + (b_in ? b_in[n] : 0.f);
-    qr[n] = v;
-    nq = fmaf(v, v, nq);
+  const int n = chunk * PIN_CHUNK + threadIdx.x * 4;
+  if (n < d_s) {
+    const float4 v = sum_splits4(part, splits, M, d_s, row, n);
+    float4 o;
+    o.x = v.x * rstd + (b_in ? b_in[n] : 0.f);
+    o.y = v.y * rstd + (b_in ? b_in[n + 1] : 0.f);
+    o.z = v.z * rstd + (b_in ? b_in[n + 2] : 0.f);
+    o.w = v.w * rstd + (b_in ? b_in[n + 3] : 0.f);
+    *reinterpret_cast<float4*>(q_out + row * d_s + n) = o;
+    nq = o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
   }
-  if (flags & XENCB_PIN_L2) {
-    nq = block_sum(nq, red);
-    const float den = sqrtf(nq) + 1e-6f;
-    for (int n = threadIdx.x; n < d_s; n += blockDim.x) qr[n] = qr[n] / den;
+  __threadfence();  // this CTA's q columns are visible to whichever CTA normalises the row
+  nq = block_sum(nq, red);
+  if (!(flags & XENCB_PIN_L2)) return;
+  // the CTA that finishes a row last divides the whole row by ||q|| + 1e-6 (chunk sums in a fixed order)
+  __shared__ int last;
+  if (threadIdx.x == 0) {
+    nq_part[row * gridDim.y + chunk] = nq;
+    __threadfence();
+    last = atomicAdd(&row_done[row], 1) == (int)gridDim.y - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  float tot = 0.f;
+  for (int c = 0; c < (int)gridDim.y; ++c) tot += __ldcg(nq_part + row * gridDim.y + c);
+  const float den = sqrtf(tot) + 1e-6f;
+  float* qr = q_out + row * d_s;
+  for (int m = threadIdx.x * 4; m < d_s; m += blockDim.x * 4) {
+    float4 o = __ldcg(reinterpret_cast<const float4*>(qr + m));
+    o.x /= den; o.y /= den; o.z /= den; o.w /= den;
+    *reinterpret_cast<float4*>(qr + m) = o;
   }
 }
 
@@ -208,49 +308,91 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const TH* __restrict__ h,
 }
 
 // ------------------------------------------------------------------------------------------------ project_out
-// One CTA per row. Dynamic smem: d_m floats holding the row of delta in float32.
+// project_out_reduce: one CTA per (row, 1024-column chunk): d = scale * gate * (sum of split partials + bias)
+// into the workspace, plus the chunk's sums of d^2 and h^2. project_out_epilogue: one CTA per row: the
+// selector's matched norm, the position mask, the cast to h's dtype, h + delta and the mag term.
 template <typename TH>
-__global__ void __launch_bounds__(256) project_out_finish_kernel(
+__global__ void __launch_bounds__(256) project_out_reduce_kernel(
     const float* __restrict__ part, int splits, int64_t M, int d_m, const float* __restrict__ b_out, float scale,
-    const float* __restrict__ gate, const float* __restrict__ sel_w, float alpha, const float* __restrict__ pos_mask,
-    const TH* h, TH* delta_out, TH* h_out, float* __restrict__ rel_out) {
-  extern __shared__ float drow[];
+    const float* __restrict__ gate, const TH* __restrict__ h, float* __restrict__ d_out,
+    float* __restrict__ norm_part, int* __restrict__ row_done) {
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
+  const int chunk = blockIdx.y;
+  if (chunk == 0 && threadIdx.x == 0) row_done[row] = 0;  // the epilogue's per-row counter
   const float g = (gate ? gate[row] : 1.f) * scale;
-
   float dd = 0.f, hh = 0.f;
-  for (int n = threadIdx.x; n < d_m; n += blockDim.x) {
-    float v = 0.f;
-    for (int z = 0; z < splits; ++z) v += part[((int64_t)z * M + row) * d_m + n];
-    v = g * (v + (b_out ? b_out[n] : 0.f));
-    drow[n] = v;
-    dd = fmaf(v, v, dd);
-    const float x = to_f32(h[row * d_m + n]);
-    hh = fmaf(x, x, hh);
+  const int n = chunk * PIN_CHUNK + threadIdx.x * 4;
+  if (n < d_m) {
+    const float4 v = sum_splits4(part, splits, M, d_m, row, n);
+    float4 o;
+    o.x = g * (v.x + (b_out ? b_out[n] : 0.f));
+    o.y = g * (v.y + (b_out ? b_out[n + 1] : 0.f));
+    o.z = g * (v.z + (b_out ? b_out[n + 2] : 0.f));
+    o.w = g * (v.w + (b_out ? b_out[n + 3] : 0.f));
+    *reinterpret_cast<float4*>(d_out + row * d_m + n) = o;
+    dd = o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) { const float y = to_f32(h[row * d_m + n + u]); hh = fmaf(y, y, hh); }
   }
   dd = block_sum(dd, red);
   hh = block_sum(hh, red);
+  if (threadIdx.x == 0) {
+    norm_part[(row * gridDim.y + chunk) * 2] = dd;
+    norm_part[(row * gridDim.y + chunk) * 2 + 1] = hh;
+  }
+}
+
+template <typename TH>
+__global__ void __launch_bounds__(256) project_out_epilogue_kernel(
+    const float* __restrict__ d_in, const float* __restrict__ norm_part, int d_m, const float* __restrict__ sel_w,
+    float alpha, const float* __restrict__ pos_mask, const TH* h, TH* delta_out, TH* h_out, float* __restrict__ rel_out,
+    float* __restrict__ cn_part, int* __restrict__ row_done) {
+  __shared__ float red[32];
+  __shared__ int last;
+  const int64_t row = blockIdx.x;
+  const int chunk = blockIdx.y, n_chunks = gridDim.y;
+  float dd = 0.f, hh = 0.f;
+  for (int c = 0; c < n_chunks; ++c) {
+    dd += norm_part[(row * n_chunks + c) * 2];
+    hh += norm_part[(row * n_chunks + c) * 2 + 1];
+  }
   const float hnorm = sqrtf(hh);
   // LayerSelector.apply: d / (||d|| / (||h|| + eps) + eps) * exp(log_alpha), then * w[..., pos]
   const float rel_d = sqrtf(dd) / (hnorm + 1e-6f) + 1e-6f;
   const float sw = sel_w ? sel_w[row] : 1.f;
   const float pm = pos_mask ? pos_mask[row] : 1.f;
-
   float cn = 0.f;
-  for (int n = threadIdx.x; n < d_m; n += blockDim.x) {
-    float v = drow[n];
-    if (sel_w) v = sw * ((v / rel_d) * alpha);
-    if (pos_mask) v *= pm;
-    const TH dv = from_f32<TH>(v);
-    const float dvf = to_f32(dv);
-    cn = fmaf(dvf, dvf, cn);
-    if (delta_out) delta_out[row * d_m + n] = dv;
-    if (h_out) h_out[row * d_m + n] = from_f32<TH>(to_f32(h[row * d_m + n]) + dvf);
+  const int n = chunk * PIN_CHUNK + threadIdx.x * 4;
+  if (n < d_m) {
+    const float4 v4 = *reinterpret_cast<const float4*>(d_in + row * d_m + n);
+    const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float v = vv[u];
+      if (sel_w) v = sw * ((v / rel_d) * alpha);
+      if (pos_mask) v *= pm;
+      const TH dv = from_f32<TH>(v);
+      const float dvf = to_f32(dv);
+      cn = fmaf(dvf, dvf, cn);
+      if (delta_out) delta_out[row * d_m + n + u] = dv;
+      if (h_out) h_out[row * d_m + n + u] = from_f32<TH>(to_f32(h[row * d_m + n + u]) + dvf);
+    }
   }
-  if (rel_out) {
-    cn = block_sum(cn, red);
-    if (threadIdx.x == 0) rel_out[row] = sqrtf(cn) / (hnorm + 1e-6f);
+  if (!rel_out) return;
+  cn = block_sum(cn, red);
+  // the CTA that finishes a row last sums the chunk norms in a fixed order
+  if (threadIdx.x == 0) {
+    cn_part[row * n_chunks + chunk] = cn;
+    __threadfence();
+    last = atomicAdd(&row_done[row], 1) == n_chunks - 1;
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    __threadfence();
+    float tot = 0.f;
+    for (int c = 0; c < n_chunks; ++c) tot += __ldcg(cn_part + row * n_chunks + c);
+    rel_out[row] = sqrtf(tot) / (hnorm + 1e-6f);
   }
 }
 

@@ -32,12 +32,25 @@ __global__ void __launch_bounds__(256) route_logits_kernel(const float* __restri
   const float* sr = S + (lib * C + c) * (int64_t)d_s;
   float d = 0.f;
   if ((d_s & 3) == 0) {
+    // four independent 16-byte loads of S in flight per lane per step
     const float4* q4 = reinterpret_cast<const float4*>(qr);
     const float4* s4 = reinterpret_cast<const float4*>(sr);
-    for (int i = lane; i < (d_s >> 2); i += 32) {
-      const float4 a = __ldg(q4 + i), b = __ldg(s4 + i);
+    const int n4 = d_s >> 2;
+    float d1 = 0.f, d2 = 0.f, d3 = 0.f;
+    int i = lane;
+    for (; i + 96 < n4; i += 128) {
+      const float4 b0 = __ldcs(s4 + i), b1 = __ldcs(s4 + i + 32), b2 = __ldcs(s4 + i + 64), b3 = __ldcs(s4 + i + 96);
+      const float4 a0 = __ldg(q4 + i), a1 = __ldg(q4 + i + 32), a2 = __ldg(q4 + i + 64), a3 = __ldg(q4 + i + 96);
+      d = fmaf(a0.x, b0.x, d); d = fmaf(a0.y, b0.y, d); d = fmaf(a0.z, b0.z, d); d = fmaf(a0.w, b0.w, d);
+      d1 = fmaf(a1.x, b1.x, d1); d1 = fmaf(a1.y, b1.y, d1); d1 = fmaf(a1.z, b1.z, d1); d1 = fmaf(a1.w, b1.w, d1);
+      d2 = fmaf(a2.x, b2.x, d2); d2 = fmaf(a2.y, b2.y, d2); d2 = fmaf(a2.z, b2.z, d2); d2 = fmaf(a2.w, b2.w, d2);
+      d3 = fmaf(a3.x, b3.x, d3); d3 = fmaf(a3.y, b3.y, d3); d3 = fmaf(a3.z, b3.z, d3); d3 = fmaf(a3.w, b3.w, d3);
+    }
+    for (; i < n4; i += 32) {
+      const float4 a = __ldg(q4 + i), b = __ldcs(s4 + i);
       d = fmaf(a.x, b.x, d); d = fmaf(a.y, b.y, d); d = fmaf(a.z, b.z, d); d = fmaf(a.w, b.w, d);
     }
+    d = (d + d1) + (d2 + d3);
   } else {
     for (int i = lane; i < d_s; i += 32) d = fmaf(__ldg(qr + i), __ldg(sr + i), d);
   }

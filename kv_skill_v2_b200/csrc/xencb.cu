@@ -125,10 +125,14 @@ GemmPlan plan_gemm(int64_t M, int N, int K, int sms) {
 }
 
 template <typename TX>
-void launch_gemm(const void* X, int64_t M, int K, const float* W, int N, const GemmPlan& p, float* part,
-                 cudaStream_t st) {
+int launch_gemm(const void* X, int64_t M, int K, const float* Wt, int N, const GemmPlan& p, float* part,
+                int* row_done, cudaStream_t st) {
+  int rc = ensure_smem(gemm_xw_splitk_kernel<TX>, (int)GEMM_SMEM);
+  if (rc) return rc;
   dim3 grid((N + GEMM_BN - 1) / GEMM_BN, (unsigned)((M + GEMM_BM - 1) / GEMM_BM), p.splits);
-  gemm_tn_splitk_kernel<TX><<<grid, GEMM_THREADS, 0, st>>>(static_cast<const TX*>(X), M, K, W, N, p.kps, part);
+  gemm_xw_splitk_kernel<TX><<<grid, GEMM_THREADS, GEMM_SMEM, st>>>(static_cast<const TX*>(X), M, K, Wt, N, p.kps,
+                                                                   part, row_done);
+  return XENCB_OK;
 }
 
 // ------------------------------------------------------------------------------------------------ read plan
@@ -299,7 +303,9 @@ size_t xencb_project_in_workspace(int64_t n_rows, int d_m, int d_s) {
   DevInfo di;
   if (device_info(&di)) return 0;
   if (n_rows <= 0 || d_m <= 0 || d_s <= 0) return 0;
-  return plan_gemm(n_rows, d_s, d_m, di.sms).part_bytes;
+  const int nch = (d_s + PIN_CHUNK - 1) / PIN_CHUNK;
+  return plan_gemm(n_rows, d_s, d_m, di.sms).part_bytes + align_up((size_t)n_rows * nch * sizeof(float), 256) +
+         align_up((size_t)n_rows * sizeof(int), 256);
 }
 
 int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const float* w_in, const float* b_in,
@@ -312,35 +318,42 @@ int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const 
     return fail(XENCB_EINVAL, "project_in: n_rows=%lld d_m=%d d_s=%d must be positive", (long long)n_rows, d_m, d_s);
   if (!elem_size(h_dtype)) return fail(XENCB_EINVAL, "project_in: h_dtype %d unknown", h_dtype);
   if (gate_w && !gate_out) return fail(XENCB_EINVAL, "project_in: gate_w given without gate_out");
+  if (d_s % 4 != 0 || !aligned(w_in, 16) || !aligned(q_out, 16))
+    return fail(XENCB_EINVAL, "project_in: d_s=%d must be a multiple of 4 and w_in / q_out 16-byte aligned", d_s);
   if (sel_w && (!z_out || n_cand <= 0 || n_cand > 32))
     return fail(XENCB_EINVAL, "project_in: selector needs z_out and 1 <= n_cand <= 32 (got %d)", n_cand);
   DevInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
   const GemmPlan gp = plan_gemm(n_rows, d_s, d_m, di.sms);
-  if (!workspace || workspace_bytes < gp.part_bytes || !aligned(workspace, 256))
-    return fail(XENCB_EINVAL, "project_in: workspace needs %zu bytes, 256-byte aligned (got %zu)", gp.part_bytes,
+  const int nch = (d_s + PIN_CHUNK - 1) / PIN_CHUNK;
+  const size_t nq_bytes = align_up((size_t)n_rows * nch * sizeof(float), 256);
+  const size_t need = gp.part_bytes + nq_bytes + align_up((size_t)n_rows * sizeof(int), 256);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+    return fail(XENCB_EINVAL, "project_in: workspace needs %zu bytes, 256-byte aligned (got %zu)", need,
                 workspace_bytes);
+  float* nq_part = reinterpret_cast<float*>(static_cast<char*>(workspace) + gp.part_bytes);
+  int* row_done = reinterpret_cast<int*>(static_cast<char*>(workspace) + gp.part_bytes + nq_bytes);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   float* part = static_cast<float*>(workspace);
   switch (h_dtype) {
-    case XENCB_F32: launch_gemm<float>(h, n_rows, d_m, w_in, d_s, gp, part, st); break;
-    case XENCB_F16: launch_gemm<__half>(h, n_rows, d_m, w_in, d_s, gp, part, st); break;
-    default: launch_gemm<__nv_bfloat16>(h, n_rows, d_m, w_in, d_s, gp, part, st); break;
+    case XENCB_F32: rc = launch_gemm<float>(h, n_rows, d_m, w_in, d_s, gp, part, row_done, st); break;
+    case XENCB_F16: rc = launch_gemm<__half>(h, n_rows, d_m, w_in, d_s, gp, part, row_done, st); break;
+    default: rc = launch_gemm<__nv_bfloat16>(h, n_rows, d_m, w_in, d_s, gp, part, row_done, st); break;
   }
+  if (rc) return rc;
   XENCB_CHECK_LAUNCH("project_in gemm launch");
 #define XENCB_PIN(T)                                                                                         \
-  project_in_finish_kernel<T><<<(unsigned)n_rows, 256, 0, st>>>(                                            \
+  project_in_reduce_kernel<T><<<dim3((unsigned)n_rows, nch), 256, 0, st>>>(                                   \
       static_cast<const T*>(h), d_m, part, gp.splits, n_rows, d_s, flags, b_in, gate_w, gate_b, sel_w, sel_b,    \
-      n_cand, \
-      rms_eps, q_out, gate_out, rstd_out, z_out)
+      n_cand, rms_eps, q_out, nq_part, row_done, gate_out, rstd_out, z_out)
   switch (h_dtype) {
     case XENCB_F32: XENCB_PIN(float); break;
     case XENCB_F16: XENCB_PIN(__half); break;
     default: XENCB_PIN(__nv_bfloat16); break;
   }
 #undef XENCB_PIN
-  XENCB_CHECK_LAUNCH("project_in finish launch");
+  XENCB_CHECK_LAUNCH("project_in reduce launch");
   return XENCB_OK;
 }
 
@@ -508,7 +521,9 @@ size_t xencb_project_out_workspace(int64_t n_rows, int d_s, int d_m) {
   DevInfo di;
   if (device_info(&di)) return 0;
   if (n_rows <= 0 || d_m <= 0 || d_s <= 0) return 0;
-  return plan_gemm(n_rows, d_m, d_s, di.sms).part_bytes;
+  const int nch = (d_m + PIN_CHUNK - 1) / PIN_CHUNK;
+  return plan_gemm(n_rows, d_m, d_s, di.sms).part_bytes + align_up((size_t)n_rows * d_m * sizeof(float), 256) +
+         align_up((size_t)n_rows * nch * 3 * sizeof(float), 256) + align_up((size_t)n_rows * sizeof(int), 256);
 }
 
 int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_out, const float* b_out, int d_m,
@@ -518,27 +533,36 @@ int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_ou
   if (!r || !w_out || !h) return fail(XENCB_EINVAL, "project_out: r, w_out and h are required");
   if (n_rows <= 0 || d_m <= 0 || d_s <= 0) return fail(XENCB_EINVAL, "project_out: sizes must be positive");
   if (!elem_size(h_dtype)) return fail(XENCB_EINVAL, "project_out: h_dtype %d unknown", h_dtype);
-  if ((size_t)d_m * 4 > 200 * 1024) return fail(XENCB_ENOTSUP, "project_out: d_m=%d too large", d_m);
+  if (d_m % 4 != 0 || !aligned(w_out, 16) || !aligned(r, 16))
+    return fail(XENCB_EINVAL, "project_out: d_m=%d must be a multiple of 4 and w_out / r 16-byte aligned", d_m);
   DevInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
   const GemmPlan gp = plan_gemm(n_rows, d_m, d_s, di.sms);
-  if (!workspace || workspace_bytes < gp.part_bytes || !aligned(workspace, 256))
-    return fail(XENCB_EINVAL, "project_out: workspace needs %zu bytes, 256-byte aligned (got %zu)", gp.part_bytes,
+  const int nch = (d_m + PIN_CHUNK - 1) / PIN_CHUNK;
+  const size_t d_bytes = align_up((size_t)n_rows * d_m * sizeof(float), 256);
+  const size_t np_bytes = align_up((size_t)n_rows * nch * 3 * sizeof(float), 256);
+  const size_t need = gp.part_bytes + d_bytes + np_bytes + align_up((size_t)n_rows * sizeof(int), 256);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
+    return fail(XENCB_EINVAL, "project_out: workspace needs %zu bytes, 256-byte aligned (got %zu)", need,
                 workspace_bytes);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   float* part = static_cast<float*>(workspace);
-  launch_gemm<float>(r, n_rows, d_s, w_out, d_m, gp, part, st);
+  float* dbuf = reinterpret_cast<float*>(static_cast<char*>(workspace) + gp.part_bytes);
+  float* norm_part = reinterpret_cast<float*>(static_cast<char*>(workspace) + gp.part_bytes + d_bytes);
+  float* cn_part = norm_part + (size_t)n_rows * nch * 2;
+  int* row_done = reinterpret_cast<int*>(static_cast<char*>(workspace) + gp.part_bytes + d_bytes + np_bytes);
+  rc = launch_gemm<float>(r, n_rows, d_s, w_out, d_m, gp, part, nullptr, st);
+  if (rc) return rc;
   XENCB_CHECK_LAUNCH("project_out gemm launch");
   const float alpha = expf(log_alpha);
-  const int smem = d_m * 4;
 #define XENCB_POUT(T)                                                                                          \
   do {                                                                                                         \
-    int rc2 = ensure_smem(project_out_finish_kernel<T>, smem > 48 * 1024 ? smem : 48 * 1024);                \
-    if (rc2) return rc2;                                                                                       \
-    project_out_finish_kernel<T><<<(unsigned)n_rows, 256, smem, st>>>(                                        \
-        part, gp.splits, n_rows, d_m, b_out, scale, gate, sel_w, alpha, pos_mask, static_cast<const T*>(h),   \
-        static_cast<T*>(delta_out), static_cast<T*>(h_out), rel_out);                                          \
+    project_out_reduce_kernel<T><<<dim3((unsigned)n_rows, nch), 256, 0, st>>>(                                \
+        part, gp.splits, n_rows, d_m, b_out, scale, gate, static_cast<const T*>(h), dbuf, norm_part, row_done);\
+    project_out_epilogue_kernel<T><<<dim3((unsigned)n_rows, nch), 256, 0, st>>>(                               \
+        dbuf, norm_part, d_m, sel_w, alpha, pos_mask, static_cast<const T*>(h), static_cast<T*>(delta_out),     \
+        static_cast<T*>(h_out), rel_out, cn_part, row_done);                                                   \
   } while (0)
   switch (h_dtype) {
     case XENCB_F32: XENCB_POUT(float); break;
@@ -546,7 +570,7 @@ int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_ou
     default: XENCB_POUT(__nv_bfloat16); break;
   }
 #undef XENCB_POUT
-  XENCB_CHECK_LAUNCH("project_out finish launch");
+  XENCB_CHECK_LAUNCH("project_out epilogue launch");
   return XENCB_OK;
 }
 
