@@ -225,8 +225,8 @@ def build_workload(torch, dev, docs: int, seed: int):
     page_of = torch.arange(docs * C, dtype=torch.int32, device=dev).view(docs, C)
     S = ops.summaries(slots, page_of, nv)
     pages = ops.Pages(slots=slots, page_of=page_of, n_valid=nv, S=S)
-    W_in = torch.randn(d_m, d_s, generator=g, device=dev) * 0.02   # input-major [in, out]
-    W_out = torch.randn(d_s, d_m, generator=g, device=dev) * 0.02
+    W_in = torch.randn(d_s, d_m, generator=g, device=dev) * 0.02   # nn.Linear layout [out, in]
+    W_out = torch.randn(d_m, d_s, generator=g, device=dev) * 0.02
     return pages, W_in, W_out, g
 
 
@@ -353,7 +353,7 @@ def run_ours(args) -> None:
                 return x
 
         reader = Reader()
-        itf = LinearInterface(W_in, W_out, [0]).to(dev).requires_grad_(False)
+        itf = LinearInterface(W_in.t(), W_out.t(), [0]).to(dev).requires_grad_(False)
         inj = LibraryInjector(reader, itf, top_k=CFG["top_k"], read_temp=CFG["read_temp"], route_temp=CFG["route_temp"])
         inj.load_library(PagedLibrary({0: pages}))
         h_host = [hs[i].view(docs, CFG["T"], d_m).cpu().pin_memory() for i in range(min(n_h, 64))]

@@ -12,8 +12,9 @@
  *               slots + p * page_stride (elements). A Library is a table page_of[lib, c] -> page index
  *               with n_valid[lib, c] valid rows (the reference's mask, xenc/library.py:51-55).
  *   S           summary keys, float32 [n_lib, C, d_s] (xenc/library.py:69-74).
- *   weights     input-major float32: w[k][n] multiplies input feature k into output n, i.e. the transpose of a
- *               torch nn.Linear weight ([in_features, out_features]); output counts are multiples of 4.
+ *   weights     float32 in torch nn.Linear layout: [out_features, in_features]; output counts are multiples of 4.
+ *               The projections run on the tcgen05 tensor cores (3xTF32) when in_features % 4 == 0 and the rows
+ *               are 16-byte aligned, else on a CUDA-core fallback.
  *
  * Return value: XENCB_OK or an error code; xencb_last_error() gives the message of the last failing call on
  * the calling thread. XENCB_EINVAL is the reference's ValueError (bad shape / argument), the others are
@@ -68,7 +69,7 @@ XENCB_API int xencb_device_status(void* stream, int clear, unsigned int* status_
  *            A full-rank A is one call with both flags; a low-rank A = Sequential(A1, A2) is a call with
  *            XENCB_PIN_RMS into a float32 [n_rows, rank] buffer, then one with XENCB_PIN_L2 over it.
  *   h        [n_rows, d_m] of h_dtype (the reference upcasts h to float32 first; so does this)
- *   w_in     [d_m, d_s] float32 (input-major); b_in [d_s] or NULL; d_s % 4 == 0
+ *   w_in     [d_s, d_m] float32; b_in [d_s] or NULL; d_s % 4 == 0
  *   gate_w   [d_m] or NULL (then gate_out is not written); gate_b the scalar gate_b[pos[li]]
  *   sel_w    [n_cand, d_m] or NULL: LayerSelector logits z = hn @ sel_w^T + sel_b (xenc/selector.py:69-74)
  *   q_out    [n_rows, d_s] float32; gate_out [n_rows] or NULL; rstd_out [n_rows] or NULL (1/rms)
@@ -146,8 +147,8 @@ XENCB_API int xencb_read_decode_noalloc(const float* q, int64_t n_rows, int d_s,
  *   d       *= pos_mask[row]                                              (pos_mask NULL -> 1)
  *   delta_out = d in h_dtype (or NULL); h_out = h + delta_out in h_dtype (or NULL; may alias h);
  *   rel_out[row] = ||delta_out|| / (||h|| + 1e-6)                         (or NULL)
- *   h        [n_rows, d_m] of h_dtype; r [n_rows, d_s] float32; w_out [d_s, d_m] (input-major); b_out [d_m] or
- *            NULL; d_m % 4 == 0. */
+ *   h        [n_rows, d_m] of h_dtype; r [n_rows, d_s] float32; w_out [d_m, d_s]; b_out [d_m] or NULL;
+ *            d_m % 4 == 0. */
 XENCB_API size_t xencb_project_out_workspace(int64_t n_rows, int d_s, int d_m);
 XENCB_API int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_out, const float* b_out, int d_m,
                       float scale, const float* gate, const float* sel_w, float log_alpha, const float* pos_mask,

@@ -4,8 +4,8 @@
 //   project_out: delta = scale * gate * (r @ W_out^T + b) -> selector matched norm -> position mask ->
 //                cast to h's dtype -> mag term and h + delta
 //
-// The contraction runs as a split-K SIMT GEMM (Y_part[z] = X[:, Kz] @ W[:, Kz]^T) into a caller-provided
-// workspace; a per-row "finish" kernel then reduces the splits and applies every elementwise step, so the
+// The contraction runs as a split-K GEMM (Y_part[z] = X[:, Kz] @ W[:, Kz]^T, gemm_tc.cuh on the tensor cores, or the
+// SIMT fallback below) into a caller-provided workspace; a per-row "finish" kernel then reduces the splits and applies every elementwise step, so the
 // full output row is available for the L2 / matched-norm reductions. rms_norm's 1/rms factor is applied to
 // the GEMM result (it is a per-row scalar), which keeps h in its storage type on the GEMM's input side.
 #pragma once
@@ -14,119 +14,98 @@
 
 namespace xencb {
 
-constexpr int GEMM_BM = 64, GEMM_BN = 128, GEMM_BK = 32, GEMM_THREADS = 128, GEMM_BSTAGES = 3;
-constexpr int GEMM_APAD = GEMM_BM + 4;
-constexpr size_t GEMM_SMEM = (size_t)(2 * GEMM_BK * GEMM_APAD + GEMM_BSTAGES * GEMM_BK * GEMM_BN) * sizeof(float);
+// SIMT fallback GEMM (shapes the TMA path cannot take: K % 4 != 0 or unaligned rows), torch nn.Linear
+// weight layout W [N, K]:
+constexpr int SG_BM = 64, SG_BN = 128, SG_BK = 16, SG_THREADS = 128;
+constexpr int SG_APAD = SG_BM + 4, SG_BPAD = SG_BN + 4;
 
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src, bool valid) {
-  const uint32_t d = smem_u32(smem_dst);
-  const int n = valid ? 16 : 0;  // 0 source bytes: the 16 destination bytes are zero-filled
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(gmem_src), "r"(n) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-// part[z][m][n] = sum_{k in [z*kps, min(K,(z+1)*kps))} X[m][k] * Wt[k][n]   (Wt input-major: [K, N])
-// grid: (ceil(N/128), ceil(M/64), splits); 128 threads, each an 8x8 register tile (rows 8*ty.., columns
-// 4*tx.. and 64+4*tx..), packed f32x2 FMAs. The weight tile streams through a 3-stage cp.async ring (16-byte
-// chunks, N % 4 == 0); the activation tile (any float type) is loaded through registers, converted and stored
-// transposed (As[k][m]) one slice ahead.
+// part[z][m][n] = sum_{k in [z*kps, min(K,(z+1)*kps))} X[m][k] * W[n][k]
+// grid: (ceil(N/BN), ceil(M/BM), splits); block 128 threads, each an 8x8 register tile.
 template <typename TX>
-__global__ void __launch_bounds__(GEMM_THREADS) gemm_xw_splitk_kernel(const TX* __restrict__ X, int64_t M, int K,
-                                                                       const float* __restrict__ Wt, int N, int kps,
+__global__ void __launch_bounds__(SG_THREADS) gemm_simt_splitk_kernel(const TX* __restrict__ X, int64_t M, int K,
+                                                                       const float* __restrict__ W, int N, int kps,
                                                                        float* __restrict__ part,
                                                                        int* __restrict__ row_done) {
-  // zero the per-row completion counters the following reduce kernel counts on (stream order)
   if (row_done && blockIdx.x == 0 && blockIdx.z == 0)
-    for (int64_t i = (int64_t)blockIdx.y * GEMM_BM + threadIdx.x; i < min(M, (int64_t)(blockIdx.y + 1) * GEMM_BM);
+    for (int64_t i = (int64_t)blockIdx.y * SG_BM + threadIdx.x; i < min(M, (int64_t)(blockIdx.y + 1) * SG_BM);
          i += blockDim.x)
       row_done[i] = 0;
-  extern __shared__ __align__(16) float gsm[];
-  float (*As)[GEMM_BK][GEMM_APAD] = reinterpret_cast<float (*)[GEMM_BK][GEMM_APAD]>(gsm);
-  float (*Bs)[GEMM_BK][GEMM_BN] = reinterpret_cast<float (*)[GEMM_BK][GEMM_BN]>(gsm + 2 * GEMM_BK * GEMM_APAD);
+  __shared__ __align__(16) float As[2][SG_BK][SG_APAD];
+  __shared__ __align__(16) float Bs[2][SG_BK][SG_BPAD];
 
   const int tid = threadIdx.x;
-  const int ty = tid >> 4, tx = tid & 15;
-  const int64_t m0 = (int64_t)blockIdx.y * GEMM_BM;
-  const int n0 = blockIdx.x * GEMM_BN;
+  const int ty = tid >> 4, tx = tid & 15;  // 8 x 16 thread grid
+  const int64_t m0 = (int64_t)blockIdx.y * SG_BM;
+  const int n0 = blockIdx.x * SG_BN;
   const int kbeg = blockIdx.z * kps;
   const int kend = min(K, kbeg + kps);
-  const int nslices = kend > kbeg ? (kend - kbeg + GEMM_BK - 1) / GEMM_BK : 0;
 
-  float2 acc[8][4];
+  float acc[8][8];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.f, 0.f);
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
 
-  auto load_b = [&](int s) {
-    const int k0 = kbeg + s * GEMM_BK;
-    float* dst = &Bs[s % GEMM_BSTAGES][0][0];
+  // staging registers: A tile 64x16 = 1024 elems -> 8 per thread; B tile 128x16 = 2048 -> 16 per thread
+  float ra[8], rb[16];
+  auto load_tile = [&](int k0) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const int c = tid + i * GEMM_THREADS;  // 0..1023 16-byte chunks
-      const int kk = c >> 5, nn = (c & 31) * 4;
-      const int gk = k0 + kk, gn = n0 + nn;
-      const bool ok = gk < kend && gn < N;  // N % 4 == 0: a chunk is all in or all out
-      cp_async16(dst + kk * GEMM_BN + nn, ok ? (const void*)(Wt + (int64_t)gk * N + gn) : (const void*)Wt, ok);
-    }
-  };
-  float ra[16];
-  auto load_a = [&](int s) {
-    const int k0 = kbeg + s * GEMM_BK;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int e = tid + i * GEMM_THREADS;  // 0..2047
-      const int mm = e >> 5, kk = e & 31;
+      const int f = tid + i * SG_THREADS;  // 0..1023
+      const int mm = f >> 4, kk = f & 15;
       const int64_t gm = m0 + mm;
       const int gk = k0 + kk;
       ra[i] = (gm < M && gk < kend) ? to_f32(X[gm * K + gk]) : 0.f;
     }
-  };
-  auto store_a = [&](int buf) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const int e = tid + i * GEMM_THREADS;
-      As[buf][e & 31][e >> 5] = ra[i];
+      const int f = tid + i * SG_THREADS;  // 0..2047
+      const int nn = f >> 4, kk = f & 15;
+      const int gn = n0 + nn;
+      const int gk = k0 + kk;
+      rb[i] = (gn < N && gk < kend) ? __ldg(W + (int64_t)gn * K + gk) : 0.f;
+    }
+  };
+  auto store_tile = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int f = tid + i * SG_THREADS;
+      As[buf][f & 15][f >> 4] = ra[i];
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int f = tid + i * SG_THREADS;
+      Bs[buf][f & 15][f >> 4] = rb[i];
     }
   };
 
-  if (nslices > 0) {
-    load_b(0);
-    cp_async_commit();
-    if (nslices > 1) load_b(1);
-    cp_async_commit();
-    load_a(0);
-    store_a(0);
-    for (int s = 0; s < nslices; ++s) {
-      cp_async_wait<1>();
-      __syncthreads();
-      if (s + 2 < nslices) load_b(s + 2);
-      cp_async_commit();
-      const bool more = s + 1 < nslices;
-      if (more) load_a(s + 1);
-      const float* as = &As[s & 1][0][0];
-      const float* bs = &Bs[s % GEMM_BSTAGES][0][0];
-#pragma unroll 8
-      for (int kk = 0; kk < GEMM_BK; ++kk) {
-        const float4 a0 = *reinterpret_cast<const float4*>(as + kk * GEMM_APAD + ty * 8);
-        const float4 a1 = *reinterpret_cast<const float4*>(as + kk * GEMM_APAD + ty * 8 + 4);
-        const float4 b0 = *reinterpret_cast<const float4*>(bs + kk * GEMM_BN + tx * 4);
-        const float4 b1 = *reinterpret_cast<const float4*>(bs + kk * GEMM_BN + 64 + tx * 4);
+  if (kbeg < kend) {
+    load_tile(kbeg);
+    store_tile(0);
+    __syncthreads();
+    int buf = 0;
+    for (int k0 = kbeg; k0 < kend; k0 += SG_BK) {
+      const bool more = k0 + SG_BK < kend;
+      if (more) load_tile(k0 + SG_BK);
+#pragma unroll
+      for (int kk = 0; kk < SG_BK; ++kk) {
+        const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 8]);
+        const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 8 + 4]);
+        const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
+        const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][64 + tx * 4]);
         const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        const float2 b[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
-                             make_float2(b1.z, b1.w)};
+        const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float2 ai = make_float2(a[i], a[i]);
+        for (int i = 0; i < 8; ++i)
 #pragma unroll
-          for (int j = 0; j < 4; ++j) acc[i][j] = __ffma2_rn(ai, b[j], acc[i][j]);
-        }
+          for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
       }
-      if (more) store_a((s + 1) & 1);
+      if (more) {
+        store_tile(buf ^ 1);
+        __syncthreads();
+        buf ^= 1;
+      }
     }
-    cp_async_wait<0>();
   }
 
   float* out = part + (int64_t)blockIdx.z * M * N;
@@ -134,27 +113,28 @@ __global__ void __launch_bounds__(GEMM_THREADS) gemm_xw_splitk_kernel(const TX* 
   for (int i = 0; i < 8; ++i) {
     const int64_t gm = m0 + ty * 8 + i;
     if (gm >= M) continue;
-    const int c0 = n0 + tx * 4, c1 = n0 + 64 + tx * 4;
-    if (c0 < N)
-      *reinterpret_cast<float4*>(out + gm * N + c0) = make_float4(acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y);
-    if (c1 < N)
-      *reinterpret_cast<float4*>(out + gm * N + c1) = make_float4(acc[i][2].x, acc[i][2].y, acc[i][3].x, acc[i][3].y);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int gn = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
+      if (gn < N) out[gm * N + gn] = acc[i][j];
+    }
   }
 }
 
-// Split count: at least ~256 columns of K per split, enough CTAs to fill the SMs about twice.
-inline int gemm_splits(int64_t M, int N, int K, int sms) {
-  const int64_t tiles = ((N + GEMM_BN - 1) / GEMM_BN) * ((M + GEMM_BM - 1) / GEMM_BM);
-  const int max_s = (K + 255) / 256;
+// Split count so that the GEMM grid covers the SMs about twice; each split is a multiple of BK.
+inline int sg_splits(int64_t M, int N, int K, int sms) {
+  const int64_t tiles = ((N + SG_BN - 1) / SG_BN) * ((M + SG_BM - 1) / SG_BM);
+  const int kblocks = (K + SG_BK - 1) / SG_BK;
   int64_t s = (2 * (int64_t)sms + tiles - 1) / tiles;
   if (s < 1) s = 1;
-  if (s > max_s) s = max_s;
+  if (s > kblocks) s = kblocks;
+  if (s > 32) s = 32;
   return (int)s;
 }
 
-inline int gemm_kps(int K, int splits) {
-  const int kblocks = (K + GEMM_BK - 1) / GEMM_BK;
-  return ((kblocks + splits - 1) / splits) * GEMM_BK;
+inline int sg_kps(int K, int splits) {
+  const int kblocks = (K + SG_BK - 1) / SG_BK;
+  return ((kblocks + splits - 1) / splits) * SG_BK;
 }
 
 // Sum of the split partials of 4 consecutive columns (col % 4 == 0, N % 4 == 0), loads kept independent.
@@ -291,6 +271,13 @@ __global__ void __launch_bounds__(256) project_in_reduce_kernel(
     o.x /= den; o.y /= den; o.z /= den; o.w /= den;
     *reinterpret_cast<float4*>(qr + m) = o;
   }
+}
+
+// X as float32 rows for the TMA path (hidden states stored in 16-bit types).
+template <typename TH>
+__global__ void __launch_bounds__(256) to_f32_kernel(const TH* __restrict__ x, int64_t n, float* __restrict__ y) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = to_f32(x[i]);
 }
 
 // rms_norm rows: out = h * rsqrt(mean(h^2) + eps); one CTA per row.

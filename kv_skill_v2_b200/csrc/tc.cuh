@@ -1,0 +1,96 @@
+// tcgen05 / TMEM / TMA (tensor) helpers for sm_100a, in inline PTX.
+//
+// Shared-memory operand descriptors follow the canonical K-major layout with 128-byte swizzle: rows of 128 bytes,
+// 16-byte chunks XOR-swizzled by (row % 8), atoms of 8 rows (1024 bytes) stacked along M/N. That is exactly
+// what a 2-D TMA load with CU_TENSOR_MAP_SWIZZLE_128B and a 128-byte inner box writes.
+//   descriptor bits: [0,14) start >> 4 | [16,30) leading byte offset >> 4 | [32,46) stride byte offset >> 4 |
+//                    [46,48) version (1 on sm_100) | [49,52) base offset | [61,64) layout (2 = 128B swizzle)
+// Instruction descriptor (kind::f16 / kind::tf32): [4,6) D format (1 = f32) | [7,10) A format | [10,13) B format
+//   (0 f16, 1 bf16, 2 tf32) | 15 / 16 A / B major (0 = K) | [17,23) N >> 3 | [24,29) M >> 4.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace xencb {
+
+__host__ __device__ constexpr uint32_t umma_idesc(int a_fmt, int b_fmt, int M, int N) {
+  return (1u << 4) | ((uint32_t)a_fmt << 7) | ((uint32_t)b_fmt << 10) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+constexpr int UMMA_F16 = 0, UMMA_BF16 = 1, UMMA_TF32 = 2;
+
+// K-major, 128-byte swizzle, atoms of 8 rows x 128 B packed along the row dimension (SBO = 1024 B).
+__device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;                 // leading byte offset (unused by swizzled K-major; 16 B)
+  d |= (uint64_t)(1024u >> 4) << 32;       // stride byte offset: next 8-row atom
+  d |= (uint64_t)1u << 46;                 // version
+  d |= (uint64_t)2u << 61;                 // SWIZZLE_128B
+  return d;
+}
+
+__device__ __forceinline__ void tc_alloc(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tc_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, issued by one thread.
+template <int KIND>  // 0: kind::f16 (f16 / bf16 operands), 1: kind::tf32
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, bool acc) {
+  const uint32_t z = 0u, en = acc ? 1u : 0u;
+  if (KIND == 1) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(en), "r"(z)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(en), "r"(z)
+        : "memory");
+  }
+}
+
+// Arrive on `bar` once every tcgen05 operation issued so far by this thread has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 16 columns of 32-bit accumulators: thread i of the warp gets lane (base + i), 16 columns.
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 2-D tiled TMA load (no multicast) into this CTA's shared memory; x (innermost) must be 16-byte aligned.
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+}  // namespace xencb

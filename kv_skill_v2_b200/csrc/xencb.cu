@@ -7,6 +7,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <cudaTypedefs.h>
 #include <unordered_map>
 #include <mutex>
 #include <string>
@@ -14,6 +15,7 @@
 
 #include "common.cuh"
 #include "project.cuh"
+#include "gemm_tc.cuh"
 #include "read_decode.cuh"
 #include "read_decode_mma.cuh"
 #include "route.cuh"
@@ -110,28 +112,108 @@ int ensure_smem(K kernel, int smem) {
 }
 
 // ------------------------------------------------------------------------------------------------ GEMM plan
+// Tensor-core path (gemm_tc.cuh) when the rows can be TMA-described (K % 4 == 0, 16-byte aligned bases);
+// otherwise the SIMT fallback. The workspace covers either, so its size does not depend on pointer values.
 struct GemmPlan {
+  bool tc;
   int splits, kps;
   size_t part_bytes;
 };
 
-GemmPlan plan_gemm(int64_t M, int N, int K, int sms) {
+GemmPlan plan_gemm_tc(int64_t M, int N, int K, int sms) {
   GemmPlan p;
-  p.splits = gemm_splits(M, N, K, sms);
-  p.kps = gemm_kps(K, p.splits);
+  p.tc = true;
+  const int64_t tiles = ((N + TC_BM - 1) / TC_BM) * ((M + TC_BN - 1) / TC_BN);
+  const int kblocks = (K + TC_BK - 1) / TC_BK;
+  int64_t s = sms / tiles;  // one CTA per SM (the stage ring takes most of the shared memory)
+  if (s < 1) s = 1;
+  if (s > kblocks) s = kblocks;
+  p.kps = (int)((kblocks + s - 1) / s) * TC_BK;
   p.splits = (K + p.kps - 1) / p.kps;
   p.part_bytes = align_up((size_t)p.splits * (size_t)M * (size_t)N * sizeof(float), 256);
   return p;
 }
 
+GemmPlan plan_gemm_simt(int64_t M, int N, int K, int sms) {
+  GemmPlan p;
+  p.tc = false;
+  p.splits = sg_splits(M, N, K, sms);
+  p.kps = sg_kps(K, p.splits);
+  p.splits = (K + p.kps - 1) / p.kps;
+  p.part_bytes = align_up((size_t)p.splits * (size_t)M * (size_t)N * sizeof(float), 256);
+  return p;
+}
+
+size_t gemm_ws_bytes(int64_t M, int N, int K, int sms, bool convert_x) {
+  size_t b = plan_gemm_simt(M, N, K, sms).part_bytes;
+  if (K % 4 == 0) {
+    size_t t = plan_gemm_tc(M, N, K, sms).part_bytes + (convert_x ? align_up((size_t)M * K * sizeof(float), 256) : 0);
+    if (t > b) b = t;
+  }
+  return b;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int tensor_map_f32_2d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+                      uint32_t box_outer) {
+  if (!g_encode) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_encode) {
+      cudaDriverEntryPointQueryResult q;
+      void* fn = nullptr;
+      cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+      if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+        return fail(XENCB_ECUDA, "cannot resolve cuTensorMapEncodeTiled from the driver");
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  }
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {inner * sizeof(float)};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t es[2] = {1, 1};
+  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
+                              es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(XENCB_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return XENCB_OK;
+}
+
+// part = split partials of X @ W^T. X: [M, K] of type TX; W: [N, K] float32 (nn.Linear layout).
+// `xbuf` (M*K float32, may be null when TX is float) stages a 16-bit X as float32 for the TMA path.
 template <typename TX>
-int launch_gemm(const void* X, int64_t M, int K, const float* Wt, int N, const GemmPlan& p, float* part,
-                int* row_done, cudaStream_t st) {
-  int rc = ensure_smem(gemm_xw_splitk_kernel<TX>, (int)GEMM_SMEM);
-  if (rc) return rc;
-  dim3 grid((N + GEMM_BN - 1) / GEMM_BN, (unsigned)((M + GEMM_BM - 1) / GEMM_BM), p.splits);
-  gemm_xw_splitk_kernel<TX><<<grid, GEMM_THREADS, GEMM_SMEM, st>>>(static_cast<const TX*>(X), M, K, Wt, N, p.kps,
-                                                                   part, row_done);
+int launch_gemm(const void* X, int64_t M, int K, const float* W, int N, int sms, float* part, float* xbuf,
+                int* row_done, cudaStream_t st, GemmPlan* used) {
+  const bool tc_ok = (K % 4 == 0) && aligned(W, 16) && (std::is_same<TX, float>::value ? aligned(X, 16) : xbuf != nullptr);
+  if (tc_ok) {
+    const GemmPlan p = plan_gemm_tc(M, N, K, sms);
+    const float* xf = static_cast<const float*>(X);
+    if (!std::is_same<TX, float>::value) {
+      const int64_t n = M * (int64_t)K;
+      to_f32_kernel<TX><<<(unsigned)std::min<int64_t>((n + 255) / 256, 4096), 256, 0, st>>>(static_cast<const TX*>(X),
+                                                                                            n, xbuf);
+      XENCB_CHECK_LAUNCH("to_f32 launch");
+      xf = xbuf;
+    }
+    CUtensorMap mw, mx;
+    int rc = tensor_map_f32_2d(&mw, W, (uint64_t)K, (uint64_t)N, TC_BK, TC_BM);
+    if (rc) return rc;
+    rc = tensor_map_f32_2d(&mx, xf, (uint64_t)K, (uint64_t)M, TC_BK, TC_BN);
+    if (rc) return rc;
+    rc = ensure_smem(gemm_tc_kernel, (int)TC_SMEM);
+    if (rc) return rc;
+    dim3 grid((N + TC_BM - 1) / TC_BM, (unsigned)((M + TC_BN - 1) / TC_BN), p.splits);
+    gemm_tc_kernel<<<grid, TC_THREADS, TC_SMEM, st>>>(mw, mx, M, N, K, p.kps, part, row_done);
+    XENCB_CHECK_LAUNCH("gemm_tc launch");
+    *used = p;
+    return XENCB_OK;
+  }
+  const GemmPlan p = plan_gemm_simt(M, N, K, sms);
+  dim3 grid((N + SG_BN - 1) / SG_BN, (unsigned)((M + SG_BM - 1) / SG_BM), p.splits);
+  gemm_simt_splitk_kernel<TX><<<grid, SG_THREADS, 0, st>>>(static_cast<const TX*>(X), M, K, W, N, p.kps, part,
+                                                           row_done);
+  XENCB_CHECK_LAUNCH("gemm_simt launch");
+  *used = p;
   return XENCB_OK;
 }
 
@@ -304,7 +386,7 @@ size_t xencb_project_in_workspace(int64_t n_rows, int d_m, int d_s) {
   if (device_info(&di)) return 0;
   if (n_rows <= 0 || d_m <= 0 || d_s <= 0) return 0;
   const int nch = (d_s + PIN_CHUNK - 1) / PIN_CHUNK;
-  return plan_gemm(n_rows, d_s, d_m, di.sms).part_bytes + align_up((size_t)n_rows * nch * sizeof(float), 256) +
+  return gemm_ws_bytes(n_rows, d_s, d_m, di.sms, true) + align_up((size_t)n_rows * nch * sizeof(float), 256) +
          align_up((size_t)n_rows * sizeof(int), 256);
 }
 
@@ -318,31 +400,35 @@ int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const 
     return fail(XENCB_EINVAL, "project_in: n_rows=%lld d_m=%d d_s=%d must be positive", (long long)n_rows, d_m, d_s);
   if (!elem_size(h_dtype)) return fail(XENCB_EINVAL, "project_in: h_dtype %d unknown", h_dtype);
   if (gate_w && !gate_out) return fail(XENCB_EINVAL, "project_in: gate_w given without gate_out");
-  if (d_s % 4 != 0 || !aligned(w_in, 16) || !aligned(q_out, 16))
-    return fail(XENCB_EINVAL, "project_in: d_s=%d must be a multiple of 4 and w_in / q_out 16-byte aligned", d_s);
+  if (d_s % 4 != 0 || !aligned(q_out, 16))
+    return fail(XENCB_EINVAL, "project_in: d_s=%d must be a multiple of 4 and q_out 16-byte aligned", d_s);
   if (sel_w && (!z_out || n_cand <= 0 || n_cand > 32))
     return fail(XENCB_EINVAL, "project_in: selector needs z_out and 1 <= n_cand <= 32 (got %d)", n_cand);
   DevInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
-  const GemmPlan gp = plan_gemm(n_rows, d_s, d_m, di.sms);
   const int nch = (d_s + PIN_CHUNK - 1) / PIN_CHUNK;
+  const size_t g_bytes = gemm_ws_bytes(n_rows, d_s, d_m, di.sms, true);
   const size_t nq_bytes = align_up((size_t)n_rows * nch * sizeof(float), 256);
-  const size_t need = gp.part_bytes + nq_bytes + align_up((size_t)n_rows * sizeof(int), 256);
+  const size_t need = g_bytes + nq_bytes + align_up((size_t)n_rows * sizeof(int), 256);
   if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
     return fail(XENCB_EINVAL, "project_in: workspace needs %zu bytes, 256-byte aligned (got %zu)", need,
                 workspace_bytes);
-  float* nq_part = reinterpret_cast<float*>(static_cast<char*>(workspace) + gp.part_bytes);
-  int* row_done = reinterpret_cast<int*>(static_cast<char*>(workspace) + gp.part_bytes + nq_bytes);
+  char* ws = static_cast<char*>(workspace);
+  float* part = reinterpret_cast<float*>(ws);
+  float* nq_part = reinterpret_cast<float*>(ws + g_bytes);
+  int* row_done = reinterpret_cast<int*>(ws + g_bytes + nq_bytes);
+  // float32 staging of a 16-bit h for the TMA path sits after the tensor-core partials
+  float* xbuf = (d_m % 4 == 0) ? reinterpret_cast<float*>(ws + plan_gemm_tc(n_rows, d_s, d_m, di.sms).part_bytes)
+                               : nullptr;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  float* part = static_cast<float*>(workspace);
+  GemmPlan gp;
   switch (h_dtype) {
-    case XENCB_F32: rc = launch_gemm<float>(h, n_rows, d_m, w_in, d_s, gp, part, row_done, st); break;
-    case XENCB_F16: rc = launch_gemm<__half>(h, n_rows, d_m, w_in, d_s, gp, part, row_done, st); break;
-    default: rc = launch_gemm<__nv_bfloat16>(h, n_rows, d_m, w_in, d_s, gp, part, row_done, st); break;
+    case XENCB_F32: rc = launch_gemm<float>(h, n_rows, d_m, w_in, d_s, di.sms, part, nullptr, row_done, st, &gp); break;
+    case XENCB_F16: rc = launch_gemm<__half>(h, n_rows, d_m, w_in, d_s, di.sms, part, xbuf, row_done, st, &gp); break;
+    default: rc = launch_gemm<__nv_bfloat16>(h, n_rows, d_m, w_in, d_s, di.sms, part, xbuf, row_done, st, &gp); break;
   }
   if (rc) return rc;
-  XENCB_CHECK_LAUNCH("project_in gemm launch");
 #define XENCB_PIN(T)                                                                                         \
   project_in_reduce_kernel<T><<<dim3((unsigned)n_rows, nch), 256, 0, st>>>(                                   \
       static_cast<const T*>(h), d_m, part, gp.splits, n_rows, d_s, flags, b_in, gate_w, gate_b, sel_w, sel_b,    \
@@ -522,7 +608,7 @@ size_t xencb_project_out_workspace(int64_t n_rows, int d_s, int d_m) {
   if (device_info(&di)) return 0;
   if (n_rows <= 0 || d_m <= 0 || d_s <= 0) return 0;
   const int nch = (d_m + PIN_CHUNK - 1) / PIN_CHUNK;
-  return plan_gemm(n_rows, d_m, d_s, di.sms).part_bytes + align_up((size_t)n_rows * d_m * sizeof(float), 256) +
+  return gemm_ws_bytes(n_rows, d_m, d_s, di.sms, false) + align_up((size_t)n_rows * d_m * sizeof(float), 256) +
          align_up((size_t)n_rows * nch * 3 * sizeof(float), 256) + align_up((size_t)n_rows * sizeof(int), 256);
 }
 
@@ -533,28 +619,29 @@ int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_ou
   if (!r || !w_out || !h) return fail(XENCB_EINVAL, "project_out: r, w_out and h are required");
   if (n_rows <= 0 || d_m <= 0 || d_s <= 0) return fail(XENCB_EINVAL, "project_out: sizes must be positive");
   if (!elem_size(h_dtype)) return fail(XENCB_EINVAL, "project_out: h_dtype %d unknown", h_dtype);
-  if (d_m % 4 != 0 || !aligned(w_out, 16) || !aligned(r, 16))
-    return fail(XENCB_EINVAL, "project_out: d_m=%d must be a multiple of 4 and w_out / r 16-byte aligned", d_m);
+  if (d_m % 4 != 0)
+    return fail(XENCB_EINVAL, "project_out: d_m=%d must be a multiple of 4", d_m);
   DevInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
-  const GemmPlan gp = plan_gemm(n_rows, d_m, d_s, di.sms);
   const int nch = (d_m + PIN_CHUNK - 1) / PIN_CHUNK;
+  const size_t g_bytes = gemm_ws_bytes(n_rows, d_m, d_s, di.sms, false);
   const size_t d_bytes = align_up((size_t)n_rows * d_m * sizeof(float), 256);
   const size_t np_bytes = align_up((size_t)n_rows * nch * 3 * sizeof(float), 256);
-  const size_t need = gp.part_bytes + d_bytes + np_bytes + align_up((size_t)n_rows * sizeof(int), 256);
+  const size_t need = g_bytes + d_bytes + np_bytes + align_up((size_t)n_rows * sizeof(int), 256);
   if (!workspace || workspace_bytes < need || !aligned(workspace, 256))
     return fail(XENCB_EINVAL, "project_out: workspace needs %zu bytes, 256-byte aligned (got %zu)", need,
                 workspace_bytes);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  float* part = static_cast<float*>(workspace);
-  float* dbuf = reinterpret_cast<float*>(static_cast<char*>(workspace) + gp.part_bytes);
-  float* norm_part = reinterpret_cast<float*>(static_cast<char*>(workspace) + gp.part_bytes + d_bytes);
+  char* ws = static_cast<char*>(workspace);
+  float* part = reinterpret_cast<float*>(ws);
+  float* dbuf = reinterpret_cast<float*>(ws + g_bytes);
+  float* norm_part = reinterpret_cast<float*>(ws + g_bytes + d_bytes);
   float* cn_part = norm_part + (size_t)n_rows * nch * 2;
-  int* row_done = reinterpret_cast<int*>(static_cast<char*>(workspace) + gp.part_bytes + d_bytes + np_bytes);
-  rc = launch_gemm<float>(r, n_rows, d_s, w_out, d_m, gp, part, nullptr, st);
+  int* row_done = reinterpret_cast<int*>(ws + g_bytes + d_bytes + np_bytes);
+  GemmPlan gp;
+  rc = launch_gemm<float>(r, n_rows, d_s, w_out, d_m, di.sms, part, nullptr, nullptr, st, &gp);
   if (rc) return rc;
-  XENCB_CHECK_LAUNCH("project_out gemm launch");
   const float alpha = expf(log_alpha);
 #define XENCB_POUT(T)                                                                                          \
   do {                                                                                                         \

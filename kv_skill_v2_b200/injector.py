@@ -47,22 +47,8 @@ def _model_device(model) -> torch.device:
     return next(model.parameters()).device
 
 
-_KMAJOR: dict = {}
-
-
-def _input_major(w: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
-    """An nn.Linear weight [out, in] as the input-major float32 [in, out] copy the projection kernels stream,
-    built once per (tensor, version, device) and rebuilt after an in-place update of the weight."""
-    key = (id(w), like.device)
-    ver = w._version
-    hit = _KMAJOR.get(key)
-    if hit is not None and hit[0] == ver and hit[1]() is w:
-        return hit[2]
-    import weakref
-
-    t = w.detach().to(device=like.device, dtype=torch.float32).t().contiguous()
-    _KMAJOR[key] = (ver, weakref.ref(w), t)
-    return t
+def _f32_on(w: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
+    return w.detach().to(device=like.device, dtype=torch.float32).contiguous()
 
 
 def _needs_grad(*objs) -> bool:
@@ -184,7 +170,7 @@ class XEncInjector(ExternalSkillInjector):
         lins = itf.query_weights()
         if len(lins) == 1:
             W, b = lins[0]
-            q, g, _, z = ops.project_in(h2, _input_major(W, h2), None if b is None else _on(b.detach(), h2).float(),
+            q, g, _, z = ops.project_in(h2, _f32_on(W, h2), None if b is None else _on(b.detach(), h2).float(),
                                         gate_w=gate_w, gate_b=gate_b, sel_w=sel_w, sel_b=sel_b)
             return q, g, gain, z
         # low-rank A: rms_norm + first map (gate and selector logits on the normed input), then map + L2
@@ -192,7 +178,7 @@ class XEncInjector(ExternalSkillInjector):
         g = z = None
         for i, (W, b) in enumerate(lins):
             first, last = i == 0, i == len(lins) - 1
-            x, g_i, _, z_i = ops.project_in(x, _input_major(W, h2),
+            x, g_i, _, z_i = ops.project_in(x, _f32_on(W, h2),
                                             None if b is None else _on(b.detach(), h2).float(), rms=first, l2=last,
                                             gate_w=gate_w if first else None, gate_b=gate_b,
                                             sel_w=sel_w if first else None, sel_b=sel_b if first else None)
@@ -205,7 +191,7 @@ class XEncInjector(ExternalSkillInjector):
         if isinstance(itf, LinearInterface):
             return _on(itf.w_out.detach(), like).float(), None
         B = itf.B
-        return _input_major(B.weight, like), None if B.bias is None else _on(B.bias.detach(), like).float()
+        return _f32_on(B.weight, like), None if B.bias is None else _on(B.bias.detach(), like).float()
 
     def _calibrate(self, r: torch.Tensor, li: int):
         gcal = 1.0

@@ -72,12 +72,12 @@ class LinearInterface(nn.Module):
             raise ValueError(f"W_in {tuple(W_in.shape)} and W_out {tuple(W_out.shape)} do not pair up")
         self.d_m, self.d_s = int(W_in.shape[0]), int(W_in.shape[1])
         self.inject_layers = [int(li) for li in (inject_layers or [])]
-        # kept input-major ([in, out]), the layout the projection kernels stream
-        self.w_in = nn.Parameter(W_in.detach().contiguous().float())
-        self.w_out = nn.Parameter(W_out.detach().contiguous().float())
+        # stored as nn.Linear weights ([out, in]), the layout the projection kernels take
+        self.w_in = nn.Parameter(W_in.detach().t().contiguous().float())
+        self.w_out = nn.Parameter(W_out.detach().t().contiguous().float())
 
     def query(self, hn):
-        q = hn @ self.w_in
+        q = hn @ self.w_in.t()
         return q / (q.norm(dim=-1, keepdim=True) + 1e-6)
 
     def gate(self, hn, li):
@@ -87,7 +87,7 @@ class LinearInterface(nn.Module):
         return torch.ones((), device=self.w_in.device)
 
     def write(self, r):
-        return r @ self.w_out
+        return r @ self.w_out.t()
 
 
 def make_interface(d_reader: int, d_encoder: int, reader_layers: list, rank: int = 0, gate_bias_init: float = -2.0,

@@ -92,15 +92,14 @@ def project_in(h2: torch.Tensor, w_in: torch.Tensor, b_in=None, *, rms: bool = T
                gate_w=None, gate_b: float = 0.0, sel_w=None, sel_b=None, eps: float = 1e-6):
     """(q [R, d_s], gate [R] | None, rstd [R], z [R, n_cand] | None) for rows h2 [R, d_m].
 
-    q = L2((rms_norm(h2) if rms else h2) @ w_in + b_in) (L2 only if l2); w_in is input-major [d_m, d_s]
-    (the transpose of an nn.Linear weight)."""
+    q = L2((rms_norm(h2) if rms else h2) @ w_in^T + b_in) (L2 only if l2); w_in is [d_s, d_m] (nn.Linear)."""
     dev = _cuda("project_in", h2, w_in, b_in, gate_w, sel_w, sel_b)
     h2 = h2.contiguous()
     w_in = _f32(w_in, "w_in")
     R, d_m = h2.shape
-    d_s = w_in.shape[1]
-    if w_in.shape[0] != d_m:
-        raise ValueError(f"w_in is {tuple(w_in.shape)}, expected [{d_m}, d_s] (input-major)")
+    d_s = w_in.shape[0]
+    if w_in.shape[1] != d_m:
+        raise ValueError(f"w_in is {tuple(w_in.shape)}, expected [d_s, {d_m}] (nn.Linear layout)")
     q = torch.empty(R, d_s, dtype=torch.float32, device=dev)
     gate = torch.empty(R, dtype=torch.float32, device=dev) if gate_w is not None else None
     rstd = torch.empty(R, dtype=torch.float32, device=dev)
@@ -124,7 +123,7 @@ def project_out(r: torch.Tensor, w_out: torch.Tensor, h2: torch.Tensor, *, b_out
                 h_out: Optional[torch.Tensor] = None, want_rel: bool = False):
     """(delta | None, h_out | None, rel | None).
 
-    d = scale * gate * (r @ w_out + b_out), w_out input-major [d_s, d_m]; optional LayerSelector matched norm
+    d = scale * gate * (r @ w_out^T + b_out), w_out [d_m, d_s] (nn.Linear); optional LayerSelector matched norm
     with per-row weight sel_w;
     d *= pos_mask; delta = d in h2's dtype; h_out = h2 + delta; rel = ||delta|| / (||h2|| + 1e-6)."""
     dev = _cuda("project_out", r, w_out, h2, b_out, gate, sel_w, pos_mask, h_out)
@@ -132,8 +131,8 @@ def project_out(r: torch.Tensor, w_out: torch.Tensor, h2: torch.Tensor, *, b_out
     w_out = _f32(w_out, "w_out")
     h2 = h2.contiguous()
     R, d_s = r.shape
-    d_m = w_out.shape[1]
-    if w_out.shape[0] != d_s or h2.shape != (R, d_m):
+    d_m = w_out.shape[0]
+    if w_out.shape[1] != d_s or h2.shape != (R, d_m):
         raise ValueError(f"project_out: r {tuple(r.shape)}, w_out {tuple(w_out.shape)}, h {tuple(h2.shape)}")
     delta = torch.empty_like(h2) if want_delta else None
     if h_out is not None and (h_out.shape != h2.shape or h_out.dtype != h2.dtype or not h_out.is_contiguous()):

@@ -53,8 +53,8 @@ def test_read_path_matches_reference(dev, name, slot_dtype):
     assert rel_err(pages.S[0], c["S"]) < 1e-5
     h = torch.from_numpy(c["h"]).to(dev)
     h2 = h.reshape(-1, h.shape[-1])
-    W_in = torch.from_numpy(c["W_in"]).contiguous().to(dev)    # [d_m, d_s], input-major
-    W_out = torch.from_numpy(c["W_out"]).contiguous().to(dev)  # [d_s, d_m]
+    W_in = torch.from_numpy(c["W_in"]).t().contiguous().to(dev)    # nn.Linear layout [d_s, d_m]
+    W_out = torch.from_numpy(c["W_out"]).t().contiguous().to(dev)  # [d_m, d_s]
     q, _, _, _ = ops.project_in(h2, W_in)
     assert rel_err(q, c["q"].reshape(q.shape)) < 1e-4
     R = q.shape[0]
@@ -140,7 +140,7 @@ def test_batched_documents_match_reference(dev):
     nv = torch.from_numpy(c["n_valid"].astype(np.int32)).to(dev)
     pages = ops.Pages(slots=slots, page_of=page_of, n_valid=nv, S=ops.summaries(slots, page_of, nv))
     h = torch.from_numpy(c["h"]).to(dev).reshape(B, -1)
-    q, _, _, _ = ops.project_in(h, torch.from_numpy(c["W_in"]).contiguous().to(dev))
+    q, _, _, _ = ops.project_in(h, torch.from_numpy(c["W_in"]).t().contiguous().to(dev))
     idx, wk, w, _ = ops.route(q, pages.S, rows_per_lib=1, top_k=2, route_temp=10.0)
     assert topk_sets(w) == topk_sets(c["w"].reshape(B, C))
     r = ops.read_decode(q, pages, idx, wk, rows_per_lib=1)
@@ -188,14 +188,12 @@ def test_projections_with_gate_selector_mask(dev, hdt):
     hn = X.rms_norm(hf)
     q_ref = X.query(hn, W_in.t().numpy(), b_in.numpy())
     g_ref = X.gate(hn, gate_w.numpy(), 0.25)[:, 0]
-    q, gate, rstd, _ = ops.project_in(h.to(dev), W_in.t().contiguous().to(dev), b_in.to(dev), gate_w=gate_w.to(dev),
-                                      gate_b=0.25)
+    q, gate, rstd, _ = ops.project_in(h.to(dev), W_in.to(dev), b_in.to(dev), gate_w=gate_w.to(dev), gate_b=0.25)
     assert rel_err(q, q_ref) < 1e-4 and rel_err(gate, g_ref) < 1e-5
     d = 0.7 * g_ref[:, None] * (r.numpy() @ W_out.t().numpy() + b_out.numpy())
     d = X.selector_apply(d, hf, sel_col.numpy(), -2.0) * pm.numpy()[:, None]
     d_h = torch.from_numpy(d.astype(np.float32)).to(hdt)
-    delta, h_new, rel = ops.project_out(r.to(dev), W_out.t().contiguous().to(dev), h.to(dev), b_out=b_out.to(dev),
-                                        scale=0.7,
+    delta, h_new, rel = ops.project_out(r.to(dev), W_out.to(dev), h.to(dev), b_out=b_out.to(dev), scale=0.7,
                                         gate=gate, sel_w=sel_col.to(dev), log_alpha=-2.0, pos_mask=pm.to(dev),
                                         want_delta=True, h_out=torch.empty_like(h.to(dev)), want_rel=True)
     assert delta.dtype == hdt and h_new.dtype == hdt
@@ -206,13 +204,29 @@ def test_projections_with_gate_selector_mask(dev, hdt):
     _status_clean(dev)
 
 
+@pytest.mark.parametrize("shape", [(64, 4096, 2048), (200, 520, 264), (7, 96, 16), (130, 30, 44), (64, 2048, 4096)])
+@pytest.mark.parametrize("hdt", [torch.float32, torch.bfloat16])
+def test_projection_gemm_fp32_faithful(dev, shape, hdt):
+    """The projection GEMM (tensor-core 3xTF32 when d_in % 4 == 0, CUDA-core fallback otherwise) against a
+    float64 product: relative error well inside float32-level accuracy (1e-5 of the largest entry)."""
+    from kv_skill_v2_b200 import ops
+    M, K, N = shape
+    g = torch.Generator().manual_seed(M + K + N)
+    h = torch.randn(M, K, generator=g).to(hdt)
+    W = torch.randn(N, K, generator=g) * 0.05
+    y, _, _, _ = ops.project_in(h.to(dev), W.to(dev), rms=False, l2=False)
+    ref = h.double() @ W.double().t()
+    assert rel_err(y, ref) < 1e-5, shape
+    _status_clean(dev)
+
+
 def test_low_rank_query_two_calls(dev):
     from kv_skill_v2_b200 import ops
     g = torch.Generator().manual_seed(8)
     h = torch.randn(9, 96, generator=g)
     A1, A2 = torch.randn(16, 96, generator=g) * 0.1, torch.randn(48, 16, generator=g) * 0.1
-    t, _, _, _ = ops.project_in(h.to(dev), A1.t().contiguous().to(dev), rms=True, l2=False)
-    q, _, _, _ = ops.project_in(t, A2.t().contiguous().to(dev), rms=False, l2=True)
+    t, _, _, _ = ops.project_in(h.to(dev), A1.to(dev), rms=True, l2=False)
+    q, _, _, _ = ops.project_in(t, A2.to(dev), rms=False, l2=True)
     ref = X.l2(X.rms_norm(h.numpy()) @ A1.t().numpy() @ A2.t().numpy())
     assert rel_err(q, ref) < 1e-4
 
@@ -376,10 +390,10 @@ def test_config2_sample_matches_oracle(dev):
     slots, nv, page_of, h, W_in, W_out = _cfg2_sample(dev, n_docs=6)
     S = ops.summaries(slots, page_of, nv)
     pages = ops.Pages(slots=slots, page_of=page_of, n_valid=nv, S=S)
-    q, _, _, _ = ops.project_in(h, W_in.t().contiguous())
+    q, _, _, _ = ops.project_in(h, W_in)
     idx, wk, w, _ = ops.route(q, S, rows_per_lib=1, top_k=4, route_temp=10.0)
     r = ops.read_decode(q, pages, idx, wk, rows_per_lib=1)
-    delta, _, _ = ops.project_out(r, W_out.t().contiguous(), h)
+    delta, _, _ = ops.project_out(r, W_out, h)
     for b in range(h.shape[0]):
         K = slots[b * 64:(b + 1) * 64].float().cpu().numpy()
         M = np.arange(K.shape[1])[None, :] < nv[b].cpu().numpy()[:, None]
@@ -400,7 +414,7 @@ def test_config2_properties(dev):
     slots, nv, page_of, h, W_in, _ = _cfg2_sample(dev, n_docs=64, seed=1)
     S = ops.summaries(slots, page_of, nv)
     pages = ops.Pages(slots=slots, page_of=page_of, n_valid=nv, S=S)
-    q, _, _, _ = ops.project_in(h, W_in.t().contiguous())
+    q, _, _, _ = ops.project_in(h, W_in)
     idx, wk, w, _ = ops.route(q, S, rows_per_lib=1, top_k=4, route_temp=10.0)
     assert ((w > 0).sum(-1) == 4).all() and torch.allclose(w.sum(-1), torch.ones(64, device=dev), atol=1e-5)
     r = ops.read_decode(q, pages, idx, wk, rows_per_lib=1)
