@@ -52,6 +52,12 @@ def parse_args(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-only", action="store_true", help="only the read kernel loop (for profilers)")
+    ap.add_argument("--no-sharded", action="store_true", help="skip the config-5 sharded read")
+    ap.add_argument("--sharded-only", action="store_true",
+                    help="only the config-5 sharded read; print its object as the line (for profilers)")
+    ap.add_argument("--no-selector", action="store_true", help="skip the config-4 multi-depth selector decode")
+    ap.add_argument("--selector-only", action="store_true",
+                    help="only the config-4 selector decode; print its object as the line (for profilers)")
     return ap.parse_args(argv)
 
 
@@ -230,11 +236,238 @@ def build_workload(torch, dev, docs: int, seed: int):
     return pages, W_in, W_out, g
 
 
+CFG5 = dict(C=2048, N=512, d_s=2560, d_m=5120, T=8, read_temp=12.0, route_temp=10.0)
+
+
+def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int, flush, stream) -> dict:
+    """one Library of 2048 chunks x 512 fp16 slots (1,048,576 slots, d_s 2560), 8 query tokens,
+    every chunk read (top_k 0); the chunks sharded evenly over the ranks, the partials exchanged by one NCCL
+    all-gather per step and merged. Strong scaling: the whole Library is the same at every N.
+
+    A step: q = project_in(h) (replicated interface weights), the rank's partial (route_lse + read_multi over its
+    chunks), all-gather of the partial blocks, shard merge, output projection + residual. The local parts run
+    as two CUDA graphs around the eager all-gather. Timed with CUDA events per step, max over ranks."""
+    from kv_skill_v2_b200 import _native, ops
+    from kv_skill_v2_b200.shard import ShardedRead, partition_chunks
+
+    C, N, d_s, d_m, T = CFG5["C"], CFG5["N"], CFG5["d_s"], CFG5["d_m"], CFG5["T"]
+    lo, hi = partition_chunks(C, world)[rank]
+    Cl = hi - lo
+    g = torch.Generator(device=dev).manual_seed(5000 + lo)
+    slots = torch.empty(Cl, N, d_s, dtype=torch.float16, device=dev)
+    for c0 in range(0, Cl, 64):
+        x = torch.randn(min(64, Cl - c0), N, d_s, generator=g, device=dev)
+        slots[c0:c0 + x.shape[0]] = (x / x.norm(dim=-1, keepdim=True)).half()
+        del x
+    page_of = torch.arange(Cl, dtype=torch.int32, device=dev).view(1, Cl)
+    nv = torch.full((1, Cl), N, dtype=torch.int32, device=dev)
+    pages = ops.Pages(slots=slots, page_of=page_of, n_valid=nv, S=ops.summaries(slots, page_of, nv))
+    gw = torch.Generator(device=dev).manual_seed(55)  # the same interface and tokens on every rank
+    W_in = torch.randn(d_s, d_m, generator=gw, device=dev) * 0.02
+    W_out = torch.randn(d_m, d_s, generator=gw, device=dev) * 0.02
+    hs = torch.randn(warmup + steps, T, d_m, generator=gw, device=dev)
+    h = hs[0].clone()
+    h_out = torch.empty_like(h)
+    sr = ShardedRead(pages, T, rows_per_lib=T)
+
+    def pre():
+        q, _, _, _ = ops.project_in(h, W_in)
+        sr.partial(q)
+
+    def post():
+        r = sr.merge()
+        ops.project_out(r, W_out, h, want_delta=False, h_out=h_out)
+
+    for _ in range(2):
+        pre(); sr.exchange(); post()
+    torch.cuda.synchronize(dev)
+    g_pre, g_post = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    n0 = _native.launch_count()
+    with torch.cuda.graph(g_pre):
+        pre()
+    with torch.cuda.graph(g_post):
+        post()
+    kernels = _native.launch_count() - n0
+    torch.cuda.synchronize(dev)
+
+    def step(i):
+        h.copy_(hs[i])
+        g_pre.replay()
+        sr.exchange()
+        g_post.replay()
+
+    for i in range(warmup):
+        flush.fill_(i & 0xFF)
+        step(i)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        flush.fill_(i & 0xFF)
+        ev[i][0].record(stream)
+        step(warmup + i)
+        ev[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    t_ms = sum(a.elapsed_time(b) for a, b in ev)
+    t_max = t_ms
+    if world > 1:
+        t = torch.tensor([t_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_max = float(t.item())
+    # the read alone on this rank (route_lse + read_multi), for the roofline
+    g_read = torch.cuda.CUDAGraph()
+    q_s, _, _, _ = ops.project_in(h, W_in)
+    with torch.cuda.graph(g_read):
+        sr.partial(q_s)
+    evr = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(max(steps, 20))]
+    for i in range(3):
+        flush.fill_(i)
+        g_read.replay()
+    for i in range(len(evr)):
+        flush.fill_(i & 0xFF)
+        evr[i][0].record(stream)
+        g_read.replay()
+        evr[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    t_read = statistics.mean(a.elapsed_time(b) for a, b in evr) / 1000.0
+    read_bytes = Cl * N * d_s * 2 + Cl * d_s * 4 + 2 * T * d_s * 4
+    step_bytes = read_bytes + 2 * d_s * d_m * 4 + 2 * T * d_m * 4
+    peak, peak_kind = hbm_peak()
+    ms = t_max / steps
+    del g_pre, g_post, g_read
+    return {"workload": "BASELINE config 5: one Library of 2048 chunks x 512 fp16 slots (1,048,576 slots), d_s 2560, "
+                        "d_m 5120, 8 query tokens, dense read of every chunk; chunks sharded evenly over the GPUs, "
+                        "partials (max, sum, acc) merged after one NCCL all-gather per step",
+            "metric": "sharded Library-read tokens/s (whole job)", "value": T * steps / (t_max / 1000.0),
+            "unit": "tokens/s", "n_gpus": world, "ms_per_step": ms, "scaling": "strong",
+            "chunks_per_gpu": Cl, "kernels_per_step": kernels, "gpu_launches": kernels * steps,
+            "step_bytes_per_gpu": step_bytes, "step_hbm_gbs_per_gpu": step_bytes / (ms / 1000.0) / 1e9,
+            "roofline": {"bound": "hbm", "kernel": "route_lse + read_multi_mma_kernel + read_multi_merge_kernel",
+                         "achieved": read_bytes / t_read / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": read_bytes / t_read / 1e9 / peak, "algorithmic_bytes_per_launch": read_bytes,
+                         "launch_us": t_read * 1e6, "peak_source": peak_kind},
+            "l2": "flushed between steps (256 MiB write); the slot shard alone is > L2 at every N <= 8"}
+
+
+CFG4 = dict(docs=32, L=8, C=32, N=512, d_s=2048, d_m=5120, sel_k=2, top_k=4, read_temp=12.0, route_temp=10.0)
+
+
+def run_selector(torch, dist, dev, world: int, rank: int, steps: int, warmup: int, flush, stream) -> dict:
+    """32 documents per GPU, each with 8 candidate depths (a Library of 32 chunks x 512 fp16
+    slots per depth, d_s 2048), d_m 5120, one query token per document; the LayerSelector keeps the top-2 depths
+    per token from given logits z ~ N(0,1) and routing keeps the top-4 chunks within each selected depth.
+
+    A step is the LibraryInjector's work at the 8 hooked layers for one token per document: selector weights,
+    then per layer the fused input projection, routing with the selector's row mask (tokens that dropped this
+    depth read nothing), the decode read and the output projection with the selector's matched-norm rescale and
+    the residual. Weak scaling: every rank its own 32 documents."""
+    from kv_skill_v2_b200 import LayerSelector, LibraryInjector, LinearInterface, PagedLibrary, _native, ops
+
+    B, L, C, N, d_s, d_m = CFG4["docs"], CFG4["L"], CFG4["C"], CFG4["N"], CFG4["d_s"], CFG4["d_m"]
+    g = torch.Generator(device=dev).manual_seed(4000 + rank)
+    layers = list(range(L))
+    po = torch.arange(B * C, dtype=torch.int32, device=dev).view(B, C)
+    nv = torch.full((B, C), N, dtype=torch.int32, device=dev)
+    slots = {}
+    for li in layers:
+        pool = torch.empty(B * C, N, d_s, dtype=torch.float16, device=dev)
+        for c0 in range(0, B * C, 128):
+            x = torch.randn(min(128, B * C - c0), N, d_s, generator=g, device=dev)
+            pool[c0:c0 + x.shape[0]] = (x / x.norm(dim=-1, keepdim=True)).half()
+            del x
+        slots[li] = pool
+    plib = PagedLibrary.from_pool(slots, po, nv)
+    W_in = torch.randn(d_m, d_s, generator=g, device=dev) * 0.02
+    W_out = torch.randn(d_s, d_m, generator=g, device=dev) * 0.02
+    itf = LinearInterface(W_in, W_out, layers).to(dev).requires_grad_(False)
+    sel = LayerSelector(d_m, layers, k=CFG4["sel_k"]).to(dev).requires_grad_(False)
+
+    class Reader(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.layers = torch.nn.ModuleList([torch.nn.Identity() for _ in range(L)])
+            self._p = torch.nn.Parameter(torch.zeros(1, device=dev), requires_grad=False)
+
+        def forward(self, x):
+            for blk in self.layers:
+                x = blk(x)
+            return x
+
+    reader = Reader()
+    inj = LibraryInjector(reader, itf, top_k=CFG4["top_k"], read_temp=CFG4["read_temp"],
+                          route_temp=CFG4["route_temp"], selector=sel)
+    inj.load_library(plib)
+    hs = torch.randn(warmup + steps, B, 1, d_m, generator=g, device=dev)
+    zs = torch.randn(warmup + steps, B, 1, L, generator=g, device=dev)
+    h_in, z_in = hs[0].clone(), zs[0].clone()
+    h_out = torch.empty_like(h_in)
+
+    def step():
+        sel.set_logits(z_in)
+        h = h_in
+        for li in layers:
+            h, _ = inj._inject(h, li)
+        h_out.copy_(h)
+
+    with torch.inference_mode():
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        n0 = _native.launch_count()
+        with torch.cuda.graph(graph):
+            step()
+        kernels = _native.launch_count() - n0
+        torch.cuda.synchronize(dev)
+        for i in range(warmup):
+            h_in.copy_(hs[i]); z_in.copy_(zs[i])
+            flush.fill_(i & 0xFF)
+            graph.replay()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for i in range(steps):
+            h_in.copy_(hs[warmup + i]); z_in.copy_(zs[warmup + i])
+            flush.fill_(i & 0xFF)
+            ev[i][0].record(stream)
+            graph.replay()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+        sel_rows = int((sel.weights() > 0).sum().item())  # (token, depth) reads of the last step
+    t_ms = sum(a.elapsed_time(b) for a, b in ev)
+    t_max = t_ms
+    if world > 1:
+        t = torch.tensor([t_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_max = float(t.item())
+    ms = t_max / steps
+    # algorithmic bytes of a step: the routed chunks of the selected depths (full chunks here), their summary
+    # keys, the interface weights once, hidden in and out
+    step_bytes = sel_rows * (CFG4["top_k"] * N * d_s * 2 + C * d_s * 4) + 2 * d_s * d_m * 4 + 2 * B * d_m * 4
+    peak, peak_kind = hbm_peak()
+    inj.detach()
+    del graph
+    return {"workload": "BASELINE config 4: 32 documents x 8 candidate depths (32 chunks x 512 fp16 slots each, "
+                        "d_s 2048), d_m 5120, LayerSelector top-2 depths from given logits ~ N(0,1), top-4 chunks "
+                        "per selected depth, 1 token per document per step",
+            "metric": "multi-depth Library-read decode tokens/s (whole job)",
+            "value": B * world * steps / (t_max / 1000.0), "unit": "tokens/s", "n_gpus": world, "ms_per_step": ms,
+            "scaling": "weak", "kernels_per_step": kernels, "gpu_launches": kernels * steps,
+            "depth_reads_per_step": sel_rows,
+            "roofline": {"bound": "hbm", "kernel": "whole step (8 hooked layers)",
+                         "achieved": step_bytes / (ms / 1000.0) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": step_bytes / (ms / 1000.0) / 1e9 / peak, "algorithmic_bytes_per_step": step_bytes,
+                         "peak_source": peak_kind},
+            "l2": "flushed between steps (256 MiB write)"}
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
 
-    from kv_skill_v2_b200 import LibraryInjector, LinearInterface, PagedLibrary, ops
+    from kv_skill_v2_b200 import LibraryInjector, LinearInterface, PagedLibrary, _native, ops
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -246,6 +479,18 @@ def run_ours(args) -> None:
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    if args.sharded_only or args.selector_only:
+        flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        fn = run_sharded if args.sharded_only else run_selector
+        res = fn(torch, dist, dev, world, rank, args.steps, args.warmup, flush, torch.cuda.current_stream(dev))
+        res["device_status"] = ops.device_status(dev)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        return
 
     docs, d_m = args.docs, CFG["d_m"]
     pages, W_in, W_out, g = build_workload(torch, dev, docs, rank)
@@ -262,8 +507,6 @@ def run_ours(args) -> None:
         _, _, rel = ops.project_out(r, W_out, h, want_delta=False, h_out=h_out, want_rel=True)
         return q, idx, wk, rel
 
-    kernels_per_step = 8  # gemm+finish (in), logits+topk, read+merge, gemm+finish (out)
-
     # ---- graph capture of one step on static buffers
     h_static = hs[0].clone()
     h_out = torch.empty_like(h_static)
@@ -271,9 +514,11 @@ def run_ours(args) -> None:
         step(h_static, h_out)
     torch.cuda.synchronize(dev)
     graph = torch.cuda.CUDAGraph()
+    n0 = _native.launch_count()
     with torch.cuda.graph(graph):
         q_s, idx_s, wk_s, rel_s = step(h_static, h_out)
     torch.cuda.synchronize(dev)
+    kernels_per_step = _native.launch_count() - n0  # libxencb kernels in the captured step; a replay re-issues them
 
     bus = None
     try:
@@ -284,10 +529,17 @@ def run_ours(args) -> None:
     sampler = ClockSampler(bus)
     with sampler:
         if args.kernel_only:
+            # profiling mode: replays only; prints the slot rows each replay's read streamed, so that an ncu
+            # capture of replay i can be set against its algorithmic bytes
+            rows = []
             for i in range(args.warmup + args.steps):
                 h_static.copy_(hs[i])
                 graph.replay()
+                rows.append(int(pages.n_valid.gather(1, idx_s.long().clamp_min(0)).sum().item()))
             torch.cuda.synchronize(dev)
+            if rank == 0:
+                print(json.dumps({"kernel_only": True, "docs": docs, "d_s": CFG["d_s"], "kernels_per_step": kernels_per_step,
+                                  "slot_rows_per_replay": rows}), flush=True)
             return
         # ---- value: graph replays, events per step, L2 flush + next input between steps
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -380,6 +632,11 @@ def run_ours(args) -> None:
             t_e2e = float(t.item())
         e2e = R * args.steps * world / (t_e2e / 1000.0)
         inj.detach()
+        sharded = selector = None
+        if not args.no_sharded:
+            sharded = run_sharded(torch, dist, dev, world, rank, args.steps, args.warmup, flush, stream)
+        if not args.no_selector:
+            selector = run_selector(torch, dist, dev, world, rank, args.steps, args.warmup, flush, stream)
     status = ops.device_status(dev)
     clocks = sampler.summary()
 
@@ -407,6 +664,8 @@ def run_ours(args) -> None:
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": R * d_m * 4, "d2h_bytes_per_step": R * d_m * 4,
                     "path": "LibraryInjector forward hook on a reader block, PagedLibrary of 64 documents"},
             "gpu_launches": kernels_per_step * args.steps,
+            "sharded": sharded,
+            "selector": selector,
             "clocks": clocks, "device_status": status}
     print(json.dumps(line), flush=True)
 

@@ -58,6 +58,10 @@ extern "C" {
 XENCB_API int xencb_abi_version(void);
 XENCB_API const char* xencb_last_error(void);
 
+/* Kernels launched (or captured into a CUDA graph) through this library in this process so far. No counterpart
+ * in the reference: a diagnostic that lets a caller count the device work one call issues. */
+XENCB_API unsigned long long xencb_launch_count(void);
+
 /* Synchronises `stream`, returns the device status bits of the current device and clears them if `clear`. */
 XENCB_API int xencb_device_status(void* stream, int clear, unsigned int* status_out);
 
@@ -70,7 +74,9 @@ XENCB_API int xencb_device_status(void* stream, int clear, unsigned int* status_
  *            XENCB_PIN_RMS into a float32 [n_rows, rank] buffer, then one with XENCB_PIN_L2 over it.
  *   h        [n_rows, d_m] of h_dtype (the reference upcasts h to float32 first; so does this)
  *   w_in     [d_s, d_m] float32; b_in [d_s] or NULL; d_s % 4 == 0
- *   gate_w   [d_m] or NULL (then gate_out is not written); gate_b the scalar gate_b[pos[li]]
+ *   gate_w   [d_m] or NULL (then gate_out is not written); gate_b the scalar gate_b[pos[li]], or gate_b_dev a
+ *            device pointer to it (when non-NULL it replaces gate_b: no host read of the parameter, so the call
+ *            can be captured in a CUDA graph)
  *   sel_w    [n_cand, d_m] or NULL: LayerSelector logits z = hn @ sel_w^T + sel_b (xenc/selector.py:69-74)
  *   q_out    [n_rows, d_s] float32; gate_out [n_rows] or NULL; rstd_out [n_rows] or NULL (1/rms)
  *   z_out    [n_rows, n_cand] or NULL
@@ -80,7 +86,7 @@ XENCB_API int xencb_device_status(void* stream, int clear, unsigned int* status_
 XENCB_API size_t xencb_project_in_workspace(int64_t n_rows, int d_m, int d_s);
 XENCB_API int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const float* w_in,
                                const float* b_in, int d_s, int flags, const float* gate_w, float gate_b,
-                               const float* sel_w, const float* sel_b, int n_cand, float rms_eps, float* q_out,
+                               const float* gate_b_dev, const float* sel_w, const float* sel_b, int n_cand, float rms_eps, float* q_out,
                                float* gate_out, float* rstd_out, float* z_out, void* workspace,
                                size_t workspace_bytes, void* stream);
 
@@ -97,11 +103,13 @@ XENCB_API int xencb_rms_norm(const void* h, int h_dtype, int64_t n_rows, int d_m
  * Outputs: idx [n_rows, k_out] chunk ids sorted by (logit desc, index asc), -1 padded; wk [n_rows, k_out]
  * their weights (0 padded); w_dense [n_rows, C] the reference's w (zeros off the kept set) or NULL;
  * logit_out [n_rows, C] raw logits or NULL. k_out = xencb_route_k(top_k, C).
- * n_chunks_of may be NULL (every Library has C chunks). */
+ * n_chunks_of may be NULL (every Library has C chunks). row_w [n_rows] may be NULL; a row with row_w == 0 (a
+ * token whose LayerSelector weight for this layer is 0, xenc/selector.py:59-67, 106-110) gets idx -1 and wk 0,
+ * so the read skips it, while its w_dense still holds the routing the reference reports. */
 XENCB_API int xencb_route_k(int top_k, int n_chunks);
 XENCB_API int xencb_route(const float* q, int64_t n_rows, int d_s, const float* S, int n_chunks, const int32_t* n_chunks_of,
-                int64_t rows_per_lib, int64_t n_lib, float route_temp, int top_k, int32_t* idx, float* wk,
-                float* w_dense, float* logit_out, void* stream);
+                int64_t rows_per_lib, int64_t n_lib, float route_temp, int top_k, const float* row_w,
+                int32_t* idx, float* wk, float* w_dense, float* logit_out, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------
  * Masked decode read over the routed chunks. Replaces the read of LibraryInjector._branch
@@ -138,12 +146,44 @@ XENCB_API int xencb_read_decode_noalloc(const float* q, int64_t n_rows, int d_s,
                                         const int32_t* idx, const float* wk, int k, float read_temp,
                                         int read_softmax, float* r_out, void* stream);
 
+/* Many-query read over whole chunks (xenc/injector.py:239-265 with T > 1 query tokens per Library, the dense read
+ * of BASELINE config 5): r[row] = sum_c w[row, c] * read(q[row], chunk c) with w [n_rows, n_chunks] float32 given
+ * per (row, chunk) -- the routing softmax (dense or top-k with zeros), or unnormalised weights for a shard partial
+ * (xencb_route_lse). Up to 8 query rows of a Library share every slot row read from HBM. Slots must be f16 or bf16
+ * and d_s a multiple of 16 (<= 2560); other shapes return XENCB_ENOTSUP (use xencb_read_decode). Libraries,
+ * pages and rows_per_lib as in xencb_read_decode; n_chunks_of [n_lib] may be NULL (all Libraries have
+ * n_chunks chunks). Workspace: xencb_read_multi_workspace bytes, 256-byte aligned. */
+XENCB_API size_t xencb_read_multi_workspace(int64_t n_rows, int64_t rows_per_lib, int n_chunks, int d_s, int page_rows,
+                                            int slots_dtype);
+XENCB_API int xencb_read_multi(const float* q, int64_t n_rows, int d_s, const void* slots, int slots_dtype,
+                               int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of,
+                               const int32_t* n_valid, int n_chunks, const int32_t* n_chunks_of, int64_t rows_per_lib,
+                               int64_t n_lib, const float* w, float read_temp, int read_softmax, float* r_out,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* Dense routing of one chunk shard of a Library (the routing softmax of xenc/injector.py:220-229 with top_k = 0,
+ * regrouped by shard): w_out [n_rows, n_chunks] = e^(l_c - max_c l_c) with l = route_temp * q . S_c, and
+ * header_out [n_rows, 4] = (max_c l_c, sum_c e^(l_c - max), 0, 0). Feeding w_out to xencb_read_multi gives the
+ * shard's accumulator A = sum_c e^(l_c - max) r_c; (header, A) is the shard's partial. */
+XENCB_API int xencb_route_lse(const float* q, int64_t n_rows, int d_s, const float* S, int n_chunks,
+                              const int32_t* n_chunks_of, int64_t rows_per_lib, int64_t n_lib, float route_temp,
+                              float* w_out, float* header_out, void* stream);
+
+/* Combines the partials of n_shards chunk shards into the read of the whole Library:
+ * parts [n_shards][n_rows * 4 + n_rows * d_s] holds per shard the headers of xencb_route_lse then the
+ * accumulators of xencb_read_multi (the layout an all-gather of each shard's block produces);
+ * r = sum_g e^(max_g - M) A_g / sum_g e^(max_g - M) sum_g with M the largest max_g. */
+XENCB_API int xencb_shard_merge(const float* parts, int n_shards, int64_t n_rows, int d_s, float* r_out, void* stream);
+
 /* ---------------------------------------------------------------------------------------------------------
  * Output projection and injection epilogue. Replaces xenc/injector.py:266-267 (gain_scale * gain * gate *
  * itf_write(r), :74-77), LayerSelector.apply (xenc/selector.py:95-110) and the hook arithmetic
  * (xenc/injector.py:185-197: delta.to(h.dtype), position mask, mag term, h + delta):
  *   d        = scale * gate[row] * (r @ W_out^T + b_out)                 (gate NULL -> 1)
  *   if sel_w: d = sel_w[row] * exp(log_alpha) * d / (||d|| / (||h|| + 1e-6) + 1e-6)
+ *   log_scale_dev (device float or NULL): the scale is multiplied by exp(*log_scale_dev) (the interface's
+ *   log_gain[pos] read on the device); log_alpha_dev (device float or NULL) replaces log_alpha. Both keep the
+ *   call free of host reads of parameters, so it can be captured in a CUDA graph.
  *   d       *= pos_mask[row]                                              (pos_mask NULL -> 1)
  *   delta_out = d in h_dtype (or NULL); h_out = h + delta_out in h_dtype (or NULL; may alias h);
  *   rel_out[row] = ||delta_out|| / (||h|| + 1e-6)                         (or NULL)
@@ -151,7 +191,8 @@ XENCB_API int xencb_read_decode_noalloc(const float* q, int64_t n_rows, int d_s,
  *            d_m % 4 == 0. */
 XENCB_API size_t xencb_project_out_workspace(int64_t n_rows, int d_s, int d_m);
 XENCB_API int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_out, const float* b_out, int d_m,
-                      float scale, const float* gate, const float* sel_w, float log_alpha, const float* pos_mask,
+                      float scale, const float* log_scale_dev, const float* gate, const float* sel_w, float log_alpha,
+                      const float* log_alpha_dev, const float* pos_mask,
                       const void* h, int h_dtype, void* delta_out, void* h_out, float* rel_out, void* workspace,
                       size_t workspace_bytes, void* stream);
 

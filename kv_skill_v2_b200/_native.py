@@ -27,20 +27,27 @@ _p, _i, _i64, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_
 SIGNATURES: dict = {
     "xencb_abi_version": (_i, []),
     "xencb_last_error": (ctypes.c_char_p, []),
+    "xencb_launch_count": (ctypes.c_ulonglong, []),
     "xencb_device_status": (_i, [_p, _i, ctypes.POINTER(ctypes.c_uint)]),
     "xencb_project_in_workspace": (_sz, [_i64, _i, _i]),
-    "xencb_project_in": (_i, [_p, _i, _i64, _i, _p, _p, _i, _i, _p, _f, _p, _p, _i, _f, _p, _p, _p, _p, _p, _sz,
-                              _p]),
+    "xencb_project_in": (_i, [_p, _i, _i64, _i, _p, _p, _i, _i, _p, _f, _p, _p, _p, _i, _f, _p, _p, _p, _p, _p,
+                              _sz, _p]),
     "xencb_rms_norm": (_i, [_p, _i, _i64, _i, _f, _p, _p]),
     "xencb_route_k": (_i, [_i, _i]),
-    "xencb_route": (_i, [_p, _i64, _i, _p, _i, _p, _i64, _i64, _f, _i, _p, _p, _p, _p, _p]),
+    "xencb_route": (_i, [_p, _i64, _i, _p, _i, _p, _i64, _i64, _f, _i, _p, _p, _p, _p, _p, _p]),
     "xencb_read_decode_workspace": (_sz, [_i64, _i, _i, _i, _i]),
     "xencb_read_decode": (_i, [_p, _i64, _i, _p, _i, _i64, _i64, _i, _p, _p, _i, _i64, _i64, _p, _p, _i, _f, _i,
                                _p, _p, _sz, _p]),
     "xencb_read_decode_noalloc": (_i, [_p, _i64, _i, _p, _i, _i64, _i64, _i, _p, _p, _i, _i64, _i64, _p, _p, _i,
                                        _f, _i, _p, _p]),
+    "xencb_read_multi_workspace": (_sz, [_i64, _i64, _i, _i, _i, _i]),
+    "xencb_read_multi": (_i, [_p, _i64, _i, _p, _i, _i64, _i64, _i, _p, _p, _i, _p, _i64, _i64, _p, _f, _i, _p, _p,
+                              _sz, _p]),
+    "xencb_route_lse": (_i, [_p, _i64, _i, _p, _i, _p, _i64, _i64, _f, _p, _p, _p]),
+    "xencb_shard_merge": (_i, [_p, _i, _i64, _i, _p, _p]),
     "xencb_project_out_workspace": (_sz, [_i64, _i, _i]),
-    "xencb_project_out": (_i, [_p, _i64, _i, _p, _p, _i, _f, _p, _p, _f, _p, _p, _i, _p, _p, _p, _p, _sz, _p]),
+    "xencb_project_out": (_i, [_p, _i64, _i, _p, _p, _i, _f, _p, _p, _p, _f, _p, _p, _p, _i, _p, _p, _p, _p, _sz,
+                               _p]),
     "xencb_selector_weights": (_i, [_p, _i64, _i, _i, _i, _p, _p]),
     "xencb_selector_logits": (_i, [_p, _i, _i64, _i, _p, _p, _i, _i, _f, _p, _p]),
     "xencb_selector_apply": (_i, [_p, _i, _p, _i, _i64, _i, _p, _i, _i, _f, _p, _p]),
@@ -100,3 +107,8 @@ def call(name: str, *args) -> int:
 
 def exported_symbols() -> list:
     return sorted(SIGNATURES)
+
+
+def launch_count() -> int:
+    """Kernels launched (or captured into a CUDA graph) by libxencb.so in this process so far."""
+    return int(lib().xencb_launch_count())

@@ -201,7 +201,7 @@ constexpr int PIN_CHUNK = 1024;  // columns per reduce CTA (256 threads x 4)
 template <typename TH>
 __global__ void __launch_bounds__(256) project_in_reduce_kernel(
     const TH* __restrict__ h, int d_m, const float* __restrict__ part, int splits, int64_t M, int d_s, int flags,
-    const float* __restrict__ b_in, const float* __restrict__ gate_w, float gate_b,
+    const float* __restrict__ b_in, const float* __restrict__ gate_w, float gate_b, const float* __restrict__ gate_b_dev,
     const float* __restrict__ sel_w, const float* __restrict__ sel_b, int n_cand, float eps,
     float* __restrict__ q_out, float* __restrict__ nq_part, int* __restrict__ row_done, float* __restrict__ gate_out,
     float* __restrict__ rstd_out, float* __restrict__ z_out) {
@@ -222,7 +222,8 @@ __global__ void __launch_bounds__(256) project_in_reduce_kernel(
     if (rstd_out && threadIdx.x == 0) rstd_out[row] = (flags & XENCB_PIN_RMS) ? rstd : 1.f;
     if (gate_w) {
       gd = block_sum(gd, red);
-      if (threadIdx.x == 0) gate_out[row] = 1.f / (1.f + expf(-(gd * rstd + gate_b)));
+      const float gb = gate_b_dev ? __ldg(gate_b_dev) : gate_b;
+      if (threadIdx.x == 0) gate_out[row] = 1.f / (1.f + expf(-(gd * rstd + gb)));
     }
     if (sel_w) {
       const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -301,13 +302,14 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const TH* __restrict__ h,
 template <typename TH>
 __global__ void __launch_bounds__(256) project_out_reduce_kernel(
     const float* __restrict__ part, int splits, int64_t M, int d_m, const float* __restrict__ b_out, float scale,
-    const float* __restrict__ gate, const TH* __restrict__ h, float* __restrict__ d_out,
+    const float* __restrict__ log_scale_dev, const float* __restrict__ gate, const TH* __restrict__ h,
+    float* __restrict__ d_out,
     float* __restrict__ norm_part, int* __restrict__ row_done) {
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const int chunk = blockIdx.y;
   if (chunk == 0 && threadIdx.x == 0) row_done[row] = 0;  // the epilogue's per-row counter
-  const float g = (gate ? gate[row] : 1.f) * scale;
+  const float g = (gate ? gate[row] : 1.f) * scale * (log_scale_dev ? expf(__ldg(log_scale_dev)) : 1.f);
   float dd = 0.f, hh = 0.f;
   const int n = chunk * PIN_CHUNK + threadIdx.x * 4;
   if (n < d_m) {
@@ -333,7 +335,7 @@ __global__ void __launch_bounds__(256) project_out_reduce_kernel(
 template <typename TH>
 __global__ void __launch_bounds__(256) project_out_epilogue_kernel(
     const float* __restrict__ d_in, const float* __restrict__ norm_part, int d_m, const float* __restrict__ sel_w,
-    float alpha, const float* __restrict__ pos_mask, const TH* h, TH* delta_out, TH* h_out, float* __restrict__ rel_out,
+    float alpha_host, const float* __restrict__ log_alpha_dev, const float* __restrict__ pos_mask, const TH* h, TH* delta_out, TH* h_out, float* __restrict__ rel_out,
     float* __restrict__ cn_part, int* __restrict__ row_done) {
   __shared__ float red[32];
   __shared__ int last;
@@ -349,6 +351,7 @@ __global__ void __launch_bounds__(256) project_out_epilogue_kernel(
   const float rel_d = sqrtf(dd) / (hnorm + 1e-6f) + 1e-6f;
   const float sw = sel_w ? sel_w[row] : 1.f;
   const float pm = pos_mask ? pos_mask[row] : 1.f;
+  const float alpha = log_alpha_dev ? expf(__ldg(log_alpha_dev)) : alpha_host;
   float cn = 0.f;
   const int n = chunk * PIN_CHUNK + threadIdx.x * 4;
   if (n < d_m) {

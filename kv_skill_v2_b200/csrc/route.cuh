@@ -73,8 +73,8 @@ constexpr int TOPK_WARPS = 4;
 // One warp per row; dynamic smem: TOPK_WARPS * C floats.
 __global__ void __launch_bounds__(TOPK_WARPS * 32) route_topk_kernel(
     const float* __restrict__ logit, int64_t n_rows, int C, const int32_t* __restrict__ n_chunks_of,
-    int64_t rows_per_lib, int top_k, int k_out, int32_t* __restrict__ idx, float* __restrict__ wk,
-    float* __restrict__ w_dense) {
+    int64_t rows_per_lib, int top_k, int k_out, const float* __restrict__ row_w, int32_t* __restrict__ idx,
+    float* __restrict__ wk, float* __restrict__ w_dense) {
   extern __shared__ float sv_all[];
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * TOPK_WARPS + w;
@@ -101,6 +101,10 @@ __global__ void __launch_bounds__(TOPK_WARPS * 32) route_topk_kernel(
     }
     if (w_dense)
       for (int c = lane; c < C; c += 32) w_dense[row * C + c] = c < nc ? expf(v[c] - mx) / sum : 0.f;
+    if (row_w && row_w[row] == 0.f) {  // a row whose weight is 0 reads nothing; w_dense keeps its routing
+      __syncwarp();
+      for (int j = lane; j < k_out; j += 32) { ir[j] = -1; wr[j] = 0.f; }
+    }
     return;
   }
   // sparse: top_k rounds of arg-max, the winner's slot is then retired to -inf
@@ -145,6 +149,39 @@ __global__ void __launch_bounds__(TOPK_WARPS * 32) route_topk_kernel(
       const int c = ir[j];
       if (c >= 0) w_dense[row * C + c] = wr[j];
     }
+  }
+  if (row_w && row_w[row] == 0.f) {  // a row whose weight is 0 reads nothing; w_dense keeps its routing
+    __syncwarp();
+    for (int j = lane; j < k_out; j += 32) { ir[j] = -1; wr[j] = 0.f; }
+  }
+}
+
+// Dense routing of a chunk shard, left unnormalised so that shards combine exactly: one warp per row turns the
+// row's logits l_c (in w, overwritten in place) into e^(l_c - max) and writes the header (max, sum, 0, 0) at
+// header[4 * row]. Chunks at or past the row's Library chunk count get weight 0; a row without chunks gets
+// (-inf, 0), which the shard merge skips.
+__global__ void __launch_bounds__(128) route_lse_kernel(float* __restrict__ w, int64_t n_rows, int C,
+                                                       const int32_t* __restrict__ n_chunks_of, int64_t rows_per_lib,
+                                                       float* __restrict__ header) {
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= n_rows) return;
+  const int64_t lib = row / rows_per_lib;
+  const int nc = n_chunks_of ? min(n_chunks_of[lib], C) : C;
+  float* wr = w + row * C;
+  float mx = -CUDART_INF_F;
+  for (int c = lane; c < nc; c += 32) mx = fmaxf(mx, wr[c]);
+  mx = warp_max(mx);
+  float sum = 0.f;
+  if (nc > 0)
+    for (int c = lane; c < nc; c += 32) sum += expf(wr[c] - mx);
+  sum = warp_sum(sum);
+  for (int c = lane; c < C; c += 32) wr[c] = c < nc ? expf(wr[c] - mx) : 0.f;
+  if (lane == 0) {
+    header[row * 4] = mx;
+    header[row * 4 + 1] = sum;
+    header[row * 4 + 2] = 0.f;
+    header[row * 4 + 3] = 0.f;
   }
 }
 

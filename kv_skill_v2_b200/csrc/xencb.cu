@@ -9,6 +9,7 @@
 #include <cstring>
 #include <cudaTypedefs.h>
 #include <unordered_map>
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <type_traits>
@@ -18,6 +19,7 @@
 #include "gemm_tc.cuh"
 #include "read_decode.cuh"
 #include "read_decode_mma.cuh"
+#include "read_multi.cuh"
 #include "route.cuh"
 
 // Scratch of xencb_read_decode_noalloc: a fixed device array, so that entry point never allocates.
@@ -42,11 +44,17 @@ int cuda_fail(cudaError_t e, const char* what) {
   return fail(XENCB_ECUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
 }
 
-#define XENCB_CHECK_LAUNCH(what)                         \
+// Kernels this library has launched (or captured into a graph) in this process; every launch site checks
+// its launch through XENCB_CHECK_LAUNCH_N, which also counts it.
+std::atomic<unsigned long long> g_launches{0};
+
+#define XENCB_CHECK_LAUNCH_N(what, n)                    \
   do {                                                   \
     cudaError_t e__ = cudaGetLastError();                \
     if (e__ != cudaSuccess) return cuda_fail(e__, what); \
+    g_launches.fetch_add((n), std::memory_order_relaxed); \
   } while (0)
+#define XENCB_CHECK_LAUNCH(what) XENCB_CHECK_LAUNCH_N(what, 1)
 
 constexpr int kMaxDev = 64;
 
@@ -353,6 +361,67 @@ int noalloc_scratch(void** out) {
   return XENCB_OK;
 }
 
+struct MultiPlan {
+  int tpw, ncw, threads, rps, row_bytes, row_stride, n_stage, grid, pieces, piece_rows, s_max, q_blocks;
+  bool split;
+  int64_t n_groups, units_per_group, n_units;
+  size_t smem, fold_bytes, finfo_bytes, open_bytes, oinfo_bytes;
+  size_t total() const { return fold_bytes + finfo_bytes + open_bytes + oinfo_bytes; }
+};
+
+int plan_multi(int64_t n_rows, int64_t rows_per_lib, int n_chunks, int d_s, int page_rows, int dtype, MultiPlan* p) {
+  DevInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  if (dtype != XENCB_F16 && dtype != XENCB_BF16)
+    return fail(XENCB_ENOTSUP, "read_multi: slots must be f16 or bf16 (f32 slots: use read_decode)");
+  if (d_s <= 0 || d_s % 16 != 0) return fail(XENCB_ENOTSUP, "read_multi: d_s=%d must be a multiple of 16", d_s);
+  p->tpw = d_s <= 2048 ? 8 : 16;
+  p->ncw = (d_s + 16 * p->tpw - 1) / (16 * p->tpw);
+  if (p->ncw > (p->tpw == 8 ? RM_MAX_WARPS : 10))
+    return fail(XENCB_ENOTSUP, "read_multi: d_s=%d above 2560 is not supported", d_s);
+  p->split = dtype == XENCB_BF16;
+  p->threads = 32 * (p->ncw + 1);
+  p->row_bytes = d_s * 2;
+  p->row_stride = p->row_bytes + 16;
+  int rps = 16;
+  while (rps < 64 && 2 * rps * p->row_stride <= 36864) rps *= 2;
+  p->rps = rps;
+  const int stage_bytes = (int)align_up((size_t)rps * p->row_stride, 128);
+  const size_t budget = (size_t)(di.max_smem_optin > 0 ? di.max_smem_optin : 232448) - 1024;
+  int n_stage = 8;
+  while (n_stage >= 2 && mq_smem_bytes(n_stage, stage_bytes, p->ncw, p->tpw, p->split) > budget) --n_stage;
+  if (n_stage < 2) return fail(XENCB_ENOTSUP, "read_multi: d_s=%d: two stages do not fit in shared memory", d_s);
+  p->n_stage = n_stage;
+  p->smem = mq_smem_bytes(n_stage, stage_bytes, p->ncw, p->tpw, p->split);
+  const int64_t libs_used = (n_rows + rows_per_lib - 1) / rows_per_lib;
+  const int64_t t_eff = rows_per_lib < n_rows ? rows_per_lib : n_rows;
+  p->q_blocks = (int)((t_eff + MQ - 1) / MQ);
+  p->n_groups = libs_used * p->q_blocks;
+  // pieces: cut chunks until every CTA has at least 32 units (load balance within 1/32), pieces >= 32 rows
+  int pieces = 1, piece_rows = page_rows;
+  while (p->n_groups * n_chunks * pieces < 32LL * di.sms && piece_rows > 32) {
+    pieces *= 2;
+    piece_rows = (int)align_up((size_t)((page_rows + pieces - 1) / pieces), 16);
+    if (piece_rows < 32) piece_rows = 32;
+    pieces = (page_rows + piece_rows - 1) / piece_rows;
+  }
+  p->pieces = pieces;
+  p->piece_rows = piece_rows;
+  p->units_per_group = (int64_t)n_chunks * pieces;
+  p->n_units = p->n_groups * p->units_per_group;
+  p->grid = (int)(p->n_units < di.sms ? p->n_units : di.sms);
+  if (p->grid < 1) p->grid = 1;
+  const int64_t lmax = (p->n_units + p->grid - 1) / p->grid;
+  p->s_max = (int)((lmax - 1 + p->units_per_group - 1) / p->units_per_group + 1);
+  p->fold_bytes = align_up((size_t)p->grid * p->s_max * MQ * d_s * sizeof(float), 256);
+  p->finfo_bytes = align_up((size_t)p->grid * p->s_max * sizeof(int64_t), 256);
+  p->open_bytes = align_up((size_t)p->grid * 2 * (MQ_OPEN + (size_t)MQ * d_s) * sizeof(float), 256);
+  p->oinfo_bytes = align_up((size_t)p->grid * 2 * sizeof(int64_t), 256);
+  return XENCB_OK;
+}
+
+
 }  // namespace
 }  // namespace xencb
 
@@ -363,6 +432,8 @@ extern "C" {
 int xencb_abi_version(void) { return XENCB_ABI_VERSION; }
 
 const char* xencb_last_error(void) { return g_err.c_str(); }
+
+unsigned long long xencb_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int xencb_device_status(void* stream, int clear, unsigned int* status_out) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -391,8 +462,8 @@ size_t xencb_project_in_workspace(int64_t n_rows, int d_m, int d_s) {
 }
 
 int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const float* w_in, const float* b_in,
-                     int d_s, int flags, const float* gate_w, float gate_b, const float* sel_w, const float* sel_b,
-                     int n_cand, float rms_eps, float* q_out, float* gate_out, float* rstd_out, float* z_out,
+                     int d_s, int flags, const float* gate_w, float gate_b, const float* gate_b_dev,
+                     const float* sel_w, const float* sel_b, int n_cand, float rms_eps, float* q_out, float* gate_out, float* rstd_out, float* z_out,
                      void* workspace, size_t workspace_bytes, void* stream) {
   if (flags & ~(XENCB_PIN_RMS | XENCB_PIN_L2)) return fail(XENCB_EINVAL, "project_in: unknown flags 0x%x", flags);
   if (!h || !w_in || !q_out) return fail(XENCB_EINVAL, "project_in: h, w_in and q_out are required");
@@ -431,7 +502,8 @@ int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const 
   if (rc) return rc;
 #define XENCB_PIN(T)                                                                                         \
   project_in_reduce_kernel<T><<<dim3((unsigned)n_rows, nch), 256, 0, st>>>(                                   \
-      static_cast<const T*>(h), d_m, part, gp.splits, n_rows, d_s, flags, b_in, gate_w, gate_b, sel_w, sel_b,    \
+      static_cast<const T*>(h), d_m, part, gp.splits, n_rows, d_s, flags, b_in, gate_w, gate_b, gate_b_dev,      \
+      sel_w, sel_b,                                                                                            \
       n_cand, rms_eps, q_out, nq_part, row_done, gate_out, rstd_out, z_out)
   switch (h_dtype) {
     case XENCB_F32: XENCB_PIN(float); break;
@@ -463,8 +535,8 @@ int xencb_rms_norm(const void* h, int h_dtype, int64_t n_rows, int d_m, float ep
 int xencb_route_k(int top_k, int n_chunks) { return (top_k > 0 && top_k < n_chunks) ? top_k : n_chunks; }
 
 int xencb_route(const float* q, int64_t n_rows, int d_s, const float* S, int n_chunks, const int32_t* n_chunks_of,
-                int64_t rows_per_lib, int64_t n_lib, float route_temp, int top_k, int32_t* idx, float* wk,
-                float* w_dense, float* logit_out, void* stream) {
+                int64_t rows_per_lib, int64_t n_lib, float route_temp, int top_k, const float* row_w, int32_t* idx,
+                float* wk, float* w_dense, float* logit_out, void* stream) {
   if (!q || !S || !idx || !wk) return fail(XENCB_EINVAL, "route: q, S, idx and wk are required");
   if (n_rows <= 0 || d_s <= 0 || n_chunks <= 0 || rows_per_lib <= 0 || n_lib <= 0)
     return fail(XENCB_EINVAL, "route: sizes must be positive (n_rows=%lld d_s=%d C=%d rows_per_lib=%lld n_lib=%lld)",
@@ -489,7 +561,7 @@ int xencb_route(const float* q, int64_t n_rows, int d_s, const float* S, int n_c
   if (rc) return rc;
   const int k_out = xencb_route_k(top_k, n_chunks);
   route_topk_kernel<<<(unsigned)((n_rows + TOPK_WARPS - 1) / TOPK_WARPS), TOPK_WARPS * 32, smem, st>>>(
-      lg, n_rows, n_chunks, n_chunks_of, rows_per_lib, top_k, k_out, idx, wk, w_dense);
+      lg, n_rows, n_chunks, n_chunks_of, rows_per_lib, top_k, k_out, row_w, idx, wk, w_dense);
   XENCB_CHECK_LAUNCH("route_topk launch");
   return XENCB_OK;
 }
@@ -602,6 +674,114 @@ int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots
   return rc;
 }
 
+// ------------------------------------------------------------------------------------------------ read_multi
+size_t xencb_read_multi_workspace(int64_t n_rows, int64_t rows_per_lib, int n_chunks, int d_s, int page_rows,
+                                  int slots_dtype) {
+  if (n_rows <= 0 || rows_per_lib <= 0 || n_chunks <= 0 || d_s <= 0 || page_rows <= 0) return 0;
+  MultiPlan p;
+  if (plan_multi(n_rows, rows_per_lib, n_chunks, d_s, page_rows, slots_dtype, &p)) return 0;
+  return p.total();
+}
+
+int xencb_read_multi(const float* q, int64_t n_rows, int d_s, const void* slots, int slots_dtype, int64_t n_pages,
+                     int64_t page_stride, int page_rows, const int32_t* page_of, const int32_t* n_valid, int n_chunks,
+                     const int32_t* n_chunks_of, int64_t rows_per_lib, int64_t n_lib, const float* w, float read_temp,
+                     int read_softmax, float* r_out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!q || !slots || !page_of || !n_valid || !w || !r_out)
+    return fail(XENCB_EINVAL, "read_multi: q, slots, page_of, n_valid, w and r_out are required");
+  if (n_rows <= 0 || d_s <= 0 || page_rows <= 0 || n_chunks <= 0 || rows_per_lib <= 0 || n_lib <= 0)
+    return fail(XENCB_EINVAL, "read_multi: sizes must be positive");
+  if ((n_rows + rows_per_lib - 1) / rows_per_lib > n_lib)
+    return fail(XENCB_EINVAL, "read_multi: %lld rows need more than %lld Libraries", (long long)n_rows,
+                (long long)n_lib);
+  if (n_pages <= 0) return fail(XENCB_EINVAL, "read_multi: n_pages=%lld must be positive", (long long)n_pages);
+  if (page_stride < (int64_t)page_rows * d_s)
+    return fail(XENCB_EINVAL, "read_multi: page_stride %lld < page_rows*d_s %lld", (long long)page_stride,
+                (long long)page_rows * d_s);
+  if (!aligned(slots, 16) || (page_stride * 2) % 16 != 0 || !aligned(q, 16) || !aligned(r_out, 16))
+    return fail(XENCB_EINVAL, "read_multi: slots, q, r_out and page_stride*elem must be 16-byte aligned");
+  MultiPlan p;
+  int rc = plan_multi(n_rows, rows_per_lib, n_chunks, d_s, page_rows, slots_dtype, &p);
+  if (rc) return rc;
+  if (!workspace || !aligned(workspace, 256) || workspace_bytes < p.total())
+    return fail(XENCB_EINVAL, "read_multi: workspace needs %zu bytes, 256-byte aligned (got %zu)", p.total(),
+                workspace_bytes);
+  MultiArgs a;
+  a.q = q; a.n_rows = n_rows; a.d_s = d_s;
+  a.slots = static_cast<const char*>(slots);
+  a.n_pages = n_pages; a.page_stride_bytes = page_stride * 2; a.page_rows = page_rows;
+  a.page_of = page_of; a.n_valid = n_valid; a.n_chunks = n_chunks; a.n_chunks_of = n_chunks_of;
+  a.rows_per_lib = rows_per_lib; a.w = w;
+  a.qscale = read_softmax ? read_temp * 1.4426950408889634f : 1.f;
+  a.q_blocks = p.q_blocks; a.n_groups = p.n_groups; a.pieces = p.pieces; a.piece_rows = p.piece_rows;
+  a.units_per_group = p.units_per_group; a.n_units = p.n_units; a.s_max = p.s_max;
+  a.rps = p.rps; a.n_stage = p.n_stage; a.row_bytes = p.row_bytes; a.row_stride = p.row_stride;
+  char* ws = static_cast<char*>(workspace);
+  a.fold = reinterpret_cast<float*>(ws);
+  a.fold_info = reinterpret_cast<int64_t*>(ws + p.fold_bytes);
+  a.open = reinterpret_cast<float*>(ws + p.fold_bytes + p.finfo_bytes);
+  a.open_info = reinterpret_cast<int64_t*>(ws + p.fold_bytes + p.finfo_bytes + p.open_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto run = [&](auto tag_t, auto tag_s, auto tag_w) -> int {
+    using T = typename decltype(tag_t)::type;
+    constexpr bool S = decltype(tag_s)::value;
+    constexpr int W = decltype(tag_w)::value;
+    constexpr bool SPLIT = std::is_same<T, __nv_bfloat16>::value;
+    auto k1 = read_multi_mma_kernel<T, SPLIT, S, W>;
+    int r2 = ensure_smem(k1, (int)p.smem);
+    if (r2) return r2;
+    k1<<<p.grid, p.threads, p.smem, st>>>(a);
+    XENCB_CHECK_LAUNCH("read_multi_mma_kernel launch");
+    dim3 mg((unsigned)p.n_groups, (unsigned)((d_s + 127) / 128));
+    read_multi_merge_kernel<S><<<mg, 128, 0, st>>>(a, p.grid, r_out);
+    XENCB_CHECK_LAUNCH("read_multi_merge_kernel launch");
+    return XENCB_OK;
+  };
+  struct F16T { using type = __half; };
+  struct BF16T { using type = __nv_bfloat16; };
+  using ST = std::true_type;
+  using SF = std::false_type;
+  using W8 = std::integral_constant<int, 8>;
+  using W16 = std::integral_constant<int, 16>;
+  if (p.tpw == 8) {
+    if (slots_dtype == XENCB_F16) rc = read_softmax ? run(F16T{}, ST{}, W8{}) : run(F16T{}, SF{}, W8{});
+    else rc = read_softmax ? run(BF16T{}, ST{}, W8{}) : run(BF16T{}, SF{}, W8{});
+  } else {
+    if (slots_dtype == XENCB_F16) rc = read_softmax ? run(F16T{}, ST{}, W16{}) : run(F16T{}, SF{}, W16{});
+    else rc = read_softmax ? run(BF16T{}, ST{}, W16{}) : run(BF16T{}, SF{}, W16{});
+  }
+  return rc;
+}
+
+int xencb_route_lse(const float* q, int64_t n_rows, int d_s, const float* S, int n_chunks, const int32_t* n_chunks_of,
+                    int64_t rows_per_lib, int64_t n_lib, float route_temp, float* w_out, float* header_out,
+                    void* stream) {
+  if (!q || !S || !w_out || !header_out) return fail(XENCB_EINVAL, "route_lse: q, S, w_out and header_out are required");
+  if (n_rows <= 0 || d_s <= 0 || n_chunks <= 0 || rows_per_lib <= 0 || n_lib <= 0)
+    return fail(XENCB_EINVAL, "route_lse: sizes must be positive");
+  if ((n_rows + rows_per_lib - 1) / rows_per_lib > n_lib)
+    return fail(XENCB_EINVAL, "route_lse: %lld rows need more than %lld Libraries", (long long)n_rows, (long long)n_lib);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t blocks = (n_rows * n_chunks + 7) / 8;
+  route_logits_kernel<<<(unsigned)blocks, 256, 0, st>>>(q, n_rows, d_s, S, n_chunks, n_chunks_of, rows_per_lib,
+                                                        route_temp, w_out);
+  XENCB_CHECK_LAUNCH("route_logits launch");
+  route_lse_kernel<<<(unsigned)((n_rows + 3) / 4), 128, 0, st>>>(w_out, n_rows, n_chunks, n_chunks_of, rows_per_lib,
+                                                                 header_out);
+  XENCB_CHECK_LAUNCH("route_lse launch");
+  return XENCB_OK;
+}
+
+int xencb_shard_merge(const float* parts, int n_shards, int64_t n_rows, int d_s, float* r_out, void* stream) {
+  if (!parts || !r_out) return fail(XENCB_EINVAL, "shard_merge: parts and r_out are required");
+  if (n_shards <= 0 || n_rows <= 0 || d_s <= 0) return fail(XENCB_EINVAL, "shard_merge: sizes must be positive");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  dim3 grid((unsigned)n_rows, (unsigned)((d_s + 1023) / 1024));
+  shard_merge_kernel<<<grid, 256, 0, st>>>(parts, n_shards, n_rows, d_s, r_out);
+  XENCB_CHECK_LAUNCH("shard_merge launch");
+  return XENCB_OK;
+}
+
 // ------------------------------------------------------------------------------------------------ project_out
 size_t xencb_project_out_workspace(int64_t n_rows, int d_s, int d_m) {
   DevInfo di;
@@ -613,7 +793,8 @@ size_t xencb_project_out_workspace(int64_t n_rows, int d_s, int d_m) {
 }
 
 int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_out, const float* b_out, int d_m,
-                      float scale, const float* gate, const float* sel_w, float log_alpha, const float* pos_mask,
+                      float scale, const float* log_scale_dev, const float* gate, const float* sel_w, float log_alpha,
+                      const float* log_alpha_dev, const float* pos_mask,
                       const void* h, int h_dtype, void* delta_out, void* h_out, float* rel_out, void* workspace,
                       size_t workspace_bytes, void* stream) {
   if (!r || !w_out || !h) return fail(XENCB_EINVAL, "project_out: r, w_out and h are required");
@@ -646,9 +827,11 @@ int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_ou
 #define XENCB_POUT(T)                                                                                          \
   do {                                                                                                         \
     project_out_reduce_kernel<T><<<dim3((unsigned)n_rows, nch), 256, 0, st>>>(                                \
-        part, gp.splits, n_rows, d_m, b_out, scale, gate, static_cast<const T*>(h), dbuf, norm_part, row_done);\
+        part, gp.splits, n_rows, d_m, b_out, scale, log_scale_dev, gate, static_cast<const T*>(h), dbuf,       \
+        norm_part, row_done);                                                                                  \
     project_out_epilogue_kernel<T><<<dim3((unsigned)n_rows, nch), 256, 0, st>>>(                               \
-        dbuf, norm_part, d_m, sel_w, alpha, pos_mask, static_cast<const T*>(h), static_cast<T*>(delta_out),     \
+        dbuf, norm_part, d_m, sel_w, alpha, log_alpha_dev, pos_mask, static_cast<const T*>(h),                 \
+        static_cast<T*>(delta_out),                                                                            \
         static_cast<T*>(h_out), rel_out, cn_part, row_done);                                                   \
   } while (0)
   switch (h_dtype) {
@@ -657,7 +840,7 @@ int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_ou
     default: XENCB_POUT(__nv_bfloat16); break;
   }
 #undef XENCB_POUT
-  XENCB_CHECK_LAUNCH("project_out epilogue launch");
+  XENCB_CHECK_LAUNCH_N("project_out reduce + epilogue launch", 2);
   return XENCB_OK;
 }
 

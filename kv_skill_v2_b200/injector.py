@@ -154,7 +154,10 @@ class XEncInjector(ExternalSkillInjector):
         return isinstance(self.itf, (ModelInterface, LinearInterface))
 
     def _query(self, h2: torch.Tensor, li: int, sel_fuse: Optional[LayerSelector] = None):
-        """(q [R, d_s], gate [R] | None, gain, z | None) for rows h2 [R, d_m] (fast interfaces)."""
+        """(q [R, d_s], gate [R] | None, log_gain | None, z | None) for rows h2 [R, d_m] (fast interfaces).
+
+        The per-layer parameters (gate_b[pos], log_gain[pos]) stay on the device and are read by the kernels, so
+        the hook path has no host reads and can be captured in a CUDA graph."""
         itf = self.itf
         sel_w = sel_b = None
         if sel_fuse is not None:
@@ -162,11 +165,11 @@ class XEncInjector(ExternalSkillInjector):
             sel_b = sel_fuse.u.bias.detach().float().to(h2.device)
         if isinstance(itf, LinearInterface):
             q, _, _, z = ops.project_in(h2, _on(itf.w_in.detach(), h2).float(), sel_w=sel_w, sel_b=sel_b)
-            return q, None, 1.0, z
+            return q, None, None, z
         p = itf._pos[li]
         gate_w = _on(itf.gate_w.detach(), h2).float()
-        gate_b = float(itf.gate_b.detach()[p])
-        gain = float(itf.log_gain.detach()[p].exp())
+        gate_b = _on(itf.gate_b.detach()[p:p + 1], h2).float()
+        gain = _on(itf.log_gain.detach()[p:p + 1], h2).float()
         lins = itf.query_weights()
         if len(lins) == 1:
             W, b = lins[0]
@@ -212,18 +215,18 @@ class XEncInjector(ExternalSkillInjector):
         lead, d_m = h.shape[:-1], h.shape[-1]
         h2 = h.reshape(-1, d_m)
         if self._fast_interface():
-            q, g, gain, _ = self._query(h2, li)
+            q, g, log_gain, _ = self._query(h2, li)
             r = self._skill_read(q, li)
             r, gcal = self._calibrate(r, li)
-            return self._finish(h, h2, r, g, gain * gcal if not isinstance(gcal, torch.Tensor) else gain, li, inject,
-                                extra=gcal if isinstance(gcal, torch.Tensor) else None)
+            return self._finish(h, h2, r, g, gcal if not isinstance(gcal, torch.Tensor) else 1.0, li, inject,
+                                extra=gcal if isinstance(gcal, torch.Tensor) else None, log_scale=log_gain)
         hn = ops.rms_norm(h2)
         q = self.itf.query(hn.view(*lead, -1)).reshape(-1, self.itf.d_s).float()
         r = self._skill_read(q, li)
         r, gcal = self._calibrate(r, li)
         return self._duck_finish(h, hn, r, gcal, li, inject)
 
-    def _finish(self, h, h2, r, g, scale, li, inject, sel_col=None, log_alpha=0.0, extra=None):
+    def _finish(self, h, h2, r, g, scale, li, inject, sel_col=None, log_alpha=0.0, extra=None, log_scale=None):
         lead = h.shape[:-1]
         W, b = self._write_weights(h2)
         pm = self._pos_mask(h) if inject else None
@@ -231,13 +234,14 @@ class XEncInjector(ExternalSkillInjector):
             g = (g if g is not None else torch.ones(r.shape[0], device=r.device)) * extra.reshape(-1).float()
         if inject:
             h_new = torch.empty_like(h2)
-            _, h_new, rel = ops.project_out(r, W, h2, b_out=b, scale=float(self.gain_scale) * float(scale), gate=g,
-                                            sel_w=sel_col, log_alpha=log_alpha, pos_mask=pm, want_delta=False,
+            _, h_new, rel = ops.project_out(r, W, h2, b_out=b, scale=float(self.gain_scale) * float(scale),
+                                            log_scale=log_scale, gate=g, sel_w=sel_col, log_alpha=log_alpha,
+                                            pos_mask=pm, want_delta=False,
                                             h_out=h_new, want_rel=True)
             return h_new.view(h.shape), rel
         delta, _, _ = ops.project_out(r, W, h2.float() if h2.dtype != torch.float32 else h2, b_out=b,
-                                      scale=float(self.gain_scale) * float(scale), gate=g, sel_w=sel_col,
-                                      log_alpha=log_alpha, want_delta=True)
+                                      scale=float(self.gain_scale) * float(scale), log_scale=log_scale, gate=g,
+                                      sel_w=sel_col, log_alpha=log_alpha, want_delta=True)
         return delta.view(*lead, -1)
 
     def _duck_finish(self, h, hn, r, gcal, li, inject, selector=None):
@@ -414,24 +418,15 @@ class LibraryInjector(XEncInjector):
         pages = self._pages(li, h)
         rpl = self._rows_per_lib(h, pages)
 
-        fuse_sel = sel is not None and li == sel.first_layer and not sel._explicit
+        fuse_sel = sel is not None and self._fast_interface() and li == sel.first_layer and not sel._explicit
         if self._fast_interface():
-            q, g, gain, z = self._query(h2, li, sel_fuse=sel if fuse_sel else None)
+            q, g, log_gain, z = self._query(h2, li, sel_fuse=sel if fuse_sel else None)
         else:
             hn = ops.rms_norm(h2)
             q = self.itf.query(hn.view(*lead, -1)).reshape(-1, self.itf.d_s).float().contiguous()
             z = None
-        idx, wk, w, _ = ops.route(q, pages.S, rows_per_lib=rpl, top_k=self.top_k, route_temp=self.route_temp,
-                                  n_chunks_of=pages.n_chunks_of)
-        r = ops.read_decode(q, pages, idx, wk, rows_per_lib=rpl, read_temp=self.read_temp,
-                            read_softmax=self.read_softmax)
-        self.last_route = w.view(*lead, pages.n_chunks)
-        if torch.is_grad_enabled():
-            self.route_terms.append((li, self.last_route))
-
-        if not self._fast_interface():
-            return self._duck_finish(h, hn, r, 1.0, li, inject, selector=sel)
-
+        # the selector's weights for this layer come first: tokens it gives weight 0 here read nothing (the
+        # reference reads every layer for every token and zeroes the delta afterwards, xenc/selector.py:106-110)
         sel_col, log_alpha = None, 0.0
         if sel is not None:
             if fuse_sel:
@@ -440,8 +435,18 @@ class LibraryInjector(XEncInjector):
             else:
                 sel.weights_for(h, li)
             sel_col = sel._w[..., sel.pos[li]].reshape(-1).float().contiguous()
-            log_alpha = float(sel.log_alpha.detach())
-        return self._finish(h, h2, r, g, gain, li, inject, sel_col=sel_col, log_alpha=log_alpha)
+            log_alpha = _on(sel.log_alpha.detach().reshape(1), h2).float()
+        idx, wk, w, _ = ops.route(q, pages.S, rows_per_lib=rpl, top_k=self.top_k, route_temp=self.route_temp,
+                                  n_chunks_of=pages.n_chunks_of, row_w=sel_col)
+        r = ops.read_decode(q, pages, idx, wk, rows_per_lib=rpl, read_temp=self.read_temp,
+                            read_softmax=self.read_softmax)
+        self.last_route = w.view(*lead, pages.n_chunks)
+        if torch.is_grad_enabled():
+            self.route_terms.append((li, self.last_route))
+
+        if not self._fast_interface():
+            return self._duck_finish(h, hn, r, 1.0, li, inject, selector=sel)
+        return self._finish(h, h2, r, g, 1.0, li, inject, sel_col=sel_col, log_alpha=log_alpha, log_scale=log_gain)
 
 
 __all__ = ["ExternalSkillInjector", "XEncInjector", "LibraryInjector", "itf_query", "itf_gate", "itf_gain",

@@ -88,11 +88,22 @@ def rms_norm(h: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
     return out.view(*h.shape[:-1], h.shape[-1])
 
 
+def _dev_scalar(x, what: str):
+    """(host value, device tensor | None): a one-element device tensor is passed by pointer (read by the kernel,
+    so the call needs no host read and stays capturable in a CUDA graph); a number is passed by value."""
+    if isinstance(x, torch.Tensor):
+        if x.numel() != 1 or not x.is_cuda:
+            raise ValueError(f"{what}: a tensor scalar must be one element on the CUDA device")
+        return 0.0, x.detach().reshape(1).to(torch.float32).contiguous()
+    return float(x), None
+
+
 def project_in(h2: torch.Tensor, w_in: torch.Tensor, b_in=None, *, rms: bool = True, l2: bool = True,
-               gate_w=None, gate_b: float = 0.0, sel_w=None, sel_b=None, eps: float = 1e-6):
+               gate_w=None, gate_b=0.0, sel_w=None, sel_b=None, eps: float = 1e-6):
     """(q [R, d_s], gate [R] | None, rstd [R], z [R, n_cand] | None) for rows h2 [R, d_m].
 
-    q = L2((rms_norm(h2) if rms else h2) @ w_in^T + b_in) (L2 only if l2); w_in is [d_s, d_m] (nn.Linear)."""
+    q = L2((rms_norm(h2) if rms else h2) @ w_in^T + b_in) (L2 only if l2); w_in is [d_s, d_m] (nn.Linear).
+    gate_b: a number, or a one-element device tensor read by the kernel."""
     dev = _cuda("project_in", h2, w_in, b_in, gate_w, sel_w, sel_b)
     h2 = h2.contiguous()
     w_in = _f32(w_in, "w_in")
@@ -109,22 +120,24 @@ def project_in(h2: torch.Tensor, w_in: torch.Tensor, b_in=None, *, rms: bool = T
     # converted inputs are bound to locals so they outlive the launch
     b_in, gate_w = _f32(b_in, "b_in"), _f32(gate_w, "gate_w")
     sel_w, sel_b = _f32(sel_w, "sel_w"), _f32(sel_b, "sel_b")
+    gb, gb_dev = _dev_scalar(gate_b, "gate_b")
     with _on_device(dev):
         ws_bytes = N.lib().xencb_project_in_workspace(R, d_m, d_s)
         ws = _workspace(ws_bytes, dev)
         N.call("xencb_project_in", _ptr(h2), _hdt(h2, "h"), R, d_m, _ptr(w_in), _ptr(b_in), d_s, flags,
-               _ptr(gate_w), float(gate_b), _ptr(sel_w), _ptr(sel_b), n_cand, eps, _ptr(q), _ptr(gate),
+               _ptr(gate_w), gb, _ptr(gb_dev), _ptr(sel_w), _ptr(sel_b), n_cand, eps, _ptr(q), _ptr(gate),
                _ptr(rstd), _ptr(z), _ptr(ws), ws.numel(), _stream(dev))
     return q, gate, rstd, z
 
 
 def project_out(r: torch.Tensor, w_out: torch.Tensor, h2: torch.Tensor, *, b_out=None, scale: float = 1.0,
-                gate=None, sel_w=None, log_alpha: float = 0.0, pos_mask=None, want_delta: bool = True,
-                h_out: Optional[torch.Tensor] = None, want_rel: bool = False):
+                log_scale: Optional[torch.Tensor] = None, gate=None, sel_w=None, log_alpha=0.0, pos_mask=None,
+                want_delta: bool = True, h_out: Optional[torch.Tensor] = None, want_rel: bool = False):
     """(delta | None, h_out | None, rel | None).
 
-    d = scale * gate * (r @ w_out^T + b_out), w_out [d_m, d_s] (nn.Linear); optional LayerSelector matched norm
-    with per-row weight sel_w;
+    d = scale * exp(log_scale) * gate * (r @ w_out^T + b_out), w_out [d_m, d_s] (nn.Linear); optional
+    LayerSelector matched norm with per-row weight sel_w and log_alpha (a number or a one-element device tensor;
+    log_scale is a one-element device tensor or None);
     d *= pos_mask; delta = d in h2's dtype; h_out = h2 + delta; rel = ||delta|| / (||h2|| + 1e-6)."""
     dev = _cuda("project_out", r, w_out, h2, b_out, gate, sel_w, pos_mask, h_out)
     r = _f32(r, "r")
@@ -140,12 +153,14 @@ def project_out(r: torch.Tensor, w_out: torch.Tensor, h2: torch.Tensor, *, b_out
     rel = torch.empty(R, dtype=torch.float32, device=dev) if want_rel else None
     b_out, gate = _f32(b_out, "b_out"), _f32(gate, "gate")
     sel_w, pos_mask = _f32(sel_w, "sel_w"), _f32(pos_mask, "pos_mask")
+    la, la_dev = _dev_scalar(log_alpha, "log_alpha")
+    ls_dev = None if log_scale is None else _dev_scalar(log_scale, "log_scale")[1]
     with _on_device(dev):
         ws_bytes = N.lib().xencb_project_out_workspace(R, d_s, d_m)
         ws = _workspace(ws_bytes, dev)
-        N.call("xencb_project_out", _ptr(r), R, d_s, _ptr(w_out), _ptr(b_out), d_m, float(scale), _ptr(gate),
-               _ptr(sel_w), float(log_alpha), _ptr(pos_mask), _ptr(h2), _hdt(h2, "h"), _ptr(delta), _ptr(h_out),
-               _ptr(rel), _ptr(ws), ws.numel(), _stream(dev))
+        N.call("xencb_project_out", _ptr(r), R, d_s, _ptr(w_out), _ptr(b_out), d_m, float(scale), _ptr(ls_dev),
+               _ptr(gate), _ptr(sel_w), la, _ptr(la_dev), _ptr(pos_mask), _ptr(h2), _hdt(h2, "h"), _ptr(delta),
+               _ptr(h_out), _ptr(rel), _ptr(ws), ws.numel(), _stream(dev))
     return delta, h_out, rel
 
 
@@ -155,9 +170,11 @@ def route_k(top_k: int, n_chunks: int) -> int:
 
 
 def route(q: torch.Tensor, S: torch.Tensor, *, rows_per_lib: int, top_k: int, route_temp: float,
-          n_chunks_of: Optional[torch.Tensor] = None, want_logits: bool = False):
-    """(idx [R, k] int32, wk [R, k], w_dense [R, C], logits [R, C] | None); S is [n_lib, C, d_s] float32."""
-    dev = _cuda("route", q, S, n_chunks_of)
+          n_chunks_of: Optional[torch.Tensor] = None, want_logits: bool = False,
+          row_w: Optional[torch.Tensor] = None):
+    """(idx [R, k] int32, wk [R, k], w_dense [R, C], logits [R, C] | None); S is [n_lib, C, d_s] float32.
+    row_w [R] (optional): rows with weight 0 get idx -1 / wk 0 (the read skips them); w_dense is unaffected."""
+    dev = _cuda("route", q, S, n_chunks_of, row_w)
     q = _f32(q, "q")
     S = _f32(S, "S")
     R, d_s = q.shape
@@ -171,9 +188,13 @@ def route(q: torch.Tensor, S: torch.Tensor, *, rows_per_lib: int, top_k: int, ro
     lg = torch.empty(R, C, dtype=torch.float32, device=dev) if want_logits else None
     if n_chunks_of is not None:
         n_chunks_of = n_chunks_of.to(torch.int32).contiguous()
+    if row_w is not None:
+        row_w = _f32(row_w.reshape(-1), "row_w")
+        if row_w.numel() != R:
+            raise ValueError(f"route: row_w has {row_w.numel()} entries for {R} rows")
     with _on_device(dev):
         N.call("xencb_route", _ptr(q), R, d_s, _ptr(S), C, _ptr(n_chunks_of), int(rows_per_lib), n_lib,
-               float(route_temp), int(top_k), _ptr(idx), _ptr(wk), _ptr(w), _ptr(lg), _stream(dev))
+               float(route_temp), int(top_k), _ptr(row_w), _ptr(idx), _ptr(wk), _ptr(w), _ptr(lg), _stream(dev))
     return idx, wk, w, lg
 
 
@@ -244,6 +265,117 @@ def read_decode(q: torch.Tensor, pages: Pages, idx: torch.Tensor, wk: torch.Tens
                _ptr(idx), _ptr(wk), k, float(read_temp), int(bool(read_softmax)), _ptr(r), _ptr(ws),
                ws.numel(), _stream(dev))
     return r
+
+
+def read_multi(q: torch.Tensor, pages: Pages, w: torch.Tensor, *, rows_per_lib: int, read_temp: float = 12.0,
+               read_softmax: bool = True, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """r [R, d_s] float32 = sum_c w[row, c] * read(q[row], chunk c): the many-query read, in which up to 8 rows of
+    a Library share each slot row fetched from HBM. w [R, C] float32 (0 = chunk not routed). Raises
+    NotImplementedError for slot types / widths the kernel does not take (see read_weighted)."""
+    dev = _cuda("read_multi", q, pages.slots, pages.page_of, pages.n_valid, w)
+    q = _f32(q, "q")
+    w = _f32(w, "w")
+    R, d_s = q.shape
+    slots = pages.slots
+    if not slots.is_contiguous():
+        raise ValueError("read_multi: the slot pool must be contiguous")
+    if slots.shape[-1] != d_s:
+        raise ValueError(f"read_multi: q has d_s={d_s}, slots have {slots.shape[-1]}")
+    if tuple(w.shape) != (R, pages.n_chunks):
+        raise ValueError(f"read_multi: w must be [{R}, {pages.n_chunks}], got {tuple(w.shape)}")
+    if out is None:
+        out = torch.empty(R, d_s, dtype=torch.float32, device=dev)
+    elif out.dtype != torch.float32 or tuple(out.shape) != (R, d_s) or not out.is_contiguous():
+        raise ValueError("read_multi: out must be a contiguous float32 [R, d_s] tensor")
+    dt = _hdt(slots, "slots")
+    nco = pages.n_chunks_of
+    if nco is not None:
+        nco = nco.to(torch.int32).contiguous()
+    with _on_device(dev):
+        ws_bytes = N.lib().xencb_read_multi_workspace(R, int(rows_per_lib), pages.n_chunks, d_s, pages.page_rows, dt)
+        if ws_bytes == 0:  # the shapes were checked above: the kernel does not take this slot type / width
+            N.check(N.ENOTSUP, "read_multi_workspace")
+        ws = _workspace(ws_bytes, dev)
+        N.call("xencb_read_multi", _ptr(q), R, d_s, _ptr(slots), dt, slots.shape[0], pages.page_rows * d_s,
+               pages.page_rows, _ptr(pages.page_of), _ptr(pages.n_valid), pages.n_chunks, _ptr(nco),
+               int(rows_per_lib), pages.n_lib, _ptr(w), float(read_temp), int(bool(read_softmax)), _ptr(out),
+               _ptr(ws), ws.numel(), _stream(dev))
+    return out
+
+
+def multi_supported(pages: Pages, n_rows: int, rows_per_lib: int) -> bool:
+    """Whether read_multi takes this slot pool (f16 / bf16 slots, d_s % 16 == 0, the stages fit on chip)."""
+    if pages.slots.dtype not in (torch.float16, torch.bfloat16) or pages.d_s % 16:
+        return False
+    with _on_device(pages.device):
+        return N.lib().xencb_read_multi_workspace(int(n_rows), int(rows_per_lib), pages.n_chunks, pages.d_s,
+                                                  pages.page_rows, _hdt(pages.slots, "slots")) > 0
+
+
+def read_weighted(q: torch.Tensor, pages: Pages, w: torch.Tensor, *, rows_per_lib: int, read_temp: float = 12.0,
+                  read_softmax: bool = True, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """read_multi where the kernel takes the shape; otherwise the decode read over every chunk of each row
+    (idx = 0..C-1, wk = w), which gives the same result with one chunk read per (row, chunk)."""
+    multi_ok = multi_supported(pages, q.shape[0], rows_per_lib)
+    if multi_ok:
+        return read_multi(q, pages, w, rows_per_lib=rows_per_lib, read_temp=read_temp, read_softmax=read_softmax,
+                          out=out)
+    R = q.shape[0]
+    idx = torch.arange(pages.n_chunks, dtype=torch.int32, device=q.device).expand(R, -1).contiguous()
+    r = read_decode(q, pages, idx, w.contiguous(), rows_per_lib=rows_per_lib, read_temp=read_temp,
+                    read_softmax=read_softmax)
+    if out is not None:
+        out.copy_(r)
+        return out
+    return r
+
+
+def route_lse(q: torch.Tensor, S: torch.Tensor, *, rows_per_lib: int, route_temp: float,
+              n_chunks_of: Optional[torch.Tensor] = None, header_out: Optional[torch.Tensor] = None):
+    """Dense routing of a chunk shard: (w [R, C] = e^(l - max), header [R, 4] = (max, sum, 0, 0))."""
+    dev = _cuda("route_lse", q, S, n_chunks_of)
+    q = _f32(q, "q")
+    S = _f32(S, "S")
+    R, d_s = q.shape
+    n_lib, C, d2 = S.shape
+    if d2 != d_s:
+        raise ValueError(f"route_lse: q has d_s={d_s}, S has {d2}")
+    w = torch.empty(R, C, dtype=torch.float32, device=dev)
+    if header_out is None:
+        header_out = torch.empty(R, 4, dtype=torch.float32, device=dev)
+    elif header_out.dtype != torch.float32 or tuple(header_out.shape) != (R, 4) or not header_out.is_contiguous():
+        raise ValueError("route_lse: header_out must be a contiguous float32 [R, 4] tensor")
+    if n_chunks_of is not None:
+        n_chunks_of = n_chunks_of.to(torch.int32).contiguous()
+    with _on_device(dev):
+        N.call("xencb_route_lse", _ptr(q), R, d_s, _ptr(S), C, _ptr(n_chunks_of), int(rows_per_lib), n_lib,
+               float(route_temp), _ptr(w), _ptr(header_out), _stream(dev))
+    return w, header_out
+
+
+def shard_block(n_rows: int, d_s: int, device, dtype=torch.float32) -> torch.Tensor:
+    """One shard's partial as a flat float32 block: n_rows headers of 4 floats, then n_rows x d_s accumulators."""
+    return torch.empty(n_rows * 4 + n_rows * d_s, dtype=dtype, device=device)
+
+
+def shard_views(block: torch.Tensor, n_rows: int, d_s: int):
+    """(header [n_rows, 4], acc [n_rows, d_s]) views of a shard block."""
+    return block[:n_rows * 4].view(n_rows, 4), block[n_rows * 4:n_rows * 4 + n_rows * d_s].view(n_rows, d_s)
+
+
+def shard_merge(parts: torch.Tensor, n_shards: int, n_rows: int, d_s: int,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """r [n_rows, d_s] from n_shards shard blocks laid end to end (what an all-gather of the blocks gives)."""
+    dev = _cuda("shard_merge", parts)
+    parts = _f32(parts, "parts")
+    if parts.numel() != n_shards * (n_rows * 4 + n_rows * d_s):
+        raise ValueError(f"shard_merge: parts has {parts.numel()} floats, expected {n_shards} blocks of "
+                         f"{n_rows * 4 + n_rows * d_s}")
+    if out is None:
+        out = torch.empty(n_rows, d_s, dtype=torch.float32, device=dev)
+    with _on_device(dev):
+        N.call("xencb_shard_merge", _ptr(parts), int(n_shards), int(n_rows), int(d_s), _ptr(out), _stream(dev))
+    return out
 
 
 # ------------------------------------------------------------------------------------------------ selector

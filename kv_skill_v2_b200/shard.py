@@ -1,0 +1,114 @@
+"""Chunk-sharded read of one large Library across the GPUs of one node (the long-document decode of BASELINE
+config 5: one Library of 2048 chunks x 512 slots, 8 query tokens, every chunk read).
+
+The reference reads one Library on one device (xenc/injector.py:149-157, 231-273). Its dense read is
+    r = sum_c w_c r_c,   w = softmax_c(l_c),  l_c = route_temp * q . S_c           (xenc/injector.py:220-229)
+which regroups by chunk shard g (chunks [lo_g, hi_g)) as
+    M_g = max_{c in g} l_c,  Z_g = sum_{c in g} e^(l_c - M_g),  A_g = sum_{c in g} e^(l_c - M_g) r_c
+    r   = sum_g e^(M_g - M) A_g / sum_g e^(M_g - M) Z_g,         M = max_g M_g.
+So each rank keeps its chunk shard of K and S in its own HBM, computes its partial (M_g, Z_g, A_g) with
+ops.route_lse + ops.read_multi into one flat block, one all-gather over the process group (NCCL over NVLink
+on GPUs) lays the blocks end to end in rank order, and ops.shard_merge combines them. Every rank takes the same
+collective steps in the same order.
+
+The compute is pluggable (`compute=`) so that the orchestration -- the partition, the block layout, the
+collective -- is testable on CPU ranks (gloo) with the oracle standing in for the kernels; the product path
+uses CudaShardCompute, and there is no CPU path.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+
+
+def partition_chunks(n_chunks: int, world: int) -> list:
+    """Even contiguous chunk ranges [(lo, hi)] per rank; the first n_chunks % world ranks get one more chunk."""
+    n_chunks, world = int(n_chunks), int(world)
+    if world <= 0:
+        raise ValueError(f"world={world} must be positive")
+    if n_chunks < world:
+        raise ValueError(f"{n_chunks} chunks cannot be sharded over {world} ranks (every shard needs a chunk)")
+    base, extra = divmod(n_chunks, world)
+    out, lo = [], 0
+    for g in range(world):
+        hi = lo + base + (1 if g < extra else 0)
+        out.append((lo, hi))
+        lo = hi
+    return out
+
+
+def shard_pages(pages: ops.Pages, lo: int, hi: int) -> ops.Pages:
+    """The view of chunks [lo, hi) of every Library in `pages` (page table, counts and keys sliced; the slot pool
+    is shared, so nothing is copied)."""
+    nco = None
+    if pages.n_chunks_of is not None:
+        nco = (pages.n_chunks_of - lo).clamp(0, hi - lo).to(torch.int32)
+    return ops.Pages(slots=pages.slots, page_of=pages.page_of[:, lo:hi].contiguous(),
+                     n_valid=pages.n_valid[:, lo:hi].contiguous(), S=pages.S[:, lo:hi].contiguous(), n_chunks_of=nco)
+
+
+class CudaShardCompute:
+    """The kernels: route_lse + the many-query read into a block, shard_merge of the gathered blocks."""
+
+    def __init__(self, route_temp: float = 10.0, read_temp: float = 12.0, read_softmax: bool = True):
+        self.route_temp, self.read_temp, self.read_softmax = float(route_temp), float(read_temp), bool(read_softmax)
+
+    def partial(self, q: torch.Tensor, pages: ops.Pages, rows_per_lib: int, header: torch.Tensor,
+                acc: torch.Tensor) -> None:
+        w, _ = ops.route_lse(q, pages.S, rows_per_lib=rows_per_lib, route_temp=self.route_temp,
+                             n_chunks_of=pages.n_chunks_of, header_out=header)
+        ops.read_weighted(q, pages, w, rows_per_lib=rows_per_lib, read_temp=self.read_temp,
+                          read_softmax=self.read_softmax, out=acc)
+
+    def merge(self, gathered: torch.Tensor, world: int, n_rows: int, d_s: int, out: torch.Tensor) -> None:
+        ops.shard_merge(gathered, world, n_rows, d_s, out=out)
+
+
+class ShardedRead:
+    """r [n_rows, d_s] of the whole Library from this rank's chunk shard `pages` (one Library, or several with
+    rows_per_lib rows each). Buffers are allocated once, so a step is CUDA-graph capturable (the all-gather
+    included, on NCCL)."""
+
+    def __init__(self, pages: ops.Pages, n_rows: int, *, rows_per_lib: Optional[int] = None, group=None,
+                 compute=None, device=None):
+        self.pages = pages
+        self.n_rows = int(n_rows)
+        self.rows_per_lib = int(rows_per_lib or n_rows)
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if self.world > 1 else 0
+        self.compute = compute or CudaShardCompute()
+        self.d_s = int(pages.S.shape[-1])
+        device = torch.device(device) if device is not None else pages.S.device
+        per = self.n_rows * 4 + self.n_rows * self.d_s
+        self.block = torch.zeros(per, dtype=torch.float32, device=device)
+        self.gathered = torch.zeros(self.world * per, dtype=torch.float32, device=device)
+        self.r = torch.empty(self.n_rows, self.d_s, dtype=torch.float32, device=device)
+        self.header, self.acc = ops.shard_views(self.block, self.n_rows, self.d_s)
+
+    def partial(self, q: torch.Tensor) -> torch.Tensor:
+        """This rank's block (headers, accumulators) for query rows q [n_rows, d_s]."""
+        if tuple(q.shape) != (self.n_rows, self.d_s):
+            raise ValueError(f"ShardedRead: q must be [{self.n_rows}, {self.d_s}], got {tuple(q.shape)}")
+        self.compute.partial(q, self.pages, self.rows_per_lib, self.header, self.acc)
+        return self.block
+
+    def exchange(self) -> None:
+        """The one collective: every rank's block, in rank order, into `gathered`."""
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.gathered, self.block, group=self.group)
+
+    def merge(self) -> torch.Tensor:
+        src = self.gathered if self.world > 1 else self.block
+        self.compute.merge(src, self.world, self.n_rows, self.d_s, self.r)
+        return self.r
+
+    def __call__(self, q: torch.Tensor) -> torch.Tensor:
+        self.partial(q)
+        self.exchange()
+        return self.merge()

@@ -39,6 +39,9 @@ def test_host_only_entry_points():
     assert L.xencb_abi_version() == N.ABI_VERSION
     assert L.xencb_route_k(4, 64) == 4 and L.xencb_route_k(0, 64) == 64 and L.xencb_route_k(64, 64) == 64
     assert isinstance(L.xencb_last_error(), bytes)
+    before = N.launch_count()
+    assert before >= 0
+    assert L.xencb_route_k(4, 64) == 4 and N.launch_count() == before  # host-only calls launch nothing
 
 
 def test_header_constants_match_binding():
