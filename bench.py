@@ -55,6 +55,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-sharded", action="store_true", help="skip the config-5 sharded read")
     ap.add_argument("--sharded-only", action="store_true",
                     help="only the config-5 sharded read; print its object as the line (for profilers)")
+    ap.add_argument("--sharded-chunks", type=int, default=2048,
+                    help="chunks of the config-5 Library (2048 = the config; smaller only for profiler captures)")
     ap.add_argument("--no-selector", action="store_true", help="skip the config-4 multi-depth selector decode")
     ap.add_argument("--selector-only", action="store_true",
                     help="only the config-4 selector decode; print its object as the line (for profilers)")
@@ -239,7 +241,8 @@ def build_workload(torch, dev, docs: int, seed: int):
 CFG5 = dict(C=2048, N=512, d_s=2560, d_m=5120, T=8, read_temp=12.0, route_temp=10.0)
 
 
-def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int, flush, stream) -> dict:
+def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int, flush, stream,
+                n_chunks: int = 2048) -> dict:
     """one Library of 2048 chunks x 512 fp16 slots (1,048,576 slots, d_s 2560), 8 query tokens,
     every chunk read (top_k 0); the chunks sharded evenly over the ranks, the partials exchanged by one NCCL
     all-gather per step and merged. Strong scaling: the whole Library is the same at every N.
@@ -250,7 +253,7 @@ def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
     from kv_skill_v2_b200 import _native, ops
     from kv_skill_v2_b200.shard import ShardedRead, partition_chunks
 
-    C, N, d_s, d_m, T = CFG5["C"], CFG5["N"], CFG5["d_s"], CFG5["d_m"], CFG5["T"]
+    C, N, d_s, d_m, T = int(n_chunks), CFG5["N"], CFG5["d_s"], CFG5["d_m"], CFG5["T"]
     lo, hi = partition_chunks(C, world)[rank]
     Cl = hi - lo
     g = torch.Generator(device=dev).manual_seed(5000 + lo)
@@ -336,9 +339,10 @@ def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
     peak, peak_kind = hbm_peak()
     ms = t_max / steps
     del g_pre, g_post, g_read
-    return {"workload": "BASELINE config 5: one Library of 2048 chunks x 512 fp16 slots (1,048,576 slots), d_s 2560, "
+    return {"workload": f"BASELINE config 5: one Library of {C} chunks x 512 fp16 slots ({C * N:,} slots), d_s 2560, "
                         "d_m 5120, 8 query tokens, dense read of every chunk; chunks sharded evenly over the GPUs, "
-                        "partials (max, sum, acc) merged after one NCCL all-gather per step",
+                        "partials (max, sum, acc) merged after one NCCL all-gather per step"
+                        + ("" if C == CFG5["C"] else f" (REDUCED from {CFG5['C']} chunks for a profiler capture)"),
             "metric": "sharded Library-read tokens/s (whole job)", "value": T * steps / (t_max / 1000.0),
             "unit": "tokens/s", "n_gpus": world, "ms_per_step": ms, "scaling": "strong",
             "chunks_per_gpu": Cl, "kernels_per_step": kernels, "gpu_launches": kernels * steps,
@@ -482,8 +486,12 @@ def run_ours(args) -> None:
 
     if args.sharded_only or args.selector_only:
         flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
-        fn = run_sharded if args.sharded_only else run_selector
-        res = fn(torch, dist, dev, world, rank, args.steps, args.warmup, flush, torch.cuda.current_stream(dev))
+        if args.sharded_only:
+            res = run_sharded(torch, dist, dev, world, rank, args.steps, args.warmup, flush,
+                              torch.cuda.current_stream(dev), n_chunks=args.sharded_chunks)
+        else:
+            res = run_selector(torch, dist, dev, world, rank, args.steps, args.warmup, flush,
+                               torch.cuda.current_stream(dev))
         res["device_status"] = ops.device_status(dev)
         if world > 1:
             dist.barrier()

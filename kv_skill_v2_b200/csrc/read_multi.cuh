@@ -57,6 +57,8 @@ struct MultiArgs {
   int64_t* fold_info;   // [grid][s_max]: group, or -1 when the slot holds nothing
   float* open;          // [grid][2][MQ_OPEN + MQ * d_s]: (m, l) per query, then acc per query
   int64_t* open_info;   // [grid][2]: group * n_chunks + chunk, or -1
+  int* merge_counter;   // [n_groups * merge slabs], zeroed here for read_multi_merge_kernel
+  int64_t n_merge_counters;
 };
 
 struct __align__(16) MultiMeta {
@@ -119,6 +121,9 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
     fence_mbar_init();
   }
   for (int i = threadIdx.x; i < a.s_max; i += blockDim.x) a.fold_info[(int64_t)blockIdx.x * a.s_max + i] = -1;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.n_merge_counters;
+       i += (int64_t)gridDim.x * blockDim.x)
+    a.merge_counter[i] = 0;
   if (threadIdx.x < 2) a.open_info[(int64_t)blockIdx.x * 2 + threadIdx.x] = -1;
   __syncthreads();
 
@@ -433,83 +438,196 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
 }
 
 // r[row] = sum of the fold slots of the CTAs covering the row's group + the open partials, merged per chunk
-// (log2-domain log-sum-exp) and weighted by w[row, c]. Grid (n_groups, ceil(d_s / 128)), 128 threads; thread
-// = one column d for the group's <= 8 query rows.
+// (log2-domain log-sum-exp) and weighted by w[row, c]. Because the merge of a chunk's pieces is a weighted sum
+// with per-(piece, query) coefficients w_c 2^(m_p - M) / L that do not depend on the column, every output is
+//     r[q][d] = sum_src coef[src][q] * data[src][q][d]        (coef = 1 for fold slots)
+// Grid (n_groups, ceil(d_s / 128), MM_SQ); block = 8 warps, lane = one float4 of columns. Each block: warp 0
+// compacts the group's open slots (unit order) and cuts them into runs of one chunk; the warps compute the runs'
+// coefficients into shared memory; then the block's quarter of the sources is summed (warps split the sources,
+// each lane keeps 8 float4 accumulators) and reduced in shared memory into a block partial. The last block of
+// a (group, column slab) adds the MM_SQ partials in a fixed order and writes r. The per-slab counters are
+// zeroed by read_multi_mma_kernel (stream order) and re-armed by the last block.
+constexpr int MM_MERGE_THREADS = 256;
+constexpr int MM_MERGE_WARPS = MM_MERGE_THREADS / 32;
+constexpr int MM_SQ = 4;                  // source splits per (group, slab)
+constexpr int MM_MERGE_MAX_CTAS = 160;    // read grids up to this many CTAs (static shared memory < 48 KB)
+constexpr int MM_MERGE_MAX_SLOTS = 2 * MM_MERGE_MAX_CTAS;
+
+struct MultiMergeArgs {
+  float* part;     // [n_groups][n_slabs][MM_SQ][MQ][128]
+  int* counter;    // [n_groups][n_slabs]
+  int n_slabs;
+};
+
 template <bool SOFTMAX>
-__global__ void __launch_bounds__(128) read_multi_merge_kernel(const MultiArgs a, int grid, float* __restrict__ r_out) {
+__global__ void __launch_bounds__(MM_MERGE_THREADS, 2) read_multi_merge_kernel(const MultiArgs a, int grid,
+                                                                               MultiMergeArgs mm,
+                                                                               float* __restrict__ r_out) {
+  __shared__ int slot_of[MM_MERGE_MAX_SLOTS];
+  __shared__ int run_start[MM_MERGE_MAX_SLOTS + 1];
+  __shared__ float coef[MM_MERGE_MAX_SLOTS][MQ];
+  __shared__ int fold_of[MM_MERGE_MAX_CTAS];
+  __shared__ int n_open, n_runs, n_fold, is_last;
+  __shared__ float4 red[MM_MERGE_WARPS][MQ][32];
   const int64_t g = blockIdx.x;
-  const int d = blockIdx.y * 128 + threadIdx.x;
+  const int slab = blockIdx.y, sq = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int d = slab * 128 + lane * 4;
+  const bool dok = d < a.d_s;  // d_s % 16 == 0: a float4 is either fully in or fully out
   const int64_t lib = g / a.q_blocks;
   const int64_t row0 = lib * a.rows_per_lib + (g - lib * a.q_blocks) * MQ;
   int64_t row_lim = lib * a.rows_per_lib + a.rows_per_lib;
   if (row_lim > a.n_rows) row_lim = a.n_rows;
   const int nq = (int)(row_lim - row0 < MQ ? row_lim - row0 : MQ);
-  if (nq <= 0 || d >= a.d_s) return;
-  float out[MQ];
-#pragma unroll
-  for (int j = 0; j < MQ; ++j) out[j] = 0.f;
+  if (nq <= 0) return;  // uniform per block (no counter of this group is ever armed)
   const int64_t b0 = mq_cta_of(g * a.units_per_group, a.n_units, grid);
   const int64_t b1 = mq_cta_of((g + 1) * a.units_per_group - 1, a.n_units, grid);
-  for (int64_t b = b0; b <= b1; ++b) {
-    const int64_t gf = mq_unit_begin(b, a.n_units, grid) / a.units_per_group;
-    const int64_t seg = g - gf;
-    if (seg < 0 || seg >= a.s_max || a.fold_info[b * a.s_max + seg] != g) continue;
-    const float* fs = a.fold + (b * a.s_max + seg) * MQ * a.d_s + d;
-#pragma unroll
-    for (int j = 0; j < MQ; ++j)
-      if (j < nq) out[j] += fs[(int64_t)j * a.d_s];
-  }
-  // open partials, in unit order: the pieces of one chunk are adjacent
-  int cur_c = -1;
-  float M[MQ], L[MQ], A[MQ];
-  auto finish = [&]() {
-    if (cur_c < 0) return;
-#pragma unroll
-    for (int j = 0; j < MQ; ++j)
-      if (j < nq && L[j] > 0.f) out[j] += a.w[(row0 + j) * a.n_chunks + cur_c] * (A[j] / L[j]);
-  };
-  for (int64_t b = b0; b <= b1; ++b) {
-    for (int s = 0; s < 2; ++s) {
-      const int64_t info = a.open_info[b * 2 + s];
-      if (info < 0 || info / a.n_chunks != g) continue;
-      const int c = (int)(info - g * a.n_chunks);
-      const float* os = a.open + (b * 2 + s) * (MQ_OPEN + (int64_t)MQ * a.d_s);
-      if (c != cur_c) {
-        finish();
-        cur_c = c;
-#pragma unroll
-        for (int j = 0; j < MQ; ++j) {
-          M[j] = -CUDART_INF_F;
-          L[j] = 0.f;
-          A[j] = 0.f;
-        }
+  const int n_cta = (int)(b1 - b0 + 1);
+
+  // ---- warp 0: fold slots and open slots of this group, compacted in unit order; runs of one chunk
+  if (warp == 0) {
+    int cnt = 0;
+    for (int base = 0; base < n_cta; base += 32) {
+      const int i = base + lane;
+      bool mine = false;
+      if (i < n_cta) {
+        const int64_t b = b0 + i;
+        const int64_t seg = g - mq_unit_begin(b, a.n_units, grid) / a.units_per_group;
+        mine = seg >= 0 && seg < a.s_max && a.fold_info[b * a.s_max + seg] == g;
       }
-#pragma unroll
-      for (int j = 0; j < MQ; ++j) {
-        if (j < nq) {
-          const float mp = os[j * 2], lp = os[j * 2 + 1];
-          const float ap = os[MQ_OPEN + (int64_t)j * a.d_s + d];
-          if (SOFTMAX) {
-            if (lp > 0.f) {
-              const float mn = fmaxf(M[j], mp);
-              const float s0 = exp2f(M[j] - mn), s1 = exp2f(mp - mn);
-              A[j] = A[j] * s0 + ap * s1;
-              L[j] = L[j] * s0 + lp * s1;
-              M[j] = mn;
-            }
-          } else {
-            A[j] += ap;
-            L[j] += lp;
+      const unsigned m = __ballot_sync(0xffffffffu, mine);
+      if (mine) fold_of[cnt + __popc(m & ((1u << lane) - 1u))] = i;
+      cnt += __popc(m);
+    }
+    int oc = 0;
+    for (int base = 0; base < 2 * n_cta; base += 32) {
+      const int i = base + lane;
+      bool mine = false;
+      if (i < 2 * n_cta) {
+        const int64_t info = a.open_info[b0 * 2 + i];
+        mine = info >= 0 && info / a.n_chunks == g;
+      }
+      const unsigned m = __ballot_sync(0xffffffffu, mine);
+      if (mine) slot_of[oc + __popc(m & ((1u << lane) - 1u))] = (int)(b0 * 2 + i);
+      oc += __popc(m);
+    }
+    __syncwarp();
+    int nr = 0;
+    for (int base = 0; base < oc; base += 32) {
+      const int i = base + lane;
+      bool start = false;
+      if (i < oc) start = i == 0 || a.open_info[slot_of[i]] != a.open_info[slot_of[i - 1]];
+      const unsigned m = __ballot_sync(0xffffffffu, start);
+      if (start) run_start[nr + __popc(m & ((1u << lane) - 1u))] = i;
+      nr += __popc(m);
+    }
+    if (lane == 0) {
+      run_start[nr] = oc;
+      n_fold = cnt;
+      n_open = oc;
+      n_runs = nr;
+    }
+  }
+  __syncthreads();
+  // ---- coefficients of the open slots: one (run, query) per thread
+  for (int t = threadIdx.x; t < n_runs * MQ; t += blockDim.x) {
+    const int rr = t / MQ, j = t - rr * MQ;
+    const int e0 = run_start[rr], e1 = run_start[rr + 1];
+    float Mx = -CUDART_INF_F, L = 0.f;
+    if (j < nq) {
+      for (int e = e0; e < e1; ++e) {
+        const float* os = a.open + (int64_t)slot_of[e] * (MQ_OPEN + (int64_t)MQ * a.d_s);
+        const float mp = os[j * 2], lp = os[j * 2 + 1];
+        if (SOFTMAX) {
+          if (lp > 0.f) {
+            const float mn = fmaxf(Mx, mp);
+            L = L * exp2f(Mx - mn) + lp * exp2f(mp - mn);
+            Mx = mn;
           }
+        } else {
+          L += lp;
         }
       }
     }
+    const int c = (int)(a.open_info[slot_of[e0]] - g * a.n_chunks);
+    const float wl = (j < nq && L > 0.f) ? a.w[(row0 + j) * a.n_chunks + c] / L : 0.f;
+    for (int e = e0; e < e1; ++e) {
+      float cf = 0.f;
+      if (wl != 0.f) {
+        const float* os = a.open + (int64_t)slot_of[e] * (MQ_OPEN + (int64_t)MQ * a.d_s);
+        cf = SOFTMAX ? (os[j * 2 + 1] > 0.f ? wl * exp2f(os[j * 2] - Mx) : 0.f) : wl;
+      }
+      coef[e][j] = cf;
+    }
   }
-  finish();
+  __syncthreads();
+  // ---- this block's quarter of the sources (folds first, then open slots)
+  const int ns = n_fold + n_open;
+  const int s_beg = (int)((int64_t)ns * sq / MM_SQ), s_end = (int)((int64_t)ns * (sq + 1) / MM_SQ);
+  float4 acc[MQ];
 #pragma unroll
-  for (int j = 0; j < MQ; ++j)
-    if (j < nq) r_out[(row0 + j) * a.d_s + d] = out[j];
+  for (int j = 0; j < MQ; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (dok) {
+    for (int si = s_beg + warp; si < s_end; si += MM_MERGE_WARPS) {
+      const float* base;
+      const float* cf = nullptr;
+      if (si < n_fold) {
+        const int64_t b = b0 + fold_of[si];
+        const int64_t seg = g - mq_unit_begin(b, a.n_units, grid) / a.units_per_group;
+        base = a.fold + (b * a.s_max + seg) * MQ * a.d_s;
+      } else {
+        const int e = si - n_fold;
+        base = a.open + (int64_t)slot_of[e] * (MQ_OPEN + (int64_t)MQ * a.d_s) + MQ_OPEN;
+        cf = coef[e];
+      }
+      float4 v[MQ];
+#pragma unroll
+      for (int j = 0; j < MQ; ++j)
+        v[j] = j < nq ? *reinterpret_cast<const float4*>(base + (int64_t)j * a.d_s + d) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < MQ; ++j) {
+        const float k = cf ? cf[j] : 1.f;
+        acc[j].x = fmaf(k, v[j].x, acc[j].x);
+        acc[j].y = fmaf(k, v[j].y, acc[j].y);
+        acc[j].z = fmaf(k, v[j].z, acc[j].z);
+        acc[j].w = fmaf(k, v[j].w, acc[j].w);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < MQ; ++j) red[warp][j][lane] = acc[j];
+  __syncthreads();
+  // block partial: thread t -> (query t / 32, float4 t % 32)
+  const int64_t pbase = ((g * mm.n_slabs + slab) * MM_SQ) * (int64_t)(MQ * 128);
+  {
+    const int j = threadIdx.x >> 5;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < MM_MERGE_WARPS; ++w) {
+      const float4 x = red[w][j][lane];
+      v.x += x.x; v.y += x.y; v.z += x.z; v.w += x.w;
+    }
+    *reinterpret_cast<float4*>(mm.part + pbase + (int64_t)sq * (MQ * 128) + j * 128 + lane * 4) = v;
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = atomicAdd(&mm.counter[g * mm.n_slabs + slab], 1) == MM_SQ - 1;
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  {
+    const int j = threadIdx.x >> 5;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int z = 0; z < MM_SQ; ++z) {
+      const float4 x = __ldcg(reinterpret_cast<const float4*>(mm.part + pbase + (int64_t)z * (MQ * 128) + j * 128 + lane * 4));
+      v.x += x.x; v.y += x.y; v.z += x.z; v.w += x.w;
+    }
+    if (j < nq && dok) *reinterpret_cast<float4*>(r_out + (row0 + j) * a.d_s + d) = v;
+  }
+  if (threadIdx.x == 0) mm.counter[g * mm.n_slabs + slab] = 0;  // re-armed for the next call
 }
+static_assert(MM_MERGE_THREADS == 32 * MQ, "the block partial maps one query per warp");
 
 // Shard merge: parts [G][n_rows * 4 + n_rows * d_s], per shard the rows' headers (max, sum, 0, 0) of the routing
 // logits followed by the rows' accumulators A_g = sum_c e^(l_c - max) r_c. With M = max_g max_g:

@@ -204,9 +204,9 @@ int launch_gemm(const void* X, int64_t M, int K, const float* W, int N, int sms,
       xf = xbuf;
     }
     CUtensorMap mw, mx;
-    int rc = tensor_map_f32_2d(&mw, W, (uint64_t)K, (uint64_t)N, TC_BK, TC_BM);
+    int rc = tensor_map_f32_2d(&mw, W, (uint64_t)K, (uint64_t)N, TC_BOX, TC_BM);
     if (rc) return rc;
-    rc = tensor_map_f32_2d(&mx, xf, (uint64_t)K, (uint64_t)M, TC_BK, TC_BN);
+    rc = tensor_map_f32_2d(&mx, xf, (uint64_t)K, (uint64_t)M, TC_BOX, TC_BN);
     if (rc) return rc;
     rc = ensure_smem(gemm_tc_kernel, (int)TC_SMEM);
     if (rc) return rc;
@@ -365,8 +365,9 @@ struct MultiPlan {
   int tpw, ncw, threads, rps, row_bytes, row_stride, n_stage, grid, pieces, piece_rows, s_max, q_blocks;
   bool split;
   int64_t n_groups, units_per_group, n_units;
-  size_t smem, fold_bytes, finfo_bytes, open_bytes, oinfo_bytes;
-  size_t total() const { return fold_bytes + finfo_bytes + open_bytes + oinfo_bytes; }
+  size_t smem, fold_bytes, finfo_bytes, open_bytes, oinfo_bytes, mpart_bytes, mcount_bytes;
+  int n_slabs;
+  size_t total() const { return fold_bytes + finfo_bytes + open_bytes + oinfo_bytes + mpart_bytes + mcount_bytes; }
 };
 
 int plan_multi(int64_t n_rows, int64_t rows_per_lib, int n_chunks, int d_s, int page_rows, int dtype, MultiPlan* p) {
@@ -412,12 +413,16 @@ int plan_multi(int64_t n_rows, int64_t rows_per_lib, int n_chunks, int d_s, int 
   p->n_units = p->n_groups * p->units_per_group;
   p->grid = (int)(p->n_units < di.sms ? p->n_units : di.sms);
   if (p->grid < 1) p->grid = 1;
+  if (p->grid > MM_MERGE_MAX_CTAS) return fail(XENCB_ENOTSUP, "read_multi: %d SMs exceed the merge's slot table", di.sms);
   const int64_t lmax = (p->n_units + p->grid - 1) / p->grid;
   p->s_max = (int)((lmax - 1 + p->units_per_group - 1) / p->units_per_group + 1);
   p->fold_bytes = align_up((size_t)p->grid * p->s_max * MQ * d_s * sizeof(float), 256);
   p->finfo_bytes = align_up((size_t)p->grid * p->s_max * sizeof(int64_t), 256);
   p->open_bytes = align_up((size_t)p->grid * 2 * (MQ_OPEN + (size_t)MQ * d_s) * sizeof(float), 256);
   p->oinfo_bytes = align_up((size_t)p->grid * 2 * sizeof(int64_t), 256);
+  p->n_slabs = (d_s + 127) / 128;
+  p->mpart_bytes = align_up((size_t)p->n_groups * p->n_slabs * MM_SQ * MQ * 128 * sizeof(float), 256);
+  p->mcount_bytes = align_up((size_t)p->n_groups * p->n_slabs * sizeof(int), 256);
   return XENCB_OK;
 }
 
@@ -721,6 +726,12 @@ int xencb_read_multi(const float* q, int64_t n_rows, int d_s, const void* slots,
   a.fold_info = reinterpret_cast<int64_t*>(ws + p.fold_bytes);
   a.open = reinterpret_cast<float*>(ws + p.fold_bytes + p.finfo_bytes);
   a.open_info = reinterpret_cast<int64_t*>(ws + p.fold_bytes + p.finfo_bytes + p.open_bytes);
+  MultiMergeArgs mm;
+  mm.part = reinterpret_cast<float*>(ws + p.fold_bytes + p.finfo_bytes + p.open_bytes + p.oinfo_bytes);
+  mm.counter = reinterpret_cast<int*>(ws + p.fold_bytes + p.finfo_bytes + p.open_bytes + p.oinfo_bytes + p.mpart_bytes);
+  mm.n_slabs = p.n_slabs;
+  a.merge_counter = mm.counter;
+  a.n_merge_counters = p.n_groups * (int64_t)p.n_slabs;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto run = [&](auto tag_t, auto tag_s, auto tag_w) -> int {
     using T = typename decltype(tag_t)::type;
@@ -732,8 +743,8 @@ int xencb_read_multi(const float* q, int64_t n_rows, int d_s, const void* slots,
     if (r2) return r2;
     k1<<<p.grid, p.threads, p.smem, st>>>(a);
     XENCB_CHECK_LAUNCH("read_multi_mma_kernel launch");
-    dim3 mg((unsigned)p.n_groups, (unsigned)((d_s + 127) / 128));
-    read_multi_merge_kernel<S><<<mg, 128, 0, st>>>(a, p.grid, r_out);
+    dim3 mg((unsigned)p.n_groups, (unsigned)p.n_slabs, MM_SQ);
+    read_multi_merge_kernel<S><<<mg, MM_MERGE_THREADS, 0, st>>>(a, p.grid, mm, r_out);
     XENCB_CHECK_LAUNCH("read_multi_merge_kernel launch");
     return XENCB_OK;
   };
