@@ -161,6 +161,20 @@ XENCB_API int xencb_read_multi(const float* q, int64_t n_rows, int d_s, const vo
                                int64_t n_lib, const float* w, float read_temp, int read_softmax, float* r_out,
                                void* workspace, size_t workspace_bytes, void* stream);
 
+/* Prefill (registration) read on the tensor cores: the same result as xencb_read_multi, computed as two tcgen05
+ * GEMMs for many query tokens per Library (T = 2048 tokens per document, every chunk read).
+ * w [n_rows, n_chunks] float32 as in xencb_read_multi. Requirements: f16 slots, d_s a multiple of 64,
+ * page_rows <= 512, a dense pool (page_stride == page_rows * d_s); rows of a page past n_valid must be finite
+ * (they are multiplied by 0). Other shapes return XENCB_ENOTSUP. q is rounded to f16 for the score product.
+ * Workspace: xencb_read_prefill_workspace bytes (q in f16 + the f16 weights P [n_rows, n_chunks * round_up(page_rows, 64)]). */
+XENCB_API size_t xencb_read_prefill_workspace(int64_t n_rows, int n_chunks, int d_s, int page_rows);
+XENCB_API int xencb_read_prefill(const float* q, int64_t n_rows, int d_s, const void* slots, int slots_dtype,
+                                 int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of,
+                                 const int32_t* n_valid, int n_chunks, const int32_t* n_chunks_of,
+                                 int64_t rows_per_lib, int64_t n_lib, const float* w, float read_temp,
+                                 int read_softmax, float* r_out, void* workspace, size_t workspace_bytes,
+                                 void* stream);
+
 /* Dense routing of one chunk shard of a Library (the routing softmax of xenc/injector.py:220-229 with top_k = 0,
  * regrouped by shard): w_out [n_rows, n_chunks] = e^(l_c - max_c l_c) with l = route_temp * q . S_c, and
  * header_out [n_rows, 4] = (max_c l_c, sum_c e^(l_c - max), 0, 0). Feeding w_out to xencb_read_multi gives the

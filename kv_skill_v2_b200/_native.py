@@ -43,6 +43,9 @@ SIGNATURES: dict = {
     "xencb_read_multi_workspace": (_sz, [_i64, _i64, _i, _i, _i, _i]),
     "xencb_read_multi": (_i, [_p, _i64, _i, _p, _i, _i64, _i64, _i, _p, _p, _i, _p, _i64, _i64, _p, _f, _i, _p, _p,
                               _sz, _p]),
+    "xencb_read_prefill_workspace": (_sz, [_i64, _i, _i, _i]),
+    "xencb_read_prefill": (_i, [_p, _i64, _i, _p, _i, _i64, _i64, _i, _p, _p, _i, _p, _i64, _i64, _p, _f, _i, _p,
+                                _p, _sz, _p]),
     "xencb_route_lse": (_i, [_p, _i64, _i, _p, _i, _p, _i64, _i64, _f, _p, _p, _p]),
     "xencb_shard_merge": (_i, [_p, _i, _i64, _i, _p, _p]),
     "xencb_project_out_workspace": (_sz, [_i64, _i, _i]),

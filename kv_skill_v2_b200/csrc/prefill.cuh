@@ -1,0 +1,324 @@
+// Prefill (registration) read on the 5th-generation tensor cores: the dense read of LibraryInjector._branch
+// (xenc/injector.py:239-265) for T query tokens per Library, as two tcgen05 GEMMs (kind::f16, f32 accumulate
+// in TMEM, operands staged by 2-D TMA with 128-byte swizzle, no multicast):
+//
+//   scores  S[t, c, j] = q16[t] . K[c, j]                                   CTA tile: 128 tokens x one chunk
+//           P[t, c, j] = w[t, c] * softmax_j<n_c(read_temp * S[t, c, :])_j   (softmax read)
+//                      = w[t, c] * S[t, c, j] / sqrt(n_c)                    (linear read)
+//                      = 0 for j >= n_c                                      P stored f16 [R, C * ncol]
+//   read    r[t]       = sum_{c, j} P[t, c, j] K[c, j]                       CTA tile: 128 tokens x 256 of d_s
+//
+// The chunk softmax is complete inside one scores tile (a chunk's <= 512 scores of a token sit in one TMEM row),
+// so P carries the final two-level weights and the read is a plain GEMM over all slots. In the read the slots
+// are the contraction dimension while a slot row stores d_s contiguously, so K enters as an MN-major B operand.
+// q is rounded to f16 for the first product (the slots are f16 already); P is f16 in [0, w].
+// Warp roles in both kernels: warp 0 lane 0 issues TMA, warp 1 lane 0 issues tcgen05.mma, warps 2-5 run the
+// epilogue (thread = token row = TMEM lane). Every wait is bounded; TMEM is freed on every path.
+#pragma once
+
+#include "tc.cuh"
+
+namespace xencb {
+
+constexpr int PF_BM = 128;      // tokens per CTA (UMMA M)
+constexpr int PF_BK = 64;       // f16 per 128-byte swizzle row = one k-block
+constexpr int PF_THREADS = 192;
+constexpr int PF_S_STAGES = 2;  // scores: A 16 KB + B up to 64 KB per stage
+constexpr int PF_S_BBYTES = 512 * 128;
+constexpr int PF_S_STAGE = PF_BM * 128 + PF_S_BBYTES;
+constexpr size_t PF_S_SMEM = 1024 + (size_t)PF_S_STAGES * PF_S_STAGE + 256;
+constexpr int PF_R_STAGES = 4;  // read: A 16 KB + B 4 x 8 KB per stage
+constexpr int PF_R_BN = 256;    // columns of d_s per read CTA
+constexpr int PF_R_STAGE = PF_BM * 128 + (PF_R_BN / 64) * 64 * 128;
+constexpr size_t PF_R_SMEM = 1024 + (size_t)PF_R_STAGES * PF_R_STAGE + 256;
+
+struct PrefillArgs {
+  int64_t n_rows;          // R
+  int64_t rows_per_lib;    // T
+  int d_s;
+  int n_chunks;            // C (page-table width)
+  int page_rows;           // N
+  int ncol;                // round_up(N, 64): P columns per chunk, <= 512
+  int64_t n_pages;
+  const int32_t* page_of;      // [n_lib, C]
+  const int32_t* n_valid;      // [n_lib, C]
+  const int32_t* n_chunks_of;  // [n_lib] or null
+  const float* w;              // [R, C]
+  float qscale;                // read_temp * log2(e)
+  int softmax;
+  __half* P;                   // [R, C * ncol]
+  float* r_out;                // [R, d_s]
+};
+
+struct PfBars {
+  uint64_t* full;
+  uint64_t* empty;
+  uint64_t* done;
+  uint32_t* tmem_slot;
+  volatile int* abort_flag;
+};
+
+__device__ __forceinline__ PfBars pf_bars(unsigned char* after_stages, int n_stage) {
+  PfBars b;
+  b.full = reinterpret_cast<uint64_t*>(after_stages);
+  b.empty = b.full + n_stage;
+  b.done = b.empty + n_stage;
+  b.tmem_slot = reinterpret_cast<uint32_t*>(b.done + 1);
+  b.abort_flag = reinterpret_cast<volatile int*>(b.tmem_slot + 1);
+  return b;
+}
+
+__device__ __forceinline__ void pf_setup(const PfBars& b, int n_stage, uint32_t tmem_cols) {
+  const int warp = threadIdx.x >> 5;
+  if (warp == 1) {
+    tc_alloc(b.tmem_slot, tmem_cols);
+    tc_relinquish();
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < n_stage; ++i) {
+      mbar_init(&b.full[i], 1);
+      mbar_init(&b.empty[i], 1);
+    }
+    mbar_init(b.done, 1);
+    *b.abort_flag = 0;
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+}
+
+// ---------------------------------------------------------------------------------------------------- scores
+__global__ void __launch_bounds__(PF_THREADS, 1) prefill_scores_kernel(const __grid_constant__ CUtensorMap map_q,
+                                                                       const __grid_constant__ CUtensorMap map_k,
+                                                                       const PrefillArgs a, int b_box_rows) {
+  extern __shared__ unsigned char pf_smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(pf_smem_raw) + 1023) & ~uintptr_t(1023));
+  const PfBars bars = pf_bars(smem + PF_S_STAGES * PF_S_STAGE, PF_S_STAGES);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t lib = blockIdx.z;
+  const int c = blockIdx.y;
+  const int64_t t0 = (int64_t)blockIdx.x * PF_BM;       // token offset inside the Library
+  const int64_t row0 = lib * a.rows_per_lib + t0;        // first q row of the tile
+  const int nkb = a.d_s / PF_BK;
+  const int nb = (a.ncol + b_box_rows - 1) / b_box_rows;  // B boxes per stage (1 or 2)
+  const uint32_t tx = (uint32_t)(PF_BM * 128 + nb * b_box_rows * 128);
+  int64_t page = a.page_of[lib * a.n_chunks + c];
+  const bool page_ok = page >= 0 && page < a.n_pages;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&map_q);
+    prefetch_tensormap(&map_k);
+  }
+  pf_setup(bars, PF_S_STAGES, 512);
+  const uint32_t taddr = *bars.tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t stream = policy_evict_first();
+      // a bad page is never read: its coordinates are moved past the pool (TMA fills zeros there)
+      const int ybase = page_ok ? (int)(page * a.page_rows) : (int)(a.n_pages * a.page_rows);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % PF_S_STAGES, use = kb / PF_S_STAGES;
+        if (use > 0 && (!mbar_wait_bounded(&bars.empty[s], (use - 1) & 1) || *bars.abort_flag)) {
+          *bars.abort_flag = 1;
+          break;
+        }
+        unsigned char* st = smem + s * PF_S_STAGE;
+        mbar_arrive_expect_tx(&bars.full[s], tx);
+        tma_load_2d(st, &map_q, kb * PF_BK, (int)row0, &bars.full[s]);
+        for (int i = 0; i < nb; ++i)
+          tma_load_2d_hint(st + PF_BM * 128 + i * b_box_rows * 128, &map_k, kb * PF_BK, ybase + i * b_box_rows,
+                           &bars.full[s], stream);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const int n_0 = a.ncol < 256 ? a.ncol : 256, n_1 = a.ncol - n_0;
+      const uint32_t id0 = umma_idesc(UMMA_F16, UMMA_F16, PF_BM, n_0);
+      const uint32_t id1 = umma_idesc(UMMA_F16, UMMA_F16, PF_BM, n_1 > 0 ? n_1 : 16);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % PF_S_STAGES, use = kb / PF_S_STAGES;
+        if (!mbar_wait_bounded(&bars.full[s], use & 1) || *bars.abort_flag) { *bars.abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t st = smem_u32(smem + s * PF_S_STAGE);
+        const uint32_t bq = st + PF_BM * 128;
+#pragma unroll
+        for (int ks = 0; ks < PF_BK / 16; ++ks) {  // 16 f16 = 32 bytes per UMMA k-step
+          const uint64_t ad = umma_desc_k_sw128(st + ks * 32);
+          tc_mma<0>(taddr, ad, umma_desc_k_sw128(bq + ks * 32), id0, kb > 0 || ks > 0);
+          if (n_1 > 0) tc_mma<0>(taddr + 256u, ad, umma_desc_k_sw128(bq + 256 * 128 + ks * 32), id1, kb > 0 || ks > 0);
+        }
+        tc_commit(&bars.empty[s]);
+      }
+      tc_commit(bars.done);
+    }
+  } else {
+    // epilogue: token row rr of the tile (TMEM lane); the chunk softmax, the routing weight, f16 P
+    const int q4 = warp & 3;
+    const int rr = q4 * 32 + lane;
+    const int64_t t = row0 + rr;
+    const bool row_ok = t0 + rr < a.rows_per_lib && t < a.n_rows;
+    const int nc = a.n_chunks_of ? min(a.n_chunks_of[lib], a.n_chunks) : a.n_chunks;
+    int nv = a.n_valid[lib * a.n_chunks + c];
+    if (nv > a.page_rows) {
+      nv = a.page_rows;
+      if (threadIdx.x == 64) flag_error(XENCB_DEV_CLAMPED);
+    }
+    if (!page_ok) {
+      nv = 0;
+      if (threadIdx.x == 64) flag_error(XENCB_DEV_BADPAGE);
+    }
+    if (nv < 0 || c >= nc) nv = 0;
+    const float wt = row_ok ? a.w[t * a.n_chunks + c] : 0.f;
+    const bool ok = mbar_wait_bounded(bars.done, 0) && !*bars.abort_flag;
+    tc_fence_after();
+    const uint32_t tl = taddr + ((uint32_t)(q4 * 32) << 16);
+    float m = -CUDART_INF_F, l = 0.f;
+    if (a.softmax) {
+      for (int c0 = 0; c0 < a.ncol; c0 += 32) {
+        float v[32];
+        tc_ld32(tl + (uint32_t)c0, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (c0 + i < nv) m = fmaxf(m, v[i]);
+      }
+      for (int c0 = 0; c0 < a.ncol; c0 += 32) {
+        float v[32];
+        tc_ld32(tl + (uint32_t)c0, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (c0 + i < nv) l += exp2f((v[i] - m) * a.qscale);
+      }
+    }
+    const float coef = (!ok || nv == 0 || wt == 0.f) ? 0.f : (a.softmax ? wt / l : wt * rsqrtf((float)nv));
+    __half* prow = a.P + t * ((int64_t)a.n_chunks * a.ncol) + (int64_t)c * a.ncol;
+    for (int c0 = 0; c0 < a.ncol; c0 += 32) {
+      float v[32];
+      tc_ld32(tl + (uint32_t)c0, v);
+      uint32_t packed[16];
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        float x0 = 0.f, x1 = 0.f;
+        if (coef != 0.f) {
+          if (c0 + i < nv) x0 = a.softmax ? coef * exp2f((v[i] - m) * a.qscale) : coef * v[i];
+          if (c0 + i + 1 < nv) x1 = a.softmax ? coef * exp2f((v[i + 1] - m) * a.qscale) : coef * v[i + 1];
+        }
+        float r0, r1;
+        packed[i / 2] = pack2<__half>(x0, x1, r0, r1);
+      }
+      if (row_ok) {
+        uint4* dst = reinterpret_cast<uint4*>(prow + c0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tc_dealloc(taddr, 512);
+}
+
+// ---------------------------------------------------------------------------------------------------- read
+__global__ void __launch_bounds__(PF_THREADS, 1) prefill_read_kernel(const __grid_constant__ CUtensorMap map_p,
+                                                                     const __grid_constant__ CUtensorMap map_k,
+                                                                     const PrefillArgs a) {
+  extern __shared__ unsigned char pf_smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(pf_smem_raw) + 1023) & ~uintptr_t(1023));
+  const PfBars bars = pf_bars(smem + PF_R_STAGES * PF_R_STAGE, PF_R_STAGES);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t lib = blockIdx.z;
+  const int n0 = blockIdx.y * PF_R_BN;
+  const int nt = min(PF_R_BN, a.d_s - n0);  // columns of this CTA (a multiple of 64)
+  const int nbox = nt / 64;
+  const int64_t t0 = (int64_t)blockIdx.x * PF_BM;
+  const int64_t row0 = lib * a.rows_per_lib + t0;
+  const int nc = a.n_chunks_of ? min(a.n_chunks_of[lib], a.n_chunks) : a.n_chunks;
+  const int kpc = a.ncol / PF_BK;  // k-blocks per chunk
+  const int nkb = nc * kpc;
+  const uint32_t tx = (uint32_t)(PF_BM * 128 + nbox * 64 * 128);
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&map_p);
+    prefetch_tensormap(&map_k);
+  }
+  pf_setup(bars, PF_R_STAGES, 256);
+  const uint32_t taddr = *bars.tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t stream = policy_evict_first();
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % PF_R_STAGES, use = kb / PF_R_STAGES;
+        if (use > 0 && (!mbar_wait_bounded(&bars.empty[s], (use - 1) & 1) || *bars.abort_flag)) {
+          *bars.abort_flag = 1;
+          break;
+        }
+        const int c = kb / kpc, jb = kb - c * kpc;
+        const int64_t page = a.page_of[lib * a.n_chunks + c];
+        // P is 0 for a bad page (the scores kernel flagged it); its rows are read from past the pool (zeros)
+        const int y = (page >= 0 && page < a.n_pages ? (int)(page * a.page_rows) : (int)(a.n_pages * a.page_rows)) +
+                      jb * PF_BK;
+        unsigned char* st = smem + s * PF_R_STAGE;
+        mbar_arrive_expect_tx(&bars.full[s], tx);
+        tma_load_2d(st, &map_p, c * a.ncol + jb * PF_BK, (int)row0, &bars.full[s]);
+        for (int i = 0; i < nbox; ++i)
+          tma_load_2d_hint(st + PF_BM * 128 + i * 64 * 128, &map_k, n0 + i * 64, y, &bars.full[s], stream);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc(UMMA_F16, UMMA_F16, PF_BM, nt, 1);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % PF_R_STAGES, use = kb / PF_R_STAGES;
+        if (!mbar_wait_bounded(&bars.full[s], use & 1) || *bars.abort_flag) { *bars.abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t st = smem_u32(smem + s * PF_R_STAGE);
+        const uint32_t bk = st + PF_BM * 128;
+#pragma unroll
+        for (int ks = 0; ks < PF_BK / 16; ++ks)  // 16 slots per k-step: A +32 B along its row, B +16 rows (2 KB)
+          tc_mma<0>(taddr, umma_desc_k_sw128(st + ks * 32), umma_desc_mn_sw128(bk + ks * 2048, 64 * 128), idesc,
+                    kb > 0 || ks > 0);
+        tc_commit(&bars.empty[s]);
+      }
+      tc_commit(bars.done);
+    }
+  } else {
+    const int q4 = warp & 3;
+    const int rr = q4 * 32 + lane;
+    const int64_t t = row0 + rr;
+    const bool row_ok = t0 + rr < a.rows_per_lib && t < a.n_rows;
+    const bool ok = nkb > 0 && mbar_wait_bounded(bars.done, 0) && !*bars.abort_flag;
+    tc_fence_after();
+    const uint32_t tl = taddr + ((uint32_t)(q4 * 32) << 16);
+    float* dst = a.r_out + t * a.d_s + n0;
+    for (int c0 = 0; c0 < nt; c0 += 32) {
+      float v[32];
+      tc_ld32(tl + (uint32_t)c0, v);
+      if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(dst + c0 + i) =
+              ok ? make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tc_dealloc(taddr, 256);
+}
+
+// q (f32) -> f16 for the scores product.
+__global__ void __launch_bounds__(256) to_f16_kernel(const float* __restrict__ x, int64_t n, __half* __restrict__ y) {
+  for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < n; i += (int64_t)gridDim.x * blockDim.x * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(x + i);
+    float r0, r1, r2, r3;
+    uint2 o;
+    o.x = pack2<__half>(v.x, v.y, r0, r1);
+    o.y = pack2<__half>(v.z, v.w, r2, r3);
+    *reinterpret_cast<uint2*>(y + i) = o;
+  }
+}
+
+}  // namespace xencb

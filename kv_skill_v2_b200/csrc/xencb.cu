@@ -20,6 +20,7 @@
 #include "read_decode.cuh"
 #include "read_decode_mma.cuh"
 #include "read_multi.cuh"
+#include "prefill.cuh"
 #include "route.cuh"
 
 // Scratch of xencb_read_decode_noalloc: a fixed device array, so that entry point never allocates.
@@ -163,8 +164,17 @@ size_t gemm_ws_bytes(int64_t M, int N, int K, int sms, bool convert_x) {
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
+int tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dt, uint32_t esize, const void* base, uint64_t inner,
+                  uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);
+
 int tensor_map_f32_2d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
                       uint32_t box_outer) {
+  return tensor_map_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, inner, outer, inner * 4, box_inner, box_outer);
+}
+
+// A 2-D tensor map with 128-byte swizzle (the canonical UMMA operand layout), OOB elements filled with zeros.
+int tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dt, uint32_t esize, const void* base, uint64_t inner,
+                  uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
   if (!g_encode) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g_encode) {
@@ -176,11 +186,12 @@ int tensor_map_f32_2d(CUtensorMap* map, const float* base, uint64_t inner, uint6
       g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
   }
+  (void)esize;
   const cuuint64_t dims[2] = {inner, outer};
-  const cuuint64_t strides[1] = {inner * sizeof(float)};
+  const cuuint64_t strides[1] = {row_bytes};
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t es[2] = {1, 1};
-  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box,
+  const CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box,
                               es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(XENCB_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -790,6 +801,74 @@ int xencb_shard_merge(const float* parts, int n_shards, int64_t n_rows, int d_s,
   dim3 grid((unsigned)n_rows, (unsigned)((d_s + 1023) / 1024));
   shard_merge_kernel<<<grid, 256, 0, st>>>(parts, n_shards, n_rows, d_s, r_out);
   XENCB_CHECK_LAUNCH("shard_merge launch");
+  return XENCB_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ read_prefill
+size_t xencb_read_prefill_workspace(int64_t n_rows, int n_chunks, int d_s, int page_rows) {
+  if (n_rows <= 0 || n_chunks <= 0 || d_s <= 0 || page_rows <= 0) return 0;
+  const int64_t ncol = (page_rows + 63) / 64 * 64;
+  return align_up((size_t)n_rows * d_s * 2, 256) + align_up((size_t)n_rows * n_chunks * ncol * 2, 256);
+}
+
+int xencb_read_prefill(const float* q, int64_t n_rows, int d_s, const void* slots, int slots_dtype, int64_t n_pages,
+                       int64_t page_stride, int page_rows, const int32_t* page_of, const int32_t* n_valid, int n_chunks,
+                       const int32_t* n_chunks_of, int64_t rows_per_lib, int64_t n_lib, const float* w, float read_temp,
+                       int read_softmax, float* r_out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!q || !slots || !page_of || !n_valid || !w || !r_out)
+    return fail(XENCB_EINVAL, "read_prefill: q, slots, page_of, n_valid, w and r_out are required");
+  if (n_rows <= 0 || d_s <= 0 || page_rows <= 0 || n_chunks <= 0 || rows_per_lib <= 0 || n_lib <= 0 || n_pages <= 0)
+    return fail(XENCB_EINVAL, "read_prefill: sizes must be positive");
+  if ((n_rows + rows_per_lib - 1) / rows_per_lib > n_lib)
+    return fail(XENCB_EINVAL, "read_prefill: %lld rows need more than %lld Libraries", (long long)n_rows,
+                (long long)n_lib);
+  if (slots_dtype != XENCB_F16) return fail(XENCB_ENOTSUP, "read_prefill: the tensor-core prefill reads f16 slots");
+  if (d_s % 64 != 0) return fail(XENCB_ENOTSUP, "read_prefill: d_s=%d must be a multiple of 64", d_s);
+  if (page_rows > 512) return fail(XENCB_ENOTSUP, "read_prefill: page_rows=%d above 512", page_rows);
+  if (page_stride != (int64_t)page_rows * d_s)
+    return fail(XENCB_ENOTSUP, "read_prefill: the slot pool must be dense ([pages, page_rows, d_s])");
+  if (n_pages * (int64_t)page_rows + 512 > INT32_MAX || (int64_t)n_chunks * 512 > INT32_MAX)
+    return fail(XENCB_ENOTSUP, "read_prefill: the slot pool is too large for 32-bit TMA coordinates");
+  if (!aligned(slots, 16) || !aligned(q, 16) || !aligned(r_out, 16))
+    return fail(XENCB_EINVAL, "read_prefill: slots, q and r_out must be 16-byte aligned");
+  const size_t need = xencb_read_prefill_workspace(n_rows, n_chunks, d_s, page_rows);
+  if (!workspace || !aligned(workspace, 256) || workspace_bytes < need)
+    return fail(XENCB_EINVAL, "read_prefill: workspace needs %zu bytes, 256-byte aligned (got %zu)", need,
+                workspace_bytes);
+  PrefillArgs a;
+  a.n_rows = n_rows; a.rows_per_lib = rows_per_lib; a.d_s = d_s; a.n_chunks = n_chunks; a.page_rows = page_rows;
+  a.ncol = (page_rows + 63) / 64 * 64; a.n_pages = n_pages; a.page_of = page_of; a.n_valid = n_valid;
+  a.n_chunks_of = n_chunks_of; a.w = w; a.qscale = read_temp * 1.4426950408889634f; a.softmax = read_softmax ? 1 : 0;
+  char* ws = static_cast<char*>(workspace);
+  __half* q16 = reinterpret_cast<__half*>(ws);
+  a.P = reinterpret_cast<__half*>(ws + align_up((size_t)n_rows * d_s * 2, 256));
+  a.r_out = r_out;
+  const int b_box_rows = a.ncol < 256 ? a.ncol : 256;
+  CUtensorMap mq, mk1, mp, mk2;
+  int rc = tensor_map_2d(&mq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q16, (uint64_t)d_s, (uint64_t)n_rows,
+                         (uint64_t)d_s * 2, PF_BK, PF_BM);
+  if (!rc) rc = tensor_map_2d(&mk1, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, slots, (uint64_t)d_s,
+                              (uint64_t)(n_pages * page_rows), (uint64_t)d_s * 2, PF_BK, (uint32_t)b_box_rows);
+  if (!rc) rc = tensor_map_2d(&mp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.P, (uint64_t)n_chunks * a.ncol,
+                              (uint64_t)n_rows, (uint64_t)n_chunks * a.ncol * 2, PF_BK, PF_BM);
+  if (!rc) rc = tensor_map_2d(&mk2, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, slots, (uint64_t)d_s,
+                              (uint64_t)(n_pages * page_rows), (uint64_t)d_s * 2, 64, PF_BK);
+  if (rc) return rc;
+  rc = ensure_smem(prefill_scores_kernel, (int)PF_S_SMEM);
+  if (!rc) rc = ensure_smem(prefill_read_kernel, (int)PF_R_SMEM);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t nq = n_rows * (int64_t)d_s;
+  to_f16_kernel<<<(unsigned)std::min<int64_t>((nq / 4 + 255) / 256, 8192), 256, 0, st>>>(q, nq, q16);
+  XENCB_CHECK_LAUNCH("to_f16 launch");
+  const int64_t libs_used = (n_rows + rows_per_lib - 1) / rows_per_lib;
+  const unsigned tiles = (unsigned)((rows_per_lib + PF_BM - 1) / PF_BM);
+  prefill_scores_kernel<<<dim3(tiles, (unsigned)n_chunks, (unsigned)libs_used), PF_THREADS, PF_S_SMEM, st>>>(mq, mk1, a,
+                                                                                                           b_box_rows);
+  XENCB_CHECK_LAUNCH("prefill_scores launch");
+  prefill_read_kernel<<<dim3(tiles, (unsigned)((d_s + PF_R_BN - 1) / PF_R_BN), (unsigned)libs_used), PF_THREADS,
+                        PF_R_SMEM, st>>>(mp, mk2, a);
+  XENCB_CHECK_LAUNCH("prefill_read launch");
   return XENCB_OK;
 }
 

@@ -303,6 +303,36 @@ def read_multi(q: torch.Tensor, pages: Pages, w: torch.Tensor, *, rows_per_lib: 
     return out
 
 
+def read_prefill(q: torch.Tensor, pages: Pages, w: torch.Tensor, *, rows_per_lib: int, read_temp: float = 12.0,
+                 read_softmax: bool = True, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The dense read for many query tokens per Library on the tensor cores (two tcgen05 GEMMs): the same result
+    as read_multi. Needs f16 slots, d_s % 64 == 0, page_rows <= 512 (NotImplementedError otherwise)."""
+    dev = _cuda("read_prefill", q, pages.slots, pages.page_of, pages.n_valid, w)
+    q = _f32(q, "q")
+    w = _f32(w, "w")
+    R, d_s = q.shape
+    slots = pages.slots
+    if slots.dtype != torch.float16 or d_s % 64 or pages.page_rows > 512:
+        raise NotImplementedError("read_prefill: f16 slots, d_s % 64 == 0 and page_rows <= 512 are required")
+    if not slots.is_contiguous() or slots.shape[-1] != d_s:
+        raise ValueError(f"read_prefill: slots must be a contiguous [P, page_rows, {d_s}] pool")
+    if tuple(w.shape) != (R, pages.n_chunks):
+        raise ValueError(f"read_prefill: w must be [{R}, {pages.n_chunks}], got {tuple(w.shape)}")
+    if out is None:
+        out = torch.empty(R, d_s, dtype=torch.float32, device=dev)
+    nco = pages.n_chunks_of
+    if nco is not None:
+        nco = nco.to(torch.int32).contiguous()
+    with _on_device(dev):
+        ws_bytes = N.lib().xencb_read_prefill_workspace(R, pages.n_chunks, d_s, pages.page_rows)
+        ws = _workspace(ws_bytes, dev)
+        N.call("xencb_read_prefill", _ptr(q), R, d_s, _ptr(slots), N.F16, slots.shape[0], pages.page_rows * d_s,
+               pages.page_rows, _ptr(pages.page_of), _ptr(pages.n_valid), pages.n_chunks, _ptr(nco),
+               int(rows_per_lib), pages.n_lib, _ptr(w), float(read_temp), int(bool(read_softmax)), _ptr(out),
+               _ptr(ws), ws.numel(), _stream(dev))
+    return out
+
+
 def multi_supported(pages: Pages, n_rows: int, rows_per_lib: int) -> bool:
     """Whether read_multi takes this slot pool (f16 / bf16 slots, d_s % 16 == 0, the stages fit on chip)."""
     if pages.slots.dtype not in (torch.float16, torch.bfloat16) or pages.d_s % 16:
