@@ -58,6 +58,11 @@ def parse_args(argv=None):
     ap.add_argument("--sharded-chunks", type=int, default=2048,
                     help="chunks of the config-5 Library (2048 = the config; smaller only for profiler captures)")
     ap.add_argument("--no-selector", action="store_true", help="skip the config-4 multi-depth selector decode")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 tensor-core prefill read")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="only the config-3 prefill; print its object as the line (for profilers)")
+    ap.add_argument("--prefill-docs", type=int, default=8,
+                    help="documents of the config-3 prefill (8 = the config; fewer only for profiler captures)")
     ap.add_argument("--selector-only", action="store_true",
                     help="only the config-4 selector decode; print its object as the line (for profilers)")
     return ap.parse_args(argv)
@@ -467,6 +472,117 @@ def run_selector(torch, dist, dev, world: int, rank: int, steps: int, warmup: in
             "l2": "flushed between steps (256 MiB write)"}
 
 
+CFG3 = dict(docs=8, T=2048, C=128, N=512, d_s=2048, d_m=4096, read_temp=12.0, route_temp=10.0)
+
+
+def tensor_peak() -> tuple:
+    """(sustained dense bf16 TFLOP/s, source): the prefill GEMMs run inside a multi-millisecond step."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops_sustained"]), "measured sustained (MEASURED_PEAKS.json)"
+        except (KeyError, ValueError):
+            pass
+    return 1400.0, "fallback 1.4 PFLOP/s sustained"
+
+
+def run_prefill(torch, dist, dev, world: int, rank: int, steps: int, warmup: int, flush, stream,
+                docs: int = 8) -> dict:
+    """8 documents per GPU, each a Library of 128 chunks x 512 fp16 slots (65,536 slots,
+    d_s 2048), T = 2048 query tokens per document with bf16 hidden states (d_m 4096), every chunk read (dense
+    routing, full masked softmax per chunk). A step: input projection, dense routing, the tensor-core prefill
+    read (scores GEMM with the chunk softmax folded into f16 weights, then the read GEMM), output projection +
+    residual. Weak scaling: every rank its own documents."""
+    from kv_skill_v2_b200 import _native, ops
+
+    B, T, C, N, d_s, d_m = int(docs), CFG3["T"], CFG3["C"], CFG3["N"], CFG3["d_s"], CFG3["d_m"]
+    g = torch.Generator(device=dev).manual_seed(3000 + rank)
+    slots = torch.empty(B * C, N, d_s, dtype=torch.float16, device=dev)
+    for c0 in range(0, B * C, 128):
+        x = torch.randn(min(128, B * C - c0), N, d_s, generator=g, device=dev)
+        slots[c0:c0 + x.shape[0]] = (x / x.norm(dim=-1, keepdim=True)).half()
+        del x
+    po = torch.arange(B * C, dtype=torch.int32, device=dev).view(B, C)
+    nv = torch.full((B, C), N, dtype=torch.int32, device=dev)
+    pages = ops.Pages(slots=slots, page_of=po, n_valid=nv, S=ops.summaries(slots, po, nv))
+    W_in = torch.randn(d_s, d_m, generator=g, device=dev) * 0.02
+    W_out = torch.randn(d_m, d_s, generator=g, device=dev) * 0.02
+    R = B * T
+    n_in = 2
+    hs = (torch.randn(n_in, R, d_m, generator=g, device=dev)).to(torch.bfloat16)
+    h = hs[0].clone()
+    h_out = torch.empty_like(h)
+    holder = {}
+
+    def step():
+        q, _, _, _ = ops.project_in(h, W_in)
+        _, _, w, _ = ops.route(q, pages.S, rows_per_lib=T, top_k=0, route_temp=CFG3["route_temp"])
+        r = ops.read_prefill(q, pages, w, rows_per_lib=T, read_temp=CFG3["read_temp"])
+        ops.project_out(r, W_out, h, want_delta=False, h_out=h_out)
+        holder["q"], holder["w"] = q, w
+
+    with torch.inference_mode():
+        step()
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        n0 = _native.launch_count()
+        with torch.cuda.graph(graph):
+            step()
+        kernels = _native.launch_count() - n0
+        q_s, w_s = holder["q"], holder["w"]
+        for i in range(warmup):
+            h.copy_(hs[i % n_in])
+            flush.fill_(i & 0xFF)
+            graph.replay()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for i in range(steps):
+            h.copy_(hs[i % n_in])
+            flush.fill_(i & 0xFF)
+            ev[i][0].record(stream)
+            graph.replay()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+        # the prefill read alone (both GEMMs), for the tensor roofline
+        rg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(rg):
+            ops.read_prefill(q_s, pages, w_s, rows_per_lib=T, read_temp=CFG3["read_temp"])
+        n_rl = max(3, min(steps, 20))
+        evr = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_rl)]
+        rg.replay()
+        for i in range(n_rl):
+            flush.fill_(i & 0xFF)
+            evr[i][0].record(stream)
+            rg.replay()
+            evr[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+    t_ms = sum(a.elapsed_time(b) for a, b in ev)
+    t_max = t_ms
+    if world > 1:
+        t = torch.tensor([t_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_max = float(t.item())
+    ms = t_max / steps
+    t_read = statistics.mean(a.elapsed_time(b) for a, b in evr) / 1000.0
+    read_flop = 2 * 2.0 * R * (C * N) * d_s                      # scores + read GEMMs
+    step_flop = read_flop + 2.0 * R * C * d_s + 2 * 2.0 * R * d_m * d_s  # + routing + both projections
+    peak, peak_src = tensor_peak()
+    del graph, rg
+    return {"workload": f"BASELINE config 3: {B} documents x T=2048 tokens, 128 chunks x 512 fp16 slots each, d_s 2048, "
+                        "d_m 4096, bf16 hiddens, every chunk read (dense routing, masked softmax per chunk)",
+            "metric": "prefill Library-read tokens/s (whole job)", "value": R * world * steps / (t_max / 1000.0),
+            "unit": "tokens/s", "n_gpus": world, "ms_per_step": ms, "scaling": "weak",
+            "kernels_per_step": kernels, "gpu_launches": kernels * steps,
+            "step_tflops": step_flop / (ms / 1000.0) / 1e12, "algorithmic_flop_per_step": step_flop,
+            "roofline": {"bound": "tensor", "kernel": "prefill_scores_kernel + prefill_read_kernel (+ q to f16)",
+                         "achieved": read_flop / t_read / 1e12, "peak": peak, "unit": "TFLOP/s",
+                         "frac": read_flop / t_read / 1e12 / peak, "algorithmic_flop_per_launch": read_flop,
+                         "launch_ms": t_read * 1e3, "peak_source": peak_src},
+            "l2": "flushed between steps (256 MiB write); the slots (2 GiB) are > L2"}
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -484,9 +600,12 @@ def run_ours(args) -> None:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    if args.sharded_only or args.selector_only:
+    if args.sharded_only or args.selector_only or args.prefill_only:
         flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
-        if args.sharded_only:
+        if args.prefill_only:
+            res = run_prefill(torch, dist, dev, world, rank, args.steps, args.warmup, flush,
+                              torch.cuda.current_stream(dev), docs=args.prefill_docs)
+        elif args.sharded_only:
             res = run_sharded(torch, dist, dev, world, rank, args.steps, args.warmup, flush,
                               torch.cuda.current_stream(dev), n_chunks=args.sharded_chunks)
         else:
@@ -640,7 +759,9 @@ def run_ours(args) -> None:
             t_e2e = float(t.item())
         e2e = R * args.steps * world / (t_e2e / 1000.0)
         inj.detach()
-        sharded = selector = None
+        sharded = selector = prefill = None
+        if not args.no_prefill:
+            prefill = run_prefill(torch, dist, dev, world, rank, max(3, args.steps // 10), args.warmup, flush, stream)
         if not args.no_sharded:
             sharded = run_sharded(torch, dist, dev, world, rank, args.steps, args.warmup, flush, stream)
         if not args.no_selector:
@@ -674,6 +795,7 @@ def run_ours(args) -> None:
             "gpu_launches": kernels_per_step * args.steps,
             "sharded": sharded,
             "selector": selector,
+            "prefill": prefill,
             "clocks": clocks, "device_status": status}
     print(json.dumps(line), flush=True)
 

@@ -1,6 +1,6 @@
 // Prefill (registration) read on the 5th-generation tensor cores: the dense read of LibraryInjector._branch
 // (xenc/injector.py:239-265) for T query tokens per Library, as two tcgen05 GEMMs (kind::f16, f32 accumulate
-// in TMEM, operands staged by 2-D TMA with 128-byte swizzle, no multicast):
+// in TMEM, operands staged by 2-D TMA with 64-byte (scores) or 128-byte (read) swizzle, no multicast):
 //
 //   scores  S[t, c, j] = q16[t] . K[c, j]                                   CTA tile: 128 tokens x one chunk
 //           P[t, c, j] = w[t, c] * softmax_j<n_c(read_temp * S[t, c, :])_j   (softmax read)
@@ -12,9 +12,13 @@
 // so P carries the final two-level weights and the read is a plain GEMM over all slots. In the read the slots
 // are the contraction dimension while a slot row stores d_s contiguously, so K enters as an MN-major B operand.
 // q is rounded to f16 for the first product (the slots are f16 already); P is f16 in [0, w].
-// Warp roles in both kernels: warp 0 lane 0 issues TMA, warp 1 lane 0 issues tcgen05.mma, warps 2-5 run the
-// epilogue (thread = token row = TMEM lane). Every wait is bounded; TMEM is freed on every path.
+// Warp roles: warp 0 lane 0 issues TMA, warp 1 lane 0 issues tcgen05.mma; the epilogue runs on 16 warps in the
+// scores kernel (warp w reads TMEM lane quarter w % 4 = 32 token rows, column group (w - 2) / 4 = 128 columns;
+// the four groups of a row combine their (max, sum) in shared memory) and on 4 warps in the read kernel
+// (thread = token row = TMEM lane). Every wait is bounded; TMEM is freed on every path.
 #pragma once
+
+#include <math_constants.h>
 
 #include "tc.cuh"
 
@@ -22,11 +26,14 @@ namespace xencb {
 
 constexpr int PF_BM = 128;      // tokens per CTA (UMMA M)
 constexpr int PF_BK = 64;       // f16 per 128-byte swizzle row = one k-block
-constexpr int PF_THREADS = 192;
-constexpr int PF_S_STAGES = 2;  // scores: A 16 KB + B up to 64 KB per stage
-constexpr int PF_S_BBYTES = 512 * 128;
-constexpr int PF_S_STAGE = PF_BM * 128 + PF_S_BBYTES;
-constexpr size_t PF_S_SMEM = 1024 + (size_t)PF_S_STAGES * PF_S_STAGE + 256;
+constexpr int PF_THREADS = 192;         // read kernel: producer, MMA, 4 epilogue warps
+constexpr int PF_S_EPI_WARPS = 16;      // scores: 4 column groups x 4 TMEM lane quarters
+constexpr int PF_S_THREADS = 32 * (2 + PF_S_EPI_WARPS);
+constexpr int PF_S_BK = 32;     // scores k-block: 32 f16 = 64-byte swizzle rows
+constexpr int PF_S_STAGES = 5;  // scores: A 8 KB + B up to 32 KB per stage
+constexpr int PF_S_BBYTES = 512 * 64;
+constexpr int PF_S_STAGE = PF_BM * 64 + PF_S_BBYTES;
+constexpr size_t PF_S_SMEM = 1024 + (size_t)PF_S_STAGES * PF_S_STAGE + 256 + 4 * 128 * 2 * 4;
 constexpr int PF_R_STAGES = 4;  // read: A 16 KB + B 4 x 8 KB per stage
 constexpr int PF_R_BN = 256;    // columns of d_s per read CTA
 constexpr int PF_R_STAGE = PF_BM * 128 + (PF_R_BN / 64) * 64 * 128;
@@ -89,7 +96,7 @@ __device__ __forceinline__ void pf_setup(const PfBars& b, int n_stage, uint32_t 
 }
 
 // ---------------------------------------------------------------------------------------------------- scores
-__global__ void __launch_bounds__(PF_THREADS, 1) prefill_scores_kernel(const __grid_constant__ CUtensorMap map_q,
+__global__ void __launch_bounds__(PF_S_THREADS, 1) prefill_scores_kernel(const __grid_constant__ CUtensorMap map_q,
                                                                        const __grid_constant__ CUtensorMap map_k,
                                                                        const PrefillArgs a, int b_box_rows) {
   extern __shared__ unsigned char pf_smem_raw[];
@@ -100,9 +107,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_scores_kernel(const __g
   const int c = blockIdx.y;
   const int64_t t0 = (int64_t)blockIdx.x * PF_BM;       // token offset inside the Library
   const int64_t row0 = lib * a.rows_per_lib + t0;        // first q row of the tile
-  const int nkb = a.d_s / PF_BK;
+  const int nkb = a.d_s / PF_S_BK;
   const int nb = (a.ncol + b_box_rows - 1) / b_box_rows;  // B boxes per stage (1 or 2)
-  const uint32_t tx = (uint32_t)(PF_BM * 128 + nb * b_box_rows * 128);
+  const uint32_t tx = (uint32_t)(PF_BM * 64 + nb * b_box_rows * 64);
   int64_t page = a.page_of[lib * a.n_chunks + c];
   const bool page_ok = page >= 0 && page < a.n_pages;
 
@@ -126,9 +133,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_scores_kernel(const __g
         }
         unsigned char* st = smem + s * PF_S_STAGE;
         mbar_arrive_expect_tx(&bars.full[s], tx);
-        tma_load_2d(st, &map_q, kb * PF_BK, (int)row0, &bars.full[s]);
+        tma_load_2d(st, &map_q, kb * PF_S_BK, (int)row0, &bars.full[s]);
         for (int i = 0; i < nb; ++i)
-          tma_load_2d_hint(st + PF_BM * 128 + i * b_box_rows * 128, &map_k, kb * PF_BK, ybase + i * b_box_rows,
+          tma_load_2d_hint(st + PF_BM * 64 + i * b_box_rows * 64, &map_k, kb * PF_S_BK, ybase + i * b_box_rows,
                            &bars.full[s], stream);
       }
     }
@@ -142,20 +149,22 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_scores_kernel(const __g
         if (!mbar_wait_bounded(&bars.full[s], use & 1) || *bars.abort_flag) { *bars.abort_flag = 1; break; }
         tc_fence_after();
         const uint32_t st = smem_u32(smem + s * PF_S_STAGE);
-        const uint32_t bq = st + PF_BM * 128;
+        const uint32_t bq = st + PF_BM * 64;
 #pragma unroll
-        for (int ks = 0; ks < PF_BK / 16; ++ks) {  // 16 f16 = 32 bytes per UMMA k-step
-          const uint64_t ad = umma_desc_k_sw128(st + ks * 32);
-          tc_mma<0>(taddr, ad, umma_desc_k_sw128(bq + ks * 32), id0, kb > 0 || ks > 0);
-          if (n_1 > 0) tc_mma<0>(taddr + 256u, ad, umma_desc_k_sw128(bq + 256 * 128 + ks * 32), id1, kb > 0 || ks > 0);
+        for (int ks = 0; ks < PF_S_BK / 16; ++ks) {  // 16 f16 = 32 bytes per UMMA k-step
+          const uint64_t ad = umma_desc_k_sw64(st + ks * 32);
+          tc_mma<0>(taddr, ad, umma_desc_k_sw64(bq + ks * 32), id0, kb > 0 || ks > 0);
+          if (n_1 > 0) tc_mma<0>(taddr + 256u, ad, umma_desc_k_sw64(bq + 256 * 64 + ks * 32), id1, kb > 0 || ks > 0);
         }
         tc_commit(&bars.empty[s]);
       }
       tc_commit(bars.done);
     }
   } else {
-    // epilogue: token row rr of the tile (TMEM lane); the chunk softmax, the routing weight, f16 P
-    const int q4 = warp & 3;
+    // epilogue: token row rr of the tile (TMEM lane), columns [128 cg, 128 cg + 128): the chunk softmax,
+    // the routing weight, f16 P
+    float* part = reinterpret_cast<float*>(const_cast<int*>(bars.abort_flag) + 4);  // [4][128 rows][2] (max, sum)
+    const int q4 = warp & 3, cg = (warp - 2) >> 2;
     const int rr = q4 * 32 + lane;
     const int64_t t = row0 + rr;
     const bool row_ok = t0 + rr < a.rows_per_lib && t < a.n_rows;
@@ -174,44 +183,63 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_scores_kernel(const __g
     const bool ok = mbar_wait_bounded(bars.done, 0) && !*bars.abort_flag;
     tc_fence_after();
     const uint32_t tl = taddr + ((uint32_t)(q4 * 32) << 16);
+    const int cbeg = cg * 128, cend = min(a.ncol, cbeg + 128);
     float m = -CUDART_INF_F, l = 0.f;
     if (a.softmax) {
-      for (int c0 = 0; c0 < a.ncol; c0 += 32) {
+      // pass 1: this group's (max, sum) by the online rule over 32-column loads
+      for (int c0 = cbeg; c0 < cend; c0 += 32) {
         float v[32];
         tc_ld32(tl + (uint32_t)c0, v);
+        float mx = -CUDART_INF_F;
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-          if (c0 + i < nv) m = fmaxf(m, v[i]);
-      }
-      for (int c0 = 0; c0 < a.ncol; c0 += 32) {
-        float v[32];
-        tc_ld32(tl + (uint32_t)c0, v);
+          if (c0 + i < nv) mx = fmaxf(mx, v[i]);
+        const float mn = fmaxf(m, mx);
+        if (mn != -CUDART_INF_F) {
+          float sum = 0.f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c0 + i < nv) l += exp2f((v[i] - m) * a.qscale);
+          for (int i = 0; i < 32; ++i)
+            if (c0 + i < nv) sum += exp2f((v[i] - mn) * a.qscale);
+          l = (m == -CUDART_INF_F ? 0.f : l * exp2f((m - mn) * a.qscale)) + sum;
+          m = mn;
+        }
       }
+      part[(cg * 128 + rr) * 2] = m;
+      part[(cg * 128 + rr) * 2 + 1] = l;
+      named_bar_sync(1, 32 * PF_S_EPI_WARPS);
+      float M = -CUDART_INF_F;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) M = fmaxf(M, part[(g * 128 + rr) * 2]);
+      float L = 0.f;
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const float mg = part[(g * 128 + rr) * 2], lg = part[(g * 128 + rr) * 2 + 1];
+        if (lg > 0.f) L += lg * exp2f((mg - M) * a.qscale);
+      }
+      m = M;
+      l = L;
     }
     const float coef = (!ok || nv == 0 || wt == 0.f) ? 0.f : (a.softmax ? wt / l : wt * rsqrtf((float)nv));
     __half* prow = a.P + t * ((int64_t)a.n_chunks * a.ncol) + (int64_t)c * a.ncol;
-    for (int c0 = 0; c0 < a.ncol; c0 += 32) {
+    // pass 2: P for this group's columns
+    for (int c0 = cbeg; c0 < cend; c0 += 32) {
       float v[32];
       tc_ld32(tl + (uint32_t)c0, v);
-      uint32_t packed[16];
+      uint4* dst = reinterpret_cast<uint4*>(prow + c0);
 #pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        float x0 = 0.f, x1 = 0.f;
-        if (coef != 0.f) {
-          if (c0 + i < nv) x0 = a.softmax ? coef * exp2f((v[i] - m) * a.qscale) : coef * v[i];
-          if (c0 + i + 1 < nv) x1 = a.softmax ? coef * exp2f((v[i + 1] - m) * a.qscale) : coef * v[i + 1];
+      for (int i8 = 0; i8 < 32; i8 += 8) {  // 8 values -> one 16-byte store
+        uint32_t pk[4];
+#pragma unroll
+        for (int i = i8; i < i8 + 8; i += 2) {
+          float x0 = 0.f, x1 = 0.f;
+          if (coef != 0.f) {
+            if (c0 + i < nv) x0 = a.softmax ? coef * exp2f((v[i] - m) * a.qscale) : coef * v[i];
+            if (c0 + i + 1 < nv) x1 = a.softmax ? coef * exp2f((v[i + 1] - m) * a.qscale) : coef * v[i + 1];
+          }
+          float r0, r1;
+          pk[(i - i8) / 2] = pack2<__half>(x0, x1, r0, r1);
         }
-        float r0, r1;
-        packed[i / 2] = pack2<__half>(x0, x1, r0, r1);
-      }
-      if (row_ok) {
-        uint4* dst = reinterpret_cast<uint4*>(prow + c0);
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+        if (row_ok) dst[i8 / 8] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
     }
   }

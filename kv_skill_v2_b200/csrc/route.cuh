@@ -58,6 +58,63 @@ __global__ void __launch_bounds__(256) route_logits_kernel(const float* __restri
   if (lane == 0) logit[row * C + c] = d * temp;
 }
 
+// Routing logits for many rows per Library (prefill): one CTA computes a 32-row x 64-chunk tile of
+// logit = (q . S) * temp with both operands staged in shared memory in 32-column slices, so q and S are read
+// once per tile instead of once per (row, chunk) dot. 256 threads, each 2 rows x 4 chunks in fp32 FMA.
+constexpr int RT_ROWS = 32, RT_CH = 64, RT_K = 32;
+__global__ void __launch_bounds__(256) route_logits_tiled_kernel(const float* __restrict__ q, int64_t n_rows, int d_s,
+                                                                const float* __restrict__ S, int C,
+                                                                const int32_t* __restrict__ n_chunks_of,
+                                                                int64_t rows_per_lib, float temp,
+                                                                float* __restrict__ logit) {
+  __shared__ float qs[RT_ROWS][RT_K + 1];
+  __shared__ float ss[RT_CH][RT_K + 1];
+  const int64_t lib = blockIdx.z;
+  const int64_t r0 = lib * rows_per_lib + (int64_t)blockIdx.x * RT_ROWS;  // first row of the tile
+  int64_t r_lim = lib * rows_per_lib + rows_per_lib;
+  if (r_lim > n_rows) r_lim = n_rows;
+  const int c0 = blockIdx.y * RT_CH;
+  const int nc = n_chunks_of ? min(n_chunks_of[lib], C) : C;
+  const int tr = threadIdx.x >> 4;  // 0..15 -> rows tr, tr + 16
+  const int tc = threadIdx.x & 15;  // 0..15 -> chunks tc + 16 j
+  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  const float* Sl = S + lib * (int64_t)C * d_s;
+  for (int k0 = 0; k0 < d_s; k0 += RT_K) {
+    for (int i = threadIdx.x; i < RT_ROWS * RT_K; i += blockDim.x) {
+      const int rr = i / RT_K, kk = i - rr * RT_K;
+      const int64_t row = r0 + rr;
+      qs[rr][kk] = (row < r_lim && k0 + kk < d_s) ? __ldg(q + row * d_s + k0 + kk) : 0.f;
+    }
+    for (int i = threadIdx.x; i < RT_CH * RT_K; i += blockDim.x) {
+      const int cc = i / RT_K, kk = i - cc * RT_K;
+      const int c = c0 + cc;
+      ss[cc][kk] = (c < nc && k0 + kk < d_s) ? __ldg(Sl + (int64_t)c * d_s + k0 + kk) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < RT_K; ++kk) {
+      const float a0 = qs[tr][kk], a1 = qs[tr + 16][kk];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float b = ss[tc + 16 * j][kk];
+        acc[0][j] = fmaf(a0, b, acc[0][j]);
+        acc[1][j] = fmaf(a1, b, acc[1][j]);
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int64_t row = r0 + tr + 16 * i;
+    if (row >= r_lim) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = c0 + tc + 16 * j;
+      if (c < C) logit[row * C + c] = c < nc ? acc[i][j] * temp : -CUDART_INF_F;
+    }
+  }
+}
+
 // Warp arg-max over (value desc, index asc); returns the winner in every lane.
 __device__ __forceinline__ void warp_argmax(float& v, int& i) {
 #pragma unroll

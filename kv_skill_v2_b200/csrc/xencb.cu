@@ -165,16 +165,19 @@ size_t gemm_ws_bytes(int64_t M, int N, int K, int sms, bool convert_x) {
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 int tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dt, uint32_t esize, const void* base, uint64_t inner,
-                  uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer);
+                  uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                  CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B);
 
 int tensor_map_f32_2d(CUtensorMap* map, const float* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
                       uint32_t box_outer) {
   return tensor_map_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, inner, outer, inner * 4, box_inner, box_outer);
 }
 
-// A 2-D tensor map with 128-byte swizzle (the canonical UMMA operand layout), OOB elements filled with zeros.
+// A 2-D tensor map with 128- or 64-byte swizzle (the canonical UMMA operand layouts), OOB elements filled with
+// zeros.
 int tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dt, uint32_t esize, const void* base, uint64_t inner,
-                  uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+                  uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                  CUtensorMapSwizzle swz) {
   if (!g_encode) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g_encode) {
@@ -192,7 +195,7 @@ int tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dt, uint32_t esize, cons
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t es[2] = {1, 1};
   const CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box,
-                              es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(XENCB_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return XENCB_OK;
@@ -438,6 +441,23 @@ int plan_multi(int64_t n_rows, int64_t rows_per_lib, int n_chunks, int d_s, int 
 }
 
 
+// Routing logits: a warp per (row, chunk) dot for decode; shared-memory tiles when a Library has many rows.
+using rc_t = int;
+rc_t launch_route_logits(const float* q, int64_t n_rows, int d_s, const float* S, int C, const int32_t* n_chunks_of,
+                         int64_t rows_per_lib, float temp, float* logit, cudaStream_t st) {
+  if (rows_per_lib >= 64) {
+    const int64_t libs = (n_rows + rows_per_lib - 1) / rows_per_lib;
+    dim3 grid((unsigned)((rows_per_lib + RT_ROWS - 1) / RT_ROWS), (unsigned)((C + RT_CH - 1) / RT_CH), (unsigned)libs);
+    route_logits_tiled_kernel<<<grid, 256, 0, st>>>(q, n_rows, d_s, S, C, n_chunks_of, rows_per_lib, temp, logit);
+    XENCB_CHECK_LAUNCH("route_logits_tiled launch");
+    return XENCB_OK;
+  }
+  const int64_t blocks = (n_rows * C + 7) / 8;
+  route_logits_kernel<<<(unsigned)blocks, 256, 0, st>>>(q, n_rows, d_s, S, C, n_chunks_of, rows_per_lib, temp, logit);
+  XENCB_CHECK_LAUNCH("route_logits launch");
+  return XENCB_OK;
+}
+
 }  // namespace
 }  // namespace xencb
 
@@ -567,11 +587,8 @@ int xencb_route(const float* q, int64_t n_rows, int d_s, const float* S, int n_c
   // logits go to logit_out when given, else to w_dense, which the top-k pass then overwrites row by row
   float* lg = logit_out ? logit_out : w_dense;
   if (!lg) return fail(XENCB_EINVAL, "route: one of w_dense / logit_out must be given (logit buffer)");
-  const int64_t warps = n_rows * n_chunks;
-  const int64_t blocks = (warps + 7) / 8;
-  route_logits_kernel<<<(unsigned)blocks, 256, 0, st>>>(q, n_rows, d_s, S, n_chunks, n_chunks_of, rows_per_lib,
-                                                        route_temp, lg);
-  XENCB_CHECK_LAUNCH("route_logits launch");
+  rc_t rl = launch_route_logits(q, n_rows, d_s, S, n_chunks, n_chunks_of, rows_per_lib, route_temp, lg, st);
+  if (rl) return rl;
   const int smem = n_chunks * 4 * TOPK_WARPS;
   int rc = ensure_smem(route_topk_kernel, smem > 48 * 1024 ? smem : 48 * 1024);
   if (rc) return rc;
@@ -784,10 +801,8 @@ int xencb_route_lse(const float* q, int64_t n_rows, int d_s, const float* S, int
   if ((n_rows + rows_per_lib - 1) / rows_per_lib > n_lib)
     return fail(XENCB_EINVAL, "route_lse: %lld rows need more than %lld Libraries", (long long)n_rows, (long long)n_lib);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int64_t blocks = (n_rows * n_chunks + 7) / 8;
-  route_logits_kernel<<<(unsigned)blocks, 256, 0, st>>>(q, n_rows, d_s, S, n_chunks, n_chunks_of, rows_per_lib,
-                                                        route_temp, w_out);
-  XENCB_CHECK_LAUNCH("route_logits launch");
+  rc_t rl = launch_route_logits(q, n_rows, d_s, S, n_chunks, n_chunks_of, rows_per_lib, route_temp, w_out, st);
+  if (rl) return rl;
   route_lse_kernel<<<(unsigned)((n_rows + 3) / 4), 128, 0, st>>>(w_out, n_rows, n_chunks, n_chunks_of, rows_per_lib,
                                                                  header_out);
   XENCB_CHECK_LAUNCH("route_lse launch");
@@ -846,9 +861,10 @@ int xencb_read_prefill(const float* q, int64_t n_rows, int d_s, const void* slot
   const int b_box_rows = a.ncol < 256 ? a.ncol : 256;
   CUtensorMap mq, mk1, mp, mk2;
   int rc = tensor_map_2d(&mq, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q16, (uint64_t)d_s, (uint64_t)n_rows,
-                         (uint64_t)d_s * 2, PF_BK, PF_BM);
+                         (uint64_t)d_s * 2, PF_S_BK, PF_BM, CU_TENSOR_MAP_SWIZZLE_64B);
   if (!rc) rc = tensor_map_2d(&mk1, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, slots, (uint64_t)d_s,
-                              (uint64_t)(n_pages * page_rows), (uint64_t)d_s * 2, PF_BK, (uint32_t)b_box_rows);
+                              (uint64_t)(n_pages * page_rows), (uint64_t)d_s * 2, PF_S_BK, (uint32_t)b_box_rows,
+                              CU_TENSOR_MAP_SWIZZLE_64B);
   if (!rc) rc = tensor_map_2d(&mp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.P, (uint64_t)n_chunks * a.ncol,
                               (uint64_t)n_rows, (uint64_t)n_chunks * a.ncol * 2, PF_BK, PF_BM);
   if (!rc) rc = tensor_map_2d(&mk2, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, slots, (uint64_t)d_s,
@@ -863,8 +879,8 @@ int xencb_read_prefill(const float* q, int64_t n_rows, int d_s, const void* slot
   XENCB_CHECK_LAUNCH("to_f16 launch");
   const int64_t libs_used = (n_rows + rows_per_lib - 1) / rows_per_lib;
   const unsigned tiles = (unsigned)((rows_per_lib + PF_BM - 1) / PF_BM);
-  prefill_scores_kernel<<<dim3(tiles, (unsigned)n_chunks, (unsigned)libs_used), PF_THREADS, PF_S_SMEM, st>>>(mq, mk1, a,
-                                                                                                           b_box_rows);
+  prefill_scores_kernel<<<dim3(tiles, (unsigned)n_chunks, (unsigned)libs_used), PF_S_THREADS, PF_S_SMEM, st>>>(
+      mq, mk1, a, b_box_rows);
   XENCB_CHECK_LAUNCH("prefill_scores launch");
   prefill_read_kernel<<<dim3(tiles, (unsigned)((d_s + PF_R_BN - 1) / PF_R_BN), (unsigned)libs_used), PF_THREADS,
                         PF_R_SMEM, st>>>(mp, mk2, a);

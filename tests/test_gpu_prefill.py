@@ -108,3 +108,27 @@ def test_prefill_config3_shapes_sample(dev):
     ref = X.read(q[idx.to(dev)].cpu().numpy(), K, M, w[idx.to(dev)].cpu().numpy(), 12.0, True)
     assert rel_err(r[idx.to(dev)], ref) < TOL
     assert ops.device_status(dev) == 0
+
+
+def test_route_logits_tiled_for_many_rows(dev):
+    """Libraries with >= 64 rows take the shared-memory-tiled logits kernel; its logits, weights and index sets
+    match the oracle's routing (xenc/injector.py:220-229), with chunk counts per Library."""
+    from kv_skill_v2_b200 import ops
+    from tests._fixtures import topk_sets
+    g = torch.Generator().manual_seed(12)
+    n_lib, T, C, d = 3, 150, 70, 96
+    S = torch.nn.functional.normalize(torch.randn(n_lib, C, d, generator=g), dim=-1)
+    q = torch.nn.functional.normalize(torch.randn(n_lib * T, d, generator=g), dim=-1)
+    nco = [70, 33, 64]
+    for top_k in (0, 4):
+        idx, wk, w, lg = ops.route(q.to(dev), S.to(dev), rows_per_lib=T, top_k=top_k, route_temp=10.0,
+                                   n_chunks_of=torch.tensor(nco, dtype=torch.int32, device=dev), want_logits=True)
+        for lib in range(n_lib):
+            rows = slice(lib * T, lib * T + T)
+            nc = nco[lib]
+            ref_l = (q[rows].numpy() @ S[lib, :nc].numpy().T) * 10.0
+            assert rel_err(lg[rows, :nc], ref_l) < 1e-5
+            assert torch.isinf(lg[rows, nc:]).all()
+            wo, _, _ = X.route(q[rows].numpy(), S[lib, :nc].numpy(), 10.0, top_k)
+            assert topk_sets(w[rows, :nc]) == topk_sets(wo)
+            assert rel_err(w[rows, :nc], wo) < 1e-5
