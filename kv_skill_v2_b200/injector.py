@@ -272,8 +272,11 @@ class XEncInjector(ExternalSkillInjector):
 
 class LibraryInjector(XEncInjector):
     def __init__(self, model, interface, read_softmax: bool = True, read_temp: float = 12.0, route_temp: float = 10.0,
-                 top_k: int = 0, selector=None, read_fp32: bool = True, slot_dtype="auto"):
+                 top_k: int = 0, selector=None, read_fp32: bool = True, slot_dtype="auto", cuda_graphs: bool = True):
         self.lib = None
+        # per-(layer, shape) CUDA graphs of the fused hook path (see _run_lib); cleared whenever the Library changes
+        self.cuda_graphs = bool(cuda_graphs)
+        self._graphs: dict = {}
         self.route_temp = float(route_temp)
         self.top_k = int(top_k)
         self.selector = selector
@@ -292,9 +295,11 @@ class LibraryInjector(XEncInjector):
     # ------------------------------------------------------------------ load / unload
     def load(self, skill: KVSkill) -> None:
         self.lib = None
+        self._graphs.clear()
         super().load(skill)
 
     def load_library(self, lib) -> None:
+        self._graphs.clear()
         if lib.d_s != self.itf.d_s:
             raise ValueError(f"library d_s={lib.d_s} (encoder) != interface d_s={self.itf.d_s}")
         missing = set(self.itf.inject_layers) - set(lib.K)
@@ -321,6 +326,7 @@ class LibraryInjector(XEncInjector):
         self.lib = lib
 
     def unload(self) -> None:
+        self._graphs.clear()
         self.skill = None
         self.lib = None
         self.mag_terms.clear()
@@ -406,7 +412,41 @@ class LibraryInjector(XEncInjector):
         rel = d.float().norm(dim=-1) / (h.float().norm(dim=-1) + 1e-6)
         return h + d, rel
 
+    def _graphable(self, h: torch.Tensor, inject: bool, sel) -> bool:
+        """The fused hook path can be replayed from a CUDA graph: injection, no selector (its weights change per
+        forward), a fast interface, no calibration or position mask, no grad, not inside a user's capture."""
+        return (self.cuda_graphs and inject and sel is None and self._fast_interface() and h.is_cuda
+                and self.calib is None and self.pos_mask is None and not torch.is_grad_enabled()
+                and not torch.cuda.is_current_stream_capturing())
+
     def _run_lib(self, h: torch.Tensor, li: int, inject: bool, sel: Optional[LayerSelector]):
+        if self.force_attn is not None or self.record_attn or self.training_attn:
+            raise NotImplementedError("force_attn / record_attn / training_attn diagnostics are not served by the "
+                                      "xencb read")
+        if not self._graphable(h, inject, sel):
+            return self._run_lib_eager(h, li, inject, sel)
+        # CUDA-graph replay: the first call for a (layer, shape, dtype, Library view) runs eagerly (which also
+        # validates and sizes the workspaces), then captures the same launches on static buffers; later calls
+        # copy h in, replay, and return copies of the static outputs (so a caller may keep them).
+        pages = self._pages(li, h)
+        key = (li, tuple(h.shape), h.dtype, h.device, id(pages), float(self.gain_scale), self.top_k,
+               float(self.read_temp), float(self.route_temp), bool(self.read_softmax))
+        ent = self._graphs.get(key)
+        if ent is None:
+            out = self._run_lib_eager(h, li, inject, sel)
+            h_static = h.detach().clone()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                h_new_s, rel_s = self._run_lib_eager(h_static, li, inject, sel)
+            self._graphs[key] = (graph, h_static, h_new_s, rel_s, self.last_route, pages)
+            return out
+        graph, h_static, h_new_s, rel_s, route_s, _ = ent
+        h_static.copy_(h)
+        graph.replay()
+        self.last_route = route_s
+        return h_new_s.clone(), rel_s.clone()
+
+    def _run_lib_eager(self, h: torch.Tensor, li: int, inject: bool, sel: Optional[LayerSelector]):
         if self.force_attn is not None or self.record_attn or self.training_attn:
             raise NotImplementedError("force_attn / record_attn / training_attn diagnostics are not served by the "
                                       "xencb read")

@@ -428,3 +428,41 @@ def test_config2_properties(dev):
     # a chunk read is a convex combination of unit rows: norm <= 1
     assert (parts[0].norm(dim=-1) <= 1.0 + 1e-4).all()
     _status_clean(dev)
+
+
+def test_injector_cuda_graph_cache(dev):
+    """The hook path replayed from a CUDA graph gives the eager path's results; outputs of successive forwards
+    stay independent; changing the Library or a scalar the graph captured re-captures."""
+    from kv_skill_v2_b200 import LibraryInjector, LinearInterface, PagedLibrary, ops
+    g = torch.Generator().manual_seed(21)
+    B, C, N, d_s, d_m = 4, 6, 64, 128, 256
+    K = torch.nn.functional.normalize(torch.randn(B * C, N, d_s, generator=g), dim=-1).half().to(dev)
+    po = torch.arange(B * C, dtype=torch.int32, device=dev).view(B, C)
+    nv = torch.full((B, C), N, dtype=torch.int32, device=dev)
+    plib = PagedLibrary({1: ops.Pages(slots=K, page_of=po, n_valid=nv, S=ops.summaries(K, po, nv))})
+    itf = LinearInterface(torch.randn(d_m, d_s, generator=g) * 0.05, torch.randn(d_s, d_m, generator=g) * 0.05,
+                          [1]).to(dev).requires_grad_(False)
+    reader = TinyReader(d_m, 3).to(dev).eval().requires_grad_(False)
+    xs = [torch.randn(B, 1, d_m, generator=g).to(dev) for _ in range(3)]
+    outs = {}
+    for graphs in (False, True):
+        inj = LibraryInjector(reader, itf, top_k=2, cuda_graphs=graphs)
+        inj.load_library(plib)
+        with torch.no_grad():
+            outs[graphs] = [reader(x) for x in xs]
+            if graphs:
+                assert len(inj._graphs) == 1
+                inj.gain_scale = 0.5
+                half = reader(xs[0])
+                assert len(inj._graphs) == 2
+                inj.gain_scale = 1.0
+                inj.load_library(plib)
+                assert len(inj._graphs) == 0
+                again = reader(xs[1])
+        inj.detach()
+    for a, b in zip(outs[False], outs[True]):
+        assert torch.allclose(a, b, rtol=0, atol=1e-6)
+    assert not torch.allclose(outs[True][0], outs[True][1])
+    assert torch.allclose(again, outs[False][1], rtol=0, atol=1e-6)
+    assert not torch.allclose(half, outs[True][0])
+    _status_clean(dev)
