@@ -143,12 +143,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Wait until the phase with parity `parity` of `bar` completed. Returns false (and flags the device status)
 // if it did not happen within XENCB_WAIT_NS; the caller must then stop using the pipeline.
+// The retries pass a suspend-time hint, so a waiting thread sleeps in the barrier instead of spinning, and the
+// clock is read only every 16th retry: a warp waiting here takes almost no issue slots from working warps.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > XENCB_WAIT_NS) {
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if ((it & 15u) == 0u && globaltimer_ns() - t0 > XENCB_WAIT_NS) {
       flag_error(XENCB_DEV_TIMEOUT);
       return false;
     }

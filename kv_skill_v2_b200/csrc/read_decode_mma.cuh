@@ -24,6 +24,7 @@ namespace xencb {
 
 constexpr int RM_TILES = 16;      // upper bound of the 16-column k-tiles per consumer warp (TPW <= RM_TILES)
 constexpr int RM_MAX_WARPS = 16;  // consumer warps per CTA
+constexpr int RM_RED_STRIDE = 20;  // floats per row of the cross-warp score buffer (>= RM_MAX_WARPS, 16-byte rows)
 
 struct __align__(16) StageMeta {
   long long item;
@@ -36,7 +37,7 @@ constexpr int RM_FIRST = 1, RM_LAST = 2, RM_DONE = 4;
 __host__ __device__ inline size_t rm_smem_bytes(int n_stage, int stage_bytes, int ncw, int tpw) {
   return (size_t)n_stage * stage_bytes           // stages
          + (size_t)ncw * 2 * tpw * 4 * 2 * 4       // q fragments
-         + 2 * (size_t)ncw * 16 * 4                 // cross-warp partial scores
+         + 2 * (size_t)16 * RM_RED_STRIDE * 4       // cross-warp partial scores [2][16 rows][stride]
          + (size_t)n_stage * sizeof(StageMeta)      // stage descriptors
          + (2 * (size_t)n_stage + 2) * 8            // full / empty / two score barriers
          + 16;                                      // abort flag
@@ -51,8 +52,8 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
   const int stage_bytes = ((a.rps * row_stride + 127) / 128) * 128;
   unsigned char* stages = smem;
   uint32_t* qfrag = reinterpret_cast<uint32_t*>(smem + (size_t)a.n_stage * stage_bytes);  // [ncw][2][TPW][4][2]
-  float* red = reinterpret_cast<float*>(qfrag + ncw * 2 * TPW * 4 * 2);                   // [2][ncw][16]
-  StageMeta* meta = reinterpret_cast<StageMeta*>(red + 2 * ncw * 16);
+  float* red = reinterpret_cast<float*>(qfrag + ncw * 2 * TPW * 4 * 2);  // [2][16 rows][RM_RED_STRIDE]
+  StageMeta* meta = reinterpret_cast<StageMeta*>(red + 2 * 16 * RM_RED_STRIDE);
   uint64_t* full = reinterpret_cast<uint64_t*>(meta + a.n_stage);
   uint64_t* empty = full + a.n_stage;
   uint64_t* sbar = empty + a.n_stage;  // [2] partial scores of a group are complete
@@ -63,6 +64,8 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
     const int n16 = a.n_stage * stage_bytes / 16;
     for (int i = threadIdx.x; i < n16; i += blockDim.x) z[i] = make_uint4(0u, 0u, 0u, 0u);
     fence_proxy_async_smem();  // the zeros precede the bulk copies into the same bytes
+    // score slots of warps >= ncw are never written: they stay 0 for the vector sum
+    for (int i = threadIdx.x; i < 2 * 16 * RM_RED_STRIDE; i += blockDim.x) red[i] = 0.f;
   }
   if (threadIdx.x == 0) {
     for (int i = 0; i < a.n_stage; ++i) {
@@ -210,10 +213,10 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
       float srow;
       if (ncw > 1) {
         const int b = grp & 1;
-        float* rb = red + b * ncw * 16;
+        float* rb = red + b * 16 * RM_RED_STRIDE;
         if ((lane & 3) == 0) {
-          rb[cw * 16 + (lane >> 2)] = sc_lo;
-          rb[cw * 16 + (lane >> 2) + 8] = sc_hi;
+          rb[(lane >> 2) * RM_RED_STRIDE + cw] = sc_lo;
+          rb[((lane >> 2) + 8) * RM_RED_STRIDE + cw] = sc_hi;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sbar[b]);
@@ -223,7 +226,13 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
           break;
         }
         srow = 0.f;
-        for (int w = 0; w < ncw; ++w) srow += rb[w * 16 + prow];
+        // the row's partials are contiguous: four 16-byte loads (rows 80 bytes apart: conflict-free), a tree sum
+        const float4* rr = reinterpret_cast<const float4*>(rb + prow * RM_RED_STRIDE);
+        float4 v4[RM_MAX_WARPS / 4];
+#pragma unroll
+        for (int j = 0; j < RM_MAX_WARPS / 4; ++j) v4[j] = 4 * j < ncw ? rr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+        srow = ((v4[0].x + v4[0].y) + (v4[0].z + v4[0].w)) + ((v4[1].x + v4[1].y) + (v4[1].z + v4[1].w)) +
+               (((v4[2].x + v4[2].y) + (v4[2].z + v4[2].w)) + ((v4[3].x + v4[3].y) + (v4[3].z + v4[3].w)));
       } else {
         const float v_lo = __shfl_sync(0xffffffffu, sc_lo, (prow & 7) * 4);
         const float v_hi = __shfl_sync(0xffffffffu, sc_hi, (prow & 7) * 4);
