@@ -441,34 +441,174 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
 // (log2-domain log-sum-exp) and weighted by w[row, c]. Because the merge of a chunk's pieces is a weighted sum
 // with per-(piece, query) coefficients w_c 2^(m_p - M) / L that do not depend on the column, every output is
 //     r[q][d] = sum_src coef[src][q] * data[src][q][d]        (coef = 1 for fold slots)
-// Grid (n_groups, ceil(d_s / 128), MM_SQ); block = 8 warps, lane = one float4 of columns. Each block: warp 0
-// compacts the group's open slots (unit order) and cuts them into runs of one chunk; the warps compute the runs'
-// coefficients into shared memory; then the block's quarter of the sources is summed (warps split the sources,
-// each lane keeps 8 float4 accumulators) and reduced in shared memory into a block partial. The last block of
-// a (group, column slab) adds the MM_SQ partials in a fixed order and writes r. The per-slab counters are
-// zeroed by read_multi_mma_kernel (stream order) and re-armed by the last block.
+// Two kernels:
+//   read_multi_coef_kernel (one CTA per group): warp 0 compacts the group's fold slots and open slots (unit
+//     order) and cuts the open slots into runs of one chunk; the threads compute the runs' coefficients; the
+//     result is the group's source list (float offset + 8 coefficients per source);
+//   read_multi_sum_kernel (grid groups x 128-column slabs x MM_SQ): each CTA sums its share of the sources with
+//     float4 loads (warps split the sources, lane = 4 columns, 8 float4 accumulators) into a block partial; the
+//     last CTA of a (group, slab) adds the MM_SQ partials in a fixed order and writes r. The per-slab counters
+//     are zeroed by read_multi_mma_kernel (stream order) and re-armed by the last CTA.
 constexpr int MM_MERGE_THREADS = 256;
 constexpr int MM_MERGE_WARPS = MM_MERGE_THREADS / 32;
-constexpr int MM_SQ = 4;                  // source splits per (group, slab)
+constexpr int MM_SQ = 8;                  // source splits per (group, slab)
 constexpr int MM_MERGE_MAX_CTAS = 160;    // read grids up to this many CTAs (static shared memory < 48 KB)
 constexpr int MM_MERGE_MAX_SLOTS = 2 * MM_MERGE_MAX_CTAS;
+constexpr int MM_SRC_PER_CTA = 3;         // sources per read CTA at most: one fold slot + two open slots
 
 struct MultiMergeArgs {
-  float* part;     // [n_groups][n_slabs][MM_SQ][MQ][128]
-  int* counter;    // [n_groups][n_slabs]
+  float* part;        // [n_groups][n_slabs][MM_SQ][MQ][128]
+  int* counter;       // [n_groups][n_slabs]
+  int64_t* src_off;   // [n_groups][MM_SRC_PER_CTA * grid]: float offset from a.fold (>= 0) or ~offset from a.open
+  float* src_coef;    // [n_groups][MM_SRC_PER_CTA * grid][MQ]
+  int* src_count;     // [n_groups]
   int n_slabs;
 };
 
 template <bool SOFTMAX>
-__global__ void __launch_bounds__(MM_MERGE_THREADS, 2) read_multi_merge_kernel(const MultiArgs a, int grid,
-                                                                               MultiMergeArgs mm,
-                                                                               float* __restrict__ r_out) {
+__global__ void __launch_bounds__(MM_MERGE_THREADS) read_multi_coef_kernel(const MultiArgs a, int grid,
+                                                                           MultiMergeArgs mm) {
   __shared__ int slot_of[MM_MERGE_MAX_SLOTS];
   __shared__ int run_start[MM_MERGE_MAX_SLOTS + 1];
-  __shared__ float coef[MM_MERGE_MAX_SLOTS][MQ];
   __shared__ int fold_of[MM_MERGE_MAX_CTAS];
-  __shared__ int n_open, n_runs, n_fold, is_last;
+  __shared__ int n_open, n_runs, n_fold;
+  const int64_t g = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t lib = g / a.q_blocks;
+  const int64_t row0 = lib * a.rows_per_lib + (g - lib * a.q_blocks) * MQ;
+  int64_t row_lim = lib * a.rows_per_lib + a.rows_per_lib;
+  if (row_lim > a.n_rows) row_lim = a.n_rows;
+  const int nq = (int)(row_lim - row0 < MQ ? row_lim - row0 : MQ);
+  const int cap = MM_SRC_PER_CTA * grid;
+  int64_t* so = mm.src_off + g * cap;
+  float* sc = mm.src_coef + g * cap * MQ;
+  if (nq <= 0) {
+    if (threadIdx.x == 0) mm.src_count[g] = 0;
+    return;
+  }
+  const int64_t b0 = mq_cta_of(g * a.units_per_group, a.n_units, grid);
+  const int64_t b1 = mq_cta_of((g + 1) * a.units_per_group - 1, a.n_units, grid);
+  const int n_cta = (int)(b1 - b0 + 1);
+  // every slot's info in one parallel pass (independent loads), then warp 0 scans shared memory
+  __shared__ int64_t oinfo_s[MM_MERGE_MAX_SLOTS];
+  __shared__ unsigned char fok_s[MM_MERGE_MAX_CTAS];
+  for (int i = threadIdx.x; i < n_cta; i += blockDim.x) {
+    const int64_t b = b0 + i;
+    const int64_t seg = g - mq_unit_begin(b, a.n_units, grid) / a.units_per_group;
+    fok_s[i] = (seg >= 0 && seg < a.s_max && a.fold_info[b * a.s_max + seg] == g) ? 1 : 0;
+  }
+  for (int i = threadIdx.x; i < 2 * n_cta; i += blockDim.x) oinfo_s[i] = a.open_info[b0 * 2 + i];
+  __syncthreads();
+  if (warp == 0) {
+    int cnt = 0;
+    for (int base = 0; base < n_cta; base += 32) {
+      const int i = base + lane;
+      const bool mine = i < n_cta && fok_s[i];
+      const unsigned m = __ballot_sync(0xffffffffu, mine);
+      if (mine) fold_of[cnt + __popc(m & ((1u << lane) - 1u))] = i;
+      cnt += __popc(m);
+    }
+    int oc = 0;
+    for (int base = 0; base < 2 * n_cta; base += 32) {
+      const int i = base + lane;
+      const bool mine = i < 2 * n_cta && oinfo_s[i] >= 0 && oinfo_s[i] / a.n_chunks == g;
+      const unsigned m = __ballot_sync(0xffffffffu, mine);
+      if (mine) slot_of[oc + __popc(m & ((1u << lane) - 1u))] = i;  // index into oinfo_s (slot b0 * 2 + i)
+      oc += __popc(m);
+    }
+    __syncwarp();
+    int nr = 0;
+    for (int base = 0; base < oc; base += 32) {
+      const int i = base + lane;
+      bool start = false;
+      if (i < oc) start = i == 0 || oinfo_s[slot_of[i]] != oinfo_s[slot_of[i - 1]];
+      const unsigned m = __ballot_sync(0xffffffffu, start);
+      if (start) run_start[nr + __popc(m & ((1u << lane) - 1u))] = i;
+      nr += __popc(m);
+    }
+    if (lane == 0) {
+      run_start[nr] = oc;
+      n_fold = cnt;
+      n_open = oc;
+      n_runs = nr;
+      mm.src_count[g] = cnt + oc;
+    }
+  }
+  __syncthreads();
+  // fold sources: coefficient 1
+  for (int i = threadIdx.x; i < n_fold; i += blockDim.x) {
+    const int64_t b = b0 + fold_of[i];
+    const int64_t seg = g - mq_unit_begin(b, a.n_units, grid) / a.units_per_group;
+    so[i] = (b * a.s_max + seg) * MQ * a.d_s;
+#pragma unroll
+    for (int j = 0; j < MQ; ++j) sc[(int64_t)i * MQ + j] = 1.f;
+  }
+  // open sources: the slots' (m, l) pairs and the runs' routing weights in parallel passes, then one
+  // (run, query) per thread from shared memory
+  __shared__ __align__(16) float ml_s[MM_MERGE_MAX_SLOTS][MQ_OPEN];
+  __shared__ float w_s[MM_MERGE_MAX_SLOTS][MQ];
+  {
+    // four 16-byte loads in flight per thread before any store (the (m, l) block of a slot is 64 bytes)
+    constexpr int PER = 4;
+    const int n4 = n_open * (MQ_OPEN / 4);
+    for (int base = threadIdx.x; base < n4; base += blockDim.x * PER) {
+      float4 v[PER];
+#pragma unroll
+      for (int u = 0; u < PER; ++u) {
+        const int t = base + u * blockDim.x;
+        if (t < n4) {
+          const int e = t / (MQ_OPEN / 4), k4 = t - e * (MQ_OPEN / 4);
+          v[u] = __ldcg(reinterpret_cast<const float4*>(a.open + (b0 * 2 + slot_of[e]) * (MQ_OPEN + (int64_t)MQ * a.d_s)) + k4);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < PER; ++u) {
+        const int t = base + u * blockDim.x;
+        if (t < n4) {
+          const int e = t / (MQ_OPEN / 4), k4 = t - e * (MQ_OPEN / 4);
+          reinterpret_cast<float4*>(ml_s[e])[k4] = v[u];
+        }
+      }
+    }
+  }
+  for (int t = threadIdx.x; t < n_runs * MQ; t += blockDim.x) {
+    const int rr = t / MQ, j = t - rr * MQ;
+    const int c = (int)(oinfo_s[slot_of[run_start[rr]]] - g * a.n_chunks);
+    w_s[rr][j] = j < nq ? a.w[(row0 + j) * a.n_chunks + c] : 0.f;
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < n_runs * MQ; t += blockDim.x) {
+    const int rr = t / MQ, j = t - rr * MQ;
+    const int e0 = run_start[rr], e1 = run_start[rr + 1];
+    float Mx = -CUDART_INF_F, L = 0.f;
+    for (int e = e0; e < e1; ++e) {
+      const float mp = ml_s[e][j * 2], lp = ml_s[e][j * 2 + 1];
+      if (SOFTMAX) {
+        if (lp > 0.f) {
+          const float mn = fmaxf(Mx, mp);
+          L = L * exp2f(Mx - mn) + lp * exp2f(mp - mn);
+          Mx = mn;
+        }
+      } else {
+        L += lp;
+      }
+    }
+    const float wl = (j < nq && L > 0.f) ? w_s[rr][j] / L : 0.f;
+    for (int e = e0; e < e1; ++e) {
+      float cf = 0.f;
+      if (wl != 0.f) cf = SOFTMAX ? (ml_s[e][j * 2 + 1] > 0.f ? wl * exp2f(ml_s[e][j * 2] - Mx) : 0.f) : wl;
+      sc[(int64_t)(n_fold + e) * MQ + j] = cf;
+      if (j == 0)
+        so[n_fold + e] = ~((b0 * 2 + slot_of[e]) * (MQ_OPEN + (int64_t)MQ * a.d_s) + MQ_OPEN);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(MM_MERGE_THREADS, 2) read_multi_sum_kernel(const MultiArgs a, int grid,
+                                                                             MultiMergeArgs mm,
+                                                                             float* __restrict__ r_out) {
   __shared__ float4 red[MM_MERGE_WARPS][MQ][32];
+  __shared__ int is_last;
   const int64_t g = blockIdx.x;
   const int slab = blockIdx.y, sq = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -479,114 +619,27 @@ __global__ void __launch_bounds__(MM_MERGE_THREADS, 2) read_multi_merge_kernel(c
   int64_t row_lim = lib * a.rows_per_lib + a.rows_per_lib;
   if (row_lim > a.n_rows) row_lim = a.n_rows;
   const int nq = (int)(row_lim - row0 < MQ ? row_lim - row0 : MQ);
-  if (nq <= 0) return;  // uniform per block (no counter of this group is ever armed)
-  const int64_t b0 = mq_cta_of(g * a.units_per_group, a.n_units, grid);
-  const int64_t b1 = mq_cta_of((g + 1) * a.units_per_group - 1, a.n_units, grid);
-  const int n_cta = (int)(b1 - b0 + 1);
-
-  // ---- warp 0: fold slots and open slots of this group, compacted in unit order; runs of one chunk
-  if (warp == 0) {
-    int cnt = 0;
-    for (int base = 0; base < n_cta; base += 32) {
-      const int i = base + lane;
-      bool mine = false;
-      if (i < n_cta) {
-        const int64_t b = b0 + i;
-        const int64_t seg = g - mq_unit_begin(b, a.n_units, grid) / a.units_per_group;
-        mine = seg >= 0 && seg < a.s_max && a.fold_info[b * a.s_max + seg] == g;
-      }
-      const unsigned m = __ballot_sync(0xffffffffu, mine);
-      if (mine) fold_of[cnt + __popc(m & ((1u << lane) - 1u))] = i;
-      cnt += __popc(m);
-    }
-    int oc = 0;
-    for (int base = 0; base < 2 * n_cta; base += 32) {
-      const int i = base + lane;
-      bool mine = false;
-      if (i < 2 * n_cta) {
-        const int64_t info = a.open_info[b0 * 2 + i];
-        mine = info >= 0 && info / a.n_chunks == g;
-      }
-      const unsigned m = __ballot_sync(0xffffffffu, mine);
-      if (mine) slot_of[oc + __popc(m & ((1u << lane) - 1u))] = (int)(b0 * 2 + i);
-      oc += __popc(m);
-    }
-    __syncwarp();
-    int nr = 0;
-    for (int base = 0; base < oc; base += 32) {
-      const int i = base + lane;
-      bool start = false;
-      if (i < oc) start = i == 0 || a.open_info[slot_of[i]] != a.open_info[slot_of[i - 1]];
-      const unsigned m = __ballot_sync(0xffffffffu, start);
-      if (start) run_start[nr + __popc(m & ((1u << lane) - 1u))] = i;
-      nr += __popc(m);
-    }
-    if (lane == 0) {
-      run_start[nr] = oc;
-      n_fold = cnt;
-      n_open = oc;
-      n_runs = nr;
-    }
-  }
-  __syncthreads();
-  // ---- coefficients of the open slots: one (run, query) per thread
-  for (int t = threadIdx.x; t < n_runs * MQ; t += blockDim.x) {
-    const int rr = t / MQ, j = t - rr * MQ;
-    const int e0 = run_start[rr], e1 = run_start[rr + 1];
-    float Mx = -CUDART_INF_F, L = 0.f;
-    if (j < nq) {
-      for (int e = e0; e < e1; ++e) {
-        const float* os = a.open + (int64_t)slot_of[e] * (MQ_OPEN + (int64_t)MQ * a.d_s);
-        const float mp = os[j * 2], lp = os[j * 2 + 1];
-        if (SOFTMAX) {
-          if (lp > 0.f) {
-            const float mn = fmaxf(Mx, mp);
-            L = L * exp2f(Mx - mn) + lp * exp2f(mp - mn);
-            Mx = mn;
-          }
-        } else {
-          L += lp;
-        }
-      }
-    }
-    const int c = (int)(a.open_info[slot_of[e0]] - g * a.n_chunks);
-    const float wl = (j < nq && L > 0.f) ? a.w[(row0 + j) * a.n_chunks + c] / L : 0.f;
-    for (int e = e0; e < e1; ++e) {
-      float cf = 0.f;
-      if (wl != 0.f) {
-        const float* os = a.open + (int64_t)slot_of[e] * (MQ_OPEN + (int64_t)MQ * a.d_s);
-        cf = SOFTMAX ? (os[j * 2 + 1] > 0.f ? wl * exp2f(os[j * 2] - Mx) : 0.f) : wl;
-      }
-      coef[e][j] = cf;
-    }
-  }
-  __syncthreads();
-  // ---- this block's quarter of the sources (folds first, then open slots)
-  const int ns = n_fold + n_open;
+  if (nq <= 0) return;  // uniform per (group): no counter of this group is ever armed
+  const int cap = MM_SRC_PER_CTA * grid;
+  const int64_t* so = mm.src_off + g * cap;
+  const float* sc = mm.src_coef + g * cap * MQ;
+  const int ns = mm.src_count[g];
   const int s_beg = (int)((int64_t)ns * sq / MM_SQ), s_end = (int)((int64_t)ns * (sq + 1) / MM_SQ);
   float4 acc[MQ];
 #pragma unroll
   for (int j = 0; j < MQ; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
   if (dok) {
     for (int si = s_beg + warp; si < s_end; si += MM_MERGE_WARPS) {
-      const float* base;
-      const float* cf = nullptr;
-      if (si < n_fold) {
-        const int64_t b = b0 + fold_of[si];
-        const int64_t seg = g - mq_unit_begin(b, a.n_units, grid) / a.units_per_group;
-        base = a.fold + (b * a.s_max + seg) * MQ * a.d_s;
-      } else {
-        const int e = si - n_fold;
-        base = a.open + (int64_t)slot_of[e] * (MQ_OPEN + (int64_t)MQ * a.d_s) + MQ_OPEN;
-        cf = coef[e];
-      }
+      const int64_t off = so[si];
+      const float* base = off >= 0 ? a.fold + off : a.open + ~off;
+      const float* cf = sc + (int64_t)si * MQ;
       float4 v[MQ];
 #pragma unroll
       for (int j = 0; j < MQ; ++j)
         v[j] = j < nq ? *reinterpret_cast<const float4*>(base + (int64_t)j * a.d_s + d) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
       for (int j = 0; j < MQ; ++j) {
-        const float k = cf ? cf[j] : 1.f;
+        const float k = cf[j];
         acc[j].x = fmaf(k, v[j].x, acc[j].x);
         acc[j].y = fmaf(k, v[j].y, acc[j].y);
         acc[j].z = fmaf(k, v[j].z, acc[j].z);
@@ -597,7 +650,6 @@ __global__ void __launch_bounds__(MM_MERGE_THREADS, 2) read_multi_merge_kernel(c
 #pragma unroll
   for (int j = 0; j < MQ; ++j) red[warp][j][lane] = acc[j];
   __syncthreads();
-  // block partial: thread t -> (query t / 32, float4 t % 32)
   const int64_t pbase = ((g * mm.n_slabs + slab) * MM_SQ) * (int64_t)(MQ * 128);
   {
     const int j = threadIdx.x >> 5;

@@ -379,9 +379,13 @@ struct MultiPlan {
   int tpw, ncw, threads, rps, row_bytes, row_stride, n_stage, grid, pieces, piece_rows, s_max, q_blocks;
   bool split;
   int64_t n_groups, units_per_group, n_units;
-  size_t smem, fold_bytes, finfo_bytes, open_bytes, oinfo_bytes, mpart_bytes, mcount_bytes;
+  size_t smem, fold_bytes, finfo_bytes, open_bytes, oinfo_bytes, mpart_bytes, mcount_bytes, soff_bytes, scoef_bytes,
+      scount_bytes;
   int n_slabs;
-  size_t total() const { return fold_bytes + finfo_bytes + open_bytes + oinfo_bytes + mpart_bytes + mcount_bytes; }
+  size_t total() const {
+    return fold_bytes + finfo_bytes + open_bytes + oinfo_bytes + mpart_bytes + mcount_bytes + soff_bytes + scoef_bytes +
+           scount_bytes;
+  }
 };
 
 int plan_multi(int64_t n_rows, int64_t rows_per_lib, int n_chunks, int d_s, int page_rows, int dtype, MultiPlan* p) {
@@ -437,6 +441,9 @@ int plan_multi(int64_t n_rows, int64_t rows_per_lib, int n_chunks, int d_s, int 
   p->n_slabs = (d_s + 127) / 128;
   p->mpart_bytes = align_up((size_t)p->n_groups * p->n_slabs * MM_SQ * MQ * 128 * sizeof(float), 256);
   p->mcount_bytes = align_up((size_t)p->n_groups * p->n_slabs * sizeof(int), 256);
+  p->soff_bytes = align_up((size_t)p->n_groups * MM_SRC_PER_CTA * p->grid * sizeof(int64_t), 256);
+  p->scoef_bytes = align_up((size_t)p->n_groups * MM_SRC_PER_CTA * p->grid * MQ * sizeof(float), 256);
+  p->scount_bytes = align_up((size_t)p->n_groups * sizeof(int), 256);
   return XENCB_OK;
 }
 
@@ -758,6 +765,12 @@ int xencb_read_multi(const float* q, int64_t n_rows, int d_s, const void* slots,
   mm.part = reinterpret_cast<float*>(ws + p.fold_bytes + p.finfo_bytes + p.open_bytes + p.oinfo_bytes);
   mm.counter = reinterpret_cast<int*>(ws + p.fold_bytes + p.finfo_bytes + p.open_bytes + p.oinfo_bytes + p.mpart_bytes);
   mm.n_slabs = p.n_slabs;
+  {
+    char* m2 = ws + p.fold_bytes + p.finfo_bytes + p.open_bytes + p.oinfo_bytes + p.mpart_bytes + p.mcount_bytes;
+    mm.src_off = reinterpret_cast<int64_t*>(m2);
+    mm.src_coef = reinterpret_cast<float*>(m2 + p.soff_bytes);
+    mm.src_count = reinterpret_cast<int*>(m2 + p.soff_bytes + p.scoef_bytes);
+  }
   a.merge_counter = mm.counter;
   a.n_merge_counters = p.n_groups * (int64_t)p.n_slabs;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -771,9 +784,11 @@ int xencb_read_multi(const float* q, int64_t n_rows, int d_s, const void* slots,
     if (r2) return r2;
     k1<<<p.grid, p.threads, p.smem, st>>>(a);
     XENCB_CHECK_LAUNCH("read_multi_mma_kernel launch");
+    read_multi_coef_kernel<S><<<(unsigned)p.n_groups, MM_MERGE_THREADS, 0, st>>>(a, p.grid, mm);
+    XENCB_CHECK_LAUNCH("read_multi_coef_kernel launch");
     dim3 mg((unsigned)p.n_groups, (unsigned)p.n_slabs, MM_SQ);
-    read_multi_merge_kernel<S><<<mg, MM_MERGE_THREADS, 0, st>>>(a, p.grid, mm, r_out);
-    XENCB_CHECK_LAUNCH("read_multi_merge_kernel launch");
+    read_multi_sum_kernel<<<mg, MM_MERGE_THREADS, 0, st>>>(a, p.grid, mm, r_out);
+    XENCB_CHECK_LAUNCH("read_multi_sum_kernel launch");
     return XENCB_OK;
   };
   struct F16T { using type = __half; };
