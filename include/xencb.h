@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define XENCB_ABI_VERSION 1
+#define XENCB_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define XENCB_API __attribute__((visibility("default")))
@@ -117,12 +117,16 @@ XENCB_API int xencb_route(const float* q, int64_t n_rows, int d_s, const float* 
  *   r[row] = sum_j wk[row, j] * read_c(q[row]),  c = idx[row, j] (skipped when c < 0 or wk == 0),
  *   read_c(q) = softmax_n(read_temp * q . k_cn) @ K_c   over the n_valid[lib, c] rows   (read_softmax != 0)
  *             = (sum_n (q . k_cn) k_cn) / sqrt(max(n_valid, 1))                         (read_softmax == 0)
- * K = V (tied). slots_dtype XENCB_F16 / XENCB_BF16 / XENCB_F32; accumulation is float32.
+ * K = V (tied) when vslots is NULL; otherwise vslots is the untied value pool (harvest="attn", xenc/library.py:
+ * 46, 61-65; xenc/injector.py:211-218, 263-265) with the same dtype and page layout as slots: the scores use K,
+ * the weighted sum uses V (f16 / bf16 slots and d_s % 16 == 0 only, else XENCB_ENOTSUP; this applies to
+ * xencb_read_multi and xencb_read_prefill as well). slots_dtype XENCB_F16 / XENCB_BF16 / XENCB_F32;
+ * accumulation is float32.
  * page_rows bounds n_valid (checked on the device: larger values are clamped and flagged). Slot pages and q
  * must be 16-byte aligned and d_s * sizeof(slot) a multiple of 16. The chunk read is split into row
  * ranges processed by a persistent, TMA-bulk-pipelined kernel and merged by log-sum-exp into r. */
 XENCB_API size_t xencb_read_decode_workspace(int64_t n_rows, int k, int d_s, int page_rows, int slots_dtype);
-XENCB_API int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots, int slots_dtype,
+XENCB_API int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots, const void* vslots, int slots_dtype,
                       int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of, const int32_t* n_valid,
                       int n_chunks, int64_t rows_per_lib, int64_t n_lib, const int32_t* idx, const float* wk, int k,
                       float read_temp, int read_softmax, float* r_out, void* workspace, size_t workspace_bytes,
@@ -155,7 +159,7 @@ XENCB_API int xencb_read_decode_noalloc(const float* q, int64_t n_rows, int d_s,
  * n_chunks chunks). Workspace: xencb_read_multi_workspace bytes, 256-byte aligned. */
 XENCB_API size_t xencb_read_multi_workspace(int64_t n_rows, int64_t rows_per_lib, int n_chunks, int d_s, int page_rows,
                                             int slots_dtype);
-XENCB_API int xencb_read_multi(const float* q, int64_t n_rows, int d_s, const void* slots, int slots_dtype,
+XENCB_API int xencb_read_multi(const float* q, int64_t n_rows, int d_s, const void* slots, const void* vslots, int slots_dtype,
                                int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of,
                                const int32_t* n_valid, int n_chunks, const int32_t* n_chunks_of, int64_t rows_per_lib,
                                int64_t n_lib, const float* w, float read_temp, int read_softmax, float* r_out,
@@ -168,7 +172,7 @@ XENCB_API int xencb_read_multi(const float* q, int64_t n_rows, int d_s, const vo
  * (they are multiplied by 0). Other shapes return XENCB_ENOTSUP. q is rounded to f16 for the score product.
  * Workspace: xencb_read_prefill_workspace bytes (q in f16 + the f16 weights P [n_rows, n_chunks * round_up(page_rows, 64)]). */
 XENCB_API size_t xencb_read_prefill_workspace(int64_t n_rows, int n_chunks, int d_s, int page_rows);
-XENCB_API int xencb_read_prefill(const float* q, int64_t n_rows, int d_s, const void* slots, int slots_dtype,
+XENCB_API int xencb_read_prefill(const float* q, int64_t n_rows, int d_s, const void* slots, const void* vslots, int slots_dtype,
                                  int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of,
                                  const int32_t* n_valid, int n_chunks, const int32_t* n_chunks_of,
                                  int64_t rows_per_lib, int64_t n_lib, const float* w, float read_temp,

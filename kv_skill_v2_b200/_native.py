@@ -19,7 +19,7 @@ OK, EINVAL, ECUDA, ENOTSUP = 0, 1, 2, 3
 DEV_TIMEOUT, DEV_CLAMPED, DEV_BADPAGE = 1, 2, 4
 PIN_RMS, PIN_L2 = 1, 2
 NOALLOC_SCRATCH_BYTES = 16 << 20
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _p, _i, _i64, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
 
@@ -36,16 +36,16 @@ SIGNATURES: dict = {
     "xencb_route_k": (_i, [_i, _i]),
     "xencb_route": (_i, [_p, _i64, _i, _p, _i, _p, _i64, _i64, _f, _i, _p, _p, _p, _p, _p, _p]),
     "xencb_read_decode_workspace": (_sz, [_i64, _i, _i, _i, _i]),
-    "xencb_read_decode": (_i, [_p, _i64, _i, _p, _i, _i64, _i64, _i, _p, _p, _i, _i64, _i64, _p, _p, _i, _f, _i,
-                               _p, _p, _sz, _p]),
+    "xencb_read_decode": (_i, [_p, _i64, _i, _p, _p, _i, _i64, _i64, _i, _p, _p, _i, _i64, _i64, _p, _p, _i, _f,
+                               _i, _p, _p, _sz, _p]),
     "xencb_read_decode_noalloc": (_i, [_p, _i64, _i, _p, _i, _i64, _i64, _i, _p, _p, _i, _i64, _i64, _p, _p, _i,
                                        _f, _i, _p, _p]),
     "xencb_read_multi_workspace": (_sz, [_i64, _i64, _i, _i, _i, _i]),
-    "xencb_read_multi": (_i, [_p, _i64, _i, _p, _i, _i64, _i64, _i, _p, _p, _i, _p, _i64, _i64, _p, _f, _i, _p, _p,
-                              _sz, _p]),
+    "xencb_read_multi": (_i, [_p, _i64, _i, _p, _p, _i, _i64, _i64, _i, _p, _p, _i, _p, _i64, _i64, _p, _f, _i, _p,
+                              _p, _sz, _p]),
     "xencb_read_prefill_workspace": (_sz, [_i64, _i, _i, _i]),
-    "xencb_read_prefill": (_i, [_p, _i64, _i, _p, _i, _i64, _i64, _i, _p, _p, _i, _p, _i64, _i64, _p, _f, _i, _p,
-                                _p, _sz, _p]),
+    "xencb_read_prefill": (_i, [_p, _i64, _i, _p, _p, _i, _i64, _i64, _i, _p, _p, _i, _p, _i64, _i64, _p, _f, _i,
+                                _p, _p, _sz, _p]),
     "xencb_route_lse": (_i, [_p, _i64, _i, _p, _i, _p, _i64, _i64, _f, _p, _p, _p]),
     "xencb_shard_merge": (_i, [_p, _i, _i64, _i, _p, _p]),
     "xencb_project_out_workspace": (_sz, [_i64, _i, _i]),

@@ -34,6 +34,7 @@ struct ReadArgs {
   int64_t n_rows;
   int d_s;
   const char* slots;
+  const char* vslots;  // untied values (same page layout as slots), or null when V = K
   int64_t n_pages;
   int64_t page_stride_bytes;
   int page_rows;

@@ -31,7 +31,7 @@ struct __align__(16) StageMeta {
   int nr;     // rows in this stage
   int flags;  // RM_FIRST | RM_LAST | RM_DONE
 };
-constexpr int RM_FIRST = 1, RM_LAST = 2, RM_DONE = 4;
+constexpr int RM_FIRST = 1, RM_LAST = 2, RM_DONE = 4, RM_VAL = 8;  // RM_VAL: a stage of value rows (untied V)
 
 // Shared-memory bytes of the tensor-core read for a plan (the host and the kernel use the same layout).
 __host__ __device__ inline size_t rm_smem_bytes(int n_stage, int stage_bytes, int ncw, int tpw) {
@@ -97,19 +97,25 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
         if (item_next < a.n_items) { nxt = decode_item(a, item_next); have_nxt = true; }
         continue;
       }
-      for (int rs = it.r0; rs < it.r1; rs += a.rps) {
+      for (int rs = it.r0; rs < it.r1 && ok; rs += a.rps) {
         const int nr = min(a.rps, it.r1 - rs);
-        const uint32_t slot = it_count % a.n_stage, use = it_count / a.n_stage;
-        if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) { ok = false; break; }
-        meta[slot].item = item;
-        meta[slot].nr = nr;
-        meta[slot].flags = (rs == it.r0 ? RM_FIRST : 0) | (rs + nr >= it.r1 ? RM_LAST : 0);
-        mbar_arrive_expect_tx(&full[slot], (uint32_t)nr * a.row_bytes);
-        unsigned char* dst = stages + (size_t)slot * stage_bytes;
-        const char* src = it.base + (int64_t)rs * a.row_bytes;
-        for (int r = 0; r < nr; ++r)
-          bulk_g2s(dst + (size_t)r * row_stride, src + (int64_t)r * a.row_bytes, (uint32_t)a.row_bytes, &full[slot], pol);
-        ++it_count;
+        const bool last = rs + nr >= it.r1;
+        // the group's key rows, then (untied values) the same rows of the value pool as a second stage
+        for (int part = 0; part < (a.vslots ? 2 : 1); ++part) {
+          const uint32_t slot = it_count % a.n_stage, use = it_count / a.n_stage;
+          if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) { ok = false; break; }
+          meta[slot].item = item;
+          meta[slot].nr = nr;
+          meta[slot].flags = part == 0 ? ((rs == it.r0 ? RM_FIRST : 0) | (last && !a.vslots ? RM_LAST : 0))
+                                       : (RM_VAL | (last ? RM_LAST : 0));
+          mbar_arrive_expect_tx(&full[slot], (uint32_t)nr * a.row_bytes);
+          unsigned char* dst = stages + (size_t)slot * stage_bytes;
+          const char* src = (part == 0 ? it.base : a.vslots + (it.base - a.slots)) + (int64_t)rs * a.row_bytes;
+          for (int r = 0; r < nr; ++r)
+            bulk_g2s(dst + (size_t)r * row_stride, src + (int64_t)r * a.row_bytes, (uint32_t)a.row_bytes, &full[slot],
+                     pol);
+          ++it_count;
+        }
         if (!have_nxt && item_next < a.n_items) { nxt = decode_item(a, item_next); have_nxt = true; }
       }
       if (!have_nxt && item_next < a.n_items) { nxt = decode_item(a, item_next); have_nxt = true; }
@@ -147,6 +153,24 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
   float acc[TPW][4];
   float m = -CUDART_INF_F, l = 0.f;
   uint32_t it_count = 0, grp = 0;
+  uint32_t vb0 = 0u, vb1 = 0u, vc0 = 0u, vc1 = 0u;  // P fragments of the last key group (untied values)
+  auto write_partial = [&](int64_t item) {
+    float* pa = a.part_acc + item * (int64_t)a.d_s;
+    if ((lane & 3) == 0) {
+#pragma unroll
+      for (int t = 0; t < TPW; ++t) {
+        if (t < nt) {
+          const int d = d0 + t * 16 + (lane >> 2);
+          pa[d] = acc[t][0];
+          pa[d + 8] = acc[t][2];
+        }
+      }
+    }
+    if (cw == 0 && lane == 0) {
+      a.part_ml[item * 2] = SOFTMAX ? m : 0.f;
+      a.part_ml[item * 2 + 1] = SOFTMAX ? l : 1.f;
+    }
+  };
 
   while (true) {
     const uint32_t slot = it_count % a.n_stage, use = it_count / a.n_stage;
@@ -154,6 +178,24 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
     if (!mbar_wait_bounded(&full[slot], use & 1) || *abort_flag) { *abort_flag = 1; break; }
     const StageMeta md = meta[slot];
     if (md.flags & RM_DONE) break;
+
+    if (md.flags & RM_VAL) {
+      // untied values: the group's P (kept from its key stage) times these value rows
+      const uint32_t vbase = stages_u32 + slot * (uint32_t)stage_bytes;
+#pragma unroll
+      for (int t = 0; t < TPW; ++t) {
+        if (t < nt) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4_t(vbase + off_a + t * 32, a0, a1, a2, a3);
+          mma16816<T>(acc[t], a0, a1, a2, a3, vb0, vb1);
+          if (SPLIT) mma16816<T>(acc[t], a0, a1, a2, a3, vc0, vc1);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (md.flags & RM_LAST) write_partial(md.item);
+      continue;
+    }
 
     if (md.flags & RM_FIRST) {
       // q fragments (B operand, query in column 0 = lanes 0..3), hi and residual, into this warp's slot
@@ -286,6 +328,10 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
       const uint32_t pb1 = lane < 4 ? ((e8 & 0xffffu) | (e9 << 16)) : 0u;
       const uint32_t pc0 = lane < 4 ? ((e0 >> 16) | (e1 & 0xffff0000u)) : 0u;
       const uint32_t pc1 = lane < 4 ? ((e8 >> 16) | (e9 & 0xffff0000u)) : 0u;
+      if (a.vslots) {  // untied: the value stage that follows does the accumulation (one group per stage)
+        vb0 = pb0; vb1 = pb1; vc0 = pc0; vc1 = pc1;
+        continue;
+      }
       // ---- accumulate: acc[d, 0] += sum_rows K[row, d] p[row]
 #pragma unroll
       for (int t = 0; t < TPW; ++t) {
@@ -300,24 +346,7 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
     if (aborted) break;
-
-    if (md.flags & RM_LAST) {
-      float* pa = a.part_acc + md.item * (int64_t)a.d_s;
-      if ((lane & 3) == 0) {
-#pragma unroll
-        for (int t = 0; t < TPW; ++t) {
-          if (t < nt) {
-            const int d = d0 + t * 16 + (lane >> 2);
-            pa[d] = acc[t][0];
-            pa[d + 8] = acc[t][2];
-          }
-        }
-      }
-      if (cw == 0 && lane == 0) {
-        a.part_ml[md.item * 2] = SOFTMAX ? m : 0.f;
-        a.part_ml[md.item * 2 + 1] = SOFTMAX ? l : 1.f;
-      }
-    }
+    if (md.flags & RM_LAST) write_partial(md.item);
   }
 }
 

@@ -36,6 +36,7 @@ struct MultiArgs {
   int64_t n_rows;
   int d_s;
   const char* slots;
+  const char* vslots;  // untied values (same page layout), or null when V = K
   int64_t n_pages;
   int64_t page_stride_bytes;
   int page_rows;
@@ -66,6 +67,7 @@ struct __align__(16) MultiMeta {
   int c, nv, nr, flags;
 };
 constexpr int MM_FIRST = 1, MM_LAST = 2, MM_DONE = 4, MM_HEAD = 8, MM_TAIL = 16, MM_PIECE0 = 32;
+constexpr int MM_VAL = 64;  // a stage of value rows (untied V): the P of the preceding key stage times these rows
 
 __host__ __device__ inline int64_t mq_unit_begin(int64_t b, int64_t n_units, int64_t grid) {
   return b * n_units / grid;
@@ -167,22 +169,28 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
       const int r1 = min(nv, p1 * a.piece_rows);
       if (r1 <= r0) continue;
       const char* base = a.slots + page * a.page_stride_bytes;
-      for (int rs = r0; rs < r1; rs += a.rps) {
+      for (int rs = r0; rs < r1 && ok; rs += a.rps) {
         const int nr = min(a.rps, r1 - rs);
-        const uint32_t slot = it_count % a.n_stage, use = it_count / a.n_stage;
-        if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) { ok = false; break; }
-        meta[slot].g = g;
-        meta[slot].c = c;
-        meta[slot].nv = nv;
-        meta[slot].nr = nr;
-        meta[slot].flags = (rs == r0 ? MM_FIRST : 0) | (rs + nr >= r1 ? MM_LAST : 0) | (head ? MM_HEAD : 0) |
-                           (tail ? MM_TAIL : 0) | (p0 == 0 ? MM_PIECE0 : 0);
-        mbar_arrive_expect_tx(&full[slot], (uint32_t)nr * a.row_bytes);
-        unsigned char* dst = stages + (size_t)slot * stage_bytes;
-        const char* src = base + (int64_t)rs * a.row_bytes;
-        for (int r = 0; r < nr; ++r)
-          bulk_g2s(dst + (size_t)r * row_stride, src + (int64_t)r * a.row_bytes, (uint32_t)a.row_bytes, &full[slot], pol);
-        ++it_count;
+        const int visit = (head ? MM_HEAD : 0) | (tail ? MM_TAIL : 0) | (p0 == 0 ? MM_PIECE0 : 0);
+        const bool last = rs + nr >= r1;
+        // key rows, then (untied values) the same rows of the value pool as the next stage
+        for (int part = 0; part < (a.vslots ? 2 : 1); ++part) {
+          const uint32_t slot = it_count % a.n_stage, use = it_count / a.n_stage;
+          if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) { ok = false; break; }
+          meta[slot].g = g;
+          meta[slot].c = c;
+          meta[slot].nv = nv;
+          meta[slot].nr = nr;
+          meta[slot].flags = visit | (part == 0 ? ((rs == r0 ? MM_FIRST : 0) | (last && !a.vslots ? MM_LAST : 0))
+                                                : (MM_VAL | (last ? MM_LAST : 0)));
+          mbar_arrive_expect_tx(&full[slot], (uint32_t)nr * a.row_bytes);
+          unsigned char* dst = stages + (size_t)slot * stage_bytes;
+          const char* src = (part == 0 ? base : a.vslots + (base - a.slots)) + (int64_t)rs * a.row_bytes;
+          for (int r = 0; r < nr; ++r)
+            bulk_g2s(dst + (size_t)r * row_stride, src + (int64_t)r * a.row_bytes, (uint32_t)a.row_bytes,
+                     &full[slot], pol);
+          ++it_count;
+        }
       }
     }
     if (ok) {
@@ -223,6 +231,61 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
   int nq = 0;
   bool fold_any = false;
   uint32_t it_count = 0, grp = 0;
+  uint32_t vb0 = 0u, vb1 = 0u, vc0 = 0u, vc1 = 0u;  // P fragments of the last key group (untied values)
+  // end of a chunk visit: fold a complete chunk into the group's slot, or write an open slot
+  auto finish_visit = [&](const MultiMeta& md) {
+      const bool open = (md.flags & (MM_HEAD | MM_TAIL)) != 0;
+      const float inv_sqrt_n = SOFTMAX ? 1.f : 1.f / sqrtf((float)md.nv);
+      if (!open) {
+        // complete chunk: fold w * acc / l into the group's slot (each lane owns its elements, so the
+        // read-modify-write needs no synchronisation)
+        float f = 0.f;
+        if (qj < nq) {
+          const float wq = a.w[(row0 + qj) * a.n_chunks + md.c];
+          f = SOFTMAX ? (l > 0.f ? wq / l : 0.f) : wq * inv_sqrt_n;
+        }
+        const float f_a = __shfl_sync(0xffffffffu, f, qa * 4);
+        const float f_b = __shfl_sync(0xffffffffu, f, qa * 4 + 4);
+        const int64_t seg = md.g - g_first;
+        float* fs = a.fold + ((int64_t)blockIdx.x * a.s_max + seg) * MQ * a.d_s;
+        float* fa = fs + (int64_t)qa * a.d_s;
+        float* fb = fa + a.d_s;
+#pragma unroll
+        for (int t = 0; t < TPW; ++t) {
+          if (t < nt) {
+            const int d = d0 + t * 16 + rl;
+            float x0 = acc[t][0] * f_a, x1 = acc[t][1] * f_b, x2 = acc[t][2] * f_a, x3 = acc[t][3] * f_b;
+            if (fold_any) {
+              x0 += fa[d]; x1 += fb[d]; x2 += fa[d + 8]; x3 += fb[d + 8];
+            }
+            fa[d] = x0; fb[d] = x1; fa[d + 8] = x2; fb[d + 8] = x3;
+          }
+        }
+        if (!fold_any && cw == 0 && lane == 0) a.fold_info[(int64_t)blockIdx.x * a.s_max + seg] = md.g;
+        fold_any = true;
+      } else {
+        const int oslot = (md.flags & MM_HEAD) ? 0 : 1;
+        float* os = a.open + ((int64_t)blockIdx.x * 2 + oslot) * (MQ_OPEN + (int64_t)MQ * a.d_s);
+        float* oa = os + MQ_OPEN + (int64_t)qa * a.d_s;
+        float* ob = oa + a.d_s;
+#pragma unroll
+        for (int t = 0; t < TPW; ++t) {
+          if (t < nt) {
+            const int d = d0 + t * 16 + rl;
+            oa[d] = acc[t][0] * inv_sqrt_n;
+            ob[d] = acc[t][1] * inv_sqrt_n;
+            oa[d + 8] = acc[t][2] * inv_sqrt_n;
+            ob[d + 8] = acc[t][3] * inv_sqrt_n;
+          }
+        }
+        if (cw == 0 && (lane & 3) == 0) {
+          os[qj * 2] = SOFTMAX ? m : 0.f;
+          os[qj * 2 + 1] = SOFTMAX ? l : ((md.flags & MM_PIECE0) ? 1.f : 0.f);
+        }
+        if (cw == 0 && lane == 0) a.open_info[(int64_t)blockIdx.x * 2 + oslot] = md.g * a.n_chunks + md.c;
+      }
+  };
+
 
   while (true) {
     const uint32_t slot = it_count % a.n_stage, use = it_count / a.n_stage;
@@ -230,6 +293,23 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
     if (!mbar_wait_bounded(&full[slot], use & 1) || *abort_flag) { *abort_flag = 1; break; }
     const MultiMeta md = meta[slot];
     if (md.flags & MM_DONE) break;
+
+    if (md.flags & MM_VAL) {
+      const uint32_t vbase = stages_u32 + slot * (uint32_t)stage_bytes;
+#pragma unroll
+      for (int t = 0; t < TPW; ++t) {
+        if (t < nt) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4_t(vbase + off_a + t * 32, a0, a1, a2, a3);
+          mma16816<T>(acc[t], a0, a1, a2, a3, vb0, vb1);
+          if (SPLIT) mma16816<T>(acc[t], a0, a1, a2, a3, vc0, vc1);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+      if (md.flags & MM_LAST) finish_visit(md);
+      continue;
+    }
 
     if (md.flags & MM_FIRST) {
       if (md.g != cur_g) {
@@ -368,6 +448,10 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
         ps += __shfl_xor_sync(0xffffffffu, ps, 2);
         l += ps;
       }
+      if (a.vslots) {  // untied: the value stage that follows does the accumulation (one group per stage)
+        vb0 = pb0; vb1 = pb1; vc0 = pc0; vc1 = pc1;
+        continue;
+      }
 #pragma unroll
       for (int t = 0; t < TPW; ++t) {
         if (t < nt) {
@@ -381,61 +465,11 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
     if (aborted) break;
-
-    if (md.flags & MM_LAST) {
-      const bool open = (md.flags & (MM_HEAD | MM_TAIL)) != 0;
-      const float inv_sqrt_n = SOFTMAX ? 1.f : 1.f / sqrtf((float)md.nv);
-      if (!open) {
-        // complete chunk: fold w * acc / l into the group's slot (each lane owns its elements, so the
-        // read-modify-write needs no synchronisation)
-        float f = 0.f;
-        if (qj < nq) {
-          const float wq = a.w[(row0 + qj) * a.n_chunks + md.c];
-          f = SOFTMAX ? (l > 0.f ? wq / l : 0.f) : wq * inv_sqrt_n;
-        }
-        const float f_a = __shfl_sync(0xffffffffu, f, qa * 4);
-        const float f_b = __shfl_sync(0xffffffffu, f, qa * 4 + 4);
-        const int64_t seg = md.g - g_first;
-        float* fs = a.fold + ((int64_t)blockIdx.x * a.s_max + seg) * MQ * a.d_s;
-        float* fa = fs + (int64_t)qa * a.d_s;
-        float* fb = fa + a.d_s;
-#pragma unroll
-        for (int t = 0; t < TPW; ++t) {
-          if (t < nt) {
-            const int d = d0 + t * 16 + rl;
-            float x0 = acc[t][0] * f_a, x1 = acc[t][1] * f_b, x2 = acc[t][2] * f_a, x3 = acc[t][3] * f_b;
-            if (fold_any) {
-              x0 += fa[d]; x1 += fb[d]; x2 += fa[d + 8]; x3 += fb[d + 8];
-            }
-            fa[d] = x0; fb[d] = x1; fa[d + 8] = x2; fb[d + 8] = x3;
-          }
-        }
-        if (!fold_any && cw == 0 && lane == 0) a.fold_info[(int64_t)blockIdx.x * a.s_max + seg] = md.g;
-        fold_any = true;
-      } else {
-        const int oslot = (md.flags & MM_HEAD) ? 0 : 1;
-        float* os = a.open + ((int64_t)blockIdx.x * 2 + oslot) * (MQ_OPEN + (int64_t)MQ * a.d_s);
-        float* oa = os + MQ_OPEN + (int64_t)qa * a.d_s;
-        float* ob = oa + a.d_s;
-#pragma unroll
-        for (int t = 0; t < TPW; ++t) {
-          if (t < nt) {
-            const int d = d0 + t * 16 + rl;
-            oa[d] = acc[t][0] * inv_sqrt_n;
-            ob[d] = acc[t][1] * inv_sqrt_n;
-            oa[d + 8] = acc[t][2] * inv_sqrt_n;
-            ob[d + 8] = acc[t][3] * inv_sqrt_n;
-          }
-        }
-        if (cw == 0 && (lane & 3) == 0) {
-          os[qj * 2] = SOFTMAX ? m : 0.f;
-          os[qj * 2 + 1] = SOFTMAX ? l : ((md.flags & MM_PIECE0) ? 1.f : 0.f);
-        }
-        if (cw == 0 && lane == 0) a.open_info[(int64_t)blockIdx.x * 2 + oslot] = md.g * a.n_chunks + md.c;
-      }
-    }
+    if (md.flags & MM_LAST) finish_visit(md);
   }
 }
+
+
 
 // r[row] = sum of the fold slots of the CTAs covering the row's group + the open partials, merged per chunk
 // (log2-domain log-sum-exp) and weighted by w[row, c]. Because the merge of a chunk's pieces is a weighted sum

@@ -248,7 +248,7 @@ struct ReadPlan {
   int64_t n_items;
 };
 
-int plan_read(int64_t n_rows, int k, int d_s, int page_rows, int dtype, ReadPlan* p) {
+int plan_read(int64_t n_rows, int k, int d_s, int page_rows, int dtype, ReadPlan* p, bool untied = false) {
   DevInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
@@ -270,6 +270,7 @@ int plan_read(int64_t n_rows, int k, int d_s, int page_rows, int dtype, ReadPlan
     const int stride = p->row_bytes + 16;
     int rps = 64;
     while (rps > 16 && rps * stride > 69632) rps >>= 1;
+    if (untied) rps = 16;  // a key stage holds one 16-row group; its value stage follows
     const int stage_bytes = (int)align_up((size_t)rps * stride, 128);
     int n_stage = 8;
     while (n_stage >= 2 && rm_smem_bytes(n_stage, stage_bytes, mma_ncw, tpw) > budget) --n_stage;
@@ -285,6 +286,8 @@ int plan_read(int64_t n_rows, int k, int d_s, int page_rows, int dtype, ReadPlan
       p->smem = rm_smem_bytes(n_stage, stage_bytes, mma_ncw, tpw);
     }
   }
+  if (!p->mma && untied)
+    return fail(XENCB_ENOTSUP, "untied values are read by the tensor-core kernel only (f16 / bf16 slots, d_s %% 16 == 0)");
   if (!p->mma) {
     // at most 15 consumer warps (512 threads per CTA with the producer warp)
     if (p->nvec <= 15 * 32) p->vpt = 1;
@@ -388,7 +391,8 @@ struct MultiPlan {
   }
 };
 
-int plan_multi(int64_t n_rows, int64_t rows_per_lib, int n_chunks, int d_s, int page_rows, int dtype, MultiPlan* p) {
+int plan_multi(int64_t n_rows, int64_t rows_per_lib, int n_chunks, int d_s, int page_rows, int dtype, MultiPlan* p,
+               bool untied = false) {
   DevInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
@@ -404,7 +408,7 @@ int plan_multi(int64_t n_rows, int64_t rows_per_lib, int n_chunks, int d_s, int 
   p->row_bytes = d_s * 2;
   p->row_stride = p->row_bytes + 16;
   int rps = 16;
-  while (rps < 64 && 2 * rps * p->row_stride <= 36864) rps *= 2;
+  while (!untied && rps < 64 && 2 * rps * p->row_stride <= 36864) rps *= 2;  // untied: one group per key stage
   p->rps = rps;
   const int stage_bytes = (int)align_up((size_t)rps * p->row_stride, 128);
   const size_t budget = (size_t)(di.max_smem_optin > 0 ? di.max_smem_optin : 232448) - 1024;
@@ -614,7 +618,7 @@ size_t xencb_read_decode_workspace(int64_t n_rows, int k, int d_s, int page_rows
   return p.acc_bytes + p.ml_bytes;
 }
 
-int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots, int slots_dtype,
+int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots, const void* vslots, int slots_dtype,
                       int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of, const int32_t* n_valid,
                       int n_chunks, int64_t rows_per_lib, int64_t n_lib, const int32_t* idx, const float* wk, int k,
                       float read_temp, int read_softmax, float* r_out, void* workspace, size_t workspace_bytes,
@@ -634,8 +638,9 @@ int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots
                 (long long)page_rows * d_s);
   if (!aligned(slots, 16) || (page_stride * es) % 16 != 0 || !aligned(q, 16) || !aligned(r_out, 16))
     return fail(XENCB_EINVAL, "read_decode: slots, q, r_out and page_stride*elem must be 16-byte aligned");
+  if (vslots && !aligned(vslots, 16)) return fail(XENCB_EINVAL, "read_decode: vslots must be 16-byte aligned");
   ReadPlan p;
-  int rc = plan_read(n_rows, k, d_s, page_rows, slots_dtype, &p);
+  int rc = plan_read(n_rows, k, d_s, page_rows, slots_dtype, &p, vslots != nullptr);
   if (rc) return rc;
   if (!workspace || !aligned(workspace, 256) || workspace_bytes < p.acc_bytes + p.ml_bytes)
     return fail(XENCB_EINVAL, "read_decode: workspace needs %zu bytes, 256-byte aligned (got %zu)",
@@ -643,6 +648,7 @@ int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots
   ReadArgs a;
   a.q = q; a.n_rows = n_rows; a.d_s = d_s;
   a.slots = static_cast<const char*>(slots);
+  a.vslots = static_cast<const char*>(vslots);
   a.n_pages = n_pages;
   a.page_stride_bytes = page_stride * es;
   a.page_rows = page_rows;
@@ -723,7 +729,8 @@ size_t xencb_read_multi_workspace(int64_t n_rows, int64_t rows_per_lib, int n_ch
   return p.total();
 }
 
-int xencb_read_multi(const float* q, int64_t n_rows, int d_s, const void* slots, int slots_dtype, int64_t n_pages,
+int xencb_read_multi(const float* q, int64_t n_rows, int d_s, const void* slots, const void* vslots, int slots_dtype,
+                     int64_t n_pages,
                      int64_t page_stride, int page_rows, const int32_t* page_of, const int32_t* n_valid, int n_chunks,
                      const int32_t* n_chunks_of, int64_t rows_per_lib, int64_t n_lib, const float* w, float read_temp,
                      int read_softmax, float* r_out, void* workspace, size_t workspace_bytes, void* stream) {
@@ -740,8 +747,9 @@ int xencb_read_multi(const float* q, int64_t n_rows, int d_s, const void* slots,
                 (long long)page_rows * d_s);
   if (!aligned(slots, 16) || (page_stride * 2) % 16 != 0 || !aligned(q, 16) || !aligned(r_out, 16))
     return fail(XENCB_EINVAL, "read_multi: slots, q, r_out and page_stride*elem must be 16-byte aligned");
+  if (vslots && !aligned(vslots, 16)) return fail(XENCB_EINVAL, "read_multi: vslots must be 16-byte aligned");
   MultiPlan p;
-  int rc = plan_multi(n_rows, rows_per_lib, n_chunks, d_s, page_rows, slots_dtype, &p);
+  int rc = plan_multi(n_rows, rows_per_lib, n_chunks, d_s, page_rows, slots_dtype, &p, vslots != nullptr);
   if (rc) return rc;
   if (!workspace || !aligned(workspace, 256) || workspace_bytes < p.total())
     return fail(XENCB_EINVAL, "read_multi: workspace needs %zu bytes, 256-byte aligned (got %zu)", p.total(),
@@ -749,6 +757,7 @@ int xencb_read_multi(const float* q, int64_t n_rows, int d_s, const void* slots,
   MultiArgs a;
   a.q = q; a.n_rows = n_rows; a.d_s = d_s;
   a.slots = static_cast<const char*>(slots);
+  a.vslots = static_cast<const char*>(vslots);
   a.n_pages = n_pages; a.page_stride_bytes = page_stride * 2; a.page_rows = page_rows;
   a.page_of = page_of; a.n_valid = n_valid; a.n_chunks = n_chunks; a.n_chunks_of = n_chunks_of;
   a.rows_per_lib = rows_per_lib; a.w = w;
@@ -841,7 +850,8 @@ size_t xencb_read_prefill_workspace(int64_t n_rows, int n_chunks, int d_s, int p
   return align_up((size_t)n_rows * d_s * 2, 256) + align_up((size_t)n_rows * n_chunks * ncol * 2, 256);
 }
 
-int xencb_read_prefill(const float* q, int64_t n_rows, int d_s, const void* slots, int slots_dtype, int64_t n_pages,
+int xencb_read_prefill(const float* q, int64_t n_rows, int d_s, const void* slots, const void* vslots, int slots_dtype,
+                       int64_t n_pages,
                        int64_t page_stride, int page_rows, const int32_t* page_of, const int32_t* n_valid, int n_chunks,
                        const int32_t* n_chunks_of, int64_t rows_per_lib, int64_t n_lib, const float* w, float read_temp,
                        int read_softmax, float* r_out, void* workspace, size_t workspace_bytes, void* stream) {
@@ -859,8 +869,8 @@ int xencb_read_prefill(const float* q, int64_t n_rows, int d_s, const void* slot
     return fail(XENCB_ENOTSUP, "read_prefill: the slot pool must be dense ([pages, page_rows, d_s])");
   if (n_pages * (int64_t)page_rows + 512 > INT32_MAX || (int64_t)n_chunks * 512 > INT32_MAX)
     return fail(XENCB_ENOTSUP, "read_prefill: the slot pool is too large for 32-bit TMA coordinates");
-  if (!aligned(slots, 16) || !aligned(q, 16) || !aligned(r_out, 16))
-    return fail(XENCB_EINVAL, "read_prefill: slots, q and r_out must be 16-byte aligned");
+  if (!aligned(slots, 16) || !aligned(q, 16) || !aligned(r_out, 16) || (vslots && !aligned(vslots, 16)))
+    return fail(XENCB_EINVAL, "read_prefill: slots, vslots, q and r_out must be 16-byte aligned");
   const size_t need = xencb_read_prefill_workspace(n_rows, n_chunks, d_s, page_rows);
   if (!workspace || !aligned(workspace, 256) || workspace_bytes < need)
     return fail(XENCB_EINVAL, "read_prefill: workspace needs %zu bytes, 256-byte aligned (got %zu)", need,
@@ -882,7 +892,7 @@ int xencb_read_prefill(const float* q, int64_t n_rows, int d_s, const void* slot
                               CU_TENSOR_MAP_SWIZZLE_64B);
   if (!rc) rc = tensor_map_2d(&mp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.P, (uint64_t)n_chunks * a.ncol,
                               (uint64_t)n_rows, (uint64_t)n_chunks * a.ncol * 2, PF_BK, PF_BM);
-  if (!rc) rc = tensor_map_2d(&mk2, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, slots, (uint64_t)d_s,
+  if (!rc) rc = tensor_map_2d(&mk2, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, vslots ? vslots : slots, (uint64_t)d_s,
                               (uint64_t)(n_pages * page_rows), (uint64_t)d_s * 2, 64, PF_BK);
   if (rc) return rc;
   rc = ensure_smem(prefill_scores_kernel, (int)PF_S_SMEM);
@@ -1070,7 +1080,7 @@ int xencb_read_decode_noalloc(const float* q, int64_t n_rows, int d_s, const voi
     if (rc) return rc;
   }
   // need == 0 means invalid arguments: xencb_read_decode reports which one (it checks them before the workspace)
-  return xencb_read_decode(q, n_rows, d_s, slots, slots_dtype, n_pages, page_stride, page_rows, page_of, n_valid,
+  return xencb_read_decode(q, n_rows, d_s, slots, nullptr, slots_dtype, n_pages, page_stride, page_rows, page_of, n_valid,
                            n_chunks, rows_per_lib, n_lib, idx, wk, k, read_temp, read_softmax, r_out, scratch,
                            need > 0 ? (size_t)XENCB_NOALLOC_SCRATCH_BYTES : 0, stream);
 }

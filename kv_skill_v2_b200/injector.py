@@ -129,15 +129,19 @@ class XEncInjector(ExternalSkillInjector):
         if key in cache:
             return cache[key]
         K, V = self.skill.K[li], self.skill.V[li]
-        if V is not K and not (V.shape == K.shape and torch.equal(V.to(K.device), K)):
-            raise NotImplementedError("untied skill values are not read by the xencb kernels yet")
+        untied = V is not K and not (V.shape == K.shape and torch.equal(V.to(K.device), K))
         Kd = K.to(like.device)
         n = int(Kd.shape[0])
-        slots = Kd.to(torch.float16) if torch.equal(Kd.to(torch.float16).to(Kd.dtype), Kd) else Kd.float()
+        vslots = None
+        if untied:
+            # The untied read runs on the tensor cores: both pools in float16.
+            slots, vslots = Kd.to(torch.float16), V.to(device=like.device, dtype=torch.float16).contiguous().view(1, n, -1)
+        else:
+            slots = Kd.to(torch.float16) if torch.equal(Kd.to(torch.float16).to(Kd.dtype), Kd) else Kd.float()
         pages = ops.Pages(slots=slots.contiguous().view(1, n, -1),
                           page_of=torch.zeros(1, 1, dtype=torch.int32, device=like.device),
                           n_valid=torch.full((1, 1), n, dtype=torch.int32, device=like.device),
-                          S=torch.zeros(1, 1, Kd.shape[-1], dtype=torch.float32, device=like.device))
+                          S=torch.zeros(1, 1, Kd.shape[-1], dtype=torch.float32, device=like.device), vslots=vslots)
         cache[key] = pages
         return pages
 

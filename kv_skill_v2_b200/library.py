@@ -163,17 +163,21 @@ class Library:
         hit = self._page_cache.get(key)
         if hit is not None:
             return hit
-        if self.V is not None:
-            raise NotImplementedError("untied Library values (harvest='attn') are not read by the xencb kernels yet")
         K = self.K[li]
         nv = self.mask[li].sum(-1).to(torch.int32)
         if require_nonempty and bool((nv == 0).any()):
             bad = torch.nonzero(nv == 0).flatten().tolist()
             raise ValueError(f"Library layer {li}: chunks {bad} have no valid slot (the softmax read is NaN)")
-        slots = _slot_storage(K.to(device), slot_dtype)
+        vslots = None
+        if self.V is None:
+            slots = _slot_storage(K.to(device), slot_dtype)
+        else:
+            slots, vslots = _untied_storage(K.to(device), self.V[li].to(device), slot_dtype)
         C = K.shape[0]
         view = Pages(slots=slots.contiguous(), page_of=torch.arange(C, dtype=torch.int32, device=device).view(1, C),
-                     n_valid=nv.to(device).view(1, C), S=self.S[li].to(device=device, dtype=torch.float32).view(1, C, -1).contiguous())
+                     n_valid=nv.to(device).view(1, C),
+                     S=self.S[li].to(device=device, dtype=torch.float32).view(1, C, -1).contiguous(),
+                     vslots=None if vslots is None else vslots.contiguous())
         self._page_cache[key] = view
         return view
 
@@ -189,6 +193,19 @@ def _slot_storage(K: torch.Tensor, slot_dtype) -> torch.Tensor:
             return K
         return K.to(torch.float32)
     return K.to(slot_dtype)
+
+
+def _untied_storage(K: torch.Tensor, V: torch.Tensor, slot_dtype):
+    """K and V pools of one dtype for an untied read, which runs on the tensor cores: float16 (or bfloat16 when
+    asked for, or when K is bfloat16). "auto" rounds float32 rows to float16, which is exact for rows harvested
+    into float16 doc caches."""
+    if slot_dtype == "auto":
+        dt = torch.bfloat16 if K.dtype == torch.bfloat16 else torch.float16
+    else:
+        dt = slot_dtype
+    if dt not in (torch.float16, torch.bfloat16):
+        raise NotImplementedError(f"untied Library values are read from float16 / bfloat16 slots, not {dt}")
+    return K.to(dt), V.to(dt)
 
 
 class PagedLibrary:
@@ -207,7 +224,6 @@ class PagedLibrary:
             if p.n_lib != first.n_lib or p.d_s != first.d_s:
                 raise ValueError("every layer of a PagedLibrary must hold the same Libraries")
         self.depths = depths
-        self.V = None
 
     @property
     def layers(self) -> list:
@@ -230,17 +246,26 @@ class PagedLibrary:
         """Layer -> slot pool (for the `li in lib.K` membership checks of the injectors)."""
         return {li: p.slots for li, p in self._pages.items()}
 
+    @property
+    def V(self) -> Optional[dict]:
+        """Layer -> value pool when the Libraries are untied, else None (V = K)."""
+        if all(p.vslots is None for p in self._pages.values()):
+            return None
+        return {li: p.vslots for li, p in self._pages.items()}
+
     def pages(self, li: int, device=None, slot_dtype="auto", require_nonempty: bool = True) -> Pages:
         p = self._pages[li]
         if device is not None and torch.device(device) != p.device:
             p = Pages(slots=p.slots.to(device), page_of=p.page_of.to(device), n_valid=p.n_valid.to(device),
-                      S=p.S.to(device), n_chunks_of=None if p.n_chunks_of is None else p.n_chunks_of.to(device))
+                      S=p.S.to(device), n_chunks_of=None if p.n_chunks_of is None else p.n_chunks_of.to(device),
+                      vslots=None if p.vslots is None else p.vslots.to(device))
             self._pages[li] = p
         return p
 
     @staticmethod
     def from_libraries(libs: list, device, slot_dtype=torch.float16) -> "PagedLibrary":
-        """Stack Libraries with the same layers and d_s; library b serves batch row b."""
+        """Stack Libraries with the same layers and d_s; library b serves batch row b. When any Library is
+        untied, every layer gets a value pool too (a tied Library's values are its keys)."""
         if not libs:
             raise ValueError("from_libraries needs at least one Library")
         layers = libs[0].layers
@@ -255,7 +280,11 @@ class PagedLibrary:
             d = libs[0].d_s
             Cmax = max(Cs)
             dt = slot_dtype if slot_dtype != "auto" else torch.float16
+            untied = any(lb.V is not None for lb in libs)
+            if untied and dt not in (torch.float16, torch.bfloat16):
+                raise NotImplementedError(f"untied Library values are read from float16 / bfloat16 slots, not {dt}")
             pool = torch.zeros(sum(Cs), Nmax, d, dtype=dt, device=device)
+            vpool = torch.zeros_like(pool) if untied else None
             page_of = torch.zeros(len(libs), Cmax, dtype=torch.int32)
             n_valid = torch.zeros(len(libs), Cmax, dtype=torch.int32)
             S = torch.zeros(len(libs), Cmax, d, dtype=torch.float32, device=device)
@@ -264,20 +293,23 @@ class PagedLibrary:
                 K = lb.K[li]
                 C, Nb = K.shape[0], K.shape[1]
                 pool[off:off + C, :Nb] = K.to(device=device, dtype=dt)
+                if untied:
+                    vpool[off:off + C, :Nb] = (lb.V[li] if lb.V is not None else K).to(device=device, dtype=dt)
                 page_of[b, :C] = torch.arange(off, off + C, dtype=torch.int32)
                 n_valid[b, :C] = lb.mask[li].sum(-1).to(torch.int32).cpu()
                 S[b, :C] = lb.S[li].to(device=device, dtype=torch.float32)
                 off += C
             n_chunks_of = torch.tensor(Cs, dtype=torch.int32, device=device)
             pages[li] = Pages(slots=pool, page_of=page_of.to(device), n_valid=n_valid.to(device), S=S,
-                              n_chunks_of=None if len(set(Cs)) == 1 else n_chunks_of)
+                              n_chunks_of=None if len(set(Cs)) == 1 else n_chunks_of, vslots=vpool)
         return PagedLibrary(pages, depths=libs[0].depths)
 
     @staticmethod
     def from_pool(layer_slots: dict, page_of: torch.Tensor, n_valid: torch.Tensor,
-                  n_chunks_of: Optional[torch.Tensor] = None) -> "PagedLibrary":
+                  n_chunks_of: Optional[torch.Tensor] = None, layer_vslots: Optional[dict] = None) -> "PagedLibrary":
         """Slots already resident on the device: {layer: pool [P, page_rows, d_s]}, a shared page table
-        [n_lib, C] and valid-row counts [n_lib, C]; the summary keys are computed on the device."""
+        [n_lib, C] and valid-row counts [n_lib, C]; the summary keys are computed on the device.
+        layer_vslots: {layer: value pool} of the same shapes for untied Libraries."""
         from .ops import summaries
 
         pages = {}
@@ -285,7 +317,8 @@ class PagedLibrary:
             po = page_of.to(device=slots.device, dtype=torch.int32).contiguous()
             nv = n_valid.to(device=slots.device, dtype=torch.int32).contiguous()
             pages[li] = Pages(slots=slots, page_of=po, n_valid=nv, S=summaries(slots, po, nv),
-                              n_chunks_of=None if n_chunks_of is None else n_chunks_of.to(slots.device, torch.int32))
+                              n_chunks_of=None if n_chunks_of is None else n_chunks_of.to(slots.device, torch.int32),
+                              vslots=None if layer_vslots is None else layer_vslots[li])
         return PagedLibrary(pages)
 
 

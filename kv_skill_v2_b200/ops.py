@@ -199,6 +199,16 @@ def route(q: torch.Tensor, S: torch.Tensor, *, rows_per_lib: int, top_k: int, ro
 
 
 # ------------------------------------------------------------------------------------------------ read
+def _vpool(pages) -> Optional[torch.Tensor]:
+    v = pages.vslots
+    if v is None:
+        return None
+    if v.shape != pages.slots.shape or v.dtype != pages.slots.dtype or v.device != pages.slots.device \
+            or not v.is_contiguous():
+        raise ValueError("Pages.vslots must match slots (shape, dtype, device) and be contiguous")
+    return v
+
+
 @dataclass
 class Pages:
     """Device view of one depth of one or more Libraries, in the layout the read kernels take.
@@ -207,13 +217,15 @@ class Pages:
     page_of  [n_lib, C] int32 page of chunk c of Library l
     n_valid  [n_lib, C] int32 valid rows (the reference's mask, as a length)
     S        [n_lib, C, d_s] float32 summary keys
-    n_chunks_of [n_lib] int32 chunks per Library (None: all have C)"""
+    n_chunks_of [n_lib] int32 chunks per Library (None: all have C)
+    vslots   untied value pool (None: V = K, tied)"""
 
     slots: torch.Tensor
     page_of: torch.Tensor
     n_valid: torch.Tensor
     S: torch.Tensor
     n_chunks_of: Optional[torch.Tensor] = None
+    vslots: Optional[torch.Tensor] = None  # untied values (harvest="attn"): same shape and dtype as slots
 
     @property
     def n_lib(self) -> int:
@@ -260,7 +272,8 @@ def read_decode(q: torch.Tensor, pages: Pages, idx: torch.Tensor, wk: torch.Tens
         if ws_bytes == 0:
             N.check(N.EINVAL, "read_decode_workspace")
         ws = _workspace(ws_bytes, dev)
-        N.call("xencb_read_decode", _ptr(q), R, d_s, _ptr(slots), dt, slots.shape[0], page_rows * d_s, page_rows,
+        N.call("xencb_read_decode", _ptr(q), R, d_s, _ptr(slots), _ptr(_vpool(pages)), dt, slots.shape[0],
+               page_rows * d_s, page_rows,
                _ptr(pages.page_of), _ptr(pages.n_valid), pages.n_chunks, int(rows_per_lib), pages.n_lib,
                _ptr(idx), _ptr(wk), k, float(read_temp), int(bool(read_softmax)), _ptr(r), _ptr(ws),
                ws.numel(), _stream(dev))
@@ -296,7 +309,8 @@ def read_multi(q: torch.Tensor, pages: Pages, w: torch.Tensor, *, rows_per_lib: 
         if ws_bytes == 0:  # the shapes were checked above: the kernel does not take this slot type / width
             N.check(N.ENOTSUP, "read_multi_workspace")
         ws = _workspace(ws_bytes, dev)
-        N.call("xencb_read_multi", _ptr(q), R, d_s, _ptr(slots), dt, slots.shape[0], pages.page_rows * d_s,
+        N.call("xencb_read_multi", _ptr(q), R, d_s, _ptr(slots), _ptr(_vpool(pages)), dt, slots.shape[0],
+               pages.page_rows * d_s,
                pages.page_rows, _ptr(pages.page_of), _ptr(pages.n_valid), pages.n_chunks, _ptr(nco),
                int(rows_per_lib), pages.n_lib, _ptr(w), float(read_temp), int(bool(read_softmax)), _ptr(out),
                _ptr(ws), ws.numel(), _stream(dev))
@@ -326,7 +340,8 @@ def read_prefill(q: torch.Tensor, pages: Pages, w: torch.Tensor, *, rows_per_lib
     with _on_device(dev):
         ws_bytes = N.lib().xencb_read_prefill_workspace(R, pages.n_chunks, d_s, pages.page_rows)
         ws = _workspace(ws_bytes, dev)
-        N.call("xencb_read_prefill", _ptr(q), R, d_s, _ptr(slots), N.F16, slots.shape[0], pages.page_rows * d_s,
+        N.call("xencb_read_prefill", _ptr(q), R, d_s, _ptr(slots), _ptr(_vpool(pages)), N.F16, slots.shape[0],
+               pages.page_rows * d_s,
                pages.page_rows, _ptr(pages.page_of), _ptr(pages.n_valid), pages.n_chunks, _ptr(nco),
                int(rows_per_lib), pages.n_lib, _ptr(w), float(read_temp), int(bool(read_softmax)), _ptr(out),
                _ptr(ws), ws.numel(), _stream(dev))

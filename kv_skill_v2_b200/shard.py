@@ -49,7 +49,8 @@ def shard_pages(pages: ops.Pages, lo: int, hi: int) -> ops.Pages:
     if pages.n_chunks_of is not None:
         nco = (pages.n_chunks_of - lo).clamp(0, hi - lo).to(torch.int32)
     return ops.Pages(slots=pages.slots, page_of=pages.page_of[:, lo:hi].contiguous(),
-                     n_valid=pages.n_valid[:, lo:hi].contiguous(), S=pages.S[:, lo:hi].contiguous(), n_chunks_of=nco)
+                     n_valid=pages.n_valid[:, lo:hi].contiguous(), S=pages.S[:, lo:hi].contiguous(), n_chunks_of=nco,
+                     vslots=pages.vslots)
 
 
 class CudaShardCompute:

@@ -139,12 +139,12 @@ def route(q: np.ndarray, S: np.ndarray, route_temp: float = 10.0, top_k: int = 0
 
 # ----------------------------------------------------------------------------------------------- read
 def read(q: np.ndarray, K: np.ndarray, M: np.ndarray, w: np.ndarray, read_temp: float = 12.0,
-         read_softmax: bool = True) -> np.ndarray:
+         read_softmax: bool = True, V: np.ndarray | None = None) -> np.ndarray:
     """The masked two-level read of LibraryInjector._branch (xenc/injector.py:239-245, 263-265).
 
     a = q . K (dense over ALL C*N slots, as the reference does); softmax(a * read_temp) within each chunk
-    over its valid slots (or linear: a * M / sqrt(n_c)); aw = a * w_c; r = aw @ K (tied values).
-    q: [R, d_s]; w: [R, C]. Returns r [R, d_s]."""
+    over its valid slots (or linear: a * M / sqrt(n_c)); aw = a * w_c; r = aw @ V with V = K (tied) unless
+    the Library has untied values (xenc/injector.py:211-218). q: [R, d_s]; w: [R, C]. Returns r [R, d_s]."""
     q = np.asarray(q, dtype=F32)
     C, N, d = K.shape
     Kf = K.reshape(C * N, d)
@@ -155,13 +155,14 @@ def read(q: np.ndarray, K: np.ndarray, M: np.ndarray, w: np.ndarray, read_temp: 
         n = np.maximum(M.sum(-1), 1).astype(F32)
         a = (np.where(M[None], a, F32(0)) / np.sqrt(n, dtype=F32)[None, :, None]).astype(F32)
     aw = (a * np.asarray(w, dtype=F32)[..., None]).astype(F32)
-    return (aw.reshape(q.shape[0], C * N) @ Kf).astype(F32)
+    Vf = Kf if V is None else np.asarray(V, dtype=F32).reshape(C * N, d)
+    return (aw.reshape(q.shape[0], C * N) @ Vf).astype(F32)
 
 
 def branch(h: np.ndarray, W_in: np.ndarray, W_out: np.ndarray, K: np.ndarray, M: np.ndarray,
            S: np.ndarray, read_temp: float = 12.0, route_temp: float = 10.0, top_k: int = 0,
            read_softmax: bool = True, b_in=None, b_out=None, gate_w=None, gate_b: float = 0.0,
-           gain: float = 1.0, gain_scale: float = 1.0):
+           gain: float = 1.0, gain_scale: float = 1.0, V: np.ndarray | None = None):
     """LibraryInjector._branch without a selector (xenc/injector.py:231-267).
 
     Interface: q = L2(rms_norm(h) @ W_in + b_in); g = sigmoid(hn.gate_w + gate_b) or 1 when gate_w is None;
@@ -170,7 +171,7 @@ def branch(h: np.ndarray, W_in: np.ndarray, W_out: np.ndarray, K: np.ndarray, M:
     hn = rms_norm(h)
     q = query(hn, W_in, b_in)
     w, logit, idx = route(q, S, route_temp, top_k)
-    r = read(q, K, M, w, read_temp, read_softmax)
+    r = read(q, K, M, w, read_temp, read_softmax, V)
     out = r @ np.asarray(W_out, dtype=F32)
     if b_out is not None:
         out = out + np.asarray(b_out, dtype=F32)

@@ -192,15 +192,18 @@ def _pad(rows):
 
 # ------------------------------------------------------------------------------------ cases
 def case_read(name, rows, h, W_in, W_out, top_k, read_softmax, out, read_temp=12.0, route_temp=10.0,
-              inputs_in=None):
+              inputs_in=None, vrows=None, center=None):
     from xenc.injector import LibraryInjector
     from xenc.library import Library
 
     rho, L = 0.5, 8
     reader = FakeReader(8, L, 0)
     li = min(L - 1, int(rho * L))
-    chunks = [{"K": {rho: r}} for r in rows]
-    lib = Library(chunks, [li], [rho])
+    if vrows is None:
+        chunks = [{"K": {rho: r}} for r in rows]
+    else:  # untied values (harvest="attn"): the read weights V, the scores use K
+        chunks = [{"K": {rho: r}, "V": {rho: v}} for r, v in zip(rows, vrows)]
+    lib = Library(chunks, [li], [rho], center=None if center is None else {rho: center})
     itf = Recorder(W_in, W_out)
     itf.inject_layers = [li]
     inj = LibraryInjector(reader, itf, read_softmax=read_softmax, read_temp=read_temp, route_temp=route_temp,
@@ -218,6 +221,11 @@ def case_read(name, rows, h, W_in, W_out, top_k, read_softmax, out, read_temp=12
                     "h": _np(h), "W_in": _np(W_in), "W_out": _np(W_out)})
     else:
         rec["inputs"] = np.array(inputs_in)
+    if vrows is not None:
+        rec["V"] = _np(_pad(vrows))
+    if center is not None:
+        rec["center"] = _np(center)
+        rec["K_lib"] = _np(lib.K[li])  # the centered slots as the Library stores them
     out[name] = rec
     inj.detach()
 
@@ -257,6 +265,23 @@ def gen_small(out):
     h2 = torch.randn(1, 5, 264, generator=g)
     case_read("odd_dims_top3", rows2, h2, torch.randn(264, 520, generator=g) * 0.05,
               torch.randn(520, 264, generator=g) * 0.05, 3, True, out)
+
+
+def gen_untied(out):
+    """Untied values (Library chunks with a separate V, xenc/library.py:46, 61-65; read xenc/injector.py:263-265)
+    and a centered Library (xenc/library.py:56-58: K = L2(K - mu) on valid rows; V is not centered)."""
+    g = torch.Generator().manual_seed(21)
+    d_s, d_m = 64, 96
+    ns = (100, 128, 37, 128, 1, 64)
+    rows = [_unit_rows(n, d_s, g) for n in ns]
+    vrows = [(torch.randn(n, d_s, generator=g) * 0.5).half() for n in ns]
+    h = torch.randn(2, 5, d_m, generator=g)
+    W_in = torch.randn(d_m, d_s, generator=g) * 0.1
+    W_out = torch.randn(d_s, d_m, generator=g) * 0.1
+    case_read("untied_top2", rows, h, W_in, W_out, 2, True, out, vrows=vrows)
+    mu = torch.randn(d_s, generator=g) * 0.05
+    case_read("untied_centered_linear", rows, h, W_in, W_out, 0, False, out, vrows=vrows, center=mu,
+              inputs_in="untied_top2")
 
 
 def gen_batch_docs(out):
@@ -400,12 +425,11 @@ def main() -> None:
     _install_deltaskill_stub()
     torch.set_num_threads(1)
     out: dict = {}
-    gen_cfg1(out)
-    gen_small(out)
-    gen_batch_docs(out)
-    gen_selector(out)
-    gen_library(out)
-    gen_hooked(out)
+    gens = {"cfg1": gen_cfg1, "small": gen_small, "batch_docs": gen_batch_docs, "selector": gen_selector,
+            "library": gen_library, "hooked": gen_hooked, "untied": gen_untied}
+    wanted = sys.argv[1:] or list(gens)  # e.g. `python make_golden.py untied` regenerates one group
+    for nm in wanted:
+        gens[nm](out)
     for name, rec in out.items():
         if name.startswith("_"):
             continue

@@ -109,6 +109,28 @@ def test_paged_library_from_libraries():
     assert torch.equal(p.slots[3, :4].float(), libs[1].K[4][1, :4])
 
 
+def test_untied_pages_and_paged_value_pools():
+    """Untied chunks give a value pool beside the key pool (same layout, float16); a tied Library stacked with an
+    untied one contributes its keys as values; float32 untied pools are refused."""
+    g = torch.Generator().manual_seed(4)
+    ch = [{"K": {0.5: unit_rows(n, 16, g)}, "V": {0.5: torch.randn(n, 16, generator=g)}} for n in (5, 9)]
+    lib = Library(ch, [4], [0.5])
+    assert lib.V is not None
+    p = lib.pages(4, "cpu")
+    assert p.vslots is not None and p.vslots.shape == p.slots.shape and p.vslots.dtype == torch.float16
+    assert torch.equal(p.vslots[1, :9], lib.V[4][1, :9].half())
+    assert torch.equal(p.slots[0, :5], lib.K[4][0, :5].half())
+    with pytest.raises(NotImplementedError):
+        lib.pages(4, "cpu", slot_dtype=torch.float32)
+    tied = Library([{"K": {0.5: unit_rows(n, 16, g)}} for n in (3, 4)], [4], [0.5])
+    pl = PagedLibrary.from_libraries([lib, tied], "cpu")
+    q = pl.pages(4)
+    assert pl.V is not None and q.vslots.shape == q.slots.shape
+    assert torch.equal(q.vslots[0, :5], lib.V[4][0, :5].half())
+    assert torch.equal(q.vslots[3, :4], q.slots[3, :4])  # the tied Library's values are its keys
+    assert PagedLibrary.from_libraries([tied], "cpu").V is None
+
+
 def test_interface_save_load_roundtrip(tmp_path):
     for with_sel in (False, True):
         for rank in (0, 8):

@@ -114,3 +114,24 @@ def test_oracle_shard_merge_equals_dense_read():
     parts = [X.shard_partials(q, K[a:b], M[a:b], S[a:b], 10.0, 12.0) for a, b in ((0, 3), (3, 5), (5, 8))]
     r = X.merge_shards(parts)
     assert rel_err(r, c["r"].reshape(r.shape)) < 1e-5
+
+
+@pytest.mark.parametrize("name", ["untied_top2", "untied_centered_linear"])
+def test_untied_values_and_centering(name):
+    """Untied V (the read weights V, the scores and summaries use K) and a centered Library
+    (K = L2(K - mu) on valid rows, V untouched): the oracle against the reference's own _branch."""
+    c = load_case(name)
+    K, n = c["K"].astype(np.float32), c["n_valid"]
+    M = np.arange(K.shape[1])[None, :] < n[:, None]
+    if "center" in c:
+        K = X.build_library([K[i, :n[i]] for i in range(len(n))], c["center"])[0]
+        assert np.abs(K - c["K_lib"]).max() < 1e-6
+    S = X.summaries(K, M)
+    assert np.abs(S - c["S"]).max() < 1e-6
+    h = c["h"].reshape(-1, c["h"].shape[-1])
+    out = X.branch(h, c["W_in"], c["W_out"], K, M, S, read_temp=float(c["read_temp"]),
+                   route_temp=float(c["route_temp"]), top_k=int(c["top_k"]), read_softmax=bool(c["read_softmax"]),
+                   V=c["V"].astype(np.float32))
+    assert topk_sets(out["w"]) == topk_sets(c["w"].reshape(out["w"].shape))
+    assert rel_err(out["r"], c["r"].reshape(out["r"].shape)) < 1e-5
+    assert rel_err(out["delta"], c["delta"].reshape(out["delta"].shape)) < 1e-5
