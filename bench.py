@@ -63,6 +63,11 @@ def parse_args(argv=None):
                     help="only the config-3 prefill; print its object as the line (for profilers)")
     ap.add_argument("--prefill-docs", type=int, default=8,
                     help="documents of the config-3 prefill (8 = the config; fewer only for profiler captures)")
+    ap.add_argument("--no-library-build", action="store_true", help="skip the device Library build")
+    ap.add_argument("--library-build-only", action="store_true",
+                    help="only the device Library build (config-2 shapes)")
+    ap.add_argument("--library-build-docs", type=int, default=16,
+                    help="documents per device Library build step (smaller for profiler captures)")
     ap.add_argument("--selector-only", action="store_true",
                     help="only the config-4 selector decode; print its object as the line (for profilers)")
     return ap.parse_args(argv)
@@ -472,6 +477,103 @@ def run_selector(torch, dist, dev, world: int, rank: int, steps: int, warmup: in
             "l2": "flushed between steps (256 MiB write)"}
 
 
+CFGB = dict(docs=16, C=64, N=512, d_s=2048)
+
+
+def run_library_build(torch, dist, dev, world: int, rank: int, steps: int, warmup: int, stream,
+                      cpu_seconds: float = 0.0, docs: int = 16) -> dict:
+    """The device Library build (xenc/library.py:47-74) at config-2 shapes: one depth of 16 documents' Libraries
+    (64 chunks x up to 512 fp16 rows, d_s 2048, the last chunk of each ragged), centred (K = L2(K - mu) on the
+    valid rows) into float16 pages, with n_valid and S. A step is one build of all 16 Libraries (the build
+    kernel + the summaries kernel). Inputs 2 GiB, outputs 2 GiB: larger than L2, so no flush is needed.
+    Algorithmic bytes: valid rows read once, every page row written once, S and mu."""
+    import numpy as np
+
+    from kv_skill_v2_b200 import _native, ops
+
+    B, C, N, d = int(docs), CFGB["C"], CFGB["N"], CFGB["d_s"]
+    g = torch.Generator().manual_seed(5000 + rank)
+    counts = [N] * (B * C)
+    for b in range(B):
+        counts[b * C + C - 1] = int(torch.randint(1, N + 1, (1,), generator=g))
+    n_rows = sum(counts)
+    gd = torch.Generator(device=dev).manual_seed(5000 + rank)
+    rows = torch.empty(n_rows, d, dtype=torch.float16, device=dev)
+    for r0 in range(0, n_rows, 65536):
+        x = torch.randn(min(65536, n_rows - r0), d, generator=gd, device=dev)
+        rows[r0:r0 + x.shape[0]] = (x / x.norm(dim=-1, keepdim=True)).half()
+        del x
+    mu = torch.randn(d, generator=gd, device=dev) * 0.01
+    slots, nv, S = ops.library_build(rows, counts, page_rows=N, mu=mu, slot_dtype=torch.float16)
+    # parity spot check against the oracle on three chunks (first, a ragged last one, one in the middle)
+    from oracle import xenc_oracle as X
+    starts = np.concatenate([[0], np.cumsum(counts)])
+    for c in (0, C - 1, (B // 2) * C + 7):
+        rr = rows[int(starts[c]):int(starts[c + 1])].float().cpu().numpy()
+        K_ref, _, S_ref = X.build_library([rr], mu.cpu().numpy())
+        assert np.abs(S[c].cpu().numpy() - S_ref[0]).max() <= 1e-6, "library_build: S differs from the oracle"
+        got = slots[c, :counts[c]].float().cpu().numpy()
+        assert np.abs(got - K_ref[0]).max() <= 1e-3 * np.abs(K_ref[0]).max(), "library_build: slots differ"
+    start = torch.zeros(len(counts) + 1, dtype=torch.int64)
+    start[1:] = torch.tensor(counts, dtype=torch.int64).cumsum(0)
+    start = start.to(dev)
+    page_of = torch.arange(B * C, dtype=torch.int32, device=dev)
+    ws_bytes = _native.lib().xencb_library_build_workspace(B * C, d, N)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+
+    def launch():
+        _native.call("xencb_library_build", ops._ptr(rows), _native.F16, n_rows, ops._ptr(start), B * C, d,
+                     ops._ptr(mu), ops._ptr(slots), _native.F16, B * C, N * d, N, ops._ptr(page_of), ops._ptr(nv),
+                     ops._ptr(S), ops._ptr(ws), ws.numel(), ops._stream(dev))
+
+    for _ in range(warmup):
+        launch()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    n0 = _native.launch_count()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        ev[i][0].record(stream)
+        launch()
+        ev[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    kernels = _native.launch_count() - n0
+    t_ms = sum(a.elapsed_time(b) for a, b in ev)
+    if world > 1:
+        t = torch.tensor([t_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_ms = float(t.item())
+    ms = t_ms / steps
+    step_bytes = n_rows * d * 2 + B * C * N * d * 2 + B * C * d * 4 + d * 4 + B * C * 4
+    peak, peak_kind = hbm_peak()
+    res = {"workload": f"device Library build at config-2 shapes: {B} documents x {C} chunks x <= {N} fp16 rows, "
+                       f"d_s {d}, centred, into fp16 pages + n_valid + S (one depth)",
+           "metric": "Libraries built per second (whole job)", "value": B * world / (ms / 1000.0),
+           "unit": "Libraries/s", "ms_per_step": ms, "n_gpus": world, "scaling": "weak",
+           "kernels_per_step": kernels // max(steps, 1), "gpu_launches": kernels,
+           "roofline": {"bound": "hbm", "kernel": "library_build_kernel + library_summaries_kernel",
+                        "achieved": step_bytes / (ms / 1000.0) / 1e9, "peak": peak, "unit": "GB/s",
+                        "frac": step_bytes / (ms / 1000.0) / 1e9 / peak, "algorithmic_bytes_per_step": step_bytes,
+                        "peak_source": peak_kind},
+           "l2": f"inputs and outputs {B * C * N * d * 2 / 2**30:.1f} GiB each (larger than L2)"}
+    if rank == 0 and world == 1 and cpu_seconds > 0:
+        # the reference's build (padding, centring, summaries) restated in numpy, one Library at a time
+        rr = rows[:sum(counts[:C])].float().cpu().numpy()
+        chunks = np.split(rr, np.cumsum(counts[:C])[:-1])
+        mu_h = mu.cpu().numpy()
+        spent, n = 0.0, 0
+        while spent < cpu_seconds and n < 50:
+            t0 = time.perf_counter()
+            X.build_library(chunks, mu_h)
+            spent += time.perf_counter() - t0
+            n += 1
+        res["cpu_baseline"] = {"value": n / spent, "unit": "Libraries/s", "cores": 1, "kind": "port",
+                               "sample": f"{n} builds of one {C}-chunk Library (oracle.build_library, numpy)"}
+    del rows, slots, ws
+    return res
+
+
 CFG3 = dict(docs=8, T=2048, C=128, N=512, d_s=2048, d_m=4096, read_temp=12.0, route_temp=10.0)
 
 
@@ -600,9 +702,14 @@ def run_ours(args) -> None:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    if args.sharded_only or args.selector_only or args.prefill_only:
+    if args.sharded_only or args.selector_only or args.prefill_only or args.library_build_only:
         flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
-        if args.prefill_only:
+        if args.library_build_only:
+            res = run_library_build(torch, dist, dev, world, rank, args.steps, args.warmup,
+                                    torch.cuda.current_stream(dev),
+                                    cpu_seconds=0.0 if args.no_cpu_baseline else args.cpu_seconds,
+                                    docs=args.library_build_docs)
+        elif args.prefill_only:
             res = run_prefill(torch, dist, dev, world, rank, args.steps, args.warmup, flush,
                               torch.cuda.current_stream(dev), docs=args.prefill_docs)
         elif args.sharded_only:
@@ -761,7 +868,9 @@ def run_ours(args) -> None:
             t_e2e = float(t.item())
         e2e = R * args.steps * world / (t_e2e / 1000.0)
         inj.detach()
-        sharded = selector = prefill = None
+        sharded = selector = prefill = lbuild = None
+        if not args.no_library_build:
+            lbuild = run_library_build(torch, dist, dev, world, rank, max(3, args.steps // 20), args.warmup, stream)
         if not args.no_prefill:
             prefill = run_prefill(torch, dist, dev, world, rank, max(3, args.steps // 10), args.warmup, flush, stream)
         if not args.no_sharded:
@@ -801,6 +910,7 @@ def run_ours(args) -> None:
             "sharded": sharded,
             "selector": selector,
             "prefill": prefill,
+            "library_build": lbuild,
             "clocks": clocks, "device_status": status}
     print(json.dumps(line), flush=True)
 

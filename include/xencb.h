@@ -49,6 +49,7 @@ extern "C" {
 #define XENCB_DEV_TIMEOUT 1u /* an mbarrier wait gave up after its time limit                  */
 #define XENCB_DEV_CLAMPED 2u /* an n_valid entry exceeded page_rows and was clamped            */
 #define XENCB_DEV_BADPAGE 4u /* a page_of entry was outside [0, n_pages); that chunk was skipped */
+#define XENCB_DEV_BADROWS 8u /* a library_build row range was outside the row buffer; built empty */
 
 /* element type codes */
 #define XENCB_F32 0
@@ -240,6 +241,25 @@ XENCB_API int xencb_selector_apply(const void* delta, int delta_dtype, const voi
  *   S[lib, c] = L2(mean of the n_valid[lib, c] rows of page page_of[lib, c]) (zero rows give S = 0). */
 XENCB_API int xencb_summaries(const void* slots, int slots_dtype, int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of,
                     const int32_t* n_valid, int64_t n_lib, int n_chunks, int d_s, float* S_out, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Library build on the device, for one depth of one or several Libraries. Replaces the per-chunk host loop of
+ * Library.__init__ (xenc/library.py:47-67) and Library._summaries (xenc/library.py:69-74):
+ *   rows       [n_rows_total, d_s] of rows_dtype: the doc cache's rows of every chunk, concatenated in chunk order
+ *   row_start  [n_chunks + 1] int64 (device): chunk c is rows [row_start[c], row_start[c + 1])
+ *   mu         [d_s] float32 or NULL: centering, K = L2(K - mu) on the chunk's rows (xenc/library.py:56-58)
+ * Page page_of[c] of `slots` (slots_dtype, page_rows x d_s, page_stride elements apart) receives the chunk's
+ * rows, then zeros up to page_rows; n_valid_out[c] = the row count (NULL: not written); S_out[c] = L2(mean of
+ * the chunk's rows) in float32, computed before the rows are rounded to slots_dtype (NULL: not written).
+ * d_s % 8 == 0; rows, slots and page_stride * element size 16-byte aligned. On the device a row range outside
+ * [0, n_rows_total] builds an empty chunk (XENCB_DEV_BADROWS) and a chunk longer than page_rows is cut
+ * (XENCB_DEV_CLAMPED). The result is deterministic (fixed summation order). */
+XENCB_API size_t xencb_library_build_workspace(int n_chunks, int d_s, int page_rows);
+XENCB_API int xencb_library_build(const void* rows, int rows_dtype, int64_t n_rows_total, const int64_t* row_start,
+                                  int n_chunks, int d_s, const float* mu, void* slots, int slots_dtype,
+                                  int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of,
+                                  int32_t* n_valid_out, float* S_out, void* workspace, size_t workspace_bytes,
+                                  void* stream);
 
 #ifdef __cplusplus
 }

@@ -55,6 +55,8 @@ SIGNATURES: dict = {
     "xencb_selector_logits": (_i, [_p, _i, _i64, _i, _p, _p, _i, _i, _f, _p, _p]),
     "xencb_selector_apply": (_i, [_p, _i, _p, _i, _i64, _i, _p, _i, _i, _f, _p, _p]),
     "xencb_summaries": (_i, [_p, _i, _i64, _i64, _i, _p, _p, _i64, _i, _i, _p, _p]),
+    "xencb_library_build_workspace": (_sz, [_i, _i, _i]),
+    "xencb_library_build": (_i, [_p, _i, _i64, _p, _i, _i, _p, _p, _i, _i64, _i64, _i, _p, _p, _p, _p, _sz, _p]),
 }
 
 _lib = None

@@ -22,6 +22,7 @@
 #include "read_multi.cuh"
 #include "prefill.cuh"
 #include "route.cuh"
+#include "library_build.cuh"
 
 // Scratch of xencb_read_decode_noalloc: a fixed device array, so that entry point never allocates.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[XENCB_NOALLOC_SCRATCH_BYTES];
@@ -473,6 +474,32 @@ rc_t launch_route_logits(const float* q, int64_t n_rows, int d_s, const float* S
 }  // namespace xencb
 
 using namespace xencb;
+
+// Library build plan: splits per chunk and the column-sum workspace.
+namespace {
+struct BuildPlan {
+  int n_split, split_rows, threads;
+  size_t part_bytes;
+};
+
+int plan_build(int n_chunks, int d_s, int page_rows, BuildPlan* p) {
+  DevInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  if (d_s > LB_MAX_THREADS * LB_VEC)
+    return fail(XENCB_ENOTSUP, "library_build: d_s=%d above %d is not supported", d_s, LB_MAX_THREADS * LB_VEC);
+  // splits: about eight CTAs per SM over all chunks (short waves, small tail), each split >= 4 row batches
+  int want = (8 * di.sms + n_chunks - 1) / n_chunks;
+  const int max_split = (page_rows + 4 * LB_ROWS - 1) / (4 * LB_ROWS);
+  if (want > max_split) want = max_split;
+  if (want < 1) want = 1;
+  p->split_rows = (int)align_up((size_t)((page_rows + want - 1) / want), LB_ROWS);
+  p->n_split = (page_rows + p->split_rows - 1) / p->split_rows;
+  p->part_bytes = align_up((size_t)n_chunks * p->n_split * d_s * sizeof(float), 256);
+  p->threads = (int)align_up((size_t)((d_s + LB_VEC - 1) / LB_VEC), 32);
+  return XENCB_OK;
+}
+}  // namespace
 
 extern "C" {
 
@@ -1059,6 +1086,69 @@ int xencb_summaries(const void* slots, int slots_dtype, int64_t n_pages, int64_t
   }
   XENCB_CHECK_LAUNCH("summaries launch");
   return XENCB_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ library build
+
+size_t xencb_library_build_workspace(int n_chunks, int d_s, int page_rows) {
+  if (n_chunks <= 0 || d_s <= 0 || page_rows <= 0) return 0;
+  BuildPlan p;
+  if (plan_build(n_chunks, d_s, page_rows, &p)) return 0;
+  return p.part_bytes;
+}
+
+int xencb_library_build(const void* rows, int rows_dtype, int64_t n_rows_total, const int64_t* row_start, int n_chunks,
+                        int d_s, const float* mu, void* slots, int slots_dtype, int64_t n_pages, int64_t page_stride,
+                        int page_rows, const int32_t* page_of, int32_t* n_valid_out, float* S_out, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  if (!row_start || !slots || !page_of) return fail(XENCB_EINVAL, "library_build: row_start, slots and page_of are required");
+  if (n_rows_total < 0 || (n_rows_total > 0 && !rows)) return fail(XENCB_EINVAL, "library_build: rows is required");
+  if (n_chunks <= 0 || d_s <= 0 || page_rows <= 0 || n_pages <= 0)
+    return fail(XENCB_EINVAL, "library_build: sizes must be positive");
+  if (d_s % LB_VEC) return fail(XENCB_EINVAL, "library_build: d_s=%d must be a multiple of %d", d_s, LB_VEC);
+  const int ei = elem_size(rows_dtype), eo = elem_size(slots_dtype);
+  if (!ei || !eo) return fail(XENCB_EINVAL, "library_build: dtype codes %d / %d unknown", rows_dtype, slots_dtype);
+  if (page_stride < (int64_t)page_rows * d_s)
+    return fail(XENCB_EINVAL, "library_build: page_stride %lld < page_rows*d_s %lld", (long long)page_stride,
+                (long long)page_rows * d_s);
+  if ((rows && !aligned(rows, 16)) || !aligned(slots, 16) || (page_stride * eo) % 16 != 0 || (mu && !aligned(mu, 16)))
+    return fail(XENCB_EINVAL, "library_build: rows, slots, mu and page_stride*elem must be 16-byte aligned");
+  BuildPlan p;
+  int rc = plan_build(n_chunks, d_s, page_rows, &p);
+  if (rc) return rc;
+  if (!workspace || !aligned(workspace, 256) || workspace_bytes < p.part_bytes)
+    return fail(XENCB_EINVAL, "library_build: workspace needs %zu bytes, 256-byte aligned (got %zu)", p.part_bytes,
+                workspace_bytes);
+  LibBuildArgs a;
+  a.rows = rows; a.n_rows_total = n_rows_total; a.row_start = row_start; a.n_chunks = n_chunks; a.d_s = d_s;
+  a.mu = mu; a.slots = slots; a.n_pages = n_pages; a.page_stride = page_stride; a.page_rows = page_rows;
+  a.page_of = page_of; a.n_split = p.n_split; a.split_rows = p.split_rows;
+  a.part = static_cast<float*>(workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto run = [&](auto ti, auto to) -> int {
+    using TI = typename decltype(ti)::type;
+    using TO = typename decltype(to)::type;
+    library_build_kernel<TI, TO><<<dim3((unsigned)n_chunks, (unsigned)p.n_split), p.threads, 0, st>>>(a);
+    XENCB_CHECK_LAUNCH("library_build_kernel launch");
+    library_summaries_kernel<<<(unsigned)n_chunks, 256, 0, st>>>(a, n_valid_out, S_out);
+    XENCB_CHECK_LAUNCH("library_summaries_kernel launch");
+    return XENCB_OK;
+  };
+  struct F32T { using type = float; };
+  struct F16T { using type = __half; };
+  struct BF16T { using type = __nv_bfloat16; };
+  auto with_out = [&](auto ti) -> int {
+    switch (slots_dtype) {
+      case XENCB_F32: return run(ti, F32T{});
+      case XENCB_F16: return run(ti, F16T{});
+      default: return run(ti, BF16T{});
+    }
+  };
+  switch (rows_dtype) {
+    case XENCB_F32: return with_out(F32T{});
+    case XENCB_F16: return with_out(F16T{});
+    default: return with_out(BF16T{});
+  }
 }
 
 int xencb_read_decode_noalloc(const float* q, int64_t n_rows, int d_s, const void* slots, int slots_dtype,

@@ -305,6 +305,76 @@ class PagedLibrary:
         return PagedLibrary(pages, depths=libs[0].depths)
 
     @staticmethod
+    def from_doc_caches(caches: list, reader_model, depths=None, device=None, center: Optional[dict] = None,
+                        slot_dtype="auto", page_rows: Optional[int] = None) -> "PagedLibrary":
+        """Build on the device, one Library per doc cache (batch row b reads caches[b]), with what
+        Library.from_doc_cache (xenc/library.py:125-136) and Library.__init__ / _summaries (:26-74) compute:
+        per depth, every doc's chunk rows go to the device in one copy and one build launch pads them into
+        pages, centres them when `center` is given and computes S from the float32 rows.
+
+        slot_dtype "auto": float16 for uncentred keys (the cache's rows are float16, so the copy is exact),
+        float32 for centred keys of a tied Library (the read then matches the reference's float32 Library),
+        float16 for an untied one (its read runs on the tensor cores)."""
+        from .ops import library_build
+
+        if not caches:
+            raise ValueError("from_doc_caches needs at least one doc cache")
+        depths = sorted(float(r) for r in (depths or caches[0]["depths"]))
+        rmap = rho_layer_map(reader_model, depths)
+        if device is None:
+            device = reader_model.device if hasattr(reader_model, "device") else "cuda"
+        device = torch.device(device)
+        Cs = [len(c["chunks"]) for c in caches]
+        if min(Cs) == 0:
+            raise ValueError("Library needs at least one chunk")
+        untied = any(ch.get("V") is not None for c in caches for ch in c["chunks"])
+        n_lib, Cmax, total = len(caches), max(Cs), sum(Cs)
+        lib_of = torch.repeat_interleave(torch.arange(n_lib), torch.tensor(Cs)).to(device)
+        col_of = torch.cat([torch.arange(c) for c in Cs]).to(device)
+        page_of = torch.zeros(n_lib, Cmax, dtype=torch.int32, device=device)
+        page_of[lib_of, col_of] = torch.arange(total, dtype=torch.int32, device=device)
+        pages = {}
+        for rho in depths:
+            li = rmap[rho]
+            krows = [_rows_of(ch, rho, "K") for c in caches for ch in c["chunks"]]
+            counts = [int(r.shape[0]) for r in krows]
+            pr = int(page_rows or max(max(counts), 1))
+            mu = None
+            if center is not None:
+                try:
+                    mu = center[key_for(center, rho)].to(device=device, dtype=torch.float32)
+                except KeyError:
+                    mu = None
+            if slot_dtype == "auto":
+                dt = torch.float32 if (mu is not None and not untied) else torch.float16
+            else:
+                dt = slot_dtype
+            flat = torch.cat([r.reshape(-1, r.shape[-1]) for r in krows]).contiguous()
+            if flat.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+                flat = flat.float()
+            flat = flat.to(device)
+            slots, nv, S = library_build(flat, counts, page_rows=pr, mu=mu, slot_dtype=dt)
+            vslots = None
+            if untied:
+                if dt not in (torch.float16, torch.bfloat16):
+                    raise NotImplementedError(f"untied Library values are read from float16 / bfloat16 slots, not {dt}")
+                vrows = [(_rows_of(ch, rho, "V") if ch.get("V") is not None else _rows_of(ch, rho, "K"))
+                         for c in caches for ch in c["chunks"]]
+                if [int(r.shape[0]) for r in vrows] != counts:
+                    raise ValueError("untied chunks need as many V rows as K rows")
+                vflat = torch.cat([r.reshape(-1, r.shape[-1]) for r in vrows]).contiguous().to(device)
+                vslots, _, _ = library_build(vflat, counts, page_rows=pr, slot_dtype=dt, want_summaries=False)
+            n_valid = torch.zeros(n_lib, Cmax, dtype=torch.int32, device=device)
+            n_valid[lib_of, col_of] = nv
+            S2 = torch.zeros(n_lib, Cmax, S.shape[-1], dtype=torch.float32, device=device)
+            S2[lib_of, col_of] = S
+            pages[li] = Pages(slots=slots, page_of=page_of, n_valid=n_valid, S=S2,
+                              n_chunks_of=None if len(set(Cs)) == 1 else torch.tensor(Cs, dtype=torch.int32,
+                                                                                      device=device),
+                              vslots=vslots)
+        return PagedLibrary(pages, depths=depths)
+
+    @staticmethod
     def from_pool(layer_slots: dict, page_of: torch.Tensor, n_valid: torch.Tensor,
                   n_chunks_of: Optional[torch.Tensor] = None, layer_vslots: Optional[dict] = None) -> "PagedLibrary":
         """Slots already resident on the device: {layer: pool [P, page_rows, d_s]}, a shared page table

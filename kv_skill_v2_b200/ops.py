@@ -478,6 +478,62 @@ def summaries(slots: torch.Tensor, page_of: torch.Tensor, n_valid: torch.Tensor)
     return S
 
 
+def library_build(rows: torch.Tensor, counts, *, page_rows: Optional[int] = None, mu: Optional[torch.Tensor] = None,
+                  slot_dtype=torch.float16, slots: Optional[torch.Tensor] = None,
+                  page_of: Optional[torch.Tensor] = None, want_summaries: bool = True):
+    """Build one depth of a Library on the device from its chunks' rows (xenc/library.py:47-74).
+
+    rows [n_rows, d_s] (f16 / bf16 / f32, on the GPU): every chunk's rows concatenated in chunk order;
+    counts: the row count of each chunk (host ints). mu [d_s]: centering, K = L2(K - mu) on the valid rows.
+    Writes the chunks into `slots` [P, page_rows, d_s] at pages `page_of` [C] (default: a new pool, page c =
+    chunk c) with zero rows after each chunk's count. Returns (slots, n_valid [C] int32, S [C, d_s] float32 or
+    None); S is computed from the float32 rows before they are rounded to the slot type."""
+    dev = _cuda("library_build", rows, mu, slots, page_of)
+    counts = [int(n) for n in (counts.tolist() if torch.is_tensor(counts) else counts)]
+    C = len(counts)
+    if C == 0:
+        raise ValueError("library_build: a Library needs at least one chunk")
+    if any(n < 0 for n in counts):
+        raise ValueError("library_build: chunk row counts must be >= 0")
+    if rows.dim() != 2 or not rows.is_contiguous():
+        raise ValueError("library_build: rows must be a contiguous [n_rows, d_s] tensor")
+    n_rows, d_s = rows.shape
+    if sum(counts) != n_rows:
+        raise ValueError(f"library_build: counts sum to {sum(counts)}, rows has {n_rows}")
+    page_rows = int(page_rows if page_rows is not None else max(max(counts), 1))
+    if max(counts) > page_rows:
+        raise ValueError(f"library_build: a chunk has {max(counts)} rows, pages hold {page_rows}")
+    if slots is None:
+        slots = torch.empty(C, page_rows, d_s, dtype=slot_dtype, device=dev)
+    elif not slots.is_contiguous() or slots.dim() != 3 or tuple(slots.shape[1:]) != (page_rows, d_s):
+        raise ValueError(f"library_build: slots must be a contiguous [P, {page_rows}, {d_s}] pool")
+    if page_of is None:
+        if slots.shape[0] < C:
+            raise ValueError(f"library_build: {C} chunks need {C} pages, the pool has {slots.shape[0]}")
+        page_of = torch.arange(C, dtype=torch.int32, device=dev)
+    page_of = page_of.to(device=dev, dtype=torch.int32).contiguous().view(-1)
+    if page_of.numel() != C:
+        raise ValueError(f"library_build: page_of has {page_of.numel()} entries for {C} chunks")
+    if mu is not None:
+        mu = _f32(mu.reshape(-1), "mu")
+        if mu.numel() != d_s:
+            raise ValueError(f"library_build: mu has {mu.numel()} entries, d_s={d_s}")
+    start = torch.zeros(C + 1, dtype=torch.int64)
+    start[1:] = torch.tensor(counts, dtype=torch.int64).cumsum(0)
+    start = start.to(dev, non_blocking=True)
+    n_valid = torch.empty(C, dtype=torch.int32, device=dev)
+    S = torch.empty(C, d_s, dtype=torch.float32, device=dev) if want_summaries else None
+    with _on_device(dev):
+        ws_bytes = N.lib().xencb_library_build_workspace(C, d_s, page_rows)
+        if ws_bytes == 0:
+            N.check(N.EINVAL, "library_build_workspace")
+        ws = _workspace(ws_bytes, dev)
+        N.call("xencb_library_build", _ptr(rows), _hdt(rows, "rows"), n_rows, _ptr(start), C, d_s, _ptr(mu),
+               _ptr(slots), _hdt(slots, "slots"), slots.shape[0], page_rows * d_s, page_rows, _ptr(page_of),
+               _ptr(n_valid), _ptr(S), _ptr(ws), ws.numel(), _stream(dev))
+    return slots, n_valid, S
+
+
 def device_status(dev: torch.device, clear: bool = True) -> int:
     """Synchronise the current stream of `dev` and return the device status bits (XENCB_DEV_*)."""
     v = ctypes.c_uint(0)
