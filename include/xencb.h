@@ -261,6 +261,34 @@ XENCB_API int xencb_library_build(const void* rows, int rows_dtype, int64_t n_ro
                                   int32_t* n_valid_out, float* S_out, void* workspace, size_t workspace_bytes,
                                   void* stream);
 
+/* ---------------------------------------------------------------------------------------------------------
+ * D8 top-k slot selection and read (xenc/topk_read.py). Slot s of a Library is row s % page_rows of its chunk
+ * s / page_rows (the residual Library's padded [C, N] slot grid, flattened as the reference's Kf[idx]).
+ *
+ * xencb_select_scores replaces TopKSelector.head_scores + pool_scores (xenc/topk_read.py:215-239):
+ *   scores[r, s] = pool_h pool_t (q[r, t, h, :] . keys[lib(r), s, h / (n_q / n_kv), :])
+ *   q [n_rows, T, n_q, hd] float32 (the reader's pre-RoPE queries at the selection layer, T positions);
+ *   keys per Library [n_chunks * page_rows, n_kv * hd], XENCB_F32 or XENCB_F16, keys_lib_stride elements apart;
+ *   query_pool 0 = max over T (T = 1 for query "last"), 1 = mean; head_pool 0 = max, 1 = mean;
+ *   slots at or past n_valid of their chunk, or in chunks past n_chunks_of[lib], score -inf.
+ * xencb_select_topk replaces sc.topk(k) (xenc/topk_read.py:251-254): per row the k largest scores, sorted by
+ *   score (descending), ties to the lower slot; idx_out [n_rows, k] int32, score_out [n_rows, k] (or NULL).
+ *   k <= 2048 and k <= n_slots.
+ * xencb_topk_read replaces TopKLibraryInjector._branch's read (xenc/topk_read.py:392-413):
+ *   a = q . K[idx] over the k slots of the row's index set, softmax(a * read_temp) or a / sqrt(k), r = a @ V[idx]
+ *   (V = vslots when not NULL, else K). Rows [b * n_rows / n_sets, (b + 1) * n_rows / n_sets) use idx[b] and
+ *   Library b when n_lib > 1 (else Library 0). attn_out [n_rows, k] receives a (NULL: not written). */
+XENCB_API int xencb_select_scores(const float* q, int64_t n_rows, int T, int n_q, int n_kv, int hd, const void* keys,
+                                  int keys_dtype, int64_t keys_lib_stride, int page_rows, int n_chunks,
+                                  const int32_t* n_valid, const int32_t* n_chunks_of, int64_t rows_per_lib,
+                                  int64_t n_lib, int query_pool, int head_pool, float* scores_out, void* stream);
+XENCB_API int xencb_select_topk(const float* scores, int64_t n_rows, int n_slots, int k, int32_t* idx_out,
+                                float* score_out, void* stream);
+XENCB_API int xencb_topk_read(const float* q, int64_t n_rows, int d_s, const void* slots, const void* vslots,
+                              int slots_dtype, int64_t n_pages, int64_t page_stride, int page_rows,
+                              const int32_t* page_of, int n_chunks, int64_t n_lib, const int32_t* idx, int n_sets,
+                              int k, float read_temp, int read_softmax, float* r_out, float* attn_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -4,6 +4,7 @@ Public API, mirroring the reference's xenc package for this path:
     Library, PagedLibrary                       (xenc/library.py)
     XEncInjector, LibraryInjector, itf_*        (xenc/injector.py)
     LayerSelector                               (xenc/selector.py)
+    TopKLibrary, TopKSelector, TopKLibraryInjector, attach_sel_keys (xenc/topk_read.py, the D8 top-k slot read)
     ModelInterface, LinearInterface, make_interface, EncoderLens, interface_param_groups,
     save_interface, load_interface, count_params (xenc/interface.py)
     DEPTHS, CAND, rho_layer_map, injection_layers, for_reader, KVSkill (xenc/__init__.py, xenc/depth_skill.py)
@@ -17,9 +18,10 @@ from .interface import (EncoderLens, LinearInterface, ModelInterface, count_para
                         load_interface, make_interface, save_interface)
 from .library import Library, PagedLibrary
 from .selector import LayerSelector
+from .topk_read import TopKLibrary, TopKLibraryInjector, TopKSelector, attach_sel_keys
 
 __all__ = ["CAND", "DEPTHS", "DepthCollisionError", "KVSkill", "for_reader", "injection_layers", "rho_layer_map",
            "ExternalSkillInjector", "LibraryInjector", "XEncInjector", "itf_gain", "itf_gate", "itf_query",
            "itf_write", "EncoderLens", "LinearInterface", "ModelInterface", "count_params",
            "interface_param_groups", "load_interface", "make_interface", "save_interface", "Library",
-           "PagedLibrary", "LayerSelector"]
+           "PagedLibrary", "LayerSelector", "TopKLibrary", "TopKLibraryInjector", "TopKSelector", "attach_sel_keys"]

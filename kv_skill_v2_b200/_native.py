@@ -57,6 +57,9 @@ SIGNATURES: dict = {
     "xencb_summaries": (_i, [_p, _i, _i64, _i64, _i, _p, _p, _i64, _i, _i, _p, _p]),
     "xencb_library_build_workspace": (_sz, [_i, _i, _i]),
     "xencb_library_build": (_i, [_p, _i, _i64, _p, _i, _i, _p, _p, _i, _i64, _i64, _i, _p, _p, _p, _p, _sz, _p]),
+    "xencb_select_scores": (_i, [_p, _i64, _i, _i, _i, _i, _p, _i, _i64, _i, _i, _p, _p, _i64, _i64, _i, _i, _p, _p]),
+    "xencb_select_topk": (_i, [_p, _i64, _i, _i, _p, _p, _p]),
+    "xencb_topk_read": (_i, [_p, _i64, _i, _p, _p, _i, _i64, _i64, _i, _p, _i, _i64, _p, _i, _i, _f, _i, _p, _p, _p]),
 }
 
 _lib = None

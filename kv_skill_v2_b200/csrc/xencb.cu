@@ -23,6 +23,7 @@
 #include "prefill.cuh"
 #include "route.cuh"
 #include "library_build.cuh"
+#include "topk_read.cuh"
 
 // Scratch of xencb_read_decode_noalloc: a fixed device array, so that entry point never allocates.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[XENCB_NOALLOC_SCRATCH_BYTES];
@@ -1148,6 +1149,113 @@ int xencb_library_build(const void* rows, int rows_dtype, int64_t n_rows_total, 
     case XENCB_F32: return with_out(F32T{});
     case XENCB_F16: return with_out(F16T{});
     default: return with_out(BF16T{});
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ D8 top-k read
+int xencb_select_scores(const float* q, int64_t n_rows, int T, int n_q, int n_kv, int hd, const void* keys,
+                        int keys_dtype, int64_t keys_lib_stride, int page_rows, int n_chunks, const int32_t* n_valid,
+                        const int32_t* n_chunks_of, int64_t rows_per_lib, int64_t n_lib, int query_pool, int head_pool,
+                        float* scores_out, void* stream) {
+  if (!q || !keys || !n_valid || !scores_out) return fail(XENCB_EINVAL, "select_scores: null pointer argument");
+  if (n_rows <= 0 || T <= 0 || n_q <= 0 || n_kv <= 0 || hd <= 0 || page_rows <= 0 || n_chunks <= 0 ||
+      rows_per_lib <= 0 || n_lib <= 0)
+    return fail(XENCB_EINVAL, "select_scores: sizes must be positive");
+  if (n_q % n_kv) return fail(XENCB_EINVAL, "select_scores: n_q=%d is not a multiple of n_kv=%d", n_q, n_kv);
+  if (n_q / n_kv > SEL_MAX_G || n_kv > SEL_MAX_KV)
+    return fail(XENCB_ENOTSUP, "select_scores: GQA groups <= %d and n_kv <= %d are supported", SEL_MAX_G, SEL_MAX_KV);
+  if (hd % 8) return fail(XENCB_EINVAL, "select_scores: head_dim=%d must be a multiple of 8", hd);
+  if ((n_rows + rows_per_lib - 1) / rows_per_lib > n_lib)
+    return fail(XENCB_EINVAL, "select_scores: %lld rows need more than %lld Libraries", (long long)n_rows,
+                (long long)n_lib);
+  if (query_pool < 0 || query_pool > 1 || head_pool < 0 || head_pool > 1)
+    return fail(XENCB_EINVAL, "select_scores: query_pool / head_pool must be 0 (max) or 1 (mean)");
+  if ((int64_t)n_chunks * page_rows > INT32_MAX) return fail(XENCB_EINVAL, "select_scores: too many slots");
+  const int es = elem_size(keys_dtype);
+  if (keys_dtype != XENCB_F32 && keys_dtype != XENCB_F16)
+    return fail(XENCB_EINVAL, "select_scores: keys must be XENCB_F32 or XENCB_F16");
+  if (keys_lib_stride < (int64_t)n_chunks * page_rows * n_kv * hd && n_lib > 1)
+    return fail(XENCB_EINVAL, "select_scores: keys_lib_stride smaller than one Library's keys");
+  if (!aligned(q, 16) || !aligned(keys, 16) || (keys_lib_stride * es) % 16)
+    return fail(XENCB_EINVAL, "select_scores: q, keys and keys_lib_stride*elem must be 16-byte aligned");
+  SelectArgs a;
+  a.q = q; a.n_rows = n_rows; a.T = T; a.n_q = n_q; a.n_kv = n_kv; a.hd = hd; a.keys = keys;
+  a.keys_lib_stride = keys_lib_stride; a.page_rows = page_rows; a.n_chunks = n_chunks; a.n_valid = n_valid;
+  a.n_chunks_of = n_chunks_of; a.rows_per_lib = rows_per_lib; a.t_pool = query_pool; a.h_pool = head_pool;
+  a.scores = scores_out;
+  const int S = n_chunks * page_rows;
+  dim3 grid((unsigned)((S + SEL_TILE - 1) / SEL_TILE), (unsigned)n_rows);
+  if (n_rows > 65535) return fail(XENCB_ENOTSUP, "select_scores: at most 65535 rows per call");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (keys_dtype == XENCB_F32) select_scores_kernel<float><<<grid, SEL_THREADS, 0, st>>>(a);
+  else select_scores_kernel<__half><<<grid, SEL_THREADS, 0, st>>>(a);
+  XENCB_CHECK_LAUNCH("select_scores_kernel launch");
+  return XENCB_OK;
+}
+
+int xencb_select_topk(const float* scores, int64_t n_rows, int n_slots, int k, int32_t* idx_out, float* score_out,
+                      void* stream) {
+  if (!scores || !idx_out) return fail(XENCB_EINVAL, "select_topk: scores and idx_out are required");
+  if (n_rows <= 0 || n_slots <= 0 || k <= 0) return fail(XENCB_EINVAL, "select_topk: sizes must be positive");
+  if (k > n_slots) return fail(XENCB_EINVAL, "select_topk: k=%d > %d slots", k, n_slots);
+  if (k > TOPK_MAX_K) return fail(XENCB_ENOTSUP, "select_topk: k=%d above %d is not supported", k, TOPK_MAX_K);
+  if (n_rows > INT32_MAX) return fail(XENCB_EINVAL, "select_topk: too many rows");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  select_topk_kernel<<<(unsigned)n_rows, TOPK_THREADS, 0, st>>>(scores, n_slots, k, idx_out, score_out);
+  XENCB_CHECK_LAUNCH("select_topk_kernel launch");
+  return XENCB_OK;
+}
+
+int xencb_topk_read(const float* q, int64_t n_rows, int d_s, const void* slots, const void* vslots, int slots_dtype,
+                    int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of, int n_chunks,
+                    int64_t n_lib, const int32_t* idx, int n_sets, int k, float read_temp, int read_softmax,
+                    float* r_out, float* attn_out, void* stream) {
+  if (!q || !slots || !page_of || !idx || !r_out) return fail(XENCB_EINVAL, "topk_read: null pointer argument");
+  if (n_rows <= 0 || d_s <= 0 || n_pages <= 0 || page_rows <= 0 || n_chunks <= 0 || n_lib <= 0 || n_sets <= 0 ||
+      k <= 0)
+    return fail(XENCB_EINVAL, "topk_read: sizes must be positive");
+  if (n_rows % n_sets) return fail(XENCB_EINVAL, "topk_read: %lld rows are not a multiple of %d index sets",
+                                   (long long)n_rows, n_sets);
+  if (n_lib > 1 && n_lib != n_sets)
+    return fail(XENCB_EINVAL, "topk_read: %lld Libraries need one index set each (got %d)", (long long)n_lib, n_sets);
+  if (d_s % 8) return fail(XENCB_EINVAL, "topk_read: d_s=%d must be a multiple of 8", d_s);
+  const int es = elem_size(slots_dtype);
+  if (!es) return fail(XENCB_EINVAL, "topk_read: slots_dtype %d unknown", slots_dtype);
+  if (page_stride < (int64_t)page_rows * d_s) return fail(XENCB_EINVAL, "topk_read: page_stride too small");
+  if (!aligned(q, 16) || !aligned(slots, 16) || (vslots && !aligned(vslots, 16)) || !aligned(r_out, 16) ||
+      (page_stride * es) % 16)
+    return fail(XENCB_EINVAL, "topk_read: q, slots, vslots, r_out and page_stride*elem must be 16-byte aligned");
+  const size_t smem = ((size_t)TR_ROWS * d_s + (size_t)TR_ROWS * k) * sizeof(float);
+  DevInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  if (smem > (size_t)(di.max_smem_optin > 0 ? di.max_smem_optin : 232448))
+    return fail(XENCB_ENOTSUP, "topk_read: d_s=%d with k=%d does not fit in shared memory", d_s, k);
+  TopkReadArgs a;
+  a.q = q; a.n_rows = n_rows; a.d_s = d_s;
+  a.slots = static_cast<const char*>(slots);
+  a.vslots = static_cast<const char*>(vslots);
+  a.n_pages = n_pages; a.page_stride_bytes = page_stride * es; a.page_rows = page_rows; a.n_chunks = n_chunks;
+  a.page_of = page_of; a.n_lib = n_lib; a.idx = idx; a.n_sets = n_sets; a.k = k;
+  a.rows_per_set = n_rows / n_sets;
+  a.qscale = read_softmax ? read_temp * 1.4426950408889634f : 1.f;
+  a.softmax = read_softmax ? 1 : 0;
+  a.r_out = r_out; a.attn_out = attn_out;
+  const int64_t yblocks = (a.rows_per_set + TR_ROWS - 1) / TR_ROWS;
+  if (yblocks > 65535) return fail(XENCB_ENOTSUP, "topk_read: too many rows per index set");
+  dim3 grid((unsigned)n_sets, (unsigned)yblocks);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto launch = [&](auto kern) -> int {
+    int r2 = ensure_smem(kern, (int)smem);
+    if (r2) return r2;
+    kern<<<grid, TR_THREADS, smem, st>>>(a);
+    XENCB_CHECK_LAUNCH("topk_read_kernel launch");
+    return XENCB_OK;
+  };
+  switch (slots_dtype) {
+    case XENCB_F32: return launch(topk_read_kernel<float>);
+    case XENCB_F16: return launch(topk_read_kernel<__half>);
+    default: return launch(topk_read_kernel<__nv_bfloat16>);
   }
 }
 

@@ -534,6 +534,79 @@ def library_build(rows: torch.Tensor, counts, *, page_rows: Optional[int] = None
     return slots, n_valid, S
 
 
+# ------------------------------------------------------------------------------------------------ D8 top-k read
+_POOL = {"max": 0, "mean": 1}
+
+
+def select_scores(q: torch.Tensor, keys: torch.Tensor, n_valid: torch.Tensor, *, page_rows: int,
+                  rows_per_lib: int, n_chunks_of: Optional[torch.Tensor] = None, query_pool: str = "max",
+                  head_pool: str = "max") -> torch.Tensor:
+    """Selection scores [R, C * page_rows] (xenc/topk_read.py:215-239).
+
+    q [R, T, n_q, hd] float32: the reader's queries at the selection layer (T = 1 for query "last");
+    keys [n_lib, C * page_rows, n_kv, hd] (float32 / float16): the selection keys on the Library's slot grid;
+    n_valid [n_lib, C]; query_pool pools positions ("max" / "mean"), head_pool pools heads ("max" / "mean")."""
+    dev = _cuda("select_scores", q, keys, n_valid, n_chunks_of)
+    q = _f32(q, "q")
+    if q.dim() != 4:
+        raise ValueError("select_scores: q must be [R, T, n_q, hd]")
+    R, T, n_q, hd = q.shape
+    if keys.dim() != 4 or keys.shape[-1] != hd:
+        raise ValueError(f"select_scores: keys must be [n_lib, slots, n_kv, {hd}]")
+    n_lib, S, n_kv, _ = keys.shape
+    n_lib2, C = n_valid.shape
+    if n_lib2 != n_lib or S != C * int(page_rows):
+        raise ValueError(f"select_scores: keys hold {S} slots per Library, n_valid gives {C} x {page_rows}")
+    keys = keys.contiguous()
+    nv = n_valid.to(torch.int32).contiguous()
+    nco = None if n_chunks_of is None else n_chunks_of.to(torch.int32).contiguous()
+    out = torch.empty(R, S, dtype=torch.float32, device=dev)
+    with _on_device(dev):
+        N.call("xencb_select_scores", _ptr(q), R, T, n_q, n_kv, hd, _ptr(keys), _hdt(keys, "keys"), S * n_kv * hd,
+               int(page_rows), C, _ptr(nv), _ptr(nco), int(rows_per_lib), n_lib, _POOL[query_pool],
+               _POOL[head_pool], _ptr(out), _stream(dev))
+    return out
+
+
+def select_topk(scores: torch.Tensor, k: int):
+    """(idx [R, k] int32, values [R, k] float32): the k largest scores per row, sorted descending (ties: lower
+    slot first) -- sc.topk(k) of xenc/topk_read.py:254."""
+    dev = _cuda("select_topk", scores)
+    scores = _f32(scores, "scores")
+    R, S = scores.shape
+    idx = torch.empty(R, int(k), dtype=torch.int32, device=dev)
+    val = torch.empty(R, int(k), dtype=torch.float32, device=dev)
+    with _on_device(dev):
+        N.call("xencb_select_topk", _ptr(scores), R, S, int(k), _ptr(idx), _ptr(val), _stream(dev))
+    return idx, val
+
+
+def topk_read(q: torch.Tensor, pages: Pages, idx: torch.Tensor, *, read_temp: float = 12.0,
+              read_softmax: bool = True, want_attn: bool = False):
+    """(r [R, d_s], attn [R, k] | None): the read restricted to the selected slots (xenc/topk_read.py:392-413).
+
+    idx [n_sets, k] int32 flat slot indices (chunk * page_rows + row); rows are split evenly over the index
+    sets in order, and set b reads Library b when pages holds several Libraries."""
+    dev = _cuda("topk_read", q, pages.slots, pages.page_of, idx)
+    q = _f32(q, "q")
+    R, d_s = q.shape
+    slots = pages.slots
+    if not slots.is_contiguous() or slots.shape[-1] != d_s:
+        raise ValueError(f"topk_read: slots must be a contiguous [P, page_rows, {d_s}] pool")
+    if idx.dtype != torch.int32 or idx.dim() != 2:
+        raise ValueError("topk_read: idx must be int32 [n_sets, k]")
+    n_sets, k = idx.shape
+    idx = idx.contiguous()
+    r = torch.empty(R, d_s, dtype=torch.float32, device=dev)
+    attn = torch.empty(R, k, dtype=torch.float32, device=dev) if want_attn else None
+    with _on_device(dev):
+        N.call("xencb_topk_read", _ptr(q), R, d_s, _ptr(slots), _ptr(_vpool(pages)), _hdt(slots, "slots"),
+               slots.shape[0], pages.page_rows * d_s, pages.page_rows, _ptr(pages.page_of), pages.n_chunks,
+               pages.n_lib, _ptr(idx), n_sets, k, float(read_temp), int(bool(read_softmax)), _ptr(r), _ptr(attn),
+               _stream(dev))
+    return r, attn
+
+
 def device_status(dev: torch.device, clear: bool = True) -> int:
     """Synchronise the current stream of `dev` and return the device status bits (XENCB_DEV_*)."""
     v = ctypes.c_uint(0)

@@ -244,3 +244,58 @@ def merge_shards(parts: list) -> np.ndarray:
 __all__ = ["l2", "rms_norm", "softmax", "topk_indices", "build_library", "summaries", "subset", "query",
            "gate", "route", "read", "branch", "selector_weights", "selector_logits", "selector_apply",
            "rel_norm", "shard_partials", "merge_shards"]
+
+
+# ----------------------------------------------------------------------------------------------- D8 top-k read
+def topk_select_scores(q: np.ndarray, keys: np.ndarray, valid: np.ndarray, query: str = "last",
+                       pool: str = "max") -> np.ndarray:
+    """TopKSelector.head_scores + pool_scores (xenc/topk_read.py:215-239).
+
+    q [B, n_q, T, hd]; keys [S, n_kv, hd]; valid [S] bool. Query head h scores KV head h // groups (GQA);
+    positions pooled per `query` (last | all_max | all_mean), heads per `pool` (max | mean); invalid = -inf."""
+    q = np.asarray(q, F32)
+    B, n_q, T, hd = q.shape
+    keys = np.asarray(keys, F32)
+    n_kv = keys.shape[1]
+    groups = n_q // n_kv
+    qh = q.reshape(B, n_kv, groups, T, hd)
+    s = np.einsum("bkgtd,skd->bkgts", qh, keys).reshape(B, n_q, T, -1).astype(F32)
+    if query == "last":
+        s = s[:, :, -1]
+    elif query == "all_max":
+        s = s.max(2)
+    elif query == "all_mean":
+        s = s.mean(2, dtype=F32)
+    else:
+        raise ValueError(f"unknown selection query {query}")
+    s = s.max(1) if pool == "max" else s.mean(1, dtype=F32)
+    return np.where(np.asarray(valid, bool)[None, :], s, F32(-np.inf)).astype(F32)
+
+
+def topk_select(scores: np.ndarray, k: int) -> np.ndarray:
+    """sc.topk(k).indices (xenc/topk_read.py:254): per row the k largest, sorted descending; ties (which
+    torch.topk leaves unordered) go to the lower slot here. -> [B, k] int64."""
+    scores = np.asarray(scores, F32)
+    order = np.lexsort((np.arange(scores.shape[-1])[None, :].repeat(scores.shape[0], 0), -scores), axis=-1)
+    return order[:, :k].astype(np.int64)
+
+
+def topk_read(q: np.ndarray, Kf: np.ndarray, idx: np.ndarray, read_temp: float = 12.0,
+              read_softmax: bool = True, Vf: np.ndarray | None = None):
+    """The read of TopKLibraryInjector._branch (xenc/topk_read.py:392-405, 412).
+
+    q [B, T, d_s]; Kf [C*N, d_s] (the padded Library flattened); idx [B, k] (or [1, k], broadcast over B).
+    a = q . Kf[idx]; softmax(a * read_temp) over k, or a / sqrt(k); r = a @ Vf[idx]. -> (r [B, T, d_s], a)."""
+    q = np.asarray(q, F32)
+    Kf = np.asarray(Kf, F32)
+    Vf = Kf if Vf is None else np.asarray(Vf, F32)
+    idx = np.asarray(idx)
+    if idx.shape[0] != q.shape[0]:
+        idx = np.repeat(idx[:1], q.shape[0], 0)
+    Ks, Vs = Kf[idx], Vf[idx]                                   # [B, k, d_s]
+    a = np.einsum("btd,bkd->btk", q, Ks).astype(F32)
+    if read_softmax:
+        a = softmax(a * F32(read_temp), -1)
+    else:
+        a = (a / F32(idx.shape[-1] ** 0.5)).astype(F32)
+    return np.einsum("btk,bkd->btd", a, Vs).astype(F32), a

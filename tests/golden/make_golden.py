@@ -16,7 +16,8 @@ sibling checkout, xenc/__init__.py:14-18), so a minimal stand-in is installed in
 * deltaskill.interface.ModelInterface A (Linear d_m->d_s, no bias), B (Linear d_s->d_m), gate_w [d_m],
                                      gate_b [L], log_gain [L], _pos -- the members xenc/injector.py:54-77
                                      reads (shapes ASSUMED).
-* deltaskill.skill.KVSkill, deltaskill.backbone_utils.decoder_layers.
+* deltaskill.skill.KVSkill, deltaskill.backbone_utils.decoder_layers (and placeholders for the chat helpers
+                                     that xenc.backbone imports; the read path never calls them).
 
 Outputs are small .npz files; the tests (which never read the reference) compare the oracle and the CUDA
 path against them. Inputs are generated with torch.Generator seeds so the cases are reproducible.
@@ -57,6 +58,11 @@ def _install_deltaskill_stub() -> None:
 
     bu = types.ModuleType("deltaskill.backbone_utils")
     bu.decoder_layers = lambda model: model.model.layers
+
+    def _unused(*a, **k):  # chat / decoding helpers xenc.backbone imports; never called on the read path
+        raise NotImplementedError("deltaskill stand-in: not part of the Library read")
+
+    bu.chat_template_kwargs = bu.final_channel = bu.is_gpt_oss = bu.skip_special_on_decode = _unused
 
     skill = types.ModuleType("deltaskill.skill")
 
@@ -418,6 +424,89 @@ def gen_hooked(out):
     out["hooked"] = rec
 
 
+def gen_topk(out):
+    """D8 top-k slot-selection read (xenc/topk_read.py): the reference's TopKLibraryInjector on a tiny attention
+    reader (tests/_fixtures.TinyAttnReader) with a ModelInterface, three settings: query "last" + max pool +
+    softmax read through both hook paths (model(x) and logits(x)) with record_attn; "all_mean" + mean pool + linear
+    read at a training-style selection position; two batch rows with "all_max"."""
+    sys.path.insert(0, str(HERE.parents[1]))
+    from deltaskill.interface import ModelInterface
+    from tests._fixtures import TinyAttnReader
+    from xenc.library import Library
+    from xenc.topk_read import TopKLibraryInjector, TopKSelector, attach_sel_keys
+
+    D, L, NKV, HD, G = 32, 8, 2, 8, 2
+    LAYERS, SEL, DS, DEP = [1, 3, 5, 7], 3, 24, [0.2, 0.4, 0.6, 0.8]
+
+    def setup(seed, ns):
+        g = torch.Generator().manual_seed(seed)
+        m = TinyAttnReader(D, L, NKV, HD, G, seed=seed).eval().requires_grad_(False)
+        chunks = [{"K": {r: _unit_rows(n, DS, g) for r in DEP}, "start": 16 * c, "n_tokens": n}
+                  for c, n in enumerate(ns)]
+        lib = Library(chunks, LAYERS, DEP)
+        ac = {"chunks": [{"K": {0.25: torch.randn(n, NKV * HD, generator=g).half()}} for n in ns]}
+        lib = attach_sel_keys(lib, ac, 0.25)
+        itf = ModelInterface(D, DS, LAYERS)
+        with torch.no_grad():
+            for p_ in itf.parameters():
+                p_.copy_(torch.randn(p_.shape, generator=g) * 0.3)
+        rec = m.arrays()
+        rec["n"] = np.array(ns, np.int32)
+        for li in LAYERS:
+            rec[f"K_{li}"] = _np(lib.K[li])
+        rec["sel_K"] = _np(lib.sel_K)
+        rec["A_w"], rec["B_w"] = _np(itf.A.weight), _np(itf.B.weight)
+        rec["gate_w"], rec["gate_b"], rec["log_gain"] = _np(itf.gate_w), _np(itf.gate_b), _np(itf.log_gain)
+        return g, m, lib, itf, rec
+
+    # 1: query last, max pool, softmax read, k = 7 of 41 valid slots
+    g, m, lib, itf, rec = setup(61, (16, 16, 9))
+    x = torch.randn(1, 11, D, generator=g)
+    inj = TopKLibraryInjector(m, itf, TopKSelector(m, SEL, k=7), read_temp=12.0)
+    inj.load_library(lib)
+    with torch.no_grad():
+        y = m(x)
+        rec["out_call"], rec["idx_call"], rec["scores_call"] = _np(y), _np(inj.last_idx), _np(inj.tk.last_scores)
+        rec["mag_call"] = np.array([float(t) for t in inj.mag_terms], np.float32)
+        inj.record_attn = True
+        lg = m.logits(x)
+    rec["x"], rec["logits"], rec["idx"] = _np(x), _np(lg), _np(inj.last_idx)
+    for li in LAYERS:
+        rec[f"attn_{li}"] = _np(inj.last_attn[li])
+    rec.update({"k": np.int32(7), "query": np.array("last"), "pool": np.array("max"), "read_softmax": np.int32(1),
+                "sel_pos": np.int32(-1), "passes": np.int32(inj.n_select_passes)})
+    inj.detach()
+    out["topk_last_softmax"] = rec
+
+    # 2: query all_mean, mean pool, linear read, selection at the last prompt position (-4)
+    g, m, lib, itf, rec = setup(62, (16, 12, 16))
+    x = torch.randn(1, 10, D, generator=g)
+    inj = TopKLibraryInjector(m, itf, TopKSelector(m, SEL, k=6, pool="mean", query="all_mean"), read_temp=12.0,
+                              read_softmax=False)
+    inj.load_library(lib)
+    inj.sel_pos = -4
+    with torch.no_grad():
+        lg = m.logits(x)
+    rec.update({"x": _np(x), "logits": _np(lg), "idx": _np(inj.last_idx), "scores": _np(inj.tk.last_scores),
+                "k": np.int32(6), "query": np.array("all_mean"), "pool": np.array("mean"),
+                "read_softmax": np.int32(0), "sel_pos": np.int32(-4)})
+    inj.detach()
+    out["topk_allmean_linear"] = rec
+
+    # 3: two batch rows, query all_max: each row selects (and reads) its own slots
+    g, m, lib, itf, rec = setup(63, (16, 16, 16, 5))
+    x = torch.randn(2, 9, D, generator=g)
+    inj = TopKLibraryInjector(m, itf, TopKSelector(m, SEL, k=5, query="all_max"), read_temp=12.0)
+    inj.load_library(lib)
+    with torch.no_grad():
+        lg = m.logits(x)
+    rec.update({"x": _np(x), "logits": _np(lg), "idx": _np(inj.last_idx), "scores": _np(inj.tk.last_scores),
+                "k": np.int32(5), "query": np.array("all_max"), "pool": np.array("max"), "read_softmax": np.int32(1),
+                "sel_pos": np.int32(-1)})
+    inj.detach()
+    out["topk_batch2_allmax"] = rec
+
+
 def main() -> None:
     if not (REF / "xenc" / "injector.py").exists():
         raise SystemExit(f"reference checkout not found at {REF}")
@@ -426,7 +515,7 @@ def main() -> None:
     torch.set_num_threads(1)
     out: dict = {}
     gens = {"cfg1": gen_cfg1, "small": gen_small, "batch_docs": gen_batch_docs, "selector": gen_selector,
-            "library": gen_library, "hooked": gen_hooked, "untied": gen_untied}
+            "library": gen_library, "hooked": gen_hooked, "untied": gen_untied, "topk": gen_topk}
     wanted = sys.argv[1:] or list(gens)  # e.g. `python make_golden.py untied` regenerates one group
     for nm in wanted:
         gens[nm](out)

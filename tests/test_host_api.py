@@ -207,3 +207,47 @@ def test_injector_guards_and_no_cpu_path():
     with torch.no_grad():
         reader(torch.randn(2, 5, 32))  # unloaded: the bare model runs
     inj.detach()
+
+
+def test_topk_library_keys_gold_hit_and_no_cpu_path():
+    """D8 host logic (xenc tests/test_topk_read.py (c), (e)): sel_K follows subset, misaligned harvests raise,
+    gold-hit statistics against brute force, and the selection has no CPU path."""
+    import math
+    from itertools import combinations
+
+    from kv_skill_v2_b200.topk_read import TopKLibrary, TopKSelector, attach_sel_keys
+    from tests._fixtures import TinyAttnReader
+
+    g = torch.Generator().manual_seed(9)
+    depths, layers = [0.2, 0.4, 0.6, 0.8], [1, 3, 5, 7]
+    ns = (16, 16, 9)
+    lib = Library([{"K": {r: unit_rows(n, 24, g) for r in depths}} for n in ns], layers, depths)
+    lib = attach_sel_keys(lib, {"chunks": [{"K": {0.25: torch.randn(n, 16, generator=g)}} for n in ns]}, 0.25)
+    assert isinstance(lib, TopKLibrary) and lib.sel_K.shape == (3, 16, 16)
+    sub = lib.subset([2, 0])
+    assert isinstance(sub, TopKLibrary) and sub.sel_K.shape[:2] == sub.mask[layers[0]].shape
+    assert torch.equal(sub.sel_K[1], lib.sel_K[0, : sub.sel_K.shape[1]])
+    bad = Library([{"K": {r: unit_rows(n, 24, g) for r in depths}} for n in ns], layers, depths)
+    with pytest.raises(ValueError):
+        attach_sel_keys(bad, {"chunks": [{"K": {0.25: torch.zeros(5, 16)}}] * 3}, 0.25)
+
+    m = TinyAttnReader(32, 8, 2, 8, 2)
+    sel = TopKSelector(m, 3, k=3)
+    n = 10
+    sel.valid = torch.ones(n, dtype=torch.bool)
+    sel.last_scores = torch.arange(n, dtype=torch.float32).flip(0).unsqueeze(0)
+    gold = torch.zeros(n, dtype=torch.bool)
+    gold[[4, 7]] = True
+    st = sel.gold_hit(gold, ks=[3, 5])
+    assert st["n_gold"] == 2 and st["best_rank"] == 4
+    assert st[3]["hit"] == 0.0 and st[5]["hit"] == 1.0 and st[5]["n_gold_sel"] == 1
+    for k in (3, 5):
+        brute = sum(any(i in (4, 7) for i in cmb) for cmb in combinations(range(n), k)) / math.comb(n, k)
+        assert abs(st[k]["chance_any"] - brute) < 1e-9
+        assert abs(st[k]["chance_frac"] - k * 2 / n) < 1e-12
+    assert sel.gold_hit(torch.zeros(n, dtype=torch.bool)) == {}
+
+    sel.set_keys(lib.sel_K, lib.mask[layers[0]])
+    assert sel.n_valid == 41 and sel.keys.shape == (48, 2, 8)
+    with pytest.raises(RuntimeError, match="CPU"):
+        sel.select_from_input(torch.randn(1, 5, 32))

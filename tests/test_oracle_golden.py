@@ -135,3 +135,72 @@ def test_untied_values_and_centering(name):
     assert topk_sets(out["w"]) == topk_sets(c["w"].reshape(out["w"].shape))
     assert rel_err(out["r"], c["r"].reshape(out["r"].shape)) < 1e-5
     assert rel_err(out["delta"], c["delta"].reshape(out["delta"].shape)) < 1e-5
+
+
+# ------------------------------------------------------------------------------------------------ D8 top-k read
+TOPK_CASES = ["topk_last_softmax", "topk_allmean_linear", "topk_batch2_allmax"]
+
+
+def _topk_oracle_forward(c):
+    """The reference's hooked D8 forward restated with the oracle: the selection from the bare reader's queries
+    at layer 3, then at each injection layer h + gain * sigmoid(hn . gate_w + gate_b) * B (topk_read(A hn))."""
+    import torch
+    from kv_skill_v2_b200.topk_read import attn_geometry, reader_queries
+    from tests._fixtures import TinyAttnReader
+
+    m = TinyAttnReader(32, 8, 2, 8, 2).load_arrays(c).eval()
+    layers, sel_layer = [1, 3, 5, 7], 3
+    x = torch.from_numpy(c["x"])
+    att = m.model.layers[sel_layer].self_attn
+    cap = {}
+    hook = att.register_forward_pre_hook(lambda mod, a: cap.setdefault("x", a[0].detach().clone()))
+    with torch.no_grad():
+        m(x)
+    hook.remove()
+    T = x.shape[1]
+    pos = T + int(c["sel_pos"]) if int(c["sel_pos"]) < 0 else int(c["sel_pos"])
+    with torch.no_grad():
+        q_sel = reader_queries(att, cap["x"][:, : pos + 1], attn_geometry(att)).numpy()
+    n = c["n"]
+    C, N = len(n), c[f"K_{layers[0]}"].shape[1]
+    valid = (np.arange(N)[None, :] < n[:, None]).reshape(-1)
+    keys = c["sel_K"].reshape(C * N, 2, 8)
+    scores = X.topk_select_scores(q_sel, keys, valid, query=str(c["query"]), pool=str(c["pool"]))
+    k = min(int(c["k"]), int(valid.sum()))
+    idx = X.topk_select(scores, k)
+
+    pos_of = {li: i for i, li in enumerate(layers)}
+
+    def inject(mod, args, out, li):
+        h = out.detach().numpy()
+        B, Tq, d = h.shape
+        hn = X.rms_norm(h.reshape(-1, d))
+        q = X.l2(hn @ c["A_w"].T).reshape(B, Tq, -1)
+        r, _ = X.topk_read(q, c[f"K_{li}"].reshape(C * N, -1), idx, read_softmax=bool(c["read_softmax"]))
+        p = pos_of[li]
+        g = 1.0 / (1.0 + np.exp(-(hn @ c["gate_w"] + c["gate_b"][p])))
+        delta = np.exp(c["log_gain"][p]) * g.reshape(B, Tq, 1) * (r @ c["B_w"].T)
+        return torch.from_numpy((h + delta).astype(np.float32))
+
+    hs = [m.model.layers[li].register_forward_hook(lambda mod, a, o, li=li: inject(mod, a, o, li)) for li in layers]
+    with torch.no_grad():
+        lg = m.logits(x).numpy()
+    for hd in hs:
+        hd.remove()
+    return scores, idx, lg
+
+
+@pytest.mark.parametrize("name", TOPK_CASES)
+def test_topk_oracle_matches_reference(name):
+    """Selection scores, the selected slot sets (in score order) and the hooked model's logits of the reference's
+    TopKLibraryInjector, restated with the oracle (selection query / pool modes, softmax and linear reads, two
+    batch rows with their own selections)."""
+    c = load_case(name)
+    scores, idx, lg = _topk_oracle_forward(c)
+    ref_scores = c["scores_call"] if "scores_call" in c else c["scores"]
+    fin = np.isfinite(ref_scores)
+    assert np.array_equal(fin, np.isfinite(scores))
+    assert np.abs(scores[fin] - ref_scores[fin]).max() < 1e-5
+    assert [set(r) for r in idx.tolist()] == [set(r) for r in c["idx"].tolist()]
+    assert np.array_equal(idx, c["idx"]), "selection order (score descending) differs"
+    assert rel_err(lg, c["logits"]) < 1e-5
