@@ -64,6 +64,8 @@ def parse_args(argv=None):
     ap.add_argument("--prefill-docs", type=int, default=8,
                     help="documents of the config-3 prefill (8 = the config; fewer only for profiler captures)")
     ap.add_argument("--no-library-build", action="store_true", help="skip the device Library build")
+    ap.add_argument("--no-topk", action="store_true", help="skip the D8 top-k slot read")
+    ap.add_argument("--topk-only", action="store_true", help="only the D8 top-k slot read")
     ap.add_argument("--library-build-only", action="store_true",
                     help="only the device Library build (config-2 shapes)")
     ap.add_argument("--library-build-docs", type=int, default=16,
@@ -574,6 +576,130 @@ def run_library_build(torch, dist, dev, world: int, rank: int, steps: int, warmu
     return res
 
 
+CFGK = dict(docs=64, C=64, N=512, d_s=2048, n_q=32, n_kv=8, hd=128, k=64, sel_docs=16)
+
+
+def run_topk(torch, dist, dev, world: int, rank: int, steps: int, warmup: int, flush, stream,
+             cpu_seconds: float = 0.0) -> dict:
+    """D8 top-k slot read (xenc/topk_read.py) at config-2 Library shapes: 64 documents of 64 chunks x 512 fp16
+    slots (d_s 2048), k = 64 selected slots per document, one decode token per document.
+
+    select: per document the selection scores of one query (32 query heads, 8 KV heads of 128: a Qwen3-8B-like
+      geometry) against its 32,768 fp16 selection keys (64 MiB), pooled max over heads, then the top-64; run
+      for 16 documents per step (1 GiB of keys: larger than L2). Algorithmic bytes: the keys once.
+    read: per decode step the gathered read of 64 documents (64 slots each) -- scores, softmax over the 64, the
+      weighted sum; algorithmic bytes: the 64 selected rows once per document (tied V = K), q and r.
+      L2 flushed between steps."""
+    import numpy as np
+
+    from kv_skill_v2_b200 import _native, ops
+
+    B, C, N, d = CFGK["docs"], CFGK["C"], CFGK["N"], CFGK["d_s"]
+    n_q, n_kv, hd, k, SB = CFGK["n_q"], CFGK["n_kv"], CFGK["hd"], CFGK["k"], CFGK["sel_docs"]
+    g = torch.Generator(device=dev).manual_seed(6000 + rank)
+    S = C * N
+    keys = (torch.randn(SB, S, n_kv, hd, generator=g, device=dev) * 0.1).half()
+    nv = torch.full((SB, C), N, dtype=torch.int32, device=dev)
+    nv[:, -1] = N // 3
+    qs = torch.randn(SB, 1, n_q, hd, generator=g, device=dev)
+    pool = torch.empty(B * C, N, d, dtype=torch.float16, device=dev)
+    for c0 in range(0, B * C, 256):
+        x = torch.randn(min(256, B * C - c0), N, d, generator=g, device=dev)
+        pool[c0:c0 + x.shape[0]] = (x / x.norm(dim=-1, keepdim=True)).half()
+        del x
+    pages = ops.Pages(slots=pool, page_of=torch.arange(B * C, dtype=torch.int32, device=dev).view(B, C),
+                      n_valid=torch.full((B, C), N, dtype=torch.int32, device=dev),
+                      S=torch.zeros(1, 1, 1, device=dev))
+    q = torch.nn.functional.normalize(torch.randn(B, d, generator=g, device=dev), dim=-1)
+    idx = torch.stack([torch.randperm(S, device=dev)[:k] for _ in range(B)]).to(torch.int32)
+
+    def select():
+        sc = ops.select_scores(qs, keys, nv, page_rows=N, rows_per_lib=1)
+        return ops.select_topk(sc, k)
+
+    def read():
+        return ops.topk_read(q, pages, idx)
+
+    # parity spot checks against the oracle (one document each)
+    from oracle import xenc_oracle as X
+    sel_idx, _ = select()
+    valid = (np.arange(N)[None, :] < nv[0].cpu().numpy()[:, None]).reshape(-1)
+    ref_sc = X.topk_select_scores(qs[:1].permute(0, 2, 1, 3).cpu().numpy(), keys[0].float().cpu().numpy(), valid)
+    assert set(sel_idx[0].cpu().tolist()) == set(X.topk_select(ref_sc, k)[0].tolist()), "select: sets differ"
+    r, _ = read()
+    Kf = pool[:C].float().reshape(C * N, d).cpu().numpy()
+    ref_r, _ = X.topk_read(q[:1].cpu().numpy()[None], Kf, idx[:1].cpu().numpy())
+    assert float(np.abs(r[0].cpu().numpy() - ref_r[0, 0]).max()) <= 2e-3 * float(np.abs(ref_r).max()), "read differs"
+
+    def timed(fn, n_steps, flush_between):
+        for _ in range(warmup):
+            fn()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        n0 = _native.launch_count()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_steps)]
+        for i in range(n_steps):
+            if flush_between:
+                flush.fill_(i & 0xFF)
+            ev[i][0].record(stream)
+            fn()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+        t = sum(a.elapsed_time(b) for a, b in ev)
+        if world > 1:
+            tt = torch.tensor([t], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t / n_steps, (_native.launch_count() - n0) // n_steps
+
+    ms_sel, kern_sel = timed(select, max(3, steps // 20), False)
+    ms_read, kern_read = timed(read, steps, True)
+    peak, peak_kind = hbm_peak()
+    sel_bytes = SB * S * n_kv * hd * 2 + SB * n_q * hd * 4 + SB * S * 4 * 2
+    read_bytes = B * k * d * 2 + 2 * B * d * 4 + B * k * 4
+    res = {"workload": f"D8 top-k slot read at config-2 Library shapes: {B} documents x {C} chunks x {N} fp16 slots, "
+                       f"d_s {d}, k {k}; selection keys {n_kv} KV heads x {hd} (fp16), {n_q} query heads",
+           "select": {"metric": "documents selected per second (whole job)", "value": SB * world / (ms_sel / 1e3),
+                      "unit": "documents/s", "ms_per_step": ms_sel, "docs_per_step": SB, "kernels_per_step": kern_sel,
+                      "roofline": {"bound": "hbm", "kernel": "select_scores_kernel + select_topk_kernel",
+                                   "achieved": sel_bytes / (ms_sel / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                                   "frac": sel_bytes / (ms_sel / 1e3) / 1e9 / peak,
+                                   "algorithmic_bytes_per_step": sel_bytes, "peak_source": peak_kind},
+                      "l2": "1 GiB of keys per step (larger than L2)"},
+           "read": {"metric": "D8 decode-read tokens/s (whole job)", "value": B * world / (ms_read / 1e3),
+                    "unit": "tokens/s", "ms_per_step": ms_read, "kernels_per_step": kern_read,
+                    "roofline": {"bound": "hbm", "kernel": "topk_read_kernel",
+                                 "achieved": read_bytes / (ms_read / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                                 "frac": read_bytes / (ms_read / 1e3) / 1e9 / peak,
+                                 "algorithmic_bytes_per_step": read_bytes, "peak_source": peak_kind},
+                    "l2": "flushed between steps (256 MiB write)"},
+           "n_gpus": world, "scaling": "weak"}
+    if rank == 0 and world == 1 and cpu_seconds > 0:
+        kq = keys[0].float().cpu().numpy()
+        q0 = qs[:1].permute(0, 2, 1, 3).cpu().numpy()
+        spent, n = 0.0, 0
+        while spent < cpu_seconds / 2 and n < 20:
+            t0 = time.perf_counter()
+            X.topk_select(X.topk_select_scores(q0, kq, valid), k)
+            spent += time.perf_counter() - t0
+            n += 1
+        res["select"]["cpu_baseline"] = {"value": n / spent, "unit": "documents/s", "cores": 1, "kind": "port",
+                                         "sample": f"{n} selections of one document (oracle, numpy)"}
+        qn = q[:1].cpu().numpy()[None]
+        ix = idx[:1].cpu().numpy()
+        spent, n = 0.0, 0
+        while spent < cpu_seconds / 2 and n < 2000:
+            t0 = time.perf_counter()
+            X.topk_read(qn, Kf, ix)
+            spent += time.perf_counter() - t0
+            n += 1
+        res["read"]["cpu_baseline"] = {"value": n / spent, "unit": "tokens/s", "cores": 1, "kind": "port",
+                                       "sample": f"{n} decode reads of one document (oracle.topk_read, numpy)"}
+    del keys, pool
+    return res
+
+
 CFG3 = dict(docs=8, T=2048, C=128, N=512, d_s=2048, d_m=4096, read_temp=12.0, route_temp=10.0)
 
 
@@ -702,9 +828,13 @@ def run_ours(args) -> None:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
-    if args.sharded_only or args.selector_only or args.prefill_only or args.library_build_only:
+    if args.sharded_only or args.selector_only or args.prefill_only or args.library_build_only or args.topk_only:
         flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
-        if args.library_build_only:
+        if args.topk_only:
+            res = run_topk(torch, dist, dev, world, rank, args.steps, args.warmup, flush,
+                           torch.cuda.current_stream(dev),
+                           cpu_seconds=0.0 if args.no_cpu_baseline else args.cpu_seconds)
+        elif args.library_build_only:
             res = run_library_build(torch, dist, dev, world, rank, args.steps, args.warmup,
                                     torch.cuda.current_stream(dev),
                                     cpu_seconds=0.0 if args.no_cpu_baseline else args.cpu_seconds,
@@ -868,7 +998,9 @@ def run_ours(args) -> None:
             t_e2e = float(t.item())
         e2e = R * args.steps * world / (t_e2e / 1000.0)
         inj.detach()
-        sharded = selector = prefill = lbuild = None
+        sharded = selector = prefill = lbuild = topk = None
+        if not args.no_topk:
+            topk = run_topk(torch, dist, dev, world, rank, args.steps, args.warmup, flush, stream)
         if not args.no_library_build:
             lbuild = run_library_build(torch, dist, dev, world, rank, max(3, args.steps // 20), args.warmup, stream)
         if not args.no_prefill:
@@ -911,6 +1043,7 @@ def run_ours(args) -> None:
             "selector": selector,
             "prefill": prefill,
             "library_build": lbuild,
+            "topk": topk,
             "clocks": clocks, "device_status": status}
     print(json.dumps(line), flush=True)
 

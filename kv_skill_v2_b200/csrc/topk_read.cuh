@@ -5,8 +5,8 @@
 //   pool_t: the one position given (query "last"), max ("all_max") or mean ("all_mean") over T positions;
 //   pool_h: max or mean over the n_q heads; slots that are not valid (n >= n_valid of the chunk, or a chunk past
 //   the Library's count) get -inf. Keys are [C * page_rows, n_kv * hd] per Library (the selection keys laid out
-//   on the residual Library's pages), float32 or float16. Grid (32-slot tiles, rows); warp w takes KV heads
-//   w, w + 8, ...; lane = slot; q is read with warp-uniform addresses (L1 broadcasts).
+//   on the residual Library's pages), float32 or float16. Grid (128-slot tiles, rows); warp w takes KV heads
+//   w, w + 8, ...; lane l scores slots l + 32u (u < 4); q is read with warp-uniform addresses (L1 broadcasts).
 //   Bound: HBM (keys read once per query row) or FMA issue, whichever is larger (about 2 FMA per key byte).
 // select_topk_kernel  (TopKSelector.select_from_input: sc.topk(k), :251-254)
 //   One CTA per row: radix select of the k-th largest score (4 passes of 8-bit histograms over orderable keys),
@@ -18,8 +18,10 @@
 //   selected rows (one row per warp at a time), warps 0..TR-1 finish one query row's softmax each, then each
 //   thread owns 8 columns and sums the selected value rows. Slot s of set b is row s % page_rows of page
 //   page_of[lib, s / page_rows] (lib = b when there are several Libraries, else 0).
+// topk_read_decode_kernel: the same read for one query row per set, split over a 4-CTA cluster (see below).
 #pragma once
 
+#include <cooperative_groups.h>
 #include <math_constants.h>
 
 #include "common.cuh"
@@ -27,7 +29,8 @@
 namespace xencb {
 
 constexpr int SEL_THREADS = 256;
-constexpr int SEL_TILE = 32;        // slots per CTA
+constexpr int SEL_SPT = 4;          // slots per thread
+constexpr int SEL_TILE = 32 * SEL_SPT;  // slots per CTA
 constexpr int SEL_MAX_G = 16;       // GQA group size supported
 constexpr int SEL_MAX_KV = 64;
 constexpr int TOPK_THREADS = 1024;
@@ -50,71 +53,109 @@ struct SelectArgs {
   float* scores;           // [R, C * page_rows]
 };
 
-template <typename TK>
+// G: the GQA group size (query heads per KV head); each thread scores SEL_SPT slots (lane + 32 u) of one KV head,
+// so every broadcast q load feeds SEL_SPT x 8 FMAs.
+template <typename TK, int G>
 __global__ void __launch_bounds__(SEL_THREADS) select_scores_kernel(const SelectArgs a) {
   __shared__ float red[SEL_MAX_KV][SEL_TILE];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = blockIdx.y;
   const int64_t lib = row / a.rows_per_lib;
   const int S = a.n_chunks * a.page_rows;
-  const int slot = blockIdx.x * SEL_TILE + lane;
-  const int g = a.n_q / a.n_kv;
+  const int base = blockIdx.x * SEL_TILE;
   const int d_k = a.n_kv * a.hd;
   const TK* kb = static_cast<const TK*>(a.keys) + lib * a.keys_lib_stride;
   const float* qrow = a.q + row * (int64_t)a.T * a.n_q * a.hd;
 
+  auto dot8 = [](float sv, const float4& q0, const float4& q1, const float* k) {
+    sv = fmaf(q0.x, k[0], sv); sv = fmaf(q0.y, k[1], sv); sv = fmaf(q0.z, k[2], sv); sv = fmaf(q0.w, k[3], sv);
+    sv = fmaf(q1.x, k[4], sv); sv = fmaf(q1.y, k[5], sv); sv = fmaf(q1.z, k[6], sv); sv = fmaf(q1.w, k[7], sv);
+    return sv;
+  };
+  auto load_k = [&](const TK* p, float* out) {
+    if constexpr (sizeof(TK) == 4) {
+      unpack16<float>(__ldg(reinterpret_cast<const uint4*>(p)), out);
+      unpack16<float>(__ldg(reinterpret_cast<const uint4*>(p + 4)), out + 4);
+    } else {
+      unpack16<TK>(__ldg(reinterpret_cast<const uint4*>(p)), out);
+    }
+  };
+  const float init_h = a.h_pool == 0 ? -CUDART_INF_F : 0.f;
   for (int kv = warp; kv < a.n_kv; kv += SEL_THREADS / 32) {
-    float hv[SEL_MAX_G];  // per head of the group, pooled over positions
+    const TK* kr[SEL_SPT];
 #pragma unroll
-    for (int i = 0; i < SEL_MAX_G; ++i) hv[i] = a.t_pool == 0 ? -CUDART_INF_F : 0.f;
-    if (slot < S) {
-      const TK* kr = kb + (int64_t)slot * d_k + kv * a.hd;
-      for (int t = 0; t < a.T; ++t) {
-        const float* qk = qrow + ((int64_t)t * a.n_q + kv * g) * a.hd;  // the group's heads at position t
-        float acc[SEL_MAX_G];
+    for (int u = 0; u < SEL_SPT; ++u) {
+      const int slot = base + lane + 32 * u;
+      kr[u] = kb + (int64_t)(slot < S ? slot : 0) * d_k + kv * a.hd;  // slots past S read slot 0, never stored
+    }
+    float p[SEL_SPT];
 #pragma unroll
-        for (int i = 0; i < SEL_MAX_G; ++i) acc[i] = 0.f;
-        for (int e = 0; e < a.hd; e += 8) {
-          float kx[8];
-          if constexpr (sizeof(TK) == 4) {
-            unpack16<float>(__ldg(reinterpret_cast<const uint4*>(kr + e)), kx);
-            unpack16<float>(__ldg(reinterpret_cast<const uint4*>(kr + e + 4)), kx + 4);
-          } else {
-            unpack16<TK>(__ldg(reinterpret_cast<const uint4*>(kr + e)), kx);
-          }
+    for (int u = 0; u < SEL_SPT; ++u) p[u] = init_h;
+    if (a.T == 1) {
+      // one position: the group's heads share every key load
+      const float* qk = qrow + (int64_t)kv * G * a.hd;
+      float acc[SEL_SPT][G];
 #pragma unroll
-          for (int hh = 0; hh < SEL_MAX_G; ++hh) {
-            if (hh < g) {  // every lane reads the same q address: a broadcast
-              const float4 q0 = __ldg(reinterpret_cast<const float4*>(qk + hh * a.hd + e));
-              const float4 q1 = __ldg(reinterpret_cast<const float4*>(qk + hh * a.hd + e + 4));
-              float sv = acc[hh];
-              sv = fmaf(q0.x, kx[0], sv); sv = fmaf(q0.y, kx[1], sv); sv = fmaf(q0.z, kx[2], sv);
-              sv = fmaf(q0.w, kx[3], sv); sv = fmaf(q1.x, kx[4], sv); sv = fmaf(q1.y, kx[5], sv);
-              sv = fmaf(q1.z, kx[6], sv); sv = fmaf(q1.w, kx[7], sv);
-              acc[hh] = sv;
+      for (int u = 0; u < SEL_SPT; ++u)
+#pragma unroll
+        for (int i = 0; i < G; ++i) acc[u][i] = 0.f;
+      for (int e = 0; e < a.hd; e += 8) {
+        float kx[SEL_SPT][8];
+#pragma unroll
+        for (int u = 0; u < SEL_SPT; ++u) load_k(kr[u] + e, kx[u]);
+#pragma unroll
+        for (int hh = 0; hh < G; ++hh) {  // every lane reads the same q address: a broadcast
+          const float4 q0 = __ldg(reinterpret_cast<const float4*>(qk + hh * a.hd + e));
+          const float4 q1 = __ldg(reinterpret_cast<const float4*>(qk + hh * a.hd + e + 4));
+#pragma unroll
+          for (int u = 0; u < SEL_SPT; ++u) acc[u][hh] = dot8(acc[u][hh], q0, q1, kx[u]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < SEL_SPT; ++u)
+#pragma unroll
+        for (int hh = 0; hh < G; ++hh) p[u] = a.h_pool == 0 ? fmaxf(p[u], acc[u][hh]) : p[u] + acc[u][hh];
+    } else {
+      // several positions: per head, pool its scores over the positions (keys re-read from L1 / L2)
+      for (int hh = 0; hh < G; ++hh) {
+        float hv[SEL_SPT];
+#pragma unroll
+        for (int u = 0; u < SEL_SPT; ++u) hv[u] = a.t_pool == 0 ? -CUDART_INF_F : 0.f;
+        for (int t = 0; t < a.T; ++t) {
+          const float* qh = qrow + ((int64_t)t * a.n_q + kv * G + hh) * a.hd;
+          float acc[SEL_SPT];
+#pragma unroll
+          for (int u = 0; u < SEL_SPT; ++u) acc[u] = 0.f;
+          for (int e = 0; e < a.hd; e += 8) {
+            const float4 q0 = __ldg(reinterpret_cast<const float4*>(qh + e));
+            const float4 q1 = __ldg(reinterpret_cast<const float4*>(qh + e + 4));
+#pragma unroll
+            for (int u = 0; u < SEL_SPT; ++u) {
+              float kx[8];
+              load_k(kr[u] + e, kx);
+              acc[u] = dot8(acc[u], q0, q1, kx);
             }
           }
+#pragma unroll
+          for (int u = 0; u < SEL_SPT; ++u) hv[u] = a.t_pool == 0 ? fmaxf(hv[u], acc[u]) : hv[u] + acc[u];
         }
 #pragma unroll
-        for (int hh = 0; hh < SEL_MAX_G; ++hh)
-          if (hh < g) hv[hh] = a.t_pool == 0 ? fmaxf(hv[hh], acc[hh]) : hv[hh] + acc[hh];
+        for (int u = 0; u < SEL_SPT; ++u) {
+          const float v = a.t_pool == 0 ? hv[u] : hv[u] / (float)a.T;
+          p[u] = a.h_pool == 0 ? fmaxf(p[u], v) : p[u] + v;
+        }
       }
     }
-    float p = a.h_pool == 0 ? -CUDART_INF_F : 0.f;
 #pragma unroll
-    for (int hh = 0; hh < SEL_MAX_G; ++hh) {
-      if (hh < g) {
-        const float v = a.t_pool == 0 ? hv[hh] : hv[hh] / (float)a.T;
-        p = a.h_pool == 0 ? fmaxf(p, v) : p + v;
-      }
-    }
-    red[kv][lane] = p;
+    for (int u = 0; u < SEL_SPT; ++u) red[kv][lane + 32 * u] = p[u];
   }
   __syncthreads();
-  if (warp == 0 && slot < S) {
+  for (int j = threadIdx.x; j < SEL_TILE; j += SEL_THREADS) {
+    const int slot = base + j;
+    if (slot >= S) continue;
     float p = a.h_pool == 0 ? -CUDART_INF_F : 0.f;
     for (int kv = 0; kv < a.n_kv; ++kv) {
-      const float v = red[kv][lane];
+      const float v = red[kv][j];
       p = a.h_pool == 0 ? fmaxf(p, v) : p + v;
     }
     if (a.h_pool == 1) p /= (float)a.n_q;
@@ -264,22 +305,47 @@ struct TopkReadArgs {
 };
 
 template <typename T>
+__device__ __forceinline__ void load_row8(const char* base, int j, float* out) {
+  const T* p = reinterpret_cast<const T*>(base) + j;
+  if constexpr (sizeof(T) == 4) {
+    unpack16<float>(__ldg(reinterpret_cast<const uint4*>(p)), out);
+    unpack16<float>(__ldg(reinterpret_cast<const uint4*>(p + 4)), out + 4);
+  } else {
+    unpack16<T>(__ldg(reinterpret_cast<const uint4*>(p)), out);
+  }
+}
+
+// NT: query rows per CTA (1 for decode, TR_ROWS otherwise), so decode does no work for absent rows.
+template <typename T, int NT>
 __global__ void __launch_bounds__(TR_THREADS) topk_read_kernel(const TopkReadArgs a) {
   extern __shared__ __align__(16) float tr_smem[];
-  float* qs = tr_smem;                                   // [TR_ROWS][d_s]
-  float* at = tr_smem + (size_t)TR_ROWS * a.d_s;         // [TR_ROWS][k]
+  float* qs = tr_smem;                                   // [NT][d_s]
+  float* at = tr_smem + (size_t)NT * a.d_s;              // [NT][k]
+  int64_t* koff = reinterpret_cast<int64_t*>(at + (((size_t)NT * a.k + 1) & ~(size_t)1));  // [k] row byte offsets
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int set = blockIdx.x;
-  const int64_t t0 = (int64_t)blockIdx.y * TR_ROWS;
+  const int64_t t0 = (int64_t)blockIdx.y * NT;
   const int64_t left = a.rows_per_set - t0;
-  const int nt = left < TR_ROWS ? (int)left : TR_ROWS;
+  const int nt = left < NT ? (int)left : NT;
   if (nt <= 0) return;
   const int64_t row0 = (int64_t)set * a.rows_per_set + t0;
   const int64_t lib = a.n_lib > 1 ? set : 0;
   const int32_t* ix = a.idx + (int64_t)set * a.k;
   const int d_s = a.d_s;
+  constexpr int ES = (int)sizeof(T);
 
-  for (int j = threadIdx.x * 4; j < TR_ROWS * d_s; j += TR_THREADS * 4) {
+  // slot -> byte offset of its row in the pool (-1: outside the grid or the pool: scores -inf, reads nothing)
+  for (int i = threadIdx.x; i < a.k; i += TR_THREADS) {
+    const int s = ix[i];
+    int64_t off = -1;
+    if (s >= 0 && s < a.n_chunks * a.page_rows) {
+      const int c = s / a.page_rows, n = s - c * a.page_rows;
+      const int64_t page = a.page_of[lib * a.n_chunks + c];
+      if (page >= 0 && page < a.n_pages) off = page * a.page_stride_bytes + (int64_t)n * d_s * ES;
+    }
+    koff[i] = off;
+  }
+  for (int j = threadIdx.x * 4; j < NT * d_s; j += TR_THREADS * 4) {
     const int t = j / d_s;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (t < nt) v = *reinterpret_cast<const float4*>(a.q + (row0 + t) * d_s + (j - t * d_s));
@@ -287,51 +353,39 @@ __global__ void __launch_bounds__(TR_THREADS) topk_read_kernel(const TopkReadArg
   }
   __syncthreads();
 
-  // slot -> row address (invalid slots or pages read nothing and score -inf / 0)
-  auto row_ptr = [&](const char* pool, int s) -> const T* {
-    if (s < 0 || s >= a.n_chunks * a.page_rows) return nullptr;
-    const int c = s / a.page_rows, n = s - c * a.page_rows;
-    const int64_t page = a.page_of[lib * a.n_chunks + c];
-    if (page < 0 || page >= a.n_pages) return nullptr;
-    return reinterpret_cast<const T*>(pool + page * a.page_stride_bytes) + (int64_t)n * d_s;
-  };
-
-  // ---- scores
+  // ---- scores: a warp per selected row, the row's 16-byte pieces loaded four at a time
   for (int i = warp; i < a.k; i += TR_THREADS / 32) {
-    const T* kr = row_ptr(a.slots, ix[i]);
-    float dot[TR_ROWS];
+    const int64_t off = koff[i];
+    float dot[NT];
 #pragma unroll
-    for (int t = 0; t < TR_ROWS; ++t) dot[t] = 0.f;
-    if (kr) {
+    for (int t = 0; t < NT; ++t) dot[t] = 0.f;
+    if (off >= 0) {
+      const char* kr = a.slots + off;
+#pragma unroll 4
       for (int j = lane * 8; j < d_s; j += 256) {
         float kx[8];
-        if constexpr (sizeof(T) == 4) {
-          unpack16<float>(__ldg(reinterpret_cast<const uint4*>(kr + j)), kx);
-          unpack16<float>(__ldg(reinterpret_cast<const uint4*>(kr + j + 4)), kx + 4);
-        } else {
-          unpack16<T>(__ldg(reinterpret_cast<const uint4*>(kr + j)), kx);
-        }
+        load_row8<T>(kr, j, kx);
 #pragma unroll
-        for (int t = 0; t < TR_ROWS; ++t) {
+        for (int t = 0; t < NT; ++t) {
           const float4 q0 = *reinterpret_cast<const float4*>(qs + t * d_s + j);
           const float4 q1 = *reinterpret_cast<const float4*>(qs + t * d_s + j + 4);
-          float s = dot[t];
-          s = fmaf(q0.x, kx[0], s); s = fmaf(q0.y, kx[1], s); s = fmaf(q0.z, kx[2], s); s = fmaf(q0.w, kx[3], s);
-          s = fmaf(q1.x, kx[4], s); s = fmaf(q1.y, kx[5], s); s = fmaf(q1.z, kx[6], s); s = fmaf(q1.w, kx[7], s);
-          dot[t] = s;
+          float sv = dot[t];
+          sv = fmaf(q0.x, kx[0], sv); sv = fmaf(q0.y, kx[1], sv); sv = fmaf(q0.z, kx[2], sv); sv = fmaf(q0.w, kx[3], sv);
+          sv = fmaf(q1.x, kx[4], sv); sv = fmaf(q1.y, kx[5], sv); sv = fmaf(q1.z, kx[6], sv); sv = fmaf(q1.w, kx[7], sv);
+          dot[t] = sv;
         }
       }
     }
 #pragma unroll
-    for (int t = 0; t < TR_ROWS; ++t) {
-      const float s = warp_sum(dot[t]);
-      if (lane == 0) at[t * a.k + i] = kr ? s : -CUDART_INF_F;
+    for (int t = 0; t < NT; ++t) {
+      const float sv = warp_sum(dot[t]);
+      if (lane == 0) at[t * a.k + i] = off >= 0 ? sv : -CUDART_INF_F;
     }
   }
   __syncthreads();
   // ---- per query row: softmax over the k scores (or the linear 1/sqrt(k) scale)
-  if (warp < nt) {
-    float* ar = at + warp * a.k;
+  for (int t = warp; t < nt; t += TR_THREADS / 32) {
+    float* ar = at + t * a.k;
     if (a.softmax) {
       // qscale = read_temp * log2(e): exp2 of the scaled, max-shifted scores
       float mx = -CUDART_INF_F;
@@ -352,36 +406,43 @@ __global__ void __launch_bounds__(TR_THREADS) topk_read_kernel(const TopkReadArg
     }
     __syncwarp();
     if (a.attn_out)
-      for (int i = lane; i < a.k; i += 32) a.attn_out[(row0 + warp) * a.k + i] = ar[i];
+      for (int i = lane; i < a.k; i += 32) a.attn_out[(row0 + t) * a.k + i] = ar[i];
   }
   __syncthreads();
-  // ---- r = a @ V over the selected rows: thread owns 8 columns (looping for d_s > 2048)
+  // ---- r = a @ V over the selected rows: a thread owns 8 columns; four value rows in flight per step
   const char* vpool = a.vslots ? a.vslots : a.slots;
   for (int j = threadIdx.x * 8; j < d_s; j += TR_THREADS * 8) {
-    float acc[TR_ROWS][8];
+    float acc[NT][8];
 #pragma unroll
-    for (int t = 0; t < TR_ROWS; ++t)
+    for (int t = 0; t < NT; ++t)
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[t][e] = 0.f;
-    for (int i = 0; i < a.k; ++i) {
-      const T* vr = row_ptr(vpool, ix[i]);
-      if (!vr) continue;
-      float vx[8];
-      if constexpr (sizeof(T) == 4) {
-        unpack16<float>(__ldg(reinterpret_cast<const uint4*>(vr + j)), vx);
-        unpack16<float>(__ldg(reinterpret_cast<const uint4*>(vr + j + 4)), vx + 4);
-      } else {
-        unpack16<T>(__ldg(reinterpret_cast<const uint4*>(vr + j)), vx);
+    for (int i0 = 0; i0 < a.k; i0 += 4) {
+      float vx[4][8];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u;
+        const int64_t off = i < a.k ? koff[i] : -1;
+        if (off >= 0) load_row8<T>(vpool + off, j, vx[u]);
+        else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) vx[u][e] = 0.f;
+        }
       }
 #pragma unroll
-      for (int t = 0; t < TR_ROWS; ++t) {
-        const float w = at[t * a.k + i];
+      for (int u = 0; u < 4; ++u) {
+        const int i = i0 + u;
+        if (i >= a.k) break;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[t][e] = fmaf(w, vx[e], acc[t][e]);
+        for (int t = 0; t < NT; ++t) {
+          const float w = at[t * a.k + i];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[t][e] = fmaf(w, vx[u][e], acc[t][e]);
+        }
       }
     }
 #pragma unroll
-    for (int t = 0; t < TR_ROWS; ++t) {
+    for (int t = 0; t < NT; ++t) {
       if (t < nt) {
         float* o = a.r_out + (row0 + t) * d_s + j;
         *reinterpret_cast<float4*>(o) = make_float4(acc[t][0], acc[t][1], acc[t][2], acc[t][3]);
@@ -389,6 +450,147 @@ __global__ void __launch_bounds__(TR_THREADS) topk_read_kernel(const TopkReadArg
       }
     }
   }
+}
+
+// Decode form (one query row per index set): a cluster of TRC CTAs per set splits the k selected rows; the
+// softmax maximum and sum and the partial weighted sums are combined through distributed shared memory, so a
+// document's rows stream through TRC SMs at once. CTA `rank` writes columns [rank, rank + TRC, ...) in 8-column
+// groups of the combined r.
+constexpr int TRC = 4;
+
+template <typename T>
+__global__ void __cluster_dims__(TRC, 1, 1) __launch_bounds__(TR_THREADS)
+topk_read_decode_kernel(const TopkReadArgs a) {
+  extern __shared__ __align__(16) float trd_smem[];
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int d_s = a.d_s;
+  const int per = (a.k + TRC - 1) / TRC;                 // rows per CTA
+  const int i0 = min(a.k, rank * per), i1 = min(a.k, i0 + per), nl = i1 - i0;
+  float* qs = trd_smem;                                  // [d_s]
+  float* part = qs + d_s;                                // [d_s] this CTA's partial r
+  float* at = part + d_s;                                // [per] scores -> weights
+  float* stats = at + ((per + 3) & ~3);                  // [4]: local max, local sum
+  int64_t* koff = reinterpret_cast<int64_t*>(stats + 4); // [per]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int set = blockIdx.x / TRC;
+  const int64_t row = set;  // one query row per set
+  const int64_t lib = a.n_lib > 1 ? set : 0;
+  const int32_t* ix = a.idx + (int64_t)set * a.k;
+  constexpr int ES = (int)sizeof(T);
+
+  for (int i = threadIdx.x; i < nl; i += TR_THREADS) {
+    const int s = ix[i0 + i];
+    int64_t off = -1;
+    if (s >= 0 && s < a.n_chunks * a.page_rows) {
+      const int c = s / a.page_rows, n = s - c * a.page_rows;
+      const int64_t page = a.page_of[lib * a.n_chunks + c];
+      if (page >= 0 && page < a.n_pages) off = page * a.page_stride_bytes + (int64_t)n * d_s * ES;
+    }
+    koff[i] = off;
+  }
+  for (int j = threadIdx.x * 4; j < d_s; j += TR_THREADS * 4)
+    *reinterpret_cast<float4*>(qs + j) = *reinterpret_cast<const float4*>(a.q + row * d_s + j);
+  __syncthreads();
+
+  // ---- scores of this CTA's rows: a warp per row, the row's pieces loaded eight at a time
+  for (int i = warp; i < nl; i += TR_THREADS / 32) {
+    const int64_t off = koff[i];
+    float dot = 0.f;
+    if (off >= 0) {
+      const char* kr = a.slots + off;
+#pragma unroll 8
+      for (int j = lane * 8; j < d_s; j += 256) {
+        float kx[8];
+        load_row8<T>(kr, j, kx);
+        const float4 q0 = *reinterpret_cast<const float4*>(qs + j);
+        const float4 q1 = *reinterpret_cast<const float4*>(qs + j + 4);
+        dot = fmaf(q0.x, kx[0], dot); dot = fmaf(q0.y, kx[1], dot); dot = fmaf(q0.z, kx[2], dot);
+        dot = fmaf(q0.w, kx[3], dot); dot = fmaf(q1.x, kx[4], dot); dot = fmaf(q1.y, kx[5], dot);
+        dot = fmaf(q1.z, kx[6], dot); dot = fmaf(q1.w, kx[7], dot);
+      }
+    }
+    dot = warp_sum(dot);
+    if (lane == 0) at[i] = off >= 0 ? dot : -CUDART_INF_F;
+  }
+  __syncthreads();
+  // ---- softmax statistics across the cluster (warp 0 of each CTA)
+  if (a.softmax) {
+    if (warp == 0) {
+      float mx = -CUDART_INF_F;
+      for (int i = lane; i < nl; i += 32) mx = fmaxf(mx, at[i] * a.qscale);
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (lane == 0) stats[0] = mx;
+    }
+    cluster.sync();
+    float gmax = -CUDART_INF_F;
+    for (int r = 0; r < TRC; ++r) gmax = fmaxf(gmax, *cluster.map_shared_rank(stats, r));
+    if (warp == 0) {
+      float sum = 0.f;
+      for (int i = lane; i < nl; i += 32) {
+        const float e = at[i] == -CUDART_INF_F ? 0.f : exp2f(at[i] * a.qscale - gmax);
+        at[i] = e;
+        sum += e;
+      }
+      sum = warp_sum(sum);
+      if (lane == 0) stats[1] = sum;
+    }
+    cluster.sync();
+    float gsum = 0.f;
+    for (int r = 0; r < TRC; ++r) gsum += *cluster.map_shared_rank(stats + 1, r);
+    const float inv = 1.f / gsum;
+    for (int i = threadIdx.x; i < nl; i += TR_THREADS) at[i] *= inv;
+  } else {
+    const float sc = rsqrtf((float)a.k);
+    for (int i = threadIdx.x; i < nl; i += TR_THREADS) at[i] = at[i] == -CUDART_INF_F ? 0.f : at[i] * sc;
+  }
+  __syncthreads();
+  if (a.attn_out)
+    for (int i = threadIdx.x; i < nl; i += TR_THREADS) a.attn_out[row * a.k + i0 + i] = at[i];
+  // ---- this CTA's partial r over its rows: a thread owns 8 columns, eight value rows in flight per step
+  const char* vpool = a.vslots ? a.vslots : a.slots;
+  for (int j = threadIdx.x * 8; j < d_s; j += TR_THREADS * 8) {
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    for (int b = 0; b < nl; b += 8) {
+      float vx[8][8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t off = b + u < nl ? koff[b + u] : -1;
+        if (off >= 0) load_row8<T>(vpool + off, j, vx[u]);
+        else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) vx[u][e] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float w = b + u < nl ? at[b + u] : 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(w, vx[u][e], acc[e]);
+      }
+    }
+    *reinterpret_cast<float4*>(part + j) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    *reinterpret_cast<float4*>(part + j + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  }
+  cluster.sync();
+  // ---- combine the partials: this CTA sums the 8-column groups g = rank, rank + TRC, ... over the cluster
+  for (int g8 = rank + TRC * (int)threadIdx.x; g8 * 8 < d_s; g8 += TRC * TR_THREADS) {
+    const int j = g8 * 8;
+    float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
+    for (int r = 0; r < TRC; ++r) {
+      const float* pr = cluster.map_shared_rank(part, r) + j;
+      const float4 x0 = *reinterpret_cast<const float4*>(pr), x1 = *reinterpret_cast<const float4*>(pr + 4);
+      s0.x += x0.x; s0.y += x0.y; s0.z += x0.z; s0.w += x0.w;
+      s1.x += x1.x; s1.y += x1.y; s1.z += x1.z; s1.w += x1.w;
+    }
+    float* o = a.r_out + row * d_s + j;
+    *reinterpret_cast<float4*>(o) = s0;
+    *reinterpret_cast<float4*>(o + 4) = s1;
+  }
+  cluster.sync();  // no CTA leaves while another still reads its shared memory
 }
 
 }  // namespace xencb

@@ -1187,8 +1187,18 @@ int xencb_select_scores(const float* q, int64_t n_rows, int T, int n_q, int n_kv
   dim3 grid((unsigned)((S + SEL_TILE - 1) / SEL_TILE), (unsigned)n_rows);
   if (n_rows > 65535) return fail(XENCB_ENOTSUP, "select_scores: at most 65535 rows per call");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (keys_dtype == XENCB_F32) select_scores_kernel<float><<<grid, SEL_THREADS, 0, st>>>(a);
-  else select_scores_kernel<__half><<<grid, SEL_THREADS, 0, st>>>(a);
+  auto run = [&](auto kf, auto kh) {
+    if (keys_dtype == XENCB_F32) kf<<<grid, SEL_THREADS, 0, st>>>(a);
+    else kh<<<grid, SEL_THREADS, 0, st>>>(a);
+  };
+  switch (n_q / n_kv) {
+    case 1: run(select_scores_kernel<float, 1>, select_scores_kernel<__half, 1>); break;
+    case 2: run(select_scores_kernel<float, 2>, select_scores_kernel<__half, 2>); break;
+    case 4: run(select_scores_kernel<float, 4>, select_scores_kernel<__half, 4>); break;
+    case 8: run(select_scores_kernel<float, 8>, select_scores_kernel<__half, 8>); break;
+    case 16: run(select_scores_kernel<float, 16>, select_scores_kernel<__half, 16>); break;
+    default: return fail(XENCB_ENOTSUP, "select_scores: GQA group %d (supported: 1, 2, 4, 8, 16)", n_q / n_kv);
+  }
   XENCB_CHECK_LAUNCH("select_scores_kernel launch");
   return XENCB_OK;
 }
@@ -1225,7 +1235,38 @@ int xencb_topk_read(const float* q, int64_t n_rows, int d_s, const void* slots, 
   if (!aligned(q, 16) || !aligned(slots, 16) || (vslots && !aligned(vslots, 16)) || !aligned(r_out, 16) ||
       (page_stride * es) % 16)
     return fail(XENCB_EINVAL, "topk_read: q, slots, vslots, r_out and page_stride*elem must be 16-byte aligned");
-  const size_t smem = ((size_t)TR_ROWS * d_s + (size_t)TR_ROWS * k) * sizeof(float);
+  const int nt_cta = n_rows / n_sets == 1 ? 1 : TR_ROWS;  // decode (one row per set): no work for absent rows
+  if (nt_cta == 1) {
+    // decode: a 4-CTA cluster per set (k split over the cluster, combined through distributed shared memory)
+    const int per = (k + TRC - 1) / TRC;
+    const size_t dsm = (2 * (size_t)d_s + (((size_t)per + 3) & ~(size_t)3) + 4) * sizeof(float) +
+                       (size_t)per * sizeof(int64_t);
+    if ((int64_t)n_sets * TRC > INT32_MAX) return fail(XENCB_EINVAL, "topk_read: too many index sets");
+    TopkReadArgs d;
+    d.q = q; d.n_rows = n_rows; d.d_s = d_s;
+    d.slots = static_cast<const char*>(slots);
+    d.vslots = static_cast<const char*>(vslots);
+    d.n_pages = n_pages; d.page_stride_bytes = page_stride * es; d.page_rows = page_rows; d.n_chunks = n_chunks;
+    d.page_of = page_of; d.n_lib = n_lib; d.idx = idx; d.n_sets = n_sets; d.k = k; d.rows_per_set = 1;
+    d.qscale = read_softmax ? read_temp * 1.4426950408889634f : 1.f;
+    d.softmax = read_softmax ? 1 : 0;
+    d.r_out = r_out; d.attn_out = attn_out;
+    cudaStream_t st0 = static_cast<cudaStream_t>(stream);
+    auto launch_d = [&](auto kern) -> int {
+      int r2 = ensure_smem(kern, (int)dsm);
+      if (r2) return r2;
+      kern<<<(unsigned)(n_sets * TRC), TR_THREADS, dsm, st0>>>(d);
+      XENCB_CHECK_LAUNCH("topk_read_decode_kernel launch");
+      return XENCB_OK;
+    };
+    switch (slots_dtype) {
+      case XENCB_F32: return launch_d(topk_read_decode_kernel<float>);
+      case XENCB_F16: return launch_d(topk_read_decode_kernel<__half>);
+      default: return launch_d(topk_read_decode_kernel<__nv_bfloat16>);
+    }
+  }
+  const size_t smem = ((size_t)nt_cta * d_s + (((size_t)nt_cta * k + 1) & ~(size_t)1)) * sizeof(float) +
+                      (size_t)k * sizeof(int64_t);
   DevInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
@@ -1241,7 +1282,7 @@ int xencb_topk_read(const float* q, int64_t n_rows, int d_s, const void* slots, 
   a.qscale = read_softmax ? read_temp * 1.4426950408889634f : 1.f;
   a.softmax = read_softmax ? 1 : 0;
   a.r_out = r_out; a.attn_out = attn_out;
-  const int64_t yblocks = (a.rows_per_set + TR_ROWS - 1) / TR_ROWS;
+  const int64_t yblocks = (a.rows_per_set + nt_cta - 1) / nt_cta;
   if (yblocks > 65535) return fail(XENCB_ENOTSUP, "topk_read: too many rows per index set");
   dim3 grid((unsigned)n_sets, (unsigned)yblocks);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -1252,10 +1293,17 @@ int xencb_topk_read(const float* q, int64_t n_rows, int d_s, const void* slots, 
     XENCB_CHECK_LAUNCH("topk_read_kernel launch");
     return XENCB_OK;
   };
+  if (nt_cta == 1) {
+    switch (slots_dtype) {
+      case XENCB_F32: return launch(topk_read_kernel<float, 1>);
+      case XENCB_F16: return launch(topk_read_kernel<__half, 1>);
+      default: return launch(topk_read_kernel<__nv_bfloat16, 1>);
+    }
+  }
   switch (slots_dtype) {
-    case XENCB_F32: return launch(topk_read_kernel<float>);
-    case XENCB_F16: return launch(topk_read_kernel<__half>);
-    default: return launch(topk_read_kernel<__nv_bfloat16>);
+    case XENCB_F32: return launch(topk_read_kernel<float, TR_ROWS>);
+    case XENCB_F16: return launch(topk_read_kernel<__half, TR_ROWS>);
+    default: return launch(topk_read_kernel<__nv_bfloat16, TR_ROWS>);
   }
 }
 

@@ -256,3 +256,16 @@ def test_topk_full_k_equals_library_read_and_decode_reuse(dev):
         assert inj.n_select_passes == 2
     inj.detach()
     _status_clean(dev)
+
+
+@pytest.mark.parametrize("k,n_sets,n_lib", [(1, 1, 1), (3, 5, 5), (64, 64, 64), (301, 5, 1), (2048, 2, 2)])
+@pytest.mark.parametrize("softmax", [True, False])
+@pytest.mark.parametrize("untied", [False, True])
+def test_topk_read_decode_cluster(dev, k, n_sets, n_lib, softmax, untied):
+    """One query row per index set: the 4-CTA cluster form (k split across the cluster, some CTAs with no rows
+    when k < 4), against the oracle."""
+    r, attn, ref_r, ref_a = _read_case(dev, torch.float16, untied, k=k, T=1, n_sets=n_sets, n_lib=n_lib,
+                                       softmax=softmax, seed=k + n_sets)
+    assert rel_err(r, ref_r) < TOL
+    assert rel_err(attn, ref_a) < TOL
+    _status_clean(dev)
