@@ -2,7 +2,7 @@
 //
 // * dtype codes and vector loads for hidden states / slots,
 // * mbarrier + cp.async.bulk (1-D TMA, no multicast) primitives in inline PTX,
-// * bounded waits: every spin on an mbarrier gives up after XENCB_WAIT_NS nanoseconds, records
+// * bounded waits: every spin on an mbarrier gives up after XENCB_WAIT_CYCLES SM cycles (1.5 s at 2 GHz), records
 //   XENCB_DEV_TIMEOUT in the per-device status word and lets the kernel return.
 #pragma once
 
@@ -13,9 +13,6 @@
 
 #include "../../include/xencb.h"
 
-#ifndef XENCB_WAIT_NS
-#define XENCB_WAIT_NS 1500000000ull  // 1.5 s: far above any healthy pipeline wait
-#endif
 
 namespace xencb {
 
@@ -97,13 +94,6 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return t;
 }
 
-// ------------------------------------------------------------------------------------------------ time
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
 // ------------------------------------------------------------------------------------------------ mbarrier
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -142,7 +132,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait until the phase with parity `parity` of `bar` completed. Returns false (and flags the device status)
-// if it did not happen within XENCB_WAIT_NS; the caller must then stop using the pipeline.
+// if it did not happen within XENCB_WAIT_CYCLES; the caller must then stop using the pipeline.
 // The retries pass a suspend-time hint, so a waiting thread sleeps in the barrier instead of spinning, and the
 // clock is read only every 16th retry: a warp waiting here takes almost no issue slots from working warps.
 __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
@@ -157,12 +147,32 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
   return ok != 0;
 }
 
+// The limit is counted on the SM's cycle counter (cheap to read, unlike the global timer, whose reads cost more
+// than a whole pipeline hand-off): XENCB_WAIT_CYCLES is 1.5 s at 2 GHz, longer in time at lower clocks.
+#ifndef XENCB_WAIT_CYCLES
+#define XENCB_WAIT_CYCLES 3000000000ll
+#endif
+
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  const long long t0 = clock64();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait_sleep(bar, parity)) return true;
-    if ((it & 15u) == 0u && globaltimer_ns() - t0 > XENCB_WAIT_NS) {
+    if ((it & 15u) == 0u && clock64() - t0 > XENCB_WAIT_CYCLES) {
+      flag_error(XENCB_DEV_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// The same bounded wait without the suspend hint: for short waits on a hot path (a phase that other warps are
+// about to complete), where a suspended thread's wake-up would cost more than the few retries it saves.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0u && clock64() - t0 > XENCB_WAIT_CYCLES) {
       flag_error(XENCB_DEV_TIMEOUT);
       return false;
     }

@@ -17,7 +17,7 @@
 // in a double-buffered shared array behind one named barrier, and lane i of every warp finishes row i & 7,
 // takes the exp2 and broadcasts the 8 weights. The online softmax state (m, l) is uniform across the CTA.
 //
-// Every mbarrier wait is bounded (XENCB_WAIT_NS); a consumer that gives up raises a shared abort flag that
+// Every mbarrier wait is bounded (XENCB_WAIT_CYCLES); a consumer that gives up raises a shared abort flag that
 // all consumers test after the next named barrier (or warp vote), so no thread is left at a barrier.
 #pragma once
 

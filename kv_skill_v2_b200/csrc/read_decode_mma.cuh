@@ -1,9 +1,9 @@
 // Tensor-core decode read (f16 / bf16 slots): the same work items and partial format as read_decode_kernel,
 // with the per-row arithmetic on mma.sync.m16n8k16.
 //
-// Producer (warp 0, lane 0): decodes each work item once (page, valid rows), then per stage of `rps` rows
-// writes a small descriptor (item, rows, first/last flags) into a shared ring and bulk-copies (TMA, no
-// multicast) the rows one per copy into the stage, rows padded by 16 bytes so the eight row addresses of an
+// Producer (warp 0): decodes each work item once (page, valid rows), then per stage of `rps` rows lane 0
+// writes a small descriptor (item, rows, first/last flags) into a shared ring and the warp's lanes bulk-copy
+// (TMA, no multicast) the rows, one copy per row issued by lane row % 32, into the stage, rows padded by 16 bytes so the eight row addresses of an
 // ldmatrix fall in distinct banks. A final descriptor marks the end of the CTA's work.
 // Consumers (warps 1..ncw): warp w owns the (16*TPW)-column slice [16*TPW*w, 16*TPW*(w+1)) of d_s. Per
 // 16-row group:
@@ -25,6 +25,7 @@ namespace xencb {
 constexpr int RM_TILES = 16;      // upper bound of the 16-column k-tiles per consumer warp (TPW <= RM_TILES)
 constexpr int RM_MAX_WARPS = 16;  // consumer warps per CTA
 constexpr int RM_RED_STRIDE = 20;  // floats per row of the cross-warp score buffer (>= RM_MAX_WARPS, 16-byte rows)
+constexpr int RM_SBUF = 4;         // score buffers: a group's scores are posted one group before they are used
 
 struct __align__(16) StageMeta {
   long long item;
@@ -33,31 +34,44 @@ struct __align__(16) StageMeta {
 };
 constexpr int RM_FIRST = 1, RM_LAST = 2, RM_DONE = 4, RM_VAL = 8;  // RM_VAL: a stage of value rows (untied V)
 
+// One posted 16-row group, as the consumers describe it to the softmax warp.
+struct __align__(16) GroupRec {
+  long long item;
+  int flags;  // RM_FIRST on an item's first group, RM_LAST on its last, RM_DONE after the CTA's last group
+  int gv;     // valid rows of the group
+};
+
 // Shared-memory bytes of the tensor-core read for a plan (the host and the kernel use the same layout).
 __host__ __device__ inline size_t rm_smem_bytes(int n_stage, int stage_bytes, int ncw, int tpw) {
   return (size_t)n_stage * stage_bytes           // stages
          + (size_t)ncw * 2 * tpw * 4 * 2 * 4       // q fragments
-         + 2 * (size_t)16 * RM_RED_STRIDE * 4       // cross-warp partial scores [2][16 rows][stride]
+         + RM_SBUF * (size_t)16 * RM_RED_STRIDE * 4  // cross-warp partial scores [RM_SBUF][16 rows][stride]
          + (size_t)n_stage * sizeof(StageMeta)      // stage descriptors
-         + (2 * (size_t)n_stage + 2) * 8            // full / empty / two score barriers
+         + RM_SBUF * sizeof(GroupRec)               // group records (consumers -> softmax warp)
+         + RM_SBUF * (size_t)(4 * 4 + 4) * 4         // P fragments [4 lanes][4 words] + rescale factor
+         + (2 * (size_t)n_stage + 2 * RM_SBUF) * 8  // full / empty / score / P barriers
          + 16;                                      // abort flag
 }
 
 template <typename T, bool SPLIT, bool SOFTMAX, int TPW>
-__global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 1) read_decode_mma_kernel(const ReadArgs a) {
+__global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 2) : 32 * 12, 1) read_decode_mma_kernel(const ReadArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ncw = (blockDim.x >> 5) - 1;
+  const int ncw = (blockDim.x >> 5) - 2;  // warp 0 producer, warps 1..ncw consumers, warp ncw + 1 softmax
   const int row_stride = a.row_stride;
   const int stage_bytes = ((a.rps * row_stride + 127) / 128) * 128;
   unsigned char* stages = smem;
   uint32_t* qfrag = reinterpret_cast<uint32_t*>(smem + (size_t)a.n_stage * stage_bytes);  // [ncw][2][TPW][4][2]
-  float* red = reinterpret_cast<float*>(qfrag + ncw * 2 * TPW * 4 * 2);  // [2][16 rows][RM_RED_STRIDE]
-  StageMeta* meta = reinterpret_cast<StageMeta*>(red + 2 * 16 * RM_RED_STRIDE);
-  uint64_t* full = reinterpret_cast<uint64_t*>(meta + a.n_stage);
+  float* red = reinterpret_cast<float*>(qfrag + ncw * 2 * TPW * 4 * 2);  // [RM_SBUF][16 rows][RM_RED_STRIDE]
+  StageMeta* meta = reinterpret_cast<StageMeta*>(red + RM_SBUF * 16 * RM_RED_STRIDE);
+  GroupRec* grec = reinterpret_cast<GroupRec*>(meta + a.n_stage);                 // [RM_SBUF]
+  uint32_t* pfrag = reinterpret_cast<uint32_t*>(grec + RM_SBUF);                  // [RM_SBUF][4 lanes][4]
+  float* psc = reinterpret_cast<float*>(pfrag + RM_SBUF * 16);                    // [RM_SBUF] rescale factors
+  uint64_t* full = reinterpret_cast<uint64_t*>(psc + RM_SBUF);
   uint64_t* empty = full + a.n_stage;
-  uint64_t* sbar = empty + a.n_stage;  // [2] partial scores of a group are complete
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(sbar + 2);
+  uint64_t* sbar = empty + a.n_stage;  // [RM_SBUF] partial scores of a group are complete
+  uint64_t* pbar = sbar + RM_SBUF;     // [RM_SBUF] the group's P fragments are published
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(pbar + RM_SBUF);
 
   {
     uint4* z = reinterpret_cast<uint4*>(stages);
@@ -65,15 +79,17 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
     for (int i = threadIdx.x; i < n16; i += blockDim.x) z[i] = make_uint4(0u, 0u, 0u, 0u);
     fence_proxy_async_smem();  // the zeros precede the bulk copies into the same bytes
     // score slots of warps >= ncw are never written: they stay 0 for the vector sum
-    for (int i = threadIdx.x; i < 2 * 16 * RM_RED_STRIDE; i += blockDim.x) red[i] = 0.f;
+    for (int i = threadIdx.x; i < RM_SBUF * 16 * RM_RED_STRIDE; i += blockDim.x) red[i] = 0.f;
   }
   if (threadIdx.x == 0) {
     for (int i = 0; i < a.n_stage; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], ncw);
     }
-    mbar_init(&sbar[0], ncw);
-    mbar_init(&sbar[1], ncw);
+    for (int i = 0; i < RM_SBUF; ++i) {
+      mbar_init(&sbar[i], ncw);
+      mbar_init(&pbar[i], 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -81,45 +97,62 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
 
   // ------------------------------------------------------------------------------------------- producer
   if (warp == 0) {
-    if (lane != 0) return;
+    // the whole warp walks the items in step; lane 0 owns the barriers and descriptors, and a stage's row
+    // copies are issued by the lanes in parallel (row r by lane r % 32)
     const uint64_t pol = policy_evict_first();
     uint32_t it_count = 0;
     bool ok = true;
-    // the next item's page and row range are looked up while the current item's stages stream in
-    ItemRange nxt;
-    bool have_nxt = blockIdx.x < a.n_items;
-    if (have_nxt) nxt = decode_item(a, blockIdx.x);
-    for (int64_t item = blockIdx.x; item < a.n_items && ok; item += gridDim.x) {
-      const ItemRange it = nxt;
-      const int64_t item_next = item + gridDim.x;
-      have_nxt = false;
-      if (!it.active || it.r1 <= it.r0) {
-        if (item_next < a.n_items) { nxt = decode_item(a, item_next); have_nxt = true; }
-        continue;
+    // the CTA's items are decoded 32 at a time, one per lane (their page and row-range lookups overlap), and
+    // handed to the whole warp by shuffles
+    ItemRange mine;
+    int64_t batch = -1;
+    int64_t k_item = 0;  // this CTA's k-th item is blockIdx.x + k * gridDim.x
+    for (int64_t item = blockIdx.x; item < a.n_items && ok; item += gridDim.x, ++k_item) {
+      if ((k_item >> 5) != batch) {
+        batch = k_item >> 5;
+        const int64_t my_item = blockIdx.x + ((batch << 5) + lane) * (int64_t)gridDim.x;
+        mine.active = false;
+        mine.r0 = mine.r1 = 0;
+        mine.base = nullptr;
+        mine.row = 0;
+        if (my_item < a.n_items) mine = decode_item(a, my_item);
       }
+      const int who = (int)(k_item & 31);  // the lane that decoded this item
+      ItemRange it;
+      it.active = __shfl_sync(0xffffffffu, (int)mine.active, who) != 0;
+      it.r0 = __shfl_sync(0xffffffffu, mine.r0, who);
+      it.r1 = __shfl_sync(0xffffffffu, mine.r1, who);
+      it.row = __shfl_sync(0xffffffffu, (long long)mine.row, who);
+      it.base = reinterpret_cast<const char*>(
+          __shfl_sync(0xffffffffu, (unsigned long long)reinterpret_cast<uintptr_t>(mine.base), who));
+      if (!it.active || it.r1 <= it.r0) continue;
       for (int rs = it.r0; rs < it.r1 && ok; rs += a.rps) {
         const int nr = min(a.rps, it.r1 - rs);
         const bool last = rs + nr >= it.r1;
         // the group's key rows, then (untied values) the same rows of the value pool as a second stage
         for (int part = 0; part < (a.vslots ? 2 : 1); ++part) {
           const uint32_t slot = it_count % a.n_stage, use = it_count / a.n_stage;
-          if (use > 0 && !mbar_wait_bounded(&empty[slot], (use - 1) & 1)) { ok = false; break; }
-          meta[slot].item = item;
-          meta[slot].nr = nr;
-          meta[slot].flags = part == 0 ? ((rs == it.r0 ? RM_FIRST : 0) | (last && !a.vslots ? RM_LAST : 0))
-                                       : (RM_VAL | (last ? RM_LAST : 0));
-          mbar_arrive_expect_tx(&full[slot], (uint32_t)nr * a.row_bytes);
+          bool good = true;
+          if (lane == 0 && use > 0) good = mbar_wait_spin(&empty[slot], (use - 1) & 1);
+          if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
+          if (lane == 0) {
+            meta[slot].item = item;
+            meta[slot].nr = nr;
+            meta[slot].flags = part == 0 ? ((rs == it.r0 ? RM_FIRST : 0) | (last && !a.vslots ? RM_LAST : 0))
+                                         : (RM_VAL | (last ? RM_LAST : 0));
+            mbar_arrive_expect_tx(&full[slot], (uint32_t)nr * a.row_bytes);
+          }
+          __syncwarp();  // the expected bytes are registered before any of the stage's copies is issued
           unsigned char* dst = stages + (size_t)slot * stage_bytes;
           const char* src = (part == 0 ? it.base : a.vslots + (it.base - a.slots)) + (int64_t)rs * a.row_bytes;
-          for (int r = 0; r < nr; ++r)
+          for (int r = lane; r < nr; r += 32)
             bulk_g2s(dst + (size_t)r * row_stride, src + (int64_t)r * a.row_bytes, (uint32_t)a.row_bytes, &full[slot],
                      pol);
           ++it_count;
         }
-        if (!have_nxt && item_next < a.n_items) { nxt = decode_item(a, item_next); have_nxt = true; }
       }
-      if (!have_nxt && item_next < a.n_items) { nxt = decode_item(a, item_next); have_nxt = true; }
     }
+    if (lane != 0) return;
     if (ok) {  // end-of-work descriptor
       const uint32_t slot = it_count % a.n_stage, use = it_count / a.n_stage;
       if (use == 0 || mbar_wait_bounded(&empty[slot], (use - 1) & 1)) {
@@ -136,6 +169,86 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
       mbar_wait_bounded(&full[last % a.n_stage], (last / a.n_stage) & 1);
     }
     return;
+  }
+
+  // ------------------------------------------------------------------------------------------- softmax warp
+  // Tied reads only (untied reads keep the per-warp softmax of the value-stage loop below). Per posted group:
+  // the 16 row scores from the consumers' partials, the online softmax of the current item (m, l per row lane),
+  // P rounded to the slot type and packed as the MMA's B fragment, the rescale factor of the running sums;
+  // then one arrive on the group's P barrier. At an item's last group it writes the item's (m, l).
+  if (warp == ncw + 1) {
+    if (a.vslots) return;
+    const int prow = lane & 15;
+    const int ka = (lane & 3) * 2;
+    float m = -CUDART_INF_F, l = 0.f;
+    for (uint32_t gs = 0;; ++gs) {
+      const uint32_t b = gs % RM_SBUF;
+      if (!mbar_wait_spin(&sbar[b], (gs / RM_SBUF) & 1) || *abort_flag) { *abort_flag = 1; return; }
+      const GroupRec gr = grec[b];
+      if (gr.flags & RM_DONE) return;
+      if (gr.flags & RM_FIRST) { m = -CUDART_INF_F; l = 0.f; }
+      // the row's partials are contiguous: four 16-byte loads (rows 80 bytes apart: conflict-free), a tree sum
+      const float4* rr = reinterpret_cast<const float4*>(red + b * 16 * RM_RED_STRIDE + prow * RM_RED_STRIDE);
+      float4 v4[RM_MAX_WARPS / 4];
+#pragma unroll
+      for (int j = 0; j < RM_MAX_WARPS / 4; ++j) v4[j] = 4 * j < ncw ? rr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float srow = ((v4[0].x + v4[0].y) + (v4[0].z + v4[0].w)) + ((v4[1].x + v4[1].y) + (v4[1].z + v4[1].w)) +
+                         (((v4[2].x + v4[2].y) + (v4[2].z + v4[2].w)) + ((v4[3].x + v4[3].y) + (v4[3].z + v4[3].w)));
+      const bool valid = prow < gr.gv;
+      float p, sc = 1.f;
+      if (SOFTMAX) {
+        float mx = valid ? srow : -CUDART_INF_F;
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        const float m_new = fmaxf(m, mx);
+        if (m_new != m) {
+          sc = m == -CUDART_INF_F ? 0.f : exp2f(m - m_new);
+          l *= sc;
+          m = m_new;
+        }
+        p = valid ? exp2f(srow - m) : 0.f;
+      } else {
+        p = valid ? srow : 0.f;
+      }
+      // round p to the slot type (+ residual for bf16); l sums the values the MMA uses (per row lane)
+      const T ph = from_f32<T>(p);
+      const float phf = to_f32(ph);
+      const T pl = from_f32<T>(SPLIT ? p - phf : 0.f);
+      if (SOFTMAX && lane < 16) l += phf + (SPLIT ? to_f32(pl) : 0.f);
+      uint16_t uh, ul;
+      memcpy(&uh, &ph, 2);
+      memcpy(&ul, &pl, 2);
+      const uint32_t ubits = (uint32_t)uh | ((uint32_t)ul << 16);
+      const uint32_t e0 = __shfl_sync(0xffffffffu, ubits, ka);
+      const uint32_t e1 = __shfl_sync(0xffffffffu, ubits, ka + 1);
+      const uint32_t e8 = __shfl_sync(0xffffffffu, ubits, ka + 8);
+      const uint32_t e9 = __shfl_sync(0xffffffffu, ubits, ka + 9);
+      if (lane < 4) {
+        uint4 f;
+        f.x = (e0 & 0xffffu) | (e1 << 16);            // P rows 2l, 2l+1
+        f.y = (e8 & 0xffffu) | (e9 << 16);            // P rows 2l+8, 2l+9
+        f.z = (e0 >> 16) | (e1 & 0xffff0000u);        // residuals (bf16)
+        f.w = (e8 >> 16) | (e9 & 0xffff0000u);
+        reinterpret_cast<uint4*>(pfrag + b * 16)[lane] = f;
+      }
+      if (lane == 0) psc[b] = sc;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pbar[b]);
+      if (gr.flags & RM_LAST) {
+        float lt = l;
+        lt += __shfl_xor_sync(0xffffffffu, lt, 1);
+        lt += __shfl_xor_sync(0xffffffffu, lt, 2);
+        lt += __shfl_xor_sync(0xffffffffu, lt, 4);
+        lt += __shfl_xor_sync(0xffffffffu, lt, 8);
+        lt += __shfl_xor_sync(0xffffffffu, lt, 16);
+        if (lane == 0) {
+          a.part_ml[gr.item * 2] = SOFTMAX ? m : 0.f;
+          a.part_ml[gr.item * 2 + 1] = SOFTMAX ? lt : 1.f;
+        }
+      }
+    }
   }
 
   // ------------------------------------------------------------------------------------------- consumers
@@ -171,6 +284,183 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
       a.part_ml[item * 2 + 1] = SOFTMAX ? l : 1.f;
     }
   };
+
+  // q fragments of an item (B operand, query in column 0 = lanes 0..3), hi and residual, into this warp's slot
+  auto load_q = [&](int64_t item) {
+    // the warp's 16*TPW columns of q: lane i loads columns [4i, 4i + 4) of each 128-column block with one
+    // 16-byte load and writes them, packed to the slot type, into their B-fragment words (tile t = i / 4:
+    // columns 16t + r; pairs r < 8 are the fragment's first word of lane r / 2, pairs r >= 8 its second)
+    const int64_t row = (item / a.n_split) / a.k;
+    const float* qr = a.q + row * a.d_s;
+#pragma unroll
+    for (int u = 0; u < TPW / 8; ++u) {
+      const int t = u * 8 + (lane >> 2);  // tile of this lane's four columns
+      if (t < nt) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(qr + d0 + t * 16 + (lane & 3) * 4));
+        const int r0 = (lane & 3) * 4;  // column of v.x within the tile
+        const int w = r0 < 8 ? 0 : 1;   // first or second fragment word
+        const int l0 = (r0 & 7) >> 1;   // fragment lane of the pair (v.x, v.y); (v.z, v.w) goes to l0 + 1
+        const float x0 = v.x * a.qscale, x1 = v.y * a.qscale, x2 = v.z * a.qscale, x3 = v.w * a.qscale;
+        float h0, h1, h2, h3, e0, e1, e2, e3;
+        qf[t * 8 + l0 * 2 + w] = pack2<T>(x0, x1, h0, h1);
+        qf[t * 8 + (l0 + 1) * 2 + w] = pack2<T>(x2, x3, h2, h3);
+        qf[(TPW + t) * 8 + l0 * 2 + w] = SPLIT ? pack2<T>(x0 - h0, x1 - h1, e0, e1) : 0u;
+        qf[(TPW + t) * 8 + (l0 + 1) * 2 + w] = SPLIT ? pack2<T>(x2 - h2, x3 - h3, e2, e3) : 0u;
+      }
+    }
+    __syncwarp();
+  };
+
+  if (!a.vslots) {
+    // Tied K = V, pipelined by one 16-row group: post group g's partial scores, then accumulate group g - 1
+    // with the P fragments the softmax warp published for it. RM_SBUF buffers: a consumer posts group g only
+    // after it waited for the P of group g - 2, so the softmax warp is done reading buffer (g - 4) by then; the
+    // softmax warp writes the P of group g after every consumer posted g, i.e. finished reading P of g - 1.
+    struct Pend {
+      uint32_t slot, gidx;
+      int g0;
+      bool first, last_group, last;
+      long long item;
+    };
+    Pend pd{};
+    bool have = false;
+    uint32_t gseq = 0;
+    auto post = [&](uint32_t slot, int g0, const StageMeta& md) {
+      const uint32_t b = gseq % RM_SBUF;
+      const uint32_t gbase = stages_u32 + slot * (uint32_t)stage_bytes + (uint32_t)(g0 * row_stride);
+      float sa[4][4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) sa[c][0] = sa[c][1] = sa[c][2] = sa[c][3] = 0.f;
+#pragma unroll
+      for (int t = 0; t < TPW; ++t) {
+        if (t < nt) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(gbase + off_s + t * 32, a0, a1, a2, a3);
+          uint32_t b0 = 0u, b1 = 0u;
+          if (lane < 4) {
+            b0 = qf[t * 8 + lane * 2];
+            b1 = qf[t * 8 + lane * 2 + 1];
+          }
+          mma16816<T>(sa[t & 3], a0, a1, a2, a3, b0, b1);
+          if (SPLIT) {
+            uint32_t c0 = 0u, c1 = 0u;
+            if (lane < 4) {
+              c0 = qf[(TPW + t) * 8 + lane * 2];
+              c1 = qf[(TPW + t) * 8 + lane * 2 + 1];
+            }
+            mma16816<T>(sa[(t + 2) & 3], a0, a1, a2, a3, c0, c1);
+          }
+        }
+      }
+      const float sc_lo = (sa[0][0] + sa[1][0]) + (sa[2][0] + sa[3][0]);  // row lane/4 (lanes with lane%4 == 0)
+      const float sc_hi = (sa[0][2] + sa[1][2]) + (sa[2][2] + sa[3][2]);  // row lane/4 + 8
+      float* rb = red + b * 16 * RM_RED_STRIDE;
+      if ((lane & 3) == 0) {
+        rb[(lane >> 2) * RM_RED_STRIDE + cw] = sc_lo;
+        rb[((lane >> 2) + 8) * RM_RED_STRIDE + cw] = sc_hi;
+      }
+      if (cw == 0 && lane == 0) {
+        const bool last_group = g0 + 16 >= md.nr;
+        GroupRec gr;
+        gr.item = md.item;
+        gr.flags = ((md.flags & RM_FIRST) && g0 == 0 ? RM_FIRST : 0) | (last_group && (md.flags & RM_LAST) ? RM_LAST : 0);
+        gr.gv = min(16, md.nr - g0);
+        grec[b] = gr;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sbar[b]);
+    };
+    auto post_done = [&]() {
+      const uint32_t b = gseq % RM_SBUF;
+      if (cw == 0 && lane == 0) {
+        GroupRec gr;
+        gr.item = -1;
+        gr.flags = RM_DONE;
+        gr.gv = 0;
+        grec[b] = gr;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sbar[b]);
+    };
+    // accumulate a posted group with its published P; release the stage after its last group
+    auto finish = [&](const Pend& g) -> bool {
+      const uint32_t b = g.gidx % RM_SBUF;
+      if (!mbar_wait_spin(&pbar[b], (g.gidx / RM_SBUF) & 1) || *abort_flag) {
+        *abort_flag = 1;
+        return false;
+      }
+      if (g.first) {
+#pragma unroll
+        for (int t = 0; t < TPW; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+      }
+      const float sc = psc[b];
+      if (sc != 1.f) {
+#pragma unroll
+        for (int t = 0; t < TPW; ++t) {
+          acc[t][0] *= sc;
+          acc[t][2] *= sc;
+        }
+      }
+      uint4 f = make_uint4(0u, 0u, 0u, 0u);
+      if (lane < 4) f = reinterpret_cast<const uint4*>(pfrag + b * 16)[lane];
+      const uint32_t gbase = stages_u32 + g.slot * (uint32_t)stage_bytes + (uint32_t)(g.g0 * row_stride);
+#pragma unroll
+      for (int t = 0; t < TPW; ++t) {
+        if (t < nt) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4_t(gbase + off_a + t * 32, a0, a1, a2, a3);
+          mma16816<T>(acc[t], a0, a1, a2, a3, f.x, f.y);
+          if (SPLIT) mma16816<T>(acc[t], a0, a1, a2, a3, f.z, f.w);
+        }
+      }
+      if (g.last_group) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[g.slot]);
+        if (g.last) {  // this warp's columns of the item's partial (the softmax warp writes its m, l)
+          float* pa = a.part_acc + g.item * (int64_t)a.d_s;
+          if ((lane & 3) == 0) {
+#pragma unroll
+            for (int t = 0; t < TPW; ++t) {
+              if (t < nt) {
+                const int d = d0 + t * 16 + (lane >> 2);
+                pa[d] = acc[t][0];
+                pa[d + 8] = acc[t][2];
+              }
+            }
+          }
+        }
+      }
+      return true;
+    };
+
+    bool ok = true;
+    while (ok) {
+      const uint32_t slot = it_count % a.n_stage, use = it_count / a.n_stage;
+      ++it_count;
+      if (!mbar_wait_spin(&full[slot], use & 1) || *abort_flag) { *abort_flag = 1; ok = false; break; }
+      const StageMeta md = meta[slot];
+      if (md.flags & RM_DONE) {
+        post_done();
+        break;
+      }
+      if (md.flags & RM_FIRST) load_q(md.item);
+      for (int g0 = 0; g0 < md.nr; g0 += 16) {
+        post(slot, g0, md);
+        if (have && !finish(pd)) { ok = false; break; }
+        pd.slot = slot;
+        pd.gidx = gseq;
+        pd.g0 = g0;
+        pd.first = (md.flags & RM_FIRST) && g0 == 0;
+        pd.last_group = g0 + 16 >= md.nr;
+        pd.last = pd.last_group && (md.flags & RM_LAST);
+        pd.item = md.item;
+        have = true;
+        ++gseq;
+      }
+    }
+    if (ok && have) finish(pd);
+    return;
+  }
 
   while (true) {
     const uint32_t slot = it_count % a.n_stage, use = it_count / a.n_stage;

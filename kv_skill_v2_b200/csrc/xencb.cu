@@ -263,8 +263,13 @@ int plan_read(int64_t n_rows, int k, int d_s, int page_rows, int dtype, ReadPlan
   const size_t budget = (size_t)(di.max_smem_optin > 0 ? di.max_smem_optin : 232448) - 1024;
   p->mma = false;
   const char* force_simt = getenv("XENCB_READ_SIMT");
-  // tensor-core read: 128-column slices (up to 16 warps) for d_s <= 2048, 256-column slices (up to 10) above
-  const int tpw = d_s <= 2048 ? 8 : 16;
+  // tensor-core read: 128-column slices (up to 16 warps) for d_s <= 2048, 256-column slices (up to 10) above;
+  // XENCB_READ_TPW=8|16 overrides the slice width (tuning)
+  int tpw = d_s <= 2048 ? 8 : 16;
+  if (const char* e = getenv("XENCB_READ_TPW")) {
+    if (e[0] == '8' && e[1] == 0) tpw = 8;
+    if (e[0] == '1' && e[1] == '6' && e[2] == 0) tpw = 16;
+  }
   const int mma_ncw = (d_s + 16 * tpw - 1) / (16 * tpw);
   const int max_ncw = tpw == 8 ? RM_MAX_WARPS : 10;
   if ((dtype == XENCB_F16 || dtype == XENCB_BF16) && d_s % 16 == 0 && mma_ncw <= max_ncw &&
@@ -281,7 +286,7 @@ int plan_read(int64_t n_rows, int k, int d_s, int page_rows, int dtype, ReadPlan
       p->tpw = tpw;
       p->vpt = 0;
       p->ncw = mma_ncw;
-      p->threads = 32 * (mma_ncw + 1);
+      p->threads = 32 * (mma_ncw + 2);  // producer + consumers + softmax warp
       p->rps = rps;
       p->row_stride = stride;
       p->n_stage = n_stage;
