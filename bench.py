@@ -284,14 +284,15 @@ def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
     h = hs[0].clone()
     h_out = torch.empty_like(h)
     sr = ShardedRead(pages, T, rows_per_lib=T)
+    P_in, P_out = ops.weights_prep(W_in), ops.weights_prep(W_out)  # 3xF16 form, prepared once
 
     def pre():
-        q, _, _, _ = ops.project_in(h, W_in)
+        q, _, _, _ = ops.project_in(h, W_in, w_prep=P_in)
         sr.partial(q)
 
     def post():
         r = sr.merge()
-        ops.project_out(r, W_out, h, want_delta=False, h_out=h_out)
+        ops.project_out(r, W_out, h, want_delta=False, h_out=h_out, w_prep=P_out)
 
     for _ in range(2):
         pre(); sr.exchange(); post()
@@ -741,12 +742,13 @@ def run_prefill(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
     h = hs[0].clone()
     h_out = torch.empty_like(h)
     holder = {}
+    P_in, P_out = ops.weights_prep(W_in), ops.weights_prep(W_out)  # 3xF16 form, prepared once
 
     def step():
-        q, _, _, _ = ops.project_in(h, W_in)
+        q, _, _, _ = ops.project_in(h, W_in, w_prep=P_in)
         _, _, w, _ = ops.route(q, pages.S, rows_per_lib=T, top_k=0, route_temp=CFG3["route_temp"])
         r = ops.read_prefill(q, pages, w, rows_per_lib=T, read_temp=CFG3["read_temp"])
-        ops.project_out(r, W_out, h, want_delta=False, h_out=h_out)
+        ops.project_out(r, W_out, h, want_delta=False, h_out=h_out, w_prep=P_out)
         holder["q"], holder["w"] = q, w
 
     with torch.inference_mode():
@@ -864,11 +866,14 @@ def run_ours(args) -> None:
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
+    # the interface weights in the 3xF16 form, prepared once as LibraryInjector does when it first uses them
+    P_in, P_out = ops.weights_prep(W_in), ops.weights_prep(W_out)
+
     def step(h, h_out):
-        q, _, _, _ = ops.project_in(h, W_in)
+        q, _, _, _ = ops.project_in(h, W_in, w_prep=P_in)
         idx, wk, _, _ = ops.route(q, pages.S, rows_per_lib=CFG["T"], top_k=CFG["top_k"], route_temp=CFG["route_temp"])
         r = ops.read_decode(q, pages, idx, wk, rows_per_lib=CFG["T"], read_temp=CFG["read_temp"])
-        _, _, rel = ops.project_out(r, W_out, h, want_delta=False, h_out=h_out, want_rel=True)
+        _, _, rel = ops.project_out(r, W_out, h, want_delta=False, h_out=h_out, want_rel=True, w_prep=P_out)
         return q, idx, wk, rel
 
     # ---- graph capture of one step on static buffers

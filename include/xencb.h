@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define XENCB_ABI_VERSION 2
+#define XENCB_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define XENCB_API __attribute__((visibility("default")))
@@ -75,6 +75,9 @@ XENCB_API int xencb_device_status(void* stream, int clear, unsigned int* status_
  *            XENCB_PIN_RMS into a float32 [n_rows, rank] buffer, then one with XENCB_PIN_L2 over it.
  *   h        [n_rows, d_m] of h_dtype (the reference upcasts h to float32 first; so does this)
  *   w_in     [d_s, d_m] float32; b_in [d_s] or NULL; d_s % 4 == 0
+ *   w_prep   NULL, or w_in prepared by xencb_weights_prep: for n_rows >= 512 (or when w_in is NULL) the GEMM
+ *            then runs as 3xF16 on the f16 tensor cores (fp32-faithful, see xencb_weights_prep; needs
+ *            d_m % 8 == 0); fewer rows keep the 3xTF32 kernel, which is faster at decode sizes
  *   gate_w   [d_m] or NULL (then gate_out is not written); gate_b the scalar gate_b[pos[li]], or gate_b_dev a
  *            device pointer to it (when non-NULL it replaces gate_b: no host read of the parameter, so the call
  *            can be captured in a CUDA graph)
@@ -86,7 +89,7 @@ XENCB_API int xencb_device_status(void* stream, int clear, unsigned int* status_
 #define XENCB_PIN_L2 2
 XENCB_API size_t xencb_project_in_workspace(int64_t n_rows, int d_m, int d_s);
 XENCB_API int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const float* w_in,
-                               const float* b_in, int d_s, int flags, const float* gate_w, float gate_b,
+                               const void* w_prep, const float* b_in, int d_s, int flags, const float* gate_w, float gate_b,
                                const float* gate_b_dev, const float* sel_w, const float* sel_b, int n_cand, float rms_eps, float* q_out,
                                float* gate_out, float* rstd_out, float* z_out, void* workspace,
                                size_t workspace_bytes, void* stream);
@@ -207,9 +210,10 @@ XENCB_API int xencb_shard_merge(const float* parts, int n_shards, int64_t n_rows
  *   delta_out = d in h_dtype (or NULL); h_out = h + delta_out in h_dtype (or NULL; may alias h);
  *   rel_out[row] = ||delta_out|| / (||h|| + 1e-6)                         (or NULL)
  *   h        [n_rows, d_m] of h_dtype; r [n_rows, d_s] float32; w_out [d_m, d_s]; b_out [d_m] or NULL;
- *            d_m % 4 == 0. */
+ *            d_m % 4 == 0. w_prep: NULL or w_out prepared by xencb_weights_prep (as for xencb_project_in). */
 XENCB_API size_t xencb_project_out_workspace(int64_t n_rows, int d_s, int d_m);
-XENCB_API int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_out, const float* b_out, int d_m,
+XENCB_API int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_out, const void* w_prep,
+                                const float* b_out, int d_m,
                       float scale, const float* log_scale_dev, const float* gate, const float* sel_w, float log_alpha,
                       const float* log_alpha_dev, const float* pos_mask,
                       const void* h, int h_dtype, void* delta_out, void* h_out, float* rel_out, void* workspace,
@@ -288,6 +292,22 @@ XENCB_API int xencb_topk_read(const float* q, int64_t n_rows, int d_s, const voi
                               int slots_dtype, int64_t n_pages, int64_t page_stride, int page_rows,
                               const int32_t* page_of, int n_chunks, int64_t n_lib, const int32_t* idx, int n_sets,
                               int k, float read_temp, int read_softmax, float* r_out, float* attn_out, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Weight preparation for the 3xF16 projection GEMM (done once per weight tensor, e.g. when an interface is
+ * loaded): w [n, k] float32 -> prep = a 256-byte head (max |w|, 1/s) followed by the stacked f16 pair
+ * [hi; lo] of w * s, s = 2^e with max|w| * s in [2^14, 2^15). hi + lo keeps ~22 mantissa bits, and the GEMM
+ * sums hi*hi + hi*lo + lo*hi (the relative error of the 3xTF32 product). k % 8 == 0; prep 256-byte aligned,
+ * at least xencb_weights_prep_bytes(n, k) bytes (4 bytes per weight + 256). */
+XENCB_API size_t xencb_weights_prep_bytes(int n, int k);
+XENCB_API int xencb_weights_prep(const float* w, int n, int k, void* prep, size_t prep_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Failure-detection self-test of the bounded waits every pipelined kernel uses: one thread waits, with a limit
+ * of limit_cycles SM cycles (the kernels use 3e9), on an mbarrier phase that nothing completes. The wait gives
+ * up, raises XENCB_DEV_TIMEOUT in the device status word and the kernel returns; *result (device int, or NULL)
+ * becomes 0. The context stays usable. */
+XENCB_API int xencb_wait_selftest(long long limit_cycles, int* result, void* stream);
 
 #ifdef __cplusplus
 }

@@ -19,7 +19,7 @@ OK, EINVAL, ECUDA, ENOTSUP = 0, 1, 2, 3
 DEV_TIMEOUT, DEV_CLAMPED, DEV_BADPAGE = 1, 2, 4
 PIN_RMS, PIN_L2 = 1, 2
 NOALLOC_SCRATCH_BYTES = 16 << 20
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 _p, _i, _i64, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
 
@@ -30,8 +30,8 @@ SIGNATURES: dict = {
     "xencb_launch_count": (ctypes.c_ulonglong, []),
     "xencb_device_status": (_i, [_p, _i, ctypes.POINTER(ctypes.c_uint)]),
     "xencb_project_in_workspace": (_sz, [_i64, _i, _i]),
-    "xencb_project_in": (_i, [_p, _i, _i64, _i, _p, _p, _i, _i, _p, _f, _p, _p, _p, _i, _f, _p, _p, _p, _p, _p,
-                              _sz, _p]),
+    "xencb_project_in": (_i, [_p, _i, _i64, _i, _p, _p, _p, _i, _i, _p, _f, _p, _p, _p, _i, _f, _p, _p, _p, _p,
+                              _p, _sz, _p]),
     "xencb_rms_norm": (_i, [_p, _i, _i64, _i, _f, _p, _p]),
     "xencb_route_k": (_i, [_i, _i]),
     "xencb_route": (_i, [_p, _i64, _i, _p, _i, _p, _i64, _i64, _f, _i, _p, _p, _p, _p, _p, _p]),
@@ -49,8 +49,8 @@ SIGNATURES: dict = {
     "xencb_route_lse": (_i, [_p, _i64, _i, _p, _i, _p, _i64, _i64, _f, _p, _p, _p]),
     "xencb_shard_merge": (_i, [_p, _i, _i64, _i, _p, _p]),
     "xencb_project_out_workspace": (_sz, [_i64, _i, _i]),
-    "xencb_project_out": (_i, [_p, _i64, _i, _p, _p, _i, _f, _p, _p, _p, _f, _p, _p, _p, _i, _p, _p, _p, _p, _sz,
-                               _p]),
+    "xencb_project_out": (_i, [_p, _i64, _i, _p, _p, _p, _i, _f, _p, _p, _p, _f, _p, _p, _p, _i, _p, _p, _p, _p,
+                               _sz, _p]),
     "xencb_selector_weights": (_i, [_p, _i64, _i, _i, _i, _p, _p]),
     "xencb_selector_logits": (_i, [_p, _i, _i64, _i, _p, _p, _i, _i, _f, _p, _p]),
     "xencb_selector_apply": (_i, [_p, _i, _p, _i, _i64, _i, _p, _i, _i, _f, _p, _p]),
@@ -60,6 +60,9 @@ SIGNATURES: dict = {
     "xencb_select_scores": (_i, [_p, _i64, _i, _i, _i, _i, _p, _i, _i64, _i, _i, _p, _p, _i64, _i64, _i, _i, _p, _p]),
     "xencb_select_topk": (_i, [_p, _i64, _i, _i, _p, _p, _p]),
     "xencb_topk_read": (_i, [_p, _i64, _i, _p, _p, _i, _i64, _i64, _i, _p, _i, _i64, _p, _i, _i, _f, _i, _p, _p, _p]),
+    "xencb_wait_selftest": (_i, [ctypes.c_longlong, _p, _p]),
+    "xencb_weights_prep_bytes": (_sz, [_i, _i]),
+    "xencb_weights_prep": (_i, [_p, _i, _i, _p, _sz, _p]),
 }
 
 _lib = None

@@ -167,16 +167,20 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 
 // The same bounded wait without the suspend hint: for short waits on a hot path (a phase that other warps are
 // about to complete), where a suspended thread's wake-up would cost more than the few retries it saves.
-__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_spin_limit(uint64_t* bar, uint32_t parity, long long limit_cycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 0u && clock64() - t0 > XENCB_WAIT_CYCLES) {
+    if ((it & 63u) == 0u && clock64() - t0 > limit_cycles) {
       flag_error(XENCB_DEV_TIMEOUT);
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity) {
+  return mbar_wait_spin_limit(bar, parity, XENCB_WAIT_CYCLES);
 }
 
 // 1-D bulk copy global -> this CTA's shared memory, completion signalled on `bar` as transaction bytes.

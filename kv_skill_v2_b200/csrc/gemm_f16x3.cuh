@@ -1,0 +1,216 @@
+// Projection GEMM, fp32-faithful on the f16 tensor cores ("3xF16"), tcgen05 + TMEM + TMA, split-K.
+//
+//   part[z][m][n] = sum_{k in split z} X[m][k] * W[n][k]         W: [N, K] (nn.Linear layout), X: [M, K]
+//
+// f16 carries the same 10 explicit mantissa bits as tf32, so splitting an fp32 value v into f16 hi = rn(v) and
+// lo = rn(v - hi) keeps ~22 bits, and hi*hi + hi*lo + lo*hi (the dropped lo*lo is below 2^-22 relative) gives the
+// accuracy of the 3xTF32 product, with twice the K per tensor-core instruction of kind::tf32 and half the
+// operand bytes. f16 has a small exponent range, so both sides are scaled by powers of two first (exact):
+//   * W once per weight tensor (xencb_weights_prep): s_w = 2^e with max|W| s_w in [2^14, 2^15), stored as the
+//     stacked f16 pair [W_hi; W_lo] ([2N, K], the same 4 bytes per weight as fp32) and 1 / s_w;
+//   * X per call and per row (split_rows_f16x2_kernel): s_m = 2^e_m from the row's max |x|, rows stacked
+//     [X_hi; X_lo] ([2M, K]) with 1 / s_m per row.
+// Values far below a row's (or the weight's) maximum lose relative precision in f16's subnormal range; their
+// share of a dot product is below 2^-28 of its largest term.
+//
+// gemm_f16x3_kernel: D[n][m] = W[n, :] . X[m, :] (128 output features = UMMA M, up to 64 tokens = UMMA N).
+// Warp 0 lane 0 TMA-loads per 64-column k-block the four 128-byte-swizzled boxes W_hi, W_lo [128 x 64] and
+// X_hi, X_lo [64 x 64] into a 4-stage ring (weights with L2 evict-last); warp 1 lane 0 issues 4 k-steps x 3
+// tcgen05.mma kind::f16 (f32 accumulate in TMEM) per k-block and commits each stage back to the producer;
+// warps 2-5 read the accumulator (tcgen05.ld), undo the scales and store the split partial. Boxes that run
+// past N or M read rows of the other half of the stacked pair or zeros; they only reach outputs n >= N or
+// m >= M, which are not stored. Every barrier wait is bounded; TMEM is freed on every path.
+#pragma once
+
+#include "tc.cuh"
+
+namespace xencb {
+
+constexpr int H3_BM = 128;  // output features per CTA (UMMA M)
+constexpr int H3_BN = 64;   // tokens per CTA (UMMA N)
+constexpr int H3_BK = 64;   // K per k-block: 64 f16 = one 128-byte swizzle row
+constexpr int H3_STAGES = 4;
+constexpr int H3_WBOX = H3_BM * H3_BK * 2;  // 16 KiB
+constexpr int H3_XBOX = H3_BN * H3_BK * 2;  // 8 KiB
+constexpr int H3_STAGE = 2 * H3_WBOX + 2 * H3_XBOX;  // W_hi | W_lo | X_hi | X_lo
+constexpr int H3_THREADS = 32 * 6;
+constexpr size_t H3_SMEM = 1024 + (size_t)H3_STAGES * H3_STAGE + 256;
+constexpr uint32_t H3_TMEM_COLS = 64;
+constexpr int64_t H3_MIN_ROWS = 512;  // below this many rows the 3xTF32 kernel is faster (latency-bound GEMMs)
+constexpr int WPREP_HEAD = 256;  // bytes before [W_hi; W_lo] in a prepared weight: float max_bits, float inv_scale
+
+// 2^e with max * 2^e in [2^14, 2^15) (e = 0 for max 0 or non-finite): exact power-of-two scale into f16 range.
+__device__ __forceinline__ float f16_range_scale(float mx) {
+  if (!(mx > 0.f) || !isfinite(mx)) return 1.f;
+  int ex;
+  frexpf(mx, &ex);  // mx = f * 2^ex, f in [0.5, 1)
+  return ldexpf(1.f, 15 - ex);
+}
+
+template <typename T>
+__device__ __forceinline__ void split_f16(float v, __half& hi, __half& lo) {
+  hi = __float2half_rn(v);
+  lo = __float2half_rn(v - __half2float(hi));
+}
+
+// Weight prep, pass 1: max |W| into the head's first word (float bits compare as unsigned for x >= 0).
+__global__ void __launch_bounds__(256) absmax_kernel(const float* __restrict__ w, int64_t n, unsigned int* out) {
+  float m = 0.f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    m = fmaxf(m, fabsf(w[i]));
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
+}
+
+// Weight prep, pass 2: [W_hi; W_lo] with the scale from pass 1, and 1 / s_w into the head.
+__global__ void __launch_bounds__(256) split_weights_kernel(const float* __restrict__ w, int64_t n,
+                                                            const unsigned int* __restrict__ maxbits,
+                                                            __half* __restrict__ hi, __half* __restrict__ lo,
+                                                            float* __restrict__ inv_scale) {
+  const float s = f16_range_scale(__uint_as_float(*maxbits));
+  if (blockIdx.x == 0 && threadIdx.x == 0) *inv_scale = 1.f / s;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    __half h, l;
+    split_f16<float>(w[i] * s, h, l);
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
+// X per call: one CTA per row, [X_hi; X_lo] rows scaled by the row's own power of two, 1 / s_m per row.
+template <typename T>
+__global__ void __launch_bounds__(256) split_rows_f16x2_kernel(const T* __restrict__ x, int64_t M, int K,
+                                                               __half* __restrict__ hi, __half* __restrict__ lo,
+                                                               float* __restrict__ inv_scale) {
+  __shared__ float red[32];
+  const int64_t m = blockIdx.x;
+  const T* xr = x + m * K;
+  float mx = 0.f;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(to_f32(xr[k])));
+  mx = warp_max(mx);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_max(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float s = f16_range_scale(red[0]);
+  if (threadIdx.x == 0) inv_scale[m] = 1.f / s;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    __half h, l;
+    split_f16<float>(to_f32(xr[k]) * s, h, l);
+    hi[m * K + k] = h;
+    lo[m * K + k] = l;
+  }
+}
+
+__global__ void __launch_bounds__(H3_THREADS, 1) gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_w,
+                                                                   const __grid_constant__ CUtensorMap map_x,
+                                                                   int64_t M, int N, int K, int kps,
+                                                                   const float* __restrict__ w_inv_scale,
+                                                                   const float* __restrict__ x_inv_scale,
+                                                                   float* __restrict__ part, int* __restrict__ row_done) {
+  extern __shared__ unsigned char h3_smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(h3_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + H3_STAGES * H3_STAGE);
+  uint64_t* sfree = full + H3_STAGES;
+  uint64_t* done = sfree + H3_STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * H3_BM;
+  const int64_t m0 = (int64_t)blockIdx.y * H3_BN;
+  const int kbeg = blockIdx.z * kps;
+  const int kend = min(K, kbeg + kps);
+  const int nkb = kend > kbeg ? (kend - kbeg + H3_BK - 1) / H3_BK : 0;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&map_w);
+    prefetch_tensormap(&map_x);
+  }
+  // zero the per-row completion counters the following reduce kernel counts on (stream order)
+  if (row_done && blockIdx.x == 0 && blockIdx.z == 0)
+    for (int64_t i = m0 + threadIdx.x; i < min(M, m0 + H3_BN); i += blockDim.x) row_done[i] = 0;
+  if (warp == 1) {
+    tc_alloc(tmem_slot, H3_TMEM_COLS);
+    tc_relinquish();
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < H3_STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&sfree[i], 1);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t taddr = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------------------------------- producer
+    if (lane == 0) {
+      const uint64_t keep = policy_evict_last();
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % H3_STAGES, use = kb / H3_STAGES;
+        if (use > 0 && (!mbar_wait_spin(&sfree[s], (use - 1) & 1) || *abort_flag)) { *abort_flag = 1; break; }
+        unsigned char* st = smem + s * H3_STAGE;
+        mbar_arrive_expect_tx(&full[s], H3_STAGE);
+        const int k = kbeg + kb * H3_BK;
+        tma_load_2d_hint(st, &map_w, k, n0, &full[s], keep);
+        tma_load_2d_hint(st + H3_WBOX, &map_w, k, N + n0, &full[s], keep);
+        tma_load_2d(st + 2 * H3_WBOX, &map_x, k, (int)m0, &full[s]);
+        tma_load_2d(st + 2 * H3_WBOX + H3_XBOX, &map_x, k, (int)(M + m0), &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc(UMMA_F16, UMMA_F16, H3_BM, H3_BN);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % H3_STAGES;
+        if (!mbar_wait_spin(&full[s], (kb / H3_STAGES) & 1) || *abort_flag) { *abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t sb = smem_u32(smem + s * H3_STAGE);
+        const uint32_t wh = sb, wl = sb + H3_WBOX, xh = sb + 2 * H3_WBOX, xl = xh + H3_XBOX;
+#pragma unroll
+        for (int ks = 0; ks < H3_BK / 16; ++ks) {  // 16 f16 per UMMA k-step: 32 bytes along the swizzle row
+          const uint32_t off = ks * 32;
+          tc_mma<0>(taddr, umma_desc_k_sw128(wh + off), umma_desc_k_sw128(xh + off), idesc, kb > 0 || ks > 0);
+          tc_mma<0>(taddr, umma_desc_k_sw128(wh + off), umma_desc_k_sw128(xl + off), idesc, true);
+          tc_mma<0>(taddr, umma_desc_k_sw128(wl + off), umma_desc_k_sw128(xh + off), idesc, true);
+        }
+        tc_commit(&sfree[s]);  // the stage is free once these MMAs have read it
+      }
+      tc_commit(done);
+    }
+  } else {
+    // ------------------------------------------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int n = n0 + q * 32 + lane;
+    float* out = part + (int64_t)blockIdx.z * M * N;
+    const bool ok = nkb > 0 && mbar_wait_bounded(done, 0) && !*abort_flag;
+    tc_fence_after();
+    const float iw = *w_inv_scale;
+#pragma unroll
+    for (int c = 0; c < H3_BN; c += 16) {
+      float v[16];
+      tc_ld16(taddr + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int64_t m = m0 + c + i;
+        if (m < M && n < N) out[m * N + n] = ok ? v[i] * iw * __ldg(x_inv_scale + m) : 0.f;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tc_dealloc(taddr, H3_TMEM_COLS);
+}
+
+}  // namespace xencb

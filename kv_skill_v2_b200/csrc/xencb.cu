@@ -17,6 +17,7 @@
 #include "common.cuh"
 #include "project.cuh"
 #include "gemm_tc.cuh"
+#include "gemm_f16x3.cuh"
 #include "read_decode.cuh"
 #include "read_decode_mma.cuh"
 #include "read_multi.cuh"
@@ -155,10 +156,17 @@ GemmPlan plan_gemm_simt(int64_t M, int N, int K, int sms) {
   return p;
 }
 
+// Workspace of a projection GEMM: the split partials, then (tensor-core paths) the X staging: float32 X for the
+// 3xTF32 kernel, or [X_hi; X_lo] f16 (the same bytes) plus one float per row for the 3xF16 kernel.
+size_t gemm_xstage_bytes(int64_t M, int K) {
+  return align_up((size_t)M * K * sizeof(float), 256) + align_up((size_t)M * sizeof(float), 256);
+}
+
 size_t gemm_ws_bytes(int64_t M, int N, int K, int sms, bool convert_x) {
+  (void)convert_x;
   size_t b = plan_gemm_simt(M, N, K, sms).part_bytes;
   if (K % 4 == 0) {
-    size_t t = plan_gemm_tc(M, N, K, sms).part_bytes + (convert_x ? align_up((size_t)M * K * sizeof(float), 256) : 0);
+    size_t t = plan_gemm_tc(M, N, K, sms).part_bytes + gemm_xstage_bytes(M, K);
     if (t > b) b = t;
   }
   return b;
@@ -207,7 +215,37 @@ int tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dt, uint32_t esize, cons
 // `xbuf` (M*K float32, may be null when TX is float) stages a 16-bit X as float32 for the TMA path.
 template <typename TX>
 int launch_gemm(const void* X, int64_t M, int K, const float* W, int N, int sms, float* part, float* xbuf,
-                int* row_done, cudaStream_t st, GemmPlan* used) {
+                int* row_done, cudaStream_t st, GemmPlan* used, const void* w_prep = nullptr) {
+  // 3xF16 (weights split once by xencb_weights_prep, X split here with a power-of-two scale per row) pays off
+  // when the GEMM is throughput-bound: many rows. At decode sizes the split-K CTAs each see a few k-blocks, the
+  // GEMM is latency-bound and the extra row-split launch costs more than the halved MMA count saves, so the
+  // 3xTF32 kernel runs unless W itself was not given.
+  const bool f16x3 = w_prep && (W == nullptr || M >= H3_MIN_ROWS);
+  if (f16x3 && K % 8 == 0 && aligned(w_prep, 256) && xbuf && M <= INT32_MAX / 2 && N <= INT32_MAX / 2) {
+    const GemmPlan p = plan_gemm_tc(M, N, K, sms);
+    __half* xs = reinterpret_cast<__half*>(xbuf);  // [X_hi; X_lo]: 2 M K halves = M K floats of staging
+    float* x_inv = reinterpret_cast<float*>(reinterpret_cast<char*>(xbuf) + align_up((size_t)M * K * sizeof(float), 256));
+    split_rows_f16x2_kernel<TX><<<(unsigned)M, 256, 0, st>>>(static_cast<const TX*>(X), M, K, xs, xs + M * (int64_t)K,
+                                                            x_inv);
+    XENCB_CHECK_LAUNCH("split_rows_f16x2 launch");
+    const char* wp = static_cast<const char*>(w_prep);
+    CUtensorMap mw, mx;
+    int rc = tensor_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, wp + WPREP_HEAD, (uint64_t)K, 2 * (uint64_t)N,
+                           (uint64_t)K * 2, H3_BK, H3_BM);
+    if (rc) return rc;
+    rc = tensor_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xs, (uint64_t)K, 2 * (uint64_t)M, (uint64_t)K * 2,
+                       H3_BK, H3_BN);
+    if (rc) return rc;
+    rc = ensure_smem(gemm_f16x3_kernel, (int)H3_SMEM);
+    if (rc) return rc;
+    dim3 grid((N + H3_BM - 1) / H3_BM, (unsigned)((M + H3_BN - 1) / H3_BN), p.splits);
+    gemm_f16x3_kernel<<<grid, H3_THREADS, H3_SMEM, st>>>(mw, mx, M, N, K, p.kps,
+                                                         reinterpret_cast<const float*>(wp) + 1, x_inv, part,
+                                                         row_done);
+    XENCB_CHECK_LAUNCH("gemm_f16x3 launch");
+    *used = p;
+    return XENCB_OK;
+  }
   const bool tc_ok = (K % 4 == 0) && aligned(W, 16) && (std::is_same<TX, float>::value ? aligned(X, 16) : xbuf != nullptr);
   if (tc_ok) {
     const GemmPlan p = plan_gemm_tc(M, N, K, sms);
@@ -481,6 +519,16 @@ rc_t launch_route_logits(const float* q, int64_t n_rows, int d_s, const float* S
 
 using namespace xencb;
 
+// The wait self-test: one thread waits, with the given limit, on an mbarrier phase that nothing completes.
+__global__ void wait_selftest_kernel(long long limit_cycles, int* result) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  const bool ok = mbar_wait_spin_limit(&bar, 0, limit_cycles);
+  if (result) *result = ok ? 1 : 0;
+}
+
 // Library build plan: splits per chunk and the column-sum workspace.
 namespace {
 struct BuildPlan {
@@ -541,12 +589,14 @@ size_t xencb_project_in_workspace(int64_t n_rows, int d_m, int d_s) {
          align_up((size_t)n_rows * sizeof(int), 256);
 }
 
-int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const float* w_in, const float* b_in,
-                     int d_s, int flags, const float* gate_w, float gate_b, const float* gate_b_dev,
+int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const float* w_in, const void* w_prep,
+                     const float* b_in, int d_s, int flags, const float* gate_w, float gate_b, const float* gate_b_dev,
                      const float* sel_w, const float* sel_b, int n_cand, float rms_eps, float* q_out, float* gate_out, float* rstd_out, float* z_out,
                      void* workspace, size_t workspace_bytes, void* stream) {
   if (flags & ~(XENCB_PIN_RMS | XENCB_PIN_L2)) return fail(XENCB_EINVAL, "project_in: unknown flags 0x%x", flags);
-  if (!h || !w_in || !q_out) return fail(XENCB_EINVAL, "project_in: h, w_in and q_out are required");
+  if (!h || (!w_in && !w_prep) || !q_out) return fail(XENCB_EINVAL, "project_in: h, w_in (or w_prep) and q_out are required");
+  if (!w_in && (d_m % 8 != 0 || !aligned(w_prep, 256)))
+    return fail(XENCB_EINVAL, "project_in: without w_in, w_prep must be 256-byte aligned and d_m %% 8 == 0");
   if (n_rows <= 0 || d_m <= 0 || d_s <= 0)
     return fail(XENCB_EINVAL, "project_in: n_rows=%lld d_m=%d d_s=%d must be positive", (long long)n_rows, d_m, d_s);
   if (!elem_size(h_dtype)) return fail(XENCB_EINVAL, "project_in: h_dtype %d unknown", h_dtype);
@@ -569,15 +619,22 @@ int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const 
   float* part = reinterpret_cast<float*>(ws);
   float* nq_part = reinterpret_cast<float*>(ws + g_bytes);
   int* row_done = reinterpret_cast<int*>(ws + g_bytes + nq_bytes);
-  // float32 staging of a 16-bit h for the TMA path sits after the tensor-core partials
+  // X staging for the tensor-core paths sits after the tensor-core partials
   float* xbuf = (d_m % 4 == 0) ? reinterpret_cast<float*>(ws + plan_gemm_tc(n_rows, d_s, d_m, di.sms).part_bytes)
                                : nullptr;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   GemmPlan gp;
   switch (h_dtype) {
-    case XENCB_F32: rc = launch_gemm<float>(h, n_rows, d_m, w_in, d_s, di.sms, part, nullptr, row_done, st, &gp); break;
-    case XENCB_F16: rc = launch_gemm<__half>(h, n_rows, d_m, w_in, d_s, di.sms, part, xbuf, row_done, st, &gp); break;
-    default: rc = launch_gemm<__nv_bfloat16>(h, n_rows, d_m, w_in, d_s, di.sms, part, xbuf, row_done, st, &gp); break;
+    case XENCB_F32:
+      rc = launch_gemm<float>(h, n_rows, d_m, w_in, d_s, di.sms, part, w_prep ? xbuf : nullptr, row_done, st, &gp,
+                              w_prep);
+      break;
+    case XENCB_F16:
+      rc = launch_gemm<__half>(h, n_rows, d_m, w_in, d_s, di.sms, part, xbuf, row_done, st, &gp, w_prep);
+      break;
+    default:
+      rc = launch_gemm<__nv_bfloat16>(h, n_rows, d_m, w_in, d_s, di.sms, part, xbuf, row_done, st, &gp, w_prep);
+      break;
   }
   if (rc) return rc;
 #define XENCB_PIN(T)                                                                                         \
@@ -956,12 +1013,15 @@ size_t xencb_project_out_workspace(int64_t n_rows, int d_s, int d_m) {
          align_up((size_t)n_rows * nch * 3 * sizeof(float), 256) + align_up((size_t)n_rows * sizeof(int), 256);
 }
 
-int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_out, const float* b_out, int d_m,
+int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_out, const void* w_prep,
+                      const float* b_out, int d_m,
                       float scale, const float* log_scale_dev, const float* gate, const float* sel_w, float log_alpha,
                       const float* log_alpha_dev, const float* pos_mask,
                       const void* h, int h_dtype, void* delta_out, void* h_out, float* rel_out, void* workspace,
                       size_t workspace_bytes, void* stream) {
-  if (!r || !w_out || !h) return fail(XENCB_EINVAL, "project_out: r, w_out and h are required");
+  if (!r || (!w_out && !w_prep) || !h) return fail(XENCB_EINVAL, "project_out: r, w_out (or w_prep) and h are required");
+  if (!w_out && (d_s % 8 != 0 || !aligned(w_prep, 256)))
+    return fail(XENCB_EINVAL, "project_out: without w_out, w_prep must be 256-byte aligned and d_s %% 8 == 0");
   if (n_rows <= 0 || d_m <= 0 || d_s <= 0) return fail(XENCB_EINVAL, "project_out: sizes must be positive");
   if (!elem_size(h_dtype)) return fail(XENCB_EINVAL, "project_out: h_dtype %d unknown", h_dtype);
   if (d_m % 4 != 0)
@@ -985,7 +1045,9 @@ int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_ou
   float* cn_part = norm_part + (size_t)n_rows * nch * 2;
   int* row_done = reinterpret_cast<int*>(ws + g_bytes + d_bytes + np_bytes);
   GemmPlan gp;
-  rc = launch_gemm<float>(r, n_rows, d_s, w_out, d_m, di.sms, part, nullptr, nullptr, st, &gp);
+  float* xbuf = (d_s % 4 == 0) ? reinterpret_cast<float*>(ws + plan_gemm_tc(n_rows, d_m, d_s, di.sms).part_bytes)
+                               : nullptr;
+  rc = launch_gemm<float>(r, n_rows, d_s, w_out, d_m, di.sms, part, w_prep ? xbuf : nullptr, nullptr, st, &gp, w_prep);
   if (rc) return rc;
   const float alpha = expf(log_alpha);
 #define XENCB_POUT(T)                                                                                          \
@@ -1310,6 +1372,40 @@ int xencb_topk_read(const float* q, int64_t n_rows, int d_s, const void* slots, 
     case XENCB_F16: return launch(topk_read_kernel<__half, TR_ROWS>);
     default: return launch(topk_read_kernel<__nv_bfloat16, TR_ROWS>);
   }
+}
+
+size_t xencb_weights_prep_bytes(int n, int k) {
+  if (n <= 0 || k <= 0) return 0;
+  return WPREP_HEAD + 4 * (size_t)n * (size_t)k;
+}
+
+int xencb_weights_prep(const float* w, int n, int k, void* prep, size_t prep_bytes, void* stream) {
+  if (!w || !prep) return fail(XENCB_EINVAL, "weights_prep: w and prep are required");
+  if (n <= 0 || k <= 0) return fail(XENCB_EINVAL, "weights_prep: sizes must be positive");
+  if (k % 8) return fail(XENCB_EINVAL, "weights_prep: k=%d must be a multiple of 8", k);
+  if (!aligned(prep, 256)) return fail(XENCB_EINVAL, "weights_prep: prep must be 256-byte aligned");
+  if (prep_bytes < xencb_weights_prep_bytes(n, k))
+    return fail(XENCB_EINVAL, "weights_prep: prep needs %zu bytes (got %zu)", xencb_weights_prep_bytes(n, k), prep_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  unsigned int* head = static_cast<unsigned int*>(prep);
+  cudaError_t e = cudaMemsetAsync(head, 0, sizeof(unsigned int), st);
+  if (e != cudaSuccess) return cuda_fail(e, "weights_prep memset");
+  const int64_t cnt = (int64_t)n * k;
+  const unsigned blocks = (unsigned)std::min<int64_t>((cnt + 255) / 256, 4096);
+  absmax_kernel<<<blocks, 256, 0, st>>>(w, cnt, head);
+  XENCB_CHECK_LAUNCH("absmax launch");
+  __half* hi = reinterpret_cast<__half*>(static_cast<char*>(prep) + WPREP_HEAD);
+  split_weights_kernel<<<blocks, 256, 0, st>>>(w, cnt, head, hi, hi + cnt, reinterpret_cast<float*>(head) + 1);
+  XENCB_CHECK_LAUNCH("split_weights launch");
+  return XENCB_OK;
+}
+
+int xencb_wait_selftest(long long limit_cycles, int* result, void* stream) {
+  if (limit_cycles <= 0 || limit_cycles > 4000000000ll)
+    return fail(XENCB_EINVAL, "wait_selftest: limit_cycles must be in (0, 4e9]");
+  wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_cycles, result);
+  XENCB_CHECK_LAUNCH("wait_selftest_kernel launch");
+  return XENCB_OK;
 }
 
 int xencb_read_decode_noalloc(const float* q, int64_t n_rows, int d_s, const void* slots, int slots_dtype,

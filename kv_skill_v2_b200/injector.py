@@ -75,6 +75,10 @@ class ExternalSkillInjector:
         self.calib: Optional[dict] = None
         self.skill: Optional[KVSkill] = None
         self.pos_mask: Optional[torch.Tensor] = None  # [B, T] multiplier of delta (None: all positions)
+        # projection weights in the 3xF16 form (ops.weights_prep), keyed by storage, version and shape; each
+        # entry keeps its source tensor alive so the key cannot be reused by another tensor
+        self.gemm_f16x3 = True
+        self._wprep: dict = {}
         self._attach()
 
     def _active(self) -> bool:
@@ -154,6 +158,27 @@ class XEncInjector(ExternalSkillInjector):
                                read_softmax=self.read_softmax)
 
     # ------------------------------------------------------------------ shared projection machinery
+    def _prep(self, W: torch.Tensor) -> Optional[torch.Tensor]:
+        """W [out, in] float32 on the device in the 3xF16 form, or None (disabled, or in % 8 != 0)."""
+        if not self.gemm_f16x3 or W.shape[-1] % 8 != 0 or not W.is_cuda:
+            return None
+        key = (W.data_ptr(), W._version, tuple(W.shape), str(W.device))
+        hit = self._wprep.get(key)
+        if hit is not None:
+            return hit[1]
+        if len(self._wprep) >= 64:
+            self._wprep.clear()
+        prep = ops.weights_prep(W)
+        self._wprep[key] = (W, prep)
+        return prep
+
+    def _weights_key(self) -> tuple:
+        """Storage and version of every interface parameter (a captured step is valid only for these)."""
+        itf = self.itf
+        if not isinstance(itf, nn.Module):
+            return ()
+        return tuple((p.data_ptr(), p._version) for p in itf.parameters())
+
     def _fast_interface(self) -> bool:
         return isinstance(self.itf, (ModelInterface, LinearInterface))
 
@@ -168,7 +193,8 @@ class XEncInjector(ExternalSkillInjector):
             sel_w = sel_fuse.u.weight.detach().float().to(h2.device)
             sel_b = sel_fuse.u.bias.detach().float().to(h2.device)
         if isinstance(itf, LinearInterface):
-            q, _, _, z = ops.project_in(h2, _on(itf.w_in.detach(), h2).float(), sel_w=sel_w, sel_b=sel_b)
+            W = _on(itf.w_in.detach(), h2).float()
+            q, _, _, z = ops.project_in(h2, W, sel_w=sel_w, sel_b=sel_b, w_prep=self._prep(W))
             return q, None, None, z
         p = itf._pos[li]
         gate_w = _on(itf.gate_w.detach(), h2).float()
@@ -177,18 +203,22 @@ class XEncInjector(ExternalSkillInjector):
         lins = itf.query_weights()
         if len(lins) == 1:
             W, b = lins[0]
-            q, g, _, z = ops.project_in(h2, _f32_on(W, h2), None if b is None else _on(b.detach(), h2).float(),
-                                        gate_w=gate_w, gate_b=gate_b, sel_w=sel_w, sel_b=sel_b)
+            Wf = _f32_on(W, h2)
+            q, g, _, z = ops.project_in(h2, Wf, None if b is None else _on(b.detach(), h2).float(),
+                                        gate_w=gate_w, gate_b=gate_b, sel_w=sel_w, sel_b=sel_b,
+                                        w_prep=self._prep(Wf))
             return q, g, gain, z
         # low-rank A: rms_norm + first map (gate and selector logits on the normed input), then map + L2
         x = h2
         g = z = None
         for i, (W, b) in enumerate(lins):
             first, last = i == 0, i == len(lins) - 1
-            x, g_i, _, z_i = ops.project_in(x, _f32_on(W, h2),
+            Wf = _f32_on(W, h2)
+            x, g_i, _, z_i = ops.project_in(x, Wf,
                                             None if b is None else _on(b.detach(), h2).float(), rms=first, l2=last,
                                             gate_w=gate_w if first else None, gate_b=gate_b,
-                                            sel_w=sel_w if first else None, sel_b=sel_b if first else None)
+                                            sel_w=sel_w if first else None, sel_b=sel_b if first else None,
+                                            w_prep=self._prep(Wf))
             if first:
                 g, z = g_i, z_i
         return x, g, gain, z
@@ -233,6 +263,7 @@ class XEncInjector(ExternalSkillInjector):
     def _finish(self, h, h2, r, g, scale, li, inject, sel_col=None, log_alpha=0.0, extra=None, log_scale=None):
         lead = h.shape[:-1]
         W, b = self._write_weights(h2)
+        wp = self._prep(W)
         pm = self._pos_mask(h) if inject else None
         if extra is not None:  # a tensor calibration gain: fold into the per-row gate
             g = (g if g is not None else torch.ones(r.shape[0], device=r.device)) * extra.reshape(-1).float()
@@ -241,11 +272,11 @@ class XEncInjector(ExternalSkillInjector):
             _, h_new, rel = ops.project_out(r, W, h2, b_out=b, scale=float(self.gain_scale) * float(scale),
                                             log_scale=log_scale, gate=g, sel_w=sel_col, log_alpha=log_alpha,
                                             pos_mask=pm, want_delta=False,
-                                            h_out=h_new, want_rel=True)
+                                            h_out=h_new, want_rel=True, w_prep=wp)
             return h_new.view(h.shape), rel
         delta, _, _ = ops.project_out(r, W, h2.float() if h2.dtype != torch.float32 else h2, b_out=b,
                                       scale=float(self.gain_scale) * float(scale), log_scale=log_scale, gate=g,
-                                      sel_w=sel_col, log_alpha=log_alpha, want_delta=True)
+                                      sel_w=sel_col, log_alpha=log_alpha, want_delta=True, w_prep=wp)
         return delta.view(*lead, -1)
 
     def _duck_finish(self, h, hn, r, gcal, li, inject, selector=None):
@@ -434,7 +465,8 @@ class LibraryInjector(XEncInjector):
         # copy h in, replay, and return copies of the static outputs (so a caller may keep them).
         pages = self._pages(li, h)
         key = (li, tuple(h.shape), h.dtype, h.device, id(pages), float(self.gain_scale), self.top_k,
-               float(self.read_temp), float(self.route_temp), bool(self.read_softmax))
+               float(self.read_temp), float(self.route_temp), bool(self.read_softmax), self._weights_key(),
+               bool(self.gemm_f16x3))
         ent = self._graphs.get(key)
         if ent is None:
             out = self._run_lib_eager(h, li, inject, sel)
@@ -442,9 +474,10 @@ class LibraryInjector(XEncInjector):
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
                 h_new_s, rel_s = self._run_lib_eager(h_static, li, inject, sel)
-            self._graphs[key] = (graph, h_static, h_new_s, rel_s, self.last_route, pages)
+            # the entry keeps the prepared weights it captured alive
+            self._graphs[key] = (graph, h_static, h_new_s, rel_s, self.last_route, pages, list(self._wprep.values()))
             return out
-        graph, h_static, h_new_s, rel_s, route_s, _ = ent
+        graph, h_static, h_new_s, rel_s, route_s, _, _ = ent
         h_static.copy_(h)
         graph.replay()
         self.last_route = route_s

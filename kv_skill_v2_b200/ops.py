@@ -98,12 +98,30 @@ def _dev_scalar(x, what: str):
     return float(x), None
 
 
+def weights_prep(w: torch.Tensor) -> torch.Tensor:
+    """The 3xF16 form of a float32 weight [n, k] (k % 8 == 0) for project_in / project_out's w_prep: a 256-byte
+    head, then the stacked f16 pair [hi; lo] of w scaled by a power of two (4 bytes per weight)."""
+    dev = _cuda("weights_prep", w)
+    w = _f32(w, "w")
+    n, k = w.shape
+    if k % 8:
+        raise ValueError(f"weights_prep: k={k} must be a multiple of 8")
+    with _on_device(dev):
+        nbytes = N.lib().xencb_weights_prep_bytes(n, k)
+        prep = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        N.call("xencb_weights_prep", _ptr(w), n, k, _ptr(prep), nbytes, _stream(dev))
+    return prep
+
+
 def project_in(h2: torch.Tensor, w_in: torch.Tensor, b_in=None, *, rms: bool = True, l2: bool = True,
-               gate_w=None, gate_b=0.0, sel_w=None, sel_b=None, eps: float = 1e-6):
+               gate_w=None, gate_b=0.0, sel_w=None, sel_b=None, eps: float = 1e-6,
+               w_prep: Optional[torch.Tensor] = None, prefer_prep: bool = False):
     """(q [R, d_s], gate [R] | None, rstd [R], z [R, n_cand] | None) for rows h2 [R, d_m].
 
     q = L2((rms_norm(h2) if rms else h2) @ w_in^T + b_in) (L2 only if l2); w_in is [d_s, d_m] (nn.Linear).
-    gate_b: a number, or a one-element device tensor read by the kernel."""
+    gate_b: a number, or a one-element device tensor read by the kernel. w_prep: weights_prep(w_in), to run the
+    GEMM as 3xF16 on the f16 tensor cores (same accuracy, twice the rate of 3xTF32) for 512 rows or more;
+    prefer_prep=True uses it at any row count (w_in then only gives the shape)."""
     dev = _cuda("project_in", h2, w_in, b_in, gate_w, sel_w, sel_b)
     h2 = h2.contiguous()
     w_in = _f32(w_in, "w_in")
@@ -124,7 +142,8 @@ def project_in(h2: torch.Tensor, w_in: torch.Tensor, b_in=None, *, rms: bool = T
     with _on_device(dev):
         ws_bytes = N.lib().xencb_project_in_workspace(R, d_m, d_s)
         ws = _workspace(ws_bytes, dev)
-        N.call("xencb_project_in", _ptr(h2), _hdt(h2, "h"), R, d_m, _ptr(w_in), _ptr(b_in), d_s, flags,
+        w_arg = None if (prefer_prep and w_prep is not None) else w_in
+        N.call("xencb_project_in", _ptr(h2), _hdt(h2, "h"), R, d_m, _ptr(w_arg), _ptr(w_prep), _ptr(b_in), d_s, flags,
                _ptr(gate_w), gb, _ptr(gb_dev), _ptr(sel_w), _ptr(sel_b), n_cand, eps, _ptr(q), _ptr(gate),
                _ptr(rstd), _ptr(z), _ptr(ws), ws.numel(), _stream(dev))
     return q, gate, rstd, z
@@ -132,13 +151,15 @@ def project_in(h2: torch.Tensor, w_in: torch.Tensor, b_in=None, *, rms: bool = T
 
 def project_out(r: torch.Tensor, w_out: torch.Tensor, h2: torch.Tensor, *, b_out=None, scale: float = 1.0,
                 log_scale: Optional[torch.Tensor] = None, gate=None, sel_w=None, log_alpha=0.0, pos_mask=None,
-                want_delta: bool = True, h_out: Optional[torch.Tensor] = None, want_rel: bool = False):
+                want_delta: bool = True, h_out: Optional[torch.Tensor] = None, want_rel: bool = False,
+                w_prep: Optional[torch.Tensor] = None, prefer_prep: bool = False):
     """(delta | None, h_out | None, rel | None).
 
     d = scale * exp(log_scale) * gate * (r @ w_out^T + b_out), w_out [d_m, d_s] (nn.Linear); optional
     LayerSelector matched norm with per-row weight sel_w and log_alpha (a number or a one-element device tensor;
     log_scale is a one-element device tensor or None);
-    d *= pos_mask; delta = d in h2's dtype; h_out = h2 + delta; rel = ||delta|| / (||h2|| + 1e-6)."""
+    d *= pos_mask; delta = d in h2's dtype; h_out = h2 + delta; rel = ||delta|| / (||h2|| + 1e-6).
+    w_prep: weights_prep(w_out) for the 3xF16 GEMM."""
     dev = _cuda("project_out", r, w_out, h2, b_out, gate, sel_w, pos_mask, h_out)
     r = _f32(r, "r")
     w_out = _f32(w_out, "w_out")
@@ -158,7 +179,9 @@ def project_out(r: torch.Tensor, w_out: torch.Tensor, h2: torch.Tensor, *, b_out
     with _on_device(dev):
         ws_bytes = N.lib().xencb_project_out_workspace(R, d_s, d_m)
         ws = _workspace(ws_bytes, dev)
-        N.call("xencb_project_out", _ptr(r), R, d_s, _ptr(w_out), _ptr(b_out), d_m, float(scale), _ptr(ls_dev),
+        w_arg = None if (prefer_prep and w_prep is not None) else w_out
+        N.call("xencb_project_out", _ptr(r), R, d_s, _ptr(w_arg), _ptr(w_prep), _ptr(b_out), d_m, float(scale),
+               _ptr(ls_dev),
                _ptr(gate), _ptr(sel_w), la, _ptr(la_dev), _ptr(pos_mask), _ptr(h2), _hdt(h2, "h"), _ptr(delta),
                _ptr(h_out), _ptr(rel), _ptr(ws), ws.numel(), _stream(dev))
     return delta, h_out, rel
@@ -605,6 +628,16 @@ def topk_read(q: torch.Tensor, pages: Pages, idx: torch.Tensor, *, read_temp: fl
                pages.n_lib, _ptr(idx), n_sets, k, float(read_temp), int(bool(read_softmax)), _ptr(r), _ptr(attn),
                _stream(dev))
     return r, attn
+
+
+def wait_selftest(dev: torch.device, limit_cycles: int = 2_000_000) -> int:
+    """Run the bounded-wait self-test on `dev` (a wait that nothing satisfies must give up); returns the
+    kernel's result (0 = gave up). The device status then carries XENCB_DEV_TIMEOUT."""
+    dev = torch.device(dev)
+    res = torch.full((1,), -1, dtype=torch.int32, device=dev)
+    with _on_device(dev):
+        N.call("xencb_wait_selftest", int(limit_cycles), _ptr(res), _stream(dev))
+    return int(res.item())
 
 
 def device_status(dev: torch.device, clear: bool = True) -> int:

@@ -220,6 +220,88 @@ def test_projection_gemm_fp32_faithful(dev, shape, hdt):
     _status_clean(dev)
 
 
+@pytest.mark.parametrize("shape", [(64, 4096, 2048), (200, 520, 264), (8, 96, 16), (130, 40, 44), (64, 2048, 4096),
+                                   (1, 64, 128), (1000, 256, 136)])
+@pytest.mark.parametrize("hdt", [torch.float32, torch.bfloat16, torch.float16])
+def test_projection_gemm_f16x3_fp32_faithful(dev, shape, hdt):
+    """The 3xF16 GEMM (weights split once by weights_prep, rows split per call with their own power-of-two scale)
+    against a float64 product: the same 1e-5 bar as 3xTF32, for row counts and widths that leave partial tiles,
+    and for inputs whose rows span very different magnitudes."""
+    from kv_skill_v2_b200 import ops
+    M, K, N = shape
+    g = torch.Generator().manual_seed(M + K + N + 7)
+    h = torch.randn(M, K, generator=g) * torch.logspace(-3, 3, M).view(M, 1)  # rows from 1e-3 to 1e3
+    h = h.to(hdt)
+    W = torch.randn(N, K, generator=g) * 0.05
+    Wd = W.to(dev)
+    prep = ops.weights_prep(Wd)
+    y, _, _, _ = ops.project_in(h.to(dev), Wd, rms=False, l2=False, w_prep=prep, prefer_prep=True)
+    ref = h.double() @ W.double().t()
+    # per-row relative error (rows have different scales)
+    err = ((y.double().cpu() - ref).abs().amax(1) / ref.abs().amax(1).clamp_min(1e-300)).max().item()
+    assert err < 1e-5, (shape, err)
+    # project_out through the same prepared form of its weight
+    Wo = torch.randn(K, N, generator=g) * 0.05
+    Wod = Wo.to(dev)
+    r = torch.randn(M, N, generator=g)
+    hh = torch.zeros(M, K, dtype=torch.float32)
+    d, _, _ = ops.project_out(r.to(dev), Wod, hh.to(dev), w_prep=ops.weights_prep(Wod) if N % 8 == 0 else None,
+                              prefer_prep=True)
+    ref_o = r.double() @ Wo.double().t()
+    assert rel_err(d, ref_o) < 1e-5, shape
+    _status_clean(dev)
+
+
+def test_injector_f16x3_matches_tf32_path(dev):
+    """The hooked model with the 3xF16 projections (default) and with 3xTF32 (gemm_f16x3 = False) agree with the
+    reference's output; the per-layer CUDA graphs are keyed by the weights' versions, so an in-place weight change
+    is seen by the next step."""
+    from kv_skill_v2_b200 import CAND, LayerSelector, Library, LibraryInjector, ModelInterface
+    c = load_case("hooked")
+    d_m = c["x"].shape[-1]
+    reader = TinyReader(d_m, 10)
+    with torch.no_grad():
+        for i, blk in enumerate(reader.model.layers):
+            blk.weight.copy_(torch.from_numpy(c[f"blk{i}_w"]))
+            blk.bias.copy_(torch.from_numpy(c[f"blk{i}_b"]))
+    reader = reader.to(dev).eval().requires_grad_(False)
+    layers = [int(x) for x in c["layers"]]
+    d_s = c[f"K_{layers[0]}"].shape[-1]
+    chunks = [{"K": {float(r): torch.from_numpy(c[f"K_{li}"][i, :n]) for r, li in zip(CAND, layers)}}
+              for i, n in enumerate(c["n"])]
+    lib = Library(chunks, layers, CAND)
+    itf = ModelInterface(d_m, d_s, layers)
+    with torch.no_grad():
+        itf.A.weight.copy_(torch.from_numpy(c["A_w"]))
+        itf.B.weight.copy_(torch.from_numpy(c["B_w"]))
+        itf.gate_w.copy_(torch.from_numpy(c["gate_w"]))
+        itf.gate_b.copy_(torch.from_numpy(c["gate_b"]))
+        itf.log_gain.copy_(torch.from_numpy(c["log_gain"]))
+    itf = itf.to(dev).requires_grad_(False)
+    x = torch.from_numpy(c["x"]).to(dev)
+    outs = []
+    for f16x3 in (True, False):
+        inj = LibraryInjector(reader, itf, top_k=4)
+        inj.gemm_f16x3 = f16x3
+        inj.load_library(lib)
+        with torch.no_grad():
+            y1 = reader(x)
+            y2 = reader(x)  # replayed from the captured graphs
+        assert rel_err(y1, c["out_sel0"]) < TOL and rel_err(y2, c["out_sel0"]) < TOL
+        outs.append(y2)
+        if f16x3:
+            with torch.no_grad():
+                itf.B.weight.mul_(2.0)   # in place: the next step must use the new weights
+                y3 = reader(x)
+                itf.B.weight.mul_(0.5)
+                y4 = reader(x)
+            assert not torch.allclose(y3, y2, atol=1e-6, rtol=0)  # the doubled write weights took effect
+            assert rel_err(y4, y2) < 1e-5
+        inj.detach()
+    assert rel_err(outs[0], outs[1]) < 1e-5
+    _status_clean(dev)
+
+
 def test_low_rank_query_two_calls(dev):
     from kv_skill_v2_b200 import ops
     g = torch.Generator().manual_seed(8)
@@ -465,4 +547,23 @@ def test_injector_cuda_graph_cache(dev):
     assert not torch.allclose(outs[True][0], outs[True][1])
     assert torch.allclose(again, outs[False][1], rtol=0, atol=1e-6)
     assert not torch.allclose(half, outs[True][0])
+    _status_clean(dev)
+
+
+def test_bounded_wait_gives_up_and_context_stays_usable(dev):
+    """Failure detection without a fault: a wait on an mbarrier phase that nothing completes gives up after its
+    cycle limit, raises XENCB_DEV_TIMEOUT in the status word, and the next read on the same context is correct."""
+    from kv_skill_v2_b200 import ops
+    assert ops.device_status(dev) == 0
+    assert ops.wait_selftest(dev, limit_cycles=2_000_000) == 0
+    st = ops.device_status(dev)
+    assert st & 1, f"status {st}: XENCB_DEV_TIMEOUT expected"
+    assert ops.device_status(dev) == 0  # read-and-clear
+    c = load_case("cfg1_softmax_top2")
+    pages = _pages_from_case(c, dev)
+    q = torch.from_numpy(c["q"]).to(dev).reshape(-1, c["q"].shape[-1])
+    R = q.shape[0]
+    idx, wk, _, _ = ops.route(q, pages.S, rows_per_lib=R, top_k=2, route_temp=float(c["route_temp"]))
+    r = ops.read_decode(q, pages, idx, wk, rows_per_lib=R, read_temp=float(c["read_temp"]))
+    assert rel_err(r, c["r"].reshape(r.shape)) < TOL
     _status_clean(dev)
