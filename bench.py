@@ -978,25 +978,52 @@ def run_ours(args) -> None:
         inj = LibraryInjector(reader, itf, top_k=CFG["top_k"], read_temp=CFG["read_temp"], route_temp=CFG["route_temp"])
         inj.load_library(PagedLibrary({0: pages}))
         h_host = [hs[i].view(docs, CFG["T"], d_m).cpu().pin_memory() for i in range(min(n_h, 64))]
-        out_host = torch.empty(docs, CFG["T"], d_m, dtype=torch.float32).pin_memory()
-        eve = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-        with torch.inference_mode():
-            for i in range(args.warmup):
-                reader(h_host[i % len(h_host)].to(dev, non_blocking=True))
+        out_host = [torch.empty(docs, CFG["T"], d_m, dtype=torch.float32).pin_memory() for _ in range(2)]
+        # a serving loop: host->device copies of the next step's hidden states and device->host copies of the last
+        # step's outputs run on a copy stream while the compute stream runs the hooked reader; two device input
+        # buffers alternate. Timed as one device span from the first upload to the last download.
+        cstream = torch.cuda.Stream(dev)
+        h_dev = [torch.empty(docs, CFG["T"], d_m, dtype=torch.float32, device=dev) for _ in range(2)]
+        h_ready = [torch.cuda.Event() for _ in range(2)]
+        h_free = [torch.cuda.Event() for _ in range(2)]
+        y_done = [torch.cuda.Event() for _ in range(2)]
+        t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+        def serve(n_steps, timed):
+            ys = [None, None]
+            with torch.cuda.stream(cstream):
+                if timed:
+                    t_start.record(cstream)
+                h_dev[0].copy_(h_host[0], non_blocking=True)
+                h_ready[0].record(cstream)
+            for i in range(n_steps):
+                b = i & 1
+                if i + 1 < n_steps:  # upload the next step's input once its buffer is free
+                    with torch.cuda.stream(cstream):
+                        if i >= 1:
+                            cstream.wait_event(h_free[1 - b])
+                        h_dev[1 - b].copy_(h_host[(i + 1) % len(h_host)], non_blocking=True)
+                        h_ready[1 - b].record(cstream)
+                stream.wait_event(h_ready[b])
+                ys[b] = reader(h_dev[b])
+                h_free[b].record(stream)
+                y_done[b].record(stream)
                 inj.mag_terms.clear()
+                with torch.cuda.stream(cstream):  # download this step's output behind the next step's compute
+                    cstream.wait_event(y_done[b])
+                    out_host[b].copy_(ys[b], non_blocking=True)
+                    ys[b].record_stream(cstream)
+            if timed:
+                t_end.record(cstream)
+
+        with torch.inference_mode():
+            serve(args.warmup, False)
             torch.cuda.synchronize(dev)
             t_host = time.perf_counter()
-            for i in range(args.steps):
-                flush.fill_(i & 0xFF)
-                eve[i][0].record(stream)
-                hd = h_host[i % len(h_host)].to(dev, non_blocking=True)
-                y = reader(hd)
-                out_host.copy_(y, non_blocking=True)
-                eve[i][1].record(stream)
-                inj.mag_terms.clear()
+            serve(args.steps, True)
             t_host = time.perf_counter() - t_host
             torch.cuda.synchronize(dev)
-        t_e2e = sum(x.elapsed_time(y) for x, y in eve)
+        t_e2e = t_start.elapsed_time(t_end)
         if world > 1:
             t = torch.tensor([t_e2e], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -1042,7 +1069,9 @@ def run_ours(args) -> None:
                     "host_enqueue_us_per_step": 1e6 * t_host / args.steps,
                     "path": "LibraryInjector forward hook on a reader block (CUDA-graph replay of the fused hook path), "
                             "PagedLibrary of 64 documents; per step an H2D copy of h from pinned memory and a D2H "
-                            "copy of the output on the compute stream, inside per-step events (L2 flushed outside)"},
+                            "copy of the output, on a copy stream overlapping the neighbouring steps' compute "
+                            "(double-buffered); one device-timed span over all steps; no L2 flush (each step "
+                            "streams ~600 MB of slots and weights, above the 126 MB L2)"},
             "gpu_launches": kernels_per_step * args.steps,
             "sharded": sharded,
             "selector": selector,
