@@ -987,6 +987,7 @@ def run_ours(args) -> None:
         h_ready = [torch.cuda.Event() for _ in range(2)]
         h_free = [torch.cuda.Event() for _ in range(2)]
         y_done = [torch.cuda.Event() for _ in range(2)]
+        d2h_done = [torch.cuda.Event() for _ in range(2)]
         t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
         def serve(n_steps, timed):
@@ -1005,6 +1006,8 @@ def run_ours(args) -> None:
                         h_dev[1 - b].copy_(h_host[(i + 1) % len(h_host)], non_blocking=True)
                         h_ready[1 - b].record(cstream)
                 stream.wait_event(h_ready[b])
+                if i >= 2:  # the host consumes step i-2's output before its buffer is reused: at most 2 steps in flight
+                    d2h_done[b].synchronize()
                 ys[b] = reader(h_dev[b])
                 h_free[b].record(stream)
                 y_done[b].record(stream)
@@ -1012,7 +1015,7 @@ def run_ours(args) -> None:
                 with torch.cuda.stream(cstream):  # download this step's output behind the next step's compute
                     cstream.wait_event(y_done[b])
                     out_host[b].copy_(ys[b], non_blocking=True)
-                    ys[b].record_stream(cstream)
+                    d2h_done[b].record(cstream)
             if timed:
                 t_end.record(cstream)
 
@@ -1070,7 +1073,8 @@ def run_ours(args) -> None:
                     "path": "LibraryInjector forward hook on a reader block (CUDA-graph replay of the fused hook path), "
                             "PagedLibrary of 64 documents; per step an H2D copy of h from pinned memory and a D2H "
                             "copy of the output, on a copy stream overlapping the neighbouring steps' compute "
-                            "(double-buffered); one device-timed span over all steps; no L2 flush (each step "
+                            "(double-buffered; the host reads step i-2's output before reusing its buffer); one "
+                            "device-timed span over all steps; no L2 flush (each step "
                             "streams ~600 MB of slots and weights, above the 126 MB L2)"},
             "gpu_launches": kernels_per_step * args.steps,
             "sharded": sharded,

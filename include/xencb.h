@@ -75,9 +75,9 @@ XENCB_API int xencb_device_status(void* stream, int clear, unsigned int* status_
  *            XENCB_PIN_RMS into a float32 [n_rows, rank] buffer, then one with XENCB_PIN_L2 over it.
  *   h        [n_rows, d_m] of h_dtype (the reference upcasts h to float32 first; so does this)
  *   w_in     [d_s, d_m] float32; b_in [d_s] or NULL; d_s % 4 == 0
- *   w_prep   NULL, or w_in prepared by xencb_weights_prep: for n_rows >= 512 (or when w_in is NULL) the GEMM
- *            then runs as 3xF16 on the f16 tensor cores (fp32-faithful, see xencb_weights_prep; needs
- *            d_m % 8 == 0); fewer rows keep the 3xTF32 kernel, which is faster at decode sizes
+ *   w_prep   NULL, or w_in prepared by xencb_weights_prep: the GEMM then runs as 3xF16 on the f16 tensor cores
+ *            (fp32-faithful, see xencb_weights_prep; needs d_m % 8 == 0 and h 16-byte aligned, else the
+ *            3xTF32 / SIMT path runs); w_in may then be NULL
  *   gate_w   [d_m] or NULL (then gate_out is not written); gate_b the scalar gate_b[pos[li]], or gate_b_dev a
  *            device pointer to it (when non-NULL it replaces gate_b: no host read of the parameter, so the call
  *            can be captured in a CUDA graph)

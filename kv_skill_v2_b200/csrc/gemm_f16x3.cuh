@@ -36,7 +36,6 @@ constexpr int H3_STAGE = 2 * H3_WBOX + 2 * H3_XBOX;  // W_hi | W_lo | X_hi | X_l
 constexpr int H3_THREADS = 32 * 6;
 constexpr size_t H3_SMEM = 1024 + (size_t)H3_STAGES * H3_STAGE + 256;
 constexpr uint32_t H3_TMEM_COLS = 64;
-constexpr int64_t H3_MIN_ROWS = 512;  // below this many rows the 3xTF32 kernel is faster (latency-bound GEMMs)
 constexpr int WPREP_HEAD = 256;  // bytes before [W_hi; W_lo] in a prepared weight: float max_bits, float inv_scale
 
 // 2^e with max * 2^e in [2^14, 2^15) (e = 0 for max 0 or non-finite): exact power-of-two scale into f16 range.
@@ -77,32 +76,70 @@ __global__ void __launch_bounds__(256) split_weights_kernel(const float* __restr
   }
 }
 
-// X per call: one CTA per row, [X_hi; X_lo] rows scaled by the row's own power of two, 1 / s_m per row.
+// X per call: one CTA per row, [X_hi; X_lo] rows scaled by the row's own power of two, 1 / s_m per row. The row
+// is read in 8-element pieces kept in registers between the max and the split (K <= 8 * 256 * SR_PIECES).
+constexpr int SR_THREADS = 256;
+constexpr int SR_PIECES = 4;
+
 template <typename T>
-__global__ void __launch_bounds__(256) split_rows_f16x2_kernel(const T* __restrict__ x, int64_t M, int K,
-                                                               __half* __restrict__ hi, __half* __restrict__ lo,
-                                                               float* __restrict__ inv_scale) {
-  __shared__ float red[32];
+__device__ __forceinline__ void load8_f32(const T* p, float* v) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    unpack16<T>(*reinterpret_cast<const uint4*>(p), v);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(SR_THREADS) split_rows_f16x2_kernel(const T* __restrict__ x, int64_t M, int K,
+                                                                      __half* __restrict__ hi, __half* __restrict__ lo,
+                                                                      float* __restrict__ inv_scale) {
+  __shared__ float red[SR_THREADS / 32];
   const int64_t m = blockIdx.x;
   const T* xr = x + m * K;
+  float v[SR_PIECES][8];
   float mx = 0.f;
-  for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(to_f32(xr[k])));
+#pragma unroll
+  for (int p = 0; p < SR_PIECES; ++p) {
+    const int k = (p * SR_THREADS + threadIdx.x) * 8;
+    if (k < K) {
+      load8_f32<T>(xr + k, v[p]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(v[p][e]));
+    }
+  }
+  // pieces beyond SR_PIECES (rows longer than 8 * 256 * SR_PIECES): the max over a second read
+  for (int k = (SR_PIECES * SR_THREADS + threadIdx.x) * 8; k < K; k += SR_THREADS * 8) {
+    float w[8];
+    load8_f32<T>(xr + k, w);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) mx = fmaxf(mx, fabsf(w[e]));
+  }
   mx = warp_max(mx);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
   __syncthreads();
-  if (threadIdx.x < 32) {
-    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-    v = warp_max(v);
-    if (threadIdx.x == 0) red[0] = v;
-  }
-  __syncthreads();
-  const float s = f16_range_scale(red[0]);
+  float rm = 0.f;
+#pragma unroll
+  for (int w = 0; w < SR_THREADS / 32; ++w) rm = fmaxf(rm, red[w]);
+  const float s = f16_range_scale(rm);
   if (threadIdx.x == 0) inv_scale[m] = 1.f / s;
-  for (int k = threadIdx.x; k < K; k += blockDim.x) {
-    __half h, l;
-    split_f16<float>(to_f32(xr[k]) * s, h, l);
-    hi[m * K + k] = h;
-    lo[m * K + k] = l;
+  auto emit = [&](int k, const float* w) {
+    alignas(16) __half h[8], l[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) split_f16<float>(w[e] * s, h[e], l[e]);
+    *reinterpret_cast<uint4*>(hi + m * K + k) = *reinterpret_cast<const uint4*>(h);
+    *reinterpret_cast<uint4*>(lo + m * K + k) = *reinterpret_cast<const uint4*>(l);
+  };
+#pragma unroll
+  for (int p = 0; p < SR_PIECES; ++p) {
+    const int k = (p * SR_THREADS + threadIdx.x) * 8;
+    if (k < K) emit(k, v[p]);
+  }
+  for (int k = (SR_PIECES * SR_THREADS + threadIdx.x) * 8; k < K; k += SR_THREADS * 8) {
+    float w[8];
+    load8_f32<T>(xr + k, w);
+    emit(k, w);
   }
 }
 

@@ -156,20 +156,22 @@ GemmPlan plan_gemm_simt(int64_t M, int N, int K, int sms) {
   return p;
 }
 
-// Workspace of a projection GEMM: the split partials, then (tensor-core paths) the X staging: float32 X for the
-// 3xTF32 kernel, or [X_hi; X_lo] f16 (the same bytes) plus one float per row for the 3xF16 kernel.
+// Workspace of a projection GEMM: the split partials of whichever kernel runs (the largest of the plans), then
+// (tensor-core paths) the X staging: float32 X for the 3xTF32 kernel, or [X_hi; X_lo] f16 (the same bytes)
+// plus one float per row for the 3xF16 kernels.
+size_t gemm_part_bytes(int64_t M, int N, int K, int sms) {
+  size_t b = plan_gemm_simt(M, N, K, sms).part_bytes;
+  if (K % 4 == 0) b = std::max(b, plan_gemm_tc(M, N, K, sms).part_bytes);
+  return b;
+}
+
 size_t gemm_xstage_bytes(int64_t M, int K) {
   return align_up((size_t)M * K * sizeof(float), 256) + align_up((size_t)M * sizeof(float), 256);
 }
 
 size_t gemm_ws_bytes(int64_t M, int N, int K, int sms, bool convert_x) {
   (void)convert_x;
-  size_t b = plan_gemm_simt(M, N, K, sms).part_bytes;
-  if (K % 4 == 0) {
-    size_t t = plan_gemm_tc(M, N, K, sms).part_bytes + gemm_xstage_bytes(M, K);
-    if (t > b) b = t;
-  }
-  return b;
+  return gemm_part_bytes(M, N, K, sms) + (K % 4 == 0 ? gemm_xstage_bytes(M, K) : 0);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
@@ -216,17 +218,16 @@ int tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dt, uint32_t esize, cons
 template <typename TX>
 int launch_gemm(const void* X, int64_t M, int K, const float* W, int N, int sms, float* part, float* xbuf,
                 int* row_done, cudaStream_t st, GemmPlan* used, const void* w_prep = nullptr) {
-  // 3xF16 (weights split once by xencb_weights_prep, X split here with a power-of-two scale per row) pays off
-  // when the GEMM is throughput-bound: many rows. At decode sizes the split-K CTAs each see a few k-blocks, the
-  // GEMM is latency-bound and the extra row-split launch costs more than the halved MMA count saves, so the
-  // 3xTF32 kernel runs unless W itself was not given.
-  const bool f16x3 = w_prep && (W == nullptr || M >= H3_MIN_ROWS);
-  if (f16x3 && K % 8 == 0 && aligned(w_prep, 256) && xbuf && M <= INT32_MAX / 2 && N <= INT32_MAX / 2) {
+  // 3xF16 (weights split once by xencb_weights_prep, X split here with a power-of-two scale per row) whenever the
+  // prepared weights are given: half the MMAs of 3xTF32, and no per-k-block split of W
+  const bool f16x3 = w_prep != nullptr;
+  if (f16x3 && K % 8 == 0 && aligned(w_prep, 256) && aligned(X, 16) && xbuf && M <= INT32_MAX / 2 &&
+      N <= INT32_MAX / 2) {
     const GemmPlan p = plan_gemm_tc(M, N, K, sms);
     __half* xs = reinterpret_cast<__half*>(xbuf);  // [X_hi; X_lo]: 2 M K halves = M K floats of staging
     float* x_inv = reinterpret_cast<float*>(reinterpret_cast<char*>(xbuf) + align_up((size_t)M * K * sizeof(float), 256));
-    split_rows_f16x2_kernel<TX><<<(unsigned)M, 256, 0, st>>>(static_cast<const TX*>(X), M, K, xs, xs + M * (int64_t)K,
-                                                            x_inv);
+    split_rows_f16x2_kernel<TX><<<(unsigned)M, SR_THREADS, 0, st>>>(static_cast<const TX*>(X), M, K, xs,
+                                                                   xs + M * (int64_t)K, x_inv);
     XENCB_CHECK_LAUNCH("split_rows_f16x2 launch");
     const char* wp = static_cast<const char*>(w_prep);
     CUtensorMap mw, mx;
@@ -620,8 +621,7 @@ int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const 
   float* nq_part = reinterpret_cast<float*>(ws + g_bytes);
   int* row_done = reinterpret_cast<int*>(ws + g_bytes + nq_bytes);
   // X staging for the tensor-core paths sits after the tensor-core partials
-  float* xbuf = (d_m % 4 == 0) ? reinterpret_cast<float*>(ws + plan_gemm_tc(n_rows, d_s, d_m, di.sms).part_bytes)
-                               : nullptr;
+  float* xbuf = (d_m % 4 == 0) ? reinterpret_cast<float*>(ws + gemm_part_bytes(n_rows, d_s, d_m, di.sms)) : nullptr;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   GemmPlan gp;
   switch (h_dtype) {
@@ -1045,8 +1045,7 @@ int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_ou
   float* cn_part = norm_part + (size_t)n_rows * nch * 2;
   int* row_done = reinterpret_cast<int*>(ws + g_bytes + d_bytes + np_bytes);
   GemmPlan gp;
-  float* xbuf = (d_s % 4 == 0) ? reinterpret_cast<float*>(ws + plan_gemm_tc(n_rows, d_m, d_s, di.sms).part_bytes)
-                               : nullptr;
+  float* xbuf = (d_s % 4 == 0) ? reinterpret_cast<float*>(ws + gemm_part_bytes(n_rows, d_m, d_s, di.sms)) : nullptr;
   rc = launch_gemm<float>(r, n_rows, d_s, w_out, d_m, di.sms, part, w_prep ? xbuf : nullptr, nullptr, st, &gp, w_prep);
   if (rc) return rc;
   const float alpha = expf(log_alpha);

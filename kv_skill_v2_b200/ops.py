@@ -120,8 +120,8 @@ def project_in(h2: torch.Tensor, w_in: torch.Tensor, b_in=None, *, rms: bool = T
 
     q = L2((rms_norm(h2) if rms else h2) @ w_in^T + b_in) (L2 only if l2); w_in is [d_s, d_m] (nn.Linear).
     gate_b: a number, or a one-element device tensor read by the kernel. w_prep: weights_prep(w_in), to run the
-    GEMM as 3xF16 on the f16 tensor cores (same accuracy, twice the rate of 3xTF32) for 512 rows or more;
-    prefer_prep=True uses it at any row count (w_in then only gives the shape)."""
+    GEMM as 3xF16 on the f16 tensor cores (same accuracy as 3xTF32, half its MMAs); prefer_prep=True passes only
+    the prepared form (w_in then only gives the shape)."""
     dev = _cuda("project_in", h2, w_in, b_in, gate_w, sel_w, sel_b)
     h2 = h2.contiguous()
     w_in = _f32(w_in, "w_in")
