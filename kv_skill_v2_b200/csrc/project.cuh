@@ -158,6 +158,45 @@ __device__ __forceinline__ float4 sum_splits4(const float* __restrict__ part, in
   return v;
 }
 
+// Split sums of VPT float4 column groups (columns n[v], v < VPT; ok[v] false for none) with 16 / VPT splits'
+// loads of each in flight, added in split order: the same sums as sum_splits4.
+template <int VPT>
+__device__ __forceinline__ void sum_splits_row(const float* __restrict__ part, int splits, int64_t M, int N,
+                                               int64_t row, const int* n, const bool* ok, float4* v) {
+  constexpr int SB = 16 / VPT;
+  const int64_t zs = M * N;
+#pragma unroll
+  for (int q = 0; q < VPT; ++q) v[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int z0 = 0; z0 < splits; z0 += SB) {
+    float4 t[VPT][SB];
+#pragma unroll
+    for (int q = 0; q < VPT; ++q)
+#pragma unroll
+      for (int u = 0; u < SB; ++u)
+        if (ok[q] && z0 + u < splits)
+          t[q][u] = *reinterpret_cast<const float4*>(part + row * N + n[q] + (int64_t)(z0 + u) * zs);
+#pragma unroll
+    for (int q = 0; q < VPT; ++q)
+#pragma unroll
+      for (int u = 0; u < SB; ++u)
+        if (ok[q] && z0 + u < splits) {
+          v[q].x += t[q][u].x; v[q].y += t[q][u].y; v[q].z += t[q][u].z; v[q].w += t[q][u].w;
+        }
+  }
+}
+
+// Two block-wide sums in one pass (blockDim.x <= 1024); `red2` holds 32 float2.
+__device__ __forceinline__ float2 block_sum2(float a, float b, float2* red2) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  a = warp_sum(a);
+  b = warp_sum(b);
+  __syncthreads();
+  if (lane == 0) red2[wid] = make_float2(a, b);
+  __syncthreads();
+  const float2 t = lane < nw ? red2[lane] : make_float2(0.f, 0.f);
+  return make_float2(warp_sum(t.x), warp_sum(t.y));
+}
+
 // Row passes with 16-byte loads, four in flight per thread: sum of x^2, and sum of x*w for up to two vectors.
 template <typename TH>
 __device__ __forceinline__ void row_dots(const TH* __restrict__ hr, int d, const float* __restrict__ w1,
@@ -274,6 +313,80 @@ __global__ void __launch_bounds__(256) project_in_reduce_kernel(
   }
 }
 
+// project_in after the GEMM in one launch when a row fits one CTA (d_s <= 4 * ROW_THREADS * VPT): thread t owns
+// the float4 column groups t + v * blockDim.x. Its split partials are requested first, then the pass over h (sum
+// of squares, gate dot); one two-value block sum gives 1/rms and the gate; q = (sum of splits) * rstd + b stays in
+// registers for the L2 norm (||q|| + 1e-6, xenc/injector.py:58), so nothing is written twice. The selector
+// logits (chunk 0's job in project_in_reduce_kernel) are the same warp dots.
+constexpr int ROW_THREADS = 512;
+template <typename TH, int VPT>
+__global__ void __launch_bounds__(ROW_THREADS) project_in_row_kernel(
+    const TH* __restrict__ h, int d_m, const float* __restrict__ part, int splits, int64_t M, int d_s, int flags,
+    const float* __restrict__ b_in, const float* __restrict__ gate_w, float gate_b, const float* __restrict__ gate_b_dev,
+    const float* __restrict__ sel_w, const float* __restrict__ sel_b, int n_cand, float eps,
+    float* __restrict__ q_out, float* __restrict__ gate_out, float* __restrict__ rstd_out, float* __restrict__ z_out) {
+  __shared__ float2 red2[32];
+  __shared__ float red[32];
+  __shared__ float zsh[32];
+  const int64_t row = blockIdx.x;
+  const TH* hr = h + row * d_m;
+  int n[VPT];
+  bool ok[VPT];
+#pragma unroll
+  for (int q = 0; q < VPT; ++q) {
+    n[q] = (threadIdx.x + q * blockDim.x) * 4;
+    ok[q] = n[q] < d_s;
+  }
+  float4 v[VPT];
+  sum_splits_row<VPT>(part, splits, M, d_s, row, n, ok, v);
+  float ss, gd, unused;
+  row_dots<TH>(hr, d_m, gate_w, nullptr, ss, gd, unused);
+  const float2 t = block_sum2(ss, gd, red2);
+  const float rstd = (flags & XENCB_PIN_RMS) ? rsqrtf(t.x / (float)d_m + eps) : 1.f;
+  if (threadIdx.x == 0) {
+    if (rstd_out) rstd_out[row] = rstd;
+    if (gate_w) {
+      const float gb = gate_b_dev ? __ldg(gate_b_dev) : gate_b;
+      gate_out[row] = 1.f / (1.f + expf(-(t.y * rstd + gb)));
+    }
+  }
+  if (sel_w) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int c = wid; c < n_cand; c += nw) {
+      const float* u = sel_w + (int64_t)c * d_m;
+      float d = 0.f;
+      for (int i = lane; i < d_m; i += 32) d = fmaf(to_f32(hr[i]), u[i], d);
+      d = warp_sum(d);
+      if (lane == 0) zsh[c] = d * rstd + (sel_b ? sel_b[c] : 0.f);
+    }
+    __syncthreads();
+    if (threadIdx.x < n_cand) z_out[row * n_cand + threadIdx.x] = zsh[threadIdx.x];
+  }
+  float4 o[VPT];
+  float nq = 0.f;
+#pragma unroll
+  for (int q = 0; q < VPT; ++q) {
+    o[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (ok[q]) {
+      const int c = n[q];
+      o[q].x = v[q].x * rstd + (b_in ? b_in[c] : 0.f);
+      o[q].y = v[q].y * rstd + (b_in ? b_in[c + 1] : 0.f);
+      o[q].z = v[q].z * rstd + (b_in ? b_in[c + 2] : 0.f);
+      o[q].w = v[q].w * rstd + (b_in ? b_in[c + 3] : 0.f);
+      nq += o[q].x * o[q].x + o[q].y * o[q].y + o[q].z * o[q].z + o[q].w * o[q].w;
+    }
+  }
+  if (flags & XENCB_PIN_L2) {
+    nq = block_sum(nq, red);
+    const float den = sqrtf(nq) + 1e-6f;
+#pragma unroll
+    for (int q = 0; q < VPT; ++q) { o[q].x /= den; o[q].y /= den; o[q].z /= den; o[q].w /= den; }
+  }
+#pragma unroll
+  for (int q = 0; q < VPT; ++q)
+    if (ok[q]) *reinterpret_cast<float4*>(q_out + row * d_s + n[q]) = o[q];
+}
+
 // X as float32 rows for the TMA path (hidden states stored in 16-bit types).
 template <typename TH>
 __global__ void __launch_bounds__(256) to_f32_kernel(const TH* __restrict__ x, int64_t n, float* __restrict__ y) {
@@ -384,6 +497,77 @@ __global__ void __launch_bounds__(256) project_out_epilogue_kernel(
     for (int c = 0; c < n_chunks; ++c) tot += __ldcg(cn_part + row * n_chunks + c);
     rel_out[row] = sqrtf(tot) / (hnorm + 1e-6f);
   }
+}
+
+// project_out after the GEMM in one launch when a row fits one CTA (d_m <= 4 * ROW_THREADS * VPT): thread t owns
+// the float4 column groups t + v * blockDim.x. d = scale * gate * (sum of splits + bias) stays in registers; one
+// two-value block sum gives ||d|| and ||h||, then the epilogue of project_out_epilogue_kernel (the selector's
+// matched norm, the position mask, the cast to h's dtype, h + delta) and, when asked, the block sum of the cast
+// delta's squares for the mag term. h_out may alias h: every thread reads its own columns of h before the block
+// sum and writes them after.
+template <typename TH, int VPT>
+__global__ void __launch_bounds__(ROW_THREADS) project_out_row_kernel(
+    const float* __restrict__ part, int splits, int64_t M, int d_m, const float* __restrict__ b_out, float scale,
+    const float* __restrict__ log_scale_dev, const float* __restrict__ gate, const TH* h,
+    const float* __restrict__ sel_w, float alpha_host, const float* __restrict__ log_alpha_dev,
+    const float* __restrict__ pos_mask, TH* delta_out, TH* h_out, float* __restrict__ rel_out) {
+  __shared__ float2 red2[32];
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  int n[VPT];
+  bool ok[VPT];
+#pragma unroll
+  for (int q = 0; q < VPT; ++q) {
+    n[q] = (threadIdx.x + q * blockDim.x) * 4;
+    ok[q] = n[q] < d_m;
+  }
+  float4 v[VPT];
+  sum_splits_row<VPT>(part, splits, M, d_m, row, n, ok, v);
+  float hx[VPT][4];
+#pragma unroll
+  for (int q = 0; q < VPT; ++q)
+#pragma unroll
+    for (int u = 0; u < 4; ++u) hx[q][u] = ok[q] ? to_f32(h[row * d_m + n[q] + u]) : 0.f;
+  const float g = (gate ? gate[row] : 1.f) * scale * (log_scale_dev ? expf(__ldg(log_scale_dev)) : 1.f);
+  float o[VPT][4];
+  float dd = 0.f, hh = 0.f;
+#pragma unroll
+  for (int q = 0; q < VPT; ++q) {
+    const int c = n[q];
+    o[q][0] = ok[q] ? g * (v[q].x + (b_out ? b_out[c] : 0.f)) : 0.f;
+    o[q][1] = ok[q] ? g * (v[q].y + (b_out ? b_out[c + 1] : 0.f)) : 0.f;
+    o[q][2] = ok[q] ? g * (v[q].z + (b_out ? b_out[c + 2] : 0.f)) : 0.f;
+    o[q][3] = ok[q] ? g * (v[q].w + (b_out ? b_out[c + 3] : 0.f)) : 0.f;
+    dd += o[q][0] * o[q][0] + o[q][1] * o[q][1] + o[q][2] * o[q][2] + o[q][3] * o[q][3];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) hh = fmaf(hx[q][u], hx[q][u], hh);
+  }
+  const float2 t = block_sum2(dd, hh, red2);
+  const float hnorm = sqrtf(t.y);
+  // LayerSelector.apply: d / (||d|| / (||h|| + eps) + eps) * exp(log_alpha), then * w[..., pos]
+  const float rel_d = sqrtf(t.x) / (hnorm + 1e-6f) + 1e-6f;
+  const float sw = sel_w ? sel_w[row] : 1.f;
+  const float pm = pos_mask ? pos_mask[row] : 1.f;
+  const float alpha = log_alpha_dev ? expf(__ldg(log_alpha_dev)) : alpha_host;
+  float cn = 0.f;
+#pragma unroll
+  for (int q = 0; q < VPT; ++q) {
+    if (!ok[q]) continue;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float x = o[q][u];
+      if (sel_w) x = sw * ((x / rel_d) * alpha);
+      if (pos_mask) x *= pm;
+      const TH dv = from_f32<TH>(x);
+      const float dvf = to_f32(dv);
+      cn = fmaf(dvf, dvf, cn);
+      if (delta_out) delta_out[row * d_m + n[q] + u] = dv;
+      if (h_out) h_out[row * d_m + n[q] + u] = from_f32<TH>(hx[q][u] + dvf);
+    }
+  }
+  if (!rel_out) return;
+  cn = block_sum(cn, red);
+  if (threadIdx.x == 0) rel_out[row] = sqrtf(cn) / (hnorm + 1e-6f);
 }
 
 // LayerSelector.apply on a given delta: one CTA per row (norms of delta and h, then the rescale).

@@ -312,28 +312,47 @@ __global__ void __launch_bounds__(512, 1) read_decode_kernel(const ReadArgs a) {
 }
 
 // r[row] = sum_j w_j * read_j; grid (n_rows, ceil(d_s / 512)), 128 threads x 4 columns.
-// Per batch of routed chunks, one thread per chunk turns its splits' (m, l) into merge coefficients in shared
-// memory (log-sum-exp within the chunk, routing weight, 1/l or 1/sqrt(n)); then every thread issues the
-// partial loads of its 4 columns independently of each other.
-constexpr int MERGE_THREADS = 128, MERGE_ENTRIES = 256;
+// Entries of a row are its (chunk j, split s) items in that order, merged in batches of MERGE_ENTRIES. Each thread
+// requests the partial vectors of its 4 columns for the batch's first MERGE_VEC entries at once, before the
+// coefficients are known; meanwhile the batch's (m, l) pairs go to shared memory and one thread per chunk turns
+// them into coefficients (log-sum-exp over the chunk's live splits, the routing weight, 1/l or 1/sqrt(n); 0 for an
+// entry that takes no part, whose vector is never used). The sum runs in entry order, so it is deterministic.
+constexpr int MERGE_THREADS = 128, MERGE_ENTRIES = 128, MERGE_VEC = 16;
+
+__device__ __forceinline__ void fma4(float c, const float4& v, float4& r) {
+  r.x = fmaf(c, v.x, r.x); r.y = fmaf(c, v.y, r.y); r.z = fmaf(c, v.z, r.z); r.w = fmaf(c, v.w, r.w);
+}
 
 template <bool SOFTMAX>
 __global__ void __launch_bounds__(MERGE_THREADS) read_merge_kernel(const ReadArgs a, float* __restrict__ r_out) {
+  __shared__ float ml[2 * MERGE_ENTRIES];
   __shared__ float coef[MERGE_ENTRIES];
-  __shared__ long long item_of[MERGE_ENTRIES];
-  __shared__ int n_entries, nan_flag;
+  __shared__ int nan_flag;
+  const int tid = threadIdx.x;
   const int64_t row = blockIdx.x;
-  const int col = (blockIdx.y * blockDim.x + threadIdx.x) * 4;
+  const int col = (blockIdx.y * blockDim.x + tid) * 4;
   const bool colok = col < a.d_s;
-  const int jb_step = max(1, MERGE_ENTRIES / a.n_split);  // chunks per batch
+  const int ns = a.n_split;
+  const int jb_step = max(1, MERGE_ENTRIES / ns);  // chunks per batch
+  const int64_t row_item0 = row * (int64_t)a.k * ns;
   float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (threadIdx.x == 0) nan_flag = 0;
+  if (tid == 0) nan_flag = 0;
   for (int jb = 0; jb < a.k; jb += jb_step) {
-    if (threadIdx.x == 0) n_entries = 0;
+    const int nj = min(jb_step, a.k - jb), ne = nj * ns;
+    const int64_t e0 = row_item0 + (int64_t)jb * ns;
+    const float* pa = a.part_acc + e0 * a.d_s + col;
+    float4 v[MERGE_VEC];
+    if (colok) {
+#pragma unroll
+      for (int u = 0; u < MERGE_VEC; ++u)
+        if (u < ne) v[u] = __ldcg(reinterpret_cast<const float4*>(pa + (int64_t)u * a.d_s));
+    }
+    for (int e = tid; e < 2 * ne; e += blockDim.x) ml[e] = a.part_ml[e0 * 2 + e];
     __syncthreads();
-    for (int jj = threadIdx.x; jj < jb_step && jb + jj < a.k; jj += blockDim.x) {
-      const int j = jb + jj;
-      const int64_t pair = row * a.k + j;
+    for (int jj = tid; jj < nj; jj += blockDim.x) {
+      float* cf = coef + jj * ns;
+      for (int s = 0; s < ns; ++s) cf[s] = 0.f;
+      const int64_t pair = row * a.k + jb + jj;
       const int32_t c = a.idx[pair];
       const float w = a.wk[pair];
       if (c < 0 || c >= a.n_chunks || w == 0.f) continue;
@@ -342,15 +361,15 @@ __global__ void __launch_bounds__(MERGE_THREADS) read_merge_kernel(const ReadArg
       if (page < 0 || page >= a.n_pages) continue;  // skipped by the read (flagged there)
       int nv = a.n_valid[lc];
       nv = nv > a.page_rows ? a.page_rows : (nv < 0 ? 0 : nv);
-      const int n_live = min(a.n_split, (nv + a.split_rows - 1) / a.split_rows);  // splits holding rows
-      const int64_t item0 = pair * a.n_split;
+      const int n_live = min(ns, (nv + a.split_rows - 1) / a.split_rows);  // splits holding rows
+      const float* mj = ml + 2 * jj * ns;
       float M = -CUDART_INF_F, L = 0.f;
       if (SOFTMAX) {
         for (int s = 0; s < n_live; ++s)
-          if (a.part_ml[(item0 + s) * 2 + 1] > 0.f) M = fmaxf(M, a.part_ml[(item0 + s) * 2]);
+          if (mj[2 * s + 1] > 0.f) M = fmaxf(M, mj[2 * s]);
         for (int s = 0; s < n_live; ++s) {
-          const float ls = a.part_ml[(item0 + s) * 2 + 1];
-          if (ls > 0.f) L += ls * exp2f(a.part_ml[(item0 + s) * 2] - M);
+          const float ls = mj[2 * s + 1];
+          if (ls > 0.f) L += ls * exp2f(mj[2 * s] - M);
         }
         if (!(L > 0.f)) {  // a routed chunk without a valid slot: the reference's softmax gives NaN
           atomicOr(&nan_flag, 1);
@@ -359,35 +378,30 @@ __global__ void __launch_bounds__(MERGE_THREADS) read_merge_kernel(const ReadArg
       } else {
         L = sqrtf((float)(nv > 1 ? nv : 1));
       }
-      for (int s = 0; s < n_live; ++s) {
-        const float ls = a.part_ml[(item0 + s) * 2 + 1];
-        if (!(ls > 0.f)) continue;
-        const int e = atomicAdd(&n_entries, 1);
-        coef[e] = SOFTMAX ? w * exp2f(a.part_ml[(item0 + s) * 2] - M) / L : w / L;
-        item_of[e] = item0 + s;
-      }
+      for (int s = 0; s < n_live; ++s)
+        if (mj[2 * s + 1] > 0.f) cf[s] = SOFTMAX ? w * exp2f(mj[2 * s] - M) / L : w / L;
     }
     __syncthreads();
-    const int ne = n_entries;
     if (colok) {
-      int e = 0;
-      for (; e + 4 <= ne; e += 4) {
-        float4 v[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          v[u] = *reinterpret_cast<const float4*>(a.part_acc + item_of[e + u] * (int64_t)a.d_s + col);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float cf = coef[e + u];
-          r.x = fmaf(cf, v[u].x, r.x); r.y = fmaf(cf, v[u].y, r.y);
-          r.z = fmaf(cf, v[u].z, r.z); r.w = fmaf(cf, v[u].w, r.w);
+      for (int u = 0; u < MERGE_VEC; ++u) {
+        if (u < ne) {
+          const float cu = coef[u];
+          if (cu != 0.f) fma4(cu, v[u], r);
         }
       }
-      for (; e < ne; ++e) {
-        const float4 v = *reinterpret_cast<const float4*>(a.part_acc + item_of[e] * (int64_t)a.d_s + col);
-        const float cf = coef[e];
-        r.x = fmaf(cf, v.x, r.x); r.y = fmaf(cf, v.y, r.y);
-        r.z = fmaf(cf, v.z, r.z); r.w = fmaf(cf, v.w, r.w);
+      for (int eb = MERGE_VEC; eb < ne; eb += MERGE_VEC) {
+#pragma unroll
+        for (int u = 0; u < MERGE_VEC; ++u)
+          if (eb + u < ne && coef[eb + u] != 0.f)
+            v[u] = __ldcg(reinterpret_cast<const float4*>(pa + (int64_t)(eb + u) * a.d_s));
+#pragma unroll
+        for (int u = 0; u < MERGE_VEC; ++u) {
+          if (eb + u < ne) {
+            const float cu = coef[eb + u];
+            if (cu != 0.f) fma4(cu, v[u], r);
+          }
+        }
       }
     }
     __syncthreads();

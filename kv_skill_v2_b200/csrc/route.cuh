@@ -1,61 +1,116 @@
 // Chunk routing (xenc/injector.py:220-229), LayerSelector weights (xenc/selector.py:59-67) and the
 // Library's summary keys (xenc/library.py:69-74).
 //
-// Routing is two kernels: route_logits (one warp per (row, chunk) dot product, q . S * route_temp, the
-// reference's order: dot first, then the temperature) and route_topk (one warp per row: k rounds of a warp
-// arg-max with ties to the lower chunk index, then the softmax over the kept logits).
+// Routing: the logits q . S * route_temp (the reference's order: dot first, then the temperature), then per row k
+// rounds of a warp arg-max with ties to the lower chunk index and the softmax over the kept logits. Decode (few
+// rows per Library) runs both in route_fused_kernel, an 8-CTA cluster per row gathering the logits in the
+// leader's shared memory; prefill-sized batches run route_logits_tiled_kernel, then route_topk_kernel.
 #pragma once
 
 #include <math_constants.h>
+
+#include <cooperative_groups.h>
 
 #include "common.cuh"
 
 namespace xencb {
 
-__global__ void __launch_bounds__(256) route_logits_kernel(const float* __restrict__ q, int64_t n_rows, int d_s,
-                                                          const float* __restrict__ S, int C,
-                                                          const int32_t* __restrict__ n_chunks_of,
-                                                          int64_t rows_per_lib, float temp,
-                                                          float* __restrict__ logit) {
-  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (gw >= n_rows * C) return;
-  const int64_t row = gw / C;
-  const int c = (int)(gw % C);
-  const int64_t lib = row / rows_per_lib;
-  const int nc = n_chunks_of ? n_chunks_of[lib] : C;
-  if (c >= nc) {
-    if (lane == 0) logit[row * C + c] = -CUDART_INF_F;
-    return;
-  }
-  const float* qr = q + row * d_s;
-  const float* sr = S + (lib * C + c) * (int64_t)d_s;
+namespace cg = cooperative_groups;
+
+// q . S over d_s fp32 columns for one warp (result in every lane); q is normally the caller's shared-memory copy
+// of the row (read by every warp of the CTA), S streams from HBM. Lanes take 16-byte vectors i = lane + 32 j and
+// accumulate j = 0, 4, 8, ... into d, j = 1, 5, ... into d1 and so on, combined as (d + d1) + (d2 + d3), then a
+// xor-shuffle tree. The first loop keeps sixteen S vectors of a lane in flight (8 KB a warp: a d_s = 2048 row in
+// one round trip); the second takes four at a time; both add in that same order, so the value does not depend on
+// how many vectors were in flight.
+__device__ __forceinline__ float route_dot(const float* qr, const float* __restrict__ sr, int d_s,
+                                           int lane) {
   float d = 0.f;
   if ((d_s & 3) == 0) {
-    // four independent 16-byte loads of S in flight per lane per step
     const float4* q4 = reinterpret_cast<const float4*>(qr);
     const float4* s4 = reinterpret_cast<const float4*>(sr);
     const int n4 = d_s >> 2;
     float d1 = 0.f, d2 = 0.f, d3 = 0.f;
     int i = lane;
+    for (; i + 480 < n4; i += 512) {
+      float4 b[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) b[u] = __ldcs(s4 + i + 32 * u);
+#pragma unroll
+      for (int u = 0; u < 16; u += 4) {
+        const float4 a0 = q4[i + 32 * u], a1 = q4[i + 32 * (u + 1)];
+        const float4 a2 = q4[i + 32 * (u + 2)], a3 = q4[i + 32 * (u + 3)];
+        d = fmaf(a0.x, b[u].x, d); d = fmaf(a0.y, b[u].y, d); d = fmaf(a0.z, b[u].z, d); d = fmaf(a0.w, b[u].w, d);
+        d1 = fmaf(a1.x, b[u + 1].x, d1); d1 = fmaf(a1.y, b[u + 1].y, d1);
+        d1 = fmaf(a1.z, b[u + 1].z, d1); d1 = fmaf(a1.w, b[u + 1].w, d1);
+        d2 = fmaf(a2.x, b[u + 2].x, d2); d2 = fmaf(a2.y, b[u + 2].y, d2);
+        d2 = fmaf(a2.z, b[u + 2].z, d2); d2 = fmaf(a2.w, b[u + 2].w, d2);
+        d3 = fmaf(a3.x, b[u + 3].x, d3); d3 = fmaf(a3.y, b[u + 3].y, d3);
+        d3 = fmaf(a3.z, b[u + 3].z, d3); d3 = fmaf(a3.w, b[u + 3].w, d3);
+      }
+    }
     for (; i + 96 < n4; i += 128) {
       const float4 b0 = __ldcs(s4 + i), b1 = __ldcs(s4 + i + 32), b2 = __ldcs(s4 + i + 64), b3 = __ldcs(s4 + i + 96);
-      const float4 a0 = __ldg(q4 + i), a1 = __ldg(q4 + i + 32), a2 = __ldg(q4 + i + 64), a3 = __ldg(q4 + i + 96);
+      const float4 a0 = q4[i], a1 = q4[i + 32], a2 = q4[i + 64], a3 = q4[i + 96];
       d = fmaf(a0.x, b0.x, d); d = fmaf(a0.y, b0.y, d); d = fmaf(a0.z, b0.z, d); d = fmaf(a0.w, b0.w, d);
       d1 = fmaf(a1.x, b1.x, d1); d1 = fmaf(a1.y, b1.y, d1); d1 = fmaf(a1.z, b1.z, d1); d1 = fmaf(a1.w, b1.w, d1);
       d2 = fmaf(a2.x, b2.x, d2); d2 = fmaf(a2.y, b2.y, d2); d2 = fmaf(a2.z, b2.z, d2); d2 = fmaf(a2.w, b2.w, d2);
       d3 = fmaf(a3.x, b3.x, d3); d3 = fmaf(a3.y, b3.y, d3); d3 = fmaf(a3.z, b3.z, d3); d3 = fmaf(a3.w, b3.w, d3);
     }
     for (; i < n4; i += 32) {
-      const float4 a = __ldg(q4 + i), b = __ldcs(s4 + i);
+      const float4 a = q4[i], b = __ldcs(s4 + i);
       d = fmaf(a.x, b.x, d); d = fmaf(a.y, b.y, d); d = fmaf(a.z, b.z, d); d = fmaf(a.w, b.w, d);
     }
     d = (d + d1) + (d2 + d3);
   } else {
-    for (int i = lane; i < d_s; i += 32) d = fmaf(__ldg(qr + i), __ldg(sr + i), d);
+    for (int i = lane; i < d_s; i += 32) d = fmaf(qr[i], __ldg(sr + i), d);
   }
-  d = warp_sum(d);
-  if (lane == 0) logit[row * C + c] = d * temp;
+  return warp_sum(d);
+}
+
+// Routing logits, few rows per Library: CTA (row, RL_CH-chunk block), 8 warps of RL_CH / 8 dot products each. The
+// Ask L2 for a warp's first S row (lane l: 128-byte lines 2l and 2l+1 of up to 8 KB) before the CTA stages q,
+// so the row is on its way while q is copied.
+__device__ __forceinline__ void prefetch_row_l2(const float* sr, int d_s, int lane) {
+  const char* p = reinterpret_cast<const char*>(sr);
+  const int bytes = d_s * 4;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int off = (2 * lane + u) * 128;
+    if (off < bytes) asm volatile("prefetch.global.L2 [%0];" ::"l"(p + off));
+  }
+}
+
+// row's q is staged in shared memory once (STAGE; dynamic smem d_s floats), else read from global memory.
+constexpr int RL_CH = 16;
+template <bool STAGE>
+__global__ void __launch_bounds__(256) route_logits_kernel(const float* __restrict__ q, int64_t n_rows, int d_s,
+                                                          const float* __restrict__ S, int C,
+                                                          const int32_t* __restrict__ n_chunks_of,
+                                                          int64_t rows_per_lib, float temp,
+                                                          float* __restrict__ logit) {
+  extern __shared__ float rl_q[];
+  const int64_t row = blockIdx.x;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* qr = q + row * d_s;
+  const int64_t lib = row / rows_per_lib;
+  const int c_first = blockIdx.y * RL_CH + w;
+  if (c_first < C) prefetch_row_l2(S + (lib * C + c_first) * (int64_t)d_s, d_s, lane);
+  if (STAGE) {
+    for (int i = threadIdx.x; i < d_s; i += blockDim.x) rl_q[i] = qr[i];
+    __syncthreads();
+    qr = rl_q;
+  }
+  const int nc = n_chunks_of ? min(n_chunks_of[lib], C) : C;
+  const int c_end = min(C, (int)(blockIdx.y + 1) * RL_CH);
+  for (int c = blockIdx.y * RL_CH + w; c < c_end; c += 8) {
+    if (c >= nc) {
+      if (lane == 0) logit[row * C + c] = -CUDART_INF_F;
+      continue;
+    }
+    const float d = route_dot(qr, S + (lib * C + c) * (int64_t)d_s, d_s, lane);
+    if (lane == 0) logit[row * C + c] = d * temp;
+  }
 }
 
 // Routing logits for many rows per Library (prefill): one CTA computes a 32-row x 64-chunk tile of
@@ -127,23 +182,15 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i) {
 
 constexpr int TOPK_WARPS = 4;
 
-// One warp per row; dynamic smem: TOPK_WARPS * C floats.
-__global__ void __launch_bounds__(TOPK_WARPS * 32) route_topk_kernel(
-    const float* __restrict__ logit, int64_t n_rows, int C, const int32_t* __restrict__ n_chunks_of,
-    int64_t rows_per_lib, int top_k, int k_out, const float* __restrict__ row_w, int32_t* __restrict__ idx,
-    float* __restrict__ wk, float* __restrict__ w_dense) {
-  extern __shared__ float sv_all[];
-  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * TOPK_WARPS + w;
-  if (row >= n_rows) return;
-  float* v = sv_all + (int64_t)w * C;
-  const int64_t lib = row / rows_per_lib;
-  const int nc = n_chunks_of ? min(n_chunks_of[lib], C) : C;
-  const float* lr = logit + row * C;
+// Top-k and softmax of one row's logits lr[0, C) by one warp; v is the warp's scratch row of C floats. Chunks at
+// or past nc take no part. Sparse (0 < top_k < nc): top_k rounds of a warp arg-max (ties to the lower chunk), the
+// winner retired to -inf, then the softmax over the kept logits. Dense: the softmax over all nc chunks, idx = 0..
+// nc-1. A row whose weight rw is 0 reads nothing (idx -1); w_dense keeps its routing. lr may alias wd: every lane
+// is done reading lr before wd is written.
+__device__ __forceinline__ void topk_row(const float* lr, float* v, int C, int nc, int top_k, int k_out, float rw,
+                                         int32_t* __restrict__ ir, float* __restrict__ wr, float* wd, int lane) {
   for (int c = lane; c < C; c += 32) v[c] = (c < nc) ? lr[c] : -CUDART_INF_F;
   __syncwarp();
-  int32_t* ir = idx + row * k_out;
-  float* wr = wk + row * k_out;
   const bool sparse = top_k > 0 && top_k < nc;
   if (!sparse) {
     float mx = -CUDART_INF_F;
@@ -156,15 +203,17 @@ __global__ void __launch_bounds__(TOPK_WARPS * 32) route_topk_kernel(
       ir[j] = j < nc ? j : -1;
       wr[j] = j < nc ? expf(v[j] - mx) / sum : 0.f;
     }
-    if (w_dense)
-      for (int c = lane; c < C; c += 32) w_dense[row * C + c] = c < nc ? expf(v[c] - mx) / sum : 0.f;
-    if (row_w && row_w[row] == 0.f) {  // a row whose weight is 0 reads nothing; w_dense keeps its routing
+    if (wd)
+      for (int c = lane; c < C; c += 32) wd[c] = c < nc ? expf(v[c] - mx) / sum : 0.f;
+    if (rw == 0.f) {
       __syncwarp();
       for (int j = lane; j < k_out; j += 32) { ir[j] = -1; wr[j] = 0.f; }
     }
     return;
   }
-  // sparse: top_k rounds of arg-max, the winner's slot is then retired to -inf
+  // lane j keeps the winner of round j (rounds 32 and up are read back from ir): no global round trip on the
+  // path of a decode row's handful of rounds
+  int mine = -1;
   for (int t = 0; t < top_k; ++t) {
     float bv = -CUDART_INF_F;
     int bi = 0x7fffffff;
@@ -173,44 +222,116 @@ __global__ void __launch_bounds__(TOPK_WARPS * 32) route_topk_kernel(
       if (x > bv || (x == bv && c < bi)) { bv = x; bi = c; }
     }
     warp_argmax(bv, bi);
+    const int win = bi < nc ? bi : -1;  // -1 only with non-finite logits
+    if (t < 32 && lane == t) mine = win;
     if (lane == 0) {
-      if (bi < nc) {
-        ir[t] = bi;
-        v[bi] = -CUDART_INF_F;
-      } else {
-        ir[t] = -1;  // only reachable with non-finite logits
-      }
+      ir[t] = win;
+      if (win >= 0) v[win] = -CUDART_INF_F;
     }
     __syncwarp();
   }
   for (int j = top_k + lane; j < k_out; j += 32) { ir[j] = -1; wr[j] = 0.f; }
-  __syncwarp();
   // softmax over the kept logits (the first one is the maximum)
   float mx = -CUDART_INF_F;
-  for (int j = lane; j < top_k; j += 32) { const int c = ir[j]; if (c >= 0) mx = fmaxf(mx, lr[c]); }
+  for (int j = lane; j < top_k; j += 32) { const int c = j < 32 ? mine : ir[j]; if (c >= 0) mx = fmaxf(mx, lr[c]); }
   mx = warp_max(mx);
   float sum = 0.f;
-  for (int j = lane; j < top_k; j += 32) { const int c = ir[j]; if (c >= 0) sum += expf(lr[c] - mx); }
+  for (int j = lane; j < top_k; j += 32) { const int c = j < 32 ? mine : ir[j]; if (c >= 0) sum += expf(lr[c] - mx); }
   sum = warp_sum(sum);
+  float w_mine = 0.f;
   for (int j = lane; j < top_k; j += 32) {
-    const int c = ir[j];
-    wr[j] = c >= 0 ? expf(lr[c] - mx) / sum : 0.f;
+    const int c = j < 32 ? mine : ir[j];
+    const float wj = c >= 0 ? expf(lr[c] - mx) / sum : 0.f;
+    wr[j] = wj;
+    if (j < 32) w_mine = wj;
   }
-  if (w_dense) {
-    // w_dense may alias the logit buffer: every lane is done reading lr before it is overwritten, and the
-    // scatter takes the weights from wk
+  if (wd) {
     __syncwarp();
-    for (int c = lane; c < C; c += 32) w_dense[row * C + c] = 0.f;
+    for (int c = lane; c < C; c += 32) wd[c] = 0.f;
     __syncwarp();
     for (int j = lane; j < top_k; j += 32) {
-      const int c = ir[j];
-      if (c >= 0) w_dense[row * C + c] = wr[j];
+      const int c = j < 32 ? mine : ir[j];
+      if (c >= 0) wd[c] = j < 32 ? w_mine : wr[j];
     }
   }
-  if (row_w && row_w[row] == 0.f) {  // a row whose weight is 0 reads nothing; w_dense keeps its routing
+  if (rw == 0.f) {
     __syncwarp();
     for (int j = lane; j < k_out; j += 32) { ir[j] = -1; wr[j] = 0.f; }
   }
+}
+
+// One warp per row; dynamic smem: TOPK_WARPS * C floats.
+__global__ void __launch_bounds__(TOPK_WARPS * 32) route_topk_kernel(
+    const float* __restrict__ logit, int64_t n_rows, int C, const int32_t* __restrict__ n_chunks_of,
+    int64_t rows_per_lib, int top_k, int k_out, const float* __restrict__ row_w, int32_t* __restrict__ idx,
+    float* __restrict__ wk, float* __restrict__ w_dense) {
+  extern __shared__ float sv_all[];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * TOPK_WARPS + w;
+  if (row >= n_rows) return;
+  const int64_t lib = row / rows_per_lib;
+  const int nc = n_chunks_of ? min(n_chunks_of[lib], C) : C;
+  topk_row(logit + row * C, sv_all + (int64_t)w * C, C, nc, top_k, k_out, row_w ? row_w[row] : 1.f,
+           idx + row * k_out, wk + row * k_out, w_dense ? w_dense + row * C : nullptr, lane);
+}
+
+// Decode routing in one launch: a cluster of RF_CL CTAs (RF_CL * 8 warps) takes `rpc` consecutive rows. Its warps
+// share the rpc * C dot products (route_dot, the same sums as route_logits_kernel), and each writes its logit
+// into the leader CTA's shared memory; after the cluster barrier the leader's warp r runs topk_row on row r.
+// Dynamic smem: the rpc q rows (rpc * d_s floats, every CTA), then 2 * rpc * C floats (the logits and the top-k
+// scratch, used in the leader CTA only).
+constexpr int RF_CL = 8;
+__global__ void __cluster_dims__(RF_CL, 1, 1) __launch_bounds__(256) route_fused_kernel(
+    const float* __restrict__ q, int64_t n_rows, int d_s, const float* __restrict__ S, int C,
+    const int32_t* __restrict__ n_chunks_of, int64_t rows_per_lib, float temp, int rpc, int top_k, int k_out,
+    const float* __restrict__ row_w, int32_t* __restrict__ idx, float* __restrict__ wk, float* __restrict__ w_dense,
+    float* __restrict__ logit_out) {
+  extern __shared__ float rf_sh[];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row0 = (int64_t)(blockIdx.x / RF_CL) * rpc;
+  float* lg_sh = rf_sh + (int64_t)rpc * d_s;  // after the staged q rows: logits, then the top-k scratch
+  float* lead = cluster.map_shared_rank(lg_sh, 0);
+  // The leader's shared memory may be written only once every CTA of the cluster runs: arrive now, wait after the
+  // first dot product (its loads are in flight meanwhile).
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+  {
+    const int t0 = rank * 8 + w, r0 = t0 / C;
+    if (t0 < rpc * C && row0 + r0 < n_rows)
+      prefetch_row_l2(S + ((row0 + r0) / rows_per_lib * C + (t0 - r0 * C)) * (int64_t)d_s, d_s, lane);
+    const int64_t n_q = (min(n_rows, row0 + rpc) - row0) * (int64_t)d_s;
+    for (int64_t i = threadIdx.x; i < n_q; i += blockDim.x) rf_sh[i] = q[row0 * d_s + i];
+    __syncthreads();
+  }
+  bool started = false;
+  const int n_dots = rpc * C;
+  for (int t = rank * 8 + w; t < n_dots; t += RF_CL * 8) {
+    const int r = t / C, c = t - r * C;
+    const int64_t row = row0 + r;
+    if (row >= n_rows) break;  // t only grows, and so does its row
+    const int64_t lib = row / rows_per_lib;
+    const int nc = n_chunks_of ? min(n_chunks_of[lib], C) : C;
+    float l = -CUDART_INF_F;
+    if (c < nc) l = route_dot(rf_sh + (int64_t)r * d_s, S + (lib * C + c) * (int64_t)d_s, d_s, lane) * temp;
+    if (!started) {
+      asm volatile("barrier.cluster.wait;" ::: "memory");
+      started = true;
+    }
+    if (lane == 0) {
+      lead[t] = l;
+      if (logit_out) logit_out[row * C + c] = l;
+    }
+  }
+  if (!started) asm volatile("barrier.cluster.wait;" ::: "memory");
+  cluster.sync();  // every logit is in the leader's shared memory
+  if (rank != 0 || w >= rpc) return;
+  const int64_t row = row0 + w;
+  if (row >= n_rows) return;
+  const int64_t lib = row / rows_per_lib;
+  const int nc = n_chunks_of ? min(n_chunks_of[lib], C) : C;
+  topk_row(lg_sh + (int64_t)w * C, lg_sh + (int64_t)(rpc + w) * C, C, nc, top_k, k_out, row_w ? row_w[row] : 1.f,
+           idx + row * k_out, wk + row * k_out, w_dense ? w_dense + row * C : nullptr, lane);
 }
 
 // Dense routing of a chunk shard, left unnormalised so that shards combine exactly: one warp per row turns the

@@ -358,7 +358,8 @@ int plan_read(int64_t n_rows, int k, int d_s, int page_rows, int dtype, ReadPlan
   // row splits: pick the count with the smallest modelled makespan on one CTA per SM
   const int64_t pairs = n_rows * k;
   const int grid_max = di.sms;
-  const int max_split = page_rows > 64 ? (page_rows + 63) / 64 : 1;
+  // (at most MERGE_ENTRIES splits: the merge keeps one chunk's coefficients in one batch)
+  const int max_split = std::min(page_rows > 64 ? (page_rows + 63) / 64 : 1, MERGE_ENTRIES);
   double best = 1e300;
   int best_n = 1, best_rows = page_rows;
   for (int n = 1; n <= max_split; ++n) {
@@ -509,8 +510,17 @@ rc_t launch_route_logits(const float* q, int64_t n_rows, int d_s, const float* S
     XENCB_CHECK_LAUNCH("route_logits_tiled launch");
     return XENCB_OK;
   }
-  const int64_t blocks = (n_rows * C + 7) / 8;
-  route_logits_kernel<<<(unsigned)blocks, 256, 0, st>>>(q, n_rows, d_s, S, C, n_chunks_of, rows_per_lib, temp, logit);
+  if (n_rows > INT32_MAX || (C + RL_CH - 1) / RL_CH > 65535)
+    return fail(XENCB_EINVAL, "route: %lld rows x %d chunks exceed the launch grid", (long long)n_rows, C);
+  const dim3 grid((unsigned)n_rows, (unsigned)((C + RL_CH - 1) / RL_CH));
+  const size_t qsmem = (size_t)d_s * sizeof(float);
+  if (qsmem <= 96 * 1024) {
+    int rc = ensure_smem(route_logits_kernel<true>, (int)std::max<size_t>(qsmem, 48 * 1024));
+    if (rc) return rc;
+    route_logits_kernel<true><<<grid, 256, qsmem, st>>>(q, n_rows, d_s, S, C, n_chunks_of, rows_per_lib, temp, logit);
+  } else {
+    route_logits_kernel<false><<<grid, 256, 0, st>>>(q, n_rows, d_s, S, C, n_chunks_of, rows_per_lib, temp, logit);
+  }
   XENCB_CHECK_LAUNCH("route_logits launch");
   return XENCB_OK;
 }
@@ -637,6 +647,31 @@ int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const 
       break;
   }
   if (rc) return rc;
+  if (d_s <= 8 * ROW_THREADS) {  // one CTA per row: the reduce, 1/rms, bias and L2 norm in registers
+    const int vpt = d_s <= 4 * ROW_THREADS ? 1 : 2;
+    const unsigned thr = (unsigned)std::min<int>(ROW_THREADS, (d_s / 4 + 31) / 32 * 32);
+    auto launch = [&](auto kern, const auto* hp) {
+      kern<<<(unsigned)n_rows, thr, 0, st>>>(hp, d_m, part, gp.splits, n_rows, d_s, flags, b_in, gate_w, gate_b,
+                                             gate_b_dev, sel_w, sel_b, n_cand, rms_eps, q_out, gate_out, rstd_out,
+                                             z_out);
+    };
+    switch (h_dtype) {
+      case XENCB_F32:
+        if (vpt == 1) launch(project_in_row_kernel<float, 1>, static_cast<const float*>(h));
+        else launch(project_in_row_kernel<float, 2>, static_cast<const float*>(h));
+        break;
+      case XENCB_F16:
+        if (vpt == 1) launch(project_in_row_kernel<__half, 1>, static_cast<const __half*>(h));
+        else launch(project_in_row_kernel<__half, 2>, static_cast<const __half*>(h));
+        break;
+      default:
+        if (vpt == 1) launch(project_in_row_kernel<__nv_bfloat16, 1>, static_cast<const __nv_bfloat16*>(h));
+        else launch(project_in_row_kernel<__nv_bfloat16, 2>, static_cast<const __nv_bfloat16*>(h));
+        break;
+    }
+    XENCB_CHECK_LAUNCH("project_in row launch");
+    return XENCB_OK;
+  }
 #define XENCB_PIN(T)                                                                                         \
   project_in_reduce_kernel<T><<<dim3((unsigned)n_rows, nch), 256, 0, st>>>(                                   \
       static_cast<const T*>(h), d_m, part, gp.splits, n_rows, d_s, flags, b_in, gate_w, gate_b, gate_b_dev,      \
@@ -685,6 +720,21 @@ int xencb_route(const float* q, int64_t n_rows, int d_s, const float* S, int n_c
   if ((size_t)n_chunks * 4 * TOPK_WARPS > 200 * 1024)
     return fail(XENCB_ENOTSUP, "route: C=%d chunks exceed the router's shared-memory row buffer", n_chunks);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int k_out = xencb_route_k(top_k, n_chunks);
+  // decode (few rows per Library, up to 128 chunks: at most two dot products per warp): one launch, a cluster of
+  // 64 warps per row (per 64 / C rows when C < 64)
+  const int rpc = std::max(1, std::min(8, 64 / n_chunks));
+  const size_t fsmem = (size_t)rpc * (d_s + 2 * (size_t)n_chunks) * sizeof(float);
+  const int64_t n_clusters = (n_rows + rpc - 1) / rpc;
+  if (rows_per_lib < 64 && n_chunks <= 128 && fsmem <= 96 * 1024 && n_clusters * RF_CL <= INT32_MAX) {
+    int rc = ensure_smem(route_fused_kernel, (int)std::max<size_t>(fsmem, 48 * 1024));
+    if (rc) return rc;
+    route_fused_kernel<<<(unsigned)(n_clusters * RF_CL), 256, fsmem, st>>>(
+        q, n_rows, d_s, S, n_chunks, n_chunks_of, rows_per_lib, route_temp, rpc, top_k, k_out, row_w, idx, wk,
+        w_dense, logit_out);
+    XENCB_CHECK_LAUNCH("route_fused launch");
+    return XENCB_OK;
+  }
   // logits go to logit_out when given, else to w_dense, which the top-k pass then overwrites row by row
   float* lg = logit_out ? logit_out : w_dense;
   if (!lg) return fail(XENCB_EINVAL, "route: one of w_dense / logit_out must be given (logit buffer)");
@@ -693,7 +743,6 @@ int xencb_route(const float* q, int64_t n_rows, int d_s, const float* S, int n_c
   const int smem = n_chunks * 4 * TOPK_WARPS;
   int rc = ensure_smem(route_topk_kernel, smem > 48 * 1024 ? smem : 48 * 1024);
   if (rc) return rc;
-  const int k_out = xencb_route_k(top_k, n_chunks);
   route_topk_kernel<<<(unsigned)((n_rows + TOPK_WARPS - 1) / TOPK_WARPS), TOPK_WARPS * 32, smem, st>>>(
       lg, n_rows, n_chunks, n_chunks_of, rows_per_lib, top_k, k_out, row_w, idx, wk, w_dense);
   XENCB_CHECK_LAUNCH("route_topk launch");
@@ -1049,6 +1098,34 @@ int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_ou
   rc = launch_gemm<float>(r, n_rows, d_s, w_out, d_m, di.sms, part, w_prep ? xbuf : nullptr, nullptr, st, &gp, w_prep);
   if (rc) return rc;
   const float alpha = expf(log_alpha);
+  if (d_m <= 8 * ROW_THREADS) {  // one CTA per row: the reduce, the norms and the epilogue in registers
+    const int vpt = d_m <= 4 * ROW_THREADS ? 1 : 2;
+    const unsigned thr = (unsigned)std::min<int>(ROW_THREADS, (d_m / 4 + 31) / 32 * 32);
+    auto launch = [&](auto kern, auto* hp) {
+      kern<<<(unsigned)n_rows, thr, 0, st>>>(part, gp.splits, n_rows, d_m, b_out, scale, log_scale_dev, gate, hp,
+                                             sel_w, alpha, log_alpha_dev, pos_mask,
+                                             static_cast<decltype(hp)>(delta_out), static_cast<decltype(hp)>(h_out),
+                                             rel_out);
+    };
+    switch (h_dtype) {
+      case XENCB_F32:
+        if (vpt == 1) launch(project_out_row_kernel<float, 1>, static_cast<float*>(const_cast<void*>(h)));
+        else launch(project_out_row_kernel<float, 2>, static_cast<float*>(const_cast<void*>(h)));
+        break;
+      case XENCB_F16:
+        if (vpt == 1) launch(project_out_row_kernel<__half, 1>, static_cast<__half*>(const_cast<void*>(h)));
+        else launch(project_out_row_kernel<__half, 2>, static_cast<__half*>(const_cast<void*>(h)));
+        break;
+      default:
+        if (vpt == 1)
+          launch(project_out_row_kernel<__nv_bfloat16, 1>, static_cast<__nv_bfloat16*>(const_cast<void*>(h)));
+        else
+          launch(project_out_row_kernel<__nv_bfloat16, 2>, static_cast<__nv_bfloat16*>(const_cast<void*>(h)));
+        break;
+    }
+    XENCB_CHECK_LAUNCH("project_out row launch");
+    return XENCB_OK;
+  }
 #define XENCB_POUT(T)                                                                                          \
   do {                                                                                                         \
     project_out_reduce_kernel<T><<<dim3((unsigned)n_rows, nch), 256, 0, st>>>(                                \

@@ -128,6 +128,48 @@ def test_route_chunks_per_library(dev):
             assert topk_sets(w[row:row + 1, : int(n_of[lib])]) == topk_sets(wo)
 
 
+@pytest.mark.parametrize("C", [1, 7, 20, 64, 100, 128, 129, 300])
+@pytest.mark.parametrize("d_s", [30, 256, 2052])
+def test_route_decode_shapes(dev, C, d_s):
+    """Decode routing (few rows per Library): up to 128 chunks one fused launch (a cluster per row, or per 64 / C
+    rows), more chunks the logits + top-k pair. Against the oracle: logits, the kept index list in (value desc,
+    index asc) order, the weights; ragged chunk counts per Library and rows of weight 0."""
+    from kv_skill_v2_b200 import ops
+    g = torch.Generator().manual_seed(100 + C + d_s)
+    rows_per_lib, n_lib = 3, 5
+    R = rows_per_lib * n_lib - 1  # the last Library has one row fewer
+    S = torch.nn.functional.normalize(torch.randn(n_lib, C, d_s, generator=g), dim=-1)
+    q = torch.nn.functional.normalize(torch.randn(R, d_s, generator=g), dim=-1)
+    n_of = torch.tensor([C, max(1, C - 3), max(1, C // 2), 1, C], dtype=torch.int32)
+    row_w = torch.ones(R)
+    row_w[4] = 0.0
+    for top_k in (0, 1, 5, 40):
+        idx, wk, w, lg = ops.route(q.to(dev), S.to(dev), rows_per_lib=rows_per_lib, top_k=top_k, route_temp=10.0,
+                                   n_chunks_of=n_of.to(dev), want_logits=True, row_w=row_w.to(dev))
+        idx, wk, w, lg = idx.cpu().numpy(), wk.cpu().numpy(), w.cpu().numpy(), lg.cpu().numpy()
+        assert idx.shape == (R, ops.route_k(top_k, C))
+        for row in range(R):
+            lib = row // rows_per_lib
+            nc = int(n_of[lib])
+            wo, lo, io = X.route(q[row:row + 1].numpy(), S[lib, :nc].numpy(), 10.0, top_k)
+            assert np.abs(lg[row, :nc] - lo[0]).max() <= 1e-5 * max(1.0, np.abs(lo).max()), (C, d_s, row)
+            assert (lg[row, nc:] == -np.inf).all()
+            assert topk_sets(w[row:row + 1, :nc]) == topk_sets(wo), (C, d_s, top_k, row)
+            assert (w[row, nc:] == 0).all()
+            assert np.abs(w[row, :nc] - wo[0]).max() < 1e-5
+            kept = min(top_k, nc) if 0 < top_k < nc else nc
+            if row_w[row] == 0:
+                assert (idx[row] == -1).all() and (wk[row] == 0).all()
+                continue
+            if 0 < top_k < nc:
+                assert idx[row, :kept].tolist() == io[0, :kept].tolist(), (C, d_s, top_k, row)
+            else:
+                assert idx[row, :nc].tolist() == list(range(nc))
+            assert (idx[row, kept:] == -1).all()
+            assert np.abs(wk[row, :kept] - w[row, idx[row, :kept]]).max() == 0
+    _status_clean(dev)
+
+
 def test_batched_documents_match_reference(dev):
     """Each row reads its own Library (a paged pool of 4 documents) -- checked per document against
     reference runs of the single-Library read."""
