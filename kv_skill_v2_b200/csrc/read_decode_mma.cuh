@@ -31,6 +31,8 @@ struct __align__(16) StageMeta {
   long long item;
   int nr;     // rows in this stage
   int flags;  // RM_FIRST | RM_LAST | RM_DONE
+  long long row;       // the item's query row
+  long long next_row;  // the query row of the CTA's next item when the producer has it decoded, else -1
 };
 constexpr int RM_FIRST = 1, RM_LAST = 2, RM_DONE = 4, RM_VAL = 8;  // RM_VAL: a stage of value rows (untied V)
 
@@ -45,6 +47,7 @@ struct __align__(16) GroupRec {
 __host__ __device__ inline size_t rm_smem_bytes(int n_stage, int stage_bytes, int ncw, int tpw) {
   return (size_t)n_stage * stage_bytes           // stages
          + (size_t)ncw * 2 * tpw * 4 * 2 * 4       // q fragments
+         + (size_t)ncw * 32 * (tpw / 8) * 16        // the next item's q, copied ahead [ncw][tpw / 8][32 lanes]
          + RM_SBUF * (size_t)16 * RM_RED_STRIDE * 4  // cross-warp partial scores [RM_SBUF][16 rows][stride]
          + (size_t)n_stage * sizeof(StageMeta)      // stage descriptors
          + RM_SBUF * sizeof(GroupRec)               // group records (consumers -> softmax warp)
@@ -62,7 +65,8 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 2) : 32 * 12, 
   const int stage_bytes = ((a.rps * row_stride + 127) / 128) * 128;
   unsigned char* stages = smem;
   uint32_t* qfrag = reinterpret_cast<uint32_t*>(smem + (size_t)a.n_stage * stage_bytes);  // [ncw][2][TPW][4][2]
-  float* red = reinterpret_cast<float*>(qfrag + ncw * 2 * TPW * 4 * 2);  // [RM_SBUF][16 rows][RM_RED_STRIDE]
+  float4* qpre = reinterpret_cast<float4*>(qfrag + ncw * 2 * TPW * 4 * 2);  // [ncw][TPW / 8][32 lanes]
+  float* red = reinterpret_cast<float*>(qpre + ncw * 32 * (TPW / 8));  // [RM_SBUF][16 rows][RM_RED_STRIDE]
   StageMeta* meta = reinterpret_cast<StageMeta*>(red + RM_SBUF * 16 * RM_RED_STRIDE);
   GroupRec* grec = reinterpret_cast<GroupRec*>(meta + a.n_stage);                 // [RM_SBUF]
   uint32_t* pfrag = reinterpret_cast<uint32_t*>(grec + RM_SBUF);                  // [RM_SBUF][4 lanes][4]
@@ -73,6 +77,16 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 2) : 32 * 12, 
   uint64_t* pbar = sbar + RM_SBUF;     // [RM_SBUF] the group's P fragments are published
   volatile int* abort_flag = reinterpret_cast<volatile int*>(pbar + RM_SBUF);
 
+  // the producer's first 32 items (one per lane) are looked up before the prologue, so the lookups overlap it
+  ItemRange mine;
+  mine.active = false;
+  mine.r0 = mine.r1 = 0;
+  mine.base = nullptr;
+  mine.row = 0;
+  if (warp == 0) {
+    const int64_t my_item = blockIdx.x + (int64_t)lane * gridDim.x;
+    if (my_item < a.n_items) mine = decode_item(a, my_item);
+  }
   {
     uint4* z = reinterpret_cast<uint4*>(stages);
     const int n16 = a.n_stage * stage_bytes / 16;
@@ -104,8 +118,7 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 2) : 32 * 12, 
     bool ok = true;
     // the CTA's items are decoded 32 at a time, one per lane (their page and row-range lookups overlap), and
     // handed to the whole warp by shuffles
-    ItemRange mine;
-    int64_t batch = -1;
+    int64_t batch = 0;
     int64_t k_item = 0;  // this CTA's k-th item is blockIdx.x + k * gridDim.x
     for (int64_t item = blockIdx.x; item < a.n_items && ok; item += gridDim.x, ++k_item) {
       if ((k_item >> 5) != batch) {
@@ -123,6 +136,8 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 2) : 32 * 12, 
       it.r0 = __shfl_sync(0xffffffffu, mine.r0, who);
       it.r1 = __shfl_sync(0xffffffffu, mine.r1, who);
       it.row = __shfl_sync(0xffffffffu, (long long)mine.row, who);
+      // the next item's row, from the lane that decoded it (the batch's last item leaves it to a global load)
+      const long long nrow = __shfl_sync(0xffffffffu, mine.active ? (long long)mine.row : -1ll, (who + 1) & 31);
       it.base = reinterpret_cast<const char*>(
           __shfl_sync(0xffffffffu, (unsigned long long)reinterpret_cast<uintptr_t>(mine.base), who));
       if (!it.active || it.r1 <= it.r0) continue;
@@ -138,6 +153,8 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 2) : 32 * 12, 
           if (lane == 0) {
             meta[slot].item = item;
             meta[slot].nr = nr;
+            meta[slot].row = it.row;
+            meta[slot].next_row = who < 31 ? nrow : -1;
             meta[slot].flags = part == 0 ? ((rs == it.r0 ? RM_FIRST : 0) | (last && !a.vslots ? RM_LAST : 0))
                                          : (RM_VAL | (last ? RM_LAST : 0));
             mbar_arrive_expect_tx(&full[slot], (uint32_t)nr * a.row_bytes);
@@ -158,6 +175,8 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 2) : 32 * 12, 
       if (use == 0 || mbar_wait_bounded(&empty[slot], (use - 1) & 1)) {
         meta[slot].item = -1;
         meta[slot].nr = 0;
+        meta[slot].row = 0;
+        meta[slot].next_row = -1;
         meta[slot].flags = RM_DONE;
         mbar_arrive(&full[slot]);
         ++it_count;
@@ -286,17 +305,39 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 2) : 32 * 12, 
   };
 
   // q fragments of an item (B operand, query in column 0 = lanes 0..3), hi and residual, into this warp's slot
-  auto load_q = [&](int64_t item) {
+  // q of the CTA's next item (its row comes with the item's first stage) is copied into this lane's slots of qpre
+  // when an item starts (cp.async, no registers held), so the next item's first group finds it on chip
+  float4* qp = qpre + cw * 32 * (TPW / 8);
+  int64_t qnext_row = -1;
+  auto load_q = [&](const StageMeta& md) {
     // the warp's 16*TPW columns of q: lane i loads columns [4i, 4i + 4) of each 128-column block with one
     // 16-byte load and writes them, packed to the slot type, into their B-fragment words (tile t = i / 4:
     // columns 16t + r; pairs r < 8 are the fragment's first word of lane r / 2, pairs r >= 8 its second)
-    const int64_t row = (item / a.n_split) / a.k;
+    const int64_t row = md.row;
     const float* qr = a.q + row * a.d_s;
+    float4 qv[TPW / 8];
+    const bool pre = row == qnext_row;
+    if (pre) cp_async_wait_all();  // this lane's own copies
+#pragma unroll
+    for (int u = 0; u < TPW / 8; ++u) {
+      const int t = u * 8 + (lane >> 2);
+      if (t < nt)
+        qv[u] = pre ? qp[u * 32 + lane] : __ldg(reinterpret_cast<const float4*>(qr + d0 + t * 16 + (lane & 3) * 4));
+    }
+    qnext_row = md.next_row;
+    if (qnext_row >= 0) {
+      const float* nq = a.q + qnext_row * a.d_s;
+#pragma unroll
+      for (int u = 0; u < TPW / 8; ++u) {
+        const int t = u * 8 + (lane >> 2);
+        if (t < nt) cp_async16(qp + u * 32 + lane, nq + d0 + t * 16 + (lane & 3) * 4);
+      }
+    }
 #pragma unroll
     for (int u = 0; u < TPW / 8; ++u) {
       const int t = u * 8 + (lane >> 2);  // tile of this lane's four columns
       if (t < nt) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(qr + d0 + t * 16 + (lane & 3) * 4));
+        const float4 v = qv[u];
         const int r0 = (lane & 3) * 4;  // column of v.x within the tile
         const int w = r0 < 8 ? 0 : 1;   // first or second fragment word
         const int l0 = (r0 & 7) >> 1;   // fragment lane of the pair (v.x, v.y); (v.z, v.w) goes to l0 + 1
@@ -443,7 +484,7 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 2) : 32 * 12, 
         post_done();
         break;
       }
-      if (md.flags & RM_FIRST) load_q(md.item);
+      if (md.flags & RM_FIRST) load_q(md);
       for (int g0 = 0; g0 < md.nr; g0 += 16) {
         post(slot, g0, md);
         if (have && !finish(pd)) { ok = false; break; }
