@@ -7,13 +7,15 @@ routing, read_temp 12, route_temp 10. A step is one pass of the hot path for the
 query projection + L2, routing, the split-K masked read, output projection + residual + mag term.
 
 * value: whole-job tokens/s with inputs resident in HBM (the step captured in a CUDA graph), timed per step
-  with CUDA events on the launching stream, L2 flushed (256 MiB write) between steps outside the events;
+  with CUDA events on the launching stream, L2 flushed between steps outside the events (a 256 MiB write, then
+  a read of the same buffer, so the flush's dirty lines are written back before the step, not during it);
   max over ranks. Multi-GPU runs are weak-scaled replicas (every rank its own 64 documents, no collective
   in the data path; one all-reduce of the elapsed time after timing).
 * e2e: the same metric through the public API -- a reader model whose hooked block runs LibraryInjector --
   from pinned host hidden states, H2D copy and D2H copy of the result inside the timed region.
-* roofline: the read (read_decode_kernel + its merge) timed alone; achieved = algorithmic bytes (valid slot
-  rows of the routed chunks, read once, + q in + r out) / time, against MEASURED_PEAKS.json hbm_gbs.
+* roofline: the read kernel timed alone (CUDA events recorded by libxencb right around it, after an L2 flush);
+  achieved = algorithmic bytes (valid slot rows of the routed chunks, read once, + q in) / time, against
+  MEASURED_PEAKS.json hbm_gbs. The whole read op (kernel + merge, one graph replay) is reported beside it.
 * cpu_baseline: the numpy oracle (a restatement of the reference's dense read) on host cores, on a bounded
   sample of the same workload.
 
@@ -40,6 +42,14 @@ UNIT = "tokens/s"
 CFG = dict(docs=64, C=64, N=512, d_s=2048, d_m=4096, top_k=4, T=1, read_temp=12.0, route_temp=10.0)
 FALLBACK_HBM_GBS = 6650.0
 FLUSH_BYTES = 256 << 20
+
+
+def l2_flush(flush, i: int) -> None:
+    """Evict L2 between timed steps: write a buffer of twice its size, then read the buffer back, so the dirty
+    lines of the write go to HBM here, outside the timed region, instead of during the next step."""
+    import torch
+    flush.fill_(i & 0xFF)
+    flush.view(torch.int32).sum()
 
 
 def parse_args(argv=None):
@@ -81,7 +91,7 @@ def config_dict(docs: int) -> dict:
             "d_m": CFG["d_m"], "top_k": CFG["top_k"], "query_tokens_per_doc": CFG["T"], "slot_dtype": "f16",
             "hidden_dtype": "f32", "weights_dtype": "f32", "read_temp": CFG["read_temp"],
             "route_temp": CFG["route_temp"], "last_chunk_valid": "U{1..512}",
-            "l2": "flushed between timed steps (256 MiB write); inputs per step > L2 as well",
+            "l2": "flushed between timed steps (256 MiB write + read back); inputs per step > L2 as well",
             "parallelism": "replicas (weak scaling, one doc batch per GPU)"}
 
 
@@ -313,14 +323,14 @@ def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
         g_post.replay()
 
     for i in range(warmup):
-        flush.fill_(i & 0xFF)
+        l2_flush(flush, i)
         step(i)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     for i in range(steps):
-        flush.fill_(i & 0xFF)
+        l2_flush(flush, i)
         ev[i][0].record(stream)
         step(warmup + i)
         ev[i][1].record(stream)
@@ -338,10 +348,10 @@ def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
         sr.partial(q_s)
     evr = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(max(steps, 20))]
     for i in range(3):
-        flush.fill_(i)
+        l2_flush(flush, i)
         g_read.replay()
     for i in range(len(evr)):
-        flush.fill_(i & 0xFF)
+        l2_flush(flush, i)
         evr[i][0].record(stream)
         g_read.replay()
         evr[i][1].record(stream)
@@ -364,7 +374,7 @@ def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
                          "achieved": read_bytes / t_read / 1e9, "peak": peak, "unit": "GB/s",
                          "frac": read_bytes / t_read / 1e9 / peak, "algorithmic_bytes_per_launch": read_bytes,
                          "launch_us": t_read * 1e6, "peak_source": peak_kind},
-            "l2": "flushed between steps (256 MiB write); the slot shard alone is > L2 at every N <= 8"}
+            "l2": "flushed between steps (256 MiB write + read back); the slot shard alone is > L2 at every N <= 8"}
 
 
 CFG4 = dict(docs=32, L=8, C=32, N=512, d_s=2048, d_m=5120, sel_k=2, top_k=4, read_temp=12.0, route_temp=10.0)
@@ -439,7 +449,7 @@ def run_selector(torch, dist, dev, world: int, rank: int, steps: int, warmup: in
         torch.cuda.synchronize(dev)
         for i in range(warmup):
             h_in.copy_(hs[i]); z_in.copy_(zs[i])
-            flush.fill_(i & 0xFF)
+            l2_flush(flush, i)
             graph.replay()
         if world > 1:
             dist.barrier()
@@ -447,7 +457,7 @@ def run_selector(torch, dist, dev, world: int, rank: int, steps: int, warmup: in
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
         for i in range(steps):
             h_in.copy_(hs[warmup + i]); z_in.copy_(zs[warmup + i])
-            flush.fill_(i & 0xFF)
+            l2_flush(flush, i)
             ev[i][0].record(stream)
             graph.replay()
             ev[i][1].record(stream)
@@ -477,7 +487,7 @@ def run_selector(torch, dist, dev, world: int, rank: int, steps: int, warmup: in
                          "achieved": step_bytes / (ms / 1000.0) / 1e9, "peak": peak, "unit": "GB/s",
                          "frac": step_bytes / (ms / 1000.0) / 1e9 / peak, "algorithmic_bytes_per_step": step_bytes,
                          "peak_source": peak_kind},
-            "l2": "flushed between steps (256 MiB write)"}
+            "l2": "flushed between steps (256 MiB write + read back)"}
 
 
 CFGB = dict(docs=16, C=64, N=512, d_s=2048)
@@ -642,7 +652,7 @@ def run_topk(torch, dist, dev, world: int, rank: int, steps: int, warmup: int, f
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_steps)]
         for i in range(n_steps):
             if flush_between:
-                flush.fill_(i & 0xFF)
+                l2_flush(flush, i)
             ev[i][0].record(stream)
             fn()
             ev[i][1].record(stream)
@@ -674,7 +684,7 @@ def run_topk(torch, dist, dev, world: int, rank: int, steps: int, warmup: int, f
                                  "achieved": read_bytes / (ms_read / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
                                  "frac": read_bytes / (ms_read / 1e3) / 1e9 / peak,
                                  "algorithmic_bytes_per_step": read_bytes, "peak_source": peak_kind},
-                    "l2": "flushed between steps (256 MiB write)"},
+                    "l2": "flushed between steps (256 MiB write + read back)"},
            "n_gpus": world, "scaling": "weak"}
     if rank == 0 and world == 1 and cpu_seconds > 0:
         kq = keys[0].float().cpu().numpy()
@@ -762,7 +772,7 @@ def run_prefill(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
         q_s, w_s = holder["q"], holder["w"]
         for i in range(warmup):
             h.copy_(hs[i % n_in])
-            flush.fill_(i & 0xFF)
+            l2_flush(flush, i)
             graph.replay()
         if world > 1:
             dist.barrier()
@@ -770,7 +780,7 @@ def run_prefill(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
         for i in range(steps):
             h.copy_(hs[i % n_in])
-            flush.fill_(i & 0xFF)
+            l2_flush(flush, i)
             ev[i][0].record(stream)
             graph.replay()
             ev[i][1].record(stream)
@@ -783,7 +793,7 @@ def run_prefill(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
         evr = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_rl)]
         rg.replay()
         for i in range(n_rl):
-            flush.fill_(i & 0xFF)
+            l2_flush(flush, i)
             evr[i][0].record(stream)
             rg.replay()
             evr[i][1].record(stream)
@@ -810,7 +820,7 @@ def run_prefill(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
                          "achieved": read_flop / t_read / 1e12, "peak": peak, "unit": "TFLOP/s",
                          "frac": read_flop / t_read / 1e12 / peak, "algorithmic_flop_per_launch": read_flop,
                          "launch_ms": t_read * 1e3, "peak_source": peak_src},
-            "l2": "flushed between steps (256 MiB write); the slots (2 GiB) are > L2"}
+            "l2": "flushed between steps (256 MiB write + read back); the slots (2 GiB) are > L2"}
 
 
 def run_ours(args) -> None:
@@ -914,7 +924,7 @@ def run_ours(args) -> None:
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
         for i in range(args.warmup):
             h_static.copy_(hs[i])
-            flush.fill_(i & 0xFF)
+            l2_flush(flush, i)
             graph.replay()
         if world > 1:
             dist.barrier()
@@ -922,7 +932,7 @@ def run_ours(args) -> None:
         rows_read = 0
         for i in range(args.steps):
             h_static.copy_(hs[args.warmup + i])
-            flush.fill_(i & 0xFF)
+            l2_flush(flush, i)
             ev[i][0].record(stream)
             graph.replay()
             ev[i][1].record(stream)
@@ -938,25 +948,33 @@ def run_ours(args) -> None:
             t_max = float(t.item())
         value = R * args.steps * world / (t_max / 1000.0)
 
-        # ---- roofline: the read alone (read_decode_kernel + merge), q/idx/wk of the last step
-        rg = torch.cuda.CUDAGraph()
-        ops.read_decode(q_s, pages, idx_s, wk_s, rows_per_lib=CFG["T"])
+        # ---- roofline: the read kernel alone (events recorded by libxencb right around it), q/idx/wk of the last
+        # step, after an L2 flush; a sleep kernel keeps the stream busy while the host enqueues the call, so the
+        # interval holds the kernel only. The whole read op (kernel + merge, one graph replay) is timed beside it.
+        n_rl = max(args.steps, 50)
+        evk = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_rl)]
+        for i in range(3):
+            l2_flush(flush, i)
+            ops.read_decode(q_s, pages, idx_s, wk_s, rows_per_lib=CFG["T"])
+        for i in range(n_rl):
+            l2_flush(flush, i)
+            torch.cuda._sleep(200000)
+            ops.read_kernel_events(evk[i][0], evk[i][1])
+            ops.read_decode(q_s, pages, idx_s, wk_s, rows_per_lib=CFG["T"])
         torch.cuda.synchronize(dev)
+        t_read = statistics.mean(a.elapsed_time(b) for a, b in evk) / 1000.0
+        rg = torch.cuda.CUDAGraph()
         with torch.cuda.graph(rg):
             ops.read_decode(q_s, pages, idx_s, wk_s, rows_per_lib=CFG["T"])
-        n_rl = max(args.steps, 50)
         evr = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_rl)]
-        for i in range(3):
-            flush.fill_(i)
-            rg.replay()
         for i in range(n_rl):
-            flush.fill_(i & 0xFF)
+            l2_flush(flush, i)
             evr[i][0].record(stream)
             rg.replay()
             evr[i][1].record(stream)
         torch.cuda.synchronize(dev)
-        t_read = statistics.mean(a.elapsed_time(b) for a, b in evr) / 1000.0
-        read_bytes = rows_read * CFG["d_s"] * 2 + 2 * R * CFG["d_s"] * 4
+        t_read_op = statistics.mean(a.elapsed_time(b) for a, b in evr) / 1000.0
+        read_bytes = rows_read * CFG["d_s"] * 2 + R * CFG["d_s"] * 4
         peak, peak_kind = hbm_peak()
         achieved = read_bytes / t_read / 1e9
         tpr = traffic_per_row()
@@ -1061,11 +1079,14 @@ def run_ours(args) -> None:
             "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Gaussian unit slots, random weights)",
             "config": config_dict(docs),
-            "roofline": {"bound": "hbm", "kernel": "read_decode_kernel + read_merge_kernel",
+            "roofline": {"bound": "hbm", "kernel": "read_decode_mma_kernel",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6.65 TB/s", "algorithmic_bytes_per_launch": read_bytes,
                          "launch_us": t_read * 1e6,
+                         "read_op_us": t_read_op * 1e6,
+                         "read_op": "read_decode_mma_kernel + read_merge_kernel as one CUDA-graph replay, events "
+                                    "around the replay",
                          "traffic": None if tpr is None else tpr * rows_read},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": R * d_m * 4, "d2h_bytes_per_step": R * d_m * 4,

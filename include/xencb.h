@@ -309,6 +309,13 @@ XENCB_API int xencb_weights_prep(const float* w, int n, int k, void* prep, size_
  * becomes 0. The context stays usable. */
 XENCB_API int xencb_wait_selftest(long long limit_cycles, int* result, void* stream);
 
+/* ---------------------------------------------------------------------------------------------------------
+ * Instrumentation for kernel timing with CUDA events: the next xencb_read_decode call on this host thread records
+ * `before` and `after` (cudaEvent_t created by the caller, timing enabled; either may be NULL) on its stream
+ * immediately before and after its main read kernel, so their interval excludes the merge launch. One-shot:
+ * the call consumes the pair. No reference counterpart (measurement only). */
+XENCB_API int xencb_read_kernel_events(void* before, void* after);
+
 #ifdef __cplusplus
 }
 #endif

@@ -61,6 +61,7 @@ SIGNATURES: dict = {
     "xencb_select_topk": (_i, [_p, _i64, _i, _i, _p, _p, _p]),
     "xencb_topk_read": (_i, [_p, _i64, _i, _p, _p, _i, _i64, _i64, _i, _p, _i, _i64, _p, _i, _i, _f, _i, _p, _p, _p]),
     "xencb_wait_selftest": (_i, [ctypes.c_longlong, _p, _p]),
+    "xencb_read_kernel_events": (_i, [_p, _p]),
     "xencb_weights_prep_bytes": (_sz, [_i, _i]),
     "xencb_weights_prep": (_i, [_p, _i, _i, _p, _sz, _p]),
 }

@@ -22,6 +22,15 @@ __device__ unsigned int g_dev_status = 0;
 
 __device__ __forceinline__ void flag_error(unsigned int bits) { atomicOr(&g_dev_status, bits); }
 
+// Programmatic dependent launch (the kernels the host launches with programmatic stream serialisation: the read
+// merge, the row split, the 3xF16 GEMM and the projection row kernels). pdl_wait() returns once the grid before
+// this one in the stream has completed and its writes are visible (a no-op for a plain launch); such a kernel
+// touches global memory only after it, apart from reads that no kernel of the step writes (the GEMM's weight
+// tiles). pdl_trigger() lets the next grid be scheduled; it is issued after pdl_wait(), except in the row split,
+// whose successor's early work reads only the weights.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------------------------------------------ dtypes
 template <typename T> struct DT;
 template <> struct DT<float> { static constexpr int code = XENCB_F32; };

@@ -96,6 +96,8 @@ __global__ void __launch_bounds__(SR_THREADS) split_rows_f16x2_kernel(const T* _
                                                                       __half* __restrict__ hi, __half* __restrict__ lo,
                                                                       float* __restrict__ inv_scale) {
   __shared__ float red[SR_THREADS / 32];
+  pdl_trigger();  // the GEMM that follows may start on its weight tiles now
+  pdl_wait();
   const int64_t m = blockIdx.x;
   const T* xr = x + m * K;
   float v[SR_PIECES][8];
@@ -168,9 +170,6 @@ __global__ void __launch_bounds__(H3_THREADS, 1) gemm_f16x3_kernel(const __grid_
     prefetch_tensormap(&map_w);
     prefetch_tensormap(&map_x);
   }
-  // zero the per-row completion counters the following reduce kernel counts on (stream order)
-  if (row_done && blockIdx.x == 0 && blockIdx.z == 0)
-    for (int64_t i = m0 + threadIdx.x; i < min(M, m0 + H3_BN); i += blockDim.x) row_done[i] = 0;
   if (warp == 1) {
     tc_alloc(tmem_slot, H3_TMEM_COLS);
     tc_relinquish();
@@ -188,12 +187,39 @@ __global__ void __launch_bounds__(H3_THREADS, 1) gemm_f16x3_kernel(const __grid_
   __syncthreads();
   tc_fence_after();
   const uint32_t taddr = *tmem_slot;
+  // Under programmatic dependent launch the producer requests the weight tiles of the first stages before the
+  // row split this GEMM reads has finished (no kernel of the step writes the weights); everything else waits.
+  const int npre = min(nkb, H3_STAGES);
+  if (threadIdx.x != 0) {
+    pdl_wait();
+    pdl_trigger();
+  }
+  // zero the per-row completion counters the following reduce kernel counts on (stream order)
+  if (row_done && blockIdx.x == 0 && blockIdx.z == 0)
+    for (int64_t i = m0 + threadIdx.x; i < min(M, m0 + H3_BN); i += blockDim.x)
+      if (threadIdx.x != 0) row_done[i] = 0;
 
   if (warp == 0) {
     // ------------------------------------------------------------------------------------------- producer
     if (lane == 0) {
       const uint64_t keep = policy_evict_last();
-      for (int kb = 0; kb < nkb; ++kb) {
+      for (int kb = 0; kb < npre; ++kb) {
+        unsigned char* st = smem + kb * H3_STAGE;
+        mbar_arrive_expect_tx(&full[kb], H3_STAGE);
+        const int k = kbeg + kb * H3_BK;
+        tma_load_2d_hint(st, &map_w, k, n0, &full[kb], keep);
+        tma_load_2d_hint(st + H3_WBOX, &map_w, k, N + n0, &full[kb], keep);
+      }
+      pdl_wait();
+      pdl_trigger();
+      if (row_done && blockIdx.x == 0 && blockIdx.z == 0 && m0 < M) row_done[m0] = 0;
+      for (int kb = 0; kb < npre; ++kb) {
+        unsigned char* st = smem + kb * H3_STAGE;
+        const int k = kbeg + kb * H3_BK;
+        tma_load_2d(st + 2 * H3_WBOX, &map_x, k, (int)m0, &full[kb]);
+        tma_load_2d(st + 2 * H3_WBOX + H3_XBOX, &map_x, k, (int)(M + m0), &full[kb]);
+      }
+      for (int kb = npre; kb < nkb; ++kb) {
         const int s = kb % H3_STAGES, use = kb / H3_STAGES;
         if (use > 0 && (!mbar_wait_spin(&sfree[s], (use - 1) & 1) || *abort_flag)) { *abort_flag = 1; break; }
         unsigned char* st = smem + s * H3_STAGE;

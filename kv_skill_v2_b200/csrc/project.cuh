@@ -328,6 +328,8 @@ __global__ void __launch_bounds__(ROW_THREADS) project_in_row_kernel(
   __shared__ float2 red2[32];
   __shared__ float red[32];
   __shared__ float zsh[32];
+  pdl_wait();
+  pdl_trigger();
   const int64_t row = blockIdx.x;
   const TH* hr = h + row * d_m;
   int n[VPT];
@@ -513,6 +515,8 @@ __global__ void __launch_bounds__(ROW_THREADS) project_out_row_kernel(
     const float* __restrict__ pos_mask, TH* delta_out, TH* h_out, float* __restrict__ rel_out) {
   __shared__ float2 red2[32];
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   const int64_t row = blockIdx.x;
   int n[VPT];
   bool ok[VPT];

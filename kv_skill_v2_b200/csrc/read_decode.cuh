@@ -328,6 +328,8 @@ __global__ void __launch_bounds__(MERGE_THREADS) read_merge_kernel(const ReadArg
   __shared__ float ml[2 * MERGE_ENTRIES];
   __shared__ float coef[MERGE_ENTRIES];
   __shared__ int nan_flag;
+  pdl_wait();
+  pdl_trigger();
   const int tid = threadIdx.x;
   const int64_t row = blockIdx.x;
   const int col = (blockIdx.y * blockDim.x + tid) * 4;

@@ -33,6 +33,8 @@ namespace xencb {
 namespace {
 
 thread_local std::string g_err;
+// events of xencb_read_kernel_events, consumed by the next read launch on this thread
+thread_local cudaEvent_t g_read_ev_before = nullptr, g_read_ev_after = nullptr;
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -59,6 +61,33 @@ std::atomic<unsigned long long> g_launches{0};
     g_launches.fetch_add((n), std::memory_order_relaxed); \
   } while (0)
 #define XENCB_CHECK_LAUNCH(what) XENCB_CHECK_LAUNCH_N(what, 1)
+
+// Launch with programmatic stream serialisation (the kernel may be scheduled while the one before it in the stream
+// drains; it holds its dependent work behind pdl_wait(), common.cuh). Only kernels written for it go through
+// here. XENCB_PDL=0 in the environment launches them plainly. A failed launch is reported by the
+// XENCB_CHECK_LAUNCH that follows (the runtime records it for cudaGetLastError).
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("XENCB_PDL");
+    return !(e && e[0] == '0' && e[1] == 0);
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  (void)cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 constexpr int kMaxDev = 64;
 
@@ -226,8 +255,8 @@ int launch_gemm(const void* X, int64_t M, int K, const float* W, int N, int sms,
     const GemmPlan p = plan_gemm_tc(M, N, K, sms);
     __half* xs = reinterpret_cast<__half*>(xbuf);  // [X_hi; X_lo]: 2 M K halves = M K floats of staging
     float* x_inv = reinterpret_cast<float*>(reinterpret_cast<char*>(xbuf) + align_up((size_t)M * K * sizeof(float), 256));
-    split_rows_f16x2_kernel<TX><<<(unsigned)M, SR_THREADS, 0, st>>>(static_cast<const TX*>(X), M, K, xs,
-                                                                   xs + M * (int64_t)K, x_inv);
+    launch_pdl(split_rows_f16x2_kernel<TX>, dim3((unsigned)M), dim3(SR_THREADS), 0, st, static_cast<const TX*>(X), M,
+               K, xs, xs + M * (int64_t)K, x_inv);
     XENCB_CHECK_LAUNCH("split_rows_f16x2 launch");
     const char* wp = static_cast<const char*>(w_prep);
     CUtensorMap mw, mx;
@@ -240,9 +269,8 @@ int launch_gemm(const void* X, int64_t M, int K, const float* W, int N, int sms,
     rc = ensure_smem(gemm_f16x3_kernel, (int)H3_SMEM);
     if (rc) return rc;
     dim3 grid((N + H3_BM - 1) / H3_BM, (unsigned)((M + H3_BN - 1) / H3_BN), p.splits);
-    gemm_f16x3_kernel<<<grid, H3_THREADS, H3_SMEM, st>>>(mw, mx, M, N, K, p.kps,
-                                                         reinterpret_cast<const float*>(wp) + 1, x_inv, part,
-                                                         row_done);
+    launch_pdl(gemm_f16x3_kernel, grid, dim3(H3_THREADS), H3_SMEM, st, mw, mx, M, N, K, p.kps,
+               reinterpret_cast<const float*>(wp) + 1, x_inv, part, row_done);
     XENCB_CHECK_LAUNCH("gemm_f16x3 launch");
     *used = p;
     return XENCB_OK;
@@ -651,9 +679,8 @@ int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const 
     const int vpt = d_s <= 4 * ROW_THREADS ? 1 : 2;
     const unsigned thr = (unsigned)std::min<int>(ROW_THREADS, (d_s / 4 + 31) / 32 * 32);
     auto launch = [&](auto kern, const auto* hp) {
-      kern<<<(unsigned)n_rows, thr, 0, st>>>(hp, d_m, part, gp.splits, n_rows, d_s, flags, b_in, gate_w, gate_b,
-                                             gate_b_dev, sel_w, sel_b, n_cand, rms_eps, q_out, gate_out, rstd_out,
-                                             z_out);
+      launch_pdl(kern, dim3((unsigned)n_rows), dim3(thr), 0, st, hp, d_m, part, gp.splits, n_rows, d_s, flags, b_in,
+                 gate_w, gate_b, gate_b_dev, sel_w, sel_b, n_cand, rms_eps, q_out, gate_out, rstd_out, z_out);
     };
     switch (h_dtype) {
       case XENCB_F32:
@@ -729,6 +756,7 @@ int xencb_route(const float* q, int64_t n_rows, int d_s, const float* S, int n_c
   if (rows_per_lib < 64 && n_chunks <= 128 && fsmem <= 96 * 1024 && n_clusters * RF_CL <= INT32_MAX) {
     int rc = ensure_smem(route_fused_kernel, (int)std::max<size_t>(fsmem, 48 * 1024));
     if (rc) return rc;
+    // a plain launch: started early beside the projection's row kernel, its S traffic slowed that kernel down
     route_fused_kernel<<<(unsigned)(n_clusters * RF_CL), 256, fsmem, st>>>(
         q, n_rows, d_s, S, n_chunks, n_chunks_of, rows_per_lib, route_temp, rpc, top_k, k_out, row_w, idx, wk,
         w_dense, logit_out);
@@ -808,10 +836,14 @@ int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots
       auto k1 = read_decode_kernel<T, V, S>;
       int r2 = ensure_smem(k1, (int)p.smem);
       if (r2) return r2;
+      cudaEvent_t ev0 = g_read_ev_before, ev1 = g_read_ev_after;
+      g_read_ev_before = g_read_ev_after = nullptr;
+      if (ev0) cudaEventRecord(ev0, st);
       k1<<<p.grid, p.threads, p.smem, st>>>(a);
       XENCB_CHECK_LAUNCH("read_decode_kernel launch");
+      if (ev1) cudaEventRecord(ev1, st);
       dim3 mg((unsigned)n_rows, (d_s + 511) / 512);
-      read_merge_kernel<S><<<mg, MERGE_THREADS, 0, st>>>(a, r_out);
+      launch_pdl(read_merge_kernel<S>, mg, dim3(MERGE_THREADS), 0, st, a, r_out);
       XENCB_CHECK_LAUNCH("read_merge_kernel launch");
       return XENCB_OK;
     };
@@ -830,10 +862,14 @@ int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots
       auto k1 = read_decode_mma_kernel<T, SPLIT, S, W>;
       int r2 = ensure_smem(k1, (int)p.smem);
       if (r2) return r2;
+      cudaEvent_t ev0 = g_read_ev_before, ev1 = g_read_ev_after;
+      g_read_ev_before = g_read_ev_after = nullptr;
+      if (ev0) cudaEventRecord(ev0, st);
       k1<<<p.grid, p.threads, p.smem, st>>>(a);
       XENCB_CHECK_LAUNCH("read_decode_mma_kernel launch");
+      if (ev1) cudaEventRecord(ev1, st);
       dim3 mg((unsigned)n_rows, (d_s + 511) / 512);
-      read_merge_kernel<S><<<mg, MERGE_THREADS, 0, st>>>(a, r_out);
+      launch_pdl(read_merge_kernel<S>, mg, dim3(MERGE_THREADS), 0, st, a, r_out);
       XENCB_CHECK_LAUNCH("read_merge_kernel launch");
       return XENCB_OK;
     };
@@ -1102,10 +1138,9 @@ int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_ou
     const int vpt = d_m <= 4 * ROW_THREADS ? 1 : 2;
     const unsigned thr = (unsigned)std::min<int>(ROW_THREADS, (d_m / 4 + 31) / 32 * 32);
     auto launch = [&](auto kern, auto* hp) {
-      kern<<<(unsigned)n_rows, thr, 0, st>>>(part, gp.splits, n_rows, d_m, b_out, scale, log_scale_dev, gate, hp,
-                                             sel_w, alpha, log_alpha_dev, pos_mask,
-                                             static_cast<decltype(hp)>(delta_out), static_cast<decltype(hp)>(h_out),
-                                             rel_out);
+      launch_pdl(kern, dim3((unsigned)n_rows), dim3(thr), 0, st, part, gp.splits, n_rows, d_m, b_out, scale,
+                 log_scale_dev, gate, hp, sel_w, alpha, log_alpha_dev, pos_mask,
+                 static_cast<decltype(hp)>(delta_out), static_cast<decltype(hp)>(h_out), rel_out);
     };
     switch (h_dtype) {
       case XENCB_F32:
@@ -1473,6 +1508,12 @@ int xencb_weights_prep(const float* w, int n, int k, void* prep, size_t prep_byt
   __half* hi = reinterpret_cast<__half*>(static_cast<char*>(prep) + WPREP_HEAD);
   split_weights_kernel<<<blocks, 256, 0, st>>>(w, cnt, head, hi, hi + cnt, reinterpret_cast<float*>(head) + 1);
   XENCB_CHECK_LAUNCH("split_weights launch");
+  return XENCB_OK;
+}
+
+int xencb_read_kernel_events(void* before, void* after) {
+  g_read_ev_before = static_cast<cudaEvent_t>(before);
+  g_read_ev_after = static_cast<cudaEvent_t>(after);
   return XENCB_OK;
 }
 

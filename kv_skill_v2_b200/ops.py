@@ -630,6 +630,16 @@ def topk_read(q: torch.Tensor, pages: Pages, idx: torch.Tensor, *, read_temp: fl
     return r, attn
 
 
+def read_kernel_events(before, after) -> None:
+    """Instrumentation: the next read_decode on this thread records the torch.cuda.Events `before` / `after`
+    (timing enabled) right around its main read kernel, leaving the merge out of the interval. One-shot."""
+    for ev in (before, after):
+        if ev is not None and not ev.cuda_event:
+            ev.record()  # torch creates the CUDA event on its first record
+    N.call("xencb_read_kernel_events", before.cuda_event if before is not None else None,
+           after.cuda_event if after is not None else None)
+
+
 def wait_selftest(dev: torch.device, limit_cycles: int = 2_000_000) -> int:
     """Run the bounded-wait self-test on `dev` (a wait that nothing satisfies must give up); returns the
     kernel's result (0 = gave up). The device status then carries XENCB_DEV_TIMEOUT."""
