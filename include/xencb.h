@@ -146,7 +146,8 @@ XENCB_API int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const v
  * device looks up that array's device address (cudaGetSymbolAddress) with the device current; make that first
  * call before any stream capture. All calls share the one array: calls on one device that overlap on the GPU
  * (issued to different streams) race and corrupt each other's results, so serialise them. Nothing in the
- * array needs to start at zero: every word the merge reads is written earlier in the same call. */
+ * array needs to start at zero: the merge uses only words written earlier in the same call (it may load the
+ * stale words of splits that hold no rows, and discards them). */
 #define XENCB_NOALLOC_SCRATCH_BYTES (16u << 20)
 XENCB_API int xencb_read_decode_noalloc(const float* q, int64_t n_rows, int d_s, const void* slots, int slots_dtype,
                                         int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of,
