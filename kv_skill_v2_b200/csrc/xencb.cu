@@ -190,7 +190,7 @@ GemmPlan plan_gemm_simt(int64_t M, int N, int K, int sms) {
 // plus one float per row for the 3xF16 kernels.
 size_t gemm_part_bytes(int64_t M, int N, int K, int sms) {
   size_t b = plan_gemm_simt(M, N, K, sms).part_bytes;
-  if (K % 4 == 0) b = std::max(b, plan_gemm_tc(M, N, K, sms).part_bytes);
+  if (K % 4 == 0) b = std::max(b, plan_gemm_tc(M, N, K, (M > H3_BN ? 2 : 1) * sms).part_bytes);
   return b;
 }
 
@@ -252,7 +252,8 @@ int launch_gemm(const void* X, int64_t M, int K, const float* W, int N, int sms,
   const bool f16x3 = w_prep != nullptr;
   if (f16x3 && K % 8 == 0 && aligned(w_prep, 256) && aligned(X, 16) && xbuf && M <= INT32_MAX / 2 &&
       N <= INT32_MAX / 2) {
-    const GemmPlan p = plan_gemm_tc(M, N, K, sms);
+    const bool two = M > H3_BN;  // more than one row tile: two CTAs per SM (see gemm_f16x3.cuh)
+    const GemmPlan p = plan_gemm_tc(M, N, K, (two ? 2 : 1) * sms);
     __half* xs = reinterpret_cast<__half*>(xbuf);  // [X_hi; X_lo]: 2 M K halves = M K floats of staging
     float* x_inv = reinterpret_cast<float*>(reinterpret_cast<char*>(xbuf) + align_up((size_t)M * K * sizeof(float), 256));
     launch_pdl(split_rows_f16x2_kernel<TX>, dim3((unsigned)M), dim3(SR_THREADS), 0, st, static_cast<const TX*>(X), M,
@@ -266,10 +267,12 @@ int launch_gemm(const void* X, int64_t M, int K, const float* W, int N, int sms,
     rc = tensor_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xs, (uint64_t)K, 2 * (uint64_t)M, (uint64_t)K * 2,
                        H3_BK, H3_BN);
     if (rc) return rc;
-    rc = ensure_smem(gemm_f16x3_kernel, (int)H3_SMEM);
+    auto kern = two ? gemm_f16x3_kernel<2, 2> : gemm_f16x3_kernel<4, 1>;
+    const size_t h3s = h3_smem(two ? 2 : 4);
+    rc = ensure_smem(kern, (int)h3s);
     if (rc) return rc;
     dim3 grid((N + H3_BM - 1) / H3_BM, (unsigned)((M + H3_BN - 1) / H3_BN), p.splits);
-    launch_pdl(gemm_f16x3_kernel, grid, dim3(H3_THREADS), H3_SMEM, st, mw, mx, M, N, K, p.kps,
+    launch_pdl(kern, grid, dim3(H3_THREADS), h3s, st, mw, mx, M, N, K, p.kps,
                reinterpret_cast<const float*>(wp) + 1, x_inv, part, row_done);
     XENCB_CHECK_LAUNCH("gemm_f16x3 launch");
     *used = p;
