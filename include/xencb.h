@@ -136,6 +136,21 @@ XENCB_API int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const v
                       float read_temp, int read_softmax, float* r_out, void* workspace, size_t workspace_bytes,
                       void* stream);
 
+/* The same read (xenc/injector.py:239-245, 263-265) planned for calls where many rows read nothing: rows whose
+ * routing weights are all zero (the LayerSelector's row mask, xenc/selector.py:106-110, makes most tokens skip
+ * most depths). Chunks are split into 64-row pieces and a one-CTA pass lists the pieces that hold rows, so the
+ * live work spreads over every SM instead of over the few CTAs whose fixed share it falls in. Results match
+ * xencb_read_decode within float32 rounding (the split sums are added in a different grouping). Tensor-core
+ * (f16 / bf16, tied) reads only; other calls run the plan of xencb_read_decode. Workspace:
+ * xencb_read_decode_sparse_workspace bytes. */
+XENCB_API size_t xencb_read_decode_sparse_workspace(int64_t n_rows, int k, int d_s, int page_rows, int slots_dtype);
+XENCB_API int xencb_read_decode_sparse(const float* q, int64_t n_rows, int d_s, const void* slots, const void* vslots,
+                                       int slots_dtype, int64_t n_pages, int64_t page_stride, int page_rows,
+                                       const int32_t* page_of, const int32_t* n_valid, int n_chunks,
+                                       int64_t rows_per_lib, int64_t n_lib, const int32_t* idx, const float* wk, int k,
+                                       float read_temp, int read_softmax, float* r_out, void* workspace,
+                                       size_t workspace_bytes, void* stream);
+
 /* Same read as xencb_read_decode, for callers that cannot allocate device memory at all: a host runtime that
  * owns every device byte through its own allocator and offers no way to request scratch, or a serving loop
  * that must not allocate (an allocation may synchronise the device). There is no counterpart of this entry

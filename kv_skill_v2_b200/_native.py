@@ -36,7 +36,10 @@ SIGNATURES: dict = {
     "xencb_route_k": (_i, [_i, _i]),
     "xencb_route": (_i, [_p, _i64, _i, _p, _i, _p, _i64, _i64, _f, _i, _p, _p, _p, _p, _p, _p]),
     "xencb_read_decode_workspace": (_sz, [_i64, _i, _i, _i, _i]),
+    "xencb_read_decode_sparse_workspace": (_sz, [_i64, _i, _i, _i, _i]),
     "xencb_read_decode": (_i, [_p, _i64, _i, _p, _p, _i, _i64, _i64, _i, _p, _p, _i, _i64, _i64, _p, _p, _i, _f,
+                               _i, _p, _p, _sz, _p]),
+    "xencb_read_decode_sparse": (_i, [_p, _i64, _i, _p, _p, _i, _i64, _i64, _i, _p, _p, _i, _i64, _i64, _p, _p, _i, _f,
                                _i, _p, _p, _sz, _p]),
     "xencb_read_decode_noalloc": (_i, [_p, _i64, _i, _p, _i, _i64, _i64, _i, _p, _p, _i, _i64, _i64, _p, _p, _i,
                                        _f, _i, _p, _p]),

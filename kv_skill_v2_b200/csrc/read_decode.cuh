@@ -51,6 +51,10 @@ struct ReadArgs {
   int64_t n_items;
   float* part_acc;  // [n_items, d_s]
   float* part_ml;   // [n_items, 2]
+  // sparse plan (xencb_read_decode_sparse): the items that hold rows, in item order, and their count, written by
+  // read_compact_kernel; null for the dense plan, whose CTAs walk every item
+  const int32_t* item_list;
+  const int* n_active;
 };
 
 struct ItemRange {
@@ -309,6 +313,63 @@ __global__ void __launch_bounds__(512, 1) read_decode_kernel(const ReadArgs a) {
       a.part_ml[item * 2 + 1] = SOFTMAX ? l : (any ? 1.f : 0.f);
     }
   }
+}
+
+// Sparse plan: one CTA lists the items (pair * n_split + split) that hold rows -- routed chunk valid, weight
+// non-zero, page inside the pool, split below the chunk's valid rows -- in item order, so that the read kernel's
+// CTAs share only live work (a read where the selector masked most rows would otherwise leave most CTAs idle
+// and a few with several items). Flags the device status as decode_item does for the pairs it skips.
+constexpr int RC_THREADS = 1024;
+__global__ void __launch_bounds__(RC_THREADS) read_compact_kernel(const ReadArgs a, int32_t* __restrict__ list,
+                                                                  int* __restrict__ n_active) {
+  __shared__ int wsum[RC_THREADS / 32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int64_t pairs = a.n_rows * a.k;
+  int total = 0;
+  for (int64_t base = 0; base < pairs; base += blockDim.x) {
+    const int64_t pr = base + threadIdx.x;
+    int cnt = 0;
+    if (pr < pairs) {
+      const int32_t c = a.idx[pr];
+      const float w = a.wk[pr];
+      if (c >= 0 && c < a.n_chunks && w != 0.f) {
+        const int64_t lc = (pr / a.k / a.rows_per_lib) * a.n_chunks + c;
+        const int64_t page = a.page_of[lc];
+        if (page < 0 || page >= a.n_pages) {
+          flag_error(XENCB_DEV_BADPAGE);
+        } else {
+          int nv = a.n_valid[lc];
+          if (nv > a.page_rows) { nv = a.page_rows; flag_error(XENCB_DEV_CLAMPED); }
+          if (nv < 0) nv = 0;
+          cnt = min(a.n_split, (nv + a.split_rows - 1) / a.split_rows);
+        }
+      }
+    }
+    // block-wide exclusive scan of cnt
+    int x = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[wid] = x;
+    __syncthreads();
+    if (wid == 0) {
+      int t = lane < nw ? wsum[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, t, o);
+        if (lane >= o) t += y;
+      }
+      if (lane < nw) wsum[lane] = t;
+    }
+    __syncthreads();
+    const int off = total + (wid > 0 ? wsum[wid - 1] : 0) + x - cnt;
+    for (int sp = 0; sp < cnt; ++sp) list[off + sp] = (int32_t)(pr * a.n_split + sp);
+    total += wsum[nw - 1];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *n_active = total;
 }
 
 // r[row] = sum_j w_j * read_j; grid (n_rows, ceil(d_s / 512)), 128 threads x 4 columns.

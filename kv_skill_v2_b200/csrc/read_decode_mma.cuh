@@ -83,9 +83,12 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 2) : 32 * 12, 
   mine.r0 = mine.r1 = 0;
   mine.base = nullptr;
   mine.row = 0;
+  // work units: every item in order, or (sparse plan) the listed items that hold rows
+  int64_t n_work = a.n_items;
   if (warp == 0) {
-    const int64_t my_item = blockIdx.x + (int64_t)lane * gridDim.x;
-    if (my_item < a.n_items) mine = decode_item(a, my_item);
+    if (a.item_list) n_work = *a.n_active;
+    const int64_t my_w = blockIdx.x + (int64_t)lane * gridDim.x;
+    if (my_w < n_work) mine = decode_item(a, a.item_list ? (int64_t)a.item_list[my_w] : my_w);
   }
   {
     uint4* z = reinterpret_cast<uint4*>(stages);
@@ -120,15 +123,16 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 2) : 32 * 12, 
     // handed to the whole warp by shuffles
     int64_t batch = 0;
     int64_t k_item = 0;  // this CTA's k-th item is blockIdx.x + k * gridDim.x
-    for (int64_t item = blockIdx.x; item < a.n_items && ok; item += gridDim.x, ++k_item) {
+    for (int64_t wu = blockIdx.x; wu < n_work && ok; wu += gridDim.x, ++k_item) {
+      const int64_t item = a.item_list ? (int64_t)a.item_list[wu] : wu;
       if ((k_item >> 5) != batch) {
         batch = k_item >> 5;
-        const int64_t my_item = blockIdx.x + ((batch << 5) + lane) * (int64_t)gridDim.x;
+        const int64_t my_w = blockIdx.x + ((batch << 5) + lane) * (int64_t)gridDim.x;
         mine.active = false;
         mine.r0 = mine.r1 = 0;
         mine.base = nullptr;
         mine.row = 0;
-        if (my_item < a.n_items) mine = decode_item(a, my_item);
+        if (my_w < n_work) mine = decode_item(a, a.item_list ? (int64_t)a.item_list[my_w] : my_w);
       }
       const int who = (int)(k_item & 31);  // the lane that decoded this item
       ItemRange it;

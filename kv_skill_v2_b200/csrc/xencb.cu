@@ -318,9 +318,12 @@ struct ReadPlan {
   int vpt, ncw, rps, n_stage, n_split, split_rows, row_bytes, row_stride, nvec, threads, grid;
   size_t smem, acc_bytes, ml_bytes;
   int64_t n_items;
+  bool sparse;        // items listed by read_compact_kernel (xencb_read_decode_sparse)
+  size_t list_bytes;  // its item list and count, after the partials
 };
 
-int plan_read(int64_t n_rows, int k, int d_s, int page_rows, int dtype, ReadPlan* p, bool untied = false) {
+int plan_read(int64_t n_rows, int k, int d_s, int page_rows, int dtype, ReadPlan* p, bool untied = false,
+              bool sparse = false) {
   DevInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
@@ -405,6 +408,17 @@ int plan_read(int64_t n_rows, int k, int d_s, int page_rows, int dtype, ReadPlan
   }
   p->n_split = best_n;
   p->split_rows = best_rows < 1 ? 1 : best_rows;
+  p->sparse = false;
+  p->list_bytes = 0;
+  if (sparse && p->mma && !untied && max_split > 1 && pairs * max_split <= INT32_MAX) {
+    // sparse plan: the finest splits (64 rows), only the splits that hold rows listed on the device, so that a
+    // read where few rows take part still spreads over every SM
+    p->sparse = true;
+    p->n_split = max_split;
+    p->split_rows = (page_rows + max_split - 1) / max_split;
+    p->split_rows = (p->split_rows + 15) / 16 * 16;
+    p->list_bytes = align_up((size_t)pairs * max_split * sizeof(int32_t), 256) + 256;
+  }
   p->n_items = pairs * p->n_split;
   p->grid = (int)(p->n_items < grid_max ? p->n_items : grid_max);
   if (p->grid < 1) p->grid = 1;
@@ -678,26 +692,23 @@ int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const 
       break;
   }
   if (rc) return rc;
-  if (d_s <= 8 * ROW_THREADS) {  // one CTA per row: the reduce, 1/rms, bias and L2 norm in registers
-    const int vpt = d_s <= 4 * ROW_THREADS ? 1 : 2;
+  if (d_s <= 12 * ROW_THREADS) {  // one CTA per row: the reduce, 1/rms, bias and L2 norm in registers
+    const int vpt = (d_s + 4 * ROW_THREADS - 1) / (4 * ROW_THREADS);  // float4 columns per thread: 1..3
     const unsigned thr = (unsigned)std::min<int>(ROW_THREADS, (d_s / 4 + 31) / 32 * 32);
     auto launch = [&](auto kern, const auto* hp) {
       launch_pdl(kern, dim3((unsigned)n_rows), dim3(thr), 0, st, hp, d_m, part, gp.splits, n_rows, d_s, flags, b_in,
                  gate_w, gate_b, gate_b_dev, sel_w, sel_b, n_cand, rms_eps, q_out, gate_out, rstd_out, z_out);
     };
+    auto by_vpt = [&](const auto* hp) {
+      using TH = std::remove_const_t<std::remove_pointer_t<decltype(hp)>>;
+      if (vpt == 1) launch(project_in_row_kernel<TH, 1>, hp);
+      else if (vpt == 2) launch(project_in_row_kernel<TH, 2>, hp);
+      else launch(project_in_row_kernel<TH, 3>, hp);
+    };
     switch (h_dtype) {
-      case XENCB_F32:
-        if (vpt == 1) launch(project_in_row_kernel<float, 1>, static_cast<const float*>(h));
-        else launch(project_in_row_kernel<float, 2>, static_cast<const float*>(h));
-        break;
-      case XENCB_F16:
-        if (vpt == 1) launch(project_in_row_kernel<__half, 1>, static_cast<const __half*>(h));
-        else launch(project_in_row_kernel<__half, 2>, static_cast<const __half*>(h));
-        break;
-      default:
-        if (vpt == 1) launch(project_in_row_kernel<__nv_bfloat16, 1>, static_cast<const __nv_bfloat16*>(h));
-        else launch(project_in_row_kernel<__nv_bfloat16, 2>, static_cast<const __nv_bfloat16*>(h));
-        break;
+      case XENCB_F32: by_vpt(static_cast<const float*>(h)); break;
+      case XENCB_F16: by_vpt(static_cast<const __half*>(h)); break;
+      default: by_vpt(static_cast<const __nv_bfloat16*>(h)); break;
     }
     XENCB_CHECK_LAUNCH("project_in row launch");
     return XENCB_OK;
@@ -788,11 +799,18 @@ size_t xencb_read_decode_workspace(int64_t n_rows, int k, int d_s, int page_rows
   return p.acc_bytes + p.ml_bytes;
 }
 
-int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots, const void* vslots, int slots_dtype,
-                      int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of, const int32_t* n_valid,
-                      int n_chunks, int64_t rows_per_lib, int64_t n_lib, const int32_t* idx, const float* wk, int k,
-                      float read_temp, int read_softmax, float* r_out, void* workspace, size_t workspace_bytes,
-                      void* stream) {
+size_t xencb_read_decode_sparse_workspace(int64_t n_rows, int k, int d_s, int page_rows, int slots_dtype) {
+  if (n_rows <= 0 || k <= 0 || d_s <= 0 || page_rows <= 0) return 0;
+  ReadPlan p;
+  if (plan_read(n_rows, k, d_s, page_rows, slots_dtype, &p, false, true)) return 0;
+  return p.acc_bytes + p.ml_bytes + p.list_bytes;
+}
+
+static int read_decode_impl(const float* q, int64_t n_rows, int d_s, const void* slots, const void* vslots, int slots_dtype,
+                     int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of, const int32_t* n_valid,
+                     int n_chunks, int64_t rows_per_lib, int64_t n_lib, const int32_t* idx, const float* wk, int k,
+                     float read_temp, int read_softmax, float* r_out, void* workspace, size_t workspace_bytes,
+                     void* stream, bool sparse) {
   if (!q || !slots || !page_of || !n_valid || !idx || !wk || !r_out)
     return fail(XENCB_EINVAL, "read_decode: q, slots, page_of, n_valid, idx, wk and r_out are required");
   if (n_rows <= 0 || d_s <= 0 || page_rows <= 0 || n_chunks <= 0 || rows_per_lib <= 0 || n_lib <= 0 || k <= 0)
@@ -810,11 +828,11 @@ int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots
     return fail(XENCB_EINVAL, "read_decode: slots, q, r_out and page_stride*elem must be 16-byte aligned");
   if (vslots && !aligned(vslots, 16)) return fail(XENCB_EINVAL, "read_decode: vslots must be 16-byte aligned");
   ReadPlan p;
-  int rc = plan_read(n_rows, k, d_s, page_rows, slots_dtype, &p, vslots != nullptr);
+  int rc = plan_read(n_rows, k, d_s, page_rows, slots_dtype, &p, vslots != nullptr, sparse);
   if (rc) return rc;
-  if (!workspace || !aligned(workspace, 256) || workspace_bytes < p.acc_bytes + p.ml_bytes)
+  if (!workspace || !aligned(workspace, 256) || workspace_bytes < p.acc_bytes + p.ml_bytes + p.list_bytes)
     return fail(XENCB_EINVAL, "read_decode: workspace needs %zu bytes, 256-byte aligned (got %zu)",
-                p.acc_bytes + p.ml_bytes, workspace_bytes);
+                p.acc_bytes + p.ml_bytes + p.list_bytes, workspace_bytes);
   ReadArgs a;
   a.q = q; a.n_rows = n_rows; a.d_s = d_s;
   a.slots = static_cast<const char*>(slots);
@@ -829,7 +847,18 @@ int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots
   a.row_bytes = p.row_bytes; a.nvec = p.nvec; a.n_items = p.n_items; a.row_stride = p.row_stride;
   a.part_acc = static_cast<float*>(workspace);
   a.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + p.acc_bytes);
+  a.item_list = nullptr;
+  a.n_active = nullptr;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (p.sparse) {
+    char* lb = static_cast<char*>(workspace) + p.acc_bytes + p.ml_bytes;
+    int32_t* list = reinterpret_cast<int32_t*>(lb);
+    int* n_act = reinterpret_cast<int*>(lb + p.list_bytes - 256);
+    read_compact_kernel<<<1, RC_THREADS, 0, st>>>(a, list, n_act);
+    XENCB_CHECK_LAUNCH("read_compact_kernel launch");
+    a.item_list = list;
+    a.n_active = n_act;
+  }
   rc = XENCB_OK;
   {
     auto run = [&](auto tag_t, auto tag_v, auto tag_s) -> int {
@@ -896,6 +925,26 @@ int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots
     }
   }
   return rc;
+}
+
+int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const void* slots, const void* vslots, int slots_dtype,
+                      int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of, const int32_t* n_valid,
+                      int n_chunks, int64_t rows_per_lib, int64_t n_lib, const int32_t* idx, const float* wk, int k,
+                      float read_temp, int read_softmax, float* r_out, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  return read_decode_impl(q, n_rows, d_s, slots, vslots, slots_dtype, n_pages, page_stride, page_rows, page_of,
+                          n_valid, n_chunks, rows_per_lib, n_lib, idx, wk, k, read_temp, read_softmax, r_out,
+                          workspace, workspace_bytes, stream, false);
+}
+
+int xencb_read_decode_sparse(const float* q, int64_t n_rows, int d_s, const void* slots, const void* vslots,
+                             int slots_dtype, int64_t n_pages, int64_t page_stride, int page_rows,
+                             const int32_t* page_of, const int32_t* n_valid, int n_chunks, int64_t rows_per_lib,
+                             int64_t n_lib, const int32_t* idx, const float* wk, int k, float read_temp,
+                             int read_softmax, float* r_out, void* workspace, size_t workspace_bytes, void* stream) {
+  return read_decode_impl(q, n_rows, d_s, slots, vslots, slots_dtype, n_pages, page_stride, page_rows, page_of,
+                          n_valid, n_chunks, rows_per_lib, n_lib, idx, wk, k, read_temp, read_softmax, r_out,
+                          workspace, workspace_bytes, stream, true);
 }
 
 // ------------------------------------------------------------------------------------------------ read_multi
@@ -1137,29 +1186,24 @@ int xencb_project_out(const float* r, int64_t n_rows, int d_s, const float* w_ou
   rc = launch_gemm<float>(r, n_rows, d_s, w_out, d_m, di.sms, part, w_prep ? xbuf : nullptr, nullptr, st, &gp, w_prep);
   if (rc) return rc;
   const float alpha = expf(log_alpha);
-  if (d_m <= 8 * ROW_THREADS) {  // one CTA per row: the reduce, the norms and the epilogue in registers
-    const int vpt = d_m <= 4 * ROW_THREADS ? 1 : 2;
+  if (d_m <= 12 * ROW_THREADS) {  // one CTA per row: the reduce, the norms and the epilogue in registers
+    const int vpt = (d_m + 4 * ROW_THREADS - 1) / (4 * ROW_THREADS);  // float4 columns per thread: 1..3
     const unsigned thr = (unsigned)std::min<int>(ROW_THREADS, (d_m / 4 + 31) / 32 * 32);
     auto launch = [&](auto kern, auto* hp) {
       launch_pdl(kern, dim3((unsigned)n_rows), dim3(thr), 0, st, part, gp.splits, n_rows, d_m, b_out, scale,
                  log_scale_dev, gate, hp, sel_w, alpha, log_alpha_dev, pos_mask,
                  static_cast<decltype(hp)>(delta_out), static_cast<decltype(hp)>(h_out), rel_out);
     };
+    auto by_vpt = [&](auto* hp) {
+      using TH = std::remove_pointer_t<decltype(hp)>;
+      if (vpt == 1) launch(project_out_row_kernel<TH, 1>, hp);
+      else if (vpt == 2) launch(project_out_row_kernel<TH, 2>, hp);
+      else launch(project_out_row_kernel<TH, 3>, hp);
+    };
     switch (h_dtype) {
-      case XENCB_F32:
-        if (vpt == 1) launch(project_out_row_kernel<float, 1>, static_cast<float*>(const_cast<void*>(h)));
-        else launch(project_out_row_kernel<float, 2>, static_cast<float*>(const_cast<void*>(h)));
-        break;
-      case XENCB_F16:
-        if (vpt == 1) launch(project_out_row_kernel<__half, 1>, static_cast<__half*>(const_cast<void*>(h)));
-        else launch(project_out_row_kernel<__half, 2>, static_cast<__half*>(const_cast<void*>(h)));
-        break;
-      default:
-        if (vpt == 1)
-          launch(project_out_row_kernel<__nv_bfloat16, 1>, static_cast<__nv_bfloat16*>(const_cast<void*>(h)));
-        else
-          launch(project_out_row_kernel<__nv_bfloat16, 2>, static_cast<__nv_bfloat16*>(const_cast<void*>(h)));
-        break;
+      case XENCB_F32: by_vpt(static_cast<float*>(const_cast<void*>(h))); break;
+      case XENCB_F16: by_vpt(static_cast<__half*>(const_cast<void*>(h))); break;
+      default: by_vpt(static_cast<__nv_bfloat16*>(const_cast<void*>(h))); break;
     }
     XENCB_CHECK_LAUNCH("project_out row launch");
     return XENCB_OK;

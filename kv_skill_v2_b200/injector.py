@@ -515,8 +515,9 @@ class LibraryInjector(XEncInjector):
             log_alpha = _on(sel.log_alpha.detach().reshape(1), h2).float()
         idx, wk, w, _ = ops.route(q, pages.S, rows_per_lib=rpl, top_k=self.top_k, route_temp=self.route_temp,
                                   n_chunks_of=pages.n_chunks_of, row_w=sel_col)
+        # with a selector most rows read nothing at most depths: the sparse plan spreads the live rows' work
         r = ops.read_decode(q, pages, idx, wk, rows_per_lib=rpl, read_temp=self.read_temp,
-                            read_softmax=self.read_softmax)
+                            read_softmax=self.read_softmax, sparse=sel_col is not None)
         self.last_route = w.view(*lead, pages.n_chunks)
         if torch.is_grad_enabled():
             self.route_terms.append((li, self.last_route))

@@ -272,8 +272,10 @@ class Pages:
 
 
 def read_decode(q: torch.Tensor, pages: Pages, idx: torch.Tensor, wk: torch.Tensor, *, rows_per_lib: int,
-                read_temp: float = 12.0, read_softmax: bool = True) -> torch.Tensor:
-    """r [R, d_s] float32: the masked two-level read over each row's routed chunks."""
+                read_temp: float = 12.0, read_softmax: bool = True, sparse: bool = False) -> torch.Tensor:
+    """r [R, d_s] float32: the masked two-level read over each row's routed chunks. sparse=True plans for calls
+    in which many rows read nothing (a selector's row mask): 64-row pieces, only the live ones listed on the
+    device (xencb_read_decode_sparse); the same result within float32 rounding."""
     dev = _cuda("read_decode", q, pages.slots, pages.page_of, pages.n_valid, idx, wk)
     q = _f32(q, "q")
     wk = _f32(wk, "wk")
@@ -291,11 +293,12 @@ def read_decode(q: torch.Tensor, pages: Pages, idx: torch.Tensor, wk: torch.Tens
     dt = _hdt(slots, "slots")
     page_rows = pages.page_rows
     with _on_device(dev):
-        ws_bytes = N.lib().xencb_read_decode_workspace(R, k, d_s, page_rows, dt)
+        name = "xencb_read_decode_sparse" if sparse else "xencb_read_decode"
+        ws_bytes = getattr(N.lib(), name + "_workspace")(R, k, d_s, page_rows, dt)
         if ws_bytes == 0:
             N.check(N.EINVAL, "read_decode_workspace")
         ws = _workspace(ws_bytes, dev)
-        N.call("xencb_read_decode", _ptr(q), R, d_s, _ptr(slots), _ptr(_vpool(pages)), dt, slots.shape[0],
+        N.call(name, _ptr(q), R, d_s, _ptr(slots), _ptr(_vpool(pages)), dt, slots.shape[0],
                page_rows * d_s, page_rows,
                _ptr(pages.page_of), _ptr(pages.n_valid), pages.n_chunks, int(rows_per_lib), pages.n_lib,
                _ptr(idx), _ptr(wk), k, float(read_temp), int(bool(read_softmax)), _ptr(r), _ptr(ws),

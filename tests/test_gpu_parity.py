@@ -100,6 +100,44 @@ def test_read_ragged_rows_both_kernels(dev, monkeypatch, kernel, slot_dtype, sof
     _status_clean(dev)
 
 
+@pytest.mark.parametrize("slot_dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("softmax", [True, False])
+@pytest.mark.parametrize("masked", [0.0, 0.75, 1.0])
+def test_read_decode_sparse_matches_dense(dev, slot_dtype, softmax, masked):
+    """The sparse plan (64-row pieces, only the pieces that hold rows listed on the device) against the dense
+    plan and the oracle: a share of the rows masked out (weight 0, as the selector's row mask does; they read
+    nothing), ragged chunks around the 16- and 64-row edges, every row its own Library."""
+    from kv_skill_v2_b200 import ops
+    g = torch.Generator().manual_seed(31)
+    B, C, N, d_s, k = 24, 16, 512, 256, 4
+    ns = torch.randint(1, N + 1, (B, C), generator=g)
+    ns.view(-1)[:8] = torch.tensor([1, 15, 16, 17, 63, 64, 65, 512])
+    K = torch.randn(B * C, N, d_s, generator=g)
+    K = (K / K.norm(dim=-1, keepdim=True)).to(slot_dtype)
+    M = np.arange(N)[None, :] < ns.view(-1, 1).numpy()
+    K[torch.from_numpy(~M)] = 0
+    Kf = K.float().numpy()
+    q = torch.nn.functional.normalize(torch.randn(B, d_s, generator=g), dim=-1)
+    page_of = torch.arange(B * C, dtype=torch.int32).view(B, C)
+    S = torch.from_numpy(np.stack([X.summaries(Kf[b * C:(b + 1) * C], M[b * C:(b + 1) * C]) for b in range(B)]))
+    pages = ops.Pages(slots=K.to(dev).contiguous(), page_of=page_of.to(dev), n_valid=ns.to(torch.int32).to(dev),
+                      S=S.to(dev))
+    row_w = (torch.rand(B, generator=g) >= masked).float()
+    idx, wk, w, _ = ops.route(q.to(dev), pages.S, rows_per_lib=1, top_k=k, route_temp=10.0, row_w=row_w.to(dev))
+    r_dense = ops.read_decode(q.to(dev), pages, idx, wk, rows_per_lib=1, read_temp=12.0, read_softmax=softmax)
+    r_sparse = ops.read_decode(q.to(dev), pages, idx, wk, rows_per_lib=1, read_temp=12.0, read_softmax=softmax,
+                               sparse=True)
+    live = row_w > 0
+    assert (r_sparse.cpu()[~live] == 0).all() and (r_dense.cpu()[~live] == 0).all()
+    if live.any():
+        assert rel_err(r_sparse[live.to(dev)], r_dense[live.to(dev)]) < TOL
+        wn = w.cpu().numpy()
+        ref = np.stack([X.read(q[b:b + 1].numpy(), Kf[b * C:(b + 1) * C], M[b * C:(b + 1) * C], wn[b:b + 1], 12.0,
+                               softmax)[0] for b in range(B) if live[b]])
+        assert rel_err(r_sparse[live.to(dev)], ref) < TOL
+    _status_clean(dev)
+
+
 def test_route_ties_go_to_lower_index(dev):
     from kv_skill_v2_b200 import ops
     S = torch.zeros(1, 6, 8, device=dev)
@@ -210,13 +248,15 @@ def test_selector_kernels_match_reference(dev):
     _status_clean(dev)
 
 
+@pytest.mark.parametrize("dims", [(37, 264, 136), (5, 5120, 2052), (3, 6148, 6144)])
 @pytest.mark.parametrize("hdt", [torch.float32, torch.bfloat16, torch.float16])
-def test_projections_with_gate_selector_mask(dev, hdt):
+def test_projections_with_gate_selector_mask(dev, hdt, dims):
     """project_in / project_out against the oracle with bias, gate, selector rescale, position mask and a
-    low-precision hidden state (cast, residual add and mag term in h's dtype)."""
+    low-precision hidden state (cast, residual add and mag term in h's dtype). Widths cover the one-CTA-per-row
+    reduce kernels with 1, 2 and 3 float4 columns per thread and, past 6144 columns, the chunked kernels."""
     from kv_skill_v2_b200 import ops
     g = torch.Generator().manual_seed(7)
-    R, d_m, d_s = 37, 264, 136
+    R, d_m, d_s = dims
     h = (torch.randn(R, d_m, generator=g) * 2).to(hdt)
     W_in = torch.randn(d_s, d_m, generator=g) * 0.05
     b_in = torch.randn(d_s, generator=g) * 0.1
