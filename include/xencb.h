@@ -138,7 +138,7 @@ XENCB_API int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const v
 
 /* The same read (xenc/injector.py:239-245, 263-265) planned for calls where many rows read nothing: rows whose
  * routing weights are all zero (the LayerSelector's row mask, xenc/selector.py:106-110, makes most tokens skip
- * most depths). Chunks are split into 64-row pieces and a one-CTA pass lists the pieces that hold rows, so the
+ * most depths). Chunks are split into 128-row pieces and a one-CTA pass lists the pieces that hold rows, so the
  * live work spreads over every SM instead of over the few CTAs whose fixed share it falls in. Results match
  * xencb_read_decode within float32 rounding (the split sums are added in a different grouping). Tensor-core
  * (f16 / bf16, tied) reads only; other calls run the plan of xencb_read_decode. Workspace:

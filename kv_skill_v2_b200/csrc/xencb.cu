@@ -410,14 +410,16 @@ int plan_read(int64_t n_rows, int k, int d_s, int page_rows, int dtype, ReadPlan
   p->split_rows = best_rows < 1 ? 1 : best_rows;
   p->sparse = false;
   p->list_bytes = 0;
-  if (sparse && p->mma && !untied && max_split > 1 && pairs * max_split <= INT32_MAX) {
-    // sparse plan: the finest splits (64 rows), only the splits that hold rows listed on the device, so that a
-    // read where few rows take part still spreads over every SM
+  const int sp_split = std::min((page_rows + 127) / 128, MERGE_ENTRIES);
+  if (sparse && p->mma && !untied && pairs * sp_split <= INT32_MAX) {
+    // sparse plan: 128-row pieces (eight 16-row stages; the merge then takes one batch of 16 entries per row at
+    // top-4), only the pieces that hold rows listed on the device, so that a read where few rows take part
+    // still spreads over every SM
     p->sparse = true;
-    p->n_split = max_split;
-    p->split_rows = (page_rows + max_split - 1) / max_split;
+    p->n_split = sp_split;
+    p->split_rows = (page_rows + sp_split - 1) / sp_split;
     p->split_rows = (p->split_rows + 15) / 16 * 16;
-    p->list_bytes = align_up((size_t)pairs * max_split * sizeof(int32_t), 256) + 256;
+    p->list_bytes = align_up((size_t)pairs * sp_split * sizeof(int32_t), 256) + 256;
   }
   p->n_items = pairs * p->n_split;
   p->grid = (int)(p->n_items < grid_max ? p->n_items : grid_max);

@@ -274,7 +274,7 @@ class Pages:
 def read_decode(q: torch.Tensor, pages: Pages, idx: torch.Tensor, wk: torch.Tensor, *, rows_per_lib: int,
                 read_temp: float = 12.0, read_softmax: bool = True, sparse: bool = False) -> torch.Tensor:
     """r [R, d_s] float32: the masked two-level read over each row's routed chunks. sparse=True plans for calls
-    in which many rows read nothing (a selector's row mask): 64-row pieces, only the live ones listed on the
+    in which many rows read nothing (a selector's row mask): 128-row pieces, only the live ones listed on the
     device (xencb_read_decode_sparse); the same result within float32 rounding."""
     dev = _cuda("read_decode", q, pages.slots, pages.page_of, pages.n_valid, idx, wk)
     q = _f32(q, "q")

@@ -104,7 +104,7 @@ def test_read_ragged_rows_both_kernels(dev, monkeypatch, kernel, slot_dtype, sof
 @pytest.mark.parametrize("softmax", [True, False])
 @pytest.mark.parametrize("masked", [0.0, 0.75, 1.0])
 def test_read_decode_sparse_matches_dense(dev, slot_dtype, softmax, masked):
-    """The sparse plan (64-row pieces, only the pieces that hold rows listed on the device) against the dense
+    """The sparse plan (128-row pieces, only the pieces that hold rows listed on the device) against the dense
     plan and the oracle: a share of the rows masked out (weight 0, as the selector's row mask does; they read
     nothing), ragged chunks around the 16- and 64-row edges, every row its own Library."""
     from kv_skill_v2_b200 import ops
