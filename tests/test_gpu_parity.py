@@ -615,10 +615,10 @@ def test_injector_cuda_graph_cache(dev):
         with torch.no_grad():
             outs[graphs] = [reader(x) for x in xs]
             if graphs:
-                assert len(inj._graphs) == 1
+                assert len({k[0] for k in inj._graphs}) == 1  # one captured configuration (per input buffer)
                 inj.gain_scale = 0.5
                 half = reader(xs[0])
-                assert len(inj._graphs) == 2
+                assert len({k[0] for k in inj._graphs}) == 2
                 inj.gain_scale = 1.0
                 inj.load_library(plib)
                 assert len(inj._graphs) == 0
@@ -629,6 +629,55 @@ def test_injector_cuda_graph_cache(dev):
     assert not torch.allclose(outs[True][0], outs[True][1])
     assert torch.allclose(again, outs[False][1], rtol=0, atol=1e-6)
     assert not torch.allclose(half, outs[True][0])
+    _status_clean(dev)
+
+
+def test_injector_graphs_on_caller_buffers(dev):
+    """The first few input buffers a hooked layer sees get graphs captured on the buffers themselves (no copy-in);
+    further ones share a graph with a copy-in. Refilling the buffers in place between steps, as a serving loop
+    does, gives the eager path's results every time."""
+    from kv_skill_v2_b200 import LibraryInjector, LinearInterface, PagedLibrary, ops
+    from kv_skill_v2_b200.injector import _PTR_GRAPHS
+
+    class IdReader(torch.nn.Module):  # the hooked block returns its input: the hook sees the caller's buffer
+        def __init__(self):
+            super().__init__()
+            self.layers = torch.nn.ModuleList([torch.nn.Identity(), torch.nn.Identity()])
+            self._p = torch.nn.Parameter(torch.zeros(1), requires_grad=False)  # the injector finds the device here
+
+        def forward(self, x):
+            for blk in self.layers:
+                x = blk(x)
+            return x
+
+    g = torch.Generator().manual_seed(23)
+    B, C, N, d_s, d_m = 4, 6, 64, 128, 256
+    K = torch.nn.functional.normalize(torch.randn(B * C, N, d_s, generator=g), dim=-1).half().to(dev)
+    po = torch.arange(B * C, dtype=torch.int32, device=dev).view(B, C)
+    nv = torch.full((B, C), N, dtype=torch.int32, device=dev)
+    plib = PagedLibrary({1: ops.Pages(slots=K, page_of=po, n_valid=nv, S=ops.summaries(K, po, nv))})
+    itf = LinearInterface(torch.randn(d_m, d_s, generator=g) * 0.05, torch.randn(d_s, d_m, generator=g) * 0.05,
+                          [1]).to(dev).requires_grad_(False)
+    reader = IdReader().to(dev)
+    n_buf = _PTR_GRAPHS + 2
+    bufs = [torch.empty(B, 1, d_m, device=dev) for _ in range(n_buf)]
+    rounds = [[torch.randn(B, 1, d_m, generator=g).to(dev) for _ in range(n_buf)] for _ in range(2)]
+    ref = LibraryInjector(reader, itf, top_k=2, cuda_graphs=False)
+    ref.load_library(plib)
+    with torch.no_grad():
+        want = [[reader(x.clone()) for x in r] for r in rounds]
+    ref.detach()
+    inj = LibraryInjector(reader, itf, top_k=2)
+    inj.load_library(plib)
+    with torch.no_grad():
+        for r, xr in enumerate(rounds):
+            for i, x in enumerate(xr):
+                bufs[i].copy_(x)
+                y = reader(bufs[i])
+                assert torch.allclose(y, want[r][i], rtol=0, atol=1e-6), (r, i)
+    on_buffer = [k for k in inj._graphs if k[1] is not None]
+    assert len(on_buffer) == _PTR_GRAPHS and any(k[1] is None for k in inj._graphs)
+    inj.detach()
     _status_clean(dev)
 
 
