@@ -100,13 +100,14 @@ def test_read_ragged_rows_both_kernels(dev, monkeypatch, kernel, slot_dtype, sof
     _status_clean(dev)
 
 
-@pytest.mark.parametrize("slot_dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("slot_dtype", [torch.float16, torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("softmax", [True, False])
 @pytest.mark.parametrize("masked", [0.0, 0.75, 1.0])
 def test_read_decode_sparse_matches_dense(dev, slot_dtype, softmax, masked):
     """The sparse plan (128-row pieces, only the pieces that hold rows listed on the device) against the dense
     plan and the oracle: a share of the rows masked out (weight 0, as the selector's row mask does; they read
-    nothing), ragged chunks around the 16- and 64-row edges, every row its own Library."""
+    nothing), ragged chunks around the 16- and 64-row edges, every row its own Library. float32 slots take the
+    CUDA-core read, where the sparse entry runs the dense plan."""
     from kv_skill_v2_b200 import ops
     g = torch.Generator().manual_seed(31)
     B, C, N, d_s, k = 24, 16, 512, 256, 4
