@@ -141,7 +141,7 @@ XENCB_API int xencb_read_decode(const float* q, int64_t n_rows, int d_s, const v
  * most depths). Chunks are split into 128-row pieces and a one-CTA pass lists the pieces that hold rows, so the
  * live work spreads over every SM instead of over the few CTAs whose fixed share it falls in. Results match
  * xencb_read_decode within float32 rounding (the split sums are added in a different grouping). Tensor-core
- * (f16 / bf16, tied) reads only; other calls run the plan of xencb_read_decode. Workspace:
+ * (f16 / bf16, tied) reads of up to 65536 (row, chunk) pairs; other calls run the plan of xencb_read_decode. Workspace:
  * xencb_read_decode_sparse_workspace bytes. */
 XENCB_API size_t xencb_read_decode_sparse_workspace(int64_t n_rows, int k, int d_s, int page_rows, int slots_dtype);
 XENCB_API int xencb_read_decode_sparse(const float* q, int64_t n_rows, int d_s, const void* slots, const void* vslots,

@@ -411,7 +411,7 @@ int plan_read(int64_t n_rows, int k, int d_s, int page_rows, int dtype, ReadPlan
   p->sparse = false;
   p->list_bytes = 0;
   const int sp_split = std::min((page_rows + 127) / 128, MERGE_ENTRIES);
-  if (sparse && p->mma && !untied && pairs * sp_split <= INT32_MAX) {
+  if (sparse && p->mma && !untied && pairs <= 65536 && pairs * sp_split <= INT32_MAX) {  // one CTA lists them
     // sparse plan: 128-row pieces (eight 16-row stages; the merge then takes one batch of 16 entries per row at
     // top-4), only the pieces that hold rows listed on the device, so that a read where few rows take part
     // still spreads over every SM
