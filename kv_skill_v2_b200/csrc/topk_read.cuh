@@ -94,6 +94,56 @@ __global__ void __launch_bounds__(SEL_THREADS) select_scores_kernel(const Select
     if (a.T == 1) {
       // one position: the group's heads share every key load
       const float* qk = qrow + (int64_t)kv * G * a.hd;
+      if constexpr (sizeof(TK) == 2 && G <= 4) {
+        if (a.hd <= 128) {
+          // 16-bit keys, head rows of up to 256 bytes: a half-warp reads one slot's head row in one coalesced
+          // request (lane l: elements [8 (l & 15), +8) of slot 2 j + (l >> 4)), four slot pairs in flight per
+          // lane; the group's q values stay in registers and 16-lane shuffle trees finish the dots
+          const int hl = lane & 15, half = lane >> 4;
+          const bool el = hl * 8 < a.hd;
+          float qv[G][8];
+#pragma unroll
+          for (int h = 0; h < G; ++h) {
+            float4 q0 = make_float4(0.f, 0.f, 0.f, 0.f), q1 = q0;
+            if (el) {
+              q0 = __ldg(reinterpret_cast<const float4*>(qk + h * a.hd + hl * 8));
+              q1 = __ldg(reinterpret_cast<const float4*>(qk + h * a.hd + hl * 8 + 4));
+            }
+            qv[h][0] = q0.x; qv[h][1] = q0.y; qv[h][2] = q0.z; qv[h][3] = q0.w;
+            qv[h][4] = q1.x; qv[h][5] = q1.y; qv[h][6] = q1.z; qv[h][7] = q1.w;
+          }
+          constexpr int SU = 4;
+          for (int sp = 0; sp < SEL_TILE; sp += 2 * SU) {
+            uint4 raw[SU];
+#pragma unroll
+            for (int u = 0; u < SU; ++u) {
+              const int slot = base + sp + 2 * u + half;
+              const int sl = slot < S ? slot : 0;  // slots past S read slot 0, never stored
+              raw[u] = el ? __ldg(reinterpret_cast<const uint4*>(kb + (int64_t)sl * d_k + kv * a.hd + hl * 8))
+                          : make_uint4(0u, 0u, 0u, 0u);
+            }
+#pragma unroll
+            for (int u = 0; u < SU; ++u) {
+              float kx[8];
+              unpack16<TK>(raw[u], kx);
+              float pv = init_h;
+#pragma unroll
+              for (int h = 0; h < G; ++h) {
+                float d = 0.f;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) d = fmaf(qv[h][e], kx[e], d);
+                d += __shfl_xor_sync(0xffffffffu, d, 8);
+                d += __shfl_xor_sync(0xffffffffu, d, 4);
+                d += __shfl_xor_sync(0xffffffffu, d, 2);
+                d += __shfl_xor_sync(0xffffffffu, d, 1);
+                pv = a.h_pool == 0 ? fmaxf(pv, d) : pv + d;
+              }
+              if (hl == 0) red[kv][sp + 2 * u + half] = pv;
+            }
+          }
+          continue;
+        }
+      }
       float acc[SEL_SPT][G];
 #pragma unroll
       for (int u = 0; u < SEL_SPT; ++u)
