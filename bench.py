@@ -1077,7 +1077,10 @@ def run_ours(args) -> None:
         return
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Gaussian unit slots, random weights)",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded Gaussian unit slots, random weights)",
+            "precision": "read: f16 slot, q and p operands with fp32 accumulate (q and the softmax weights p are "
+                         "rounded to f16 before the tensor-core products); projections: fp32-faithful 3xF16 "
+                         "(about 22-bit operands, fp32 accumulate); routing logits and softmax in fp32",
             "config": config_dict(docs),
             "roofline": {"bound": "hbm", "kernel": "read_decode_mma_kernel",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,

@@ -159,7 +159,9 @@ XENCB_API int xencb_read_decode_sparse(const float* q, int64_t n_rows, int d_s, 
  * GPU that loads the library keeps until the process exits. A call whose scratch need
  * (xencb_read_decode_workspace) exceeds it returns XENCB_EINVAL and launches nothing. The first call on each
  * device looks up that array's device address (cudaGetSymbolAddress) with the device current; make that first
- * call before any stream capture. All calls share the one array: calls on one device that overlap on the GPU
+ * call before any stream capture. The address is kept for the life of the process: it does not survive
+ * cudaDeviceReset or any other teardown of the device's primary context, after which this entry point must not
+ * be called again in that process. All calls share the one array: calls on one device that overlap on the GPU
  * (issued to different streams) race and corrupt each other's results, so serialise them. Nothing in the
  * array needs to start at zero: the merge uses only words written earlier in the same call (it may load the
  * stale words of splits that hold no rows, and discards them). */

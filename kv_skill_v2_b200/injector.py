@@ -482,6 +482,7 @@ class LibraryInjector(XEncInjector):
                 n_ptr = sum(1 for k in self._graphs if k[0] == base)
                 on_buffer = n_ptr < _PTR_GRAPHS
                 out = self._run_lib_eager(h, li, inject, sel)
+                route_eager = self.last_route
                 h_static = h.detach() if on_buffer else h.detach().clone()
                 graph = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(graph):
@@ -490,6 +491,8 @@ class LibraryInjector(XEncInjector):
                 self._graphs[(base, h.data_ptr() if on_buffer else None)] = (
                     graph, None if on_buffer else h_static, h_new_s, rel_s, self.last_route, pages,
                     list(self._wprep.values()))
+                # the captured step has not run yet: this call's routing is the eager run's
+                self.last_route = route_eager
                 return out
         graph, h_static, h_new_s, rel_s, route_s, _, _ = ent
         if h_static is not None:

@@ -1,8 +1,8 @@
 """Generate the golden fixtures under tests/golden/ by running the REFERENCE's own Library read.
 
-Run in a container that has the reference checkout (read-only) at $XENC_REF (default /root/reference):
+Run where a checkout of the reference exists, naming its root in XENC_REF (there is no default):
 
-    python tests/golden/make_golden.py
+    XENC_REF=<path to the reference checkout> python tests/golden/make_golden.py
 
 It imports the reference's unchanged `xenc.library.Library`, `xenc.injector.LibraryInjector` and
 `xenc.selector.LayerSelector`. Their dependency `deltaskill` is not vendored in the reference (it is a
@@ -35,7 +35,7 @@ import torch
 import torch.nn as nn
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("XENC_REF", "/root/reference"))
+REF = Path(os.environ["XENC_REF"]) if os.environ.get("XENC_REF") else None
 
 
 # ------------------------------------------------------------------------------------ deltaskill stand-in
@@ -508,6 +508,8 @@ def gen_topk(out):
 
 
 def main() -> None:
+    if REF is None:
+        raise SystemExit("set XENC_REF to the root of a reference checkout (the directory holding xenc/)")
     if not (REF / "xenc" / "injector.py").exists():
         raise SystemExit(f"reference checkout not found at {REF}")
     sys.path.insert(0, str(REF))

@@ -34,7 +34,7 @@ def _status_clean(dev):
 # ------------------------------------------------------------------------------------------------ kernels
 @pytest.mark.parametrize("keys_dtype", [torch.float16, torch.float32])
 @pytest.mark.parametrize("geom", [(2, 2, 8), (8, 4, 128), (1, 16, 64), (4, 1, 32)])  # (n_kv, groups, hd)
-@pytest.mark.parametrize("mode", [("last", "max"), ("all_max", "mean"), ("all_mean", "max")])
+@pytest.mark.parametrize("mode", [("last", "max"), ("last", "mean"), ("all_max", "mean"), ("all_mean", "max")])
 def test_select_scores_against_oracle(dev, keys_dtype, geom, mode):
     from kv_skill_v2_b200 import ops
     n_kv, groups, hd = geom
