@@ -23,11 +23,13 @@ __device__ unsigned int g_dev_status = 0;
 __device__ __forceinline__ void flag_error(unsigned int bits) { atomicOr(&g_dev_status, bits); }
 
 // Programmatic dependent launch (the kernels the host launches with programmatic stream serialisation: the read
-// merge, the row split, the 3xF16 GEMM and the projection row kernels). pdl_wait() returns once the grid before
-// this one in the stream has completed and its writes are visible (a no-op for a plain launch); such a kernel
-// touches global memory only after it, apart from reads that no kernel of the step writes (the GEMM's weight
-// tiles). pdl_trigger() lets the next grid be scheduled; it is issued after pdl_wait(), except in the row split,
-// whose successor's early work reads only the weights.
+// merge, the row split, the 3xF16 GEMM, the projection row kernels and the fused decode router). pdl_wait()
+// returns once the grid before this one in the stream has completed and its writes are visible (a no-op for a
+// plain launch). Before it such a kernel only reads, and only data that no kernel still running can be writing:
+// the GEMM's weight tiles and the router's summary keys (Library data), and the row kernels' hidden-state rows
+// (they start after the GEMM has passed its own wait, so the kernel that wrote h has completed). Nothing is written
+// before the wait. pdl_trigger() lets the next grid be scheduled; the row split and the row kernels issue it first
+// thing (their successors' early work is such a read), the others after their wait.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
@@ -208,6 +210,12 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
       ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
+}
+
+// Ask L2 to fetch [gmem_src, gmem_src + bytes) from HBM (no shared memory, no completion to wait for): a later
+// copy of the same bytes finds them in L2. `bytes` and the address must be multiples of 16.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* gmem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gmem_src), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ uint64_t policy_evict_first() {

@@ -328,10 +328,24 @@ __global__ void __launch_bounds__(ROW_THREADS) project_in_row_kernel(
   __shared__ float2 red2[32];
   __shared__ float red[32];
   __shared__ float zsh[32];
-  pdl_wait();
+  // The pass over h runs before the wait: this kernel starts only after the GEMM passed its own wait, so the row
+  // split that read h, and the kernel that wrote it, have completed. Nothing is written before the wait.
   pdl_trigger();
   const int64_t row = blockIdx.x;
   const TH* hr = h + row * d_m;
+  float ss, gd, unused;
+  row_dots<TH>(hr, d_m, gate_w, nullptr, ss, gd, unused);
+  if (sel_w) {  // the selector's logit dots, scaled by 1/rms below
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int c = wid; c < n_cand; c += nw) {
+      const float* u = sel_w + (int64_t)c * d_m;
+      float d = 0.f;
+      for (int i = lane; i < d_m; i += 32) d = fmaf(to_f32(hr[i]), u[i], d);
+      d = warp_sum(d);
+      if (lane == 0) zsh[c] = d;
+    }
+  }
+  pdl_wait();
   int n[VPT];
   bool ok[VPT];
 #pragma unroll
@@ -341,9 +355,7 @@ __global__ void __launch_bounds__(ROW_THREADS) project_in_row_kernel(
   }
   float4 v[VPT];
   sum_splits_row<VPT>(part, splits, M, d_s, row, n, ok, v);
-  float ss, gd, unused;
-  row_dots<TH>(hr, d_m, gate_w, nullptr, ss, gd, unused);
-  const float2 t = block_sum2(ss, gd, red2);
+  const float2 t = block_sum2(ss, gd, red2);  // (its barrier also publishes zsh)
   const float rstd = (flags & XENCB_PIN_RMS) ? rsqrtf(t.x / (float)d_m + eps) : 1.f;
   if (threadIdx.x == 0) {
     if (rstd_out) rstd_out[row] = rstd;
@@ -352,18 +364,8 @@ __global__ void __launch_bounds__(ROW_THREADS) project_in_row_kernel(
       gate_out[row] = 1.f / (1.f + expf(-(t.y * rstd + gb)));
     }
   }
-  if (sel_w) {
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (int c = wid; c < n_cand; c += nw) {
-      const float* u = sel_w + (int64_t)c * d_m;
-      float d = 0.f;
-      for (int i = lane; i < d_m; i += 32) d = fmaf(to_f32(hr[i]), u[i], d);
-      d = warp_sum(d);
-      if (lane == 0) zsh[c] = d * rstd + (sel_b ? sel_b[c] : 0.f);
-    }
-    __syncthreads();
-    if (threadIdx.x < n_cand) z_out[row * n_cand + threadIdx.x] = zsh[threadIdx.x];
-  }
+  if (sel_w && threadIdx.x < n_cand)
+    z_out[row * n_cand + threadIdx.x] = zsh[threadIdx.x] * rstd + (sel_b ? sel_b[threadIdx.x] : 0.f);
   float4 o[VPT];
   float nq = 0.f;
 #pragma unroll
@@ -515,7 +517,8 @@ __global__ void __launch_bounds__(ROW_THREADS) project_out_row_kernel(
     const float* __restrict__ pos_mask, TH* delta_out, TH* h_out, float* __restrict__ rel_out) {
   __shared__ float2 red2[32];
   __shared__ float red[32];
-  pdl_wait();
+  // h is the hook's input, complete before the step's first kernel: its row is read (and ||h|| summed) before the
+  // wait; the next kernel may start its own early work now. Nothing is written before the wait.
   pdl_trigger();
   const int64_t row = blockIdx.x;
   int n[VPT];
@@ -525,16 +528,21 @@ __global__ void __launch_bounds__(ROW_THREADS) project_out_row_kernel(
     n[q] = (threadIdx.x + q * blockDim.x) * 4;
     ok[q] = n[q] < d_m;
   }
-  float4 v[VPT];
-  sum_splits_row<VPT>(part, splits, M, d_m, row, n, ok, v);
   float hx[VPT][4];
+  float hh = 0.f;
 #pragma unroll
   for (int q = 0; q < VPT; ++q)
 #pragma unroll
-    for (int u = 0; u < 4; ++u) hx[q][u] = ok[q] ? to_f32(h[row * d_m + n[q] + u]) : 0.f;
+    for (int u = 0; u < 4; ++u) {
+      hx[q][u] = ok[q] ? to_f32(h[row * d_m + n[q] + u]) : 0.f;
+      hh = fmaf(hx[q][u], hx[q][u], hh);
+    }
+  pdl_wait();
+  float4 v[VPT];
+  sum_splits_row<VPT>(part, splits, M, d_m, row, n, ok, v);
   const float g = (gate ? gate[row] : 1.f) * scale * (log_scale_dev ? expf(__ldg(log_scale_dev)) : 1.f);
   float o[VPT][4];
-  float dd = 0.f, hh = 0.f;
+  float dd = 0.f;
 #pragma unroll
   for (int q = 0; q < VPT; ++q) {
     const int c = n[q];
@@ -543,8 +551,6 @@ __global__ void __launch_bounds__(ROW_THREADS) project_out_row_kernel(
     o[q][2] = ok[q] ? g * (v[q].z + (b_out ? b_out[c + 2] : 0.f)) : 0.f;
     o[q][3] = ok[q] ? g * (v[q].w + (b_out ? b_out[c + 3] : 0.f)) : 0.f;
     dd += o[q][0] * o[q][0] + o[q][1] * o[q][1] + o[q][2] * o[q][2] + o[q][3] * o[q][3];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) hh = fmaf(hx[q][u], hx[q][u], hh);
   }
   const float2 t = block_sum2(dd, hh, red2);
   const float hnorm = sqrtf(t.y);

@@ -297,9 +297,23 @@ __global__ void __cluster_dims__(RF_CL, 1, 1) __launch_bounds__(256) route_fused
   // first dot product (its loads are in flight meanwhile).
   asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
   {
-    const int t0 = rank * 8 + w, r0 = t0 / C;
-    if (t0 < rpc * C && row0 + r0 < n_rows)
-      prefetch_row_l2(S + ((row0 + r0) / rows_per_lib * C + (t0 - r0 * C)) * (int64_t)d_s, d_s, lane);
+    // Launched with programmatic serialisation: the S rows of this warp's dot products (Library data that no kernel
+    // of the step writes) are requested from HBM before the wait for q, so they stream in while the input
+    // projection finishes.
+    for (int t = rank * 8 + w; t < rpc * C; t += RF_CL * 8) {
+      const int r = t / C, c = t - r * C;
+      const int64_t row = row0 + r;
+      if (row >= n_rows) break;
+      const int64_t lib = row / rows_per_lib;
+      if (c >= (n_chunks_of ? min(n_chunks_of[lib], C) : C)) continue;
+      const float* sr = S + (lib * C + c) * (int64_t)d_s;
+      if ((d_s & 3) == 0) {
+        if (lane == 0) prefetch_l2_bulk(sr, (uint32_t)d_s * 4u);
+      } else {
+        prefetch_row_l2(sr, d_s, lane);
+      }
+    }
+    pdl_wait();
     const int64_t n_q = (min(n_rows, row0 + rpc) - row0) * (int64_t)d_s;
     for (int64_t i = threadIdx.x; i < n_q; i += blockDim.x) rf_sh[i] = q[row0 * d_s + i];
     __syncthreads();

@@ -772,10 +772,10 @@ int xencb_route(const float* q, int64_t n_rows, int d_s, const float* S, int n_c
   if (rows_per_lib < 64 && n_chunks <= 128 && fsmem <= 96 * 1024 && n_clusters * RF_CL <= INT32_MAX) {
     int rc = ensure_smem(route_fused_kernel, (int)std::max<size_t>(fsmem, 48 * 1024));
     if (rc) return rc;
-    // a plain launch: started early beside the projection's row kernel, its S traffic slowed that kernel down
-    route_fused_kernel<<<(unsigned)(n_clusters * RF_CL), 256, fsmem, st>>>(
-        q, n_rows, d_s, S, n_chunks, n_chunks_of, rows_per_lib, route_temp, rpc, top_k, k_out, row_w, idx, wk,
-        w_dense, logit_out);
+    // programmatic serialisation: the kernel requests its S rows before it waits for q (the input projection)
+    launch_pdl(route_fused_kernel, dim3((unsigned)(n_clusters * RF_CL)), dim3(256), fsmem, st, q, n_rows, d_s, S,
+               n_chunks, n_chunks_of, rows_per_lib, route_temp, rpc, top_k, k_out, row_w, idx, wk, w_dense,
+               logit_out);
     XENCB_CHECK_LAUNCH("route_fused launch");
     return XENCB_OK;
   }

@@ -514,23 +514,29 @@ class LibraryInjector(XEncInjector):
         rpl = self._rows_per_lib(h, pages)
 
         fuse_sel = sel is not None and self._fast_interface() and li == sel.first_layer and not sel._explicit
+        # the selector's weights for this layer come first: tokens it gives weight 0 here read nothing (the
+        # reference reads every layer for every token and zeroes the delta afterwards, xenc/selector.py:106-110).
+        # Unless the input projection computes them (fused logits), they are taken before it, so that the router
+        # follows the projection directly in the stream and can start on its summary keys early.
+        sel_col, log_alpha = None, 0.0
+
+        def sel_column():
+            return (sel._w[..., sel.pos[li]].reshape(-1).float().contiguous(),
+                    _on(sel.log_alpha.detach().reshape(1), h2).float())
+
+        if sel is not None and not fuse_sel:
+            sel.weights_for(h, li)
+            sel_col, log_alpha = sel_column()
         if self._fast_interface():
             q, g, log_gain, z = self._query(h2, li, sel_fuse=sel if fuse_sel else None)
         else:
             hn = ops.rms_norm(h2)
             q = self.itf.query(hn.view(*lead, -1)).reshape(-1, self.itf.d_s).float().contiguous()
             z = None
-        # the selector's weights for this layer come first: tokens it gives weight 0 here read nothing (the
-        # reference reads every layer for every token and zeroes the delta afterwards, xenc/selector.py:106-110)
-        sel_col, log_alpha = None, 0.0
-        if sel is not None:
-            if fuse_sel:
-                sel._w = sel._weights_from_logits(z.view(*lead, sel.n_cand))
-                sel._explicit = False
-            else:
-                sel.weights_for(h, li)
-            sel_col = sel._w[..., sel.pos[li]].reshape(-1).float().contiguous()
-            log_alpha = _on(sel.log_alpha.detach().reshape(1), h2).float()
+        if fuse_sel:
+            sel._w = sel._weights_from_logits(z.view(*lead, sel.n_cand))
+            sel._explicit = False
+            sel_col, log_alpha = sel_column()
         idx, wk, w, _ = ops.route(q, pages.S, rows_per_lib=rpl, top_k=self.top_k, route_temp=self.route_temp,
                                   n_chunks_of=pages.n_chunks_of, row_w=sel_col)
         # with a selector most rows read nothing at most depths: the sparse plan spreads the live rows' work
