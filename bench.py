@@ -880,8 +880,8 @@ def run_ours(args) -> None:
     P_in, P_out = ops.weights_prep(W_in), ops.weights_prep(W_out)
 
     def step(h, h_out):
-        q, _, _, _ = ops.project_in(h, W_in, w_prep=P_in)
-        idx, wk, _, _ = ops.route(q, pages.S, rows_per_lib=CFG["T"], top_k=CFG["top_k"], route_temp=CFG["route_temp"])
+        q, _, _, idx, wk, _, _ = ops.project_in_route(h, W_in, S=pages.S, rows_per_lib=CFG["T"], top_k=CFG["top_k"],
+                                                      route_temp=CFG["route_temp"], w_prep=P_in)
         r = ops.read_decode(q, pages, idx, wk, rows_per_lib=CFG["T"], read_temp=CFG["read_temp"])
         _, _, rel = ops.project_out(r, W_out, h, want_delta=False, h_out=h_out, want_rel=True, w_prep=P_out)
         return q, idx, wk, rel

@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define XENCB_ABI_VERSION 3
+#define XENCB_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define XENCB_API __attribute__((visibility("default")))
@@ -114,6 +114,21 @@ XENCB_API int xencb_route_k(int top_k, int n_chunks);
 XENCB_API int xencb_route(const float* q, int64_t n_rows, int d_s, const float* S, int n_chunks, const int32_t* n_chunks_of,
                 int64_t rows_per_lib, int64_t n_lib, float route_temp, int top_k, const float* row_w,
                 int32_t* idx, float* wk, float* w_dense, float* logit_out, void* stream);
+
+/* Decode form of xencb_project_in followed by xencb_route (xenc/injector.py:235-236, :54-58 and :220-229 in one
+ * pass after the projection GEMM): each row's q is L2-normalised and routed in the same CTA, with the row's
+ * summary keys fetched while the GEMM runs. Arguments as the two calls (the route's q is q_out); the outputs are
+ * the same values (q bit for bit, the logits summed in the same order). Takes decode rows only: rows_per_lib < 64,
+ * flags with XENCB_PIN_L2, d_s <= 6144 and (d_s + 2 * n_chunks) * 4 bytes <= 96 KiB; anything else returns
+ * XENCB_ENOTSUP and launches nothing (use the two calls). Workspace: xencb_project_in_workspace bytes. */
+XENCB_API int xencb_project_in_route(const void* h, int h_dtype, int64_t n_rows, int d_m, const float* w_in,
+                                     const void* w_prep, const float* b_in, int d_s, int flags, const float* gate_w,
+                                     float gate_b, const float* gate_b_dev, const float* sel_w, const float* sel_b,
+                                     int n_cand, float rms_eps, float* q_out, float* gate_out, float* rstd_out,
+                                     float* z_out, const float* S, int n_chunks, const int32_t* n_chunks_of,
+                                     int64_t rows_per_lib, int64_t n_lib, float route_temp, int top_k,
+                                     const float* row_w, int32_t* idx, float* wk, float* w_dense, float* logit_out,
+                                     void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------
  * Masked decode read over the routed chunks. Replaces the read of LibraryInjector._branch

@@ -261,17 +261,22 @@ __global__ void __launch_bounds__(H3_THREADS, MINB) gemm_f16x3_kernel(const __gr
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int n = n0 + q * 32 + lane;
     float* out = part + (int64_t)blockIdx.z * M * N;
+    // the scales are read while the MMAs run: one row scale per lane (rows m0 + lane, m0 + 32 + lane), handed to
+    // the other lanes by shuffles; only the accumulator columns that hold rows are read back
+    const float iw = *w_inv_scale;
+    const float xs0 = m0 + lane < M ? x_inv_scale[m0 + lane] : 0.f;
+    const float xs1 = m0 + 32 + lane < M ? x_inv_scale[m0 + 32 + lane] : 0.f;
+    const int rows = (int)min((int64_t)H3_BN, M - m0);
     const bool ok = nkb > 0 && mbar_wait_bounded(done, 0) && !*abort_flag;
     tc_fence_after();
-    const float iw = *w_inv_scale;
+    for (int c = 0; c < rows; c += 32) {
+      float v[32];
+      tc_ld32(taddr + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
+      const float xs = c == 0 ? xs0 : xs1;
 #pragma unroll
-    for (int c = 0; c < H3_BN; c += 16) {
-      float v[16];
-      tc_ld16(taddr + ((uint32_t)(q * 32) << 16) + (uint32_t)c, v);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int64_t m = m0 + c + i;
-        if (m < M && n < N) out[m * N + n] = ok ? v[i] * iw * __ldg(x_inv_scale + m) : 0.f;
+      for (int i = 0; i < 32; ++i) {
+        const float sm = __shfl_sync(0xffffffffu, xs, i);
+        if (c + i < rows && n < N) out[(m0 + c + i) * N + n] = ok ? v[i] * iw * sm : 0.f;
       }
     }
   }

@@ -314,73 +314,89 @@ __global__ void __launch_bounds__(256) project_in_reduce_kernel(
 }
 
 // project_in after the GEMM in one launch when a row fits one CTA (d_s <= 4 * ROW_THREADS * VPT): thread t owns
-// the float4 column groups t + v * blockDim.x. Its split partials are requested first, then the pass over h (sum
-// of squares, gate dot); one two-value block sum gives 1/rms and the gate; q = (sum of splits) * rstd + b stays in
-// registers for the L2 norm (||q|| + 1e-6, xenc/injector.py:58), so nothing is written twice. The selector
-// logits (chunk 0's job in project_in_reduce_kernel) are the same warp dots.
+// the float4 column groups t + v * blockDim.x. The pass over h (sum of squares, gate dot, the selector's logit
+// dots) runs before the wait for the GEMM: this kernel starts only after the GEMM passed its own wait, so the row
+// split that read h, and the kernel that wrote it, have completed; nothing is written before the wait. Then the
+// split partials; one two-value block sum gives 1/rms and the gate; q = (sum of splits) * rstd + b stays in
+// registers for the L2 norm (||q|| + 1e-6, xenc/injector.py:58), so nothing is written twice.
+// The two halves are shared with the fused decode router (route.cuh), which continues from q in registers.
 constexpr int ROW_THREADS = 512;
-template <typename TH, int VPT>
-__global__ void __launch_bounds__(ROW_THREADS) project_in_row_kernel(
-    const TH* __restrict__ h, int d_m, const float* __restrict__ part, int splits, int64_t M, int d_s, int flags,
-    const float* __restrict__ b_in, const float* __restrict__ gate_w, float gate_b, const float* __restrict__ gate_b_dev,
-    const float* __restrict__ sel_w, const float* __restrict__ sel_b, int n_cand, float eps,
-    float* __restrict__ q_out, float* __restrict__ gate_out, float* __restrict__ rstd_out, float* __restrict__ z_out) {
-  __shared__ float2 red2[32];
-  __shared__ float red[32];
-  __shared__ float zsh[32];
-  // The pass over h runs before the wait: this kernel starts only after the GEMM passed its own wait, so the row
-  // split that read h, and the kernel that wrote it, have completed. Nothing is written before the wait.
-  pdl_trigger();
-  const int64_t row = blockIdx.x;
-  const TH* hr = h + row * d_m;
+
+struct PinArgs {
+  int d_m;
+  const float* part;
+  int splits;
+  int64_t M;
+  int d_s, flags;
+  const float* b_in;
+  const float* gate_w;
+  float gate_b;
+  const float* gate_b_dev;
+  const float* sel_w;
+  const float* sel_b;
+  int n_cand;
+  float eps;
+  float* q_out;
+  float* gate_out;
+  float* rstd_out;
+  float* z_out;
+};
+
+// First half (before the wait): (sum of h^2, gate dot); the selector's logit dots go to zsh[n_cand].
+template <typename TH>
+__device__ __forceinline__ float2 pin_row_pre(const TH* __restrict__ hr, const PinArgs& a, float* zsh) {
   float ss, gd, unused;
-  row_dots<TH>(hr, d_m, gate_w, nullptr, ss, gd, unused);
-  if (sel_w) {  // the selector's logit dots, scaled by 1/rms below
+  row_dots<TH>(hr, a.d_m, a.gate_w, nullptr, ss, gd, unused);
+  if (a.sel_w) {
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (int c = wid; c < n_cand; c += nw) {
-      const float* u = sel_w + (int64_t)c * d_m;
+    for (int c = wid; c < a.n_cand; c += nw) {
+      const float* u = a.sel_w + (int64_t)c * a.d_m;
       float d = 0.f;
-      for (int i = lane; i < d_m; i += 32) d = fmaf(to_f32(hr[i]), u[i], d);
+      for (int i = lane; i < a.d_m; i += 32) d = fmaf(to_f32(hr[i]), u[i], d);
       d = warp_sum(d);
       if (lane == 0) zsh[c] = d;
     }
   }
-  pdl_wait();
-  int n[VPT];
-  bool ok[VPT];
+  return make_float2(ss, gd);
+}
+
+// Second half (after the wait): q's columns n[v] (ok[v]: inside d_s) in o[v], written to q_out; 1/rms, the gate
+// and the selector logits written too.
+template <int VPT>
+__device__ __forceinline__ void pin_row_post(const PinArgs& a, int64_t row, float2 pre, const float* zsh,
+                                             float2* red2, float* red, float4* o, int* n, bool* ok) {
 #pragma unroll
   for (int q = 0; q < VPT; ++q) {
     n[q] = (threadIdx.x + q * blockDim.x) * 4;
-    ok[q] = n[q] < d_s;
+    ok[q] = n[q] < a.d_s;
   }
   float4 v[VPT];
-  sum_splits_row<VPT>(part, splits, M, d_s, row, n, ok, v);
-  const float2 t = block_sum2(ss, gd, red2);  // (its barrier also publishes zsh)
-  const float rstd = (flags & XENCB_PIN_RMS) ? rsqrtf(t.x / (float)d_m + eps) : 1.f;
+  sum_splits_row<VPT>(a.part, a.splits, a.M, a.d_s, row, n, ok, v);
+  const float2 t = block_sum2(pre.x, pre.y, red2);  // (its barrier also publishes zsh)
+  const float rstd = (a.flags & XENCB_PIN_RMS) ? rsqrtf(t.x / (float)a.d_m + a.eps) : 1.f;
   if (threadIdx.x == 0) {
-    if (rstd_out) rstd_out[row] = rstd;
-    if (gate_w) {
-      const float gb = gate_b_dev ? __ldg(gate_b_dev) : gate_b;
-      gate_out[row] = 1.f / (1.f + expf(-(t.y * rstd + gb)));
+    if (a.rstd_out) a.rstd_out[row] = rstd;
+    if (a.gate_w) {
+      const float gb = a.gate_b_dev ? __ldg(a.gate_b_dev) : a.gate_b;
+      a.gate_out[row] = 1.f / (1.f + expf(-(t.y * rstd + gb)));
     }
   }
-  if (sel_w && threadIdx.x < n_cand)
-    z_out[row * n_cand + threadIdx.x] = zsh[threadIdx.x] * rstd + (sel_b ? sel_b[threadIdx.x] : 0.f);
-  float4 o[VPT];
+  if (a.sel_w && threadIdx.x < a.n_cand)
+    a.z_out[row * a.n_cand + threadIdx.x] = zsh[threadIdx.x] * rstd + (a.sel_b ? a.sel_b[threadIdx.x] : 0.f);
   float nq = 0.f;
 #pragma unroll
   for (int q = 0; q < VPT; ++q) {
     o[q] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (ok[q]) {
       const int c = n[q];
-      o[q].x = v[q].x * rstd + (b_in ? b_in[c] : 0.f);
-      o[q].y = v[q].y * rstd + (b_in ? b_in[c + 1] : 0.f);
-      o[q].z = v[q].z * rstd + (b_in ? b_in[c + 2] : 0.f);
-      o[q].w = v[q].w * rstd + (b_in ? b_in[c + 3] : 0.f);
+      o[q].x = v[q].x * rstd + (a.b_in ? a.b_in[c] : 0.f);
+      o[q].y = v[q].y * rstd + (a.b_in ? a.b_in[c + 1] : 0.f);
+      o[q].z = v[q].z * rstd + (a.b_in ? a.b_in[c + 2] : 0.f);
+      o[q].w = v[q].w * rstd + (a.b_in ? a.b_in[c + 3] : 0.f);
       nq += o[q].x * o[q].x + o[q].y * o[q].y + o[q].z * o[q].z + o[q].w * o[q].w;
     }
   }
-  if (flags & XENCB_PIN_L2) {
+  if (a.flags & XENCB_PIN_L2) {
     nq = block_sum(nq, red);
     const float den = sqrtf(nq) + 1e-6f;
 #pragma unroll
@@ -388,7 +404,22 @@ __global__ void __launch_bounds__(ROW_THREADS) project_in_row_kernel(
   }
 #pragma unroll
   for (int q = 0; q < VPT; ++q)
-    if (ok[q]) *reinterpret_cast<float4*>(q_out + row * d_s + n[q]) = o[q];
+    if (ok[q]) *reinterpret_cast<float4*>(a.q_out + row * a.d_s + n[q]) = o[q];
+}
+
+template <typename TH, int VPT>
+__global__ void __launch_bounds__(ROW_THREADS) project_in_row_kernel(const TH* __restrict__ h, const PinArgs a) {
+  __shared__ float2 red2[32];
+  __shared__ float red[32];
+  __shared__ float zsh[32];
+  pdl_trigger();
+  const int64_t row = blockIdx.x;
+  const float2 pre = pin_row_pre<TH>(h + row * a.d_m, a, zsh);
+  pdl_wait();
+  float4 o[VPT];
+  int n[VPT];
+  bool ok[VPT];
+  pin_row_post<VPT>(a, row, pre, zsh, red2, red, o, n, ok);
 }
 
 // X as float32 rows for the TMA path (hidden states stored in 16-bit types).

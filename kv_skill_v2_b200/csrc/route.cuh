@@ -12,6 +12,7 @@
 #include <cooperative_groups.h>
 
 #include "common.cuh"
+#include "project.cuh"
 
 namespace xencb {
 
@@ -273,6 +274,66 @@ __global__ void __launch_bounds__(TOPK_WARPS * 32) route_topk_kernel(
   const int nc = n_chunks_of ? min(n_chunks_of[lib], C) : C;
   topk_row(logit + row * C, sv_all + (int64_t)w * C, C, nc, top_k, k_out, row_w ? row_w[row] : 1.f,
            idx + row * k_out, wk + row * k_out, w_dense ? w_dense + row * C : nullptr, lane);
+}
+
+// Decode: the input projection's row pass (project.cuh) and the routing of the same row in one CTA per row, so q
+// never leaves the CTA between the two: the row's summary keys are requested from HBM before the wait for the
+// GEMM (Library data that no kernel of the step writes), q is kept in shared memory once normalised, each warp
+// takes the dot products of chunks w, w + n_warps, ... with the S rows now in L2 (route_dot: the same sums in
+// the same order as route_fused_kernel), and warp 0 runs topk_row. Dynamic smem: q [d_s], the logits [C] and the
+// top-k scratch [C] floats.
+struct RouteFuse {
+  const float* S;
+  int C;
+  const int32_t* n_chunks_of;
+  int64_t rows_per_lib;
+  float temp;
+  int top_k, k_out;
+  const float* row_w;
+  int32_t* idx;
+  float* wk;
+  float* w_dense;
+  float* logit_out;
+};
+
+template <typename TH, int VPT>
+__global__ void __launch_bounds__(ROW_THREADS) project_in_route_kernel(const TH* __restrict__ h, const PinArgs a,
+                                                                      const RouteFuse rf) {
+  extern __shared__ float pr_sh[];
+  __shared__ float2 red2[32];
+  __shared__ float red[32];
+  __shared__ float zsh[32];
+  pdl_trigger();
+  const int64_t row = blockIdx.x;
+  const int64_t lib = row / rf.rows_per_lib;
+  const int nc = rf.n_chunks_of ? min(rf.n_chunks_of[lib], rf.C) : rf.C;
+  const float* s_lib = rf.S + lib * rf.C * (int64_t)a.d_s;
+  for (int c = threadIdx.x; c < nc; c += blockDim.x) prefetch_l2_bulk(s_lib + (int64_t)c * a.d_s, (uint32_t)a.d_s * 4u);
+  const float2 pre = pin_row_pre<TH>(h + row * a.d_m, a, zsh);
+  pdl_wait();
+  float4 o[VPT];
+  int n[VPT];
+  bool ok[VPT];
+  pin_row_post<VPT>(a, row, pre, zsh, red2, red, o, n, ok);
+  float* qs = pr_sh;
+  float* lg = pr_sh + a.d_s;
+#pragma unroll
+  for (int q = 0; q < VPT; ++q)
+    if (ok[q]) *reinterpret_cast<float4*>(qs + n[q]) = o[q];
+  __syncthreads();
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int c = w; c < rf.C; c += nw) {
+    float l = -CUDART_INF_F;
+    if (c < nc) l = route_dot(qs, s_lib + (int64_t)c * a.d_s, a.d_s, lane) * rf.temp;
+    if (lane == 0) {
+      lg[c] = l;
+      if (rf.logit_out) rf.logit_out[row * rf.C + c] = l;
+    }
+  }
+  __syncthreads();
+  if (w == 0)
+    topk_row(lg, lg + rf.C, rf.C, nc, rf.top_k, rf.k_out, rf.row_w ? rf.row_w[row] : 1.f, rf.idx + row * rf.k_out,
+             rf.wk + row * rf.k_out, rf.w_dense ? rf.w_dense + row * rf.C : nullptr, lane);
 }
 
 // Decode routing in one launch: a cluster of RF_CL CTAs (RF_CL * 8 warps) takes `rpc` consecutive rows. Its warps

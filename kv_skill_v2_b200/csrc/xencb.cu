@@ -647,10 +647,13 @@ size_t xencb_project_in_workspace(int64_t n_rows, int d_m, int d_s) {
          align_up((size_t)n_rows * sizeof(int), 256);
 }
 
-int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const float* w_in, const void* w_prep,
-                     const float* b_in, int d_s, int flags, const float* gate_w, float gate_b, const float* gate_b_dev,
-                     const float* sel_w, const float* sel_b, int n_cand, float rms_eps, float* q_out, float* gate_out, float* rstd_out, float* z_out,
-                     void* workspace, size_t workspace_bytes, void* stream) {
+// project_in, and (rf given) the fused decode routing of its rows: returns XENCB_ENOTSUP, launching nothing, when
+// the fused form does not take the shape.
+static int project_in_impl(const void* h, int h_dtype, int64_t n_rows, int d_m, const float* w_in, const void* w_prep,
+                           const float* b_in, int d_s, int flags, const float* gate_w, float gate_b,
+                           const float* gate_b_dev, const float* sel_w, const float* sel_b, int n_cand, float rms_eps,
+                           float* q_out, float* gate_out, float* rstd_out, float* z_out, void* workspace,
+                           size_t workspace_bytes, void* stream, const RouteFuse* rf) {
   if (flags & ~(XENCB_PIN_RMS | XENCB_PIN_L2)) return fail(XENCB_EINVAL, "project_in: unknown flags 0x%x", flags);
   if (!h || (!w_in && !w_prep) || !q_out) return fail(XENCB_EINVAL, "project_in: h, w_in (or w_prep) and q_out are required");
   if (!w_in && (d_m % 8 != 0 || !aligned(w_prep, 256)))
@@ -663,6 +666,10 @@ int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const 
     return fail(XENCB_EINVAL, "project_in: d_s=%d must be a multiple of 4 and q_out 16-byte aligned", d_s);
   if (sel_w && (!z_out || n_cand <= 0 || n_cand > 32))
     return fail(XENCB_EINVAL, "project_in: selector needs z_out and 1 <= n_cand <= 32 (got %d)", n_cand);
+  const size_t rf_smem = rf ? ((size_t)d_s + 2 * (size_t)rf->C) * sizeof(float) : 0;
+  if (rf && (d_s > 12 * ROW_THREADS || !(flags & XENCB_PIN_L2) || rf->rows_per_lib >= 64 || rf_smem > 96 * 1024))
+    return fail(XENCB_ENOTSUP, "project_in_route: the fused form takes decode rows (rows_per_lib < 64), L2-normalised "
+                "q, d_s <= %d and d_s + 2 * C <= 24576 floats", 12 * ROW_THREADS);
   DevInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
@@ -697,21 +704,36 @@ int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const 
   if (d_s <= 12 * ROW_THREADS) {  // one CTA per row: the reduce, 1/rms, bias and L2 norm in registers
     const int vpt = (d_s + 4 * ROW_THREADS - 1) / (4 * ROW_THREADS);  // float4 columns per thread: 1..3
     const unsigned thr = (unsigned)std::min<int>(ROW_THREADS, (d_s / 4 + 31) / 32 * 32);
+    const PinArgs pa{d_m, part, gp.splits, n_rows, d_s, flags, b_in, gate_w, gate_b, gate_b_dev, sel_w, sel_b,
+                     n_cand, rms_eps, q_out, gate_out, rstd_out, z_out};
+    int lrc = XENCB_OK;
     auto launch = [&](auto kern, const auto* hp) {
-      launch_pdl(kern, dim3((unsigned)n_rows), dim3(thr), 0, st, hp, d_m, part, gp.splits, n_rows, d_s, flags, b_in,
-                 gate_w, gate_b, gate_b_dev, sel_w, sel_b, n_cand, rms_eps, q_out, gate_out, rstd_out, z_out);
+      launch_pdl(kern, dim3((unsigned)n_rows), dim3(thr), 0, st, hp, pa);
+    };
+    auto launch_rf = [&](auto kern, const auto* hp) {
+      lrc = ensure_smem(kern, (int)std::max<size_t>(rf_smem, 48 * 1024));
+      if (!lrc) launch_pdl(kern, dim3((unsigned)n_rows), dim3(thr), rf_smem, st, hp, pa, *rf);
     };
     auto by_vpt = [&](const auto* hp) {
       using TH = std::remove_const_t<std::remove_pointer_t<decltype(hp)>>;
-      if (vpt == 1) launch(project_in_row_kernel<TH, 1>, hp);
-      else if (vpt == 2) launch(project_in_row_kernel<TH, 2>, hp);
-      else launch(project_in_row_kernel<TH, 3>, hp);
+      if (rf) {
+        if (vpt == 1) launch_rf(project_in_route_kernel<TH, 1>, hp);
+        else if (vpt == 2) launch_rf(project_in_route_kernel<TH, 2>, hp);
+        else launch_rf(project_in_route_kernel<TH, 3>, hp);
+      } else if (vpt == 1) {
+        launch(project_in_row_kernel<TH, 1>, hp);
+      } else if (vpt == 2) {
+        launch(project_in_row_kernel<TH, 2>, hp);
+      } else {
+        launch(project_in_row_kernel<TH, 3>, hp);
+      }
     };
     switch (h_dtype) {
       case XENCB_F32: by_vpt(static_cast<const float*>(h)); break;
       case XENCB_F16: by_vpt(static_cast<const __half*>(h)); break;
       default: by_vpt(static_cast<const __nv_bfloat16*>(h)); break;
     }
+    if (lrc) return lrc;
     XENCB_CHECK_LAUNCH("project_in row launch");
     return XENCB_OK;
   }
@@ -728,6 +750,38 @@ int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const 
 #undef XENCB_PIN
   XENCB_CHECK_LAUNCH("project_in reduce launch");
   return XENCB_OK;
+}
+
+int xencb_project_in(const void* h, int h_dtype, int64_t n_rows, int d_m, const float* w_in, const void* w_prep,
+                     const float* b_in, int d_s, int flags, const float* gate_w, float gate_b, const float* gate_b_dev,
+                     const float* sel_w, const float* sel_b, int n_cand, float rms_eps, float* q_out, float* gate_out,
+                     float* rstd_out, float* z_out, void* workspace, size_t workspace_bytes, void* stream) {
+  return project_in_impl(h, h_dtype, n_rows, d_m, w_in, w_prep, b_in, d_s, flags, gate_w, gate_b, gate_b_dev, sel_w,
+                         sel_b, n_cand, rms_eps, q_out, gate_out, rstd_out, z_out, workspace, workspace_bytes, stream,
+                         nullptr);
+}
+
+int xencb_project_in_route(const void* h, int h_dtype, int64_t n_rows, int d_m, const float* w_in, const void* w_prep,
+                           const float* b_in, int d_s, int flags, const float* gate_w, float gate_b,
+                           const float* gate_b_dev, const float* sel_w, const float* sel_b, int n_cand, float rms_eps,
+                           float* q_out, float* gate_out, float* rstd_out, float* z_out, const float* S, int n_chunks,
+                           const int32_t* n_chunks_of, int64_t rows_per_lib, int64_t n_lib, float route_temp, int top_k,
+                           const float* row_w, int32_t* idx, float* wk, float* w_dense, float* logit_out,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  if (!S || !idx || !wk) return fail(XENCB_EINVAL, "project_in_route: S, idx and wk are required");
+  if (n_rows <= 0 || n_chunks <= 0 || rows_per_lib <= 0 || n_lib <= 0)
+    return fail(XENCB_EINVAL, "project_in_route: sizes must be positive (n_rows=%lld C=%d rows_per_lib=%lld "
+                "n_lib=%lld)", (long long)n_rows, n_chunks, (long long)rows_per_lib, (long long)n_lib);
+  if ((n_rows + rows_per_lib - 1) / rows_per_lib > n_lib)
+    return fail(XENCB_EINVAL, "project_in_route: %lld rows at %lld rows per Library need more than %lld Libraries",
+                (long long)n_rows, (long long)rows_per_lib, (long long)n_lib);
+  if (top_k < 0) return fail(XENCB_EINVAL, "project_in_route: top_k=%d must be >= 0", top_k);
+  if (!aligned(S, 16)) return fail(XENCB_EINVAL, "project_in_route: S must be 16-byte aligned");
+  const RouteFuse rf{S, n_chunks, n_chunks_of, rows_per_lib, route_temp, top_k, xencb_route_k(top_k, n_chunks), row_w,
+                     idx, wk, w_dense, logit_out};
+  return project_in_impl(h, h_dtype, n_rows, d_m, w_in, w_prep, b_in, d_s, flags, gate_w, gate_b, gate_b_dev, sel_w,
+                         sel_b, n_cand, rms_eps, q_out, gate_out, rstd_out, z_out, workspace, workspace_bytes, stream,
+                         &rf);
 }
 
 int xencb_rms_norm(const void* h, int h_dtype, int64_t n_rows, int d_m, float eps, float* out, void* stream) {

@@ -227,6 +227,30 @@ class XEncInjector(ExternalSkillInjector):
                 g, z = g_i, z_i
         return x, g, gain, z
 
+    def _query_route(self, h2: torch.Tensor, li: int, pages: ops.Pages, rpl: int, top_k: int, route_temp: float,
+                     row_w: Optional[torch.Tensor]):
+        """(q, gate | None, log_gain | None, idx, wk, w) from the fused input projection + routing of decode rows,
+        or None when the interface's query map is not one linear layer (low-rank A: two projections)."""
+        itf = self.itf
+        if isinstance(itf, LinearInterface):
+            W = _on(itf.w_in.detach(), h2).float()
+            q, _, _, idx, wk, w, _ = ops.project_in_route(
+                h2, W, S=pages.S, rows_per_lib=rpl, top_k=top_k, route_temp=route_temp,
+                n_chunks_of=pages.n_chunks_of, row_w=row_w, w_prep=self._prep(W))
+            return q, None, None, idx, wk, w
+        lins = itf.query_weights()
+        if len(lins) != 1:
+            return None
+        p = itf._pos[li]
+        W, b = lins[0]
+        Wf = _f32_on(W, h2)
+        q, g, _, idx, wk, w, _ = ops.project_in_route(
+            h2, Wf, None if b is None else _on(b.detach(), h2).float(), S=pages.S, rows_per_lib=rpl, top_k=top_k,
+            route_temp=route_temp, n_chunks_of=pages.n_chunks_of, row_w=row_w,
+            gate_w=_on(itf.gate_w.detach(), h2).float(), gate_b=_on(itf.gate_b.detach()[p:p + 1], h2).float(),
+            w_prep=self._prep(Wf))
+        return q, g, _on(itf.log_gain.detach()[p:p + 1], h2).float(), idx, wk, w
+
     def _write_weights(self, like: torch.Tensor):
         itf = self.itf
         if isinstance(itf, LinearInterface):
@@ -527,18 +551,25 @@ class LibraryInjector(XEncInjector):
         if sel is not None and not fuse_sel:
             sel.weights_for(h, li)
             sel_col, log_alpha = sel_column()
-        if self._fast_interface():
-            q, g, log_gain, z = self._query(h2, li, sel_fuse=sel if fuse_sel else None)
+        # decode rows: q and its routing in one pass after the projection GEMM
+        routed = None
+        if self._fast_interface() and not fuse_sel and rpl < 64:
+            routed = self._query_route(h2, li, pages, rpl, self.top_k, self.route_temp, sel_col)
+        if routed is not None:
+            q, g, log_gain, idx, wk, w = routed
         else:
-            hn = ops.rms_norm(h2)
-            q = self.itf.query(hn.view(*lead, -1)).reshape(-1, self.itf.d_s).float().contiguous()
-            z = None
-        if fuse_sel:
-            sel._w = sel._weights_from_logits(z.view(*lead, sel.n_cand))
-            sel._explicit = False
-            sel_col, log_alpha = sel_column()
-        idx, wk, w, _ = ops.route(q, pages.S, rows_per_lib=rpl, top_k=self.top_k, route_temp=self.route_temp,
-                                  n_chunks_of=pages.n_chunks_of, row_w=sel_col)
+            if self._fast_interface():
+                q, g, log_gain, z = self._query(h2, li, sel_fuse=sel if fuse_sel else None)
+            else:
+                hn = ops.rms_norm(h2)
+                q = self.itf.query(hn.view(*lead, -1)).reshape(-1, self.itf.d_s).float().contiguous()
+                z = None
+            if fuse_sel:
+                sel._w = sel._weights_from_logits(z.view(*lead, sel.n_cand))
+                sel._explicit = False
+                sel_col, log_alpha = sel_column()
+            idx, wk, w, _ = ops.route(q, pages.S, rows_per_lib=rpl, top_k=self.top_k, route_temp=self.route_temp,
+                                      n_chunks_of=pages.n_chunks_of, row_w=sel_col)
         # with a selector most rows read nothing at most depths: the sparse plan spreads the live rows' work
         r = ops.read_decode(q, pages, idx, wk, rows_per_lib=rpl, read_temp=self.read_temp,
                             read_softmax=self.read_softmax, sparse=sel_col is not None)

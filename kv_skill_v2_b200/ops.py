@@ -149,6 +149,61 @@ def project_in(h2: torch.Tensor, w_in: torch.Tensor, b_in=None, *, rms: bool = T
     return q, gate, rstd, z
 
 
+def project_in_route(h2: torch.Tensor, w_in: torch.Tensor, b_in=None, *, S: torch.Tensor, rows_per_lib: int,
+                     top_k: int, route_temp: float, n_chunks_of: Optional[torch.Tensor] = None,
+                     row_w: Optional[torch.Tensor] = None, want_logits: bool = False, gate_w=None, gate_b=0.0,
+                     eps: float = 1e-6, w_prep: Optional[torch.Tensor] = None):
+    """project_in (rms + L2) and route for decode rows in one pass after the GEMM (xencb_project_in_route):
+    (q, gate | None, rstd, idx, wk, w_dense, logits | None), the same values as project_in then route. Shapes
+    the fused form does not take (rows_per_lib >= 64, very wide rows) run the two calls."""
+    dev = _cuda("project_in_route", h2, w_in, b_in, gate_w, S, n_chunks_of, row_w)
+    if int(rows_per_lib) >= 64:
+        q, g, rstd, _ = project_in(h2, w_in, b_in, gate_w=gate_w, gate_b=gate_b, eps=eps, w_prep=w_prep)
+        idx, wk, w, lg = route(q, S, rows_per_lib=rows_per_lib, top_k=top_k, route_temp=route_temp,
+                               n_chunks_of=n_chunks_of, want_logits=want_logits, row_w=row_w)
+        return q, g, rstd, idx, wk, w, lg
+    h2 = h2.contiguous()
+    w_in = _f32(w_in, "w_in")
+    S = _f32(S, "S")
+    R, d_m = h2.shape
+    d_s = w_in.shape[0]
+    if w_in.shape[1] != d_m:
+        raise ValueError(f"w_in is {tuple(w_in.shape)}, expected [d_s, {d_m}] (nn.Linear layout)")
+    n_lib, C, d2 = S.shape
+    if d2 != d_s:
+        raise ValueError(f"project_in_route: q has d_s={d_s}, S has {d2}")
+    k = route_k(top_k, C)
+    q = torch.empty(R, d_s, dtype=torch.float32, device=dev)
+    gate = torch.empty(R, dtype=torch.float32, device=dev) if gate_w is not None else None
+    rstd = torch.empty(R, dtype=torch.float32, device=dev)
+    idx = torch.empty(R, k, dtype=torch.int32, device=dev)
+    wk = torch.empty(R, k, dtype=torch.float32, device=dev)
+    w = torch.empty(R, C, dtype=torch.float32, device=dev)
+    lg = torch.empty(R, C, dtype=torch.float32, device=dev) if want_logits else None
+    b_in, gate_w = _f32(b_in, "b_in"), _f32(gate_w, "gate_w")
+    gb, gb_dev = _dev_scalar(gate_b, "gate_b")
+    if n_chunks_of is not None:
+        n_chunks_of = n_chunks_of.to(torch.int32).contiguous()
+    if row_w is not None:
+        row_w = _f32(row_w.reshape(-1), "row_w")
+        if row_w.numel() != R:
+            raise ValueError(f"project_in_route: row_w has {row_w.numel()} entries for {R} rows")
+    with _on_device(dev):
+        ws = _workspace(N.lib().xencb_project_in_workspace(R, d_m, d_s), dev)
+        rc = N.lib().xencb_project_in_route(
+            _ptr(h2), _hdt(h2, "h"), R, d_m, _ptr(w_in), _ptr(w_prep), _ptr(b_in), d_s, N.PIN_RMS | N.PIN_L2,
+            _ptr(gate_w), gb, _ptr(gb_dev), None, None, 0, eps, _ptr(q), _ptr(gate), _ptr(rstd), None, _ptr(S), C,
+            _ptr(n_chunks_of), int(rows_per_lib), n_lib, float(route_temp), int(top_k), _ptr(row_w), _ptr(idx),
+            _ptr(wk), _ptr(w), _ptr(lg), _ptr(ws), ws.numel(), _stream(dev))
+        if rc == N.ENOTSUP:  # nothing was launched: the two calls
+            q, g2, rstd, _ = project_in(h2, w_in, b_in, gate_w=gate_w, gate_b=gate_b, eps=eps, w_prep=w_prep)
+            idx, wk, w, lg = route(q, S, rows_per_lib=rows_per_lib, top_k=top_k, route_temp=route_temp,
+                                   n_chunks_of=n_chunks_of, want_logits=want_logits, row_w=row_w)
+            return q, g2, rstd, idx, wk, w, lg
+        N.check(rc, "xencb_project_in_route")
+    return q, gate, rstd, idx, wk, w, lg
+
+
 def project_out(r: torch.Tensor, w_out: torch.Tensor, h2: torch.Tensor, *, b_out=None, scale: float = 1.0,
                 log_scale: Optional[torch.Tensor] = None, gate=None, sel_w=None, log_alpha=0.0, pos_mask=None,
                 want_delta: bool = True, h_out: Optional[torch.Tensor] = None, want_rel: bool = False,

@@ -699,3 +699,40 @@ def test_bounded_wait_gives_up_and_context_stays_usable(dev):
     r = ops.read_decode(q, pages, idx, wk, rows_per_lib=R, read_temp=float(c["read_temp"]))
     assert rel_err(r, c["r"].reshape(r.shape)) < TOL
     _status_clean(dev)
+
+
+@pytest.mark.parametrize("case", [
+    # (n_lib, rows_per_lib, C, d_s, d_m, top_k, h dtype, gate, bias, n_chunks_of, row mask)
+    (64, 1, 64, 2048, 4096, 4, torch.float32, False, False, False, False),   # config-2 shapes
+    (8, 1, 32, 512, 640, 4, torch.float32, True, True, False, True),         # gate, bias, selector row mask
+    (5, 3, 8, 256, 512, 0, torch.bfloat16, True, False, True, False),        # dense, chunk counts per Library
+    (3, 2, 70, 384, 256, 5, torch.float16, False, True, True, True),
+])
+def test_project_in_route_matches_the_two_calls(dev, case):
+    """xencb_project_in_route gives project_in's q and route's logits, index sets, weights and dense weights
+    bit for bit (the same sums in the same order), with and without gate, bias, per-Library chunk counts and a
+    selector row mask."""
+    from kv_skill_v2_b200 import ops
+    n_lib, rpl, C, d_s, d_m, top_k, hdt, use_gate, use_bias, use_nco, use_mask = case
+    g = torch.Generator().manual_seed(C + d_s)
+    R = n_lib * rpl
+    h = torch.randn(R, d_m, generator=g).to(dev, hdt)
+    W = (torch.randn(d_s, d_m, generator=g) * 0.02).to(dev)
+    b = (torch.randn(d_s, generator=g) * 0.01).to(dev) if use_bias else None
+    gate_w = (torch.randn(d_m, generator=g) * 0.02).to(dev) if use_gate else None
+    gate_b = torch.tensor([0.3], device=dev)
+    S = torch.nn.functional.normalize(torch.randn(n_lib, C, d_s, generator=g), dim=-1).to(dev)
+    nco = torch.randint(1, C + 1, (n_lib,), generator=g, dtype=torch.int32).to(dev) if use_nco else None
+    row_w = (torch.rand(R, generator=g) > 0.5).float().to(dev) if use_mask else None
+    prep = ops.weights_prep(W)
+    q0, g0, r0, _ = ops.project_in(h, W, b, gate_w=gate_w, gate_b=gate_b, w_prep=prep)
+    i0, k0, w0, l0 = ops.route(q0, S, rows_per_lib=rpl, top_k=top_k, route_temp=10.0, n_chunks_of=nco,
+                               want_logits=True, row_w=row_w)
+    q1, g1, r1, i1, k1, w1, l1 = ops.project_in_route(h, W, b, S=S, rows_per_lib=rpl, top_k=top_k, route_temp=10.0,
+                                                      n_chunks_of=nco, row_w=row_w, want_logits=True,
+                                                      gate_w=gate_w, gate_b=gate_b, w_prep=prep)
+    assert torch.equal(q0, q1) and torch.equal(r0, r1)
+    assert (g0 is None and g1 is None) or torch.equal(g0, g1)
+    assert torch.equal(l0, l1), "routing logits differ"
+    assert torch.equal(i0, i1) and torch.equal(k0, k1) and torch.equal(w0, w1)
+    _status_clean(dev)
