@@ -361,7 +361,7 @@ __device__ __forceinline__ float2 pin_row_pre(const TH* __restrict__ hr, const P
 }
 
 // Second half (after the wait): q's columns n[v] (ok[v]: inside d_s) in o[v], written to q_out; 1/rms, the gate
-// and the selector logits written too.
+// and the selector logits written too (each output skipped when its pointer is null).
 template <int VPT>
 __device__ __forceinline__ void pin_row_post(const PinArgs& a, int64_t row, float2 pre, const float* zsh,
                                              float2* red2, float* red, float4* o, int* n, bool* ok) {
@@ -376,12 +376,12 @@ __device__ __forceinline__ void pin_row_post(const PinArgs& a, int64_t row, floa
   const float rstd = (a.flags & XENCB_PIN_RMS) ? rsqrtf(t.x / (float)a.d_m + a.eps) : 1.f;
   if (threadIdx.x == 0) {
     if (a.rstd_out) a.rstd_out[row] = rstd;
-    if (a.gate_w) {
+    if (a.gate_w && a.gate_out) {
       const float gb = a.gate_b_dev ? __ldg(a.gate_b_dev) : a.gate_b;
       a.gate_out[row] = 1.f / (1.f + expf(-(t.y * rstd + gb)));
     }
   }
-  if (a.sel_w && threadIdx.x < a.n_cand)
+  if (a.sel_w && a.z_out && threadIdx.x < a.n_cand)
     a.z_out[row * a.n_cand + threadIdx.x] = zsh[threadIdx.x] * rstd + (a.sel_b ? a.sel_b[threadIdx.x] : 0.f);
   float nq = 0.f;
 #pragma unroll
@@ -402,9 +402,11 @@ __device__ __forceinline__ void pin_row_post(const PinArgs& a, int64_t row, floa
 #pragma unroll
     for (int q = 0; q < VPT; ++q) { o[q].x /= den; o[q].y /= den; o[q].z /= den; o[q].w /= den; }
   }
+  if (a.q_out) {
 #pragma unroll
-  for (int q = 0; q < VPT; ++q)
-    if (ok[q]) *reinterpret_cast<float4*>(a.q_out + row * a.d_s + n[q]) = o[q];
+    for (int q = 0; q < VPT; ++q)
+      if (ok[q]) *reinterpret_cast<float4*>(a.q_out + row * a.d_s + n[q]) = o[q];
+  }
 }
 
 template <typename TH, int VPT>

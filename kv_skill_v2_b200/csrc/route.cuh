@@ -183,16 +183,77 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i) {
 
 constexpr int TOPK_WARPS = 4;
 
-// Top-k and softmax of one row's logits lr[0, C) by one warp; v is the warp's scratch row of C floats. Chunks at
-// or past nc take no part. Sparse (0 < top_k < nc): top_k rounds of a warp arg-max (ties to the lower chunk), the
-// winner retired to -inf, then the softmax over the kept logits. Dense: the softmax over all nc chunks, idx = 0..
-// nc-1. A row whose weight rw is 0 reads nothing (idx -1); w_dense keeps its routing. lr may alias wd: every lane
-// is done reading lr before wd is written.
+// topk_row for rows of up to 32 * TK_R chunks and k <= 32, with the logits held in registers (lane l owns chunks
+// l + 32 i): each round is a register arg-max, a warp arg-max and a retire by the owning lane, with no shared
+// memory and no warp barrier. Same selection, order and arithmetic as topk_row. lr may alias wd.
+constexpr int TK_R = 8;
+__device__ __forceinline__ void topk_row_reg(const float* lr, int C, int nc, int top_k, int k_out, float rw,
+                                             int32_t* __restrict__ ir, float* __restrict__ wr, float* wd, int lane) {
+  float x[TK_R];
+#pragma unroll
+  for (int i = 0; i < TK_R; ++i) {
+    const int c = lane + 32 * i;
+    x[i] = c < nc ? lr[c] : -CUDART_INF_F;
+  }
+  const bool skip = rw == 0.f;
+  int mine = -1;
+  float lmine = -CUDART_INF_F;
+  for (int t = 0; t < top_k; ++t) {
+    float bv = -CUDART_INF_F;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < TK_R; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nc && (x[i] > bv || (x[i] == bv && c < bi))) { bv = x[i]; bi = c; }
+    }
+    warp_argmax(bv, bi);
+    const int win = bi < nc ? bi : -1;  // -1 only with non-finite logits
+    if (lane == t) { mine = win; lmine = bv; }
+    if (win >= 0 && (win & 31) == lane) {
+#pragma unroll
+      for (int i = 0; i < TK_R; ++i)
+        if (lane + 32 * i == win) x[i] = -CUDART_INF_F;
+    }
+  }
+  const bool kept = lane < top_k && mine >= 0;
+  if (!kept) lmine = -CUDART_INF_F;
+  const float mx = warp_max(lmine);
+  const float sum = warp_sum(kept ? expf(lmine - mx) : 0.f);
+  const float wmine = kept ? expf(lmine - mx) / sum : 0.f;
+  if (wd) {
+    for (int c0 = 0; c0 < C; c0 += 32) {
+      const int c = c0 + lane;
+      float val = 0.f;
+      for (int j = 0; j < top_k; ++j) {
+        const int cj = __shfl_sync(0xffffffffu, mine, j);
+        const float wj = __shfl_sync(0xffffffffu, wmine, j);
+        if (cj == c) val = wj;
+      }
+      if (c < C) wd[c] = val;
+    }
+  }
+  for (int j = lane; j < k_out; j += 32) {
+    ir[j] = (skip || j >= top_k) ? -1 : mine;
+    wr[j] = (skip || j >= top_k) ? 0.f : wmine;
+  }
+}
+
+// Top-k and softmax of one row's logits lr[0, C) by one warp; v is the warp's scratch row of C floats (shared
+// memory). Chunks at or past nc take no part. Sparse (0 < top_k < nc): top_k rounds of a warp arg-max (ties to
+// the lower chunk), the winner retired to -inf in v, then the softmax over the kept logits. Dense: the softmax
+// over all nc chunks, idx = 0..nc-1. A row whose weight rw is 0 reads nothing (idx -1); w_dense keeps its
+// routing. lr may alias wd. Every output is written once, after all reads: a __syncwarp() after a global store
+// orders that store, and waits for it, so no warp barrier follows one here.
 __device__ __forceinline__ void topk_row(const float* lr, float* v, int C, int nc, int top_k, int k_out, float rw,
                                          int32_t* __restrict__ ir, float* __restrict__ wr, float* wd, int lane) {
+  const bool sparse = top_k > 0 && top_k < nc;
+  if (sparse && top_k <= 32 && C <= 32 * TK_R) {
+    topk_row_reg(lr, C, nc, top_k, k_out, rw, ir, wr, wd, lane);
+    return;
+  }
   for (int c = lane; c < C; c += 32) v[c] = (c < nc) ? lr[c] : -CUDART_INF_F;
   __syncwarp();
-  const bool sparse = top_k > 0 && top_k < nc;
+  const bool skip = rw == 0.f;
   if (!sparse) {
     float mx = -CUDART_INF_F;
     for (int c = lane; c < nc; c += 32) mx = fmaxf(mx, v[c]);
@@ -201,19 +262,14 @@ __device__ __forceinline__ void topk_row(const float* lr, float* v, int C, int n
     for (int c = lane; c < nc; c += 32) sum += expf(v[c] - mx);
     sum = warp_sum(sum);
     for (int j = lane; j < k_out; j += 32) {
-      ir[j] = j < nc ? j : -1;
-      wr[j] = j < nc ? expf(v[j] - mx) / sum : 0.f;
+      ir[j] = (j < nc && !skip) ? j : -1;
+      wr[j] = (j < nc && !skip) ? expf(v[j] - mx) / sum : 0.f;
     }
     if (wd)
       for (int c = lane; c < C; c += 32) wd[c] = c < nc ? expf(v[c] - mx) / sum : 0.f;
-    if (rw == 0.f) {
-      __syncwarp();
-      for (int j = lane; j < k_out; j += 32) { ir[j] = -1; wr[j] = 0.f; }
-    }
     return;
   }
-  // lane j keeps the winner of round j (rounds 32 and up are read back from ir): no global round trip on the
-  // path of a decode row's handful of rounds
+  // lane j keeps the winner of round j in a register; rounds 32 and up (k > 32, rare) go to ir
   int mine = -1;
   for (int t = 0; t < top_k; ++t) {
     float bv = -CUDART_INF_F;
@@ -224,40 +280,49 @@ __device__ __forceinline__ void topk_row(const float* lr, float* v, int C, int n
     }
     warp_argmax(bv, bi);
     const int win = bi < nc ? bi : -1;  // -1 only with non-finite logits
-    if (t < 32 && lane == t) mine = win;
-    if (lane == 0) {
+    if (t < 32) {
+      if (lane == t) mine = win;
+    } else if (lane == 0) {
       ir[t] = win;
-      if (win >= 0) v[win] = -CUDART_INF_F;
     }
+    if (lane == 0 && win >= 0) v[win] = -CUDART_INF_F;
     __syncwarp();
   }
-  for (int j = top_k + lane; j < k_out; j += 32) { ir[j] = -1; wr[j] = 0.f; }
-  // softmax over the kept logits (the first one is the maximum)
-  float mx = -CUDART_INF_F;
-  for (int j = lane; j < top_k; j += 32) { const int c = j < 32 ? mine : ir[j]; if (c >= 0) mx = fmaxf(mx, lr[c]); }
+  // softmax over the kept logits (the first one is the maximum); lr is read before anything is written to wd
+  const bool kept = lane < top_k && mine >= 0;
+  const float lmine = kept ? lr[mine] : -CUDART_INF_F;
+  float mx = lmine;
+  for (int j = 32 + lane; j < top_k; j += 32) { const int c = ir[j]; if (c >= 0) mx = fmaxf(mx, lr[c]); }
   mx = warp_max(mx);
-  float sum = 0.f;
-  for (int j = lane; j < top_k; j += 32) { const int c = j < 32 ? mine : ir[j]; if (c >= 0) sum += expf(lr[c] - mx); }
+  float sum = kept ? expf(lmine - mx) : 0.f;
+  for (int j = 32 + lane; j < top_k; j += 32) { const int c = ir[j]; if (c >= 0) sum += expf(lr[c] - mx); }
   sum = warp_sum(sum);
-  float w_mine = 0.f;
-  for (int j = lane; j < top_k; j += 32) {
-    const int c = j < 32 ? mine : ir[j];
-    const float wj = c >= 0 ? expf(lr[c] - mx) / sum : 0.f;
-    wr[j] = wj;
-    if (j < 32) w_mine = wj;
-  }
+  const float wmine = kept ? expf(lmine - mx) / sum : 0.f;
+  for (int j = 32 + lane; j < top_k; j += 32) { const int c = ir[j]; wr[j] = c >= 0 ? expf(lr[c] - mx) / sum : 0.f; }
+  if (top_k > 32) __syncwarp();  // rounds >= 32: their ir / wr entries are read back below
   if (wd) {
-    __syncwarp();
-    for (int c = lane; c < C; c += 32) wd[c] = 0.f;
-    __syncwarp();
-    for (int j = lane; j < top_k; j += 32) {
-      const int c = j < 32 ? mine : ir[j];
-      if (c >= 0) wd[c] = j < 32 ? w_mine : wr[j];
+    for (int c0 = 0; c0 < C; c0 += 32) {
+      const int c = c0 + lane;
+      float val = 0.f;
+      for (int j = 0; j < min(top_k, 32); ++j) {
+        const int cj = __shfl_sync(0xffffffffu, mine, j);
+        const float wj = __shfl_sync(0xffffffffu, wmine, j);
+        if (cj == c) val = wj;
+      }
+      for (int j = 32; j < top_k; ++j)
+        if (ir[j] == c) val = wr[j];
+      if (c < C) wd[c] = val;
     }
   }
-  if (rw == 0.f) {
-    __syncwarp();
-    for (int j = lane; j < k_out; j += 32) { ir[j] = -1; wr[j] = 0.f; }
+  if (top_k > 32) __syncwarp();
+  for (int j = lane; j < k_out; j += 32) {
+    if (j < 32) {
+      ir[j] = (skip || j >= top_k) ? -1 : mine;
+      wr[j] = (skip || j >= top_k) ? 0.f : wmine;
+    } else if (skip || j >= top_k) {
+      ir[j] = -1;
+      wr[j] = 0.f;
+    }
   }
 }
 
