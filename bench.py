@@ -270,8 +270,8 @@ def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
     all-gather per step and merged. Strong scaling: the whole Library is the same at every N.
 
     A step: q = project_in(h) (replicated interface weights), the rank's partial (route_lse + read_multi over its
-    chunks), all-gather of the partial blocks, shard merge, output projection + residual. The local parts run
-    as two CUDA graphs around the eager all-gather. Timed with CUDA events per step, max over ranks."""
+    chunks), all-gather of the partial blocks, shard merge, output projection + residual, captured as one CUDA
+    graph with the NCCL all-gather inside. Timed with CUDA events per step, max over ranks."""
     from kv_skill_v2_b200 import _native, ops
     from kv_skill_v2_b200.shard import ShardedRead, partition_chunks
 
@@ -304,23 +304,22 @@ def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
         r = sr.merge()
         ops.project_out(r, W_out, h, want_delta=False, h_out=h_out, w_prep=P_out)
 
-    for _ in range(2):
+    for _ in range(2):  # eager steps first: the NCCL communicator exists before the capture
         pre(); sr.exchange(); post()
     torch.cuda.synchronize(dev)
-    g_pre, g_post = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    # the whole step, the all-gather included, is one CUDA graph
+    g_step = torch.cuda.CUDAGraph()
     n0 = _native.launch_count()
-    with torch.cuda.graph(g_pre):
+    with torch.cuda.graph(g_step):
         pre()
-    with torch.cuda.graph(g_post):
+        sr.exchange()
         post()
     kernels = _native.launch_count() - n0
     torch.cuda.synchronize(dev)
 
     def step(i):
         h.copy_(hs[i])
-        g_pre.replay()
-        sr.exchange()
-        g_post.replay()
+        g_step.replay()
 
     for i in range(warmup):
         l2_flush(flush, i)
@@ -357,11 +356,39 @@ def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
         evr[i][1].record(stream)
     torch.cuda.synchronize(dev)
     t_read = statistics.mean(a.elapsed_time(b) for a, b in evr) / 1000.0
+
+    # the other parts of the step, each replayed alone (every rank replays the same graphs in the same order):
+    # the replicated input projection, the all-gather, merge + output projection; and, for the choice of keeping
+    # the projections replicated, the input projection of one rank's share of W_in's rows (what a rank would run
+    # with the projections sharded, before an extra all-gather of q)
+    def timed(fn, n=20):
+        gph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gph):
+            fn()
+        ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        gph.replay()
+        for i in range(n):
+            l2_flush(flush, i)
+            ev2[i][0].record(stream)
+            gph.replay()
+            ev2[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+        t = statistics.mean(a.elapsed_time(b) for a, b in ev2) * 1000.0
+        del gph
+        return t
+    n_sh = max(64, (d_s // max(world, 1)) // 64 * 64)
+    W_sh = W_in[:n_sh].contiguous()
+    P_sh = ops.weights_prep(W_sh)
+    comp = {"project_in": timed(lambda: ops.project_in(h, W_in, w_prep=P_in)),
+            "route_lse_read_multi": t_read * 1e6,
+            "all_gather": timed(sr.exchange) if world > 1 else 0.0,
+            "merge_project_out": timed(post),
+            f"project_in_{n_sh}_of_{d_s}_rows": timed(lambda: ops.project_in(h, W_sh, w_prep=P_sh))}
     read_bytes = Cl * N * d_s * 2 + Cl * d_s * 4 + 2 * T * d_s * 4
     step_bytes = read_bytes + 2 * d_s * d_m * 4 + 2 * T * d_m * 4
     peak, peak_kind = hbm_peak()
     ms = t_max / steps
-    del g_pre, g_post, g_read
+    del g_step, g_read
     return {"workload": f"BASELINE config 5: one Library of {C} chunks x 512 fp16 slots ({C * N:,} slots), d_s 2560, "
                         "d_m 5120, 8 query tokens, dense read of every chunk; chunks sharded evenly over the GPUs, "
                         "partials (max, sum, acc) merged after one NCCL all-gather per step"
@@ -369,6 +396,9 @@ def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
             "metric": "sharded Library-read tokens/s (whole job)", "value": T * steps / (t_max / 1000.0),
             "unit": "tokens/s", "n_gpus": world, "ms_per_step": ms, "scaling": "strong",
             "chunks_per_gpu": Cl, "kernels_per_step": kernels, "gpu_launches": kernels * steps,
+            "components_us": comp,
+            "step": "one CUDA graph per step: input projection (replicated), route_lse + read_multi over the rank's "
+                    "chunks, NCCL all-gather of the partial blocks, shard merge, output projection (replicated)",
             "step_bytes_per_gpu": step_bytes, "step_hbm_gbs_per_gpu": step_bytes / (ms / 1000.0) / 1e9,
             "roofline": {"bound": "hbm", "kernel": "route_lse + read_multi_mma_kernel + read_multi_merge_kernel",
                          "achieved": read_bytes / t_read / 1e9, "peak": peak, "unit": "GB/s",

@@ -166,6 +166,35 @@ XENCB_API int xencb_read_decode_sparse(const float* q, int64_t n_rows, int d_s, 
                                        float read_temp, int read_softmax, float* r_out, void* workspace,
                                        size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------------------------------------------------
+ * Attention diagnostics of LibraryInjector._branch.
+ *
+ * xencb_read_attn replaces record_attn (xenc/injector.py:259-260: last_attn[li] = aw[0, -1]): the route-weighted
+ * slot attention of query row `row` (Library row / rows_per_lib), attn_out [n_chunks, page_rows] float32:
+ *   attn[c, n] = wk[row, j] * softmax_n(read_temp * q[row] . k_cn)   for c = idx[row, j] and n < n_valid
+ *                (read_softmax == 0: wk[row, j] * (q[row] . k_cn) / sqrt(max(n_valid, 1)))
+ *   and 0 for chunks the row was not routed to and for rows past n_valid. Scores in float32 from the slots.
+ * Arguments as xencb_read_decode (idx / wk as xencb_route writes them). */
+XENCB_API int xencb_read_attn(const float* q, int64_t row, int d_s, const void* slots, int slots_dtype,
+                              int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of,
+                              const int32_t* n_valid, int n_chunks, int64_t rows_per_lib, int64_t n_lib,
+                              const int32_t* idx, const float* wk, int k, float read_temp, int read_softmax,
+                              float* attn_out, void* stream);
+
+/* xencb_read_forced replaces the force_attn override (xenc/injector.py:246-258) for one Library (page_of and
+ * n_valid [n_chunks]): the given addressing fa [n_chunks, page_rows] float32 replaces the computed one for every
+ * one of n_rows query rows,
+ *   r_out[t] = s_t * sum_{c, n < n_valid[c]} fa[c, n] v_cn      (v = vslots when untied, else the slots)
+ *   s_t = ||r0[t]|| / (||fa @ K|| + 1e-6) when norm_match (force_norm_match; r0 [n_rows, d_s] is the ordinary
+ *   read, aw @ K), else 1; scale_out [n_rows] (or NULL) receives s_t. Workspace: xencb_read_forced_workspace
+ *   bytes, 256-byte aligned. */
+XENCB_API size_t xencb_read_forced_workspace(int n_chunks, int d_s);
+XENCB_API int xencb_read_forced(const float* fa, int d_s, const void* slots, const void* vslots, int slots_dtype,
+                                int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of,
+                                const int32_t* n_valid, int n_chunks, const float* r0, int64_t n_rows,
+                                int norm_match, float* r_out, float* scale_out, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
 /* Same read as xencb_read_decode, for callers that cannot allocate device memory at all: a host runtime that
  * owns every device byte through its own allocator and offers no way to request scratch, or a serving loop
  * that must not allocate (an allocation may synchronise the device). There is no counterpart of this entry

@@ -45,6 +45,10 @@ SIGNATURES: dict = {
                                _i, _p, _p, _sz, _p]),
     "xencb_read_decode_noalloc": (_i, [_p, _i64, _i, _p, _i, _i64, _i64, _i, _p, _p, _i, _i64, _i64, _p, _p, _i,
                                        _f, _i, _p, _p]),
+    "xencb_read_attn": (_i, [_p, _i64, _i, _p, _i, _i64, _i64, _i, _p, _p, _i, _i64, _i64, _p, _p, _i, _f, _i, _p,
+                             _p]),
+    "xencb_read_forced_workspace": (_sz, [_i, _i]),
+    "xencb_read_forced": (_i, [_p, _i, _p, _p, _i, _i64, _i64, _i, _p, _p, _i, _p, _i64, _i, _p, _p, _p, _sz, _p]),
     "xencb_read_multi_workspace": (_sz, [_i64, _i64, _i, _i, _i, _i]),
     "xencb_read_multi": (_i, [_p, _i64, _i, _p, _p, _i, _i64, _i64, _i, _p, _p, _i, _p, _i64, _i64, _p, _f, _i, _p,
                               _p, _sz, _p]),

@@ -25,6 +25,7 @@
 #include "route.cuh"
 #include "library_build.cuh"
 #include "topk_read.cuh"
+#include "attn.cuh"
 
 // Scratch of xencb_read_decode_noalloc: a fixed device array, so that entry point never allocates.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[XENCB_NOALLOC_SCRATCH_BYTES];
@@ -1626,6 +1627,97 @@ int xencb_wait_selftest(long long limit_cycles, int* result, void* stream) {
   wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_cycles, result);
   XENCB_CHECK_LAUNCH("wait_selftest_kernel launch");
   return XENCB_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ attention diagnostics
+int xencb_read_attn(const float* q, int64_t row, int d_s, const void* slots, int slots_dtype, int64_t n_pages,
+                    int64_t page_stride, int page_rows, const int32_t* page_of, const int32_t* n_valid, int n_chunks,
+                    int64_t rows_per_lib, int64_t n_lib, const int32_t* idx, const float* wk, int k, float read_temp,
+                    int read_softmax, float* attn_out, void* stream) {
+  if (!q || !slots || !page_of || !n_valid || !idx || !wk || !attn_out)
+    return fail(XENCB_EINVAL, "read_attn: q, slots, page_of, n_valid, idx, wk and attn_out are required");
+  if (row < 0 || d_s <= 0 || page_rows <= 0 || n_chunks <= 0 || rows_per_lib <= 0 || n_lib <= 0 || k <= 0 ||
+      n_pages <= 0)
+    return fail(XENCB_EINVAL, "read_attn: sizes must be positive and row >= 0");
+  const int64_t lib = row / rows_per_lib;
+  if (lib >= n_lib) return fail(XENCB_EINVAL, "read_attn: row %lld reads Library %lld of %lld", (long long)row,
+                                (long long)lib, (long long)n_lib);
+  const int es = elem_size(slots_dtype);
+  if (!es) return fail(XENCB_EINVAL, "read_attn: slots_dtype %d unknown", slots_dtype);
+  if (page_stride < (int64_t)page_rows * d_s)
+    return fail(XENCB_EINVAL, "read_attn: page_stride %lld < page_rows*d_s", (long long)page_stride);
+  const size_t smem = ((size_t)d_s + (size_t)page_rows) * sizeof(float);
+  if (smem > 200 * 1024) return fail(XENCB_ENOTSUP, "read_attn: d_s + page_rows = %zu floats exceed shared memory",
+                                     smem / 4);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float* qr = q + row * (int64_t)d_s;
+  const int32_t* po = page_of + lib * n_chunks;
+  const int32_t* nv = n_valid + lib * n_chunks;
+  const int32_t* ir = idx + row * (int64_t)k;
+  const float* wr = wk + row * (int64_t)k;
+  const char* sp = static_cast<const char*>(slots);
+  auto run = [&](auto kern) -> int {
+    int rc = ensure_smem(kern, (int)std::max<size_t>(smem, 48 * 1024));
+    if (rc) return rc;
+    kern<<<(unsigned)n_chunks, AT_THREADS, smem, st>>>(qr, d_s, sp, n_pages, page_stride * es, page_rows, po, nv, ir,
+                                                       wr, k, read_temp, read_softmax, attn_out);
+    XENCB_CHECK_LAUNCH("read_attn launch");
+    return XENCB_OK;
+  };
+  switch (slots_dtype) {
+    case XENCB_F16: return run(read_attn_kernel<__half>);
+    case XENCB_BF16: return run(read_attn_kernel<__nv_bfloat16>);
+    default: return run(read_attn_kernel<float>);
+  }
+}
+
+size_t xencb_read_forced_workspace(int n_chunks, int d_s) {
+  if (n_chunks <= 0 || d_s <= 0) return 0;
+  return 2 * align_up((size_t)n_chunks * d_s * sizeof(float), 256);
+}
+
+int xencb_read_forced(const float* fa, int d_s, const void* slots, const void* vslots, int slots_dtype,
+                      int64_t n_pages, int64_t page_stride, int page_rows, const int32_t* page_of,
+                      const int32_t* n_valid, int n_chunks, const float* r0, int64_t n_rows, int norm_match,
+                      float* r_out, float* scale_out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!fa || !slots || !page_of || !n_valid || !r_out)
+    return fail(XENCB_EINVAL, "read_forced: fa, slots, page_of, n_valid and r_out are required");
+  if (d_s <= 0 || page_rows <= 0 || n_chunks <= 0 || n_rows <= 0 || n_pages <= 0)
+    return fail(XENCB_EINVAL, "read_forced: sizes must be positive");
+  if (norm_match && !r0) return fail(XENCB_EINVAL, "read_forced: force_norm_match needs r0 (the ordinary read)");
+  const int es = elem_size(slots_dtype);
+  if (!es) return fail(XENCB_EINVAL, "read_forced: slots_dtype %d unknown", slots_dtype);
+  if (page_stride < (int64_t)page_rows * d_s)
+    return fail(XENCB_EINVAL, "read_forced: page_stride %lld < page_rows*d_s", (long long)page_stride);
+  const size_t one = align_up((size_t)n_chunks * d_s * sizeof(float), 256);
+  if (!workspace || !aligned(workspace, 256) || workspace_bytes < 2 * one)
+    return fail(XENCB_EINVAL, "read_forced: workspace needs %zu bytes, 256-byte aligned (got %zu)", 2 * one,
+                workspace_bytes);
+  float* part_v = static_cast<float*>(workspace);
+  float* part_k = reinterpret_cast<float*>(static_cast<char*>(workspace) + one);
+  const bool untied = vslots != nullptr;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const dim3 grid((unsigned)n_chunks, (unsigned)((d_s + 4 * AT_THREADS - 1) / (4 * AT_THREADS)));
+  auto run = [&](auto kern) -> int {
+    kern<<<grid, AT_THREADS, 0, st>>>(fa, d_s, static_cast<const char*>(untied ? vslots : slots), n_pages,
+                                      page_stride * es, page_rows, page_of, n_valid, part_v);
+    XENCB_CHECK_LAUNCH("forced_partial launch");
+    if (untied && norm_match) {  // the norm is taken on K (xenc/injector.py:252-254), the read on V
+      kern<<<grid, AT_THREADS, 0, st>>>(fa, d_s, static_cast<const char*>(slots), n_pages, page_stride * es,
+                                        page_rows, page_of, n_valid, part_k);
+      XENCB_CHECK_LAUNCH("forced_partial launch");
+    }
+    forced_rows_kernel<<<(unsigned)n_rows, AT_THREADS, 0, st>>>(part_v, (untied && norm_match) ? part_k : part_v,
+                                                               n_chunks, d_s, norm_match ? r0 : nullptr, r_out,
+                                                               scale_out);
+    XENCB_CHECK_LAUNCH("forced_rows launch");
+    return XENCB_OK;
+  };
+  switch (slots_dtype) {
+    case XENCB_F16: return run(forced_partial_kernel<__half>);
+    case XENCB_BF16: return run(forced_partial_kernel<__nv_bfloat16>);
+    default: return run(forced_partial_kernel<float>);
+  }
 }
 
 int xencb_read_decode_noalloc(const float* q, int64_t n_rows, int d_s, const void* slots, int slots_dtype,

@@ -477,15 +477,51 @@ class LibraryInjector(XEncInjector):
 
     def _graphable(self, h: torch.Tensor, inject: bool, sel) -> bool:
         """The fused hook path can be replayed from a CUDA graph: injection, no selector (its weights change per
-        forward), a fast interface, no calibration or position mask, no grad, not inside a user's capture."""
+        forward), a fast interface, no calibration or position mask, no attention diagnostics, no grad, not inside
+        a user's capture."""
         return (self.cuda_graphs and inject and sel is None and self._fast_interface() and h.is_cuda
-                and self.calib is None and self.pos_mask is None and not torch.is_grad_enabled()
+                and self.calib is None and self.pos_mask is None and not self.record_attn
+                and self.force_attn is None and not torch.is_grad_enabled()
                 and not torch.cuda.is_current_stream_capturing())
 
+    def _check_diagnostics(self) -> None:
+        if self.training_attn and torch.is_grad_enabled():
+            raise NotImplementedError("training_attn keeps the attention for a training loss (autograd); the xencb "
+                                      "read is forward-only")
+
+    def _read_with_diagnostics(self, h: torch.Tensor, li: int, q: torch.Tensor, pages: ops.Pages, idx, wk,
+                               rpl: int, sparse: bool) -> torch.Tensor:
+        """The read of _branch, with force_attn (the given [C, N] addressing replaces the computed one,
+        xenc/injector.py:246-258) and record_attn (last_attn[li] = the last position's route-weighted slot
+        attention of batch row 0, :259-260)."""
+        force = self.force_attn
+        fa = None
+        if force is not None:
+            fa = force.get(li) if isinstance(force, dict) else force
+            if fa is None:
+                raise ValueError(f"force_attn has no addressing for layer {li}")
+            fa = _on(torch.as_tensor(fa), q).float()
+            if tuple(fa.shape) != (pages.n_chunks, pages.page_rows):
+                raise ValueError(f"force_attn {tuple(fa.shape)} != library [C,N] {(pages.n_chunks, pages.page_rows)}")
+        r = None
+        if fa is None or self.force_norm_match:
+            r = ops.read_decode(q, pages, idx, wk, rows_per_lib=rpl, read_temp=self.read_temp,
+                                read_softmax=self.read_softmax, sparse=sparse)
+        scale = None
+        if fa is not None:
+            r, scale = ops.read_forced(fa, pages, q.shape[0], r0=r, norm_match=self.force_norm_match)
+        if self.record_attn:
+            row = (h.shape[-2] if h.dim() >= 3 else h.shape[0]) - 1  # batch row 0, last position
+            if fa is not None:
+                attn = fa * scale[row]
+            else:
+                attn = ops.read_attn(q, pages, idx, wk, row=row, rows_per_lib=rpl, read_temp=self.read_temp,
+                                     read_softmax=self.read_softmax)
+            self.last_attn[li] = attn.detach().float().cpu()
+        return r
+
     def _run_lib(self, h: torch.Tensor, li: int, inject: bool, sel: Optional[LayerSelector]):
-        if self.force_attn is not None or self.record_attn or self.training_attn:
-            raise NotImplementedError("force_attn / record_attn / training_attn diagnostics are not served by the "
-                                      "xencb read")
+        self._check_diagnostics()
         if not self._graphable(h, inject, sel):
             return self._run_lib_eager(h, li, inject, sel)
         # CUDA-graph replay: the first call for a (layer, shape, dtype, Library view) runs eagerly (which also
@@ -526,9 +562,7 @@ class LibraryInjector(XEncInjector):
         return h_new_s.clone(), rel_s.clone()
 
     def _run_lib_eager(self, h: torch.Tensor, li: int, inject: bool, sel: Optional[LayerSelector]):
-        if self.force_attn is not None or self.record_attn or self.training_attn:
-            raise NotImplementedError("force_attn / record_attn / training_attn diagnostics are not served by the "
-                                      "xencb read")
+        self._check_diagnostics()
         self._check_forward_only(h)
         if sel is not None and _needs_grad(sel):
             raise RuntimeError("the xencb Library read is forward-only; freeze the LayerSelector or use no_grad")
@@ -571,8 +605,11 @@ class LibraryInjector(XEncInjector):
             idx, wk, w, _ = ops.route(q, pages.S, rows_per_lib=rpl, top_k=self.top_k, route_temp=self.route_temp,
                                       n_chunks_of=pages.n_chunks_of, row_w=sel_col)
         # with a selector most rows read nothing at most depths: the sparse plan spreads the live rows' work
-        r = ops.read_decode(q, pages, idx, wk, rows_per_lib=rpl, read_temp=self.read_temp,
-                            read_softmax=self.read_softmax, sparse=sel_col is not None)
+        if self.record_attn or self.force_attn is not None:
+            r = self._read_with_diagnostics(h, li, q, pages, idx, wk, rpl, sparse=sel_col is not None)
+        else:
+            r = ops.read_decode(q, pages, idx, wk, rows_per_lib=rpl, read_temp=self.read_temp,
+                                read_softmax=self.read_softmax, sparse=sel_col is not None)
         self.last_route = w.view(*lead, pages.n_chunks)
         if torch.is_grad_enabled():
             self.route_terms.append((li, self.last_route))

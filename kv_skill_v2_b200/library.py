@@ -155,9 +155,13 @@ class Library:
     def pages(self, li: int, device, slot_dtype="auto", require_nonempty: bool = True) -> Pages:
         """The paged view of layer `li` on `device` (built once and cached).
 
-        slot_dtype "auto" keeps float32 slots in float16 when that is exact (it is for Libraries built from
-        doc caches, which store float16 rows), else in their own dtype. An empty chunk is rejected when
-        `require_nonempty`: the reference's softmax read returns NaN for such a Library."""
+        slot_dtype "auto" stores float32 rows as float16 slots, exactly for Libraries built from doc caches
+        (float16 rows), rounded otherwise (centred Libraries: L2(K - mu) is not float16-exact) when the values fit
+        float16's range; the summary keys S are kept from the float32 rows, so routing is unchanged, and the read
+        of rounded rows stays within the path's 2e-3 output bound (each element moves by at most 2^-11 of itself).
+        This keeps every float32 Library on the tensor-core read; slot_dtype=torch.float32 keeps float32 slots
+        (the CUDA-core read). An empty chunk is rejected when `require_nonempty`: the reference's softmax read
+        returns NaN for such a Library."""
         device = torch.device(device)
         key = (li, str(device), str(slot_dtype))
         hit = self._page_cache.get(key)
@@ -185,9 +189,8 @@ class Library:
 def _slot_storage(K: torch.Tensor, slot_dtype) -> torch.Tensor:
     if slot_dtype == "auto":
         if K.dtype == torch.float32:
-            h = K.to(torch.float16)
-            if torch.equal(h.to(torch.float32), K):
-                return h
+            if bool(torch.isfinite(K).all()) and float(K.abs().max()) <= 65504.0:
+                return K.to(torch.float16)
             return K
         if K.dtype in (torch.float16, torch.bfloat16):
             return K
@@ -312,9 +315,10 @@ class PagedLibrary:
         per depth, every doc's chunk rows go to the device in one copy and one build launch pads them into
         pages, centres them when `center` is given and computes S from the float32 rows.
 
-        slot_dtype "auto": float16 for uncentred keys (the cache's rows are float16, so the copy is exact),
-        float32 for centred keys of a tied Library (the read then matches the reference's float32 Library),
-        float16 for an untied one (its read runs on the tensor cores)."""
+        slot_dtype "auto": float16 (the cache's rows are float16, so the copy of uncentred keys is exact; centred
+        keys are rounded to float16 after the centring, with S from the float32 rows, so routing is unchanged and
+        the read stays within the path's 2e-3 bound on the tensor-core kernel); torch.float32 keeps centred keys in
+        float32 (the CUDA-core read)."""
         from .ops import library_build
 
         if not caches:
@@ -346,7 +350,7 @@ class PagedLibrary:
                 except KeyError:
                     mu = None
             if slot_dtype == "auto":
-                dt = torch.float32 if (mu is not None and not untied) else torch.float16
+                dt = torch.float16
             else:
                 dt = slot_dtype
             flat = torch.cat([r.reshape(-1, r.shape[-1]) for r in krows]).contiguous()

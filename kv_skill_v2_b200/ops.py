@@ -361,6 +361,56 @@ def read_decode(q: torch.Tensor, pages: Pages, idx: torch.Tensor, wk: torch.Tens
     return r
 
 
+def read_attn(q: torch.Tensor, pages: Pages, idx: torch.Tensor, wk: torch.Tensor, *, row: int, rows_per_lib: int,
+              read_temp: float = 12.0, read_softmax: bool = True) -> torch.Tensor:
+    """[C, page_rows] float32: the route-weighted slot attention of query row `row` (record_attn,
+    xenc/injector.py:259-260); zeros for chunks the row was not routed to and rows past n_valid."""
+    dev = _cuda("read_attn", q, pages.slots, pages.page_of, pages.n_valid, idx, wk)
+    q = _f32(q, "q")
+    wk = _f32(wk, "wk")
+    R, d_s = q.shape
+    if not 0 <= int(row) < R:
+        raise ValueError(f"read_attn: row {row} outside [0, {R})")
+    if idx.dtype != torch.int32 or idx.shape != wk.shape or idx.shape[0] != R:
+        raise ValueError("read_attn: idx must be int32 [R, k] matching wk")
+    idx = idx.contiguous()
+    out = torch.empty(pages.n_chunks, pages.page_rows, dtype=torch.float32, device=dev)
+    slots = pages.slots
+    with _on_device(dev):
+        N.call("xencb_read_attn", _ptr(q), int(row), d_s, _ptr(slots), _hdt(slots, "slots"), slots.shape[0],
+               pages.page_rows * d_s, pages.page_rows, _ptr(pages.page_of), _ptr(pages.n_valid), pages.n_chunks,
+               int(rows_per_lib), pages.n_lib, _ptr(idx), _ptr(wk), int(idx.shape[1]), float(read_temp),
+               int(bool(read_softmax)), _ptr(out), _stream(dev))
+    return out
+
+
+def read_forced(fa: torch.Tensor, pages: Pages, n_rows: int, *, r0: Optional[torch.Tensor] = None,
+                norm_match: bool = False):
+    """(r [n_rows, d_s], scale [n_rows]): the read with the given addressing fa [C, page_rows] in place of the
+    computed one (force_attn, xenc/injector.py:246-258); with norm_match each row is scaled to ||r0[row]|| (r0 the
+    ordinary read) over ||fa @ K||. One Library."""
+    dev = _cuda("read_forced", fa, pages.slots, pages.page_of, pages.n_valid, r0)
+    if pages.n_lib != 1:
+        raise NotImplementedError("read_forced: force_attn addresses one Library")
+    fa = _f32(fa, "force_attn")
+    C, P = pages.n_chunks, pages.page_rows
+    if tuple(fa.shape) != (C, P):
+        raise ValueError(f"force_attn {tuple(fa.shape)} != library [C,N] {(C, P)}")
+    d_s = pages.d_s
+    r0 = _f32(r0, "r0")
+    if norm_match and (r0 is None or tuple(r0.shape) != (int(n_rows), d_s)):
+        raise ValueError(f"read_forced: norm_match needs r0 [{n_rows}, {d_s}]")
+    r = torch.empty(int(n_rows), d_s, dtype=torch.float32, device=dev)
+    scale = torch.empty(int(n_rows), dtype=torch.float32, device=dev)
+    slots = pages.slots
+    with _on_device(dev):
+        ws = _workspace(N.lib().xencb_read_forced_workspace(C, d_s), dev)
+        N.call("xencb_read_forced", _ptr(fa), d_s, _ptr(slots), _ptr(_vpool(pages)), _hdt(slots, "slots"),
+               slots.shape[0], P * d_s, P, _ptr(pages.page_of), _ptr(pages.n_valid), C, _ptr(r0), int(n_rows),
+               int(bool(norm_match)), _ptr(r), _ptr(scale), _ptr(ws), ws.numel(), _stream(dev))
+    return r, scale
+
+
 def read_multi(q: torch.Tensor, pages: Pages, w: torch.Tensor, *, rows_per_lib: int, read_temp: float = 12.0,
                read_softmax: bool = True, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """r [R, d_s] float32 = sum_c w[row, c] * read(q[row], chunk c): the many-query read, in which up to 8 rows of

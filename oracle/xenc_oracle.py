@@ -159,6 +159,40 @@ def read(q: np.ndarray, K: np.ndarray, M: np.ndarray, w: np.ndarray, read_temp: 
     return (aw.reshape(q.shape[0], C * N) @ Vf).astype(F32)
 
 
+def route_attn(q: np.ndarray, K: np.ndarray, M: np.ndarray, w: np.ndarray, read_temp: float = 12.0,
+               read_softmax: bool = True) -> np.ndarray:
+    """The route-weighted slot attention aw = a * w of LibraryInjector._branch (xenc/injector.py:239-245):
+    [R, C, N]; record_attn keeps aw of the last position of batch row 0 (:259-260)."""
+    q = np.asarray(q, dtype=F32)
+    C, N, d = K.shape
+    a = (q @ K.reshape(C * N, d).T).reshape(q.shape[0], C, N).astype(F32)
+    if read_softmax:
+        a = softmax(np.where(M[None], a * F32(read_temp), F32(-np.inf)), -1)
+    else:
+        n = np.maximum(M.sum(-1), 1).astype(F32)
+        a = (np.where(M[None], a, F32(0)) / np.sqrt(n, dtype=F32)[None, :, None]).astype(F32)
+    return (a * np.asarray(w, dtype=F32)[..., None]).astype(F32)
+
+
+def forced_read(fa: np.ndarray, K: np.ndarray, aw: np.ndarray | None = None, norm_match: bool = False,
+                V: np.ndarray | None = None):
+    """force_attn (xenc/injector.py:246-258): the given addressing fa [C, N] replaces aw for every token; with
+    force_norm_match it is scaled per token so that ||fa @ K|| = ||aw @ K||. Returns (r [R, d_s], aw_used
+    [R, C, N]); R is aw's row count (1 when aw is None)."""
+    fa = np.asarray(fa, dtype=F32)
+    C, N, d = K.shape
+    Kf = K.reshape(C * N, d)
+    R = 1 if aw is None else aw.shape[0]
+    use = np.broadcast_to(fa, (R, C, N)).astype(F32)
+    if norm_match:
+        r0 = aw.reshape(R, C * N) @ Kf
+        r1 = use.reshape(R, C * N) @ Kf
+        scale = np.linalg.norm(r0, axis=-1, keepdims=True) / (np.linalg.norm(r1, axis=-1, keepdims=True) + F32(EPS))
+        use = (use * scale.astype(F32)[:, :, None]).astype(F32)
+    Vf = Kf if V is None else np.asarray(V, dtype=F32).reshape(C * N, d)
+    return (use.reshape(R, C * N) @ Vf).astype(F32), use
+
+
 def branch(h: np.ndarray, W_in: np.ndarray, W_out: np.ndarray, K: np.ndarray, M: np.ndarray,
            S: np.ndarray, read_temp: float = 12.0, route_temp: float = 10.0, top_k: int = 0,
            read_softmax: bool = True, b_in=None, b_out=None, gate_w=None, gate_b: float = 0.0,
@@ -242,7 +276,7 @@ def merge_shards(parts: list) -> np.ndarray:
 
 
 __all__ = ["l2", "rms_norm", "softmax", "topk_indices", "build_library", "summaries", "subset", "query",
-           "gate", "route", "read", "branch", "selector_weights", "selector_logits", "selector_apply",
+           "gate", "route", "read", "route_attn", "forced_read", "branch", "selector_weights", "selector_logits", "selector_apply",
            "rel_norm", "shard_partials", "merge_shards"]
 
 

@@ -315,6 +315,53 @@ def gen_batch_docs(out):
                               "read_temp": np.float32(12.0), "route_temp": np.float32(10.0)}
 
 
+def gen_attn(out):
+    """LibraryInjector's attention diagnostics (xenc/injector.py:246-260): record_attn (last_attn[li] = the
+    last position's route-weighted slot attention of batch row 0, [C, N]) for a softmax top-k read and a linear
+    dense read, and force_attn (a given [C, N] addressing in place of the computed one), with and without
+    force_norm_match. Two batch rows, three positions, a ragged Library."""
+    from xenc.injector import LibraryInjector
+    from xenc.library import Library
+
+    g = torch.Generator().manual_seed(41)
+    d_s, d_m, C, N, rho, L = 48, 64, 5, 24, 0.5, 8
+    counts = [24, 9, 24, 17, 3]
+    rows = [_unit_rows(n, d_s, g) for n in counts]
+    h = torch.randn(2, 3, d_m, generator=g)
+    W_in = torch.randn(d_m, d_s, generator=g) * 0.2
+    W_out = torch.randn(d_s, d_m, generator=g) * 0.2
+    fa = torch.rand(C, N, generator=g) * (torch.arange(N).view(1, N) < torch.tensor(counts).view(C, 1))
+    fa = fa / fa.sum()
+    reader = FakeReader(8, L, 0)
+    li = min(L - 1, int(rho * L))
+    base = {"K": _np(_pad(rows)), "n_valid": np.array(counts, np.int32), "h": _np(h), "W_in": _np(W_in),
+            "W_out": _np(W_out), "force": _np(fa), "layer": np.int32(li)}
+    for name, top_k, sm, force, norm in (("attn_record_top2", 2, True, False, False),
+                                         ("attn_record_linear", 0, False, False, False),
+                                         ("attn_force", 2, True, True, False),
+                                         ("attn_force_norm", 2, True, True, True)):
+        lib = Library([{"K": {rho: r}} for r in rows], [li], [rho])
+        itf = Recorder(W_in, W_out)
+        itf.inject_layers = [li]
+        inj = LibraryInjector(reader, itf, read_softmax=sm, read_temp=12.0, route_temp=10.0, top_k=top_k)
+        inj.load_library(lib)
+        inj.record_attn = True
+        if force:
+            inj.force_attn = {li: fa}
+            inj.force_norm_match = norm
+        with torch.no_grad():
+            delta = inj._branch(h, li)
+        rec = {"w": _np(inj.last_route), "r": _np(itf.rs[-1]), "delta": _np(delta), "last_attn": _np(inj.last_attn[li]),
+               "top_k": np.int32(top_k), "read_softmax": np.int32(sm), "force_norm_match": np.int32(norm),
+               "read_temp": np.float32(12.0), "route_temp": np.float32(10.0)}
+        if name == "attn_record_top2":
+            rec.update(base)
+        else:
+            rec["inputs"] = np.array("attn_record_top2")
+        out[name] = rec
+        inj.detach()
+
+
 def gen_selector(out):
     from deltaskill.derive import rms_norm
     from xenc.selector import LayerSelector
@@ -517,7 +564,8 @@ def main() -> None:
     torch.set_num_threads(1)
     out: dict = {}
     gens = {"cfg1": gen_cfg1, "small": gen_small, "batch_docs": gen_batch_docs, "selector": gen_selector,
-            "library": gen_library, "hooked": gen_hooked, "untied": gen_untied, "topk": gen_topk}
+            "library": gen_library, "hooked": gen_hooked, "untied": gen_untied, "topk": gen_topk,
+            "attn": gen_attn}
     wanted = sys.argv[1:] or list(gens)  # e.g. `python make_golden.py untied` regenerates one group
     for nm in wanted:
         gens[nm](out)

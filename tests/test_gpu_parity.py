@@ -12,7 +12,7 @@ import pytest
 import torch
 
 from oracle import xenc_oracle as X
-from tests._fixtures import TOL, TinyReader, load_case, rel_err, topk_sets
+from tests._fixtures import GOLDEN, TOL, TinyReader, load_case, rel_err, topk_sets
 
 pytestmark = pytest.mark.gpu
 
@@ -735,4 +735,38 @@ def test_project_in_route_matches_the_two_calls(dev, case):
     assert (g0 is None and g1 is None) or torch.equal(g0, g1)
     assert torch.equal(l0, l1), "routing logits differ"
     assert torch.equal(i0, i1) and torch.equal(k0, k1) and torch.equal(w0, w1)
+    _status_clean(dev)
+
+
+@pytest.mark.parametrize("name", ["attn_record_top2", "attn_record_linear", "attn_force", "attn_force_norm"])
+def test_attention_diagnostics_against_reference(dev, name):
+    """record_attn (last_attn[li]: the last position's route-weighted slot attention of batch row 0) and force_attn
+    (a given [C, N] addressing replacing the computed one, with and without force_norm_match) through
+    LibraryInjector, against the reference's own LibraryInjector run (xenc/injector.py:246-262)."""
+    from kv_skill_v2_b200 import Library, LibraryInjector, LinearInterface
+    c = load_case(name)
+    base = dict(np.load(GOLDEN / "attn_record_top2.npz"))
+    li = int(base["layer"])
+    K, nv = base["K"], base["n_valid"]
+    lib = Library([{"K": {0.5: torch.from_numpy(K[i, :n]).float()}} for i, n in enumerate(nv)], [li], [0.5])
+    reader = TinyReader(8, 8).to(dev)
+    itf = LinearInterface(torch.from_numpy(base["W_in"]), torch.from_numpy(base["W_out"]), [li]).to(dev)
+    inj = LibraryInjector(reader, itf, top_k=int(c["top_k"]), read_softmax=bool(c["read_softmax"]),
+                          read_temp=float(c["read_temp"]), route_temp=float(c["route_temp"]))
+    inj.load_library(lib)
+    inj.record_attn = True
+    if name.startswith("attn_force"):
+        inj.force_attn = {li: torch.from_numpy(base["force"])}
+        inj.force_norm_match = bool(c["force_norm_match"])
+    with torch.no_grad():
+        delta = inj._branch(torch.from_numpy(base["h"]).to(dev), li)
+    assert topk_sets(inj.last_route) == topk_sets(c["w"])
+    assert inj.last_attn[li].device.type == "cpu" and tuple(inj.last_attn[li].shape) == c["last_attn"].shape
+    assert rel_err(inj.last_attn[li], c["last_attn"]) < (TOL if name == "attn_force_norm" else 1e-5)
+    assert rel_err(delta, c["delta"]) < TOL
+    inj.force_attn = {li: torch.zeros(3, 3)}
+    with pytest.raises(ValueError, match="force_attn"):
+        with torch.no_grad():
+            inj._branch(torch.from_numpy(base["h"]).to(dev), li)
+    inj.detach()
     _status_clean(dev)

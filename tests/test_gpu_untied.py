@@ -185,3 +185,31 @@ def test_untied_float32_slots_are_refused(dev):
     idx, wk, _, _ = ops.route(q, pages.S, rows_per_lib=2, top_k=2, route_temp=10.0)
     with pytest.raises(NotImplementedError):
         ops.read_decode(q, pages, idx, wk, rows_per_lib=2)
+
+
+def test_centered_library_reads_float16_slots_against_oracle(dev):
+    """A centred tied Library (K = L2(K - mu), xenc/library.py:56-58: float32 rows that float16 does not hold
+    exactly) is stored as float16 slots by default, so it is read by the tensor-core kernel; S comes from the
+    float32 rows. Routing matches the oracle's exactly and the read is within the path's tolerance of the oracle's
+    float32 read; slot_dtype=torch.float32 keeps float32 slots."""
+    from kv_skill_v2_b200 import Library, ops
+    from oracle import xenc_oracle as X
+    g = torch.Generator().manual_seed(31)
+    d, counts = 256, (64, 40, 64, 17, 64)
+    rows = [torch.randn(n, d, generator=g) for n in counts]
+    mu = torch.randn(d, generator=g) * 0.3
+    lib = Library([{"K": {0.5: r}} for r in rows], [3], [0.5], center={0.5: mu})
+    K_ref, M_ref, S_ref = X.build_library([r.numpy() for r in rows], mu.numpy())
+    pages = lib.pages(3, dev)
+    assert pages.slots.dtype == torch.float16
+    assert lib.pages(3, dev, slot_dtype=torch.float32).slots.dtype == torch.float32
+    assert rel_err(pages.S[0], S_ref) < 1e-5
+    q = torch.nn.functional.normalize(torch.randn(6, d, generator=g), dim=-1)
+    w_ref, _, _ = X.route(q.numpy(), S_ref, 10.0, 2)
+    r_ref = X.read(q.numpy(), K_ref, M_ref, w_ref, 12.0, True)
+    qd = q.to(dev)
+    idx, wk, w, _ = ops.route(qd, pages.S, rows_per_lib=6, top_k=2, route_temp=10.0)
+    assert topk_sets(w) == topk_sets(w_ref)
+    r = ops.read_decode(qd, pages, idx, wk, rows_per_lib=6)
+    assert rel_err(r, r_ref) < TOL
+    _status_clean(dev)

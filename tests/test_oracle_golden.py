@@ -204,3 +204,30 @@ def test_topk_oracle_matches_reference(name):
     assert [set(r) for r in idx.tolist()] == [set(r) for r in c["idx"].tolist()]
     assert np.array_equal(idx, c["idx"]), "selection order (score descending) differs"
     assert rel_err(lg, c["logits"]) < 1e-5
+
+
+ATTN_CASES = ["attn_record_top2", "attn_record_linear", "attn_force", "attn_force_norm"]
+
+
+@pytest.mark.parametrize("name", ATTN_CASES)
+def test_attention_diagnostics_oracle_matches_reference(name):
+    """record_attn's last_attn and force_attn's read (with and without force_norm_match) of the reference's
+    LibraryInjector (xenc/injector.py:246-262), restated with X.route_attn / X.forced_read."""
+    c = load_case(name)
+    base = dict(np.load(G / "attn_record_top2.npz"))  # the inputs every case shares, the forced addressing too
+    K = base["K"].astype(np.float32)
+    C, N, _ = K.shape
+    M = np.arange(N)[None, :] < base["n_valid"][:, None]
+    h = base["h"]
+    B, T, d_m = h.shape
+    q = X.query(X.rms_norm(h.reshape(-1, d_m)), base["W_in"])
+    w, _, _ = X.route(q, X.summaries(K, M), float(c["route_temp"]), int(c["top_k"]))
+    assert topk_sets(w) == topk_sets(c["w"].reshape(-1, C))
+    aw = X.route_attn(q, K, M, w, float(c["read_temp"]), bool(c["read_softmax"]))
+    if name.startswith("attn_force"):
+        r, aw = X.forced_read(base["force"], K, aw, bool(c["force_norm_match"]))
+    else:
+        r = (aw.reshape(B * T, C * N) @ K.reshape(C * N, -1)).astype(np.float32)
+    assert rel_err(aw[T - 1], c["last_attn"]) < 1e-5  # batch row 0, last position
+    assert rel_err(r, c["r"].reshape(B * T, -1)) < 1e-5
+    assert rel_err(r @ base["W_out"], c["delta"].reshape(B * T, -1)) < 1e-5
