@@ -342,12 +342,14 @@ struct PinArgs {
   float* z_out;
 };
 
-// First half (before the wait): (sum of h^2, gate dot); the selector's logit dots go to zsh[n_cand].
+// First half (before the wait): (sum of h^2, gate dot); the selector's logit dots go to zsh[n_cand] (skipped when
+// `sel` is false: a CTA that writes no outputs).
 template <typename TH>
-__device__ __forceinline__ float2 pin_row_pre(const TH* __restrict__ hr, const PinArgs& a, float* zsh) {
+__device__ __forceinline__ float2 pin_row_pre(const TH* __restrict__ hr, const PinArgs& a, float* zsh,
+                                              bool sel = true) {
   float ss, gd, unused;
   row_dots<TH>(hr, a.d_m, a.gate_w, nullptr, ss, gd, unused);
-  if (a.sel_w) {
+  if (a.sel_w && sel) {
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
     for (int c = wid; c < a.n_cand; c += nw) {
       const float* u = a.sel_w + (int64_t)c * a.d_m;
@@ -361,10 +363,12 @@ __device__ __forceinline__ float2 pin_row_pre(const TH* __restrict__ hr, const P
 }
 
 // Second half (after the wait): q's columns n[v] (ok[v]: inside d_s) in o[v], written to q_out; 1/rms, the gate
-// and the selector logits written too (each output skipped when its pointer is null).
+// and the selector logits written too (each output skipped when its pointer is null, all of them when `write` is
+// false).
 template <int VPT>
 __device__ __forceinline__ void pin_row_post(const PinArgs& a, int64_t row, float2 pre, const float* zsh,
-                                             float2* red2, float* red, float4* o, int* n, bool* ok) {
+                                             float2* red2, float* red, float4* o, int* n, bool* ok,
+                                             bool write = true) {
 #pragma unroll
   for (int q = 0; q < VPT; ++q) {
     n[q] = (threadIdx.x + q * blockDim.x) * 4;
@@ -374,14 +378,14 @@ __device__ __forceinline__ void pin_row_post(const PinArgs& a, int64_t row, floa
   sum_splits_row<VPT>(a.part, a.splits, a.M, a.d_s, row, n, ok, v);
   const float2 t = block_sum2(pre.x, pre.y, red2);  // (its barrier also publishes zsh)
   const float rstd = (a.flags & XENCB_PIN_RMS) ? rsqrtf(t.x / (float)a.d_m + a.eps) : 1.f;
-  if (threadIdx.x == 0) {
+  if (write && threadIdx.x == 0) {
     if (a.rstd_out) a.rstd_out[row] = rstd;
     if (a.gate_w && a.gate_out) {
       const float gb = a.gate_b_dev ? __ldg(a.gate_b_dev) : a.gate_b;
       a.gate_out[row] = 1.f / (1.f + expf(-(t.y * rstd + gb)));
     }
   }
-  if (a.sel_w && a.z_out && threadIdx.x < a.n_cand)
+  if (write && a.sel_w && a.z_out && threadIdx.x < a.n_cand)
     a.z_out[row * a.n_cand + threadIdx.x] = zsh[threadIdx.x] * rstd + (a.sel_b ? a.sel_b[threadIdx.x] : 0.f);
   float nq = 0.f;
 #pragma unroll
@@ -402,7 +406,7 @@ __device__ __forceinline__ void pin_row_post(const PinArgs& a, int64_t row, floa
 #pragma unroll
     for (int q = 0; q < VPT; ++q) { o[q].x /= den; o[q].y /= den; o[q].z /= den; o[q].w /= den; }
   }
-  if (a.q_out) {
+  if (write && a.q_out) {
 #pragma unroll
     for (int q = 0; q < VPT; ++q)
       if (ok[q]) *reinterpret_cast<float4*>(a.q_out + row * a.d_s + n[q]) = o[q];

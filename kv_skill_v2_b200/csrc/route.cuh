@@ -359,8 +359,16 @@ struct RouteFuse {
   float* wk;
   float* w_dense;
   float* logit_out;
+  // With gridDim.y = G > 1 CTAs per row: the row's logits pass through xlg [n_rows, C] (global), and done[row]
+  // (zeroed by the projection GEMM of the same call) counts the CTAs that stored theirs.
+  float* xlg;
+  int* done;
 };
 
+// Grid (n_rows, G). CTA (row, g) computes the row's q (every CTA the same values; only g = 0 writes q, 1/rms, the
+// gate and the selector logits) and the dot products of chunks [g * per, (g + 1) * per), per = ceil(C / G): the
+// row's summary keys stream through G SMs instead of one. With G > 1 each CTA stores its logits in xlg, and the
+// CTA that counts last in done[row] (after a fence) reads the whole row back and runs the top-k.
 template <typename TH, int VPT>
 __global__ void __launch_bounds__(ROW_THREADS) project_in_route_kernel(const TH* __restrict__ h, const PinArgs a,
                                                                       const RouteFuse rf) {
@@ -368,18 +376,23 @@ __global__ void __launch_bounds__(ROW_THREADS) project_in_route_kernel(const TH*
   __shared__ float2 red2[32];
   __shared__ float red[32];
   __shared__ float zsh[32];
+  __shared__ int last_sh;
   pdl_trigger();
   const int64_t row = blockIdx.x;
+  const int G = (int)gridDim.y, g = (int)blockIdx.y;
   const int64_t lib = row / rf.rows_per_lib;
   const int nc = rf.n_chunks_of ? min(rf.n_chunks_of[lib], rf.C) : rf.C;
+  const int per = (rf.C + G - 1) / G;
+  const int c_lo = g * per, c_hi = min(rf.C, c_lo + per);
   const float* s_lib = rf.S + lib * rf.C * (int64_t)a.d_s;
-  for (int c = threadIdx.x; c < nc; c += blockDim.x) prefetch_l2_bulk(s_lib + (int64_t)c * a.d_s, (uint32_t)a.d_s * 4u);
-  const float2 pre = pin_row_pre<TH>(h + row * a.d_m, a, zsh);
+  for (int c = c_lo + (int)threadIdx.x; c < min(c_hi, nc); c += blockDim.x)
+    prefetch_l2_bulk(s_lib + (int64_t)c * a.d_s, (uint32_t)a.d_s * 4u);
+  const float2 pre = pin_row_pre<TH>(h + row * a.d_m, a, zsh, g == 0);
   pdl_wait();
   float4 o[VPT];
   int n[VPT];
   bool ok[VPT];
-  pin_row_post<VPT>(a, row, pre, zsh, red2, red, o, n, ok);
+  pin_row_post<VPT>(a, row, pre, zsh, red2, red, o, n, ok, g == 0);
   float* qs = pr_sh;
   float* lg = pr_sh + a.d_s;
 #pragma unroll
@@ -387,18 +400,31 @@ __global__ void __launch_bounds__(ROW_THREADS) project_in_route_kernel(const TH*
     if (ok[q]) *reinterpret_cast<float4*>(qs + n[q]) = o[q];
   __syncthreads();
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int c = w; c < rf.C; c += nw) {
+  float* xr = G > 1 ? rf.xlg + row * rf.C : nullptr;
+  for (int c = c_lo + w; c < c_hi; c += nw) {
     float l = -CUDART_INF_F;
     if (c < nc) l = route_dot(qs, s_lib + (int64_t)c * a.d_s, a.d_s, lane) * rf.temp;
     if (lane == 0) {
-      lg[c] = l;
-      if (rf.logit_out) rf.logit_out[row * rf.C + c] = l;
+      if (xr) xr[c] = l;
+      else lg[c] = l;
+      if (rf.logit_out && rf.logit_out != rf.xlg) rf.logit_out[row * rf.C + c] = l;
     }
   }
   __syncthreads();
-  if (w == 0)
-    topk_row(lg, lg + rf.C, rf.C, nc, rf.top_k, rf.k_out, rf.row_w ? rf.row_w[row] : 1.f, rf.idx + row * rf.k_out,
-             rf.wk + row * rf.k_out, rf.w_dense ? rf.w_dense + row * rf.C : nullptr, lane);
+  if (G > 1) {
+    if (threadIdx.x == 0) {
+      __threadfence();  // this CTA's logits (ordered before by the barrier) become visible before the count
+      last_sh = atomicAdd(rf.done + row, 1) == G - 1;
+      if (last_sh) __threadfence();
+    }
+    __syncthreads();
+    if (!last_sh) return;
+    for (int c = threadIdx.x; c < rf.C; c += blockDim.x) lg[c] = __ldcg(xr + c);
+    __syncthreads();
+  }
+  if (w != 0) return;
+  topk_row(lg, lg + rf.C, rf.C, nc, rf.top_k, rf.k_out, rf.row_w ? rf.row_w[row] : 1.f, rf.idx + row * rf.k_out,
+           rf.wk + row * rf.k_out, rf.w_dense ? rf.w_dense + row * rf.C : nullptr, lane);
 }
 
 // Decode routing in one launch: a cluster of RF_CL CTAs (RF_CL * 8 warps) takes `rpc` consecutive rows. Its warps

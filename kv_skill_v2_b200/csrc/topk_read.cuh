@@ -216,6 +216,126 @@ __global__ void __launch_bounds__(SEL_THREADS) select_scores_kernel(const Select
   }
 }
 
+// One query position, f16 keys, GQA groups G <= 4, head rows of 32 P2 elements (P2 = 1, 2, 4): the dot
+// products on the tensor cores. Per KV head, an m16n8k16 chain scores 16 slots (MMA rows) against 8 columns: the
+// group's G query heads rounded to f16 (hi) and their remainders q - hi (lo), both after a power-of-two scale per
+// (row, KV head) that puts max|q| in [2^13, 2^14); the score of head h is (D[:, h] + D[:, G + h]) / scale. The keys
+// are exact in f16 and the products exact in the f32 accumulator, so the error is that of a ~22-bit q (the same
+// 1e-5 bar as the f32 path). The A fragments are loaded from global memory directly: lane (g, t) reads 16 bytes
+// of slot rows g and g + 8 at element 32 j + 8 t of the head row, so four lanes cover 64 contiguous bytes of a
+// row; this assigns the contraction index of k-step 2 j + e as  kk -> 32 j + 8 (kk % 8 / 2) + 4 e + 2 (kk / 8)
+// + kk % 2, and the B fragments (q) follow the same map. Warp w takes KV heads w, w + 8, ... over the CTA's
+// SEL_TILE slots, two 16-slot groups of loads in flight; the per-head pooling goes through a 16 x 8 shared tile
+// per warp, the pooling over KV heads and the validity as in select_scores_kernel.
+constexpr int SELM_GROUPS = SEL_TILE / 16;
+
+template <int G, int P2>
+__global__ void __launch_bounds__(SEL_THREADS, 2) select_scores_mma_kernel(const SelectArgs a) {
+  __shared__ float red[SEL_MAX_KV][SEL_TILE];
+  __shared__ float dt[SEL_THREADS / 32][16][9];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int64_t row = blockIdx.y;
+  const int64_t lib = row / a.rows_per_lib;
+  const int S = a.n_chunks * a.page_rows;
+  const int base = blockIdx.x * SEL_TILE;
+  const int hd = 32 * P2;
+  const int d_k = a.n_kv * hd;
+  const __half* kb = static_cast<const __half*>(a.keys) + lib * a.keys_lib_stride;
+  const float* qrow = a.q + row * (int64_t)a.n_q * hd;
+  const float init_h = a.h_pool == 0 ? -CUDART_INF_F : 0.f;
+  float (*tile)[9] = dt[warp];
+  for (int kv = warp; kv < a.n_kv; kv += SEL_THREADS / 32) {
+    const float* qk = qrow + (int64_t)kv * G * hd;
+    uint4 ra[2][P2], rb[2][P2];
+    auto load = [&](int gi) {
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        int s0 = base + 16 * (gi + u) + g, s1 = s0 + 8;
+        s0 = s0 < S ? s0 : S - 1;  // slots past S read the last slot, never stored
+        s1 = s1 < S ? s1 : S - 1;
+        const __half* p0 = kb + (int64_t)s0 * d_k + kv * hd + 8 * t;
+        const __half* p1 = kb + (int64_t)s1 * d_k + kv * hd + 8 * t;
+#pragma unroll
+        for (int j = 0; j < P2; ++j) {
+          ra[u][j] = __ldg(reinterpret_cast<const uint4*>(p0 + 32 * j));
+          rb[u][j] = __ldg(reinterpret_cast<const uint4*>(p1 + 32 * j));
+        }
+      }
+    };
+    load(0);  // the first keys are in flight while q is prepared
+    // scale: a power of two that puts the group's max|q| in [2^13, 2^14)
+    float mx = 0.f;
+    for (int i = lane; i < G * hd; i += 32) mx = fmaxf(mx, fabsf(__ldg(qk + i)));
+    mx = warp_max(mx);
+    int ex = 0;
+    if (mx > 0.f && mx <= 3.0e38f) frexpf(mx, &ex);
+    const float sc = (mx > 0.f && mx <= 3.0e38f) ? ldexpf(1.f, 14 - ex) : 1.f;
+    const float inv = 1.f / sc;  // exact: a power of two
+    // B fragments: column g is hi of head g (g < G), lo of head g - G (G <= g < 2 G), else 0
+    uint32_t bq[4 * P2][2];
+#pragma unroll
+    for (int ks = 0; ks < 4 * P2; ++ks) {
+      const int e0 = 32 * (ks >> 1) + 8 * t + 4 * (ks & 1);
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      if (g < 2 * G) {
+        const float* qh = qk + (g % G) * hd + e0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float x = __ldg(qh + i) * sc;
+          const float hi = __half2float(__float2half_rn(x));
+          v[i] = g < G ? hi : x - hi;
+        }
+      }
+      float r0, r1;
+      bq[ks][0] = pack2<__half>(v[0], v[1], r0, r1);
+      bq[ks][1] = pack2<__half>(v[2], v[3], r0, r1);
+    }
+    for (int gi = 0; gi < SELM_GROUPS; gi += 2) {
+      if (gi) load(gi);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < P2; ++j) {
+          mma16816<__half>(d, ra[u][j].x, rb[u][j].x, ra[u][j].y, rb[u][j].y, bq[2 * j][0], bq[2 * j][1]);
+          mma16816<__half>(d, ra[u][j].z, rb[u][j].z, ra[u][j].w, rb[u][j].w, bq[2 * j + 1][0], bq[2 * j + 1][1]);
+        }
+        tile[g][2 * t] = d[0];
+        tile[g][2 * t + 1] = d[1];
+        tile[g + 8][2 * t] = d[2];
+        tile[g + 8][2 * t + 1] = d[3];
+        __syncwarp();
+        if (lane < 16) {
+          float pv = init_h;
+#pragma unroll
+          for (int h = 0; h < G; ++h) {
+            const float x = (tile[lane][h] + tile[lane][G + h]) * inv;
+            pv = a.h_pool == 0 ? fmaxf(pv, x) : pv + x;
+          }
+          red[kv][16 * (gi + u) + lane] = pv;
+        }
+        __syncwarp();
+      }
+    }
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < SEL_TILE; j += SEL_THREADS) {
+    const int slot = base + j;
+    if (slot >= S) continue;
+    float p = init_h;
+    for (int kv = 0; kv < a.n_kv; ++kv) {
+      const float v = red[kv][j];
+      p = a.h_pool == 0 ? fmaxf(p, v) : p + v;
+    }
+    if (a.h_pool == 1) p /= (float)a.n_q;
+    const int c = slot / a.page_rows, n = slot - c * a.page_rows;
+    const int nc = a.n_chunks_of ? a.n_chunks_of[lib] : a.n_chunks;
+    const bool valid = c < nc && n < a.n_valid[lib * a.n_chunks + c];
+    a.scores[row * (int64_t)S + slot] = valid ? p : -CUDART_INF_F;
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ top-k
 __device__ __forceinline__ uint32_t order_key(float x) {  // larger float -> larger unsigned key
   const uint32_t u = x == 0.f ? 0u : __float_as_uint(x);  // -0 and +0 compare equal, as floats do

@@ -711,9 +711,20 @@ static int project_in_impl(const void* h, int h_dtype, int64_t n_rows, int d_m, 
     auto launch = [&](auto kern, const auto* hp) {
       launch_pdl(kern, dim3((unsigned)n_rows), dim3(thr), 0, st, hp, pa);
     };
+    // Routing CTAs per row: enough to fill the SMs once (a row's summary keys through up to 8 SMs), when the call
+    // has a [n_rows, C] output to pass the logits through. XENCB_ROUTE_CTAS=<n> in the environment fixes it.
+    int G = 1;
+    if (rf && (rf->logit_out || rf->w_dense)) {
+      G = (int)std::max<int64_t>(1, std::min<int64_t>(8, di.sms / n_rows));
+      if (const char* e = getenv("XENCB_ROUTE_CTAS")) G = std::max(1, std::min(8, atoi(e)));
+      G = std::min(G, rf->C);
+    }
     auto launch_rf = [&](auto kern, const auto* hp) {
       lrc = ensure_smem(kern, (int)std::max<size_t>(rf_smem, 48 * 1024));
-      if (!lrc) launch_pdl(kern, dim3((unsigned)n_rows), dim3(thr), rf_smem, st, hp, pa, *rf);
+      RouteFuse r2 = *rf;
+      r2.xlg = rf->logit_out ? rf->logit_out : rf->w_dense;
+      r2.done = row_done;
+      if (!lrc) launch_pdl(kern, dim3((unsigned)n_rows, (unsigned)G), dim3(thr), rf_smem, st, hp, pa, r2);
     };
     auto by_vpt = [&](const auto* hp) {
       using TH = std::remove_const_t<std::remove_pointer_t<decltype(hp)>>;
@@ -778,8 +789,8 @@ int xencb_project_in_route(const void* h, int h_dtype, int64_t n_rows, int d_m, 
                 (long long)n_rows, (long long)rows_per_lib, (long long)n_lib);
   if (top_k < 0) return fail(XENCB_EINVAL, "project_in_route: top_k=%d must be >= 0", top_k);
   if (!aligned(S, 16)) return fail(XENCB_EINVAL, "project_in_route: S must be 16-byte aligned");
-  const RouteFuse rf{S, n_chunks, n_chunks_of, rows_per_lib, route_temp, top_k, xencb_route_k(top_k, n_chunks), row_w,
-                     idx, wk, w_dense, logit_out};
+  const RouteFuse rf{S,  n_chunks, n_chunks_of, rows_per_lib, route_temp, top_k, xencb_route_k(top_k, n_chunks),
+                     row_w, idx, wk, w_dense, logit_out, nullptr, nullptr};
   return project_in_impl(h, h_dtype, n_rows, d_m, w_in, w_prep, b_in, d_s, flags, gate_w, gate_b, gate_b_dev, sel_w,
                          sel_b, n_cand, rms_eps, q_out, gate_out, rstd_out, z_out, workspace, workspace_bytes, stream,
                          &rf);
@@ -1469,6 +1480,27 @@ int xencb_select_scores(const float* q, int64_t n_rows, int T, int n_q, int n_kv
   dim3 grid((unsigned)((S + SEL_TILE - 1) / SEL_TILE), (unsigned)n_rows);
   if (n_rows > 65535) return fail(XENCB_ENOTSUP, "select_scores: at most 65535 rows per call");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // one position with f16 keys: the tensor-core scores (XENCB_SELECT_SIMT=1 in the environment keeps the FMA path)
+  const int G = n_q / n_kv;
+  const char* simt = getenv("XENCB_SELECT_SIMT");
+  if (T == 1 && keys_dtype == XENCB_F16 && (G == 1 || G == 2 || G == 4) &&
+      (hd == 32 || hd == 64 || hd == 128) && !(simt && simt[0] == '1')) {
+    auto by_p2 = [&](auto k1, auto k2, auto k4) {
+      switch (hd) {
+        case 32: k1<<<grid, SEL_THREADS, 0, st>>>(a); break;
+        case 64: k2<<<grid, SEL_THREADS, 0, st>>>(a); break;
+        default: k4<<<grid, SEL_THREADS, 0, st>>>(a); break;
+      }
+    };
+#define XENCB_SELM(GG) \
+  by_p2(select_scores_mma_kernel<GG, 1>, select_scores_mma_kernel<GG, 2>, select_scores_mma_kernel<GG, 4>)
+    if (G == 1) XENCB_SELM(1);
+    else if (G == 2) XENCB_SELM(2);
+    else XENCB_SELM(4);
+#undef XENCB_SELM
+    XENCB_CHECK_LAUNCH("select_scores_mma_kernel launch");
+    return XENCB_OK;
+  }
   auto run = [&](auto kf, auto kh) {
     if (keys_dtype == XENCB_F32) kf<<<grid, SEL_THREADS, 0, st>>>(a);
     else kh<<<grid, SEL_THREADS, 0, st>>>(a);

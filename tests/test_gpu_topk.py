@@ -33,7 +33,7 @@ def _status_clean(dev):
 
 # ------------------------------------------------------------------------------------------------ kernels
 @pytest.mark.parametrize("keys_dtype", [torch.float16, torch.float32])
-@pytest.mark.parametrize("geom", [(2, 2, 8), (8, 4, 128), (1, 16, 64), (4, 1, 32)])  # (n_kv, groups, hd)
+@pytest.mark.parametrize("geom", [(2, 2, 8), (8, 4, 128), (1, 16, 64), (4, 1, 32), (4, 2, 64)])  # (n_kv, groups, hd)
 @pytest.mark.parametrize("mode", [("last", "max"), ("last", "mean"), ("all_max", "mean"), ("all_mean", "max")])
 def test_select_scores_against_oracle(dev, keys_dtype, geom, mode):
     from kv_skill_v2_b200 import ops
@@ -54,6 +54,44 @@ def test_select_scores_against_oracle(dev, keys_dtype, geom, mode):
     assert np.array_equal(np.isfinite(got), np.isfinite(ref))
     fin = np.isfinite(ref)
     assert np.abs(got[fin] - ref[fin]).max() <= 1e-5 * max(1.0, np.abs(ref[fin]).max())
+    _status_clean(dev)
+
+
+@pytest.mark.parametrize("qmag", [1e-5, 1.0, 3e3])
+@pytest.mark.parametrize("pool", ["max", "mean"])
+def test_select_scores_tensor_core_path(dev, qmag, pool):
+    """One position with f16 keys takes the tensor-core kernel (q split into f16 hi + lo after a power-of-two scale
+    per KV head): several 128-slot tiles, a ragged last tile, invalid rows, a KV head whose q is all zero, and q
+    magnitudes far from 1; scores within 1e-5 of the oracle and the same top-k sets as the FMA path."""
+    from kv_skill_v2_b200 import ops
+    g = torch.Generator().manual_seed(int(qmag * 10) + 7)
+    n_kv, groups, hd, C, N, B = 8, 4, 128, 7, 96, 4
+    nv = torch.tensor([[96, 95, 1, 64, 33, 96, 17]], dtype=torch.int32)
+    keys = (torch.randn(1, C * N, n_kv, hd, generator=g) * 2).half()
+    q = torch.randn(B, 1, n_kv * groups, hd, generator=g) * qmag
+    q[1, 0, 4:8] = 0.0  # KV head 1 of row 1: all-zero queries
+    sc = ops.select_scores(q.to(dev), keys.to(dev), nv.to(dev), page_rows=N, rows_per_lib=B, head_pool=pool)
+    valid = (np.arange(N)[None, :] < nv.numpy()[0][:, None]).reshape(-1)
+    ref = X.topk_select_scores(q.permute(0, 2, 1, 3).numpy(), keys[0].float().numpy(), valid, query="last",
+                               pool=pool)
+    got = sc.cpu().numpy()
+    assert np.array_equal(np.isfinite(got), np.isfinite(ref))
+    fin = np.isfinite(ref)
+    assert np.abs(got[fin] - ref[fin]).max() <= 1e-5 * np.abs(ref[fin]).max()
+    import os
+    os.environ["XENCB_SELECT_SIMT"] = "1"
+    try:
+        sc2 = ops.select_scores(q.to(dev), keys.to(dev), nv.to(dev), page_rows=N, rows_per_lib=B, head_pool=pool)
+    finally:
+        del os.environ["XENCB_SELECT_SIMT"]
+    k = 64
+    i1, _ = ops.select_topk(sc, k)
+    i2, _ = ops.select_topk(sc2, k)
+    for r in range(B):
+        a, b = set(i1[r].tolist()), set(i2[r].tolist())
+        if a != b:  # only a near-tie at the k-th score may differ
+            s = np.sort(ref[r][fin[r]])[::-1]
+            assert s[k - 1] - s[k] <= 2e-5 * np.abs(s).max(), (r, a ^ b)
     _status_clean(dev)
 
 
