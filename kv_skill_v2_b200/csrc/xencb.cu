@@ -1200,7 +1200,7 @@ int xencb_read_prefill(const float* q, int64_t n_rows, int d_s, const void* slot
   const int64_t libs_used = (n_rows + rows_per_lib - 1) / rows_per_lib;
   const unsigned tiles = (unsigned)((rows_per_lib + PF_BM - 1) / PF_BM);
   prefill_scores_kernel<<<dim3(tiles, (unsigned)n_chunks, (unsigned)libs_used), PF_S_THREADS, PF_S_SMEM, st>>>(
-      mq, mk1, a, b_box_rows);
+      mq, mk1, mp, a, b_box_rows);
   XENCB_CHECK_LAUNCH("prefill_scores launch");
   prefill_read_kernel<<<dim3(tiles, (unsigned)((d_s + PF_R_BN - 1) / PF_R_BN), (unsigned)libs_used), PF_THREADS,
                         PF_R_SMEM, st>>>(mp, mk2, a);

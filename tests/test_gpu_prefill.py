@@ -50,6 +50,7 @@ CASES = [
     (1, 256, 5, 512, 256, 0, None),      # 512 score columns per chunk: two N=256 MMAs
     (2, 130, 3, 320, 64, 2, None),       # 320 columns (256 + 64), top-k weights
     (3, 64, 7, 128, 512, 3, [7, 4, 6]),  # chunk counts per Library
+    (2, 300, 4, 256, 128, 2, [4, 3]),    # 256 columns: CTA pairs with an odd tile count, chunk counts per Library
 ]
 
 
@@ -132,3 +133,4 @@ def test_route_logits_tiled_for_many_rows(dev):
             wo, _, _ = X.route(q[rows].numpy(), S[lib, :nc].numpy(), 10.0, top_k)
             assert topk_sets(w[rows, :nc]) == topk_sets(wo)
             assert rel_err(w[rows, :nc], wo) < 1e-5
+
