@@ -397,6 +397,131 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_read_kernel(const __gri
   if (warp == 1) tc_dealloc(taddr, 256);
 }
 
+// The read as CTA pairs (2-CTA cluster, cta_group::2): CTAs 2p and 2p + 1 take token tiles 2p and 2p + 1 and the
+// same 512 columns of d_s. Each loads its own 128 rows of P and, of each 256-column half, its 128 columns of the
+// slots (the even CTA the first 128); the even CTA issues M = 256, N = 256 MMAs over both CTAs' shared memory into
+// each CTA's 512 TMEM columns. Per SM and 64-slot k-block that is 48 KiB of operands for 128 x 512 x 64 MACs,
+// half of what the single-CTA kernel moves for the same work, so the 4-stage ring covers twice the latency.
+// Barriers as in a pair: both CTAs' copies count on the even CTA's full barrier, its commits arrive on both
+// CTAs' empty and done barriers; TMEM is allocated and freed by warp 1 of both CTAs. d_s % 512 == 0.
+constexpr int PF2R_BN = 512;                          // columns of d_s per pair
+constexpr int PF2R_A = PF_BM * 128;                   // P: 128 rows x 64 slots
+constexpr int PF2R_B = 4 * 64 * 128;                  // this CTA's 4 boxes of 64 columns x 64 slots
+constexpr int PF2R_STAGE = PF2R_A + PF2R_B;
+constexpr int PF2R_STAGES = 4;
+constexpr size_t PF2R_SMEM = 1024 + (size_t)PF2R_STAGES * PF2R_STAGE + 256;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
+    prefill_read_pair_kernel(const __grid_constant__ CUtensorMap map_p, const __grid_constant__ CUtensorMap map_k,
+                             const PrefillArgs a) {
+  extern __shared__ unsigned char pf_smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(pf_smem_raw) + 1023) & ~uintptr_t(1023));
+  const PfBars bars = pf_bars(smem + PF2R_STAGES * PF2R_STAGE, PF2R_STAGES);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int64_t lib = blockIdx.z;
+  const int n0 = blockIdx.y * PF2R_BN;
+  const int64_t t0 = (int64_t)blockIdx.x * PF_BM;
+  const int64_t row0 = lib * a.rows_per_lib + t0;
+  const int nc = a.n_chunks_of ? min(a.n_chunks_of[lib], a.n_chunks) : a.n_chunks;
+  const int kpc = a.ncol / PF_BK;  // k-blocks per chunk
+  const int nkb = nc * kpc;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&map_p);
+    prefetch_tensormap(&map_k);
+  }
+  if (warp == 1) {
+    tc_alloc_cg2(bars.tmem_slot, 512);
+    tc_relinquish_cg2();
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < PF2R_STAGES; ++i) {
+      mbar_init(&bars.full[i], 1);
+      mbar_init(&bars.empty[i], 1);
+    }
+    mbar_init(bars.done, 1);
+    *bars.abort_flag = 0;
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the even CTA's barriers are initialised before the odd CTA's copies count on them
+  tc_fence_after();
+  const uint32_t taddr = *bars.tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t stream = policy_evict_first();
+      const uint32_t tx = 2u * (uint32_t)PF2R_STAGE;  // both CTAs' bytes land on the even CTA's barrier
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % PF2R_STAGES, use = kb / PF2R_STAGES;
+        if (use > 0 && (!mbar_wait_bounded(&bars.empty[s], (use - 1) & 1) || *bars.abort_flag)) {
+          *bars.abort_flag = 1;
+          break;
+        }
+        const int c = kb / kpc, jb = kb - c * kpc;
+        const int64_t page = a.page_of[lib * a.n_chunks + c];
+        // P is 0 for a bad page (the scores kernel flagged it); its rows are read from past the pool (zeros)
+        const int y = (page >= 0 && page < a.n_pages ? (int)(page * a.page_rows) : (int)(a.n_pages * a.page_rows)) +
+                      jb * PF_BK;
+        unsigned char* st = smem + s * PF2R_STAGE;
+        const uint32_t fb = cluster_map(&bars.full[s], 0);
+        if (rank == 0) mbar_arrive_expect_tx(&bars.full[s], tx);
+        tma_load_2d_cg2(st, &map_p, c * a.ncol + jb * PF_BK, (int)row0, fb);
+        for (int h = 0; h < 2; ++h)
+          for (int i = 0; i < 2; ++i)
+            tma_load_2d_cg2_hint(st + PF2R_A + (2 * h + i) * 64 * 128, &map_k, n0 + 256 * h + (int)rank * 128 + 64 * i,
+                                 y, fb, stream);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = umma_idesc(UMMA_F16, UMMA_F16, 2 * PF_BM, 256, 1);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % PF2R_STAGES, use = kb / PF2R_STAGES;
+        if (!mbar_wait_bounded(&bars.full[s], use & 1) || *bars.abort_flag) { *bars.abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t st = smem_u32(smem + s * PF2R_STAGE);
+#pragma unroll
+        for (int ks = 0; ks < PF_BK / 16; ++ks) {  // 16 slots per k-step: A +32 B along its row, B +16 rows (2 KB)
+          const uint64_t ad = umma_desc_k_sw128(st + ks * 32);
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            tc_mma_cg2(taddr + 256u * h, ad, umma_desc_mn_sw128(st + PF2R_A + 2 * h * 64 * 128 + ks * 2048, 64 * 128),
+                       idesc, kb > 0 || ks > 0);
+        }
+        tc_commit_cg2_mc(&bars.empty[s], 3);
+      }
+      tc_commit_cg2_mc(bars.done, 3);
+    }
+  } else {
+    const int q4 = warp & 3;
+    const int rr = q4 * 32 + lane;
+    const int64_t t = row0 + rr;
+    const bool row_ok = t0 + rr < a.rows_per_lib && t < a.n_rows;
+    const bool ok = nkb > 0 && mbar_wait_bounded(bars.done, 0) && !*bars.abort_flag;
+    tc_fence_after();
+    const uint32_t tl = taddr + ((uint32_t)(q4 * 32) << 16);
+    float* dst = a.r_out + t * a.d_s + n0;
+    for (int c0 = 0; c0 < PF2R_BN; c0 += 32) {
+      float v[32];
+      tc_ld32(tl + (uint32_t)c0, v);
+      if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(dst + c0 + i) =
+              ok ? make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA frees TMEM or leaves while the pair's MMAs or the other epilogue may run
+  tc_fence_after();
+  if (warp == 1) tc_dealloc_cg2(taddr, 512);
+}
+
 // q (f32) -> f16 for the scores product.
 __global__ void __launch_bounds__(256) to_f16_kernel(const float* __restrict__ x, int64_t n, __half* __restrict__ y) {
   for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < n; i += (int64_t)gridDim.x * blockDim.x * 4) {

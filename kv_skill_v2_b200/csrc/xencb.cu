@@ -1202,8 +1202,18 @@ int xencb_read_prefill(const float* q, int64_t n_rows, int d_s, const void* slot
   prefill_scores_kernel<<<dim3(tiles, (unsigned)n_chunks, (unsigned)libs_used), PF_S_THREADS, PF_S_SMEM, st>>>(
       mq, mk1, mp, a, b_box_rows);
   XENCB_CHECK_LAUNCH("prefill_scores launch");
-  prefill_read_kernel<<<dim3(tiles, (unsigned)((d_s + PF_R_BN - 1) / PF_R_BN), (unsigned)libs_used), PF_THREADS,
-                        PF_R_SMEM, st>>>(mp, mk2, a);
+  // d_s in 512-column slices: the read as CTA pairs (half the operand bytes per SM); XENCB_PREFILL_PAIR=0 in the
+  // environment keeps the single-CTA kernel
+  const char* pair_env = getenv("XENCB_PREFILL_PAIR");
+  if (d_s % PF2R_BN == 0 && !(pair_env && pair_env[0] == '0')) {
+    rc = ensure_smem(prefill_read_pair_kernel, (int)PF2R_SMEM);
+    if (rc) return rc;
+    prefill_read_pair_kernel<<<dim3((tiles + 1) / 2 * 2, (unsigned)(d_s / PF2R_BN), (unsigned)libs_used),
+                               PF_THREADS, PF2R_SMEM, st>>>(mp, mk2, a);
+  } else {
+    prefill_read_kernel<<<dim3(tiles, (unsigned)((d_s + PF_R_BN - 1) / PF_R_BN), (unsigned)libs_used), PF_THREADS,
+                          PF_R_SMEM, st>>>(mp, mk2, a);
+  }
   XENCB_CHECK_LAUNCH("prefill_read launch");
   return XENCB_OK;
 }

@@ -134,3 +134,21 @@ def test_route_logits_tiled_for_many_rows(dev):
             assert topk_sets(w[rows, :nc]) == topk_sets(wo)
             assert rel_err(w[rows, :nc], wo) < 1e-5
 
+
+
+@pytest.mark.parametrize("T", [390, 256])
+def test_prefill_pair_read_matches_single(dev, T):
+    """The read as CTA pairs (cta_group::2, d_s in 512-column slices) gives the single-CTA kernel's r."""
+    import os
+    from kv_skill_v2_b200 import ops
+    pages, _, _ = _build(2, 5, 192, 1024, seed=T, dev=dev)
+    q = torch.nn.functional.normalize(torch.randn(2 * T, 1024, generator=torch.Generator().manual_seed(4)), dim=-1)
+    _, _, w, _ = ops.route(q.to(dev), pages.S, rows_per_lib=T, top_k=3, route_temp=10.0)
+    a = ops.read_prefill(q.to(dev), pages, w, rows_per_lib=T)
+    os.environ["XENCB_PREFILL_PAIR"] = "0"
+    try:
+        b = ops.read_prefill(q.to(dev), pages, w, rows_per_lib=T)
+    finally:
+        del os.environ["XENCB_PREFILL_PAIR"]
+    assert rel_err(a, b) < 1e-6
+    assert ops.device_status(dev) == 0
