@@ -342,6 +342,140 @@ __device__ __forceinline__ uint32_t order_key(float x) {  // larger float -> lar
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// The same selection for rows of up to TOPK_THREADS * TK_KPT slots with the row held in registers: thread t owns
+// slots [t * TK_KPT, (t + 1) * TK_KPT) (read once, 16-byte loads), so the four radix passes and the compaction
+// read no memory. Each warp counts into its own shared histogram (two 16-bit bins per word: at most
+// 32 * TK_KPT = 1024 per bin), so the first pass, where nearly every key falls in one or two bins, no longer
+// serialises the whole block on those bins' atomics; 256 threads then sum the 32 warp histograms per bin.
+constexpr int TK_KPT = 32;
+
+__global__ void __launch_bounds__(TOPK_THREADS) select_topk_reg_kernel(const float* __restrict__ scores, int S, int k,
+                                                                       int32_t* __restrict__ idx_out,
+                                                                       float* __restrict__ score_out) {
+  __shared__ uint32_t whist[TOPK_THREADS / 32][128];
+  __shared__ int hist[256];
+  __shared__ int sh_bin, sh_rem;
+  __shared__ int cnt_gt[TOPK_THREADS], cnt_eq[TOPK_THREADS];
+  __shared__ uint32_t skey[TOPK_MAX_K];
+  __shared__ int sidx[TOPK_MAX_K];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const float* sc = scores + (int64_t)blockIdx.x * S;
+  const int i0 = tid * TK_KPT;
+  uint32_t key[TK_KPT];
+  if (i0 + TK_KPT <= S && (S & 3) == 0) {
+#pragma unroll
+    for (int j = 0; j < TK_KPT; j += 4) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(sc + i0 + j));
+      key[j] = order_key(v.x); key[j + 1] = order_key(v.y); key[j + 2] = order_key(v.z); key[j + 3] = order_key(v.w);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < TK_KPT; ++j) key[j] = i0 + j < S ? order_key(__ldg(sc + i0 + j)) : 0u;  // 0: below any key
+  }
+
+  // ---- radix select: the k-th largest key, 8 bits at a time from the top
+  uint32_t prefix = 0, pmask = 0;
+  int rem = k;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = lane; i < 128; i += 32) whist[warp][i] = 0u;
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < TK_KPT; ++j) {
+      if ((key[j] & pmask) == prefix) {
+        const uint32_t b = (key[j] >> shift) & 255u;
+        atomicAdd(&whist[warp][b >> 1], 1u << ((b & 1u) << 4));
+      }
+    }
+    __syncthreads();
+    if (tid < 256) {
+      int t = 0;
+      for (int w = 0; w < TOPK_THREADS / 32; ++w) t += (int)((whist[w][tid >> 1] >> ((tid & 1) << 4)) & 0xffffu);
+      hist[tid] = t;
+    }
+    __syncthreads();
+    if (tid < 32) {
+      int part = 0;
+      for (int b = 0; b < 8; ++b) part += hist[255 - 8 * tid - b];
+      int incl = part;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (tid >= o) incl += v;
+      }
+      const int excl = incl - part;
+      if (excl < rem && incl >= rem) {
+        int run = excl;
+        for (int b = 0; b < 8; ++b) {
+          const int bin = 255 - 8 * tid - b;
+          if (run + hist[bin] >= rem) { sh_bin = bin; sh_rem = rem - run; break; }
+          run += hist[bin];
+        }
+      }
+    }
+    __syncthreads();
+    prefix |= (uint32_t)sh_bin << shift;
+    pmask |= 255u << shift;
+    rem = sh_rem;
+  }
+  const uint32_t thr = prefix;
+  const int take_eq = rem;
+
+  // ---- index-ordered compaction over the thread's own slots
+  int ngt = 0, neq = 0;
+#pragma unroll
+  for (int j = 0; j < TK_KPT; ++j) {
+    ngt += key[j] > thr;
+    neq += key[j] == thr;
+  }
+  cnt_gt[tid] = ngt;
+  cnt_eq[tid] = neq;
+  __syncthreads();
+  for (int o = 1; o < TOPK_THREADS; o <<= 1) {
+    const int a_gt = tid >= o ? cnt_gt[tid - o] : 0;
+    const int a_eq = tid >= o ? cnt_eq[tid - o] : 0;
+    __syncthreads();
+    cnt_gt[tid] += a_gt;
+    cnt_eq[tid] += a_eq;
+    __syncthreads();
+  }
+  const int n_gt_total = cnt_gt[TOPK_THREADS - 1];
+  int pos_gt = cnt_gt[tid] - ngt, pos_eq = cnt_eq[tid] - neq;
+#pragma unroll
+  for (int j = 0; j < TK_KPT; ++j) {
+    if (key[j] > thr) {
+      skey[pos_gt] = key[j]; sidx[pos_gt] = i0 + j; ++pos_gt;
+    } else if (key[j] == thr) {
+      if (pos_eq < take_eq) { skey[n_gt_total + pos_eq] = key[j]; sidx[n_gt_total + pos_eq] = i0 + j; }
+      ++pos_eq;
+    }
+  }
+  int kp = 1;
+  while (kp < k) kp <<= 1;
+  for (int i = k + tid; i < kp; i += TOPK_THREADS) { skey[i] = 0u; sidx[i] = 0x7fffffff; }
+  __syncthreads();
+  for (int size = 2; size <= kp; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = tid; i < kp; i += TOPK_THREADS) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool up = (i & size) == 0;
+          const uint32_t ki = skey[i], kj = skey[j];
+          const int xi = sidx[i], xj = sidx[j];
+          const bool i_first = ki > kj || (ki == kj && xi < xj);
+          if (up ? !i_first : i_first) {
+            skey[i] = kj; skey[j] = ki; sidx[i] = xj; sidx[j] = xi;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = tid; i < k; i += TOPK_THREADS) {
+    idx_out[(int64_t)blockIdx.x * k + i] = sidx[i];
+    if (score_out) score_out[(int64_t)blockIdx.x * k + i] = sc[sidx[i]];
+  }
+}
+
 __global__ void __launch_bounds__(TOPK_THREADS) select_topk_kernel(const float* __restrict__ scores, int S, int k,
                                                                    int32_t* __restrict__ idx_out,
                                                                    float* __restrict__ score_out) {

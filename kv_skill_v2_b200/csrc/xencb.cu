@@ -1535,7 +1535,11 @@ int xencb_select_topk(const float* scores, int64_t n_rows, int n_slots, int k, i
   if (k > TOPK_MAX_K) return fail(XENCB_ENOTSUP, "select_topk: k=%d above %d is not supported", k, TOPK_MAX_K);
   if (n_rows > INT32_MAX) return fail(XENCB_EINVAL, "select_topk: too many rows");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  select_topk_kernel<<<(unsigned)n_rows, TOPK_THREADS, 0, st>>>(scores, n_slots, k, idx_out, score_out);
+  const char* reg_env = getenv("XENCB_TOPK_REG");
+  if (n_slots <= TOPK_THREADS * TK_KPT && !(reg_env && reg_env[0] == '0'))
+    select_topk_reg_kernel<<<(unsigned)n_rows, TOPK_THREADS, 0, st>>>(scores, n_slots, k, idx_out, score_out);
+  else
+    select_topk_kernel<<<(unsigned)n_rows, TOPK_THREADS, 0, st>>>(scores, n_slots, k, idx_out, score_out);
   XENCB_CHECK_LAUNCH("select_topk_kernel launch");
   return XENCB_OK;
 }

@@ -118,7 +118,8 @@ def test_select_scores_several_libraries(dev):
     _status_clean(dev)
 
 
-@pytest.mark.parametrize("S,k", [(48, 7), (1000, 1), (4096, 64), (65536, 64), (65536, 2048), (300, 300)])
+@pytest.mark.parametrize("S,k", [(48, 7), (1000, 1), (4096, 64), (65536, 64), (65536, 2048), (300, 300),
+                                 (32768, 64), (32767, 2048), (1023, 5)])
 def test_select_topk_exact(dev, S, k):
     """Exact top-k in score order, ties to the lower slot, -inf slots last: against a lexicographic sort."""
     from kv_skill_v2_b200 import ops
