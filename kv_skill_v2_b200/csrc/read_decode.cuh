@@ -55,7 +55,26 @@ struct ReadArgs {
   // read_compact_kernel; null for the dense plan, whose CTAs walk every item
   const int32_t* item_list;
   const int* n_active;
+  // the same plan built inside the tensor-core read kernel (no list, no extra launch): for up to RM_PLAN_PAIRS
+  // pairs every CTA counts the live pieces of each pair and scans them in shared memory; 0 = off
+  int plan_pairs;
 };
+
+constexpr int RM_PLAN_PAIRS = 1024;
+
+// Pieces of pair `pr` that hold rows (routed chunk valid, weight != 0, page in the pool): the read_compact count.
+__device__ __forceinline__ int pair_pieces(const ReadArgs& a, int64_t pr) {
+  const int32_t c = a.idx[pr];
+  const float w = a.wk[pr];
+  if (c < 0 || c >= a.n_chunks || w == 0.f) return 0;
+  const int64_t lc = (pr / a.k / a.rows_per_lib) * a.n_chunks + c;
+  const int64_t page = a.page_of[lc];
+  if (page < 0 || page >= a.n_pages) return 0;  // decode_item flags it
+  int nv = a.n_valid[lc];
+  if (nv > a.page_rows) nv = a.page_rows;
+  if (nv < 0) nv = 0;
+  return min(a.n_split, (nv + a.split_rows - 1) / a.split_rows);
+}
 
 struct ItemRange {
   int64_t row;

@@ -44,6 +44,23 @@ struct __align__(16) GroupRec {
 };
 
 // Shared-memory bytes of the tensor-core read for a plan (the host and the kernel use the same layout).
+// Item of work unit w: the listed item (sparse plan from read_compact_kernel), the in-kernel plan (the pair p with
+// plan[p] <= w < plan[p + 1], plan = exclusive prefix sums of the pairs' live pieces, and its piece w - plan[p]),
+// or w itself (dense plan).
+__device__ __forceinline__ int64_t work_item(const ReadArgs& a, const int* plan, int64_t w) {
+  if (a.item_list) return a.item_list[w];
+  if (a.plan_pairs > 0) {
+    int lo = 0, hi = a.plan_pairs;  // plan[lo] <= w < plan[hi]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (plan[mid] <= w) lo = mid;
+      else hi = mid;
+    }
+    return (int64_t)lo * a.n_split + (w - plan[lo]);
+  }
+  return w;
+}
+
 __host__ __device__ inline size_t rm_smem_bytes(int n_stage, int stage_bytes, int ncw, int tpw) {
   return (size_t)n_stage * stage_bytes           // stages
          + (size_t)ncw * 2 * tpw * 4 * 2 * 4       // q fragments
@@ -76,19 +93,45 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 2) : 32 * 12, 
   uint64_t* sbar = empty + a.n_stage;  // [RM_SBUF] partial scores of a group are complete
   uint64_t* pbar = sbar + RM_SBUF;     // [RM_SBUF] the group's P fragments are published
   volatile int* abort_flag = reinterpret_cast<volatile int*>(pbar + RM_SBUF);
+  int* plan = const_cast<int*>(reinterpret_cast<volatile int*>(abort_flag) + 4);  // [plan_pairs + 1], in-kernel plan
 
+  // work units: every item in order, or (sparse plan) the items that hold rows: listed by read_compact_kernel, or
+  // counted and scanned here by the whole block
+  int64_t n_work = a.n_items;
+  if (a.plan_pairs > 0) {
+    const int np = a.plan_pairs;
+    for (int pr = threadIdx.x; pr < np; pr += blockDim.x) plan[pr + 1] = pair_pieces(a, pr);
+    __syncthreads();
+    if (warp == 0) {  // lane l scans pairs [l * per, (l + 1) * per), then a warp scan of the lanes' sums
+      const int per = (np + 31) / 32, b0 = min(np, lane * per), b1 = min(np, b0 + per);
+      int sum = 0;
+      for (int i = b0; i < b1; ++i) sum += plan[i + 1];
+      int incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      int run = incl - sum;
+      for (int i = b0; i < b1; ++i) {
+        run += plan[i + 1];
+        plan[i + 1] = run;
+      }
+      if (lane == 0) plan[0] = 0;
+    }
+    __syncthreads();
+    n_work = plan[np];
+  }
   // the producer's first 32 items (one per lane) are looked up before the prologue, so the lookups overlap it
   ItemRange mine;
   mine.active = false;
   mine.r0 = mine.r1 = 0;
   mine.base = nullptr;
   mine.row = 0;
-  // work units: every item in order, or (sparse plan) the listed items that hold rows
-  int64_t n_work = a.n_items;
   if (warp == 0) {
     if (a.item_list) n_work = *a.n_active;
     const int64_t my_w = blockIdx.x + (int64_t)lane * gridDim.x;
-    if (my_w < n_work) mine = decode_item(a, a.item_list ? (int64_t)a.item_list[my_w] : my_w);
+    if (my_w < n_work) mine = decode_item(a, work_item(a, plan, my_w));
   }
   {
     uint4* z = reinterpret_cast<uint4*>(stages);
@@ -124,7 +167,7 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 2) : 32 * 12, 
     int64_t batch = 0;
     int64_t k_item = 0;  // this CTA's k-th item is blockIdx.x + k * gridDim.x
     for (int64_t wu = blockIdx.x; wu < n_work && ok; wu += gridDim.x, ++k_item) {
-      const int64_t item = a.item_list ? (int64_t)a.item_list[wu] : wu;
+      const int64_t item = work_item(a, plan, wu);
       if ((k_item >> 5) != batch) {
         batch = k_item >> 5;
         const int64_t my_w = blockIdx.x + ((batch << 5) + lane) * (int64_t)gridDim.x;
@@ -132,7 +175,7 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 2) : 32 * 12, 
         mine.r0 = mine.r1 = 0;
         mine.base = nullptr;
         mine.row = 0;
-        if (my_w < n_work) mine = decode_item(a, a.item_list ? (int64_t)a.item_list[my_w] : my_w);
+        if (my_w < n_work) mine = decode_item(a, work_item(a, plan, my_w));
       }
       const int who = (int)(k_item & 31);  // the lane that decoded this item
       ItemRange it;

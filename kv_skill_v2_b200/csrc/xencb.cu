@@ -917,8 +917,20 @@ static int read_decode_impl(const float* q, int64_t n_rows, int d_s, const void*
   a.part_ml = reinterpret_cast<float*>(static_cast<char*>(workspace) + p.acc_bytes);
   a.item_list = nullptr;
   a.n_active = nullptr;
+  a.plan_pairs = 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (p.sparse) {
+  // the sparse plan inside the tensor-core kernel when the pairs' prefix sums fit next to its shared memory
+  // (XENCB_READ_PLAN_KERNEL=1 in the environment keeps the separate compaction kernel)
+  const char* plan_env = getenv("XENCB_READ_PLAN_KERNEL");
+  const size_t plan_bytes = align_up((size_t)(n_rows * k + 1) * sizeof(int), 16);
+  DevInfo di2;
+  const bool plan_inline = p.sparse && p.mma && n_rows * k <= RM_PLAN_PAIRS && !(plan_env && plan_env[0] == '1') &&
+                           device_info(&di2) == XENCB_OK &&
+                           p.smem + plan_bytes <= (size_t)(di2.max_smem_optin > 0 ? di2.max_smem_optin : 232448) - 1024;
+  if (plan_inline) {
+    a.plan_pairs = (int)(n_rows * k);
+    p.smem += plan_bytes;
+  } else if (p.sparse) {
     char* lb = static_cast<char*>(workspace) + p.acc_bytes + p.ml_bytes;
     int32_t* list = reinterpret_cast<int32_t*>(lb);
     int* n_act = reinterpret_cast<int*>(lb + p.list_bytes - 256);

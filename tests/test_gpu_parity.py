@@ -136,6 +136,16 @@ def test_read_decode_sparse_matches_dense(dev, slot_dtype, softmax, masked):
         ref = np.stack([X.read(q[b:b + 1].numpy(), Kf[b * C:(b + 1) * C], M[b * C:(b + 1) * C], wn[b:b + 1], 12.0,
                                softmax)[0] for b in range(B) if live[b]])
         assert rel_err(r_sparse[live.to(dev)], ref) < TOL
+    # 96 pairs: the tensor-core kernel builds the piece list itself; the separate compaction kernel lists the same
+    # pieces in the same order, so the two agree bit for bit
+    import os
+    os.environ["XENCB_READ_PLAN_KERNEL"] = "1"
+    try:
+        r_listed = ops.read_decode(q.to(dev), pages, idx, wk, rows_per_lib=1, read_temp=12.0, read_softmax=softmax,
+                                   sparse=True)
+    finally:
+        del os.environ["XENCB_READ_PLAN_KERNEL"]
+    assert torch.equal(r_listed, r_sparse)
     _status_clean(dev)
 
 
