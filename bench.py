@@ -266,12 +266,13 @@ CFG5 = dict(C=2048, N=512, d_s=2560, d_m=5120, T=8, read_temp=12.0, route_temp=1
 def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int, flush, stream,
                 n_chunks: int = 2048) -> dict:
     """one Library of 2048 chunks x 512 fp16 slots (1,048,576 slots, d_s 2560), 8 query tokens,
-    every chunk read (top_k 0); the chunks sharded evenly over the ranks, the partials exchanged by one NCCL
-    all-gather per step and merged. Strong scaling: the whole Library is the same at every N.
+    every chunk read (top_k 0); the chunks sharded evenly over the ranks, the partials exchanged once per step
+    (pushed over NVLink peer memory, one GPU per rank) and merged. Strong scaling: the whole Library is the same at
+    every N.
 
     A step: q = project_in(h) (replicated interface weights), the rank's partial (route_lse + read_multi over its
-    chunks), all-gather of the partial blocks, shard merge, output projection + residual, captured as one CUDA
-    graph with the NCCL all-gather inside. Timed with CUDA events per step, max over ranks."""
+    chunks), the exchange of the partial blocks, shard merge, output projection + residual, captured as one CUDA
+    graph with the exchange inside. Timed with CUDA events per step, max over ranks."""
     from kv_skill_v2_b200 import _native, ops
     from kv_skill_v2_b200.shard import ShardedRead, partition_chunks
 
@@ -293,8 +294,16 @@ def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
     hs = torch.randn(warmup + steps, T, d_m, generator=gw, device=dev)
     h = hs[0].clone()
     h_out = torch.empty_like(h)
-    sr = ShardedRead(pages, T, rows_per_lib=T)
+    # N > 1: the blocks over NVLink peer memory when every rank has its own GPU (XENCB_SHARD_EXCHANGE=collective in
+    # the environment: one NCCL all-gather instead)
+    sr = ShardedRead(pages, T, rows_per_lib=T, exchange=os.environ.get("XENCB_SHARD_EXCHANGE", "auto"))
     P_in, P_out = ops.weights_prep(W_in), ops.weights_prep(W_out)  # 3xF16 form, prepared once
+    if world > 1 and sr.exchange_kind == "peer":  # the peer exchange gives the all-gather's result, bit for bit
+        sr_c = ShardedRead(pages, T, rows_per_lib=T, exchange="collective")
+        q0, _, _, _ = ops.project_in(h, W_in, w_prep=P_in)
+        ra = sr(q0).clone()
+        assert torch.equal(ra, sr_c(q0)), "peer exchange differs from the all-gather"
+        del sr_c
 
     def pre():
         q, _, _, _ = ops.project_in(h, W_in, w_prep=P_in)
@@ -304,7 +313,7 @@ def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
         r = sr.merge()
         ops.project_out(r, W_out, h, want_delta=False, h_out=h_out, w_prep=P_out)
 
-    for _ in range(2):  # eager steps first: the NCCL communicator exists before the capture
+    for _ in range(2):  # eager steps first: the communicator (or the peer mappings) exist before the capture
         pre(); sr.exchange(); post()
     torch.cuda.synchronize(dev)
     # the whole step, the all-gather included, is one CUDA graph
@@ -381,7 +390,7 @@ def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
     P_sh = ops.weights_prep(W_sh)
     comp = {"project_in": timed(lambda: ops.project_in(h, W_in, w_prep=P_in)),
             "route_lse_read_multi": t_read * 1e6,
-            "all_gather": timed(sr.exchange) if world > 1 else 0.0,
+            "exchange": timed(sr.exchange) if world > 1 else 0.0,
             "merge_project_out": timed(post),
             f"project_in_{n_sh}_of_{d_s}_rows": timed(lambda: ops.project_in(h, W_sh, w_prep=P_sh))}
     read_bytes = Cl * N * d_s * 2 + Cl * d_s * 4 + 2 * T * d_s * 4
@@ -389,16 +398,20 @@ def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
     peak, peak_kind = hbm_peak()
     ms = t_max / steps
     del g_step, g_read
+    kind = sr.exchange_kind
+    sr.close()
     return {"workload": f"BASELINE config 5: one Library of {C} chunks x 512 fp16 slots ({C * N:,} slots), d_s 2560, "
                         "d_m 5120, 8 query tokens, dense read of every chunk; chunks sharded evenly over the GPUs, "
-                        "partials (max, sum, acc) merged after one NCCL all-gather per step"
+                        "partials (max, sum, acc) exchanged once per step and merged"
                         + ("" if C == CFG5["C"] else f" (REDUCED from {CFG5['C']} chunks for a profiler capture)"),
             "metric": "sharded Library-read tokens/s (whole job)", "value": T * steps / (t_max / 1000.0),
             "unit": "tokens/s", "n_gpus": world, "ms_per_step": ms, "scaling": "strong",
             "chunks_per_gpu": Cl, "kernels_per_step": kernels, "gpu_launches": kernels * steps,
-            "components_us": comp,
+            "components_us": comp, "exchange": kind,
             "step": "one CUDA graph per step: input projection (replicated), route_lse + read_multi over the rank's "
-                    "chunks, NCCL all-gather of the partial blocks, shard merge, output projection (replicated)",
+                    "chunks, the partial blocks pushed to every rank over NVLink peer memory (exchange 'peer'; "
+                    "'collective': one NCCL all-gather), shard merge after the blocks' flags, output projection "
+                    "(replicated)",
             "step_bytes_per_gpu": step_bytes, "step_hbm_gbs_per_gpu": step_bytes / (ms / 1000.0) / 1e9,
             "roofline": {"bound": "hbm", "kernel": "route_lse + read_multi_mma_kernel + read_multi_merge_kernel",
                          "achieved": read_bytes / t_read / 1e9, "peak": peak, "unit": "GB/s",

@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define XENCB_ABI_VERSION 4
+#define XENCB_ABI_VERSION 5
 
 #if defined(__GNUC__)
 #define XENCB_API __attribute__((visibility("default")))
@@ -258,6 +258,30 @@ XENCB_API int xencb_route_lse(const float* q, int64_t n_rows, int d_s, const flo
  * accumulators of xencb_read_multi (the layout an all-gather of each shard's block produces);
  * r = sum_g e^(max_g - M) A_g / sum_g e^(max_g - M) sum_g with M the largest max_g. */
 XENCB_API int xencb_shard_merge(const float* parts, int n_shards, int64_t n_rows, int d_s, float* r_out, void* stream);
+
+/* Exchange of the partial blocks over NVLink peer memory, in place of the all-gather before xencb_shard_merge
+ * (one process per GPU, every rank on its own GPU of one node). Each rank allocates an exchange buffer of
+ * xencb_exch_bytes(world, per) bytes (per = n_rows * (4 + d_s) floats, the block of xencb_shard_merge) with
+ * xencb_exch_alloc, which also returns its CUDA IPC handle (64 bytes); the ranks swap handles on the host and open
+ * each other's buffers with xencb_exch_open. A step is then
+ *   xencb_shard_push(block, ...)          this rank's block into slot `rank` of every rank's buffer (plain peer
+ *                                         stores), and that slot's flag raised to the step's epoch;
+ *   xencb_shard_merge_wait(own buffer, ...) waits for every rank's flag, then the merge of xencb_shard_merge.
+ * peers_dev: device array [world] of uint64 buffer addresses (this rank's own buffer at index `rank`, the opened
+ * peer mappings elsewhere). state: 3 uint32 of device memory, zero before the first push, kept across steps (the
+ * epochs; a CUDA graph of a step can be replayed). Blocks of consecutive steps alternate between two halves of
+ * the buffer, so a rank one step ahead never overwrites a block that is being merged. A flag that does not
+ * arrive within about 1.5 s sets XENCB_DEV_TIMEOUT. xencb_exch_close unmaps a peer buffer, xencb_exch_free frees
+ * the rank's own. world <= 64. */
+XENCB_API size_t xencb_exch_bytes(int world, int64_t per);
+XENCB_API int xencb_exch_alloc(size_t bytes, void** ptr, void* handle_out);
+XENCB_API int xencb_exch_open(const void* handle, void** peer_ptr);
+XENCB_API int xencb_exch_close(void* peer_ptr);
+XENCB_API int xencb_exch_free(void* ptr);
+XENCB_API int xencb_shard_push(const float* block, int64_t per, const void* peers_dev, int world, int rank,
+                               uint32_t* state, void* stream);
+XENCB_API int xencb_shard_merge_wait(const void* exch, int world, int64_t n_rows, int d_s, const uint32_t* state,
+                                     float* r_out, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------
  * Output projection and injection epilogue. Replaces xenc/injector.py:266-267 (gain_scale * gain * gate *

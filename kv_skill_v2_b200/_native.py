@@ -19,7 +19,7 @@ OK, EINVAL, ECUDA, ENOTSUP = 0, 1, 2, 3
 DEV_TIMEOUT, DEV_CLAMPED, DEV_BADPAGE = 1, 2, 4
 PIN_RMS, PIN_L2 = 1, 2
 NOALLOC_SCRATCH_BYTES = 16 << 20
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 _p, _i, _i64, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
 
@@ -57,6 +57,13 @@ SIGNATURES: dict = {
                                 _p, _p, _sz, _p]),
     "xencb_route_lse": (_i, [_p, _i64, _i, _p, _i, _p, _i64, _i64, _f, _p, _p, _p]),
     "xencb_shard_merge": (_i, [_p, _i, _i64, _i, _p, _p]),
+    "xencb_exch_bytes": (_sz, [_i, _i64]),
+    "xencb_exch_alloc": (_i, [_sz, ctypes.POINTER(ctypes.c_void_p), _p]),
+    "xencb_exch_open": (_i, [_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "xencb_exch_close": (_i, [_p]),
+    "xencb_exch_free": (_i, [_p]),
+    "xencb_shard_push": (_i, [_p, _i64, _p, _i, _i, _p, _p]),
+    "xencb_shard_merge_wait": (_i, [_p, _i, _i64, _i, _p, _p, _p]),
     "xencb_project_out_workspace": (_sz, [_i64, _i, _i]),
     "xencb_project_out": (_i, [_p, _i64, _i, _p, _p, _p, _i, _f, _p, _p, _p, _f, _p, _p, _p, _i, _p, _p, _p, _p,
                                _sz, _p]),

@@ -26,6 +26,7 @@
 #include "library_build.cuh"
 #include "topk_read.cuh"
 #include "attn.cuh"
+#include "exchange.cuh"
 
 // Scratch of xencb_read_decode_noalloc: a fixed device array, so that entry point never allocates.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[XENCB_NOALLOC_SCRATCH_BYTES];
@@ -1137,6 +1138,79 @@ int xencb_route_lse(const float* q, int64_t n_rows, int d_s, const float* S, int
   route_lse_kernel<<<(unsigned)((n_rows + 3) / 4), 128, 0, st>>>(w_out, n_rows, n_chunks, n_chunks_of, rows_per_lib,
                                                                  header_out);
   XENCB_CHECK_LAUNCH("route_lse launch");
+  return XENCB_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ peer exchange
+size_t xencb_exch_bytes(int world, int64_t per) {
+  if (world <= 0 || world > EX_MAX_RANKS || per <= 0) return 0;
+  return align_up((size_t)EX_FLAG_BYTES + 2 * (size_t)world * (size_t)per * sizeof(float), 256);
+}
+
+int xencb_exch_alloc(size_t bytes, void** ptr, void* handle_out) {
+  if (!ptr || !handle_out || bytes == 0) return fail(XENCB_EINVAL, "exch_alloc: ptr, handle_out and bytes are required");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return fail(XENCB_ECUDA, "exch_alloc: cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+  e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(XENCB_ECUDA, "exch_alloc: %s", cudaGetErrorString(e));
+  }
+  std::memcpy(handle_out, &h, sizeof(h));
+  *ptr = p;
+  return XENCB_OK;
+}
+
+int xencb_exch_open(const void* handle, void** peer_ptr) {
+  if (!handle || !peer_ptr) return fail(XENCB_EINVAL, "exch_open: handle and peer_ptr are required");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(XENCB_ECUDA, "exch_open: cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+  *peer_ptr = p;
+  return XENCB_OK;
+}
+
+int xencb_exch_close(void* peer_ptr) {
+  if (!peer_ptr) return XENCB_OK;
+  const cudaError_t e = cudaIpcCloseMemHandle(peer_ptr);
+  if (e != cudaSuccess) return fail(XENCB_ECUDA, "exch_close: %s", cudaGetErrorString(e));
+  return XENCB_OK;
+}
+
+int xencb_exch_free(void* ptr) {
+  if (!ptr) return XENCB_OK;
+  const cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return fail(XENCB_ECUDA, "exch_free: %s", cudaGetErrorString(e));
+  return XENCB_OK;
+}
+
+int xencb_shard_push(const float* block, int64_t per, const void* peers_dev, int world, int rank, uint32_t* state,
+                     void* stream) {
+  if (!block || !peers_dev || !state) return fail(XENCB_EINVAL, "shard_push: block, peers_dev and state are required");
+  if (world <= 0 || world > EX_MAX_RANKS || rank < 0 || rank >= world || per <= 0)
+    return fail(XENCB_EINVAL, "shard_push: world=%d rank=%d per=%lld (1 <= world <= %d)", world, rank, (long long)per,
+                EX_MAX_RANKS);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  shard_push_kernel<<<dim3((unsigned)world, EX_SLICES), EX_PUSH_THREADS, 0, st>>>(
+      block, per, static_cast<const uint64_t*>(peers_dev), world, rank, state);
+  XENCB_CHECK_LAUNCH("shard_push launch");
+  return XENCB_OK;
+}
+
+int xencb_shard_merge_wait(const void* exch, int world, int64_t n_rows, int d_s, const uint32_t* state, float* r_out,
+                           void* stream) {
+  if (!exch || !state || !r_out) return fail(XENCB_EINVAL, "shard_merge_wait: exch, state and r_out are required");
+  if (world <= 0 || world > EX_MAX_RANKS || n_rows <= 0 || d_s <= 0)
+    return fail(XENCB_EINVAL, "shard_merge_wait: sizes must be positive (world <= %d)", EX_MAX_RANKS);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  dim3 grid((unsigned)n_rows, (unsigned)((d_s + 1023) / 1024));
+  shard_merge_wait_kernel<<<grid, 256, 0, st>>>(static_cast<const char*>(exch), world, n_rows, d_s, state, r_out);
+  XENCB_CHECK_LAUNCH("shard_merge_wait launch");
   return XENCB_OK;
 }
 

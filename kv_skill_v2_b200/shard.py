@@ -7,9 +7,11 @@ which regroups by chunk shard g (chunks [lo_g, hi_g)) as
     M_g = max_{c in g} l_c,  Z_g = sum_{c in g} e^(l_c - M_g),  A_g = sum_{c in g} e^(l_c - M_g) r_c
     r   = sum_g e^(M_g - M) A_g / sum_g e^(M_g - M) Z_g,         M = max_g M_g.
 So each rank keeps its chunk shard of K and S in its own HBM, computes its partial (M_g, Z_g, A_g) with
-ops.route_lse + ops.read_multi into one flat block, one all-gather over the process group (NCCL over NVLink
-on GPUs) lays the blocks end to end in rank order, and ops.shard_merge combines them. Every rank takes the same
-collective steps in the same order.
+ops.route_lse + ops.read_multi into one flat block, the blocks are exchanged, and ops.shard_merge combines them.
+On GPUs with one process per GPU of one node the exchange goes over NVLink peer memory (PeerExchange: each rank's
+block pushed straight into every rank's exchange buffer, the merge waiting on per-block flags); otherwise one
+all-gather over the process group lays the blocks end to end in rank order. Every rank takes the same exchange
+steps in the same order.
 
 The compute is pluggable (`compute=`) so that the orchestration -- the partition, the block layout, the
 collective -- is testable on CPU ranks (gloo) with the oracle standing in for the kernels; the product path
@@ -18,11 +20,14 @@ uses CudaShardCompute, and there is no CPU path.
 
 from __future__ import annotations
 
+import ctypes
+import socket
 from typing import Optional
 
 import torch
 import torch.distributed as dist
 
+from . import _native as N
 from . import ops
 
 
@@ -70,13 +75,93 @@ class CudaShardCompute:
         ops.shard_merge(gathered, world, n_rows, d_s, out=out)
 
 
+class PeerExchange:
+    """The partial blocks of a chunk-sharded read over NVLink peer memory (xencb_shard_push /
+    xencb_shard_merge_wait): every rank allocates an exchange buffer (xencb_exch_alloc), the CUDA IPC handles are
+    swapped once over the process group and each rank maps the others' buffers (xencb_exch_open). A step pushes
+    this rank's block into slot `rank` of every buffer with plain peer stores and raises that slot's flag; the merge
+    waits for the flags (bounded) and combines the blocks. The epochs live in a small device state, so a step
+    captured in a CUDA graph replays. close() (collective) unmaps and frees."""
+
+    def __init__(self, per: int, world: int, rank: int, device: torch.device, group=None):
+        L = N.lib()
+        self.per, self.world, self.rank, self.group = int(per), int(world), int(rank), group
+        self.device = torch.device(device)
+        nbytes = L.xencb_exch_bytes(self.world, self.per)
+        if nbytes == 0:
+            raise ValueError(f"PeerExchange: world={world} per={per} is not supported")
+        ptr = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        with torch.cuda.device(self.device):
+            N.check(L.xencb_exch_alloc(nbytes, ctypes.byref(ptr), ctypes.cast(handle, ctypes.c_void_p)),
+                    "xencb_exch_alloc")
+        self.ptr = ptr.value
+        self.opened = []
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        peers = []
+        try:
+            for g, h in enumerate(handles):
+                if g == self.rank:
+                    peers.append(self.ptr)
+                    continue
+                pp = ctypes.c_void_p()
+                hb = ctypes.create_string_buffer(bytes(h), 64)
+                with torch.cuda.device(self.device):
+                    N.check(L.xencb_exch_open(ctypes.cast(hb, ctypes.c_void_p), ctypes.byref(pp)), "xencb_exch_open")
+                peers.append(pp.value)
+                self.opened.append(pp.value)
+        except Exception:
+            self._release()
+            raise
+        self.peers_dev = torch.tensor(peers, dtype=torch.int64, device=self.device)
+        self.state = torch.zeros(4, dtype=torch.int32, device=self.device)
+        dist.barrier(group=group)  # every buffer is mapped everywhere before the first push
+
+    def push(self, block: torch.Tensor) -> None:
+        N.call("xencb_shard_push", ops._ptr(block), self.per, ops._ptr(self.peers_dev), self.world, self.rank,
+               ops._ptr(self.state), ops._stream(self.device))
+
+    def merge(self, n_rows: int, d_s: int, out: torch.Tensor) -> torch.Tensor:
+        N.call("xencb_shard_merge_wait", ctypes.c_void_p(self.ptr), self.world, int(n_rows), int(d_s),
+               ops._ptr(self.state), ops._ptr(out), ops._stream(self.device))
+        return out
+
+    def _release(self) -> None:
+        L = N.lib()
+        with torch.cuda.device(self.device):
+            for pp in self.opened:
+                L.xencb_exch_close(ctypes.c_void_p(pp))
+            self.opened = []
+            if self.ptr:
+                L.xencb_exch_free(ctypes.c_void_p(self.ptr))
+                self.ptr = None
+
+    def close(self) -> None:
+        """Collective: no rank unmaps or frees while another may still push into its buffer."""
+        if self.ptr is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self._release()
+
+
+def _one_gpu_per_rank(device: torch.device, group=None) -> bool:
+    """Every rank of `group` on its own GPU of this node (the peer exchange's precondition)."""
+    me = (socket.gethostname(), str(torch.cuda.get_device_properties(device).uuid))
+    world = dist.get_world_size(group)
+    seen = [None] * world
+    dist.all_gather_object(seen, me, group=group)
+    return len({h for h, _ in seen}) == 1 and len({u for _, u in seen}) == world
+
+
 class ShardedRead:
     """r [n_rows, d_s] of the whole Library from this rank's chunk shard `pages` (one Library, or several with
     rows_per_lib rows each). Buffers are allocated once, so a step is CUDA-graph capturable (the all-gather
     included, on NCCL)."""
 
     def __init__(self, pages: ops.Pages, n_rows: int, *, rows_per_lib: Optional[int] = None, group=None,
-                 compute=None, device=None):
+                 compute=None, device=None, exchange: str = "auto"):
         self.pages = pages
         self.n_rows = int(n_rows)
         self.rows_per_lib = int(rows_per_lib or n_rows)
@@ -91,6 +176,18 @@ class ShardedRead:
         self.gathered = torch.zeros(self.world * per, dtype=torch.float32, device=device)
         self.r = torch.empty(self.n_rows, self.d_s, dtype=torch.float32, device=device)
         self.header, self.acc = ops.shard_views(self.block, self.n_rows, self.d_s)
+        # exchange: "peer" (NVLink peer memory), "collective" (all-gather), or "auto" (peer when every rank has
+        # its own GPU of one node and the kernels are the CUDA ones)
+        if exchange not in ("auto", "peer", "collective"):
+            raise ValueError(f"ShardedRead: exchange={exchange!r} is not one of auto, peer, collective")
+        self.peer = None
+        want_peer = (self.world > 1 and exchange != "collective" and device.type == "cuda"
+                     and isinstance(self.compute, CudaShardCompute))
+        if want_peer and _one_gpu_per_rank(device, group):
+            self.peer = PeerExchange(per, self.world, self.rank, device, group)
+        elif exchange == "peer" and self.world > 1:
+            raise ValueError("ShardedRead: exchange='peer' needs CUDA kernels and one GPU per rank on one node")
+        self.exchange_kind = "peer" if self.peer is not None else ("collective" if self.world > 1 else "none")
 
     def partial(self, q: torch.Tensor) -> torch.Tensor:
         """This rank's block (headers, accumulators) for query rows q [n_rows, d_s]."""
@@ -100,14 +197,24 @@ class ShardedRead:
         return self.block
 
     def exchange(self) -> None:
-        """The one collective: every rank's block, in rank order, into `gathered`."""
-        if self.world > 1:
+        """Every rank's block to every rank: pushed over peer memory, or one all-gather into `gathered`."""
+        if self.peer is not None:
+            self.peer.push(self.block)
+        elif self.world > 1:
             dist.all_gather_into_tensor(self.gathered, self.block, group=self.group)
 
     def merge(self) -> torch.Tensor:
+        if self.peer is not None:
+            return self.peer.merge(self.n_rows, self.d_s, self.r)
         src = self.gathered if self.world > 1 else self.block
         self.compute.merge(src, self.world, self.n_rows, self.d_s, self.r)
         return self.r
+
+    def close(self) -> None:
+        """Collective when the exchange is on peer memory: unmaps and frees the exchange buffers."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def __call__(self, q: torch.Tensor) -> torch.Tensor:
         self.partial(q)
