@@ -342,45 +342,51 @@ __device__ __forceinline__ uint32_t order_key(float x) {  // larger float -> lar
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// The same selection for rows of up to TOPK_THREADS * TK_KPT slots with the row held in registers: thread t owns
-// slots [t * TK_KPT, (t + 1) * TK_KPT) (read once, 16-byte loads), so the four radix passes and the compaction
-// read no memory. Each warp counts into its own shared histogram (two 16-bit bins per word: at most
-// 32 * TK_KPT = 1024 per bin), so the first pass, where nearly every key falls in one or two bins, no longer
-// serialises the whole block on those bins' atomics; 256 threads then sum the 32 warp histograms per bin.
-constexpr int TK_KPT = 32;
+// The same selection for rows of up to TKC_CL * TKC_THREADS * TKC_KPT slots, spread over a cluster of TKC_CL
+// CTAs: CTA c owns the contiguous slots [c * slice, (c + 1) * slice), held in registers (thread t: TKC_KPT
+// consecutive slots). Each radix pass builds the CTA's histogram (per-warp packed histograms as above), and after
+// one cluster barrier every CTA sums the TKC_CL histograms through distributed shared memory and takes the same
+// bin (histograms alternate between two buffers by pass, so a CTA never overwrites one another CTA may still
+// read). The compaction scans the CTAs' (greater, equal) counts in cluster order, which is slot order, so ties at
+// the threshold still go to the lower slots; each CTA writes its winners into CTA 0's arrays, which sorts them.
+// Per-warp histograms (two 16-bit bins per word, at most 32 * TKC_KPT per bin) keep the first pass, where nearly
+// every key falls in one or two bins, from serialising the CTA on those bins' atomics.
+constexpr int TKC_CL = 8;
+constexpr int TKC_THREADS = 512;
+constexpr int TKC_KPT = 8;
 
-__global__ void __launch_bounds__(TOPK_THREADS) select_topk_reg_kernel(const float* __restrict__ scores, int S, int k,
-                                                                       int32_t* __restrict__ idx_out,
-                                                                       float* __restrict__ score_out) {
-  __shared__ uint32_t whist[TOPK_THREADS / 32][128];
-  __shared__ int hist[256];
+__global__ void __cluster_dims__(TKC_CL, 1, 1) __launch_bounds__(TKC_THREADS)
+    select_topk_cluster_kernel(const float* __restrict__ scores, int S, int k, int32_t* __restrict__ idx_out,
+                               float* __restrict__ score_out) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  __shared__ uint32_t whist[TKC_THREADS / 32][128];
+  __shared__ int hist[2][256];
+  __shared__ int tot[256];
   __shared__ int sh_bin, sh_rem;
-  __shared__ int cnt_gt[TOPK_THREADS], cnt_eq[TOPK_THREADS];
+  __shared__ int cnt_gt[TKC_THREADS], cnt_eq[TKC_THREADS];
+  __shared__ int cta_cnt[2];
   __shared__ uint32_t skey[TOPK_MAX_K];
   __shared__ int sidx[TOPK_MAX_K];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const float* sc = scores + (int64_t)blockIdx.x * S;
-  const int i0 = tid * TK_KPT;
-  uint32_t key[TK_KPT];
-  if (i0 + TK_KPT <= S && (S & 3) == 0) {
+  const int crank = (int)cluster.block_rank();
+  const int64_t row = blockIdx.x / TKC_CL;
+  const float* sc = scores + row * S;
+  const int slice = (S + TKC_CL - 1) / TKC_CL;
+  const int i0 = crank * slice + tid * TKC_KPT;
+  const int iend = min(S, (crank + 1) * slice);
+  uint32_t key[TKC_KPT];
 #pragma unroll
-    for (int j = 0; j < TK_KPT; j += 4) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(sc + i0 + j));
-      key[j] = order_key(v.x); key[j + 1] = order_key(v.y); key[j + 2] = order_key(v.z); key[j + 3] = order_key(v.w);
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < TK_KPT; ++j) key[j] = i0 + j < S ? order_key(__ldg(sc + i0 + j)) : 0u;  // 0: below any key
-  }
+  for (int j = 0; j < TKC_KPT; ++j) key[j] = i0 + j < iend ? order_key(__ldg(sc + i0 + j)) : 0u;
 
-  // ---- radix select: the k-th largest key, 8 bits at a time from the top
   uint32_t prefix = 0, pmask = 0;
   int rem = k;
-  for (int shift = 24; shift >= 0; shift -= 8) {
+  int buf = 0;
+  for (int shift = 24; shift >= 0; shift -= 8, buf ^= 1) {
     for (int i = lane; i < 128; i += 32) whist[warp][i] = 0u;
     __syncwarp();
 #pragma unroll
-    for (int j = 0; j < TK_KPT; ++j) {
+    for (int j = 0; j < TKC_KPT; ++j) {
       if ((key[j] & pmask) == prefix) {
         const uint32_t b = (key[j] >> shift) & 255u;
         atomicAdd(&whist[warp][b >> 1], 1u << ((b & 1u) << 4));
@@ -389,13 +395,19 @@ __global__ void __launch_bounds__(TOPK_THREADS) select_topk_reg_kernel(const flo
     __syncthreads();
     if (tid < 256) {
       int t = 0;
-      for (int w = 0; w < TOPK_THREADS / 32; ++w) t += (int)((whist[w][tid >> 1] >> ((tid & 1) << 4)) & 0xffffu);
-      hist[tid] = t;
+      for (int w = 0; w < TKC_THREADS / 32; ++w) t += (int)((whist[w][tid >> 1] >> ((tid & 1) << 4)) & 0xffffu);
+      hist[buf][tid] = t;
+    }
+    cluster.sync();  // every CTA's histogram of this pass is complete
+    if (tid < 256) {
+      int t = 0;
+      for (int r = 0; r < TKC_CL; ++r) t += cluster.map_shared_rank(&hist[buf][0], r)[tid];
+      tot[tid] = t;
     }
     __syncthreads();
     if (tid < 32) {
       int part = 0;
-      for (int b = 0; b < 8; ++b) part += hist[255 - 8 * tid - b];
+      for (int b = 0; b < 8; ++b) part += tot[255 - 8 * tid - b];
       int incl = part;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -407,8 +419,8 @@ __global__ void __launch_bounds__(TOPK_THREADS) select_topk_reg_kernel(const flo
         int run = excl;
         for (int b = 0; b < 8; ++b) {
           const int bin = 255 - 8 * tid - b;
-          if (run + hist[bin] >= rem) { sh_bin = bin; sh_rem = rem - run; break; }
-          run += hist[bin];
+          if (run + tot[bin] >= rem) { sh_bin = bin; sh_rem = rem - run; break; }
+          run += tot[bin];
         }
       }
     }
@@ -420,17 +432,17 @@ __global__ void __launch_bounds__(TOPK_THREADS) select_topk_reg_kernel(const flo
   const uint32_t thr = prefix;
   const int take_eq = rem;
 
-  // ---- index-ordered compaction over the thread's own slots
+  // ---- compaction: thread order within the CTA, CTA order within the cluster (both slot order)
   int ngt = 0, neq = 0;
 #pragma unroll
-  for (int j = 0; j < TK_KPT; ++j) {
+  for (int j = 0; j < TKC_KPT; ++j) {
     ngt += key[j] > thr;
     neq += key[j] == thr;
   }
   cnt_gt[tid] = ngt;
   cnt_eq[tid] = neq;
   __syncthreads();
-  for (int o = 1; o < TOPK_THREADS; o <<= 1) {
+  for (int o = 1; o < TKC_THREADS; o <<= 1) {
     const int a_gt = tid >= o ? cnt_gt[tid - o] : 0;
     const int a_eq = tid >= o ? cnt_eq[tid - o] : 0;
     __syncthreads();
@@ -438,24 +450,39 @@ __global__ void __launch_bounds__(TOPK_THREADS) select_topk_reg_kernel(const flo
     cnt_eq[tid] += a_eq;
     __syncthreads();
   }
-  const int n_gt_total = cnt_gt[TOPK_THREADS - 1];
-  int pos_gt = cnt_gt[tid] - ngt, pos_eq = cnt_eq[tid] - neq;
+  if (tid == 0) {
+    cta_cnt[0] = cnt_gt[TKC_THREADS - 1];
+    cta_cnt[1] = cnt_eq[TKC_THREADS - 1];
+  }
+  cluster.sync();  // every CTA's totals are published
+  int off_gt = 0, off_eq = 0, n_gt_total = 0;
+  for (int r = 0; r < TKC_CL; ++r) {
+    const int* cc = cluster.map_shared_rank(cta_cnt, r);
+    const int g = cc[0], e = cc[1];
+    if (r < crank) { off_gt += g; off_eq += e; }
+    n_gt_total += g;
+  }
+  uint32_t* lkey = cluster.map_shared_rank(skey, 0);
+  int* lidx = cluster.map_shared_rank(sidx, 0);
+  int pos_gt = off_gt + cnt_gt[tid] - ngt, pos_eq = off_eq + cnt_eq[tid] - neq;
 #pragma unroll
-  for (int j = 0; j < TK_KPT; ++j) {
+  for (int j = 0; j < TKC_KPT; ++j) {
     if (key[j] > thr) {
-      skey[pos_gt] = key[j]; sidx[pos_gt] = i0 + j; ++pos_gt;
+      lkey[pos_gt] = key[j]; lidx[pos_gt] = i0 + j; ++pos_gt;
     } else if (key[j] == thr) {
-      if (pos_eq < take_eq) { skey[n_gt_total + pos_eq] = key[j]; sidx[n_gt_total + pos_eq] = i0 + j; }
+      if (pos_eq < take_eq) { lkey[n_gt_total + pos_eq] = key[j]; lidx[n_gt_total + pos_eq] = i0 + j; }
       ++pos_eq;
     }
   }
+  cluster.sync();  // CTA 0 holds the k winners; the other CTAs are done
+  if (crank != 0) return;
   int kp = 1;
   while (kp < k) kp <<= 1;
-  for (int i = k + tid; i < kp; i += TOPK_THREADS) { skey[i] = 0u; sidx[i] = 0x7fffffff; }
+  for (int i = k + tid; i < kp; i += TKC_THREADS) { skey[i] = 0u; sidx[i] = 0x7fffffff; }
   __syncthreads();
   for (int size = 2; size <= kp; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = tid; i < kp; i += TOPK_THREADS) {
+      for (int i = tid; i < kp; i += TKC_THREADS) {
         const int j = i ^ stride;
         if (j > i) {
           const bool up = (i & size) == 0;
@@ -470,9 +497,9 @@ __global__ void __launch_bounds__(TOPK_THREADS) select_topk_reg_kernel(const flo
       __syncthreads();
     }
   }
-  for (int i = tid; i < k; i += TOPK_THREADS) {
-    idx_out[(int64_t)blockIdx.x * k + i] = sidx[i];
-    if (score_out) score_out[(int64_t)blockIdx.x * k + i] = sc[sidx[i]];
+  for (int i = tid; i < k; i += TKC_THREADS) {
+    idx_out[row * k + i] = sidx[i];
+    if (score_out) score_out[row * k + i] = sc[sidx[i]];
   }
 }
 

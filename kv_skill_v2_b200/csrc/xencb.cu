@@ -1621,9 +1621,11 @@ int xencb_select_topk(const float* scores, int64_t n_rows, int n_slots, int k, i
   if (k > TOPK_MAX_K) return fail(XENCB_ENOTSUP, "select_topk: k=%d above %d is not supported", k, TOPK_MAX_K);
   if (n_rows > INT32_MAX) return fail(XENCB_EINVAL, "select_topk: too many rows");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const char* reg_env = getenv("XENCB_TOPK_REG");
-  if (n_slots <= TOPK_THREADS * TK_KPT && !(reg_env && reg_env[0] == '0'))
-    select_topk_reg_kernel<<<(unsigned)n_rows, TOPK_THREADS, 0, st>>>(scores, n_slots, k, idx_out, score_out);
+  // rows up to 32,768 slots: a cluster of 8 CTAs per row; XENCB_TOPK_CLUSTER=0 in the environment keeps one CTA
+  const char* cl_env = getenv("XENCB_TOPK_CLUSTER");
+  if (n_slots <= TKC_CL * TKC_THREADS * TKC_KPT && n_rows * TKC_CL <= INT32_MAX && !(cl_env && cl_env[0] == '0'))
+    select_topk_cluster_kernel<<<(unsigned)(n_rows * TKC_CL), TKC_THREADS, 0, st>>>(scores, n_slots, k, idx_out,
+                                                                                    score_out);
   else
     select_topk_kernel<<<(unsigned)n_rows, TOPK_THREADS, 0, st>>>(scores, n_slots, k, idx_out, score_out);
   XENCB_CHECK_LAUNCH("select_topk_kernel launch");
