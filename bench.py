@@ -725,14 +725,14 @@ def run_topk(torch, dist, dev, world: int, rank: int, steps: int, warmup: int, f
                        f"d_s {d}, k {k}; selection keys {n_kv} KV heads x {hd} (fp16), {n_q} query heads",
            "select": {"metric": "documents selected per second (whole job)", "value": SB * world / (ms_sel / 1e3),
                       "unit": "documents/s", "ms_per_step": ms_sel, "docs_per_step": SB, "kernels_per_step": kern_sel,
-                      "roofline": {"bound": "hbm", "kernel": "select_scores_kernel + select_topk_kernel",
+                      "roofline": {"bound": "hbm", "kernel": "select_scores_mma_kernel + select_topk_cluster_kernel",
                                    "achieved": sel_bytes / (ms_sel / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
                                    "frac": sel_bytes / (ms_sel / 1e3) / 1e9 / peak,
                                    "algorithmic_bytes_per_step": sel_bytes, "peak_source": peak_kind},
                       "l2": "1 GiB of keys per step (larger than L2)"},
            "read": {"metric": "D8 decode-read tokens/s (whole job)", "value": B * world / (ms_read / 1e3),
                     "unit": "tokens/s", "ms_per_step": ms_read, "kernels_per_step": kern_read,
-                    "roofline": {"bound": "hbm", "kernel": "topk_read_kernel",
+                    "roofline": {"bound": "hbm", "kernel": "topk_read_decode_kernel",
                                  "achieved": read_bytes / (ms_read / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
                                  "frac": read_bytes / (ms_read / 1e3) / 1e9 / peak,
                                  "algorithmic_bytes_per_step": read_bytes, "peak_source": peak_kind},
@@ -868,7 +868,7 @@ def run_prefill(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
             "unit": "tokens/s", "n_gpus": world, "ms_per_step": ms, "scaling": "weak",
             "kernels_per_step": kernels, "gpu_launches": kernels * steps,
             "step_tflops": step_flop / (ms / 1000.0) / 1e12, "algorithmic_flop_per_step": step_flop,
-            "roofline": {"bound": "tensor", "kernel": "prefill_scores_kernel + prefill_read_kernel (+ q to f16)",
+            "roofline": {"bound": "tensor", "kernel": "prefill_scores_kernel + prefill_read_pair_kernel (+ q to f16)",
                          "achieved": read_flop / t_read / 1e12, "peak": peak, "unit": "TFLOP/s",
                          "frac": read_flop / t_read / 1e12 / peak, "algorithmic_flop_per_launch": read_flop,
                          "launch_ms": t_read * 1e3, "peak_source": peak_src},
