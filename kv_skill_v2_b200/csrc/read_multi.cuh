@@ -9,8 +9,9 @@
 // takes the contiguous range [b*U/grid, (b+1)*U/grid). A chunk whose units all fall in one CTA is complete
 // there: at its end the CTA adds w[row, c] * acc / l for each query into the group's fold slot (a per-CTA
 // accumulator in global memory, which stays in L2). A chunk cut by a range boundary leaves an open partial
-// (m, l, acc) per query in the CTA's head or tail slot. read_multi_merge_kernel adds, per group, the fold
-// slots of the CTAs that cover it and the open partials (log-sum-exp merged per chunk, then weighted).
+// (m, l, acc) per query in the CTA's head or tail slot. read_multi_coef_kernel and read_multi_sum_kernel add, per
+// group, the fold slots of the CTAs that cover it and the open partials (log-sum-exp merged per chunk, then
+// weighted).
 //
 // CTA shape and the per-16-row arithmetic follow read_decode_mma_kernel: warp 0 lane 0 issues one 1-D bulk copy
 // (TMA, no multicast) per slot row into padded shared-memory rows; consumer warp w owns the 16*TPW columns
@@ -58,7 +59,7 @@ struct MultiArgs {
   int64_t* fold_info;   // [grid][s_max]: group, or -1 when the slot holds nothing
   float* open;          // [grid][2][MQ_OPEN + MQ * d_s]: (m, l) per query, then acc per query
   int64_t* open_info;   // [grid][2]: group * n_chunks + chunk, or -1
-  int* merge_counter;   // [n_groups * merge slabs], zeroed here for read_multi_merge_kernel
+  int* merge_counter;   // [n_groups * merge slabs], zeroed here for read_multi_sum_kernel
   int64_t n_merge_counters;
 };
 
