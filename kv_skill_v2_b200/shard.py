@@ -20,6 +20,7 @@ uses CudaShardCompute, and there is no CPU path.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import socket
 from typing import Optional
@@ -84,39 +85,49 @@ class PeerExchange:
     captured in a CUDA graph replays. close() (collective) unmaps and frees."""
 
     def __init__(self, per: int, world: int, rank: int, device: torch.device, group=None):
+        """Collective. Every rank takes the same steps whatever fails locally; `ok` is True only when every rank
+        mapped every buffer (otherwise nothing stays allocated and the caller uses the all-gather)."""
         L = N.lib()
         self.per, self.world, self.rank, self.group = int(per), int(world), int(rank), group
         self.device = torch.device(device)
+        self.ptr, self.opened = None, []
+        ok = True
+        handle = ctypes.create_string_buffer(64)
         nbytes = L.xencb_exch_bytes(self.world, self.per)
         if nbytes == 0:
-            raise ValueError(f"PeerExchange: world={world} per={per} is not supported")
-        ptr = ctypes.c_void_p()
-        handle = ctypes.create_string_buffer(64)
-        with torch.cuda.device(self.device):
-            N.check(L.xencb_exch_alloc(nbytes, ctypes.byref(ptr), ctypes.cast(handle, ctypes.c_void_p)),
-                    "xencb_exch_alloc")
-        self.ptr = ptr.value
-        self.opened = []
+            ok = False
+        else:
+            ptr = ctypes.c_void_p()
+            with self._on_device():
+                ok = L.xencb_exch_alloc(nbytes, ctypes.byref(ptr), ctypes.cast(handle, ctypes.c_void_p)) == N.OK
+            self.ptr = ptr.value if ok else None
         handles = [None] * self.world
-        dist.all_gather_object(handles, handle.raw, group=group)
+        dist.all_gather_object(handles, handle.raw if ok else None, group=group)
         peers = []
-        try:
+        if ok and all(h is not None for h in handles):
             for g, h in enumerate(handles):
                 if g == self.rank:
                     peers.append(self.ptr)
                     continue
                 pp = ctypes.c_void_p()
                 hb = ctypes.create_string_buffer(bytes(h), 64)
-                with torch.cuda.device(self.device):
-                    N.check(L.xencb_exch_open(ctypes.cast(hb, ctypes.c_void_p), ctypes.byref(pp)), "xencb_exch_open")
+                with self._on_device():
+                    if L.xencb_exch_open(ctypes.cast(hb, ctypes.c_void_p), ctypes.byref(pp)) != N.OK:
+                        ok = False
+                        break
                 peers.append(pp.value)
                 self.opened.append(pp.value)
-        except Exception:
+        else:
+            ok = False
+        votes = [None] * self.world
+        dist.all_gather_object(votes, ok, group=group)
+        self.ok = all(votes)
+        if not self.ok:
             self._release()
-            raise
-        self.peers_dev = torch.tensor(peers, dtype=torch.int64, device=self.device)
-        self.state = torch.zeros(4, dtype=torch.int32, device=self.device)
-        dist.barrier(group=group)  # every buffer is mapped everywhere before the first push
+        else:
+            self.peers_dev = torch.tensor(peers, dtype=torch.int64, device=self.device)
+            self.state = torch.zeros(4, dtype=torch.int32, device=self.device)
+        dist.barrier(group=group)  # every buffer is mapped everywhere (or released everywhere) before going on
 
     def push(self, block: torch.Tensor) -> None:
         N.call("xencb_shard_push", ops._ptr(block), self.per, ops._ptr(self.peers_dev), self.world, self.rank,
@@ -127,21 +138,25 @@ class PeerExchange:
                ops._ptr(self.state), ops._ptr(out), ops._stream(self.device))
         return out
 
+    def _on_device(self):
+        return torch.cuda.device(self.device) if self.device.type == "cuda" else contextlib.nullcontext()
+
     def _release(self) -> None:
         L = N.lib()
-        with torch.cuda.device(self.device):
+        with self._on_device():
             for pp in self.opened:
                 L.xencb_exch_close(ctypes.c_void_p(pp))
             self.opened = []
             if self.ptr:
                 L.xencb_exch_free(ctypes.c_void_p(self.ptr))
-                self.ptr = None
+            self.ptr = None
 
     def close(self) -> None:
         """Collective: no rank unmaps or frees while another may still push into its buffer."""
         if self.ptr is None:
             return
-        torch.cuda.synchronize(self.device)
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
         self._release()
 
@@ -184,9 +199,11 @@ class ShardedRead:
         want_peer = (self.world > 1 and exchange != "collective" and device.type == "cuda"
                      and isinstance(self.compute, CudaShardCompute))
         if want_peer and _one_gpu_per_rank(device, group):
-            self.peer = PeerExchange(per, self.world, self.rank, device, group)
-        elif exchange == "peer" and self.world > 1:
-            raise ValueError("ShardedRead: exchange='peer' needs CUDA kernels and one GPU per rank on one node")
+            pe = PeerExchange(per, self.world, self.rank, device, group)
+            self.peer = pe if pe.ok else None
+        if self.peer is None and exchange == "peer" and self.world > 1:
+            raise ValueError("ShardedRead: exchange='peer' needs CUDA kernels, one GPU per rank on one node and "
+                             "peer mappings of the exchange buffers")
         self.exchange_kind = "peer" if self.peer is not None else ("collective" if self.world > 1 else "none")
 
     def partial(self, q: torch.Tensor) -> torch.Tensor:

@@ -133,3 +133,75 @@ def test_sharded_read_gloo_matches_unsharded_oracle(tmp_path, world, softmax):
     ref = X.read(q, K, M, w, 12.0, softmax)
     for g in range(world):
         assert np.abs(got[g] - ref).max() <= 1e-5 * np.abs(ref).max(), g
+
+
+class _FakeExchLib:
+    """Stands in for libxencb's exchange entry points on CPU ranks: allocation and mapping succeed or fail as
+    told, and every successful call is recorded, so the collective set-up of PeerExchange is checked without a
+    GPU."""
+
+    def __init__(self, fail_alloc=False, fail_open=False):
+        self.fail_alloc, self.fail_open = fail_alloc, fail_open
+        self.calls = []
+
+    def xencb_exch_bytes(self, world, per):
+        return 256 + 2 * world * per * 4
+
+    def xencb_exch_alloc(self, nbytes, ptr_ref, handle):
+        if self.fail_alloc:
+            return 2
+        import ctypes
+        self.calls.append("alloc")
+        ctypes.cast(ptr_ref, ctypes.POINTER(ctypes.c_void_p))[0] = 0x1000
+        return 0
+
+    def xencb_exch_open(self, handle, ptr_ref):
+        if self.fail_open:
+            return 2
+        import ctypes
+        self.calls.append("open")
+        ctypes.cast(ptr_ref, ctypes.POINTER(ctypes.c_void_p))[0] = 0x2000
+        return 0
+
+    def xencb_exch_close(self, p):
+        self.calls.append("close")
+        return 0
+
+    def xencb_exch_free(self, p):
+        self.calls.append("free")
+        return 0
+
+
+def _exch_rank(rank, world, port, failing_rank, mode, result_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from kv_skill_v2_b200 import _native as N
+        from kv_skill_v2_b200.shard import PeerExchange
+        fake = _FakeExchLib(fail_alloc=(mode == "alloc" and rank == failing_rank),
+                            fail_open=(mode == "open" and rank == failing_rank))
+        N.lib = lambda: fake  # this spawned process only
+        pe = PeerExchange(per=40, world=world, rank=rank, device=torch.device("cpu"))
+        held = "alloc" in fake.calls and "free" not in fake.calls
+        with open(f"{result_path}.{rank}", "w") as f:
+            f.write(f"{int(pe.ok)} {int(held)} {fake.calls.count('open')} {fake.calls.count('close')}")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode", ["none", "alloc", "open"])
+def test_peer_exchange_setup_agrees_across_ranks(tmp_path, mode):
+    """One rank failing to allocate or to map a peer buffer makes every rank give the peer exchange up (and free
+    what it holds) instead of leaving the ranks on different exchanges; without failures every rank maps the
+    others' buffers and keeps its own."""
+    world, failing = 3, 1
+    out = tmp_path / "r"
+    mp.start_processes(_exch_rank, args=(world, _free_port(), failing, mode, str(out)), nprocs=world, join=True,
+                       start_method="spawn")
+    res = [open(f"{out}.{r}").read().split() for r in range(world)]
+    assert {r[0] for r in res} == ({"1"} if mode == "none" else {"0"})
+    for r in res:
+        if mode == "none":
+            assert r[1] == "1" and r[2] == str(world - 1)
+        else:
+            assert r[1] == "0" and r[2] == r[3]  # nothing left allocated, every opened mapping closed
