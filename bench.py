@@ -1060,6 +1060,8 @@ def run_ours(args) -> None:
         d2h_done = [torch.cuda.Event() for _ in range(2)]
         t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
+        waited = [0.0]
+
         def serve(n_steps, timed):
             ys = [None, None]
             with torch.cuda.stream(cstream):
@@ -1077,7 +1079,9 @@ def run_ours(args) -> None:
                         h_ready[1 - b].record(cstream)
                 stream.wait_event(h_ready[b])
                 if i >= 2:  # the host consumes step i-2's output before its buffer is reused: at most 2 steps in flight
+                    tw = time.perf_counter()
                     d2h_done[b].synchronize()
+                    waited[0] += time.perf_counter() - tw
                 ys[b] = reader(h_dev[b])
                 h_free[b].record(stream)
                 y_done[b].record(stream)
@@ -1093,6 +1097,7 @@ def run_ours(args) -> None:
             serve(args.warmup, False)
             torch.cuda.synchronize(dev)
             t_host = time.perf_counter()
+            waited[0] = 0.0
             serve(args.steps, True)
             t_host = time.perf_counter() - t_host
             torch.cuda.synchronize(dev)
@@ -1146,6 +1151,7 @@ def run_ours(args) -> None:
             "cpu_baseline": cpu,
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": R * d_m * 4, "d2h_bytes_per_step": R * d_m * 4,
                     "host_enqueue_us_per_step": 1e6 * t_host / args.steps,
+                    "host_wait_us_per_step": 1e6 * waited[0] / args.steps,
                     "path": "LibraryInjector forward hook on a reader block (CUDA-graph replay of the fused hook path), "
                             "PagedLibrary of 64 documents; per step an H2D copy of h from pinned memory and a D2H "
                             "copy of the output, on a copy stream overlapping the neighbouring steps' compute "
