@@ -305,9 +305,8 @@ def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
         assert torch.equal(ra, sr_c(q0)), "peer exchange differs from the all-gather"
         del sr_c
 
-    def pre():
-        q, _, _, _ = ops.project_in(h, W_in, w_prep=P_in)
-        sr.partial(q)
+    def pre():  # the input projection fused with the shard's routing, then the read
+        sr.partial_from_hidden(h, W_in, P_in)
 
     def post():
         r = sr.merge()
@@ -408,8 +407,8 @@ def run_sharded(torch, dist, dev, world: int, rank: int, steps: int, warmup: int
             "unit": "tokens/s", "n_gpus": world, "ms_per_step": ms, "scaling": "strong",
             "chunks_per_gpu": Cl, "kernels_per_step": kernels, "gpu_launches": kernels * steps,
             "components_us": comp, "exchange": kind,
-            "step": "one CUDA graph per step: input projection (replicated), route_lse + read_multi over the rank's "
-                    "chunks, the partial blocks pushed to every rank over NVLink peer memory (exchange 'peer'; "
+            "step": "one CUDA graph per step: input projection (replicated) fused with the dense routing of the "
+                    "rank's chunks, read_multi over them, the partial blocks pushed to every rank over NVLink peer memory (exchange 'peer'; "
                     "'collective': one NCCL all-gather), shard merge after the blocks' flags, output projection "
                     "(replicated)",
             "step_bytes_per_gpu": step_bytes, "step_hbm_gbs_per_gpu": step_bytes / (ms / 1000.0) / 1e9,

@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define XENCB_ABI_VERSION 5
+#define XENCB_ABI_VERSION 6
 
 #if defined(__GNUC__)
 #define XENCB_API __attribute__((visibility("default")))
@@ -129,6 +129,21 @@ XENCB_API int xencb_project_in_route(const void* h, int h_dtype, int64_t n_rows,
                                      int64_t rows_per_lib, int64_t n_lib, float route_temp, int top_k,
                                      const float* row_w, int32_t* idx, float* wk, float* w_dense, float* logit_out,
                                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* Decode form of xencb_project_in followed by xencb_route_lse (dense routing of a chunk shard for the sharded
+ * read: xenc/injector.py:235-236, :54-58 and the routing softmax of :220-229 left unnormalised): the projection
+ * GEMM, then per row q, its logits over every chunk and w_out = e^(l - max), header_out [n_rows, 4] =
+ * (max, sum, 0, 0), the same values bit for bit as the two calls. The row's dot products are spread over up to
+ * 32 CTAs. Takes what xencb_project_in_route takes (rows_per_lib < 64, flags with XENCB_PIN_L2, d_s <= 6144,
+ * (d_s + 2 * n_chunks) * 4 bytes <= 96 KiB), else XENCB_ENOTSUP with nothing launched. Workspace:
+ * xencb_project_in_workspace bytes. */
+XENCB_API int xencb_project_in_route_lse(const void* h, int h_dtype, int64_t n_rows, int d_m, const float* w_in,
+                                         const void* w_prep, const float* b_in, int d_s, int flags,
+                                         const float* gate_w, float gate_b, const float* gate_b_dev, float rms_eps,
+                                         float* q_out, float* gate_out, float* rstd_out, const float* S,
+                                         int n_chunks, const int32_t* n_chunks_of, int64_t rows_per_lib,
+                                         int64_t n_lib, float route_temp, float* w_out, float* header_out,
+                                         void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------
  * Masked decode read over the routed chunks. Replaces the read of LibraryInjector._branch

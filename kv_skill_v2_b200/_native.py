@@ -19,7 +19,7 @@ OK, EINVAL, ECUDA, ENOTSUP = 0, 1, 2, 3
 DEV_TIMEOUT, DEV_CLAMPED, DEV_BADPAGE = 1, 2, 4
 PIN_RMS, PIN_L2 = 1, 2
 NOALLOC_SCRATCH_BYTES = 16 << 20
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 _p, _i, _i64, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
 
@@ -34,6 +34,8 @@ SIGNATURES: dict = {
                               _p, _sz, _p]),
     "xencb_project_in_route": (_i, [_p, _i, _i64, _i, _p, _p, _p, _i, _i, _p, _f, _p, _p, _p, _i, _f, _p, _p, _p,
                                     _p, _p, _i, _p, _i64, _i64, _f, _i, _p, _p, _p, _p, _p, _p, _sz, _p]),
+    "xencb_project_in_route_lse": (_i, [_p, _i, _i64, _i, _p, _p, _p, _i, _i, _p, _f, _p, _f, _p, _p, _p, _p, _i, _p,
+                                        _i64, _i64, _f, _p, _p, _p, _sz, _p]),
     "xencb_rms_norm": (_i, [_p, _i, _i64, _i, _f, _p, _p]),
     "xencb_route_k": (_i, [_i, _i]),
     "xencb_route": (_i, [_p, _i64, _i, _p, _i, _p, _i64, _i64, _f, _i, _p, _p, _p, _p, _p, _p]),

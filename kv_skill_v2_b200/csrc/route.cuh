@@ -363,12 +363,16 @@ struct RouteFuse {
   // (zeroed by the projection GEMM of the same call) counts the CTAs that stored theirs.
   float* xlg;
   int* done;
+  // dense shard routing instead of the top-k (non-null): route_lse_kernel's output, w_dense = e^(l - max) and
+  // lse_header[4 row] = (max, sum, 0, 0)
+  float* lse_header;
 };
 
 // Grid (n_rows, G). CTA (row, g) computes the row's q (every CTA the same values; only g = 0 writes q, 1/rms, the
 // gate and the selector logits) and the dot products of chunks [g * per, (g + 1) * per), per = ceil(C / G): the
 // row's summary keys stream through G SMs instead of one. With G > 1 each CTA stores its logits in xlg, and the
-// CTA that counts last in done[row] (after a fence) reads the whole row back and runs the top-k.
+// CTA that counts last in done[row] (after a fence) reads the whole row back and runs the top-k (or, for dense
+// shard routing, route_lse_kernel's max / sum and unnormalised weights).
 template <typename TH, int VPT>
 __global__ void __launch_bounds__(ROW_THREADS) project_in_route_kernel(const TH* __restrict__ h, const PinArgs a,
                                                                       const RouteFuse rf) {
@@ -423,6 +427,24 @@ __global__ void __launch_bounds__(ROW_THREADS) project_in_route_kernel(const TH*
     __syncthreads();
   }
   if (w != 0) return;
+  if (rf.lse_header) {  // route_lse_kernel's arithmetic, in its order, on the row's logits
+    float mx = -CUDART_INF_F;
+    for (int c = lane; c < nc; c += 32) mx = fmaxf(mx, lg[c]);
+    mx = warp_max(mx);
+    float sum = 0.f;
+    if (nc > 0)
+      for (int c = lane; c < nc; c += 32) sum += expf(lg[c] - mx);
+    sum = warp_sum(sum);
+    float* wr = rf.w_dense + row * rf.C;
+    for (int c = lane; c < rf.C; c += 32) wr[c] = c < nc ? expf(lg[c] - mx) : 0.f;
+    if (lane == 0) {
+      rf.lse_header[row * 4] = mx;
+      rf.lse_header[row * 4 + 1] = sum;
+      rf.lse_header[row * 4 + 2] = 0.f;
+      rf.lse_header[row * 4 + 3] = 0.f;
+    }
+    return;
+  }
   topk_row(lg, lg + rf.C, rf.C, nc, rf.top_k, rf.k_out, rf.row_w ? rf.row_w[row] : 1.f, rf.idx + row * rf.k_out,
            rf.wk + row * rf.k_out, rf.w_dense ? rf.w_dense + row * rf.C : nullptr, lane);
 }

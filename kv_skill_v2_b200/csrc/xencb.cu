@@ -716,7 +716,8 @@ static int project_in_impl(const void* h, int h_dtype, int64_t n_rows, int d_m, 
     // has a [n_rows, C] output to pass the logits through. XENCB_ROUTE_CTAS=<n> in the environment fixes it.
     int G = 1;
     if (rf && (rf->logit_out || rf->w_dense)) {
-      G = (int)std::max<int64_t>(1, std::min<int64_t>(8, di.sms / n_rows));
+      // dense shard routing reads every chunk: up to 32 CTAs per row there
+      G = (int)std::max<int64_t>(1, std::min<int64_t>(rf->lse_header ? 32 : 8, di.sms / n_rows));
       if (const char* e = getenv("XENCB_ROUTE_CTAS")) G = std::max(1, std::min(8, atoi(e)));
       G = std::min(G, rf->C);
     }
@@ -791,10 +792,30 @@ int xencb_project_in_route(const void* h, int h_dtype, int64_t n_rows, int d_m, 
   if (top_k < 0) return fail(XENCB_EINVAL, "project_in_route: top_k=%d must be >= 0", top_k);
   if (!aligned(S, 16)) return fail(XENCB_EINVAL, "project_in_route: S must be 16-byte aligned");
   const RouteFuse rf{S,  n_chunks, n_chunks_of, rows_per_lib, route_temp, top_k, xencb_route_k(top_k, n_chunks),
-                     row_w, idx, wk, w_dense, logit_out, nullptr, nullptr};
+                     row_w, idx, wk, w_dense, logit_out, nullptr, nullptr, nullptr};
   return project_in_impl(h, h_dtype, n_rows, d_m, w_in, w_prep, b_in, d_s, flags, gate_w, gate_b, gate_b_dev, sel_w,
                          sel_b, n_cand, rms_eps, q_out, gate_out, rstd_out, z_out, workspace, workspace_bytes, stream,
                          &rf);
+}
+
+int xencb_project_in_route_lse(const void* h, int h_dtype, int64_t n_rows, int d_m, const float* w_in,
+                               const void* w_prep, const float* b_in, int d_s, int flags, const float* gate_w,
+                               float gate_b, const float* gate_b_dev, float rms_eps, float* q_out, float* gate_out,
+                               float* rstd_out, const float* S, int n_chunks, const int32_t* n_chunks_of,
+                               int64_t rows_per_lib, int64_t n_lib, float route_temp, float* w_out, float* header_out,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  if (!S || !w_out || !header_out) return fail(XENCB_EINVAL, "project_in_route_lse: S, w_out and header_out are required");
+  if (n_rows <= 0 || n_chunks <= 0 || rows_per_lib <= 0 || n_lib <= 0)
+    return fail(XENCB_EINVAL, "project_in_route_lse: sizes must be positive");
+  if ((n_rows + rows_per_lib - 1) / rows_per_lib > n_lib)
+    return fail(XENCB_EINVAL, "project_in_route_lse: %lld rows at %lld rows per Library need more than %lld "
+                "Libraries", (long long)n_rows, (long long)rows_per_lib, (long long)n_lib);
+  if (!aligned(S, 16)) return fail(XENCB_EINVAL, "project_in_route_lse: S must be 16-byte aligned");
+  const RouteFuse rf{S, n_chunks, n_chunks_of, rows_per_lib, route_temp, 0, 0, nullptr, nullptr, nullptr, w_out,
+                     nullptr, nullptr, nullptr, header_out};
+  return project_in_impl(h, h_dtype, n_rows, d_m, w_in, w_prep, b_in, d_s, flags, gate_w, gate_b, gate_b_dev,
+                         nullptr, nullptr, 0, rms_eps, q_out, gate_out, rstd_out, nullptr, workspace, workspace_bytes,
+                         stream, &rf);
 }
 
 int xencb_rms_norm(const void* h, int h_dtype, int64_t n_rows, int d_m, float eps, float* out, void* stream) {

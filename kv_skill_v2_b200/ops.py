@@ -204,6 +204,51 @@ def project_in_route(h2: torch.Tensor, w_in: torch.Tensor, b_in=None, *, S: torc
     return q, gate, rstd, idx, wk, w, lg
 
 
+def project_in_route_lse(h2: torch.Tensor, w_in: torch.Tensor, b_in=None, *, S: torch.Tensor, rows_per_lib: int,
+                         route_temp: float, n_chunks_of: Optional[torch.Tensor] = None,
+                         header_out: Optional[torch.Tensor] = None, eps: float = 1e-6,
+                         w_prep: Optional[torch.Tensor] = None):
+    """project_in (rms + L2) and the dense shard routing of route_lse in one pass after the GEMM
+    (xencb_project_in_route_lse): (q, w [R, C] = e^(l - max), header [R, 4] = (max, sum, 0, 0)), the same values as
+    project_in then route_lse. Shapes the fused form does not take run the two calls."""
+    dev = _cuda("project_in_route_lse", h2, w_in, b_in, S, n_chunks_of)
+    h2 = h2.contiguous()
+    w_in = _f32(w_in, "w_in")
+    S = _f32(S, "S")
+    R, d_m = h2.shape
+    d_s = w_in.shape[0]
+    if w_in.shape[1] != d_m:
+        raise ValueError(f"w_in is {tuple(w_in.shape)}, expected [d_s, {d_m}] (nn.Linear layout)")
+    n_lib, C, d2 = S.shape
+    if d2 != d_s:
+        raise ValueError(f"project_in_route_lse: q has d_s={d_s}, S has {d2}")
+    if header_out is None:
+        header_out = torch.empty(R, 4, dtype=torch.float32, device=dev)
+    elif header_out.dtype != torch.float32 or tuple(header_out.shape) != (R, 4) or not header_out.is_contiguous():
+        raise ValueError("project_in_route_lse: header_out must be a contiguous float32 [R, 4] tensor")
+    if n_chunks_of is not None:
+        n_chunks_of = n_chunks_of.to(torch.int32).contiguous()
+    two_calls = int(rows_per_lib) >= 64
+    if not two_calls:
+        q = torch.empty(R, d_s, dtype=torch.float32, device=dev)
+        rstd = torch.empty(R, dtype=torch.float32, device=dev)
+        w = torch.empty(R, C, dtype=torch.float32, device=dev)
+        b_in = _f32(b_in, "b_in")
+        with _on_device(dev):
+            ws = _workspace(N.lib().xencb_project_in_workspace(R, d_m, d_s), dev)
+            rc = N.lib().xencb_project_in_route_lse(
+                _ptr(h2), _hdt(h2, "h"), R, d_m, _ptr(w_in), _ptr(w_prep), _ptr(b_in), d_s, N.PIN_RMS | N.PIN_L2,
+                None, 0.0, None, eps, _ptr(q), None, _ptr(rstd), _ptr(S), C, _ptr(n_chunks_of), int(rows_per_lib),
+                n_lib, float(route_temp), _ptr(w), _ptr(header_out), _ptr(ws), ws.numel(), _stream(dev))
+            if rc != N.ENOTSUP:
+                N.check(rc, "xencb_project_in_route_lse")
+                return q, w, header_out
+    q, _, _, _ = project_in(h2, w_in, b_in, eps=eps, w_prep=w_prep)
+    w, _ = route_lse(q, S, rows_per_lib=rows_per_lib, route_temp=route_temp, n_chunks_of=n_chunks_of,
+                     header_out=header_out)
+    return q, w, header_out
+
+
 def project_out(r: torch.Tensor, w_out: torch.Tensor, h2: torch.Tensor, *, b_out=None, scale: float = 1.0,
                 log_scale: Optional[torch.Tensor] = None, gate=None, sel_w=None, log_alpha=0.0, pos_mask=None,
                 want_delta: bool = True, h_out: Optional[torch.Tensor] = None, want_rel: bool = False,

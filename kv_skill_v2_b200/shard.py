@@ -72,6 +72,17 @@ class CudaShardCompute:
         ops.read_weighted(q, pages, w, rows_per_lib=rows_per_lib, read_temp=self.read_temp,
                           read_softmax=self.read_softmax, out=acc)
 
+    def partial_from_hidden(self, h: torch.Tensor, w_in: torch.Tensor, w_prep, pages: ops.Pages, rows_per_lib: int,
+                            header: torch.Tensor, acc: torch.Tensor) -> torch.Tensor:
+        """The input projection of the hidden rows h fused with the shard's routing (one pass after the GEMM),
+        then the read; returns q."""
+        q, w, _ = ops.project_in_route_lse(h, w_in, S=pages.S, rows_per_lib=rows_per_lib,
+                                           route_temp=self.route_temp, n_chunks_of=pages.n_chunks_of,
+                                           header_out=header, w_prep=w_prep)
+        ops.read_weighted(q, pages, w, rows_per_lib=rows_per_lib, read_temp=self.read_temp,
+                          read_softmax=self.read_softmax, out=acc)
+        return q
+
     def merge(self, gathered: torch.Tensor, world: int, n_rows: int, d_s: int, out: torch.Tensor) -> None:
         ops.shard_merge(gathered, world, n_rows, d_s, out=out)
 
@@ -205,6 +216,14 @@ class ShardedRead:
             raise ValueError("ShardedRead: exchange='peer' needs CUDA kernels, one GPU per rank on one node and "
                              "peer mappings of the exchange buffers")
         self.exchange_kind = "peer" if self.peer is not None else ("collective" if self.world > 1 else "none")
+
+    def partial_from_hidden(self, h: torch.Tensor, w_in: torch.Tensor, w_prep=None) -> torch.Tensor:
+        """This rank's block from the hidden rows h [n_rows, d_m]: q = project_in(h) (rms, L2) fused with the
+        routing, then the read (CUDA kernels only). Returns the block."""
+        if not isinstance(self.compute, CudaShardCompute):
+            raise TypeError("ShardedRead.partial_from_hidden needs the CUDA kernels")
+        self.compute.partial_from_hidden(h, w_in, w_prep, self.pages, self.rows_per_lib, self.header, self.acc)
+        return self.block
 
     def partial(self, q: torch.Tensor) -> torch.Tensor:
         """This rank's block (headers, accumulators) for query rows q [n_rows, d_s]."""

@@ -748,6 +748,34 @@ def test_project_in_route_matches_the_two_calls(dev, case):
     _status_clean(dev)
 
 
+@pytest.mark.parametrize("case", [
+    # (n_lib, rows_per_lib, C, d_s, d_m, use_nco)
+    (1, 8, 256, 2560, 5120, False),    # one rank's config-5 shard at 8 GPUs: up to 18 CTAs per row
+    (1, 8, 2048, 2560, 1024, False),   # the whole config-5 Library: 114 chunks per CTA
+    (3, 4, 5, 256, 512, True),         # fewer chunks than CTAs, per-Library chunk counts
+    (1, 64, 16, 128, 256, False),      # rows_per_lib >= 64: the two calls
+])
+def test_project_in_route_lse_matches_the_two_calls(dev, case):
+    """xencb_project_in_route_lse gives project_in's q and route_lse's unnormalised weights and (max, sum) headers
+    bit for bit (the same sums in the same order), so a sharded read that uses it merges as before."""
+    from kv_skill_v2_b200 import ops
+    n_lib, rpl, C, d_s, d_m, use_nco = case
+    g = torch.Generator().manual_seed(C + d_s + rpl)
+    R = n_lib * rpl
+    h = torch.randn(R, d_m, generator=g).to(dev)
+    W = (torch.randn(d_s, d_m, generator=g) * 0.02).to(dev)
+    S = torch.nn.functional.normalize(torch.randn(n_lib, C, d_s, generator=g), dim=-1).to(dev)
+    nco = torch.randint(1, C + 1, (n_lib,), generator=g, dtype=torch.int32).to(dev) if use_nco else None
+    prep = ops.weights_prep(W)
+    q0, _, _, _ = ops.project_in(h, W, w_prep=prep)
+    w0, h0 = ops.route_lse(q0, S, rows_per_lib=rpl, route_temp=10.0, n_chunks_of=nco)
+    q1, w1, h1 = ops.project_in_route_lse(h, W, S=S, rows_per_lib=rpl, route_temp=10.0, n_chunks_of=nco,
+                                          w_prep=prep)
+    assert torch.equal(q0, q1)
+    assert torch.equal(w0, w1) and torch.equal(h0, h1)
+    _status_clean(dev)
+
+
 @pytest.mark.parametrize("name", ["attn_record_top2", "attn_record_linear", "attn_force", "attn_force_norm"])
 def test_attention_diagnostics_against_reference(dev, name):
     """record_attn (last_attn[li]: the last position's route-weighted slot attention of batch row 0) and force_attn
