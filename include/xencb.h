@@ -396,10 +396,12 @@ XENCB_API int xencb_topk_read(const float* q, int64_t n_rows, int d_s, const voi
 
 /* ---------------------------------------------------------------------------------------------------------
  * Weight preparation for the 3xF16 projection GEMM (done once per weight tensor, e.g. when an interface is
- * loaded): w [n, k] float32 -> prep = a 256-byte head (max |w|, 1/s) followed by the stacked f16 pair
- * [hi; lo] of w * s, s = 2^e with max|w| * s in [2^14, 2^15). hi + lo keeps ~22 mantissa bits, and the GEMM
- * sums hi*hi + hi*lo + lo*hi (the relative error of the 3xTF32 product). k % 8 == 0; prep 256-byte aligned,
- * at least xencb_weights_prep_bytes(n, k) bytes (4 bytes per weight + 256). */
+ * loaded): w [n, k] float32 -> prep = a 256-byte head (max |w|, 1/s) followed by the f16 pair hi, lo of
+ * w * s, s = 2^e with max|w| * s in [2^14, 2^15), in 128 x 64 tiles (per 128-row band and 64-column block, the
+ * hi tile then the lo tile, 32 KiB, bands outer; zeros past n and k), so that the GEMM reads each CTA's share
+ * of the weight as one contiguous run. hi + lo keeps ~22 mantissa bits, and the GEMM sums hi*hi + hi*lo +
+ * lo*hi (the relative error of the 3xTF32 product). k % 8 == 0; prep 256-byte aligned, at least
+ * xencb_weights_prep_bytes(n, k) bytes (4 bytes per weight with n rounded up to 128 and k to 64, + 256). */
 XENCB_API size_t xencb_weights_prep_bytes(int n, int k);
 XENCB_API int xencb_weights_prep(const float* w, int n, int k, void* prep, size_t prep_bytes, void* stream);
 

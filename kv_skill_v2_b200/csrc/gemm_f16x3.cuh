@@ -6,20 +6,22 @@
 // lo = rn(v - hi) keeps ~22 bits, and hi*hi + hi*lo + lo*hi (the dropped lo*lo is below 2^-22 relative) gives the
 // accuracy of the 3xTF32 product, with twice the K per tensor-core instruction of kind::tf32 and half the
 // operand bytes. f16 has a small exponent range, so both sides are scaled by powers of two first (exact):
-//   * W once per weight tensor (xencb_weights_prep): s_w = 2^e with max|W| s_w in [2^14, 2^15), stored as the
-//     stacked f16 pair [W_hi; W_lo] ([2N, K], the same 4 bytes per weight as fp32) and 1 / s_w;
+//   * W once per weight tensor (xencb_weights_prep): s_w = 2^e with max|W| s_w in [2^14, 2^15), stored as f16
+//     tiles of W_hi and W_lo (the same 4 bytes per weight as fp32; layout at split_weights_kernel) and 1 / s_w;
 //   * X per call and per row (split_rows_f16x2_kernel): s_m = 2^e_m from the row's max |x|, rows stacked
 //     [X_hi; X_lo] ([2M, K]) with 1 / s_m per row.
 // Values far below a row's (or the weight's) maximum lose relative precision in f16's subnormal range; their
 // share of a dot product is below 2^-28 of its largest term.
 //
 // gemm_f16x3_kernel: D[n][m] = W[n, :] . X[m, :] (128 output features = UMMA M, up to 64 tokens = UMMA N).
-// Warp 0 lane 0 TMA-loads per 64-column k-block the four 128-byte-swizzled boxes W_hi, W_lo [128 x 64] and
-// X_hi, X_lo [64 x 64] into a 4- or 2-stage ring (weights with L2 evict-last); warp 1 lane 0 issues 4 k-steps x 3
-// tcgen05.mma kind::f16 (f32 accumulate in TMEM) per k-block and commits each stage back to the producer;
-// warps 2-5 read the accumulator (tcgen05.ld), undo the scales and store the split partial. Boxes that run
-// past N or M read rows of the other half of the stacked pair or zeros; they only reach outputs n >= N or
-// m >= M, which are not stored. Every barrier wait is bounded; TMEM is freed on every path.
+// Warp 0 lane 0 TMA-loads per 64-column k-block the tile pair W_hi, W_lo [2 x 128 x 64] (one contiguous 32 KiB
+// run of the prepared weight, so a CTA's k-blocks are one sequential stream) and the boxes X_hi, X_lo [64 x 64],
+// all 128-byte-swizzled, into a 4- or 2-stage ring (weights with L2 evict-last); warp 1 lane 0 issues 4 k-steps
+// x 3 tcgen05.mma kind::f16 (f32 accumulate in TMEM) per k-block and commits each stage back to the producer;
+// warps 2-5 read the accumulator (tcgen05.ld), undo the scales and store the split partial. Weight rows past N
+// and columns past K are zeros in the prepared tiles; X boxes that run past M read rows of the other half of
+// the stacked pair or zeros, which only reach outputs m >= M (not stored). Every barrier wait is bounded; TMEM
+// is freed on every path.
 #pragma once
 
 #include "tc.cuh"
@@ -39,7 +41,13 @@ constexpr int H3_THREADS = 32 * 6;
 // slower at config 2).
 __host__ __device__ constexpr size_t h3_smem(int stages) { return 1024 + (size_t)stages * H3_STAGE + 256; }
 constexpr uint32_t H3_TMEM_COLS = 64;
-constexpr int WPREP_HEAD = 256;  // bytes before [W_hi; W_lo] in a prepared weight: float max_bits, float inv_scale
+constexpr int WPREP_HEAD = 256;  // bytes before the tiles of a prepared weight: float max_bits, float inv_scale
+constexpr int WPREP_PAIR = 2 * H3_BM * H3_BK;  // halves per tile pair (W_hi tile, then W_lo tile): 32 KiB
+
+// Tile pairs of a prepared [n, k] weight: 128-row bands x 64-column blocks.
+__host__ __device__ inline int64_t wprep_pairs(int64_t n, int64_t k) {
+  return ((n + H3_BM - 1) / H3_BM) * ((k + H3_BK - 1) / H3_BK);
+}
 
 // 2^e with max * 2^e in [2^14, 2^15) (e = 0 for max 0 or non-finite): exact power-of-two scale into f16 range.
 __device__ __forceinline__ float f16_range_scale(float mx) {
@@ -64,18 +72,34 @@ __global__ void __launch_bounds__(256) absmax_kernel(const float* __restrict__ w
   if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
 }
 
-// Weight prep, pass 2: [W_hi; W_lo] with the scale from pass 1, and 1 / s_w into the head.
-__global__ void __launch_bounds__(256) split_weights_kernel(const float* __restrict__ w, int64_t n,
+// Weight prep, pass 2: the tiles of W_hi and W_lo with the scale from pass 1, and 1 / s_w into the head.
+// Layout: tile pair p = band * KB + block (KB = ceil(k / 64) blocks per band; band = 128 rows of W, block = 64
+// columns) at p * 32 KiB: the band's 128 x 64 f16 tile of W_hi, then the one of W_lo, each row-major (128 bytes
+// a row). Rows past n and columns past k are zeros. Each thread writes 8 consecutive halves of a tile row
+// (k % 8 == 0, so a group of 8 is either all inside k or all past it).
+__global__ void __launch_bounds__(256) split_weights_kernel(const float* __restrict__ w, int n, int k,
                                                             const unsigned int* __restrict__ maxbits,
-                                                            __half* __restrict__ hi, __half* __restrict__ lo,
+                                                            __half* __restrict__ tiles,
                                                             float* __restrict__ inv_scale) {
   const float s = f16_range_scale(__uint_as_float(*maxbits));
   if (blockIdx.x == 0 && threadIdx.x == 0) *inv_scale = 1.f / s;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    __half h, l;
-    split_f16<float>(w[i] * s, h, l);
-    hi[i] = h;
-    lo[i] = l;
+  const int KB = (k + H3_BK - 1) / H3_BK;
+  const int64_t groups = wprep_pairs(n, k) * (H3_BM * H3_BK / 8);
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < groups;
+       g += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t p = g / (H3_BM * H3_BK / 8);
+    const int r = (int)(g / (H3_BK / 8)) % H3_BM, c8 = (int)(g % (H3_BK / 8));
+    const int row = (int)(p / KB) * H3_BM + r, col = (int)(p % KB) * H3_BK + c8 * 8;
+    const bool in = row < n && col < k;  // scalar loads: w needs no more than float alignment
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = in ? w[(int64_t)row * k + col + e] : 0.f;
+    alignas(16) __half h[8], l[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) split_f16<float>(v[e] * s, h[e], l[e]);
+    __half* dst = tiles + p * WPREP_PAIR + r * H3_BK + c8 * 8;
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(h);
+    *reinterpret_cast<uint4*>(dst + H3_BM * H3_BK) = *reinterpret_cast<const uint4*>(l);
   }
 }
 
@@ -169,6 +193,8 @@ __global__ void __launch_bounds__(H3_THREADS, MINB) gemm_f16x3_kernel(const __gr
   const int kbeg = blockIdx.z * kps;
   const int kend = min(K, kbeg + kps);
   const int nkb = kend > kbeg ? (kend - kbeg + H3_BK - 1) / H3_BK : 0;
+  // the prepared weight's tile-pair rows: pair (band blockIdx.x, block kb) starts at row 256 * pair
+  const int wrow0 = (blockIdx.x * ((K + H3_BK - 1) / H3_BK) + kbeg / H3_BK) * 2 * H3_BM;
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&map_w);
@@ -212,9 +238,7 @@ __global__ void __launch_bounds__(H3_THREADS, MINB) gemm_f16x3_kernel(const __gr
       for (int kb = 0; kb < npre; ++kb) {
         unsigned char* st = smem + kb * H3_STAGE;
         mbar_arrive_expect_tx(&full[kb], H3_STAGE);
-        const int k = kbeg + kb * H3_BK;
-        tma_load_2d_hint(st, &map_w, k, n0, &full[kb], keep);
-        tma_load_2d_hint(st + H3_WBOX, &map_w, k, N + n0, &full[kb], keep);
+        tma_load_2d_hint(st, &map_w, 0, wrow0 + kb * 2 * H3_BM, &full[kb], keep);
       }
       pdl_wait();
       pdl_trigger();
@@ -231,8 +255,7 @@ __global__ void __launch_bounds__(H3_THREADS, MINB) gemm_f16x3_kernel(const __gr
         unsigned char* st = smem + s * H3_STAGE;
         mbar_arrive_expect_tx(&full[s], H3_STAGE);
         const int k = kbeg + kb * H3_BK;
-        tma_load_2d_hint(st, &map_w, k, n0, &full[s], keep);
-        tma_load_2d_hint(st + H3_WBOX, &map_w, k, N + n0, &full[s], keep);
+        tma_load_2d_hint(st, &map_w, 0, wrow0 + kb * 2 * H3_BM, &full[s], keep);  // W_hi then W_lo tile
         tma_load_2d(st + 2 * H3_WBOX, &map_x, k, (int)m0, &full[s]);
         tma_load_2d(st + 2 * H3_WBOX + H3_XBOX, &map_x, k, (int)(M + m0), &full[s]);
       }

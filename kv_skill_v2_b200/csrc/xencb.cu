@@ -253,7 +253,7 @@ int launch_gemm(const void* X, int64_t M, int K, const float* W, int N, int sms,
   // prepared weights are given: half the MMAs of 3xTF32, and no per-k-block split of W
   const bool f16x3 = w_prep != nullptr;
   if (f16x3 && K % 8 == 0 && aligned(w_prep, 256) && aligned(X, 16) && xbuf && M <= INT32_MAX / 2 &&
-      N <= INT32_MAX / 2) {
+      N <= INT32_MAX / 2 && wprep_pairs(N, K) * 2 * H3_BM <= INT32_MAX) {
     const bool two = M > H3_BN;  // more than one row tile: two CTAs per SM (see gemm_f16x3.cuh)
     const GemmPlan p = plan_gemm_tc(M, N, K, (two ? 2 : 1) * sms);
     __half* xs = reinterpret_cast<__half*>(xbuf);  // [X_hi; X_lo]: 2 M K halves = M K floats of staging
@@ -263,8 +263,9 @@ int launch_gemm(const void* X, int64_t M, int K, const float* W, int N, int sms,
     XENCB_CHECK_LAUNCH("split_rows_f16x2 launch");
     const char* wp = static_cast<const char*>(w_prep);
     CUtensorMap mw, mx;
-    int rc = tensor_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, wp + WPREP_HEAD, (uint64_t)K, 2 * (uint64_t)N,
-                           (uint64_t)K * 2, H3_BK, H3_BM);
+    // the prepared tiles as one [pairs * 256, 64] f16 matrix: a box of 256 rows is one tile pair (W_hi, W_lo)
+    int rc = tensor_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, wp + WPREP_HEAD, H3_BK,
+                           (uint64_t)wprep_pairs(N, K) * 2 * H3_BM, H3_BK * 2, H3_BK, 2 * H3_BM);
     if (rc) return rc;
     rc = tensor_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xs, (uint64_t)K, 2 * (uint64_t)M, (uint64_t)K * 2,
                        H3_BK, H3_BN);
@@ -1746,7 +1747,7 @@ int xencb_topk_read(const float* q, int64_t n_rows, int d_s, const void* slots, 
 
 size_t xencb_weights_prep_bytes(int n, int k) {
   if (n <= 0 || k <= 0) return 0;
-  return WPREP_HEAD + 4 * (size_t)n * (size_t)k;
+  return WPREP_HEAD + (size_t)wprep_pairs(n, k) * WPREP_PAIR * sizeof(__half);
 }
 
 int xencb_weights_prep(const float* w, int n, int k, void* prep, size_t prep_bytes, void* stream) {
@@ -1764,8 +1765,8 @@ int xencb_weights_prep(const float* w, int n, int k, void* prep, size_t prep_byt
   const unsigned blocks = (unsigned)std::min<int64_t>((cnt + 255) / 256, 4096);
   absmax_kernel<<<blocks, 256, 0, st>>>(w, cnt, head);
   XENCB_CHECK_LAUNCH("absmax launch");
-  __half* hi = reinterpret_cast<__half*>(static_cast<char*>(prep) + WPREP_HEAD);
-  split_weights_kernel<<<blocks, 256, 0, st>>>(w, cnt, head, hi, hi + cnt, reinterpret_cast<float*>(head) + 1);
+  __half* tiles = reinterpret_cast<__half*>(static_cast<char*>(prep) + WPREP_HEAD);
+  split_weights_kernel<<<blocks, 256, 0, st>>>(w, n, k, head, tiles, reinterpret_cast<float*>(head) + 1);
   XENCB_CHECK_LAUNCH("split_weights launch");
   return XENCB_OK;
 }

@@ -100,7 +100,8 @@ def _dev_scalar(x, what: str):
 
 def weights_prep(w: torch.Tensor) -> torch.Tensor:
     """The 3xF16 form of a float32 weight [n, k] (k % 8 == 0) for project_in / project_out's w_prep: a 256-byte
-    head, then the stacked f16 pair [hi; lo] of w scaled by a power of two (4 bytes per weight)."""
+    head, then the f16 pair hi, lo of w scaled by a power of two, in 128 x 64 tiles (4 bytes per weight, n rounded
+    up to 128 and k to 64)."""
     dev = _cuda("weights_prep", w)
     w = _f32(w, "w")
     n, k = w.shape

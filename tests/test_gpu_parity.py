@@ -345,6 +345,31 @@ def test_projection_gemm_f16x3_fp32_faithful(dev, shape, hdt):
     _status_clean(dev)
 
 
+@pytest.mark.parametrize("nk", [(200, 520), (128, 64), (4096, 2048), (44, 40)])
+def test_weights_prep_tile_layout(dev, nk):
+    """weights_prep's layout: a 256-byte head (max |w|, 1/s), then per 128-row band and 64-column block the
+    128 x 64 f16 tile of hi = rn(w s) and the one of lo = rn(w s - hi), bands outer, zeros past n and k."""
+    from kv_skill_v2_b200 import ops
+    n, k = nk
+    g = torch.Generator().manual_seed(n + k)
+    W = torch.randn(n, k, generator=g) * 0.05
+    prep = ops.weights_prep(W.to(dev)).cpu()
+    NT, KB = (n + 127) // 128, (k + 63) // 64
+    assert prep.numel() == 256 + NT * KB * 2 * 128 * 64 * 2
+    head = prep[:8].view(torch.float32)
+    assert head[0].item() == W.abs().max().item()
+    s = 1.0 / head[1].item()
+    assert s == 2.0 ** round(np.log2(s))  # a power of two
+    tiles = prep[256:].view(torch.float16).view(NT, KB, 2, 128, 64)
+    full = tiles.permute(2, 0, 3, 1, 4).reshape(2, NT * 128, KB * 64)  # [hi | lo][band row][block column]
+    v = W * s
+    hi = v.half()
+    lo = (v - hi.float()).half()
+    assert torch.equal(full[0, :n, :k], hi) and torch.equal(full[1, :n, :k], lo)
+    assert not full[:, n:, :].any() and not full[:, :, k:].any()
+    _status_clean(dev)
+
+
 def test_injector_f16x3_matches_tf32_path(dev):
     """The hooked model with the 3xF16 projections (default) and with 3xTF32 (gemm_f16x3 = False) agree with the
     reference's output; the per-layer CUDA graphs are keyed by the weights' versions, so an in-place weight change
