@@ -95,6 +95,31 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 2) : 32 * 12, 
   volatile int* abort_flag = reinterpret_cast<volatile int*>(pbar + RM_SBUF);
   int* plan = const_cast<int*>(reinterpret_cast<volatile int*>(abort_flag) + 4);  // [plan_pairs + 1], in-kernel plan
 
+  {
+    uint4* z = reinterpret_cast<uint4*>(stages);
+    const int n16 = a.n_stage * stage_bytes / 16;
+    for (int i = threadIdx.x; i < n16; i += blockDim.x) z[i] = make_uint4(0u, 0u, 0u, 0u);
+    fence_proxy_async_smem();  // the zeros precede the bulk copies into the same bytes
+    // score slots of warps >= ncw are never written: they stay 0 for the vector sum
+    for (int i = threadIdx.x; i < RM_SBUF * 16 * RM_RED_STRIDE; i += blockDim.x) red[i] = 0.f;
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < a.n_stage; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], ncw);
+    }
+    for (int i = 0; i < RM_SBUF; ++i) {
+      mbar_init(&sbar[i], ncw);
+      mbar_init(&pbar[i], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  // Under programmatic dependent launch everything above (shared memory only) overlaps the kernel before; the
+  // routing outputs (idx, wk) and q are read only after the wait. The trigger lets the merge be scheduled.
+  pdl_wait();
+  pdl_trigger();
+
   // work units: every item in order, or (sparse plan) the items that hold rows: listed by read_compact_kernel, or
   // counted and scanned here by the whole block
   int64_t n_work = a.n_items;
@@ -122,7 +147,7 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 2) : 32 * 12, 
     __syncthreads();
     n_work = plan[np];
   }
-  // the producer's first 32 items (one per lane) are looked up before the prologue, so the lookups overlap it
+  // the producer's first 32 items are looked up together (one per lane), so their lookups overlap one another
   ItemRange mine;
   mine.active = false;
   mine.r0 = mine.r1 = 0;
@@ -132,26 +157,6 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 2) : 32 * 12, 
     if (a.item_list) n_work = *a.n_active;
     const int64_t my_w = blockIdx.x + (int64_t)lane * gridDim.x;
     if (my_w < n_work) mine = decode_item(a, work_item(a, plan, my_w));
-  }
-  {
-    uint4* z = reinterpret_cast<uint4*>(stages);
-    const int n16 = a.n_stage * stage_bytes / 16;
-    for (int i = threadIdx.x; i < n16; i += blockDim.x) z[i] = make_uint4(0u, 0u, 0u, 0u);
-    fence_proxy_async_smem();  // the zeros precede the bulk copies into the same bytes
-    // score slots of warps >= ncw are never written: they stay 0 for the vector sum
-    for (int i = threadIdx.x; i < RM_SBUF * 16 * RM_RED_STRIDE; i += blockDim.x) red[i] = 0.f;
-  }
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < a.n_stage; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], ncw);
-    }
-    for (int i = 0; i < RM_SBUF; ++i) {
-      mbar_init(&sbar[i], ncw);
-      mbar_init(&pbar[i], 1);
-    }
-    *abort_flag = 0;
-    fence_mbar_init();
   }
   __syncthreads();
 

@@ -1000,7 +1000,7 @@ static int read_decode_impl(const float* q, int64_t n_rows, int d_s, const void*
       cudaEvent_t ev0 = g_read_ev_before, ev1 = g_read_ev_after;
       g_read_ev_before = g_read_ev_after = nullptr;
       if (ev0) cudaEventRecord(ev0, st);
-      k1<<<p.grid, p.threads, p.smem, st>>>(a);
+      launch_pdl(k1, dim3(p.grid), dim3(p.threads), p.smem, st, a);
       XENCB_CHECK_LAUNCH("read_decode_mma_kernel launch");
       if (ev1) cudaEventRecord(ev1, st);
       dim3 mg((unsigned)n_rows, (d_s + 511) / 512);
