@@ -123,6 +123,10 @@ __global__ void __launch_bounds__(TPW == 8 ? 32 * (RM_MAX_WARPS + 1) : 32 * 11, 
     *abort_flag = 0;
     fence_mbar_init();
   }
+  // Under programmatic dependent launch the shared-memory set-up above overlaps the kernel before; global memory
+  // is read and written only after the wait. The trigger lets the merge's first kernel be scheduled.
+  pdl_wait();
+  pdl_trigger();
   for (int i = threadIdx.x; i < a.s_max; i += blockDim.x) a.fold_info[(int64_t)blockIdx.x * a.s_max + i] = -1;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.n_merge_counters;
        i += (int64_t)gridDim.x * blockDim.x)
@@ -507,6 +511,8 @@ __global__ void __launch_bounds__(MM_MERGE_THREADS) read_multi_coef_kernel(const
   __shared__ int run_start[MM_MERGE_MAX_SLOTS + 1];
   __shared__ int fold_of[MM_MERGE_MAX_CTAS];
   __shared__ int n_open, n_runs, n_fold;
+  pdl_wait();
+  pdl_trigger();
   const int64_t g = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t lib = g / a.q_blocks;
@@ -644,6 +650,8 @@ __global__ void __launch_bounds__(MM_MERGE_THREADS, 2) read_multi_sum_kernel(con
                                                                              float* __restrict__ r_out) {
   __shared__ float4 red[MM_MERGE_WARPS][MQ][32];
   __shared__ int is_last;
+  pdl_wait();
+  pdl_trigger();
   const int64_t g = blockIdx.x;
   const int slab = blockIdx.y, sq = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

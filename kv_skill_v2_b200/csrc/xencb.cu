@@ -1121,12 +1121,13 @@ int xencb_read_multi(const float* q, int64_t n_rows, int d_s, const void* slots,
     auto k1 = read_multi_mma_kernel<T, SPLIT, S, W>;
     int r2 = ensure_smem(k1, (int)p.smem);
     if (r2) return r2;
-    k1<<<p.grid, p.threads, p.smem, st>>>(a);
+    launch_pdl(k1, dim3(p.grid), dim3(p.threads), p.smem, st, a);
     XENCB_CHECK_LAUNCH("read_multi_mma_kernel launch");
-    read_multi_coef_kernel<S><<<(unsigned)p.n_groups, MM_MERGE_THREADS, 0, st>>>(a, p.grid, mm);
+    launch_pdl(read_multi_coef_kernel<S>, dim3((unsigned)p.n_groups), dim3(MM_MERGE_THREADS), 0, st, a, (int)p.grid,
+               mm);
     XENCB_CHECK_LAUNCH("read_multi_coef_kernel launch");
     dim3 mg((unsigned)p.n_groups, (unsigned)p.n_slabs, MM_SQ);
-    read_multi_sum_kernel<<<mg, MM_MERGE_THREADS, 0, st>>>(a, p.grid, mm, r_out);
+    launch_pdl(read_multi_sum_kernel, mg, dim3(MM_MERGE_THREADS), 0, st, a, (int)p.grid, mm, r_out);
     XENCB_CHECK_LAUNCH("read_multi_sum_kernel launch");
     return XENCB_OK;
   };
