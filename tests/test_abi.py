@@ -42,6 +42,11 @@ def test_host_only_entry_points():
     before = N.launch_count()
     assert before >= 0
     assert L.xencb_route_k(4, 64) == 4 and N.launch_count() == before  # host-only calls launch nothing
+    # prepared 3xF16 weights: a 256-byte head, then per 128-row band and 64-column block a 32 KiB tile pair
+    for n, k in [(2048, 4096), (200, 520), (128, 64), (44, 40), (1, 8)]:
+        pairs = -(-n // 128) * -(-k // 64)
+        assert L.xencb_weights_prep_bytes(n, k) == 256 + pairs * 2 * 128 * 64 * 2
+    assert L.xencb_weights_prep_bytes(0, 64) == 0 and L.xencb_weights_prep_bytes(64, 0) == 0
 
 
 def test_header_constants_match_binding():
